@@ -1,0 +1,396 @@
+#!/usr/bin/env python
+# SPDX-License-Identifier: MIT
+"""Benchmark of the quantized matmul hot path on B200.
+
+Headline metric: Q4_K GEMV HBM GB/s. Workload = BASELINE
+config 1 (Q4_K x Q8_K matvec, K=1024, N=3072) over a pool of G distinct
+weight matrices per GPU (default 320 -> 566 MB, > 4x the 126 MB L2, so
+every step streams weights from HBM; no flush needed). One step = quantize
+the G activation rows to Q8_K (one launch) + the G matvecs (one grouped
+persistent launch). GB/s counts algorithmic bytes per matvec: weights
+1,769,472 + Q8_K activation 1,168 + fp32 output 12,288 = 1,782,928.
+
+  value  -- device-resident inputs, CUDA-event time of K steps (max over ranks)
+  e2e    -- the same work through the C-ABI with HOST buffers: per step the
+            activations are copied from pinned host memory and the outputs
+            read back, inside the timed region
+  roofline -- the grouped matvec kernel alone: algorithmic bytes / its mean
+            launch time (events around each launch on its stream) vs the
+            measured HBM copy bandwidth in MEASURED_PEAKS.json
+  cpu_baseline -- the reference's own SIMD row dot (oracle/_ref, compiled
+            from its sources) over all host cores on a bounded sample
+
+Multi-GPU (torchrun, one process per GPU): every rank streams its own pool
+(weak scaling, no data-path collective); NCCL only carries the barrier and
+the max-over-ranks of the elapsed time.
+
+--impl reference runs the reference's CPU implementation of the path
+(oracle/_ref/libqhref.so: simd_q4k_row_dot_q8k with rows split over all host
+threads) on the same workload/metric; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "qwen.haiku_b200")
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_K GEMV HBM GB/s (% of 8 TB/s); decode tok/s at batch 1 and 64/GPU"
+K_IN, N_OUT = 1024, 3072
+W_BYTES = N_OUT * (K_IN // 256) * 144          # 1,769,472
+X_BYTES = (K_IN // 256) * 292                   # Q8_K activation (reference block size)
+O_BYTES = N_OUT * 4
+ALGO_BYTES = W_BYTES + X_BYTES + O_BYTES        # 1,782,928 per matvec
+NOMINAL_HBM_GBS = 8000.0
+
+
+def load_pkg():
+    name = "qwen_haiku_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(
+        name, os.path.join(PKG_DIR, "__init__.py"), submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+        self.path = os.path.join("/tmp", f"qh_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or (self.uuid and parts[0] != self.uuid):
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                smax.append(float(parts[2].split()[0]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's own SIMD dot over all host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_run(qh, n_mats: int, passes_budget_s: float, max_passes: int = None):
+    """Returns (GB/s, cores, sample description, kind, per-pass seconds list)."""
+    import numpy as np
+    from oracle.oracle import Oracle, Ref, to_q8k_blocks
+    cores = len(os.sched_getaffinity(0))
+    h = qh.host
+    base = [h.synth_blocks(qh.Q4_K, N_OUT * 4, 0xC0FFEE + i) for i in range(min(n_mats, 8))]
+    pool = [base[i % len(base)].copy() for i in range(n_mats)]  # distinct addresses
+    x = h.synth_normal(K_IN, 0xACE)
+    if Ref.available():
+        ref = Ref()
+        qs, d, bs = ref.quantize_q8k(x.reshape(1, K_IN))
+        xq = to_q8k_blocks(qs[0], d[0], bs[0])
+        out = np.empty(N_OUT, np.float32)
+
+        def one_pass():
+            ref.matvec_pool_mt(qh.Q4_K, pool, N_OUT, K_IN, xq, cores, out)
+        kind = "reference"
+        label = ref.label
+    else:
+        orc = Oracle()
+        qs, d, bs = orc.quantize_q8k(x.reshape(1, K_IN))
+
+        def one_pass():
+            for w in pool:
+                orc.matvec_preq(qh.Q4_K, w, N_OUT, K_IN, qs[0], d[0], bs[0])
+        kind, label, cores = "port", "oracle restatement (1 thread)", 1
+    times = []
+    t_total = 0.0
+    while True:
+        t0 = time.perf_counter()
+        one_pass()
+        dt = time.perf_counter() - t0
+        times.append(dt)
+        t_total += dt
+        if max_passes is not None and len(times) >= max_passes:
+            break
+        if max_passes is None and t_total >= passes_budget_s:
+            break
+    per_pass = statistics.median(times)
+    gbs = n_mats * ALGO_BYTES / per_pass / 1e9
+    sample = (f"{n_mats} config-1 Q4_K matvecs ({n_mats * W_BYTES / 1e6:.0f} MB weights) per pass, "
+              f"{len(times)} passes; {label}, rows split over {cores} threads")
+    return gbs, cores, sample, kind, times
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    qh = load_pkg()
+    n_mats = 64
+    gbs, cores, sample, kind, times = cpu_reference_run(qh, n_mats, 0.0, max_passes=args.warmup + args.steps)
+    timed = times[args.warmup:] if len(times) > args.warmup else times
+    per = statistics.median(timed)
+    value = n_mats * ALGO_BYTES / per / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
+        "config": {"workload": f"Q4_K GEMV K={K_IN} N={N_OUT} (BASELINE config 1), reference CPU SIMD path",
+                   "k": K_IN, "n": N_OUT, "pool_matrices": n_mats},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import ctypes as C
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    qh = load_pkg()
+    h = qh.host
+    L = qh.lib()
+    qh.check(L.qh_set_device(local), "qh_set_device")
+    G = args.pool
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+
+    # weights: 16 distinct generated matrices replicated over G distinct
+    # device regions (distinct addresses defeat L2 reuse; content may repeat)
+    n_distinct = min(G, 16)
+    host_w = [h.synth_blocks(qh.Q4_K, N_OUT * 4, 0x5EED0000 + 1000 * rank + i) for i in range(n_distinct)]
+    wdev = torch.empty((G, W_BYTES), dtype=torch.uint8, device="cuda")
+    for g in range(G):
+        wdev[g].copy_(torch.from_numpy(host_w[g % n_distinct]), non_blocking=False)
+    x_host = h.synth_normal(G * K_IN, 0xABC + rank).reshape(G, K_IN)
+    x_pin = torch.from_numpy(x_host).pin_memory()
+    x_dev = x_pin.to("cuda")
+    xq = torch.empty(int(L.qh_q8k_bytes(K_IN, G)), dtype=torch.uint8, device="cuda")
+    out = torch.empty((G, N_OUT), dtype=torch.float32, device="cuda")
+    out_pin = torch.empty((G, N_OUT), dtype=torch.float32).pin_memory()
+    jobs = [(wdev[g], xq, out[g], K_IN, N_OUT, G, g) for g in range(G)]
+    plan = h.MatvecPlan(qh.Q4_K, jobs, 1)
+    info = plan.info()
+
+    def quantize():
+        qh.check(L.qh_quantize_q8k(C.c_void_p(x_dev.data_ptr()), K_IN, G, C.c_void_p(xq.data_ptr()), sh),
+                 "qh_quantize_q8k")
+
+    # parity spot check of the benchmarked path (not timed)
+    quantize()
+    plan.run(sh)
+    torch.cuda.synchronize()
+    from oracle.oracle import Oracle
+    orc = Oracle()
+    for g in (0, G - 1):
+        want = orc.matmul(qh.Q4_K, host_w[g % n_distinct], N_OUT, K_IN, x_host[g:g + 1])
+        if not np.array_equal(out[g].cpu().numpy().view(np.uint32), want.view(np.uint32).ravel()):
+            raise SystemExit(f"bench parity check failed for matrix {g}")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing ----
+    for _ in range(args.warmup):
+        quantize()
+        plan.run(sh)
+    uuid = ""
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev0.record(stream)
+    for i in range(args.steps):
+        quantize()
+        kev[i][0].record(stream)
+        plan.run(sh)
+        kev[i][1].record(stream)
+    ev1.record(stream)
+    barrier()
+    elapsed_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    kern_ms = [a.elapsed_time(b) for a, b in kev]
+    # ---- end to end through the C-ABI with host buffers ----
+    for _ in range(2):
+        qh.check(L.qh_memcpy_h2d(C.c_void_p(x_dev.data_ptr()), C.c_void_p(x_pin.data_ptr()), x_pin.numel() * 4, sh), "h2d")
+        quantize()
+        plan.run(sh)
+        qh.check(L.qh_memcpy_d2h(C.c_void_p(out_pin.data_ptr()), C.c_void_p(out.data_ptr()), out.numel() * 4, sh), "d2h")
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        qh.check(L.qh_memcpy_h2d(C.c_void_p(x_dev.data_ptr()), C.c_void_p(x_pin.data_ptr()), x_pin.numel() * 4, sh), "h2d")
+        quantize()
+        plan.run(sh)
+        qh.check(L.qh_memcpy_d2h(C.c_void_p(out_pin.data_ptr()), C.c_void_p(out.data_ptr()), out.numel() * 4, sh), "d2h")
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    qh.check(L.qh_check_device_error(None), "device error word")
+
+    total_bytes = world * G * args.steps * ALGO_BYTES
+    value = total_bytes / (elapsed_ms / 1e3) / 1e9
+    e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
+    kern_mean_ms = statistics.mean(kern_ms)
+    achieved = G * ALGO_BYTES / (kern_mean_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        plan.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        gbs, cores, sample, kind, _ = cpu_reference_run(qh, 64, args.cpu_seconds)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemv_q4k_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                t = json.load(f)
+            # bytes per matvec measured by ncu, scaled to this launch's G matvecs
+            traffic = round(t["dram_bytes_per_matvec"] * G)
+        except Exception:
+            traffic = None
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8+fp32", "data": "synthetic",
+        "config": {"workload": f"Q4_K GEMV K={K_IN} N={N_OUT} (BASELINE config 1) x {G} distinct matrices per GPU per step",
+                   "k": K_IN, "n": N_OUT, "pool_matrices_per_gpu": G,
+                   "pool_bytes_per_gpu": G * W_BYTES, "l2": "inputs larger than L2 (566 MB pool > 126 MB), no flush",
+                   "parallelism": f"dp{world} (independent matrices per GPU)",
+                   "tiling": info},
+        "pct_of_nominal_8tbs": round(value / (NOMINAL_HBM_GBS * world) * 100, 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "kernel": "qh::gemv_kernel<Q4_K,1> (grouped)", "launch_ms": round(kern_mean_ms, 5),
+                     "algorithmic_bytes_per_launch": G * ALGO_BYTES, "traffic": traffic},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": G * K_IN * 4, "d2h_bytes_per_step": G * N_OUT * 4,
+                "ms_per_step": round(e2e_ms / args.steps, 4)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    plan.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--pool", type=int, default=320)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,181 @@
+/* SPDX-License-Identifier: MIT
+ *
+ * qh_backend.h -- C-ABI of the B200 (sm_100a) backend for qwen.haiku's
+ * quantized matmul path.
+ *
+ * This header is the drop-in boundary. The reference computes every
+ * projection of the model through
+ *     matmul_dispatch(w, x)                       slm/model.c:220-264
+ * which switches on the GGUF type of `w` and calls one of
+ *     tensor_matmul_q4k_f32(w_blocks, out_f, k, x)  slm/tensor.c:827-853
+ *     tensor_matmul_q5k_f32(...)                    slm/tensor.c:898-919
+ *     tensor_matmul_q8_0_f32(...)                   slm/tensor.c:952-981
+ *     tensor_matmul_q6k_f32(...)                    slm/tensor.c:1012-1033
+ * each of which quantizes every activation row to Q8_K (Q8_0 for Q8_0
+ * weights) and takes one SIMD row dot per output feature
+ *     simd_q{4k,5k,6k}_row_dot_q8k / simd_q8_0_dot_q8_0   simd/simd.c:236-250.
+ * The entry points below replace those calls one for one on device memory.
+ *
+ * Conventions
+ *   - Plain C types only. Pointers named d_* are device pointers (any
+ *     allocation visible to the current CUDA device); h_* are host pointers.
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy default
+ *     stream. Every compute call is asynchronous on that stream.
+ *   - Weights stay in their GGUF block layout (simd/quants.h:94-130): a
+ *     (k, out_f) weight is out_f rows of k/256 (Q8_0: k/32) blocks, rows
+ *     back to back. The weight pointer must be 16-byte aligned.
+ *   - x is fp32 [n_tok][k] (the reference's x->ne[0] == k), out is fp32
+ *     [n_tok][out_f]; both caller-allocated.
+ *   - Every call returns QH_OK (0) or a negative QH_ERR_* status and never
+ *     aborts (the reference abort()s on an unsupported type,
+ *     slm/model.c:259-261; here that is QH_ERR_UNSUPPORTED). The message of
+ *     the last failure on the calling thread is qh_last_error().
+ *   - Results are bit-identical to the reference's CPU path built with gcc
+ *     -std=c17 (scalar / AVX2 / AVX-VNNI tiers agree on these formats).
+ */
+#ifndef QH_BACKEND_H
+#define QH_BACKEND_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define QH_OK               0
+#define QH_ERR_INVALID     -1  /* bad argument (null pointer, size, shape) */
+#define QH_ERR_UNSUPPORTED -2  /* weight type without a kernel here */
+#define QH_ERR_CUDA        -3  /* CUDA runtime error (see qh_last_error) */
+#define QH_ERR_ALIGN       -4  /* pointer alignment requirement not met */
+#define QH_ERR_WORKSPACE   -5  /* workspace missing or too small */
+#define QH_ERR_DEVICE      -6  /* a kernel reported a device-side error */
+
+/* GGUF tensor type ids (slm/gguf.c:52-59). */
+#define QH_TYPE_F32   0
+#define QH_TYPE_Q8_0  8
+#define QH_TYPE_Q4_K 12
+#define QH_TYPE_Q5_K 13
+#define QH_TYPE_Q6_K 14
+
+/* ------------------------------------------------------------------------
+ * Runtime plumbing
+ * ---------------------------------------------------------------------- */
+
+/* Library version string. */
+const char *qh_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *qh_last_error(void);
+
+/* Number of visible CUDA devices (0 when none); never fails. */
+int qh_device_count(void);
+
+/* Make `device` current for the calling thread. */
+int qh_set_device(int device);
+
+/* Device memory and copies (thin wrappers over the CUDA runtime). */
+int qh_malloc(void **d_ptr, size_t bytes);
+int qh_free(void *d_ptr);
+int qh_memcpy_h2d(void *d_dst, const void *h_src, size_t bytes, void *stream);
+int qh_memcpy_d2h(void *h_dst, const void *d_src, size_t bytes, void *stream);
+int qh_memset(void *d_dst, int value, size_t bytes, void *stream);
+int qh_stream_sync(void *stream);
+
+/* Reads and clears the device error word of the current device (set by a
+ * kernel whose bounded wait ran out). QH_OK when clear, QH_ERR_DEVICE when
+ * a kernel reported an error (the code is returned in *code if non-null). */
+int qh_check_device_error(int *code);
+
+/* ------------------------------------------------------------------------
+ * Activation quantizers (slm/tensor.c:683-720 and 930-950)
+ *
+ * Quantized activations use split planes (qs int8[n_tok][k], then per-block
+ * scales, then Q8_K bsums) instead of the reference's q8k_block array; the
+ * numbers are identical. Byte sizes from qh_q8k_bytes / qh_q8_0_bytes.
+ * ---------------------------------------------------------------------- */
+int64_t qh_q8k_bytes(int64_t k, int64_t n_tok);
+int64_t qh_q8_0_bytes(int64_t k, int64_t n_tok);
+/* Byte offsets of the scale and bsum planes inside a Q8_K split buffer. */
+int64_t qh_q8k_d_offset(int64_t k, int64_t n_tok);
+int64_t qh_q8k_bsums_offset(int64_t k, int64_t n_tok);
+/* Byte offset of the fp16 scale plane inside a Q8_0 split buffer. */
+int64_t qh_q8_0_d_offset(int64_t k, int64_t n_tok);
+
+/* quantize_row_q8_K (slm/tensor.c:683) over n_tok rows; k % 256 == 0. */
+int qh_quantize_q8k(const float *d_x, int64_t k, int64_t n_tok, void *d_q8k, void *stream);
+/* tensor_quantize_row_q8_0 (slm/tensor.c:930) over n_tok rows; k % 32 == 0. */
+int qh_quantize_q8_0(const float *d_x, int64_t k, int64_t n_tok, void *d_q8_0, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Matmul entry points
+ * ---------------------------------------------------------------------- */
+
+/* Device workspace bytes a matmul of this type/shape needs (the quantized
+ * activation rows the reference takes from its arena, slm/tensor.c:836). */
+int64_t qh_matmul_workspace_bytes(int type, int64_t k, int64_t n_tok);
+
+/* tensor_matmul_q4k_f32 (slm/tensor.c:827): out = W x, W Q4_K (k, out_f). */
+int qh_matmul_q4k_f32(const void *d_w, int64_t out_f, int64_t k, const float *d_x,
+                      int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes,
+                      void *stream);
+/* tensor_matmul_q5k_f32 (slm/tensor.c:898). */
+int qh_matmul_q5k_f32(const void *d_w, int64_t out_f, int64_t k, const float *d_x,
+                      int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes,
+                      void *stream);
+/* tensor_matmul_q6k_f32 (slm/tensor.c:1012). */
+int qh_matmul_q6k_f32(const void *d_w, int64_t out_f, int64_t k, const float *d_x,
+                      int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes,
+                      void *stream);
+/* tensor_matmul_q8_0_f32 (slm/tensor.c:952); activations go through the
+ * Q8_0 quantizer (roundf), not Q8_K. */
+int qh_matmul_q8_0_f32(const void *d_w, int64_t out_f, int64_t k, const float *d_x,
+                       int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes,
+                       void *stream);
+
+/* matmul_dispatch (slm/model.c:220): dispatch on the GGUF weight type with
+ * the GGUF shape order (k = shape[0], out_f = shape[1]). */
+int qh_matmul(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x,
+              int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes, void *stream);
+
+/* Same as qh_matmul with the activations already quantized by
+ * qh_quantize_q8k (qh_quantize_q8_0 for Q8_0), so one quantization can feed
+ * several projections of the same input (q/k/v, gate/up). */
+int qh_matmul_preq(int type, const void *d_w, int64_t k, int64_t out_f, const void *d_xq,
+                   int64_t n_tok, float *d_out, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Grouped matvec plans: many independent (weight, quantized activation,
+ * output) jobs of one weight type in ONE persistent launch. A decode step
+ * issues its projections this way (e.g. q, k, v of one layer). No host
+ * reference counterpart: the reference calls tensor_matmul_* once per
+ * weight. Plan creation allocates a small device job table once; running a
+ * plan allocates nothing and can be captured in a CUDA graph.
+ * ---------------------------------------------------------------------- */
+typedef struct qh_matvec_job {
+    const void *d_w;   /* GGUF blocks, (k, out_f), 16-byte aligned */
+    const void *d_xq;  /* split Q8_K (Q8_0) activation buffer of xq_rows rows of k */
+    float *d_out;      /* fp32 [n_tok][out_f] */
+    int64_t k;
+    int64_t out_f;
+    int64_t xq_rows;   /* rows the split buffer was quantized for (0: n_tok) */
+    int64_t xq_row0;   /* first of the job's n_tok rows inside that buffer */
+} qh_matvec_job;
+
+typedef struct qh_matvec_plan_s *qh_matvec_plan;
+
+/* n_tok in [1, 8]. */
+int qh_matvec_plan_create(int type, const qh_matvec_job *h_jobs, int n_jobs, int64_t n_tok,
+                          qh_matvec_plan *out_plan);
+int qh_matvec_plan_run(qh_matvec_plan plan, void *stream);
+/* Rows per tile, pipeline stages, grid size and shared memory chosen. */
+int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, int *grid,
+                        int *smem_bytes);
+int qh_matvec_plan_destroy(qh_matvec_plan plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QH_BACKEND_H */

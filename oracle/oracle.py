@@ -1,0 +1,256 @@
+# SPDX-License-Identifier: MIT
+"""ctypes loaders for the CPU checkers -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+``--impl reference`` legs use this module, and only as the checker or the
+timed CPU baseline; the qwen.haiku_b200 package never imports it.
+
+  Oracle -- oracle/liboracle.so, this repository's C restatement
+            (oracle/qh_oracle.c) of the reference's quantizers and dots.
+  Ref    -- oracle/_ref/libqhref.so, the reference's own C sources compiled
+            where they lie (oracle/ref_harness.c + oracle/Makefile).
+
+Activation rows are passed as split planes (qs int8 [n, k], d f32 [n, k/256],
+bsums int16 [n, k/256, 16]); ``to_q8k_blocks`` packs them into the
+reference's 292-byte q8k_block array (simd/quants.h:94-99).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libqhref.so")
+
+Q8_0, Q4_K, Q5_K, Q6_K = 8, 12, 13, 14
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34}
+BLOCK_WEIGHTS = {Q4_K: 256, Q5_K: 256, Q6_K: 256, Q8_0: 32}
+
+_P, _I, _I64, _F = C.c_void_p, C.c_int, C.c_int64, C.c_float
+
+
+def build(force: bool = False) -> None:
+    """make -C oracle (liboracle.so; _ref/libqhref.so when the reference exists)."""
+    if force or not os.path.exists(ORACLE_SO):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+def to_q8k_blocks(qs: np.ndarray, d: np.ndarray, bs: np.ndarray) -> np.ndarray:
+    """Split planes of ONE row -> q8k_block[k/256] bytes (292 B each)."""
+    nb = d.shape[-1]
+    out = np.zeros((nb, 292), dtype=np.uint8)
+    out[:, 0:4] = np.ascontiguousarray(d.reshape(nb).astype(np.float32)).view(np.uint8).reshape(nb, 4)
+    out[:, 4:260] = qs.reshape(nb, 256).view(np.uint8)
+    out[:, 260:292] = np.ascontiguousarray(bs.reshape(nb, 16).astype(np.int16)).view(np.uint8).reshape(nb, 32)
+    return out.reshape(-1)
+
+
+def from_q8k_blocks(raw: np.ndarray, k: int):
+    nb = k // 256
+    r = raw.reshape(nb, 292)
+    d = np.ascontiguousarray(r[:, 0:4]).view(np.float32).reshape(nb)
+    qs = np.ascontiguousarray(r[:, 4:260]).view(np.int8).reshape(k)
+    bs = np.ascontiguousarray(r[:, 260:292]).view(np.int16).reshape(nb, 16)
+    return qs, d, bs
+
+
+def to_q8_0_blocks(qs: np.ndarray, dbits: np.ndarray) -> np.ndarray:
+    nb = dbits.shape[-1]
+    out = np.zeros((nb, 34), dtype=np.uint8)
+    out[:, 0:2] = np.ascontiguousarray(dbits.reshape(nb).astype(np.uint16)).view(np.uint8).reshape(nb, 2)
+    out[:, 2:34] = qs.reshape(nb, 32).view(np.uint8)
+    return out.reshape(-1)
+
+
+def from_q8_0_blocks(raw: np.ndarray, k: int):
+    nb = k // 32
+    r = raw.reshape(nb, 34)
+    return (np.ascontiguousarray(r[:, 2:34]).view(np.int8).reshape(k),
+            np.ascontiguousarray(r[:, 0:2]).view(np.uint16).reshape(nb))
+
+
+class Oracle:
+    """This repository's CPU restatement (oracle/qh_oracle.c)."""
+
+    def __init__(self):
+        build()
+        L = C.CDLL(ORACLE_SO)
+        L.orc_quantize_row_q8k.argtypes = [_P, _I64, _P, _P, _P]
+        L.orc_quantize_row_q8_0.argtypes = [_P, _I64, _P, _P]
+        for n in ("orc_q4k_block_ints", "orc_q5k_block_ints", "orc_q6k_block_ints"):
+            getattr(L, n).argtypes = [_P, _P, _P, _P, _P]
+        for n in ("orc_q4k_row_dot", "orc_q5k_row_dot", "orc_q6k_row_dot"):
+            getattr(L, n).argtypes = [_I, _P, _P, _P, _P]
+            getattr(L, n).restype = _F
+        for n in ("orc_q8_0_row_dot", "orc_q8_0_row_dot_scalar"):
+            getattr(L, n).argtypes = [_I64, _P, _P, _P]
+            getattr(L, n).restype = _F
+        L.orc_dequant_block.argtypes = [_I, _P, _P]
+        L.orc_matmul.argtypes = [_I, _P, _I64, _I64, _P, _I64, _P, _P, _P, _P]
+        L.orc_matmul.restype = _I
+        self.L = L
+
+    def quantize_q8k(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n, k = x.reshape(-1, x.shape[-1]).shape
+        qs = np.empty((n, k), np.int8)
+        d = np.empty((n, k // 256), np.float32)
+        bs = np.empty((n, k // 256, 16), np.int16)
+        for t in range(n):
+            self.L.orc_quantize_row_q8k(_ptr(x.reshape(n, k)[t]), k, _ptr(d[t]), _ptr(qs[t]), _ptr(bs[t]))
+        return qs, d, bs
+
+    def quantize_q8_0(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n, k = x.reshape(-1, x.shape[-1]).shape
+        qs = np.empty((n, k), np.int8)
+        d = np.empty((n, k // 32), np.uint16)
+        for t in range(n):
+            self.L.orc_quantize_row_q8_0(_ptr(x.reshape(n, k)[t]), k, _ptr(d[t]), _ptr(qs[t]))
+        return qs, d
+
+    def block_ints(self, gtype, blk: np.ndarray, q8: np.ndarray, bs: np.ndarray):
+        fn = {Q4_K: self.L.orc_q4k_block_ints, Q5_K: self.L.orc_q5k_block_ints,
+              Q6_K: self.L.orc_q6k_block_ints}[gtype]
+        a, b = C.c_int32(), C.c_int32()
+        blk = np.ascontiguousarray(blk, np.uint8)
+        q8 = np.ascontiguousarray(q8, np.int8)
+        bs = np.ascontiguousarray(bs, np.int16)
+        fn(_ptr(blk), _ptr(q8), _ptr(bs), C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    def matvec_preq(self, gtype, w: np.ndarray, out_f: int, k: int, qs, d, bs=None) -> np.ndarray:
+        """Row dots of every weight row against ONE pre-quantized row."""
+        out = np.empty(out_f, np.float32)
+        rb = (k // BLOCK_WEIGHTS[gtype]) * BLOCK_BYTES[gtype]
+        w = np.ascontiguousarray(w, np.uint8)
+        qs = np.ascontiguousarray(qs, np.int8)
+        d = np.ascontiguousarray(d)
+        if gtype == Q8_0:
+            for j in range(out_f):
+                out[j] = self.L.orc_q8_0_row_dot(k, C.c_void_p(w.ctypes.data + j * rb), _ptr(d), _ptr(qs))
+            return out
+        bs = np.ascontiguousarray(bs, np.int16)
+        fn = {Q4_K: self.L.orc_q4k_row_dot, Q5_K: self.L.orc_q5k_row_dot, Q6_K: self.L.orc_q6k_row_dot}[gtype]
+        for j in range(out_f):
+            out[j] = fn(k // 256, C.c_void_p(w.ctypes.data + j * rb), _ptr(d), _ptr(qs), _ptr(bs))
+        return out
+
+    def matmul(self, gtype, w: np.ndarray, out_f: int, k: int, x: np.ndarray) -> np.ndarray:
+        """tensor_matmul_*_f32 restatement: x fp32 [n, k] -> out [n, out_f]."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, k)
+        n = x.shape[0]
+        out = np.empty((n, out_f), np.float32)
+        sq = np.empty(k, np.int8)
+        sd = np.empty(max(k // 32, 1), np.float32)
+        sb = np.empty(max(k // 16, 1), np.int16)
+        w = np.ascontiguousarray(w, np.uint8)
+        rc = self.L.orc_matmul(gtype, _ptr(w), out_f, k, _ptr(x), n, _ptr(out), _ptr(sq), _ptr(sd), _ptr(sb))
+        if rc != 0:
+            raise ValueError(f"orc_matmul rejected type {gtype} k {k}")
+        return out
+
+    def dequant_block(self, gtype, blk: np.ndarray) -> np.ndarray:
+        y = np.empty(256, np.float32)
+        self.L.orc_dequant_block(gtype, _ptr(np.ascontiguousarray(blk, np.uint8)), _ptr(y))
+        return y
+
+
+class Ref:
+    """The reference's own C code (oracle/_ref/libqhref.so)."""
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_SO)
+
+    def __init__(self):
+        if not os.path.exists(REF_SO):
+            build(force=True)
+        L = C.CDLL(REF_SO)
+        L.ref_simd_init()
+        L.ref_dispatch_label.restype = C.c_char_p
+        for n in ("ref_q4k_row_dot", "ref_q5k_row_dot", "ref_q6k_row_dot",
+                  "ref_scalar_q4k_row_dot", "ref_scalar_q5k_row_dot", "ref_scalar_q6k_row_dot"):
+            getattr(L, n).argtypes = [_I, _P, _P]
+            getattr(L, n).restype = _F
+        for n in ("ref_q8_0_dot", "ref_scalar_q8_0_dot"):
+            getattr(L, n).argtypes = [_P, _P, _I64]
+            getattr(L, n).restype = _F
+        L.ref_quantize_row_q8k.argtypes = [_P, _P, _I64]
+        L.ref_quantize_row_q8_0.argtypes = [_P, _P, _I64]
+        L.ref_dequant_block.argtypes = [_I, _P, _P]
+        L.ref_matmul.argtypes = [_I, _P, _I64, _I64, _P, _I64, _P]
+        L.ref_matmul.restype = _I
+        L.ref_matvec_mt.argtypes = [_I, _P, _I64, _I64, _P, _P, _I]
+        L.ref_matvec_mt.restype = _I
+        L.ref_matvec_pool_mt.argtypes = [_I, _P, _I, _I64, _I64, _P, _P, _I]
+        L.ref_matvec_pool_mt.restype = _I
+        self.L = L
+        self.label = L.ref_dispatch_label().decode()
+
+    def quantize_q8k(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, x.shape[-1])
+        n, k = x.shape
+        raws = []
+        for t in range(n):
+            raw = np.empty((k // 256) * 292, np.uint8)
+            self.L.ref_quantize_row_q8k(_ptr(x[t]), _ptr(raw), k)
+            raws.append(raw)
+        parts = [from_q8k_blocks(r, k) for r in raws]
+        return (np.stack([p[0] for p in parts]), np.stack([p[1] for p in parts]),
+                np.stack([p[2] for p in parts]))
+
+    def quantize_q8_0(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, x.shape[-1])
+        n, k = x.shape
+        parts = []
+        for t in range(n):
+            raw = np.empty((k // 32) * 34, np.uint8)
+            self.L.ref_quantize_row_q8_0(_ptr(x[t]), _ptr(raw), k)
+            parts.append(from_q8_0_blocks(raw, k))
+        return np.stack([p[0] for p in parts]), np.stack([p[1] for p in parts])
+
+    def matmul(self, gtype, w: np.ndarray, out_f: int, k: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, k)
+        n = x.shape[0]
+        out = np.empty((n, out_f), np.float32)
+        w = np.ascontiguousarray(w, np.uint8)
+        rc = self.L.ref_matmul(gtype, _ptr(w), out_f, k, _ptr(x), n, _ptr(out))
+        if rc != 0:
+            raise ValueError(f"ref_matmul rejected type {gtype}")
+        return out
+
+    def row_dot(self, gtype, row: np.ndarray, xq_blocks: np.ndarray, k: int, scalar=False) -> float:
+        row = np.ascontiguousarray(row, np.uint8)
+        if gtype == Q8_0:
+            fn = self.L.ref_scalar_q8_0_dot if scalar else self.L.ref_q8_0_dot
+            return fn(_ptr(row), _ptr(xq_blocks), k)
+        name = {Q4_K: "q4k", Q5_K: "q5k", Q6_K: "q6k"}[gtype]
+        fn = getattr(self.L, f"ref_scalar_{name}_row_dot" if scalar else f"ref_{name}_row_dot")
+        return fn(k // 256, _ptr(row), _ptr(xq_blocks))
+
+    def matvec_mt(self, gtype, w: np.ndarray, out_f: int, k: int, xq_blocks: np.ndarray,
+                  nthreads: int, out: np.ndarray = None) -> np.ndarray:
+        if out is None:
+            out = np.empty(out_f, np.float32)
+        self.L.ref_matvec_mt(gtype, _ptr(w), out_f, k, _ptr(xq_blocks), _ptr(out), nthreads)
+        return out
+
+    def matvec_pool_mt(self, gtype, pool, out_f: int, k: int, xq_blocks: np.ndarray,
+                       nthreads: int, out: np.ndarray) -> None:
+        """Every matrix of `pool` against one activation row, rows over threads."""
+        ptrs = (C.c_void_p * len(pool))(*[w.ctypes.data for w in pool])
+        self.L.ref_matvec_pool_mt(gtype, ptrs, len(pool), out_f, k, _ptr(xq_blocks), _ptr(out), nthreads)
+
+    def dequant_block(self, gtype, blk: np.ndarray) -> np.ndarray:
+        y = np.empty(256, np.float32)
+        self.L.ref_dequant_block(gtype, _ptr(np.ascontiguousarray(blk, np.uint8)), _ptr(y))
+        return y

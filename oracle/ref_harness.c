@@ -1,0 +1,213 @@
+// SPDX-License-Identifier: MIT
+//
+// ref_harness.c -- exports the reference's own CPU code for the quantized
+// matmul path (and its model forward step) from a shared library.
+//
+// TEST INFRASTRUCTURE, NOT PRODUCT CODE. oracle/Makefile compiles this file
+// with the qwen.haiku sources on the include path (the reference is a
+// single-translation-unit C17 program: slm/qwen.c pulls in model.c,
+// tensor.c, simd/simd.c, simd/avx.c and simd/quants.h). No reference source
+// is copied here; these are thin wrappers that reach the reference's static
+// functions through that translation unit. Output: oracle/_ref/libqhref.so.
+//
+// Wrapped entry points:
+//   simd_init / simd_dispatch_label            simd/simd.c:191-234
+//   simd_q{4k,5k,6k}_row_dot_q8k, _q8_0_dot    simd/simd.c:236-250
+//   q_scalar_*                                 simd/quants.h:244-402
+//   quantize_row_q8_K                          slm/tensor.c:683-720
+//   tensor_quantize_row_q8_0                   slm/tensor.c:930-950
+//   matmul_dispatch                            slm/model.c:220-264
+//   q{4k,5k,6k}_dequant_block                  slm/tensor.c:800, 867, 988
+//   slm_forward_step + sample_argmax           slm/qwen.c:874-981, slm/model.c:401
+
+#include "slm/qwen.c"
+#include "slm/sampler.c"
+
+#include <pthread.h>
+
+void ref_simd_init(void) { simd_init(); }
+const char *ref_dispatch_label(void) { return simd_dispatch_label(); }
+
+float ref_q4k_row_dot(int nb, const void *w, const void *y) {
+    return simd_q4k_row_dot_q8k(nb, (const q4k_block *)w, (const q8k_block *)y);
+}
+float ref_q5k_row_dot(int nb, const void *w, const void *y) {
+    return simd_q5k_row_dot_q8k(nb, (const q5k_block *)w, (const q8k_block *)y);
+}
+float ref_q6k_row_dot(int nb, const void *w, const void *y) {
+    return simd_q6k_row_dot_q8k(nb, (const q6k_block *)w, (const q8k_block *)y);
+}
+float ref_q8_0_dot(const void *w, const void *y, int64_t k) {
+    return simd_q8_0_dot_q8_0((const q8_0_block *)w, (const q8_0_block *)y, k);
+}
+float ref_scalar_q4k_row_dot(int nb, const void *w, const void *y) {
+    return q_scalar_q4k_row_dot_q8k(nb, (const q4k_block *)w, (const q8k_block *)y);
+}
+float ref_scalar_q5k_row_dot(int nb, const void *w, const void *y) {
+    return q_scalar_q5k_row_dot_q8k(nb, (const q5k_block *)w, (const q8k_block *)y);
+}
+float ref_scalar_q6k_row_dot(int nb, const void *w, const void *y) {
+    return q_scalar_q6k_row_dot_q8k(nb, (const q6k_block *)w, (const q8k_block *)y);
+}
+float ref_scalar_q8_0_dot(const void *w, const void *y, int64_t k) {
+    return q_scalar_q8_0_dot_q8_0((const q8_0_block *)w, (const q8_0_block *)y, k);
+}
+
+int ref_sizeof_q8k_block(void) { return (int)sizeof(q8k_block); }
+
+// Activation quantizers exactly as the matmul wrappers call them.
+void ref_quantize_row_q8k(const float *x, void *dst, int64_t k) {
+    quantize_row_q8_K(x, (q8k_block *)dst, k);
+}
+void ref_quantize_row_q8_0(const float *x, void *dst, int64_t k) {
+    tensor_quantize_row_q8_0(x, (q8_0_block *)dst, k);
+}
+
+void ref_dequant_block(int type, const void *blk, float *y) {
+    switch (type) {
+        case GGUF_TT_Q4_K: q4k_dequant_block((const q4k_block *)blk, y); break;
+        case GGUF_TT_Q5_K: q5k_dequant_block((const q5k_block *)blk, y); break;
+        case GGUF_TT_Q6_K: q6k_dequant_block((const q6k_block *)blk, y); break;
+        default: break;
+    }
+}
+
+// matmul_dispatch on a weight tensor of GGUF type `type`, shape (k, out_f);
+// x is [n][k] fp32, out is [n][out_f] fp32. This is the reference's own
+// single-threaded path (LLM_PAR_FOR is a plain loop off Apple).
+int ref_matmul(int type, const void *w, int64_t out_f, int64_t k,
+               const float *x, int64_t n, float *out) {
+    simd_init();
+    size_t need = (size_t)(k * n + out_f * n) * sizeof(float) + (size_t)k * 4 + (1u << 20);
+    struct arena *a = arena_new(need);
+    struct tensor *xt = tensor_new_2d(a, k, n);
+    memcpy(xt->data, x, (size_t)(k * n) * sizeof(float));
+    struct slm_tensor wt;
+    memset(&wt, 0, sizeof(wt));
+    wt.data = w;
+    wt.type = type;
+    wt.n_dims = 2;
+    wt.shape[0] = k;
+    wt.shape[1] = out_f;
+    wt.shape[2] = wt.shape[3] = 1;
+    int rc = -1;
+    if (type == GGUF_TT_Q4_K || type == GGUF_TT_Q5_K || type == GGUF_TT_Q6_K ||
+        type == GGUF_TT_Q8_0 || type == GGUF_TT_F32) {
+        struct tensor *r = matmul_dispatch(&wt, xt);
+        memcpy(out, r->data, (size_t)(out_f * n) * sizeof(float));
+        rc = 0;
+    }
+    arena_free(a);
+    return rc;
+}
+
+// ---------------------------------------------------------------------------
+// All-cores CPU baseline: the reference's dispatched row dot, with the output
+// rows split over `nthreads` pthreads (the reference's LLM_PAR_FOR runs rows
+// sequentially on Linux; this harness only spreads the same calls over cores).
+// `xq` is ONE pre-quantized activation row (q8k_block[k/256], or
+// q8_0_block[k/32] for Q8_0). Rows [0, out_f) of matrix w.
+// ---------------------------------------------------------------------------
+struct mt_job {
+    int type;
+    const uint8_t *w;
+    int64_t k, r0, r1, row_bytes;
+    const void *xq;
+    float *out;
+};
+
+static void *mt_worker(void *arg) {
+    struct mt_job *j = (struct mt_job *)arg;
+    const int nb = (int)(j->k / QK_K);
+    for (int64_t r = j->r0; r < j->r1; r++) {
+        const void *row = j->w + r * j->row_bytes;
+        float v = 0.0f;
+        switch (j->type) {
+            case GGUF_TT_Q4_K: v = simd_q4k_row_dot_q8k(nb, row, j->xq); break;
+            case GGUF_TT_Q5_K: v = simd_q5k_row_dot_q8k(nb, row, j->xq); break;
+            case GGUF_TT_Q6_K: v = simd_q6k_row_dot_q8k(nb, row, j->xq); break;
+            case GGUF_TT_Q8_0: v = simd_q8_0_dot_q8_0(row, j->xq, j->k); break;
+            default: break;
+        }
+        j->out[r] = v;
+    }
+    return NULL;
+}
+
+int ref_matvec_mt(int type, const void *w, int64_t out_f, int64_t k,
+                  const void *xq, float *out, int nthreads) {
+    simd_init();
+    int64_t row_bytes;
+    switch (type) {
+        case GGUF_TT_Q4_K: row_bytes = (k / QK_K) * 144; break;
+        case GGUF_TT_Q5_K: row_bytes = (k / QK_K) * 176; break;
+        case GGUF_TT_Q6_K: row_bytes = (k / QK_K) * 210; break;
+        case GGUF_TT_Q8_0: row_bytes = (k / 32) * 34; break;
+        default: return -1;
+    }
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    pthread_t th[256];
+    struct mt_job jobs[256];
+    int64_t per = (out_f + nthreads - 1) / nthreads;
+    int started = 0;
+    for (int t = 0; t < nthreads; t++) {
+        int64_t r0 = t * per, r1 = r0 + per < out_f ? r0 + per : out_f;
+        if (r0 >= r1) break;
+        jobs[t] = (struct mt_job){type, (const uint8_t *)w, k, r0, r1, row_bytes, xq, out};
+        if (nthreads == 1) { mt_worker(&jobs[t]); started = 0; break; }
+        pthread_create(&th[t], NULL, mt_worker, &jobs[t]);
+        started++;
+    }
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    return 0;
+}
+
+// Same as ref_matvec_mt over a pool of n_mats matrices (each out_f rows, one
+// shared activation row): each thread walks its row range of every matrix,
+// so threads are created once per pass instead of once per matrix.
+struct pool_job {
+    int type;
+    const uint8_t *const *ws;
+    int n_mats;
+    int64_t k, r0, r1, row_bytes;
+    const void *xq;
+    float *out;
+};
+
+static void *pool_worker(void *arg) {
+    struct pool_job *p = (struct pool_job *)arg;
+    for (int m = 0; m < p->n_mats; m++) {
+        struct mt_job j = {p->type, p->ws[m], p->k, p->r0, p->r1, p->row_bytes, p->xq, p->out};
+        mt_worker(&j);
+    }
+    return NULL;
+}
+
+int ref_matvec_pool_mt(int type, const void *const *ws, int n_mats, int64_t out_f, int64_t k,
+                       const void *xq, float *out, int nthreads) {
+    simd_init();
+    int64_t row_bytes;
+    switch (type) {
+        case GGUF_TT_Q4_K: row_bytes = (k / QK_K) * 144; break;
+        case GGUF_TT_Q5_K: row_bytes = (k / QK_K) * 176; break;
+        case GGUF_TT_Q6_K: row_bytes = (k / QK_K) * 210; break;
+        case GGUF_TT_Q8_0: row_bytes = (k / 32) * 34; break;
+        default: return -1;
+    }
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    pthread_t th[256];
+    struct pool_job jobs[256];
+    int64_t per = (out_f + nthreads - 1) / nthreads;
+    int started = 0;
+    for (int t = 0; t < nthreads; t++) {
+        int64_t r0 = t * per, r1 = r0 + per < out_f ? r0 + per : out_f;
+        if (r0 >= r1) break;
+        jobs[t] = (struct pool_job){type, (const uint8_t *const *)ws, n_mats, k, r0, r1, row_bytes, xq, out};
+        pthread_create(&th[t], NULL, pool_worker, &jobs[t]);
+        started++;
+    }
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    return 0;
+}

@@ -1,0 +1,120 @@
+# SPDX-License-Identifier: MIT
+"""qwen.haiku_b200 -- B200 (sm_100a) backend for qwen.haiku's quantized
+matmul path, loaded from the in-tree C-ABI library libqh200.so.
+
+The package directory name contains a dot, so it is loaded by path (see
+``load()`` in tests/conftest.py, bench.py and __graft_entry__.py); inside it
+everything is plain relative imports.
+
+Python here is glue: ctypes bindings of include/qh_backend.h and
+include/qh_synth.h, plus a thin mirror of the reference's matmul interface
+(slm/tensor.c:827-1033, slm/model.c:220) over device buffers for tests and
+benchmarks. All arithmetic runs in the CUDA kernels of libqh200.so; there is
+no CPU fallback -- calls fail loudly when the library or a GPU is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqh200.so")
+
+# Status codes (include/qh_backend.h).
+QH_OK = 0
+STATUS_NAMES = {
+    -1: "QH_ERR_INVALID", -2: "QH_ERR_UNSUPPORTED", -3: "QH_ERR_CUDA",
+    -4: "QH_ERR_ALIGN", -5: "QH_ERR_WORKSPACE", -6: "QH_ERR_DEVICE",
+}
+
+# GGUF tensor types (slm/gguf.c:52-59).
+F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
+TYPE_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34}
+BLOCK_WEIGHTS = {Q4_K: 256, Q5_K: 256, Q6_K: 256, Q8_0: 32}
+
+
+class QHError(RuntimeError):
+    """A libqh200 call returned a non-zero status."""
+
+    def __init__(self, status: int, where: str, message: str):
+        super().__init__(f"{where}: {STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class MatvecJob(C.Structure):
+    _fields_ = [("d_w", C.c_void_p), ("d_xq", C.c_void_p), ("d_out", C.c_void_p),
+                ("k", C.c_int64), ("out_f", C.c_int64),
+                ("xq_rows", C.c_int64), ("xq_row0", C.c_int64)]
+
+
+_P, _I, _I64, _U64, _F, _SZ = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_float, C.c_size_t
+
+# name -> (restype, argtypes); every declaration of include/qh_backend.h and
+# include/qh_synth.h.
+SIGNATURES = {
+    "qh_version": (C.c_char_p, []),
+    "qh_last_error": (C.c_char_p, []),
+    "qh_device_count": (_I, []),
+    "qh_set_device": (_I, [_I]),
+    "qh_malloc": (_I, [C.POINTER(C.c_void_p), _SZ]),
+    "qh_free": (_I, [_P]),
+    "qh_memcpy_h2d": (_I, [_P, _P, _SZ, _P]),
+    "qh_memcpy_d2h": (_I, [_P, _P, _SZ, _P]),
+    "qh_memset": (_I, [_P, _I, _SZ, _P]),
+    "qh_stream_sync": (_I, [_P]),
+    "qh_check_device_error": (_I, [C.POINTER(C.c_int)]),
+    "qh_q8k_bytes": (_I64, [_I64, _I64]),
+    "qh_q8_0_bytes": (_I64, [_I64, _I64]),
+    "qh_q8k_d_offset": (_I64, [_I64, _I64]),
+    "qh_q8k_bsums_offset": (_I64, [_I64, _I64]),
+    "qh_q8_0_d_offset": (_I64, [_I64, _I64]),
+    "qh_quantize_q8k": (_I, [_P, _I64, _I64, _P, _P]),
+    "qh_quantize_q8_0": (_I, [_P, _I64, _I64, _P, _P]),
+    "qh_matmul_workspace_bytes": (_I64, [_I, _I64, _I64]),
+    "qh_matmul_q4k_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qh_matmul_q5k_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qh_matmul_q6k_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qh_matmul_q8_0_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qh_matmul": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qh_matmul_preq": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P]),
+    "qh_matvec_plan_create": (_I, [_I, C.POINTER(MatvecJob), _I, _I64, C.POINTER(C.c_void_p)]),
+    "qh_matvec_plan_run": (_I, [_P, _P]),
+    "qh_matvec_plan_info": (_I, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
+    "qh_matvec_plan_destroy": (_I, [_P]),
+    "qh_synth_u64": (_U64, [_U64, _U64]),
+    "qh_synth_normal": (_I, [_U64, _I64, _F, _F, _P]),
+    "qh_synth_blocks": (_I, [_I, _I64, _U64, _P]),
+    "qh_synth_quantize": (_I, [_I, _P, _I64, _I64, _P]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded libqh200.so with every C-ABI signature declared."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise QHError(-3, "load", f"{LIB_PATH} is missing; run qwen.haiku_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def check(status: int, where: str) -> None:
+    if status != QH_OK:
+        raise QHError(status, where, lib().qh_last_error().decode(errors="replace"))
+
+
+def row_bytes(gtype: int, k: int) -> int:
+    return (k // BLOCK_WEIGHTS[gtype]) * BLOCK_BYTES[gtype]
+
+
+from . import host  # noqa: E402  (host-side helpers over the bindings)
+
+__all__ = ["lib", "check", "QHError", "MatvecJob", "host", "row_bytes",
+           "F32", "Q8_0", "Q4_K", "Q5_K", "Q6_K", "BLOCK_BYTES", "BLOCK_WEIGHTS"]

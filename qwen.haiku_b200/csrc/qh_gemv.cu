@@ -1,0 +1,515 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_gemv.cu -- decode-time quantized matvec (and small-n matmul) for the
+// GGUF K-quant / Q8_0 weight formats on sm_100a.
+//
+// Replaces the reference's per-row SIMD dots (simd/quants.h:244-402,
+// simd/avx.c:420-591) as driven by tensor_matmul_{q4k,q5k,q6k,q8_0}_f32
+// (slm/tensor.c:827-1033): out[t][j] = row_dot(W row j, Q8 activation row t).
+//
+// Design (memory-bound stream):
+//   * Persistent grouped kernel: the launch walks a list of independent jobs
+//     (weight matrix, activation, output) of one weight type; each job is
+//     cut into tiles of R consecutive rows (a contiguous byte range).
+//   * Warp 8 (one elected lane) is the producer: it streams each tile into a
+//     ring of shared-memory stages with a 1-D bulk copy on the TMA engine
+//     (cp.async.bulk + mbarrier complete_tx). Ranges are copied from their
+//     16-byte-aligned start; the <16-byte tail of a range is fetched with
+//     plain loads so the copy never reads past the matrix.
+//   * Warps 0..7 consume: every warp owns whole 8-row groups (round-robin
+//     across tiles, so short tiles still spread over all warps) and keeps
+//     the tile's rows in shared memory while it walks their blocks.
+//   * Integer block sums use dp4a/dp2a; the fp32 combination of each block
+//     and the block-sequential row sum are done with explicitly rounded
+//     __fmul_rn/__fsub_rn/__fadd_rn (no FMA contraction) in exactly the
+//     reference's order, so the outputs are bit-identical to the reference's
+//     scalar/AVX-VNNI/AVX2 results. Q8_0 reproduces the AVX tiers' 8-lane
+//     fused-multiply-add accumulation and their horizontal-sum order.
+//   * Every mbarrier wait is bounded; a timeout records an error in the
+//     device error word and the CTA drains its own copies and returns.
+
+#include <algorithm>
+
+#include "qh_common.cuh"
+#include "qh_internal.h"
+
+namespace qh {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = 32 * (kConsumerWarps + 1);
+// Shared memory per CTA: 1 KiB of barriers/metadata + the stage ring. Two
+// CTAs fit on one SM (228 KiB per SM, 1 KiB reserved per CTA).
+constexpr int kSmemHeader = 1024;
+constexpr int kSmemDataBudget = 112 * 1024;
+
+__device__ __forceinline__ GemvJob load_job(const GemvParams &p, int j) {
+    return p.n_jobs <= kGemvInlineJobs ? p.jobs[j] : p.table[j];
+}
+
+// Largest job index whose tile_begin <= tile.
+__device__ __forceinline__ int find_job(const GemvParams &p, int tile) {
+    if (p.n_jobs <= kGemvInlineJobs) {
+        int j = 0;
+        for (int i = 1; i < p.n_jobs; ++i)
+            if (p.jobs[i].tile_begin <= tile) j = i;
+        return j;
+    }
+    int lo = 0, hi = p.n_jobs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(&p.table[mid].tile_begin) <= tile) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ---------------------------------------------------------------------------
+// Per-type consumers. A call handles one 8-row group whose rows start at
+// `grp` in shared memory (row stride = job.row_bytes). Lanes: r = lane/4 is
+// the row, q = lane%4 a quarter of every super-block.
+// ---------------------------------------------------------------------------
+
+// Unpacked 6-bit scales/mins of the four sub-blocks a lane covers in a
+// Q4_K/Q5_K super-block (simd/quants.h:215-224). With j0 = q/2 the lane
+// covers sub-blocks 2j0, 2j0+1 (stored in scale bytes 0..7) and 2j0+4,
+// 2j0+5 (stored across bytes 8..11 plus the top bits of bytes 0..7).
+struct KScales {
+    int sc_a, sc_b, sc_c, sc_d;
+    int mins_ab, mins_cd;  // bytes {m_a, m_a, m_b, m_b} for dp2a against bsum pairs
+};
+
+__device__ __forceinline__ KScales unpack_kscales(const uint4 &h, uint32_t sh) {
+    const uint32_t L = (h.y >> sh) & 0xffffu;  // scales[2j0], scales[2j0+1]
+    const uint32_t M = (h.z >> sh) & 0xffffu;  // scales[2j0+4], scales[2j0+5]
+    const uint32_t H = (h.w >> sh) & 0xffffu;  // scales[2j0+8], scales[2j0+9]
+    const uint32_t sc_ab = L & 0x3f3fu;
+    const uint32_t m_ab = M & 0x3f3fu;
+    const uint32_t sc_cd = (H & 0x0f0fu) | ((L >> 2) & 0x3030u);
+    const uint32_t m_cd = ((H >> 4) & 0x0f0fu) | ((M >> 2) & 0x3030u);
+    KScales s;
+    s.sc_a = static_cast<int>(sc_ab & 0xffu);
+    s.sc_b = static_cast<int>(sc_ab >> 8);
+    s.sc_c = static_cast<int>(sc_cd & 0xffu);
+    s.sc_d = static_cast<int>(sc_cd >> 8);
+    s.mins_ab = static_cast<int>(__byte_perm(m_ab, 0u, 0x1100u));
+    s.mins_cd = static_cast<int>(__byte_perm(m_cd, 0u, 0x1100u));
+    return s;
+}
+
+__device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                     const int4 &x, int acc) {
+    acc = __dp4a(static_cast<int>(w0), x.x, acc);
+    acc = __dp4a(static_cast<int>(w1), x.y, acc);
+    acc = __dp4a(static_cast<int>(w2), x.z, acc);
+    acc = __dp4a(static_cast<int>(w3), x.w, acc);
+    return acc;
+}
+
+// Shared tail of Q4_K/Q5_K: integer dots with the four activation slices,
+// scale, mins via dp2a, 4-lane reduction, fp32 combination.
+template <int NT>
+__device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const uint32_t (&wb)[4],
+                                                  const uint32_t (&wc)[4], const uint32_t (&wd)[4],
+                                                  const KScales &s, float dw, float dmw,
+                                                  const GemvJob &job, int b, int j0, int r0,
+                                                  int n_tok, float (&acc)[NT]) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (t < n_tok) {
+            const int8_t *xq = job.xqs + static_cast<int64_t>(t) * job.k + b * QH_QK + 64 * j0 + r0;
+            const int4 xa = ldg128(xq);
+            const int4 xb = ldg128(xq + 32);
+            const int4 xc = ldg128(xq + 128);
+            const int4 xd = ldg128(xq + 160);
+            const int da = dot16(wa[0], wa[1], wa[2], wa[3], xa, 0);
+            const int db = dot16(wb[0], wb[1], wb[2], wb[3], xb, 0);
+            const int dc = dot16(wc[0], wc[1], wc[2], wc[3], xc, 0);
+            const int dd = dot16(wd[0], wd[1], wd[2], wd[3], xd, 0);
+            int isum = da * s.sc_a + db * s.sc_b + dc * s.sc_c + dd * s.sc_d;
+            const int16_t *bs = job.xbs + (static_cast<int64_t>(t) * job.nb + b) * 16 + 4 * j0;
+            const int2 bl = __ldg(reinterpret_cast<const int2 *>(bs));
+            const int2 bh = __ldg(reinterpret_cast<const int2 *>(bs + 8));
+            int mins = __dp2a_lo(bl.x, s.mins_ab, 0);
+            mins = __dp2a_hi(bl.y, s.mins_ab, mins);
+            mins = __dp2a_lo(bh.x, s.mins_cd, mins);
+            mins = __dp2a_hi(bh.y, s.mins_cd, mins);
+            isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+            mins += __shfl_xor_sync(0xffffffffu, mins, 1);
+            isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+            mins += __shfl_xor_sync(0xffffffffu, mins, 2);
+            const float yd = __ldg(static_cast<const float *>(job.xd) + t * job.nb + b);
+            const float d = __fmul_rn(yd, dw);
+            const float dmin = __fmul_rn(yd, dmw);
+            acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d, static_cast<float>(isum)),
+                                                 __fmul_rn(dmin, static_cast<float>(mins))));
+        }
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job, int row0,
+                                          int nvalid, int n_tok) {
+    const int lane = threadIdx.x & 31;
+    const int r = lane >> 2, q = lane & 3, j0 = q >> 1, r0 = (q & 1) << 4;
+    const uint8_t *row = grp + r * job.row_bytes;
+    const uint32_t sh = 16u * static_cast<uint32_t>(j0);
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    for (int b = 0; b < job.nb; ++b) {
+        const uint8_t *blk = row + b * QH_Q4K_BYTES;
+        const uint4 h = lds128(blk);
+        const uint4 qa = lds128(blk + 16 + 16 * q);  // qs[32*j0 + r0 .. +16]
+        const uint4 qc = lds128(blk + 80 + 16 * q);  // qs[32*(j0+2) + r0 .. +16]
+        const KScales s = unpack_kscales(h, sh);
+        const uint32_t m4 = 0x0f0f0f0fu;
+        const uint32_t wa[4] = {qa.x & m4, qa.y & m4, qa.z & m4, qa.w & m4};
+        const uint32_t wb[4] = {(qa.x >> 4) & m4, (qa.y >> 4) & m4, (qa.z >> 4) & m4, (qa.w >> 4) & m4};
+        const uint32_t wc[4] = {qc.x & m4, qc.y & m4, qc.z & m4, qc.w & m4};
+        const uint32_t wd[4] = {(qc.x >> 4) & m4, (qc.y >> 4) & m4, (qc.z >> 4) & m4, (qc.w >> 4) & m4};
+        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, b, j0,
+                              r0, n_tok, acc);
+    }
+    if (q == 0 && r < nvalid) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc[t];
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job, int row0,
+                                          int nvalid, int n_tok) {
+    const int lane = threadIdx.x & 31;
+    const int r = lane >> 2, q = lane & 3, j0 = q >> 1, r0 = (q & 1) << 4;
+    const uint8_t *row = grp + r * job.row_bytes;
+    const uint32_t sh = 16u * static_cast<uint32_t>(j0);
+    // 5th bit of sub-block s sits in bit s of qh[l]; move it to bit 4.
+    const uint32_t up_a = 4u - 2u * j0, up_b = 3u - 2u * j0;  // s = 2j0, 2j0+1
+    const uint32_t dn_c = 2u * j0, dn_d = 2u * j0 + 1u;       // s = 2j0+4, 2j0+5
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    for (int b = 0; b < job.nb; ++b) {
+        const uint8_t *blk = row + b * QH_Q5K_BYTES;
+        const uint4 h = lds128(blk);
+        const uint4 hv = lds128(blk + 16 + r0);       // qh[r0 .. r0+16)
+        const uint4 qa = lds128(blk + 48 + 16 * q);   // qs[32*j0 + r0 ..]
+        const uint4 qc = lds128(blk + 112 + 16 * q);  // qs[32*(j0+2) + r0 ..]
+        const KScales s = unpack_kscales(h, sh);
+        const uint32_t m4 = 0x0f0f0f0fu, b4 = 0x10101010u;
+        const uint32_t qh[4] = {hv.x, hv.y, hv.z, hv.w};
+        const uint32_t la[4] = {qa.x, qa.y, qa.z, qa.w};
+        const uint32_t lc[4] = {qc.x, qc.y, qc.z, qc.w};
+        uint32_t wa[4], wb[4], wc[4], wd[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            wa[i] = (la[i] & m4) | ((qh[i] << up_a) & b4);
+            wb[i] = ((la[i] >> 4) & m4) | ((qh[i] << up_b) & b4);
+            wc[i] = (lc[i] & m4) | ((qh[i] >> dn_c) & b4);
+            wd[i] = ((lc[i] >> 4) & m4) | ((qh[i] >> dn_d) & b4);
+        }
+        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, b, j0,
+                              r0, n_tok, acc);
+    }
+    if (q == 0 && r < nvalid) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc[t];
+    }
+}
+
+// Q6_K: lane q covers half n = q/2 of the super-block and 16 positions
+// l0 = 16*(q%2) inside each of its four 32-wide quarters, i.e. the
+// 16-wide sub-blocks 8n + q%2 + {0,2,4,6}. Blocks are 210 bytes, so rows
+// and blocks are only 2-byte aligned in shared memory.
+template <int NT>
+__device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job, int row0,
+                                          int nvalid, int n_tok) {
+    const int lane = threadIdx.x & 31;
+    const int r = lane >> 2, q = lane & 3, n = q >> 1, l0 = (q & 1) << 4;
+    const uint8_t *row = grp + r * job.row_bytes;
+    const uint32_t bs_shift = 16u * static_cast<uint32_t>(q & 1);
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    for (int b = 0; b < job.nb; ++b) {
+        const uint8_t *blk = row + b * QH_Q6K_BYTES;
+        const uint4 qa = lds128_a2(blk + 64 * n + l0);        // ql, quarters 0 (low) / 2 (high)
+        const uint4 qb = lds128_a2(blk + 64 * n + 32 + l0);   // ql, quarters 1 (low) / 3 (high)
+        const uint4 hv = lds128_a2(blk + 128 + 32 * n + l0);  // qh, 2 bits per quarter
+        const int8_t *scp = reinterpret_cast<const int8_t *>(blk + 192 + 8 * n + (q & 1));
+        const int s0 = scp[0], s1 = scp[2], s2 = scp[4], s3 = scp[6];
+        const float dw = h2f_bits(*reinterpret_cast<const uint16_t *>(blk + 208));
+        const uint32_t m4 = 0x0f0f0f0fu, m2 = 0x30303030u;
+        const uint32_t la[4] = {qa.x, qa.y, qa.z, qa.w};
+        const uint32_t lb[4] = {qb.x, qb.y, qb.z, qb.w};
+        const uint32_t qh[4] = {hv.x, hv.y, hv.z, hv.w};
+        uint32_t wa[4], wb[4], wc[4], wd[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            wa[i] = (la[i] & m4) | ((qh[i] << 4) & m2);
+            wb[i] = (lb[i] & m4) | ((qh[i] << 2) & m2);
+            wc[i] = ((la[i] >> 4) & m4) | (qh[i] & m2);
+            wd[i] = ((lb[i] >> 4) & m4) | ((qh[i] >> 2) & m2);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (t < n_tok) {
+                const int8_t *xq = job.xqs + static_cast<int64_t>(t) * job.k + b * QH_QK + 128 * n + l0;
+                const int da = dot16(wa[0], wa[1], wa[2], wa[3], ldg128(xq), 0);
+                const int db = dot16(wb[0], wb[1], wb[2], wb[3], ldg128(xq + 32), 0);
+                const int dc = dot16(wc[0], wc[1], wc[2], wc[3], ldg128(xq + 64), 0);
+                const int dd = dot16(wd[0], wd[1], wd[2], wd[3], ldg128(xq + 96), 0);
+                const int4 bv = ldg128(job.xbs + (static_cast<int64_t>(t) * job.nb + b) * 16 + 8 * n);
+                const int b0 = static_cast<int16_t>(static_cast<uint32_t>(bv.x) >> bs_shift);
+                const int b1 = static_cast<int16_t>(static_cast<uint32_t>(bv.y) >> bs_shift);
+                const int b2 = static_cast<int16_t>(static_cast<uint32_t>(bv.z) >> bs_shift);
+                const int b3 = static_cast<int16_t>(static_cast<uint32_t>(bv.w) >> bs_shift);
+                // sum of scale * (dot - 32 * bsum) == isum - 32 * isum_mins
+                int tot = s0 * (da - 32 * b0) + s1 * (db - 32 * b1) + s2 * (dc - 32 * b2) +
+                          s3 * (dd - 32 * b3);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                const float yd = __ldg(static_cast<const float *>(job.xd) + t * job.nb + b);
+                acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, yd), static_cast<float>(tot)));
+            }
+        }
+    }
+    if (q == 0 && r < nvalid) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc[t];
+    }
+}
+
+// Q8_0 (against Q8_0 activations): 8 lanes per row, lane jj owns bytes
+// 4jj..4jj+3 of every 32-block -- the lane layout of the reference's AVX
+// tiers -- and accumulates with one FMA per block; 4 rows per pass.
+template <int NT>
+__device__ __forceinline__ void group_q8_0(const uint8_t *grp, const GemvJob &job, int row0,
+                                           int nvalid, int n_tok) {
+    const int lane = threadIdx.x & 31;
+    const int rr = lane >> 3, jj = lane & 7;
+    const uint16_t *xd = static_cast<const uint16_t *>(job.xd);
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+        const int r = pass * 4 + rr;
+        const uint8_t *row = grp + r * job.row_bytes;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        for (int b = 0; b < job.nb; ++b) {
+            const uint8_t *blk = row + b * QH_Q8_0_BYTES;
+            const int wq = static_cast<int>(lds32_a2(blk + 2 + 4 * jj));
+            const float dw = h2f_bits(*reinterpret_cast<const uint16_t *>(blk));
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t < n_tok) {
+                    const int xw = __ldg(reinterpret_cast<const int *>(
+                        job.xqs + static_cast<int64_t>(t) * job.k + b * QH_QK8_0 + 4 * jj));
+                    const float dx = h2f_bits(__ldg(xd + t * job.nb + b));
+                    const int s = __dp4a(wq, xw, 0);
+                    acc[t] = __fmaf_rn(static_cast<float>(s), __fmul_rn(dw, dx), acc[t]);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (t < n_tok) {
+                float v = acc[t];
+                v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+                v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+                v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+                if (jj == 0 && r < nvalid)
+                    job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = v;
+            }
+        }
+    }
+}
+
+template <int TYPE, int NT>
+__device__ __forceinline__ void process_group(const uint8_t *grp, const GemvJob &job, int row0,
+                                              int nvalid, int n_tok) {
+    if constexpr (TYPE == QH_GGUF_Q4_K) group_q4k<NT>(grp, job, row0, nvalid, n_tok);
+    else if constexpr (TYPE == QH_GGUF_Q5_K) group_q5k<NT>(grp, job, row0, nvalid, n_tok);
+    else if constexpr (TYPE == QH_GGUF_Q6_K) group_q6k<NT>(grp, job, row0, nvalid, n_tok);
+    else group_q8_0<NT>(grp, job, row0, nvalid, n_tok);
+}
+
+// ---------------------------------------------------------------------------
+// The kernel: producer lane + 8 consumer warps over a ring of stages.
+// ---------------------------------------------------------------------------
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kGemvMaxStages;
+    int4 *meta = reinterpret_cast<int4 *>(smem + 256);  // {job, row0, nrows, byte offset}
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 512);
+    uint8_t *data = smem + kSmemHeader;
+
+    const int S = p.n_stages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    const int n_my = static_cast<int>(blockIdx.x) < p.total_tiles
+                         ? (p.total_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                         : 0;
+
+    if (warp == kConsumerWarps) {
+        if (lane != 0) return;
+        // ----- producer -----
+        int issued = 0;
+        for (int i = 0; i < n_my; ++i) {
+            if (*abort_flag) break;
+            const int s = i % S;
+            const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+            if (i >= S && !mbar_wait(&empty[s], ph ^ 1u)) {
+                report_error(p.err_flag, kDevWaitTimeout);
+                *abort_flag = 1;
+                break;
+            }
+            const int tile = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+            const int j = find_job(p, tile);
+            const GemvJob job = load_job(p, j);
+            const int row0 = (tile - job.tile_begin) * p.rows_per_tile;
+            const int nrows = min(p.rows_per_tile, job.n_rows - row0);
+            const uint8_t *g0 = job.w + static_cast<int64_t>(row0) * job.row_bytes;
+            const uint8_t *g1 = g0 + static_cast<int64_t>(nrows) * job.row_bytes;
+            const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g0) & ~uintptr_t(15));
+            const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g1) & ~uintptr_t(15));
+            uint8_t *dst = data + static_cast<int64_t>(s) * p.stage_bytes;
+            const uint32_t bulk = static_cast<uint32_t>(a1 - a0);
+            const int tail = static_cast<int>(g1 - a1);
+            for (int t = 0; t < tail; ++t) dst[bulk + t] = __ldg(a1 + t);
+            meta[s] = make_int4(j, row0, nrows, static_cast<int>(g0 - a0));
+            // Order this thread's generic-proxy shared writes before the
+            // async-proxy bulk copy that later reuses the stage.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(&full[s], bulk);
+            if (bulk) bulk_copy_g2s(dst, a0, bulk, &full[s]);
+            ++issued;
+        }
+        // Drain: wait for this CTA's own copies in flight before exiting.
+        for (int i = max(0, issued - S); i < issued; ++i)
+            if (!mbar_wait(&full[i % S], static_cast<uint32_t>(i / S) & 1u))
+                report_error(p.err_flag, kDevWaitTimeout);
+        return;
+    }
+
+    // ----- consumers -----
+    int group_base = 0;
+    for (int i = 0; i < n_my; ++i) {
+        const int s = i % S;
+        const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+        if (!mbar_wait(&full[s], ph)) {
+            report_error(p.err_flag, kDevWaitTimeout);
+            *abort_flag = 1;
+            break;
+        }
+        const int4 m = meta[s];
+        const GemvJob job = load_job(p, m.x);
+        const int ngroups = (m.z + 7) >> 3;
+        int g = warp - group_base % kConsumerWarps;
+        if (g < 0) g += kConsumerWarps;
+        const uint8_t *base = data + static_cast<int64_t>(s) * p.stage_bytes + m.w;
+        for (; g < ngroups; g += kConsumerWarps)
+            process_group<TYPE, NT>(base + static_cast<int64_t>(g) * 8 * job.row_bytes, job,
+                                    m.y + 8 * g, min(8, m.z - 8 * g), p.n_tok);
+        group_base += ngroups;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (*abort_flag) break;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: planning and launch.
+// ---------------------------------------------------------------------------
+
+cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_count,
+                      GemvParams *p, GemvGeometry *g) {
+    if (n_jobs <= 0 || n_tok < 1 || n_tok > 8 || qhf_block_bytes(type) == 0)
+        return cudaErrorInvalidValue;
+    int64_t max_row = 0, total_rows = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+        if (jobs[j].n_rows <= 0 || jobs[j].row_bytes <= 0) return cudaErrorInvalidValue;
+        max_row = std::max<int64_t>(max_row, jobs[j].row_bytes);
+        total_rows += jobs[j].n_rows;
+    }
+    const int max_ctas = 2 * sm_count;
+    // Rows per tile: a multiple of 8, at most a third of the ring, and small
+    // enough that the launch has ~2 tiles per CTA slot.
+    int64_t r_cap = (kSmemDataBudget / 3 - 32) / max_row / 8 * 8;
+    if (r_cap < 8) {
+        r_cap = (kSmemDataBudget / 2 - 32) / max_row / 8 * 8;
+        if (r_cap < 8) return cudaErrorInvalidValue;  // a row longer than ~7 KiB
+    }
+    int64_t r_bal = (total_rows / (2 * static_cast<int64_t>(max_ctas))) / 8 * 8;
+    const int64_t R = std::max<int64_t>(8, std::min<int64_t>(std::min<int64_t>(r_cap, r_bal), 64));
+    const int64_t stage_bytes = ((R * max_row + 32) + 127) / 128 * 128;
+    const int64_t stages = std::min<int64_t>(kGemvMaxStages, kSmemDataBudget / stage_bytes);
+    if (stages < 2) return cudaErrorInvalidValue;
+    int64_t tiles = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+        jobs[j].tile_begin = static_cast<int32_t>(tiles);
+        jobs[j].n_tiles = static_cast<int32_t>((jobs[j].n_rows + R - 1) / R);
+        tiles += jobs[j].n_tiles;
+    }
+    if (tiles > (1ll << 30)) return cudaErrorInvalidValue;
+    p->n_jobs = n_jobs;
+    p->total_tiles = static_cast<int32_t>(tiles);
+    p->rows_per_tile = static_cast<int32_t>(R);
+    p->n_stages = static_cast<int32_t>(stages);
+    p->stage_bytes = static_cast<int32_t>(stage_bytes);
+    p->n_tok = n_tok;
+    for (int j = 0; j < kGemvInlineJobs; ++j) p->jobs[j] = j < n_jobs ? jobs[j] : GemvJob{};
+    g->grid = static_cast<int>(std::min<int64_t>(tiles, max_ctas));
+    g->smem_bytes = static_cast<int>(kSmemHeader + stages * stage_bytes);
+    return cudaSuccess;
+}
+
+template <int TYPE, int NT>
+static cudaError_t launch_one(const GemvParams &p, const GemvGeometry &g, cudaStream_t stream) {
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemHeader + kSmemDataBudget);
+        if (e != cudaSuccess) return e;
+        attr_done[dev] = true;
+    }
+    gemv_kernel<TYPE, NT><<<g.grid, kGemvThreads, g.smem_bytes, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <int TYPE>
+static cudaError_t launch_type(const GemvParams &p, const GemvGeometry &g, cudaStream_t stream) {
+    if (p.n_tok <= 1) return launch_one<TYPE, 1>(p, g, stream);
+    if (p.n_tok <= 2) return launch_one<TYPE, 2>(p, g, stream);
+    if (p.n_tok <= 4) return launch_one<TYPE, 4>(p, g, stream);
+    return launch_one<TYPE, 8>(p, g, stream);
+}
+
+cudaError_t gemv_launch(int type, const GemvParams &p, const GemvGeometry &g, cudaStream_t stream) {
+    if (g.grid <= 0) return cudaSuccess;
+    switch (type) {
+        case QH_GGUF_Q4_K: return launch_type<QH_GGUF_Q4_K>(p, g, stream);
+        case QH_GGUF_Q5_K: return launch_type<QH_GGUF_Q5_K>(p, g, stream);
+        case QH_GGUF_Q6_K: return launch_type<QH_GGUF_Q6_K>(p, g, stream);
+        case QH_GGUF_Q8_0: return launch_type<QH_GGUF_Q8_0>(p, g, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace qh

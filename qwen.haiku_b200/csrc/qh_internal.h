@@ -1,0 +1,76 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_internal.h -- launch-side interfaces between the C-ABI layer
+// (qh_api.cu) and the kernel files. Not installed; C++ linkage.
+
+#ifndef QH_INTERNAL_H
+#define QH_INTERNAL_H
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "qh_formats.h"
+
+namespace qh {
+
+// One independent matvec (or n_tok-token matmul) in a grouped launch.
+// Activation pointers address the split layouts of qh_formats.h for the
+// job's own K: xqs int8 [n_tok][K]; xd f32 [n_tok][K/256] (Q8_K) or fp16
+// bits [n_tok][K/32] (Q8_0); xbs int16 [n_tok][K/256][16] (Q8_K only).
+struct GemvJob {
+    const uint8_t *w;
+    const int8_t *xqs;
+    const void *xd;
+    const int16_t *xbs;
+    float *out;
+    int32_t n_rows;      // N, output features
+    int32_t nb;          // blocks per row
+    int32_t row_bytes;   // nb * block bytes
+    int32_t k;           // K, input features
+    int32_t tile_begin;  // first global tile index of this job (filled by the planner)
+    int32_t n_tiles;     // tiles of this job (filled by the planner)
+};
+
+constexpr int kGemvInlineJobs = 8;
+constexpr int kGemvMaxStages = 16;
+
+struct GemvParams {
+    int32_t n_jobs;
+    int32_t total_tiles;
+    int32_t rows_per_tile;
+    int32_t n_stages;
+    int32_t stage_bytes;
+    int32_t n_tok;
+    const GemvJob *table;  // device copy of all jobs when n_jobs > kGemvInlineJobs
+    int *err_flag;         // device error word
+    GemvJob jobs[kGemvInlineJobs];
+};
+
+// Launch geometry chosen by the planner.
+struct GemvGeometry {
+    int grid;
+    int smem_bytes;
+};
+
+// Fills tile_begin/n_tiles of `jobs`, the tiling fields of `p` and the
+// launch geometry. All jobs share `type`; returns cudaErrorInvalidValue if a
+// row is too long to stage. `sm_count` is the device's multiprocessor count.
+cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_count,
+                      GemvParams *p, GemvGeometry *g);
+
+// Launches the grouped GEMV kernel for `type`; p.n_tok in [1, 8].
+cudaError_t gemv_launch(int type, const GemvParams &p, const GemvGeometry &g,
+                        cudaStream_t stream);
+
+// Activation quantizers: x fp32 [n_tok][k] -> split layouts.
+cudaError_t quantize_q8k_launch(const float *x, int64_t k, int64_t n_tok, void *q8k,
+                                cudaStream_t stream);
+cudaError_t quantize_q8_0_launch(const float *x, int64_t k, int64_t n_tok, void *q8_0,
+                                 cudaStream_t stream);
+
+// Device error word (lazily allocated per device) and its reset/read.
+int *device_error_word();
+
+}  // namespace qh
+
+#endif  // QH_INTERNAL_H

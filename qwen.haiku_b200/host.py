@@ -1,0 +1,177 @@
+# SPDX-License-Identifier: MIT
+"""Host-side mirror of the reference's matmul interface over libqh200.
+
+``matmul(gtype, w, k, out_f, x)`` is matmul_dispatch (slm/model.c:220) and
+``tensor_matmul_q4k_f32(w, out_f, k, x)`` etc. mirror slm/tensor.c:827-1033:
+same argument meaning, x is fp32 [n_tok, k], the result is fp32
+[n_tok, out_f]. Device memory comes from torch CUDA tensors (plumbing only);
+every computation is a libqh200 kernel launched on torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import (BLOCK_BYTES, BLOCK_WEIGHTS, MatvecJob, Q4_K, Q5_K, Q6_K, Q8_0, QHError, check,
+               lib)
+
+# ---------------------------------------------------------------------------
+# Synthetic inputs (host only, no GPU needed)
+# ---------------------------------------------------------------------------
+
+
+def synth_blocks(gtype: int, n_blocks: int, seed: int) -> np.ndarray:
+    out = np.empty(n_blocks * BLOCK_BYTES[gtype], dtype=np.uint8)
+    check(lib().qh_synth_blocks(gtype, n_blocks, seed, out.ctypes.data), "qh_synth_blocks")
+    return out
+
+
+def synth_normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    check(lib().qh_synth_normal(seed, n, mean, std, out.ctypes.data), "qh_synth_normal")
+    return out
+
+
+def synth_quantize(gtype: int, w: np.ndarray) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, k = w.shape
+    out = np.empty(rows * (k // BLOCK_WEIGHTS[gtype]) * BLOCK_BYTES[gtype], dtype=np.uint8)
+    check(lib().qh_synth_quantize(gtype, w.ctypes.data, rows, k, out.ctypes.data), "qh_synth_quantize")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Device plumbing (torch tensors as allocations, torch's stream as the stream)
+# ---------------------------------------------------------------------------
+
+
+def _torch():
+    import torch
+    if not torch.cuda.is_available():
+        raise QHError(-3, "device", "no CUDA device visible; the qh200 kernels need a B200")
+    return torch
+
+
+def stream_handle():
+    return C.c_void_p(_torch().cuda.current_stream().cuda_stream)
+
+
+def to_device(a: np.ndarray):
+    torch = _torch()
+    t = torch.from_numpy(np.ascontiguousarray(a)).to("cuda")
+    return t
+
+
+def dptr(t) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr())
+
+
+def quantize_q8k(x, k: int, n_tok: int):
+    """qh_quantize_q8k into a fresh split buffer (uint8 tensor)."""
+    torch = _torch()
+    buf = torch.zeros(int(lib().qh_q8k_bytes(k, n_tok)), dtype=torch.uint8, device="cuda")
+    check(lib().qh_quantize_q8k(dptr(x), k, n_tok, dptr(buf), stream_handle()), "qh_quantize_q8k")
+    return buf
+
+
+def quantize_q8_0(x, k: int, n_tok: int):
+    torch = _torch()
+    buf = torch.zeros(int(lib().qh_q8_0_bytes(k, n_tok)), dtype=torch.uint8, device="cuda")
+    check(lib().qh_quantize_q8_0(dptr(x), k, n_tok, dptr(buf), stream_handle()), "qh_quantize_q8_0")
+    return buf
+
+
+def unpack_q8k(buf: np.ndarray, k: int, n_tok: int):
+    """(qs int8 [n_tok,k], d f32 [n_tok,k/256], bsums int16 [n_tok,k/256,16])."""
+    L = lib()
+    nb = k // 256
+    d_off, b_off = int(L.qh_q8k_d_offset(k, n_tok)), int(L.qh_q8k_bsums_offset(k, n_tok))
+    qs = buf[: k * n_tok].view(np.int8).reshape(n_tok, k)
+    d = buf[d_off: d_off + 4 * nb * n_tok].view(np.float32).reshape(n_tok, nb)
+    bs = buf[b_off: b_off + 32 * nb * n_tok].view(np.int16).reshape(n_tok, nb, 16)
+    return qs, d, bs
+
+
+def unpack_q8_0(buf: np.ndarray, k: int, n_tok: int):
+    """(qs int8 [n_tok,k], d fp16 bits uint16 [n_tok,k/32])."""
+    nb = k // 32
+    d_off = int(lib().qh_q8_0_d_offset(k, n_tok))
+    qs = buf[: k * n_tok].view(np.int8).reshape(n_tok, k)
+    d = buf[d_off: d_off + 2 * nb * n_tok].view(np.uint16).reshape(n_tok, nb)
+    return qs, d
+
+
+def matmul(gtype: int, w, k: int, out_f: int, x, n_tok: int = None, out=None, work=None):
+    """matmul_dispatch mirror: w device GGUF blocks (k, out_f), x fp32 [n_tok, k]."""
+    torch = _torch()
+    if n_tok is None:
+        n_tok = x.numel() // k
+    if out is None:
+        out = torch.empty((n_tok, out_f), dtype=torch.float32, device="cuda")
+    need = int(lib().qh_matmul_workspace_bytes(gtype, k, n_tok))
+    if need < 0:
+        raise QHError(-2, "matmul", f"unsupported type {gtype}")
+    if work is None or work.numel() < need:
+        work = torch.empty(need, dtype=torch.uint8, device="cuda")
+    check(lib().qh_matmul(gtype, dptr(w), k, out_f, dptr(x), n_tok, dptr(out), dptr(work),
+                          work.numel(), stream_handle()), "qh_matmul")
+    return out
+
+
+def tensor_matmul_q4k_f32(w, out_f, k, x):
+    return matmul(Q4_K, w, k, out_f, x)
+
+
+def tensor_matmul_q5k_f32(w, out_f, k, x):
+    return matmul(Q5_K, w, k, out_f, x)
+
+
+def tensor_matmul_q6k_f32(w, out_f, k, x):
+    return matmul(Q6_K, w, k, out_f, x)
+
+
+def tensor_matmul_q8_0_f32(w, out_f, k, x):
+    return matmul(Q8_0, w, k, out_f, x)
+
+
+class MatvecPlan:
+    """Grouped matvec plan over device buffers.
+
+    jobs = [(w, xq, out, k, out_f)] or [(w, xq, out, k, out_f, xq_rows, xq_row0)]
+    where xq is a split activation buffer quantized for xq_rows rows and the
+    job uses rows [xq_row0, xq_row0 + n_tok).
+    """
+
+    def __init__(self, gtype: int, jobs, n_tok: int = 1):
+        arr = (MatvecJob * len(jobs))()
+        for i, job in enumerate(jobs):
+            w, xq, out, k, out_f = job[:5]
+            rows, row0 = (job[5], job[6]) if len(job) > 5 else (0, 0)
+            arr[i] = MatvecJob(w.data_ptr(), xq.data_ptr(), out.data_ptr(), k, out_f, rows, row0)
+        self._keep = jobs
+        h = C.c_void_p()
+        check(lib().qh_matvec_plan_create(gtype, arr, len(jobs), n_tok, C.byref(h)),
+              "qh_matvec_plan_create")
+        self.handle = h
+
+    def run(self, stream=None):
+        check(lib().qh_matvec_plan_run(self.handle, stream if stream is not None else stream_handle()),
+              "qh_matvec_plan_run")
+
+    def info(self):
+        r, s, g, m = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        check(lib().qh_matvec_plan_info(self.handle, C.byref(r), C.byref(s), C.byref(g), C.byref(m)),
+              "qh_matvec_plan_info")
+        return {"rows_per_tile": r.value, "stages": s.value, "grid": g.value, "smem": m.value}
+
+    def close(self):
+        if self.handle:
+            lib().qh_matvec_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
