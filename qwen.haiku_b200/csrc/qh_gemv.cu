@@ -125,13 +125,16 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
             const int dc = dot16(wc[0], wc[1], wc[2], wc[3], xc, 0);
             const int dd = dot16(wd[0], wd[1], wd[2], wd[3], xd, 0);
             int isum = da * s.sc_a + db * s.sc_b + dc * s.sc_c + dd * s.sc_d;
-            const int16_t *bs = job.xbs + (static_cast<int64_t>(t) * job.nb + b) * 16 + 4 * j0;
-            const int2 bl = __ldg(reinterpret_cast<const int2 *>(bs));
-            const int2 bh = __ldg(reinterpret_cast<const int2 *>(bs + 8));
-            int mins = __dp2a_lo(bl.x, s.mins_ab, 0);
-            mins = __dp2a_hi(bl.y, s.mins_ab, mins);
-            mins = __dp2a_lo(bh.x, s.mins_cd, mins);
-            mins = __dp2a_hi(bh.y, s.mins_cd, mins);
+            // Lanes q and q^1 share the four sub-blocks (each holds 16 of their
+            // 32 weights), so the min terms are split between them: the lane
+            // with r0 == 0 takes sub-blocks 2j0, 2j0+1 (bsum pairs at 4j0),
+            // the other 2j0+4, 2j0+5 (bsum pairs at 4j0+8).
+            const int hi = r0 >> 4;
+            const int2 bp = __ldg(reinterpret_cast<const int2 *>(
+                job.xbs + (static_cast<int64_t>(t) * job.nb + b) * 16 + 4 * j0 + 8 * hi));
+            const int msel = hi ? s.mins_cd : s.mins_ab;
+            int mins = __dp2a_lo(bp.x, msel, 0);
+            mins = __dp2a_hi(bp.y, msel, mins);
             isum += __shfl_xor_sync(0xffffffffu, isum, 1);
             mins += __shfl_xor_sync(0xffffffffu, mins, 1);
             isum += __shfl_xor_sync(0xffffffffu, isum, 2);
