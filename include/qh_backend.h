@@ -134,6 +134,22 @@ int qh_matmul_q8_0_f32(const void *d_w, int64_t out_f, int64_t k, const float *d
                        int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes,
                        void *stream);
 
+/* No counterpart in the reference (its CPU matmuls take their scratch from
+ * the context arena). Same computation and results as qh_matmul_q4k_f32,
+ * for callers that are not allowed to allocate device memory -- e.g. a host
+ * that reserves all device memory in its own pool at start-up, or a service
+ * that forbids cudaMalloc after initialization because an allocation can
+ * synchronize the device. It needs no workspace: the quantized activation
+ * rows go to a fixed 128 KiB device array inside this library (every GPU
+ * that loads the library holds it until exit); shapes needing more than
+ * 131,072 - 256 bytes of activation scratch (qh_q8k_bytes(k, n_tok)) are
+ * rejected with QH_ERR_WORKSPACE. Calls allocate nothing. All calls share
+ * the array, so calls whose work overlaps on the GPU race: serialize them on
+ * one stream. The first call on each device (with that device current)
+ * looks up the array's device address; make it before any stream capture. */
+int qh_matmul_q4k_f32_noalloc(const void *d_w, int64_t out_f, int64_t k, const float *d_x,
+                              int64_t n_tok, float *d_out, void *stream);
+
 /* matmul_dispatch (slm/model.c:220): dispatch on the GGUF weight type with
  * the GGUF shape order (k = shape[0], out_f = shape[1]). */
 int qh_matmul(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x,

@@ -76,6 +76,7 @@ SIGNATURES = {
     "qh_matmul_q5k_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_matmul_q6k_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_matmul_q8_0_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qh_matmul_q4k_f32_noalloc": (_I, [_P, _I64, _I64, _P, _I64, _P, _P]),
     "qh_matmul": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_matmul_preq": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P]),
     "qh_matvec_plan_create": (_I, [_I, C.POINTER(MatvecJob), _I, _I64, C.POINTER(C.c_void_p)]),

@@ -149,6 +149,8 @@ int matmul_impl(int type, const void *d_w, int64_t k, int64_t out_f, const float
 }  // namespace
 
 namespace qh {
+void set_last_error_message(const char *msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
+
 int *device_error_word() {
     int *w = nullptr;
     device_state(nullptr, &w);

@@ -71,6 +71,9 @@ cudaError_t quantize_q8_0_launch(const float *x, int64_t k, int64_t n_tok, void 
 // Device error word (lazily allocated per device) and its reset/read.
 int *device_error_word();
 
+// Sets the calling thread's qh_last_error() message.
+void set_last_error_message(const char *msg);
+
 }  // namespace qh
 
 #endif  // QH_INTERNAL_H

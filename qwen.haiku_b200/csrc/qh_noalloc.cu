@@ -1,0 +1,141 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_noalloc.cu -- qh_matmul_q4k_f32_noalloc: the Q4_K matmul (activation
+// quantization + grouped matvec kernel) for callers that may not allocate
+// device memory.
+//
+// Who needs it: some host programs own every byte of device memory
+// themselves -- an application that carves all buffers out of one pool it
+// reserved at start-up, or a latency-critical service that forbids any
+// cudaMalloc after initialization because an allocation can synchronize
+// the device and stall its other streams. Such a caller can hand us its
+// weights, input and output buffers, but it cannot give us (or let us
+// create) the extra device buffer that holds the quantized activation rows.
+// This entry point keeps that buffer in a fixed, file-scope device array
+// instead, so it allocates nothing.
+//
+// Costs and rules of the fixed array:
+//   * Every GPU that loads this library holds kNoallocScratchBytes of it
+//     until the process exits, whether or not this entry point is called.
+//   * All calls share it and it keeps the last call's contents, so two calls
+//     whose work overlaps on the GPU (different streams, or different host
+//     threads on one device) race on it. Serialize them on one stream.
+//   * The quantized rows are rewritten completely by every call; the only
+//     part that must start at zero -- the kernel error word in the first
+//     256 bytes -- is cleared on the caller's stream at the start of each
+//     call.
+//   * Host code cannot use the array's name as a device address, so the
+//     first call on each device (with that device current) looks the
+//     address up with cudaGetSymbolAddress and caches it. Make that first
+//     call before starting any stream capture on that device.
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "../../include/qh_backend.h"
+#include "qh_internal.h"
+
+namespace {
+
+// 256 bytes of control (the error word) followed by the quantized activation
+// rows. 128 KiB holds e.g. 112 rows of k = 1024 or 35 rows of k = 3584.
+constexpr int64_t kNoallocScratchBytes = 128 * 1024;
+constexpr int64_t kNoallocControlBytes = 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+void *g_scratch_addr[kMaxDevices] = {nullptr};
+int g_sms[kMaxDevices] = {0};
+
+thread_local char g_msg[256];
+
+int noalloc_fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    qh::set_last_error_message(g_msg);
+    return code;
+}
+
+// Once per device, with that device current: resolve the array's device
+// address and read the SM count. Allocates nothing.
+int noalloc_setup(void **scratch, int *sms) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return noalloc_fail(QH_ERR_INVALID, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_scratch_addr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return noalloc_fail(QH_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        int n = 0;
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess)
+            return noalloc_fail(QH_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+        g_sms[dev] = n;
+        g_scratch_addr[dev] = p;
+    }
+    *scratch = g_scratch_addr[dev];
+    *sms = g_sms[dev];
+    return QH_OK;
+}
+
+}  // namespace
+
+extern "C" int qh_matmul_q4k_f32_noalloc(const void *d_w, int64_t out_f, int64_t k, const float *d_x,
+                                         int64_t n_tok, float *d_out, void *stream) {
+    if (!d_w || !d_x || !d_out) return noalloc_fail(QH_ERR_INVALID, "null pointer");
+    if (k <= 0 || k % QH_QK || out_f <= 0 || out_f > (1ll << 30) || n_tok <= 0)
+        return noalloc_fail(QH_ERR_INVALID, "bad shape k=%lld out_f=%lld n_tok=%lld", (long long)k,
+                            (long long)out_f, (long long)n_tok);
+    if (reinterpret_cast<uintptr_t>(d_w) & 15) return noalloc_fail(QH_ERR_ALIGN, "weights not 16-byte aligned");
+    const int64_t need = qhf_q8k_total_bytes(k, n_tok);
+    if (need > kNoallocScratchBytes - kNoallocControlBytes)
+        return noalloc_fail(QH_ERR_WORKSPACE,
+                            "k=%lld x n_tok=%lld needs %lld bytes of activation scratch; the fixed "
+                            "array holds %lld (use qh_matmul_q4k_f32 with a workspace)",
+                            (long long)k, (long long)n_tok, (long long)need,
+                            (long long)(kNoallocScratchBytes - kNoallocControlBytes));
+    void *base = nullptr;
+    int sms = 0;
+    int rc = noalloc_setup(&base, &sms);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int *err_word = static_cast<int *>(base);
+    uint8_t *xq = static_cast<uint8_t *>(base) + kNoallocControlBytes;
+    cudaError_t e = cudaMemsetAsync(err_word, 0, sizeof(int), s);
+    if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "clear error word: %s", cudaGetErrorString(e));
+    e = qh::quantize_q8k_launch(d_x, k, n_tok, xq, s);
+    if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "quantize launch: %s", cudaGetErrorString(e));
+    const int nb = static_cast<int>(k / QH_QK);
+    for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
+        const int nt = static_cast<int>(n_tok - t0 < 8 ? n_tok - t0 : 8);
+        qh::GemvJob job{};
+        job.w = static_cast<const uint8_t *>(d_w);
+        job.k = static_cast<int32_t>(k);
+        job.nb = nb;
+        job.row_bytes = nb * QH_Q4K_BYTES;
+        job.n_rows = static_cast<int32_t>(out_f);
+        job.xqs = reinterpret_cast<const int8_t *>(xq) + t0 * k;
+        job.xd = xq + qhf_q8k_d_offset(k, n_tok) + t0 * nb * 4;
+        job.xbs = reinterpret_cast<const int16_t *>(xq + qhf_q8k_bsums_offset(k, n_tok)) + t0 * nb * 16;
+        job.out = d_out + t0 * out_f;
+        qh::GemvParams p{};
+        qh::GemvGeometry g{};
+        e = qh::gemv_plan(QH_GGUF_Q4_K, &job, 1, nt, sms, &p, &g);
+        if (e != cudaSuccess) return noalloc_fail(QH_ERR_INVALID, "cannot tile rows of k=%lld", (long long)k);
+        p.err_flag = err_word;
+        p.table = nullptr;
+        e = qh::gemv_launch(QH_GGUF_Q4_K, p, g, s);
+        if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
+    }
+    return QH_OK;
+}
