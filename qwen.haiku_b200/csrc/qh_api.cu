@@ -97,10 +97,12 @@ qh::GemvJob make_job(int type, const void *w, int64_t k, int64_t out_f, const vo
     j.n_rows = static_cast<int32_t>(out_f);
     j.xqs = reinterpret_cast<const int8_t *>(base) + t0 * k;
     if (type == QH_GGUF_Q8_0) {
-        j.xd = base + qhf_q8_0_d_offset(k, n_tok) + t0 * j.nb * 2;
+        j.d_stride = static_cast<int32_t>(qhf_q8_0_d_stride(k));
+        j.xd = base + qhf_q8_0_d_offset(k, n_tok) + t0 * j.d_stride * 2;
         j.xbs = nullptr;
     } else {
-        j.xd = base + qhf_q8k_d_offset(k, n_tok) + t0 * j.nb * 4;
+        j.d_stride = static_cast<int32_t>(qhf_q8k_d_stride(k));
+        j.xd = base + qhf_q8k_d_offset(k, n_tok) + t0 * j.d_stride * 4;
         j.xbs = reinterpret_cast<const int16_t *>(base + qhf_q8k_bsums_offset(k, n_tok)) + t0 * j.nb * 16;
     }
     j.out = out + t0 * out_f;
@@ -113,14 +115,20 @@ int run_preq(int type, const void *d_w, int64_t k, int64_t out_f, const void *d_
     int *err;
     int rc = device_state(&sms, &err);
     if (rc) return rc;
-    for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
-        const int nt = static_cast<int>(n_tok - t0 < 8 ? n_tok - t0 : 8);
-        qh::GemvJob job = make_job(type, d_w, k, out_f, d_xq, n_tok, t0, d_out);
+    int chunk = 8;  // tokens per launch; halved while a stage cannot hold them
+    for (int64_t t0 = 0; t0 < n_tok; t0 += chunk) {
         qh::GemvParams p{};
         qh::GemvGeometry g{};
-        cudaError_t e = qh::gemv_plan(type, &job, 1, nt, sms, &p, &g);
-        if (e != cudaSuccess) return fail(QH_ERR_INVALID, "matmul: cannot tile rows of %lld bytes",
-                                          (long long)qhf_row_bytes(type, k));
+        cudaError_t e;
+        for (;;) {
+            const int nt = static_cast<int>(n_tok - t0 < chunk ? n_tok - t0 : chunk);
+            qh::GemvJob job = make_job(type, d_w, k, out_f, d_xq, n_tok, t0, d_out);
+            e = qh::gemv_plan(type, &job, 1, nt, sms, &p, &g);
+            if (e == cudaSuccess || chunk == 1) break;
+            chunk >>= 1;
+        }
+        if (e != cudaSuccess) return fail(QH_ERR_INVALID, "matmul: cannot tile rows of %lld bytes (%s)",
+                                          (long long)qhf_row_bytes(type, k), cudaGetErrorString(e));
         p.err_flag = err;
         p.table = nullptr;
         e = qh::gemv_launch(type, p, g, s);
@@ -335,7 +343,7 @@ int qh_matvec_plan_create(int type, const qh_matvec_job *h_jobs, int n_jobs, int
     cudaError_t e = qh::gemv_plan(type, jobs.data(), n_jobs, static_cast<int>(n_tok), sms, &p->params, &p->geom);
     if (e != cudaSuccess) {
         delete p;
-        return fail(QH_ERR_INVALID, "plan_create: cannot tile these rows");
+        return fail(QH_ERR_INVALID, "plan_create: cannot tile these rows (%s)", cudaGetErrorString(e));
     }
     p->params.err_flag = err;
     p->params.table = nullptr;

@@ -78,23 +78,27 @@ static inline QH_HD int64_t qhf_row_bytes(int type, int64_t k) {
     return (k / qhf_block_weights(type)) * qhf_block_bytes(type);
 }
 
-// Q8_K split activation layout.
+// Q8_K split activation layout. The per-token scale row is padded to a
+// multiple of 4 floats (16 bytes) so every plane of a row range is a
+// 16-byte-aligned contiguous span (bulk-copyable).
+static inline QH_HD int64_t qhf_q8k_d_stride(int64_t k) { return ((k / QH_QK) + 3) & ~(int64_t)3; }
 static inline QH_HD int64_t qhf_q8k_d_offset(int64_t k, int64_t n_tok) {
     return qhf_align16(k * n_tok);
 }
 static inline QH_HD int64_t qhf_q8k_bsums_offset(int64_t k, int64_t n_tok) {
-    return qhf_align16(qhf_q8k_d_offset(k, n_tok) + (k / QH_QK) * n_tok * 4);
+    return qhf_align16(qhf_q8k_d_offset(k, n_tok) + qhf_q8k_d_stride(k) * n_tok * 4);
 }
 static inline QH_HD int64_t qhf_q8k_total_bytes(int64_t k, int64_t n_tok) {
     return qhf_align16(qhf_q8k_bsums_offset(k, n_tok) + (k / 16) * n_tok * 2);
 }
 
-// Q8_0 split activation layout.
+// Q8_0 split activation layout; fp16 scale rows padded to 8 halves (16 bytes).
+static inline QH_HD int64_t qhf_q8_0_d_stride(int64_t k) { return ((k / QH_QK8_0) + 7) & ~(int64_t)7; }
 static inline QH_HD int64_t qhf_q8_0_d_offset(int64_t k, int64_t n_tok) {
     return qhf_align16(k * n_tok);
 }
 static inline QH_HD int64_t qhf_q8_0_total_bytes(int64_t k, int64_t n_tok) {
-    return qhf_align16(qhf_q8_0_d_offset(k, n_tok) + (k / QH_QK8_0) * n_tok * 2);
+    return qhf_align16(qhf_q8_0_d_offset(k, n_tok) + qhf_q8_0_d_stride(k) * n_tok * 2);
 }
 
 #endif  // QH_FORMATS_H

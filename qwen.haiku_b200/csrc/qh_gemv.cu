@@ -37,10 +37,18 @@ namespace qh {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kGemvThreads = 32 * (kConsumerWarps + 1);
-// Shared memory per CTA: 1 KiB of barriers/metadata + the stage ring. Two
-// CTAs fit on one SM (228 KiB per SM, 1 KiB reserved per CTA).
-constexpr int kSmemHeader = 1024;
-constexpr int kSmemDataBudget = 112 * 1024;
+// Shared memory per CTA: 2 KiB of barriers/stage metadata + the stage ring.
+// Two CTAs fit on one SM (228 KiB per SM, 1 KiB reserved per CTA).
+constexpr int kSmemHeader = 2048;
+constexpr int kSmemDataBudget = 110 * 1024;  // per CTA at 2 CTAs/SM
+
+// Per-stage metadata written by the producer: the tile's job descriptor
+// (so consumers never touch the global job table) and its row range.
+struct StageMeta {
+    GemvJob job;
+    int32_t row0, nrows, offset, pad;
+};
+static_assert(sizeof(StageMeta) <= 96, "stage metadata slot");
 
 __device__ __forceinline__ GemvJob load_job(const GemvParams &p, int j) {
     return p.n_jobs <= kGemvInlineJobs ? p.jobs[j] : p.table[j];
@@ -67,6 +75,27 @@ __device__ __forceinline__ int find_job(const GemvParams &p, int tile) {
 // `grp` in shared memory (row stride = job.row_bytes). Lanes: r = lane/4 is
 // the row, q = lane%4 a quarter of every super-block.
 // ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                     const int4 &x, int acc) {
+    acc = __dp4a(static_cast<int>(w0), x.x, acc);
+    acc = __dp4a(static_cast<int>(w1), x.y, acc);
+    acc = __dp4a(static_cast<int>(w2), x.z, acc);
+    acc = __dp4a(static_cast<int>(w3), x.w, acc);
+    return acc;
+}
+
+// The job's activation planes as staged in shared memory next to the
+// weight tile (same split layout as in global memory, rows [t0, t0+n_tok)).
+struct XView {
+    const int8_t *qs;   // [n_tok][k]
+    const int16_t *bs;  // [n_tok][nb][16]   (Q8_K only)
+    const uint8_t *d;   // [n_tok][d_stride] f32 (Q8_K) or fp16 bits (Q8_0)
+};
+
+__device__ __forceinline__ int4 lds128i(const int8_t *p) {
+    return *reinterpret_cast<const int4 *>(p);
+}
 
 // Unpacked 6-bit scales/mins of the four sub-blocks a lane covers in a
 // Q4_K/Q5_K super-block (simd/quants.h:215-224). With j0 = q/2 the lane
@@ -95,31 +124,22 @@ __device__ __forceinline__ KScales unpack_kscales(const uint4 &h, uint32_t sh) {
     return s;
 }
 
-__device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
-                                     const int4 &x, int acc) {
-    acc = __dp4a(static_cast<int>(w0), x.x, acc);
-    acc = __dp4a(static_cast<int>(w1), x.y, acc);
-    acc = __dp4a(static_cast<int>(w2), x.z, acc);
-    acc = __dp4a(static_cast<int>(w3), x.w, acc);
-    return acc;
-}
-
 // Shared tail of Q4_K/Q5_K: integer dots with the four activation slices,
 // scale, mins via dp2a, 4-lane reduction, fp32 combination.
 template <int NT>
 __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const uint32_t (&wb)[4],
                                                   const uint32_t (&wc)[4], const uint32_t (&wd)[4],
                                                   const KScales &s, float dw, float dmw,
-                                                  const GemvJob &job, int b, int j0, int r0,
-                                                  int n_tok, float (&acc)[NT]) {
+                                                  const GemvJob &job, const XView &x, int b, int j0,
+                                                  int r0, int n_tok, float (&acc)[NT]) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
         if (t < n_tok) {
-            const int8_t *xq = job.xqs + static_cast<int64_t>(t) * job.k + b * QH_QK + 64 * j0 + r0;
-            const int4 xa = ldg128(xq);
-            const int4 xb = ldg128(xq + 32);
-            const int4 xc = ldg128(xq + 128);
-            const int4 xd = ldg128(xq + 160);
+            const int8_t *xq = x.qs + t * job.k + b * QH_QK + 64 * j0 + r0;
+            const int4 xa = lds128i(xq);
+            const int4 xb = lds128i(xq + 32);
+            const int4 xc = lds128i(xq + 128);
+            const int4 xd = lds128i(xq + 160);
             const int da = dot16(wa[0], wa[1], wa[2], wa[3], xa, 0);
             const int db = dot16(wb[0], wb[1], wb[2], wb[3], xb, 0);
             const int dc = dot16(wc[0], wc[1], wc[2], wc[3], xc, 0);
@@ -130,8 +150,7 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
             // with r0 == 0 takes sub-blocks 2j0, 2j0+1 (bsum pairs at 4j0),
             // the other 2j0+4, 2j0+5 (bsum pairs at 4j0+8).
             const int hi = r0 >> 4;
-            const int2 bp = __ldg(reinterpret_cast<const int2 *>(
-                job.xbs + (static_cast<int64_t>(t) * job.nb + b) * 16 + 4 * j0 + 8 * hi));
+            const int2 bp = *reinterpret_cast<const int2 *>(x.bs + (t * job.nb + b) * 16 + 4 * j0 + 8 * hi);
             const int msel = hi ? s.mins_cd : s.mins_ab;
             int mins = __dp2a_lo(bp.x, msel, 0);
             mins = __dp2a_hi(bp.y, msel, mins);
@@ -139,7 +158,7 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
             mins += __shfl_xor_sync(0xffffffffu, mins, 1);
             isum += __shfl_xor_sync(0xffffffffu, isum, 2);
             mins += __shfl_xor_sync(0xffffffffu, mins, 2);
-            const float yd = __ldg(static_cast<const float *>(job.xd) + t * job.nb + b);
+            const float yd = reinterpret_cast<const float *>(x.d)[t * job.d_stride + b];
             const float d = __fmul_rn(yd, dw);
             const float dmin = __fmul_rn(yd, dmw);
             acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d, static_cast<float>(isum)),
@@ -149,11 +168,11 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
 }
 
 template <int NT>
-__device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job, int row0,
+__device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
                                           int nvalid, int n_tok) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, q = lane & 3, j0 = q >> 1, r0 = (q & 1) << 4;
-    const uint8_t *row = grp + r * job.row_bytes;
+    const uint8_t *row = grp + r * job.box_pitch;
     const uint32_t sh = 16u * static_cast<uint32_t>(j0);
     float acc[NT];
 #pragma unroll
@@ -169,7 +188,7 @@ __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job
         const uint32_t wb[4] = {(qa.x >> 4) & m4, (qa.y >> 4) & m4, (qa.z >> 4) & m4, (qa.w >> 4) & m4};
         const uint32_t wc[4] = {qc.x & m4, qc.y & m4, qc.z & m4, qc.w & m4};
         const uint32_t wd[4] = {(qc.x >> 4) & m4, (qc.y >> 4) & m4, (qc.z >> 4) & m4, (qc.w >> 4) & m4};
-        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, b, j0,
+        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, x, b, j0,
                               r0, n_tok, acc);
     }
     if (q == 0 && r < nvalid) {
@@ -180,11 +199,11 @@ __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job
 }
 
 template <int NT>
-__device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job, int row0,
+__device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
                                           int nvalid, int n_tok) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, q = lane & 3, j0 = q >> 1, r0 = (q & 1) << 4;
-    const uint8_t *row = grp + r * job.row_bytes;
+    const uint8_t *row = grp + r * job.box_pitch;
     const uint32_t sh = 16u * static_cast<uint32_t>(j0);
     // 5th bit of sub-block s sits in bit s of qh[l]; move it to bit 4.
     const uint32_t up_a = 4u - 2u * j0, up_b = 3u - 2u * j0;  // s = 2j0, 2j0+1
@@ -211,7 +230,7 @@ __device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job
             wc[i] = (lc[i] & m4) | ((qh[i] >> dn_c) & b4);
             wd[i] = ((lc[i] >> 4) & m4) | ((qh[i] >> dn_d) & b4);
         }
-        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, b, j0,
+        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, x, b, j0,
                               r0, n_tok, acc);
     }
     if (q == 0 && r < nvalid) {
@@ -221,16 +240,12 @@ __device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job
     }
 }
 
-// Q6_K: lane q covers half n = q/2 of the super-block and 16 positions
-// l0 = 16*(q%2) inside each of its four 32-wide quarters, i.e. the
-// 16-wide sub-blocks 8n + q%2 + {0,2,4,6}. Blocks are 210 bytes, so rows
-// and blocks are only 2-byte aligned in shared memory.
 template <int NT>
-__device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job, int row0,
+__device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
                                           int nvalid, int n_tok) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, q = lane & 3, n = q >> 1, l0 = (q & 1) << 4;
-    const uint8_t *row = grp + r * job.row_bytes;
+    const uint8_t *row = grp + r * job.box_pitch;
     const uint32_t bs_shift = 16u * static_cast<uint32_t>(q & 1);
     float acc[NT];
 #pragma unroll
@@ -258,12 +273,12 @@ __device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             if (t < n_tok) {
-                const int8_t *xq = job.xqs + static_cast<int64_t>(t) * job.k + b * QH_QK + 128 * n + l0;
-                const int da = dot16(wa[0], wa[1], wa[2], wa[3], ldg128(xq), 0);
-                const int db = dot16(wb[0], wb[1], wb[2], wb[3], ldg128(xq + 32), 0);
-                const int dc = dot16(wc[0], wc[1], wc[2], wc[3], ldg128(xq + 64), 0);
-                const int dd = dot16(wd[0], wd[1], wd[2], wd[3], ldg128(xq + 96), 0);
-                const int4 bv = ldg128(job.xbs + (static_cast<int64_t>(t) * job.nb + b) * 16 + 8 * n);
+                const int8_t *xq = x.qs + t * job.k + b * QH_QK + 128 * n + l0;
+                const int da = dot16(wa[0], wa[1], wa[2], wa[3], lds128i(xq), 0);
+                const int db = dot16(wb[0], wb[1], wb[2], wb[3], lds128i(xq + 32), 0);
+                const int dc = dot16(wc[0], wc[1], wc[2], wc[3], lds128i(xq + 64), 0);
+                const int dd = dot16(wd[0], wd[1], wd[2], wd[3], lds128i(xq + 96), 0);
+                const int4 bv = *reinterpret_cast<const int4 *>(x.bs + (t * job.nb + b) * 16 + 8 * n);
                 const int b0 = static_cast<int16_t>(static_cast<uint32_t>(bv.x) >> bs_shift);
                 const int b1 = static_cast<int16_t>(static_cast<uint32_t>(bv.y) >> bs_shift);
                 const int b2 = static_cast<int16_t>(static_cast<uint32_t>(bv.z) >> bs_shift);
@@ -273,7 +288,7 @@ __device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job
                           s3 * (dd - 32 * b3);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 1);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 2);
-                const float yd = __ldg(static_cast<const float *>(job.xd) + t * job.nb + b);
+                const float yd = reinterpret_cast<const float *>(x.d)[t * job.d_stride + b];
                 acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, yd), static_cast<float>(tot)));
             }
         }
@@ -289,15 +304,15 @@ __device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job
 // 4jj..4jj+3 of every 32-block -- the lane layout of the reference's AVX
 // tiers -- and accumulates with one FMA per block; 4 rows per pass.
 template <int NT>
-__device__ __forceinline__ void group_q8_0(const uint8_t *grp, const GemvJob &job, int row0,
+__device__ __forceinline__ void group_q8_0(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
                                            int nvalid, int n_tok) {
     const int lane = threadIdx.x & 31;
     const int rr = lane >> 3, jj = lane & 7;
-    const uint16_t *xd = static_cast<const uint16_t *>(job.xd);
+    const uint16_t *xd = reinterpret_cast<const uint16_t *>(x.d);
 #pragma unroll 1
     for (int pass = 0; pass < 2; ++pass) {
         const int r = pass * 4 + rr;
-        const uint8_t *row = grp + r * job.row_bytes;
+        const uint8_t *row = grp + r * job.box_pitch;
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
@@ -308,9 +323,8 @@ __device__ __forceinline__ void group_q8_0(const uint8_t *grp, const GemvJob &jo
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (t < n_tok) {
-                    const int xw = __ldg(reinterpret_cast<const int *>(
-                        job.xqs + static_cast<int64_t>(t) * job.k + b * QH_QK8_0 + 4 * jj));
-                    const float dx = h2f_bits(__ldg(xd + t * job.nb + b));
+                    const int xw = *reinterpret_cast<const int *>(x.qs + t * job.k + b * QH_QK8_0 + 4 * jj);
+                    const float dx = h2f_bits(xd[t * job.d_stride + b]);
                     const int s = __dp4a(wq, xw, 0);
                     acc[t] = __fmaf_rn(static_cast<float>(s), __fmul_rn(dw, dx), acc[t]);
                 }
@@ -331,12 +345,25 @@ __device__ __forceinline__ void group_q8_0(const uint8_t *grp, const GemvJob &jo
 }
 
 template <int TYPE, int NT>
-__device__ __forceinline__ void process_group(const uint8_t *grp, const GemvJob &job, int row0,
-                                              int nvalid, int n_tok) {
-    if constexpr (TYPE == QH_GGUF_Q4_K) group_q4k<NT>(grp, job, row0, nvalid, n_tok);
-    else if constexpr (TYPE == QH_GGUF_Q5_K) group_q5k<NT>(grp, job, row0, nvalid, n_tok);
-    else if constexpr (TYPE == QH_GGUF_Q6_K) group_q6k<NT>(grp, job, row0, nvalid, n_tok);
-    else group_q8_0<NT>(grp, job, row0, nvalid, n_tok);
+__device__ __forceinline__ void process_group(const uint8_t *wbase, int tile_rows, int trow,
+                                              const GemvJob &job, const XView &x, int row0, int nvalid,
+                                              int n_tok) {
+    const uint8_t *grp = wbase + trow * job.box_pitch;
+    if constexpr (TYPE == QH_GGUF_Q4_K) group_q4k<NT>(grp, job, x, row0, nvalid, n_tok);
+    else if constexpr (TYPE == QH_GGUF_Q5_K) group_q5k<NT>(grp, job, x, row0, nvalid, n_tok);
+    else if constexpr (TYPE == QH_GGUF_Q6_K) group_q6k<NT>(grp, job, x, row0, nvalid, n_tok);
+    else group_q8_0<NT>(grp, job, x, row0, nvalid, n_tok);
+}
+
+// Rows per consumer work unit: 8 rows of 4 lanes each.
+constexpr int kGroupRows = 8;
+
+// Bytes of the staged activation planes of one job (n_tok rows).
+__host__ __device__ __forceinline__ void x_plane_bytes(int type, const GemvJob &job, int n_tok,
+                                                       uint32_t *qs, uint32_t *bs, uint32_t *d) {
+    *qs = static_cast<uint32_t>(n_tok) * static_cast<uint32_t>(job.k);
+    *bs = type == QH_GGUF_Q8_0 ? 0u : static_cast<uint32_t>(n_tok * job.nb * 32);
+    *d = static_cast<uint32_t>(n_tok * job.d_stride * (type == QH_GGUF_Q8_0 ? 2 : 4));
 }
 
 // ---------------------------------------------------------------------------
@@ -347,9 +374,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kGemvMaxStages;
-    int4 *meta = reinterpret_cast<int4 *>(smem + 256);  // {job, row0, nrows, byte offset}
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 512);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 256);
+    StageMeta *meta = reinterpret_cast<StageMeta *>(smem + 384);  // kGemvMaxStages x 96 B
     uint8_t *data = smem + kSmemHeader;
+    constexpr int GR = kGroupRows;
 
     const int S = p.n_stages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -363,47 +391,69 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
     __syncthreads();
 
-    const int n_my = static_cast<int>(blockIdx.x) < p.total_tiles
-                         ? (p.total_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
-                         : 0;
+    // Each CTA streams one contiguous range of tiles (sequential addresses,
+    // jobs visited in order).
+    const int t_begin = static_cast<int>(static_cast<int64_t>(p.total_tiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(p.total_tiles) * (blockIdx.x + 1) / gridDim.x);
+    const int n_my = t_end - t_begin;
 
     if (warp == kConsumerWarps) {
-        if (lane != 0) return;
-        // ----- producer -----
+        // ----- producer warp (uniform control flow; lane 0 owns the barriers) -----
         int issued = 0;
+        int j = n_my > 0 ? find_job(p, t_begin) : 0;
+        GemvJob job = load_job(p, j);
         for (int i = 0; i < n_my; ++i) {
-            if (*abort_flag) break;
+            // Every decision that ends the loop is made warp-uniform, so the
+            // __syncwarp below never waits for a lane that has left.
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
             const int s = i % S;
             const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-            if (i >= S && !mbar_wait(&empty[s], ph ^ 1u)) {
-                report_error(p.err_flag, kDevWaitTimeout);
-                *abort_flag = 1;
+            const bool ok = __all_sync(0xffffffffu, i < S || mbar_wait(&empty[s], ph ^ 1u));
+            if (!ok) {
+                if (lane == 0) {
+                    report_error(p.err_flag, kDevWaitTimeout);
+                    *abort_flag = 1;
+                }
                 break;
             }
-            const int tile = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
-            const int j = find_job(p, tile);
-            const GemvJob job = load_job(p, j);
+            const int tile = t_begin + i;
+            while (tile >= job.tile_begin + job.n_tiles && j + 1 < p.n_jobs) job = load_job(p, ++j);
             const int row0 = (tile - job.tile_begin) * p.rows_per_tile;
             const int nrows = min(p.rows_per_tile, job.n_rows - row0);
             const uint8_t *g0 = job.w + static_cast<int64_t>(row0) * job.row_bytes;
+            uint8_t *dst = data + static_cast<int64_t>(s) * p.stage_bytes;
+            uint32_t xq_b, xb_b, xd_b;
+            x_plane_bytes(TYPE, job, p.n_tok, &xq_b, &xb_b, &xd_b);
+            uint8_t *xdst = dst + p.x_offset;
             const uint8_t *g1 = g0 + static_cast<int64_t>(nrows) * job.row_bytes;
             const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g0) & ~uintptr_t(15));
             const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g1) & ~uintptr_t(15));
-            uint8_t *dst = data + static_cast<int64_t>(s) * p.stage_bytes;
-            const uint32_t bulk = static_cast<uint32_t>(a1 - a0);
-            const int tail = static_cast<int>(g1 - a1);
-            for (int t = 0; t < tail; ++t) dst[bulk + t] = __ldg(a1 + t);
-            meta[s] = make_int4(j, row0, nrows, static_cast<int>(g0 - a0));
-            // Order this thread's generic-proxy shared writes before the
-            // async-proxy bulk copy that later reuses the stage.
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive_expect_tx(&full[s], bulk);
-            if (bulk) bulk_copy_g2s(dst, a0, bulk, &full[s]);
+            const uint32_t wbytes = static_cast<uint32_t>(a1 - a0);
+            const int offset = static_cast<int>(g0 - a0);
+            if (lane == 0)
+                for (int t = 0; t < static_cast<int>(g1 - a1); ++t) dst[wbytes + t] = __ldg(a1 + t);
+            if (lane == 0) {
+                meta[s].job = job;
+                meta[s].row0 = row0;
+                meta[s].nrows = nrows;
+                meta[s].offset = offset;
+                // Order this thread's generic-proxy shared writes before the
+                // async-proxy bulk copies that later reuse the stage.
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&full[s], wbytes + xq_b + xb_b + xd_b);
+            }
+            __syncwarp();
+            if (lane == 0 && wbytes) bulk_copy_g2s(dst, a0, wbytes, &full[s]);
+            if (lane == 0) {
+                bulk_copy_g2s(xdst, job.xqs, xq_b, &full[s]);
+                if (xb_b) bulk_copy_g2s(xdst + xq_b, job.xbs, xb_b, &full[s]);
+                bulk_copy_g2s(xdst + xq_b + xb_b, job.xd, xd_b, &full[s]);
+            }
             ++issued;
         }
-        // Drain: wait for this CTA's own copies in flight before exiting.
+        // Drain: wait for this CTA's copies in flight before exiting.
         for (int i = max(0, issued - S); i < issued; ++i)
-            if (!mbar_wait(&full[i % S], static_cast<uint32_t>(i / S) & 1u))
+            if (!mbar_wait(&full[i % S], static_cast<uint32_t>(i / S) & 1u) && lane == 0)
                 report_error(p.err_flag, kDevWaitTimeout);
         return;
     }
@@ -418,15 +468,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             *abort_flag = 1;
             break;
         }
-        const int4 m = meta[s];
-        const GemvJob job = load_job(p, m.x);
-        const int ngroups = (m.z + 7) >> 3;
+        const GemvJob job = meta[s].job;
+        const int row0 = meta[s].row0, nrows = meta[s].nrows;
+        const int ngroups = (nrows + GR - 1) / GR;
         int g = warp - group_base % kConsumerWarps;
         if (g < 0) g += kConsumerWarps;
-        const uint8_t *base = data + static_cast<int64_t>(s) * p.stage_bytes + m.w;
+        const uint8_t *stage = data + static_cast<int64_t>(s) * p.stage_bytes;
+        const uint8_t *base = stage + meta[s].offset;
+        XView x;
+        x.qs = reinterpret_cast<const int8_t *>(stage + p.x_offset);
+        x.bs = reinterpret_cast<const int16_t *>(stage + p.x_offset + p.n_tok * job.k);
+        x.d = stage + p.x_offset + p.n_tok * job.k + (TYPE == QH_GGUF_Q8_0 ? 0 : p.n_tok * job.nb * 32);
         for (; g < ngroups; g += kConsumerWarps)
-            process_group<TYPE, NT>(base + static_cast<int64_t>(g) * 8 * job.row_bytes, job,
-                                    m.y + 8 * g, min(8, m.z - 8 * g), p.n_tok);
+            process_group<TYPE, NT>(base, p.rows_per_tile, GR * g, job, x, row0 + GR * g,
+                                    min(GR, nrows - GR * g), p.n_tok);
         group_base += ngroups;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -442,25 +497,33 @@ cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_cou
                       GemvParams *p, GemvGeometry *g) {
     if (n_jobs <= 0 || n_tok < 1 || n_tok > 8 || qhf_block_bytes(type) == 0)
         return cudaErrorInvalidValue;
-    int64_t max_row = 0, total_rows = 0;
+    const int GR = kGroupRows;
+    int64_t max_pitch = 0, total_rows = 0, max_x = 0;
     for (int j = 0; j < n_jobs; ++j) {
         if (jobs[j].n_rows <= 0 || jobs[j].row_bytes <= 0) return cudaErrorInvalidValue;
-        max_row = std::max<int64_t>(max_row, jobs[j].row_bytes);
+        jobs[j].box_blocks = jobs[j].nb;
+        jobs[j].box_pitch = jobs[j].row_bytes;
+        max_pitch = std::max<int64_t>(max_pitch, jobs[j].row_bytes);
         total_rows += jobs[j].n_rows;
+        uint32_t a, b, c;
+        x_plane_bytes(type, jobs[j], n_tok, &a, &b, &c);
+        max_x = std::max<int64_t>(max_x, static_cast<int64_t>(a) + b + c);
     }
+    const int64_t budget = kSmemDataBudget;
     const int max_ctas = 2 * sm_count;
-    // Rows per tile: a multiple of 8, at most a third of the ring, and small
-    // enough that the launch has ~2 tiles per CTA slot.
-    int64_t r_cap = (kSmemDataBudget / 3 - 32) / max_row / 8 * 8;
-    if (r_cap < 8) {
-        r_cap = (kSmemDataBudget / 2 - 32) / max_row / 8 * 8;
-        if (r_cap < 8) return cudaErrorInvalidValue;  // a row longer than ~7 KiB
-    }
-    int64_t r_bal = (total_rows / (2 * static_cast<int64_t>(max_ctas))) / 8 * 8;
-    const int64_t R = std::max<int64_t>(8, std::min<int64_t>(std::min<int64_t>(r_cap, r_bal), 64));
-    const int64_t stage_bytes = ((R * max_row + 32) + 127) / 128 * 128;
-    const int64_t stages = std::min<int64_t>(kGemvMaxStages, kSmemDataBudget / stage_bytes);
-    if (stages < 2) return cudaErrorInvalidValue;
+    const int64_t x_bytes = (max_x + 127) / 128 * 128;
+    // Rows per tile: a multiple of the group size, at most 64, small enough
+    // that the launch has ~2 tiles per CTA, and shrunk until the ring holds
+    // at least 3 stages (2 at the very least).
+    const int64_t r_max = 64;
+    const int64_t r_bal = (total_rows / (2 * static_cast<int64_t>(max_ctas))) / GR * GR;
+    int64_t R = std::max<int64_t>(GR, std::min<int64_t>(r_bal, r_max));
+    auto stage_of = [&](int64_t r) { return (r * max_pitch + 32 + 127) / 128 * 128 + x_bytes; };
+    while (R > GR && budget / stage_of(R) < 3) R -= GR;
+    const int64_t w_bytes = (R * max_pitch + 32 + 127) / 128 * 128;
+    const int64_t stage_bytes = w_bytes + x_bytes;
+    const int64_t stages = std::min<int64_t>(kGemvMaxStages, budget / stage_bytes);
+    if (stages < 2) return cudaErrorInvalidValue;  // a row (+ activations) too long to stage
     int64_t tiles = 0;
     for (int j = 0; j < n_jobs; ++j) {
         jobs[j].tile_begin = static_cast<int32_t>(tiles);
@@ -474,6 +537,7 @@ cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_cou
     p->n_stages = static_cast<int32_t>(stages);
     p->stage_bytes = static_cast<int32_t>(stage_bytes);
     p->n_tok = n_tok;
+    p->x_offset = static_cast<int32_t>(w_bytes);
     for (int j = 0; j < kGemvInlineJobs; ++j) p->jobs[j] = j < n_jobs ? jobs[j] : GemvJob{};
     g->grid = static_cast<int>(std::min<int64_t>(tiles, max_ctas));
     g->smem_bytes = static_cast<int>(kSmemHeader + stages * stage_bytes);

@@ -27,6 +27,9 @@ struct GemvJob {
     int32_t nb;          // blocks per row
     int32_t row_bytes;   // nb * block bytes
     int32_t k;           // K, input features
+    int32_t d_stride;    // scale-plane elements per token row (f32 for Q8_K, fp16 for Q8_0)
+    int32_t box_blocks;  // blocks per staged row segment (filled by the planner)
+    int32_t box_pitch;   // shared-memory pitch of a staged row segment, bytes (planner)
     int32_t tile_begin;  // first global tile index of this job (filled by the planner)
     int32_t n_tiles;     // tiles of this job (filled by the planner)
 };
@@ -41,6 +44,7 @@ struct GemvParams {
     int32_t n_stages;
     int32_t stage_bytes;
     int32_t n_tok;
+    int32_t x_offset;      // byte offset of the staged activation planes inside a stage
     const GemvJob *table;  // device copy of all jobs when n_jobs > kGemvInlineJobs
     int *err_flag;         // device error word
     GemvJob jobs[kGemvInlineJobs];
@@ -52,9 +56,10 @@ struct GemvGeometry {
     int smem_bytes;
 };
 
-// Fills tile_begin/n_tiles of `jobs`, the tiling fields of `p` and the
-// launch geometry. All jobs share `type`; returns cudaErrorInvalidValue if a
-// row is too long to stage. `sm_count` is the device's multiprocessor count.
+// Fills tile_begin/n_tiles/box fields of `jobs`, the tiling fields of `p`
+// and the launch geometry. All jobs share `type`; returns
+// cudaErrorInvalidValue if a row is too long to stage. `sm_count` is the
+// device's multiprocessor count.
 cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_count,
                       GemvParams *p, GemvGeometry *g);
 

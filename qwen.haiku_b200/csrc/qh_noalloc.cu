@@ -125,7 +125,8 @@ extern "C" int qh_matmul_q4k_f32_noalloc(const void *d_w, int64_t out_f, int64_t
         job.row_bytes = nb * QH_Q4K_BYTES;
         job.n_rows = static_cast<int32_t>(out_f);
         job.xqs = reinterpret_cast<const int8_t *>(xq) + t0 * k;
-        job.xd = xq + qhf_q8k_d_offset(k, n_tok) + t0 * nb * 4;
+        job.d_stride = static_cast<int32_t>(qhf_q8k_d_stride(k));
+        job.xd = xq + qhf_q8k_d_offset(k, n_tok) + t0 * job.d_stride * 4;
         job.xbs = reinterpret_cast<const int16_t *>(xq + qhf_q8k_bsums_offset(k, n_tok)) + t0 * nb * 16;
         job.out = d_out + t0 * out_f;
         qh::GemvParams p{};

@@ -61,9 +61,9 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float *__restri
         q = (__float_as_int(biased) & 0x007fffff) - 0x00400000;
         if (f != f) q = 0;  // x86 default NaN (0xffc00000) decodes to 0 there
         q = q > 127 ? 127 : (q < -128 ? -128 : q);
-        if (tid == 0) dv[static_cast<int64_t>(tok) * nb + blk] = __fdiv_rn(1.0f, iscale);
+        if (tid == 0) dv[static_cast<int64_t>(tok) * qhf_q8k_d_stride(k) + blk] = __fdiv_rn(1.0f, iscale);
     } else if (tid == 0) {
-        dv[static_cast<int64_t>(tok) * nb + blk] = 0.0f;
+        dv[static_cast<int64_t>(tok) * qhf_q8k_d_stride(k) + blk] = 0.0f;
     }
     qs[base + tid] = static_cast<int8_t>(q);
     // 16-element group sums: each half-warp is one group.
@@ -92,7 +92,10 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restr
     int q = static_cast<int>(roundf(__fmul_rn(v, id)));
     q = q > 127 ? 127 : (q < -128 ? -128 : q);
     qs[b * QH_QK8_0 + lane] = static_cast<int8_t>(q);
-    if (lane == 0) dbits[b] = __half_as_ushort(__float2half_rn(d));
+    if (lane == 0) {
+        const int64_t nb0 = k / QH_QK8_0;
+        dbits[(b / nb0) * qhf_q8_0_d_stride(k) + b % nb0] = __half_as_ushort(__float2half_rn(d));
+    }
 }
 
 cudaError_t quantize_q8k_launch(const float *x, int64_t k, int64_t n_tok, void *q8k,

@@ -86,9 +86,10 @@ def unpack_q8k(buf: np.ndarray, k: int, n_tok: int):
     """(qs int8 [n_tok,k], d f32 [n_tok,k/256], bsums int16 [n_tok,k/256,16])."""
     L = lib()
     nb = k // 256
+    stride = (nb + 3) // 4 * 4          # scale rows padded to 16 bytes
     d_off, b_off = int(L.qh_q8k_d_offset(k, n_tok)), int(L.qh_q8k_bsums_offset(k, n_tok))
     qs = buf[: k * n_tok].view(np.int8).reshape(n_tok, k)
-    d = buf[d_off: d_off + 4 * nb * n_tok].view(np.float32).reshape(n_tok, nb)
+    d = buf[d_off: d_off + 4 * stride * n_tok].view(np.float32).reshape(n_tok, stride)[:, :nb]
     bs = buf[b_off: b_off + 32 * nb * n_tok].view(np.int16).reshape(n_tok, nb, 16)
     return qs, d, bs
 
@@ -96,9 +97,10 @@ def unpack_q8k(buf: np.ndarray, k: int, n_tok: int):
 def unpack_q8_0(buf: np.ndarray, k: int, n_tok: int):
     """(qs int8 [n_tok,k], d fp16 bits uint16 [n_tok,k/32])."""
     nb = k // 32
+    stride = (nb + 7) // 8 * 8          # scale rows padded to 16 bytes
     d_off = int(lib().qh_q8_0_d_offset(k, n_tok))
     qs = buf[: k * n_tok].view(np.int8).reshape(n_tok, k)
-    d = buf[d_off: d_off + 2 * nb * n_tok].view(np.uint16).reshape(n_tok, nb)
+    d = buf[d_off: d_off + 2 * stride * n_tok].view(np.uint16).reshape(n_tok, stride)[:, :nb]
     return qs, d
 
 
