@@ -1,0 +1,91 @@
+/* SPDX-License-Identifier: MIT
+ *
+ * qh_kernels.h -- C-ABI of the non-matmul kernels of the hybrid forward pass
+ * (the device counterparts of the reference's per-token fp32 code). The
+ * host step driver (qwen.haiku_b200/csrc/qh_slm.c) chains them with the
+ * matmul plans of qh_backend.h. Every call works on B sequences at once,
+ * device pointers, asynchronous on `stream`, returns QH_OK or QH_ERR_*.
+ *
+ * Rounding follows the reference operation by operation: products and sums
+ * the reference does in float are done with explicitly rounded float ops
+ * (no FMA contraction), and its double-precision accumulations stay double.
+ */
+#ifndef QH_KERNELS_H
+#define QH_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Token embedding from a Q6_K table of shape (hidden, vocab): h[b] = the
+ * dequantized row tokens[b] (q6k_dequant_block, slm/tensor.c:988;
+ * slm/qwen.c:885-907). */
+int qh_embed_q6k(const void *d_table, int64_t hidden, const int32_t *d_tokens, int32_t B, float *d_h,
+                 void *stream);
+
+/* RMSNorm over rows of `dim` (tensor_rms_norm, slm/tensor.c:348-369):
+ * y = x * (1 / sqrtf(float(sum(x*x) / dim) + eps)) * w, the sum of squares
+ * accumulated in double. */
+int qh_rmsnorm(const float *d_x, const float *d_w, int64_t dim, int64_t rows, float eps, float *d_y,
+               void *stream);
+
+/* h += mix over n floats (tensor_add, slm/tensor.c:285). */
+int qh_add(float *d_h, const float *d_mix, int64_t n, void *stream);
+
+/* out = silu(gate) * up over n floats (simd_silu_f32 + tensor_mul,
+ * slm/qwen.c:952-955). */
+int qh_swiglu(const float *d_gate, const float *d_up, float *d_out, int64_t n, void *stream);
+
+/* Gated DeltaNet pre-processing for one layer, B sequences
+ * (slm/qwen.c:357-475): push qkv into the conv ring slot pos % kk,
+ * causal conv + SiLU, split into Q/K/V, per-head L2 norm of Q (scaled by
+ * 1/sqrt(head_dim)) and K, beta = sigmoid(b), g = exp(ssm_a *
+ * softplus(a + dt_bias)).
+ *   qkv [B][conv_dim], ring [B][kk][conv_dim], conv_w [conv_dim][kk],
+ *   b, a [B][heads]; out q, k, v [B][heads*hd], beta, g [B][heads]. */
+int qh_gdn_pre(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b,
+               const float *d_a, const float *d_dt_bias, const float *d_ssm_a, int32_t B,
+               int32_t heads, int32_t hd, int32_t kk, int32_t pos, float *d_q, float *d_k, float *d_v,
+               float *d_beta, float *d_g, void *stream);
+
+/* Gated DeltaNet recurrence (slm/qwen.c:499-557) over state [B][heads][hd
+ * k][hd v]: state *= g; kv = state^T K; delta = (V - kv) * beta;
+ * state += K delta^T; out = state^T Q -- both reductions over k in double,
+ * in the reference's order. out [B][heads*hd]. */
+int qh_gdn_recurrence(float *d_state, const float *d_q, const float *d_k, const float *d_v,
+                      const float *d_beta, const float *d_g, int32_t B, int32_t heads, int32_t hd,
+                      float *d_out, void *stream);
+
+/* Gated RMSNorm per head (slm/qwen.c:571-598): y = ((x * rs) * w) * silu(z). */
+int qh_gdn_gated_norm(const float *d_x, const float *d_z, const float *d_w, int32_t B, int32_t heads,
+                      int32_t hd, float eps, float *d_y, void *stream);
+
+/* Attention pre-processing for one layer (slm/model.c:831-913): split the
+ * head-interleaved Q/gate projection, per-head RMSNorm of Q and K, partial
+ * interleaved-MRoPE with the host-built cos/sin table rope[pos][rope_dim/2][2],
+ * append K (roped) and V as fp16 at row pos of the layer's caches
+ * [B][max_pos][kvh][hd]. qraw [B][2*nh*hd], k, v [B][kvh*hd] in; q [B][nh][hd],
+ * gate [B][nh*hd] out. */
+int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
+                const float *d_knorm_w, const float *d_rope, int32_t B, int32_t nh, int32_t kvh,
+                int32_t hd, int32_t rope_dim, float eps, int32_t pos, int32_t max_pos, float *d_q,
+                float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream);
+
+/* Causal GQA attention of the new query over cache rows 0..pos, then the
+ * sigmoid output gate (tensor_attention, slm/tensor.c:1049-1102;
+ * slm/model.c:940-947). ctx [B][nh*hd]. */
+int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache,
+                   const float *d_gate, int32_t B, int32_t nh, int32_t kvh, int32_t hd, int32_t pos,
+                   int32_t max_pos, float *d_ctx, void *stream);
+
+/* Greedy pick per row (sample_argmax, slm/model.c:401-412): index of the
+ * first maximum of logits [B][vocab]. */
+int qh_argmax(const float *d_logits, int32_t B, int64_t vocab, int32_t *d_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QH_KERNELS_H */

@@ -1,0 +1,104 @@
+/* SPDX-License-Identifier: MIT
+ *
+ * qh_slm.h -- the Qwen3.5-0.8B-shaped hybrid forward pass (Gated DeltaNet
+ * + gated attention) on B200, token level.
+ *
+ * Reference counterparts (qwen.haiku, path:line):
+ *   struct slm_config                    slm/model.c:72-98
+ *   struct slm_weights / slm_load_weights slm/model.c:154-188, slm/qwen.c:174-252
+ *   slm_ctx caches (KV, conv ring, SSM)  slm/model.c:289-391, 488-504
+ *   slm_forward_step                     slm/qwen.c:874-981
+ *     slm_forward_ssm (GDN layer)        slm/qwen.c:318-611
+ *     slm_forward_attn (attention layer) slm/model.c:766-953
+ *   sample_argmax (greedy pick)          slm/model.c:401-412
+ * The reference's text layer (tokenizer, chat template, sampler chain,
+ * agent) is not part of this path: these entry points take token ids.
+ *
+ * One qh_slm holds the weights of one model on one GPU plus the decode
+ * state of n_seq independent sequences (the reference's slm_ctx, one per
+ * sequence); a step advances every sequence by one token at the same
+ * position, i.e. batched decode for data-parallel serving. All calls return
+ * QH_OK or a negative QH_ERR_* status (include/qh_backend.h).
+ */
+#ifndef QH_SLM_H
+#define QH_SLM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct qh_slm_config {
+    int32_t n_layers;           /* 24 */
+    int32_t hidden;             /* 1024 */
+    int32_t ffn;                /* 3584 */
+    int32_t vocab;              /* 151936 */
+    int32_t n_heads;            /* attention query heads, 8 */
+    int32_t n_kv_heads;         /* 2 */
+    int32_t head_dim;           /* 128 */
+    int32_t rope_dim;           /* rotated dims per head, 64 */
+    float rope_theta;           /* 1e6 */
+    int32_t rope_sections[4];   /* interleaved MRoPE sections, {11, 11, 10, 0} */
+    float norm_eps;             /* RMSNorm epsilon */
+    int32_t gdn_heads;          /* Gated DeltaNet heads, 16 */
+    int32_t gdn_head_dim;       /* key = value head dim, 128 */
+    int32_t conv_kernel;        /* 4 */
+    int32_t full_attn_interval; /* every 4th layer is attention (L % 4 == 3) */
+    int32_t max_pos;            /* KV-cache positions per sequence */
+} qh_slm_config;
+
+/* BASELINE config 4/5 shape: Qwen3.5-0.8B-like hybrid, vocab 151936. */
+void qh_slm_config_default(qh_slm_config *cfg, int32_t max_pos);
+
+/* ------------------------------------------------------------------------
+ * Synthetic weights (host). The reference runs on a real GGUF; with none
+ * available, a seeded blob of tensors with the GGUF names, types and shapes
+ * stands in: matrices N(0, 0.02) quantized with qh_synth_quantize (Q4_K,
+ * Q6_K for ffn_down and the tied token embedding / LM head), fp32 norms
+ * 1 + N(0, 0.02), ssm_a = -exp(N(0, 0.02)), conv1d N(0, 0.5), dt bias
+ * N(0, 0.02). Shapes follow GGUF order: shape[0] = input dim.
+ * ---------------------------------------------------------------------- */
+typedef struct qh_blob qh_blob;
+
+int qh_blob_synthetic(const qh_slm_config *cfg, uint64_t seed, qh_blob **out);
+int qh_blob_count(const qh_blob *blob);
+/* Tensor i: GGUF name, GGUF type id, shape (shape[1] = 1 for vectors), host
+ * data and byte size. Pointers stay valid until qh_blob_free. */
+int qh_blob_tensor(const qh_blob *blob, int i, const char **name, int32_t *type, int64_t shape[2],
+                   const void **data, int64_t *nbytes);
+/* Index of the tensor named `name`, or -1. */
+int qh_blob_find(const qh_blob *blob, const char *name);
+void qh_blob_free(qh_blob *blob);
+
+/* ------------------------------------------------------------------------
+ * Device model + n_seq sequences
+ * ---------------------------------------------------------------------- */
+typedef struct qh_slm qh_slm;
+
+/* Uploads every blob tensor to the current device (weights keep their GGUF
+ * block layout) and allocates the caches of n_seq sequences. */
+int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, qh_slm **out);
+void qh_slm_destroy(qh_slm *m);
+
+/* Clears every sequence's KV cache, conv ring and recurrent state. */
+int qh_slm_reset(qh_slm *m);
+
+/* slm_forward_step + sample_argmax for all n_seq sequences at position pos:
+ * h_tokens[n_seq] in, h_next[n_seq] (greedy argmax) out, optionally the
+ * logits h_logits[n_seq][vocab]. Synchronous. */
+int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next, float *h_logits);
+
+/* Greedy generation: feeds the n_prompt tokens of every sequence one step
+ * at a time (as the reference's default prefill does), then n_new greedy
+ * steps; out[s][i] is the i-th generated token of sequence s. */
+int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out);
+
+/* Device memory held by the model (weights) and by the per-sequence state. */
+int qh_slm_memory(const qh_slm *m, int64_t *weight_bytes, int64_t *state_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QH_SLM_H */

@@ -25,6 +25,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libqhref.so")
+REF_CR_SO = os.path.join(HERE, "_ref", "libqhref_crlibm.so")
 
 Q8_0, Q4_K, Q5_K, Q6_K = 8, 12, 13, 14
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34}
@@ -168,13 +169,15 @@ class Ref:
     """The reference's own C code (oracle/_ref/libqhref.so)."""
 
     @staticmethod
-    def available() -> bool:
-        return os.path.exists(REF_SO)
+    def available(crlibm: bool = False) -> bool:
+        return os.path.exists(REF_CR_SO if crlibm else REF_SO)
 
-    def __init__(self):
-        if not os.path.exists(REF_SO):
+    def __init__(self, crlibm: bool = False):
+        """crlibm=True loads the build whose expf/logf are correctly rounded."""
+        path = REF_CR_SO if crlibm else REF_SO
+        if not os.path.exists(path):
             build(force=True)
-        L = C.CDLL(REF_SO)
+        L = C.CDLL(path)
         L.ref_simd_init()
         L.ref_dispatch_label.restype = C.c_char_p
         for n in ("ref_q4k_row_dot", "ref_q5k_row_dot", "ref_q6k_row_dot",
@@ -254,3 +257,44 @@ class Ref:
         y = np.empty(256, np.float32)
         self.L.ref_dequant_block(gtype, _ptr(np.ascontiguousarray(blk, np.uint8)), _ptr(y))
         return y
+
+
+class RefModel:
+    """The reference's slm_forward_step over a synthetic blob's tensors."""
+
+    def __init__(self, ref: "Ref", cfg, tensors):
+        L = ref.L
+        L.ref_model_create.restype = C.c_void_p
+        L.ref_model_create.argtypes = [_P, _P, _I, _P, _P, _P, _P]
+        L.ref_model_step.argtypes = [_P, C.c_int32, C.c_int32, _P]
+        L.ref_model_step.restype = C.c_int
+        L.ref_model_destroy.argtypes = [_P]
+        ic = np.array([cfg.n_layers, cfg.hidden, cfg.ffn, cfg.vocab, cfg.n_heads, cfg.n_kv_heads,
+                       cfg.head_dim, cfg.rope_dim, *list(cfg.rope_sections), cfg.gdn_heads,
+                       cfg.gdn_head_dim, cfg.conv_kernel, cfg.full_attn_interval, cfg.max_pos], np.int32)
+        fc = np.array([cfg.rope_theta, cfg.norm_eps], np.float32)
+        n = len(tensors)
+        self._names = [t[0].encode() for t in tensors]
+        names = (C.c_char_p * n)(*self._names)
+        types = np.array([t[1] for t in tensors], np.int32)
+        shapes = np.array([t[2] for t in tensors], np.int64).reshape(n, 2)
+        datas = (C.c_void_p * n)(*[t[3] for t in tensors])
+        self._keep = (ic, fc, names, types, shapes, datas)
+        self.L, self.vocab = L, cfg.vocab
+        self.h = L.ref_model_create(_ptr(ic), _ptr(fc), n, names, _ptr(types), _ptr(shapes), datas)
+
+    def step(self, tok: int, pos: int, want_logits: bool = False):
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        a = self.L.ref_model_step(self.h, int(tok), int(pos), _ptr(logits) if logits is not None else None)
+        return (a, logits) if want_logits else a
+
+    def close(self):
+        if self.h:
+            self.L.ref_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

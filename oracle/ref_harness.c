@@ -20,6 +20,20 @@
 //   q{4k,5k,6k}_dequant_block                  slm/tensor.c:800, 867, 988
 //   slm_forward_step + sample_argmax           slm/qwen.c:874-981, slm/model.c:401
 
+// Built twice by oracle/Makefile: libqhref.so is the reference as shipped;
+// libqhref_crlibm.so (-DQH_CR_LIBM) is the same sources with expf/logf
+// resolved to correctly rounded versions (double-precision exp/log rounded
+// once to float). The host glibc's expf/logf are not correctly rounded for
+// ~6e-4 of inputs; the device kernels evaluate them correctly rounded, so
+// the second build isolates that libm difference from everything else.
+#ifdef QH_CR_LIBM
+#include <math.h>
+static float qh_cr_expf(float x) { return (float)exp((double)x); }
+static float qh_cr_logf(float x) { return (float)log((double)x); }
+#define expf qh_cr_expf
+#define logf qh_cr_logf
+#endif
+
 #include "slm/qwen.c"
 #include "slm/sampler.c"
 
@@ -210,4 +224,132 @@ int ref_matvec_pool_mt(int type, const void *const *ws, int n_mats, int64_t out_
     }
     for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
     return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Model level: the reference's own forward step over caller-provided weights.
+// Builds struct slm_model / slm_ctx the way slm_model_load + slm_ctx_create
+// do (slm/model.c:1130-1240, slm/qwen.c:59-252), but from an in-memory table
+// of named tensors instead of a GGUF file, then runs slm_forward_step
+// (slm/qwen.c:874) and sample_argmax (slm/model.c:401).
+//
+// ic[] = {n_layers, hidden, ffn, vocab, n_heads, n_kv_heads, head_dim,
+//         rope_dim, sec0, sec1, sec2, sec3, gdn_heads, gdn_head_dim,
+//         conv_kernel, full_attn_interval, max_pos}
+// fc[] = {rope_theta, norm_eps}
+// ---------------------------------------------------------------------------
+struct ref_model {
+    struct slm_model m;
+    struct slm_ctx c;
+};
+
+static int ref_find(int n, const char **names, const char *want) {
+    for (int i = 0; i < n; i++)
+        if (strcmp(names[i], want) == 0) return i;
+    return -1;
+}
+
+static void ref_bind(struct slm_tensor *t, int i, const int32_t *types, const int64_t *shapes,
+                     const void **datas) {
+    memset(t, 0, sizeof(*t));
+    if (i < 0) return;
+    t->data = datas[i];
+    t->type = types[i];
+    t->shape[0] = shapes[2 * i];
+    t->shape[1] = shapes[2 * i + 1];
+    t->shape[2] = t->shape[3] = 1;
+    t->n_dims = t->shape[1] > 1 ? 2 : 1;
+}
+
+void *ref_model_create(const int32_t *ic, const float *fc, int n, const char **names,
+                       const int32_t *types, const int64_t *shapes, const void **datas) {
+    simd_init();
+    struct ref_model *r = (struct ref_model *)calloc(1, sizeof(*r));
+    struct slm_config *cfg = &r->m.cfg;
+    cfg->n_layers = ic[0];
+    cfg->hidden_dim = ic[1];
+    cfg->ffn_dim = ic[2];
+    cfg->vocab_size = ic[3];
+    cfg->n_heads = ic[4];
+    cfg->n_kv_heads = ic[5];
+    cfg->head_dim = ic[6];
+    cfg->rope_dim = ic[7];
+    for (int i = 0; i < 4; i++) cfg->rope_sections[i] = ic[8 + i];
+    cfg->linear_n_heads = ic[12];
+    cfg->linear_k_head_dim = ic[13];
+    cfg->linear_v_head_dim = ic[13];
+    cfg->linear_conv_kernel = ic[14];
+    cfg->full_attn_interval = ic[15];
+    cfg->max_position = ic[16];
+    cfg->rope_theta = fc[0];
+    cfg->norm_eps = fc[1];
+    cfg->is_hybrid = 1;
+    cfg->attn_output_gate = 1;
+    cfg->eot_id = -1;
+
+    struct slm_weights *W = &r->m.W;
+    char nm[96];
+    ref_bind(&W->tok_embd, ref_find(n, names, "token_embd.weight"), types, shapes, datas);
+    ref_bind(&W->output_norm, ref_find(n, names, "output_norm.weight"), types, shapes, datas);
+    int out_i = ref_find(n, names, "output.weight");
+    if (out_i >= 0) ref_bind(&W->output, out_i, types, shapes, datas);
+    else W->output = W->tok_embd;
+    W->layers = (struct slm_layer *)calloc((size_t)cfg->n_layers, sizeof(struct slm_layer));
+    for (int L = 0; L < cfg->n_layers; L++) {
+        struct slm_layer *Lw = &W->layers[L];
+#define BIND(field, fmt) do { snprintf(nm, sizeof(nm), fmt, L); \
+        ref_bind(&Lw->field, ref_find(n, names, nm), types, shapes, datas); } while (0)
+        snprintf(nm, sizeof(nm), "blk.%d.ssm_a", L);
+        Lw->is_ssm = ref_find(n, names, nm) >= 0;
+        BIND(attn_norm, "blk.%d.attn_norm.weight");
+        BIND(ffn_norm, "blk.%d.post_attention_norm.weight");
+        BIND(ffn_gate, "blk.%d.ffn_gate.weight");
+        BIND(ffn_up, "blk.%d.ffn_up.weight");
+        BIND(ffn_down, "blk.%d.ffn_down.weight");
+        if (Lw->is_ssm) {
+            BIND(attn_qkv, "blk.%d.attn_qkv.weight");
+            BIND(attn_gate, "blk.%d.attn_gate.weight");
+            BIND(ssm_a, "blk.%d.ssm_a");
+            BIND(ssm_alpha, "blk.%d.ssm_alpha.weight");
+            BIND(ssm_beta, "blk.%d.ssm_beta.weight");
+            BIND(ssm_conv1d, "blk.%d.ssm_conv1d.weight");
+            BIND(ssm_dt_bias, "blk.%d.ssm_dt.bias");
+            BIND(ssm_norm, "blk.%d.ssm_norm.weight");
+            BIND(ssm_out, "blk.%d.ssm_out.weight");
+        } else {
+            BIND(attn_q, "blk.%d.attn_q.weight");
+            BIND(attn_k, "blk.%d.attn_k.weight");
+            BIND(attn_v, "blk.%d.attn_v.weight");
+            BIND(attn_q_norm, "blk.%d.attn_q_norm.weight");
+            BIND(attn_k_norm, "blk.%d.attn_k_norm.weight");
+            BIND(attn_out, "blk.%d.attn_output.weight");
+        }
+#undef BIND
+    }
+    r->m.loaded = 1;
+    r->c.model = &r->m;
+    r->c.ctrl = slm_ctrl_defaults();
+    kv_init(&r->c.kv, cfg->n_layers, cfg->n_kv_heads, cfg->head_dim, cfg->max_position);
+    ssm_cache_init(&r->c.ssm, cfg);
+    r->c.arena = arena_new(64 * 1024 * 1024);
+    return r;
+}
+
+// One slm_forward_step; copies the logits out (if non-null) and returns
+// sample_argmax of them.
+int ref_model_step(void *h, int32_t tok, int32_t pos, float *logits) {
+    struct ref_model *r = (struct ref_model *)h;
+    struct tensor *lg = slm_forward_step(&r->c, tok, pos);
+    if (logits) memcpy(logits, lg->data, (size_t)r->m.cfg.vocab_size * sizeof(float));
+    return sample_argmax(lg);
+}
+
+void ref_model_destroy(void *h) {
+    struct ref_model *r = (struct ref_model *)h;
+    if (!r) return;
+    ssm_cache_free(&r->c.ssm);
+    kv_free(&r->c.kv);
+    arena_free(r->c.arena);
+    free(r->m.W.layers);
+    free(r);
 }

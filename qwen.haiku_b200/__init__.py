@@ -89,6 +89,48 @@ SIGNATURES = {
     "qh_synth_quantize": (_I, [_I, _P, _I64, _I64, _P]),
 }
 
+class SlmConfig(C.Structure):
+    """qh_slm_config (include/qh_slm.h)."""
+    _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("ffn", C.c_int32), ("vocab", C.c_int32),
+                ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("rope_dim", C.c_int32), ("rope_theta", C.c_float), ("rope_sections", C.c_int32 * 4),
+                ("norm_eps", C.c_float), ("gdn_heads", C.c_int32), ("gdn_head_dim", C.c_int32),
+                ("conv_kernel", C.c_int32), ("full_attn_interval", C.c_int32), ("max_pos", C.c_int32)]
+
+
+SIGNATURES.update({
+    "qh_slm_config_default": (None, [C.POINTER(SlmConfig), C.c_int32]),
+    "qh_blob_synthetic": (_I, [C.POINTER(SlmConfig), _U64, C.POINTER(C.c_void_p)]),
+    "qh_blob_count": (_I, [_P]),
+    "qh_blob_tensor": (_I, [_P, _I, C.POINTER(C.c_char_p), C.POINTER(C.c_int32), C.POINTER(_I64),
+                           C.POINTER(C.c_void_p), C.POINTER(_I64)]),
+    "qh_blob_find": (_I, [_P, C.c_char_p]),
+    "qh_blob_free": (None, [_P]),
+    "qh_slm_create": (_I, [C.POINTER(SlmConfig), _P, C.c_int32, C.POINTER(C.c_void_p)]),
+    "qh_slm_destroy": (None, [_P]),
+    "qh_slm_reset": (_I, [_P]),
+    "qh_slm_step": (_I, [_P, _P, C.c_int32, _P, _P]),
+    "qh_slm_generate": (_I, [_P, _P, C.c_int32, C.c_int32, _P]),
+    "qh_slm_memory": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64)]),
+})
+
+_F32P = C.c_void_p
+SIGNATURES.update({  # include/qh_kernels.h
+    "qh_embed_q6k": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
+    "qh_rmsnorm": (_I, [_P, _P, _I64, _I64, C.c_float, _P, _P]),
+    "qh_add": (_I, [_P, _P, _I64, _P]),
+    "qh_swiglu": (_I, [_P, _P, _P, _I64, _P]),
+    "qh_gdn_pre": (_I, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                        _P, _P, _P, _P, _P, _P]),
+    "qh_gdn_recurrence": (_I, [_P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, _P, _P]),
+    "qh_gdn_gated_norm": (_I, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_float, _P, _P]),
+    "qh_attn_pre": (_I, [_P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                         C.c_float, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
+    "qh_attn_decode": (_I, [_P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                            _P, _P]),
+    "qh_argmax": (_I, [_P, C.c_int32, _I64, _P, _P]),
+})
+
 _lib = None
 
 

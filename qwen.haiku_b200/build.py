@@ -30,7 +30,7 @@ NVCC_FLAGS = ARCH + [
     "-Xptxas", "-warn-spills", "--expt-relaxed-constexpr",
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
-CC_FLAGS = ["-O2", "-std=c17", "-ffp-contract=off", "-fPIC", "-Wall", "-Wextra",
+CC_FLAGS = ["-O2", "-std=c17", "-ffp-contract=off", "-fPIC", "-Wall", "-Wextra", "-I/usr/local/cuda/include",
             f"-I{INCLUDE}", f"-I{CSRC}"]
 
 

@@ -1,0 +1,464 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_model.cu -- the non-matmul kernels of the hybrid forward pass
+// (include/qh_kernels.h) on sm_100a.
+//
+// Every kernel reproduces the reference's operation order where that order
+// is cheap to keep: float products and sums use explicitly rounded
+// __fmul_rn/__fadd_rn (never contracted into FMAs), sequential reductions
+// the reference does in float over a short axis stay sequential in one
+// thread (attention dot products, softmax sum, value accumulation), and its
+// double-precision sums stay double (norms, the DeltaNet kv/out products).
+// Transcendentals are evaluated in double precision and rounded once to
+// float (expf_cr/logf_cr below): that is the correctly rounded float result
+// except when the exact value lies within ~1e-16 (relative) of a float
+// rounding boundary, which is what the reference's host libm returns as
+// well -- single-precision device expf/logf differ from it by an ulp often
+// enough that the next layer's Q8_K quantization flips int8 values and the
+// token streams drift. RoPE cos/sin come from a host-computed table so they
+// match the reference's libm bit for bit.
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+
+#include "../../include/qh_backend.h"
+#include "../../include/qh_kernels.h"
+#include "qh_common.cuh"
+#include "qh_internal.h"
+
+namespace qh {
+
+__device__ __forceinline__ float expf_cr(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+__device__ __forceinline__ float logf_cr(float x) { return static_cast<float>(log(static_cast<double>(x))); }
+
+__device__ __forceinline__ float silu_f(float x) {
+    return __fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x)));
+}
+
+__device__ __forceinline__ float sigmoid_f(float x) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-x)));
+}
+
+// Block-wide double sum (blockDim.x multiple of 32, <= 1024); all threads
+// get the result.
+__device__ double block_sum_d(double v, double *scratch) {
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    for (int w = 0; w < nw; ++w) t += scratch[w];
+    return t;
+}
+
+__device__ float block_max_f(float v, float *scratch) {
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = scratch[0];
+    for (int w = 1; w < nw; ++w) t = fmaxf(t, scratch[w]);
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// Embedding: one CTA of 256 threads per (token, super-block).
+// ---------------------------------------------------------------------------
+__global__ void embed_q6k_kernel(const uint8_t *__restrict__ table, int64_t hidden,
+                                 const int32_t *__restrict__ tokens, float *__restrict__ h) {
+    const int b = blockIdx.y, sb = blockIdx.x, p = threadIdx.x;
+    const int64_t nb = hidden / QH_QK;
+    const uint8_t *blk = table + (static_cast<int64_t>(tokens[b]) * nb + sb) * QH_Q6K_BYTES;
+    const int half = p >> 7, r = (p >> 5) & 3, l = p & 31;
+    const uint8_t lo_byte = blk[64 * half + 32 * (r & 1) + l];
+    const int lo = (r >> 1) ? (lo_byte >> 4) : (lo_byte & 0x0f);
+    const int hi2 = (blk[128 + 32 * half + l] >> (2 * r)) & 3;
+    const int q = (lo | (hi2 << 4)) - 32;
+    const float d = h2f_bits(static_cast<uint32_t>(blk[208]) | (static_cast<uint32_t>(blk[209]) << 8));
+    const float sc = static_cast<float>(static_cast<int8_t>(blk[192 + (p >> 4)]));
+    h[static_cast<int64_t>(b) * hidden + sb * QH_QK + p] = __fmul_rn(__fmul_rn(d, sc), static_cast<float>(q));
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm: one CTA per row.
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int64_t dim,
+                               float eps, float *__restrict__ y) {
+    __shared__ double scratch[32];
+    const float *xr = x + blockIdx.x * dim;
+    float *yr = y + blockIdx.x * dim;
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float v = xr[i];
+        s += static_cast<double>(__fmul_rn(v, v));
+    }
+    const double ssq = block_sum_d(s, scratch);
+    const float rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(dim)), eps)));
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], rscale), w[i]);
+}
+
+__global__ void add_kernel(float *__restrict__ h, const float *__restrict__ mix, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = __fadd_rn(h[i], mix[i]);
+}
+
+__global__ void swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ o,
+                              int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) o[i] = __fmul_rn(silu_f(g[i]), u[i]);
+}
+
+// ---------------------------------------------------------------------------
+// Gated DeltaNet pre-processing: one CTA (hd threads) per (sequence, head).
+// Thread t owns the Q, K and V channels t of its head.
+// ---------------------------------------------------------------------------
+__global__ void gdn_pre_kernel(const float *__restrict__ qkv, float *__restrict__ ring,
+                               const float *__restrict__ conv_w, const float *__restrict__ bb,
+                               const float *__restrict__ aa, const float *__restrict__ dt_bias,
+                               const float *__restrict__ ssm_a, int heads, int hd, int kk, int pos,
+                               float *__restrict__ qo, float *__restrict__ ko, float *__restrict__ vo,
+                               float *__restrict__ beta, float *__restrict__ gout) {
+    __shared__ double scratch[32];
+    const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+    const int kdim = heads * hd, conv_dim = 3 * kdim;
+    const int slot = pos % kk, head_after = (pos + 1) % kk;
+    const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
+    float *rg = ring + static_cast<int64_t>(b) * kk * conv_dim;
+    float mixed[3];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * hd + t;
+        rg[static_cast<int64_t>(slot) * conv_dim + ch] = src[ch];
+        float acc = 0.0f;
+        for (int k = 0; k < kk; ++k) {
+            const int sl = (head_after + k) % kk;
+            acc = __fadd_rn(acc, __fmul_rn(rg[static_cast<int64_t>(sl) * conv_dim + ch], conv_w[ch * kk + k]));
+        }
+        mixed[part] = silu_f(acc);
+    }
+    // per-head L2 norms (double sums of float squares), eps applied via fmaxf
+    const double qss = block_sum_d(static_cast<double>(__fmul_rn(mixed[0], mixed[0])), scratch);
+    const double kss = block_sum_d(static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+    const float qrs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qss)), 1e-6f));
+    const float krs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(kss)), 1e-6f));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));
+    const int64_t o = static_cast<int64_t>(b) * kdim + h * hd + t;
+    qo[o] = __fmul_rn(__fmul_rn(mixed[0], qrs), scale);
+    ko[o] = __fmul_rn(mixed[1], krs);
+    vo[o] = mixed[2];
+    if (t == 0) {
+        const int i = b * heads + h;
+        beta[i] = sigmoid_f(bb[i]);
+        const float a = __fadd_rn(aa[i], dt_bias[h]);
+        const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
+        gout[i] = expf_cr(__fmul_rn(ssm_a[h], sp));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Gated DeltaNet recurrence: one CTA per (sequence, head); thread v owns
+// state column v (hd values in registers), so both reductions over k are
+// sequential in k exactly as in the reference.
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(HD) gdn_recurrence_kernel(float *__restrict__ state,
+                                                            const float *__restrict__ q,
+                                                            const float *__restrict__ kv,
+                                                            const float *__restrict__ vv,
+                                                            const float *__restrict__ beta,
+                                                            const float *__restrict__ g, int heads,
+                                                            float *__restrict__ out) {
+    __shared__ float Ks[HD], Qs[HD];
+    const int b = blockIdx.x, h = blockIdx.y, v = threadIdx.x;
+    const int64_t vec = (static_cast<int64_t>(b) * heads + h) * HD;
+    Ks[v] = kv[vec + v];
+    Qs[v] = q[vec + v];
+    __syncthreads();
+    float *st = state + (static_cast<int64_t>(b) * heads + h) * HD * HD;
+    const float gh = g[b * heads + h], bh = beta[b * heads + h];
+    float s[HD];
+    double acc = 0.0;
+#pragma unroll
+    for (int k = 0; k < HD; ++k) {
+        s[k] = __fmul_rn(st[k * HD + v], gh);
+        acc += static_cast<double>(__fmul_rn(s[k], Ks[k]));
+    }
+    const float delta = __fmul_rn(__fsub_rn(vv[vec + v], static_cast<float>(acc)), bh);
+    double acc2 = 0.0;
+#pragma unroll
+    for (int k = 0; k < HD; ++k) {
+        s[k] = __fadd_rn(s[k], __fmul_rn(Ks[k], delta));
+        st[k * HD + v] = s[k];
+        acc2 += static_cast<double>(__fmul_rn(s[k], Qs[k]));
+    }
+    out[vec + v] = static_cast<float>(acc2);
+}
+
+// Gated RMSNorm: one CTA (hd threads) per (sequence, head).
+__global__ void gdn_gated_norm_kernel(const float *__restrict__ x, const float *__restrict__ z,
+                                      const float *__restrict__ w, int hd, float eps, float *__restrict__ y) {
+    __shared__ double scratch[32];
+    const int64_t base = (static_cast<int64_t>(blockIdx.x) * gridDim.y + blockIdx.y) * hd;
+    const int t = threadIdx.x;
+    const float v = x[base + t];
+    const double ssq = block_sum_d(static_cast<double>(__fmul_rn(v, v)), scratch);
+    const float mean = static_cast<float>(ssq / static_cast<double>(hd));
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    y[base + t] = __fmul_rn(__fmul_rn(__fmul_rn(v, rs), w[t]), silu_f(z[base + t]));
+}
+
+// ---------------------------------------------------------------------------
+// Attention pre-processing: CTA (b, j), hd threads; j < nh is query head j
+// (also emits its gate), j >= nh is KV head j - nh (appends K and V).
+// ---------------------------------------------------------------------------
+__global__ void attn_pre_kernel(const float *__restrict__ qraw, const float *__restrict__ kin,
+                                const float *__restrict__ vin, const float *__restrict__ qn_w,
+                                const float *__restrict__ kn_w, const float *__restrict__ rope, int nh,
+                                int kvh, int hd, int rope_dim, float eps, int pos, int max_pos,
+                                float *__restrict__ qout, float *__restrict__ gate,
+                                __half *__restrict__ kcache, __half *__restrict__ vcache) {
+    __shared__ double scratch[32];
+    __shared__ float xs[512];
+    const int b = blockIdx.x, j = blockIdx.y, t = threadIdx.x;
+    const bool is_q = j < nh;
+    float x;
+    if (is_q) {
+        const float *src = qraw + static_cast<int64_t>(b) * 2 * nh * hd + static_cast<int64_t>(j) * 2 * hd;
+        x = src[t];
+        gate[static_cast<int64_t>(b) * nh * hd + j * hd + t] = src[hd + t];
+    } else {
+        x = kin[static_cast<int64_t>(b) * kvh * hd + (j - nh) * hd + t];
+    }
+    const double ssq = block_sum_d(static_cast<double>(__fmul_rn(x, x)), scratch);
+    const float rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(hd)), eps)));
+    const float xn = __fmul_rn(__fmul_rn(x, rscale), (is_q ? qn_w : kn_w)[t]);
+    xs[t] = xn;
+    __syncthreads();
+    const int half = rope_dim / 2;
+    float y = xn;
+    if (t < rope_dim) {
+        const int i = t < half ? t : t - half;
+        const float c = rope[(static_cast<int64_t>(pos) * half + i) * 2];
+        const float sn = rope[(static_cast<int64_t>(pos) * half + i) * 2 + 1];
+        const float x0 = xs[i], x1 = xs[i + half];
+        y = t < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn))
+                     : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+    if (is_q) {
+        qout[(static_cast<int64_t>(b) * nh + j) * hd + t] = y;
+    } else {
+        const int kh = j - nh;
+        const int64_t row = ((static_cast<int64_t>(b) * max_pos + pos) * kvh + kh) * hd + t;
+        kcache[row] = __float2half_rn(y);
+        vcache[row] = __float2half_rn(vin[static_cast<int64_t>(b) * kvh * hd + kh * hd + t]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Attention over the cache: one CTA (hd threads) per (sequence, query head).
+// ---------------------------------------------------------------------------
+__global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__restrict__ kcache,
+                                   const __half *__restrict__ vcache, const float *__restrict__ gate,
+                                   int nh, int kvh, int hd, int pos, int max_pos, float *__restrict__ ctx) {
+    extern __shared__ float sh[];  // [hd] query, [pos+1] scores, [32] scratch
+    float *qs = sh;
+    float *sc = sh + hd;
+    float *scratch = sc + (pos + 1);
+    __shared__ float total;
+    const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+    const int kh = h / (nh / kvh);
+    const int n = pos + 1;
+    qs[t] = q[(static_cast<int64_t>(b) * nh + h) * hd + t];
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));
+    const __half *kb = kcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * hd;
+    const __half *vb = vcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * hd;
+    const int64_t rstride = static_cast<int64_t>(kvh) * hd;
+    float lmax = -INFINITY;
+    for (int i = t; i < n; i += blockDim.x) {
+        const __half *kr = kb + i * rstride;
+        float dot = 0.0f;
+        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], __half2float(kr[d])));
+        const float s = __fmul_rn(dot, scale);
+        sc[i] = s;
+        lmax = fmaxf(lmax, s);
+    }
+    const float m = block_max_f(lmax, scratch);
+    for (int i = t; i < n; i += blockDim.x) sc[i] = expf_cr(__fsub_rn(sc[i], m));
+    __syncthreads();
+    if (t == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < n; ++i) s = __fadd_rn(s, sc[i]);
+        total = s;
+    }
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, total);
+    for (int i = t; i < n; i += blockDim.x) sc[i] = __fmul_rn(sc[i], inv);
+    __syncthreads();
+    float o = 0.0f;
+    for (int i = 0; i < n; ++i) o = __fadd_rn(o, __fmul_rn(sc[i], __half2float(vb[i * rstride + t])));
+    const int64_t oi = static_cast<int64_t>(b) * nh * hd + h * hd + t;
+    ctx[oi] = __fmul_rn(o, sigmoid_f(gate[oi]));
+}
+
+// Greedy argmax: one CTA per row; ties keep the smaller index.
+__global__ void argmax_kernel(const float *__restrict__ logits, int64_t vocab, int32_t *__restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float *row = logits + static_cast<int64_t>(blockIdx.x) * vocab;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float v = row[i];
+        if (v > best) { best = v; bi = static_cast<int>(i); }
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = sv[0];
+        int i = si[0];
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > b || (sv[w] == b && si[w] < i)) { b = sv[w]; i = si[w]; }
+        out[blockIdx.x] = i == 0x7fffffff ? 0 : i;
+    }
+}
+
+}  // namespace qh
+
+// ---------------------------------------------------------------------------
+// C-ABI launchers
+// ---------------------------------------------------------------------------
+namespace {
+int launch_status(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return QH_OK;
+    char msg[256];
+    snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(e));
+    qh::set_last_error_message(msg);
+    return QH_ERR_CUDA;
+}
+int bad(const char *what) {
+    qh::set_last_error_message(what);
+    return QH_ERR_INVALID;
+}
+}  // namespace
+
+extern "C" {
+
+int qh_embed_q6k(const void *d_table, int64_t hidden, const int32_t *d_tokens, int32_t B, float *d_h,
+                 void *stream) {
+    if (!d_table || !d_tokens || !d_h || hidden % 256 || B <= 0) return bad("qh_embed_q6k: bad arguments");
+    dim3 grid(static_cast<unsigned>(hidden / 256), static_cast<unsigned>(B));
+    qh::embed_q6k_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t *>(d_table), hidden, d_tokens, d_h);
+    return launch_status("qh_embed_q6k");
+}
+
+int qh_rmsnorm(const float *d_x, const float *d_w, int64_t dim, int64_t rows, float eps, float *d_y,
+               void *stream) {
+    if (!d_x || !d_w || !d_y || dim <= 0 || rows <= 0 || rows > 0x7fffffff) return bad("qh_rmsnorm: bad arguments");
+    const int threads = dim >= 256 ? 256 : 128;
+    qh::rmsnorm_kernel<<<static_cast<unsigned>(rows), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_x, d_w, dim, eps, d_y);
+    return launch_status("qh_rmsnorm");
+}
+
+int qh_add(float *d_h, const float *d_mix, int64_t n, void *stream) {
+    if (!d_h || !d_mix || n <= 0) return bad("qh_add: bad arguments");
+    qh::add_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(d_h, d_mix, n);
+    return launch_status("qh_add");
+}
+
+int qh_swiglu(const float *d_gate, const float *d_up, float *d_out, int64_t n, void *stream) {
+    if (!d_gate || !d_up || !d_out || n <= 0) return bad("qh_swiglu: bad arguments");
+    qh::swiglu_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_gate, d_up, d_out, n);
+    return launch_status("qh_swiglu");
+}
+
+int qh_gdn_pre(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b,
+               const float *d_a, const float *d_dt_bias, const float *d_ssm_a, int32_t B,
+               int32_t heads, int32_t hd, int32_t kk, int32_t pos, float *d_q, float *d_k, float *d_v,
+               float *d_beta, float *d_g, void *stream) {
+    if (B <= 0 || heads <= 0 || hd <= 0 || hd % 32 || hd > 1024 || kk <= 0 || pos < 0)
+        return bad("qh_gdn_pre: bad arguments");
+    dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
+    qh::gdn_pre_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, heads, hd, kk, pos, d_q, d_k, d_v, d_beta, d_g);
+    return launch_status("qh_gdn_pre");
+}
+
+int qh_gdn_recurrence(float *d_state, const float *d_q, const float *d_k, const float *d_v,
+                      const float *d_beta, const float *d_g, int32_t B, int32_t heads, int32_t hd,
+                      float *d_out, void *stream) {
+    if (B <= 0 || heads <= 0) return bad("qh_gdn_recurrence: bad arguments");
+    if (hd != 128) {
+        qh::set_last_error_message("qh_gdn_recurrence: head dim must be 128");
+        return QH_ERR_UNSUPPORTED;
+    }
+    dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
+    qh::gdn_recurrence_kernel<128><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_state, d_q, d_k, d_v, d_beta, d_g, heads, d_out);
+    return launch_status("qh_gdn_recurrence");
+}
+
+int qh_gdn_gated_norm(const float *d_x, const float *d_z, const float *d_w, int32_t B, int32_t heads,
+                      int32_t hd, float eps, float *d_y, void *stream) {
+    if (B <= 0 || heads <= 0 || hd <= 0 || hd % 32 || hd > 1024) return bad("qh_gdn_gated_norm: bad arguments");
+    dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
+    qh::gdn_gated_norm_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(d_x, d_z, d_w, hd, eps, d_y);
+    return launch_status("qh_gdn_gated_norm");
+}
+
+int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
+                const float *d_knorm_w, const float *d_rope, int32_t B, int32_t nh, int32_t kvh,
+                int32_t hd, int32_t rope_dim, float eps, int32_t pos, int32_t max_pos, float *d_q,
+                float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream) {
+    if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 512 || rope_dim > hd || rope_dim % 2 ||
+        pos < 0 || pos >= max_pos)
+        return bad("qh_attn_pre: bad arguments");
+    dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh + kvh));
+    qh::attn_pre_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, nh, kvh, hd, rope_dim, eps, pos, max_pos, d_q, d_gate,
+        reinterpret_cast<__half *>(d_kcache), reinterpret_cast<__half *>(d_vcache));
+    return launch_status("qh_attn_pre");
+}
+
+int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache,
+                   const float *d_gate, int32_t B, int32_t nh, int32_t kvh, int32_t hd, int32_t pos,
+                   int32_t max_pos, float *d_ctx, void *stream) {
+    if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 1024 || pos < 0 || pos >= max_pos)
+        return bad("qh_attn_decode: bad arguments");
+    const size_t smem = sizeof(float) * (static_cast<size_t>(hd) + pos + 1 + 32);
+    if (smem > 200 * 1024) return bad("qh_attn_decode: context too long");
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaFuncSetAttribute(qh::attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr_done[dev] = true;
+    }
+    dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh));
+    qh::attn_decode_kernel<<<grid, hd, smem, static_cast<cudaStream_t>(stream)>>>(
+        d_q, reinterpret_cast<const __half *>(d_kcache), reinterpret_cast<const __half *>(d_vcache), d_gate, nh,
+        kvh, hd, pos, max_pos, d_ctx);
+    return launch_status("qh_attn_decode");
+}
+
+int qh_argmax(const float *d_logits, int32_t B, int64_t vocab, int32_t *d_out, void *stream) {
+    if (!d_logits || !d_out || B <= 0 || vocab <= 0) return bad("qh_argmax: bad arguments");
+    qh::argmax_kernel<<<static_cast<unsigned>(B), 1024, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, vocab, d_out);
+    return launch_status("qh_argmax");
+}
+
+}  // extern "C"

@@ -1,0 +1,448 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_slm.c -- host step driver of the hybrid forward pass (include/qh_slm.h).
+//
+// C host layer over the backend C-ABI: it uploads the GGUF-layout weights,
+// owns the per-sequence caches and chains, per token and for all sequences
+// at once, the same operations as the reference's slm_forward_step
+// (slm/qwen.c:874-981):
+//   embed (Q6_K row) -> for each layer:
+//     GDN layer  (slm/qwen.c:318-611): rmsnorm, one grouped matvec launch for
+//       attn_qkv/attn_gate/ssm_beta/ssm_alpha, conv+SiLU+L2norm+beta/g,
+//       recurrence, gated norm, ssm_out;
+//     attention  (slm/model.c:766-953): rmsnorm, grouped q/k/v, q/k norm +
+//       MRoPE + fp16 KV append, attention + sigmoid gate, attn_output;
+//     residual add, post-attention rmsnorm, grouped ffn_gate/ffn_up, SwiGLU,
+//     ffn_down (Q6_K), residual add;
+//   output rmsnorm -> tied Q6_K LM head -> argmax.
+// Every matmul input is quantized once on the device (Q8_K) and shared by
+// the projections that read it, which is what the reference's
+// tensor_matmul_* wrappers compute per call.
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <cuda_runtime_api.h>
+
+#include "qh_backend.h"
+#include "qh_formats.h"
+#include "qh_kernels.h"
+#include "qh_slm.h"
+
+#define MAX_LAYERS 128
+
+typedef struct {
+    qh_matvec_plan plan[8];  // one per 8-token chunk set (see make_plan)
+    int nplan;
+} plan_set;
+
+typedef struct {
+    int is_attn;
+    const float *attn_norm, *ffn_norm;
+    const void *ffn_gate, *ffn_up, *ffn_down;
+    // GDN
+    const void *qkv, *gate, *alpha, *beta, *ssm_out;
+    const float *ssm_a, *conv_w, *dt_bias, *ssm_norm;
+    // attention
+    const void *wq, *wk, *wv, *wo;
+    const float *q_norm, *k_norm;
+    int gdn_index, attn_index;
+    plan_set p_in, p_out, p_ffn, p_down;
+} layer;
+
+struct qh_slm {
+    qh_slm_config cfg;
+    int32_t B;
+    cudaStream_t stream;
+    void **allocs;
+    int nallocs, capallocs;
+    int64_t weight_bytes, state_bytes;
+    const void *tok_embd;
+    const float *out_norm;
+    layer L[MAX_LAYERS];
+    int n_gdn, n_attn;
+    // activations [B][...]
+    float *h, *hn, *mix, *qkv, *z, *bt, *at, *gq, *gk, *gv, *gbeta, *gg, *gout, *gy;
+    float *qraw, *kb, *vb, *aq, *agate, *actx, *fgate, *fup, *fact, *logits, *rope;
+    void *xq_h, *xq_gdn, *xq_ffn;  // split Q8_K activations for K = hidden, gdn width, ffn
+    int32_t *d_tok, *d_next;
+    int32_t *h_tok, *h_next;  // pinned
+    // caches
+    float *ring, *state;
+    uint16_t *kcache, *vcache;
+    plan_set p_head;
+};
+
+static int dev_alloc(qh_slm *m, void **p, size_t bytes, int64_t *counter) {
+    if (m->nallocs == m->capallocs) {
+        int cap = m->capallocs ? 2 * m->capallocs : 256;
+        void **a = (void **)realloc(m->allocs, sizeof(void *) * cap);
+        if (!a) return QH_ERR_INVALID;
+        m->allocs = a;
+        m->capallocs = cap;
+    }
+    int rc = qh_malloc(p, bytes);
+    if (rc) return rc;
+    m->allocs[m->nallocs++] = *p;
+    if (counter) *counter += (int64_t)bytes;
+    return QH_OK;
+}
+
+#define CK(x) do { int rc_ = (x); if (rc_) return rc_; } while (0)
+
+static int upload(qh_slm *m, const qh_blob *blob, const char *name, const void **out) {
+    int i = qh_blob_find(blob, name);
+    if (i < 0) return QH_ERR_INVALID;
+    const void *data;
+    int64_t nbytes;
+    CK(qh_blob_tensor(blob, i, NULL, NULL, NULL, &data, &nbytes));
+    void *d;
+    CK(dev_alloc(m, &d, (size_t)nbytes, &m->weight_bytes));
+    CK(qh_memcpy_h2d(d, data, (size_t)nbytes, m->stream));
+    *out = d;
+    return QH_OK;
+}
+
+// A plan over `nm` matrices of one type sharing the activation buffer xq
+// (quantized for B rows of k). B <= 8: one job per matrix with n_tok = B;
+// B > 8 (a multiple of 8): one job per (matrix, 8-row chunk).
+static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *const *w,
+                     const int64_t *out_f, float *const *out, const void *xq, int64_t k) {
+    const int32_t B = m->B;
+    const int chunks = B <= 8 ? 1 : B / 8;
+    const int nt = B <= 8 ? B : 8;
+    qh_matvec_job *jobs = (qh_matvec_job *)calloc((size_t)nm * chunks, sizeof(qh_matvec_job));
+    if (!jobs) return QH_ERR_INVALID;
+    int n = 0;
+    for (int c = 0; c < chunks; ++c)
+        for (int i = 0; i < nm; ++i) {
+            jobs[n].d_w = w[i];
+            jobs[n].d_xq = xq;
+            jobs[n].d_out = out[i] + (int64_t)c * nt * out_f[i];
+            jobs[n].k = k;
+            jobs[n].out_f = out_f[i];
+            jobs[n].xq_rows = B;
+            jobs[n].xq_row0 = (int64_t)c * nt;
+            ++n;
+        }
+    int rc = qh_matvec_plan_create(type, jobs, n, nt, &ps->plan[0]);
+    free(jobs);
+    if (rc) return rc;
+    ps->nplan = 1;
+    return QH_OK;
+}
+
+static int run_plans(qh_slm *m, plan_set *ps) {
+    for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
+    return QH_OK;
+}
+
+static void free_plans(plan_set *ps) {
+    for (int i = 0; i < ps->nplan; ++i) qh_matvec_plan_destroy(ps->plan[i]);
+    ps->nplan = 0;
+}
+
+// cos/sin of the interleaved-MRoPE angles for text positions, computed with
+// the host libm exactly as tensor_rope_mrope_i does (slm/tensor.c:394-437):
+// pair i rotates by pos * theta^(-2i/rope_dim) when i % 3 == 0 and
+// i < 3*sections[0]; the H/W/E axes are 0 for text, leaving those pairs
+// unrotated (cos 1, sin 0).
+static void rope_table(const qh_slm_config *c, float *tab) {
+    const int half = c->rope_dim / 2;
+    for (int p = 0; p < c->max_pos; ++p)
+        for (int i = 0; i < half; ++i) {
+            float pos_axis = 0.0f;
+            if (i % 3 == 0 && i < 3 * c->rope_sections[0]) pos_axis = (float)p;
+            const float theta_scale = powf(c->rope_theta, -2.0f * (float)i / (float)c->rope_dim);
+            const float theta = pos_axis * theta_scale;
+            tab[((size_t)p * half + i) * 2] = cosf(theta);
+            tab[((size_t)p * half + i) * 2 + 1] = sinf(theta);
+        }
+}
+
+static int bind_layers(qh_slm *m, const qh_blob *blob) {
+    const qh_slm_config *c = &m->cfg;
+    char nm[96];
+#define W(field, fmt) do { snprintf(nm, sizeof(nm), fmt, l); CK(upload(m, blob, nm, (const void **)&Ly->field)); } while (0)
+    for (int l = 0; l < c->n_layers; ++l) {
+        layer *Ly = &m->L[l];
+        snprintf(nm, sizeof(nm), "blk.%d.ssm_a", l);
+        Ly->is_attn = qh_blob_find(blob, nm) < 0;
+        W(attn_norm, "blk.%d.attn_norm.weight");
+        W(ffn_norm, "blk.%d.post_attention_norm.weight");
+        W(ffn_gate, "blk.%d.ffn_gate.weight");
+        W(ffn_up, "blk.%d.ffn_up.weight");
+        W(ffn_down, "blk.%d.ffn_down.weight");
+        if (Ly->is_attn) {
+            W(wq, "blk.%d.attn_q.weight");
+            W(wk, "blk.%d.attn_k.weight");
+            W(wv, "blk.%d.attn_v.weight");
+            W(wo, "blk.%d.attn_output.weight");
+            W(q_norm, "blk.%d.attn_q_norm.weight");
+            W(k_norm, "blk.%d.attn_k_norm.weight");
+            Ly->attn_index = m->n_attn++;
+        } else {
+            W(qkv, "blk.%d.attn_qkv.weight");
+            W(gate, "blk.%d.attn_gate.weight");
+            W(alpha, "blk.%d.ssm_alpha.weight");
+            W(beta, "blk.%d.ssm_beta.weight");
+            W(ssm_out, "blk.%d.ssm_out.weight");
+            W(ssm_a, "blk.%d.ssm_a");
+            W(conv_w, "blk.%d.ssm_conv1d.weight");
+            W(dt_bias, "blk.%d.ssm_dt.bias");
+            W(ssm_norm, "blk.%d.ssm_norm.weight");
+            Ly->gdn_index = m->n_gdn++;
+        }
+    }
+#undef W
+    return QH_OK;
+}
+
+static int alloc_f(qh_slm *m, float **p, int64_t n) { return dev_alloc(m, (void **)p, (size_t)n * 4, NULL); }
+
+int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, qh_slm **out) {
+    if (!cfg || !blob || !out || n_seq <= 0 || (n_seq > 8 && n_seq % 8) || cfg->n_layers > MAX_LAYERS ||
+        cfg->n_heads % cfg->n_kv_heads || cfg->max_pos <= 0)
+        return QH_ERR_INVALID;
+    *out = NULL;
+    qh_slm *m = (qh_slm *)calloc(1, sizeof(qh_slm));
+    if (!m) return QH_ERR_INVALID;
+    m->cfg = *cfg;
+    m->B = n_seq;
+    int rc = QH_OK;
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
+#define TRY(x) do { rc = (x); if (rc) goto fail; } while (0)
+    TRY(upload(m, blob, "token_embd.weight", &m->tok_embd));
+    TRY(upload(m, blob, "output_norm.weight", (const void **)&m->out_norm));
+    TRY(bind_layers(m, blob));
+    {
+        const int64_t B = n_seq, H = cfg->hidden, F = cfg->ffn, hd = cfg->head_dim;
+        const int64_t kdim = (int64_t)cfg->gdn_heads * cfg->gdn_head_dim, conv_dim = 3 * kdim;
+        const int64_t qdim = (int64_t)cfg->n_heads * hd, kvd = (int64_t)cfg->n_kv_heads * hd;
+        TRY(alloc_f(m, &m->h, B * H));
+        TRY(alloc_f(m, &m->hn, B * H));
+        TRY(alloc_f(m, &m->mix, B * H));
+        TRY(alloc_f(m, &m->qkv, B * conv_dim));
+        TRY(alloc_f(m, &m->z, B * kdim));
+        TRY(alloc_f(m, &m->bt, B * cfg->gdn_heads));
+        TRY(alloc_f(m, &m->at, B * cfg->gdn_heads));
+        TRY(alloc_f(m, &m->gq, B * kdim));
+        TRY(alloc_f(m, &m->gk, B * kdim));
+        TRY(alloc_f(m, &m->gv, B * kdim));
+        TRY(alloc_f(m, &m->gbeta, B * cfg->gdn_heads));
+        TRY(alloc_f(m, &m->gg, B * cfg->gdn_heads));
+        TRY(alloc_f(m, &m->gout, B * kdim));
+        TRY(alloc_f(m, &m->gy, B * kdim));
+        TRY(alloc_f(m, &m->qraw, B * 2 * qdim));
+        TRY(alloc_f(m, &m->kb, B * kvd));
+        TRY(alloc_f(m, &m->vb, B * kvd));
+        TRY(alloc_f(m, &m->aq, B * qdim));
+        TRY(alloc_f(m, &m->agate, B * qdim));
+        TRY(alloc_f(m, &m->actx, B * qdim));
+        TRY(alloc_f(m, &m->fgate, B * F));
+        TRY(alloc_f(m, &m->fup, B * F));
+        TRY(alloc_f(m, &m->fact, B * F));
+        TRY(alloc_f(m, &m->logits, B * cfg->vocab));
+        const int64_t max_in = H > qdim ? H : qdim;
+        TRY(dev_alloc(m, &m->xq_h, (size_t)qh_q8k_bytes(max_in, B), NULL));
+        TRY(dev_alloc(m, &m->xq_gdn, (size_t)qh_q8k_bytes(kdim, B), NULL));
+        TRY(dev_alloc(m, &m->xq_ffn, (size_t)qh_q8k_bytes(F, B), NULL));
+        TRY(dev_alloc(m, (void **)&m->d_tok, (size_t)B * 4, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_next, (size_t)B * 4, NULL));
+        if (cudaMallocHost((void **)&m->h_tok, (size_t)B * 4) != cudaSuccess ||
+            cudaMallocHost((void **)&m->h_next, (size_t)B * 4) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
+        // caches
+        const int64_t ng = m->n_gdn > 0 ? m->n_gdn : 1, na = m->n_attn > 0 ? m->n_attn : 1;
+        TRY(dev_alloc(m, (void **)&m->ring, (size_t)(ng * B * cfg->conv_kernel * conv_dim * 4), &m->state_bytes));
+        TRY(dev_alloc(m, (void **)&m->state,
+                      (size_t)(ng * B * cfg->gdn_heads * (int64_t)cfg->gdn_head_dim * cfg->gdn_head_dim * 4),
+                      &m->state_bytes));
+        const size_t kv = (size_t)(na * B * cfg->max_pos * kvd * 2);
+        TRY(dev_alloc(m, (void **)&m->kcache, kv, &m->state_bytes));
+        TRY(dev_alloc(m, (void **)&m->vcache, kv, &m->state_bytes));
+        // rope table
+        const size_t rb = (size_t)cfg->max_pos * (cfg->rope_dim / 2) * 2 * sizeof(float);
+        float *tab = (float *)malloc(rb);
+        if (!tab) { rc = QH_ERR_INVALID; goto fail; }
+        rope_table(cfg, tab);
+        rc = dev_alloc(m, (void **)&m->rope, rb, NULL);
+        if (!rc) rc = qh_memcpy_h2d(m->rope, tab, rb, m->stream);
+        if (!rc) rc = qh_stream_sync(m->stream);
+        free(tab);
+        if (rc) goto fail;
+        // matvec plans
+        for (int l = 0; l < cfg->n_layers; ++l) {
+            layer *Ly = &m->L[l];
+            if (Ly->is_attn) {
+                const void *w[3] = {Ly->wq, Ly->wk, Ly->wv};
+                const int64_t of[3] = {2 * qdim, kvd, kvd};
+                float *o[3] = {m->qraw, m->kb, m->vb};
+                TRY(make_plan(m, &Ly->p_in, QH_TYPE_Q4_K, 3, w, of, o, m->xq_h, H));
+                const void *w2[1] = {Ly->wo};
+                const int64_t of2[1] = {H};
+                float *o2[1] = {m->mix};
+                TRY(make_plan(m, &Ly->p_out, QH_TYPE_Q4_K, 1, w2, of2, o2, m->xq_h, qdim));
+            } else {
+                const void *w[4] = {Ly->qkv, Ly->gate, Ly->beta, Ly->alpha};
+                const int64_t of[4] = {conv_dim, kdim, cfg->gdn_heads, cfg->gdn_heads};
+                float *o[4] = {m->qkv, m->z, m->bt, m->at};
+                TRY(make_plan(m, &Ly->p_in, QH_TYPE_Q4_K, 4, w, of, o, m->xq_h, H));
+                const void *w2[1] = {Ly->ssm_out};
+                const int64_t of2[1] = {H};
+                float *o2[1] = {m->mix};
+                TRY(make_plan(m, &Ly->p_out, QH_TYPE_Q4_K, 1, w2, of2, o2, m->xq_gdn, kdim));
+            }
+            const void *wf[2] = {Ly->ffn_gate, Ly->ffn_up};
+            const int64_t off[2] = {F, F};
+            float *of_[2] = {m->fgate, m->fup};
+            TRY(make_plan(m, &Ly->p_ffn, QH_TYPE_Q4_K, 2, wf, off, of_, m->xq_h, H));
+            const void *wd[1] = {Ly->ffn_down};
+            const int64_t ofd[1] = {H};
+            float *od[1] = {m->mix};
+            TRY(make_plan(m, &Ly->p_down, QH_TYPE_Q6_K, 1, wd, ofd, od, m->xq_ffn, F));
+        }
+        const void *wh[1] = {m->tok_embd};
+        const int64_t ofh[1] = {cfg->vocab};
+        float *oh[1] = {m->logits};
+        TRY(make_plan(m, &m->p_head, QH_TYPE_Q6_K, 1, wh, ofh, oh, m->xq_h, H));
+    }
+#undef TRY
+    rc = qh_slm_reset(m);
+    if (rc) goto fail;
+    *out = m;
+    return QH_OK;
+fail:
+    qh_slm_destroy(m);
+    return rc ? rc : QH_ERR_INVALID;
+}
+
+void qh_slm_destroy(qh_slm *m) {
+    if (!m) return;
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (int l = 0; l < m->cfg.n_layers && l < MAX_LAYERS; ++l) {
+        free_plans(&m->L[l].p_in);
+        free_plans(&m->L[l].p_out);
+        free_plans(&m->L[l].p_ffn);
+        free_plans(&m->L[l].p_down);
+    }
+    free_plans(&m->p_head);
+    for (int i = 0; i < m->nallocs; ++i) qh_free(m->allocs[i]);
+    free(m->allocs);
+    if (m->h_tok) cudaFreeHost(m->h_tok);
+    if (m->h_next) cudaFreeHost(m->h_next);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    free(m);
+}
+
+int qh_slm_reset(qh_slm *m) {
+    if (!m) return QH_ERR_INVALID;
+    const qh_slm_config *c = &m->cfg;
+    const int64_t B = m->B, kdim = (int64_t)c->gdn_heads * c->gdn_head_dim;
+    const int64_t ng = m->n_gdn > 0 ? m->n_gdn : 1, na = m->n_attn > 0 ? m->n_attn : 1;
+    const int64_t kvd = (int64_t)c->n_kv_heads * c->head_dim;
+    CK(qh_memset(m->ring, 0, (size_t)(ng * B * c->conv_kernel * 3 * kdim * 4), m->stream));
+    CK(qh_memset(m->state, 0, (size_t)(ng * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim * 4), m->stream));
+    CK(qh_memset(m->kcache, 0, (size_t)(na * B * c->max_pos * kvd * 2), m->stream));
+    CK(qh_memset(m->vcache, 0, (size_t)(na * B * c->max_pos * kvd * 2), m->stream));
+    return qh_stream_sync(m->stream);
+}
+
+// One forward step for all sequences; tokens already in m->d_tok.
+static int forward(qh_slm *m, int32_t pos) {
+    const qh_slm_config *c = &m->cfg;
+    const int32_t B = m->B;
+    const int64_t H = c->hidden, F = c->ffn, hd = c->head_dim;
+    const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
+    const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
+    void *s = m->stream;
+    CK(qh_embed_q6k(m->tok_embd, H, m->d_tok, B, m->h, s));
+    for (int l = 0; l < c->n_layers; ++l) {
+        layer *Ly = &m->L[l];
+        CK(qh_rmsnorm(m->h, Ly->attn_norm, H, B, c->norm_eps, m->hn, s));
+        CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
+        CK(run_plans(m, &Ly->p_in));
+        if (Ly->is_attn) {
+            const int64_t ai = Ly->attn_index;
+            uint16_t *kc = m->kcache + ai * B * c->max_pos * kvd;
+            uint16_t *vc = m->vcache + ai * B * c->max_pos * kvd;
+            CK(qh_attn_pre(m->qraw, m->kb, m->vb, Ly->q_norm, Ly->k_norm, m->rope, B, c->n_heads, c->n_kv_heads,
+                           (int32_t)hd, c->rope_dim, c->norm_eps, pos, c->max_pos, m->aq, m->agate, kc, vc, s));
+            CK(qh_attn_decode(m->aq, kc, vc, m->agate, B, c->n_heads, c->n_kv_heads, (int32_t)hd, pos,
+                              c->max_pos, m->actx, s));
+            CK(qh_quantize_q8k(m->actx, qdim, B, m->xq_h, s));
+        } else {
+            const int64_t gi = Ly->gdn_index;
+            float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
+            float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
+            CK(qh_gdn_pre(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, B, c->gdn_heads,
+                          c->gdn_head_dim, c->conv_kernel, pos, m->gq, m->gk, m->gv, m->gbeta, m->gg, s));
+            CK(qh_gdn_recurrence(state, m->gq, m->gk, m->gv, m->gbeta, m->gg, B, c->gdn_heads, c->gdn_head_dim,
+                                 m->gout, s));
+            CK(qh_gdn_gated_norm(m->gout, m->z, Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->norm_eps,
+                                 m->gy, s));
+            CK(qh_quantize_q8k(m->gy, kdim, B, m->xq_gdn, s));
+        }
+        CK(run_plans(m, &Ly->p_out));
+        CK(qh_add(m->h, m->mix, B * H, s));
+        CK(qh_rmsnorm(m->h, Ly->ffn_norm, H, B, c->norm_eps, m->hn, s));
+        CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
+        CK(run_plans(m, &Ly->p_ffn));
+        CK(qh_swiglu(m->fgate, m->fup, m->fact, B * F, s));
+        CK(qh_quantize_q8k(m->fact, F, B, m->xq_ffn, s));
+        CK(run_plans(m, &Ly->p_down));
+        CK(qh_add(m->h, m->mix, B * H, s));
+    }
+    CK(qh_rmsnorm(m->h, m->out_norm, H, B, c->norm_eps, m->hn, s));
+    CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
+    CK(run_plans(m, &m->p_head));
+    CK(qh_argmax(m->logits, B, c->vocab, m->d_next, s));
+    return QH_OK;
+}
+
+int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next, float *h_logits) {
+    if (!m || !h_tokens || pos < 0 || pos >= m->cfg.max_pos) return QH_ERR_INVALID;
+    memcpy(m->h_tok, h_tokens, sizeof(int32_t) * m->B);
+    for (int32_t b = 0; b < m->B; ++b)
+        if (m->h_tok[b] < 0 || m->h_tok[b] >= m->cfg.vocab) return QH_ERR_INVALID;
+    CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * m->B, m->stream));
+    CK(forward(m, pos));
+    CK(qh_memcpy_d2h(m->h_next, m->d_next, sizeof(int32_t) * m->B, m->stream));
+    if (h_logits)
+        CK(qh_memcpy_d2h(h_logits, m->logits, sizeof(float) * (size_t)m->B * m->cfg.vocab, m->stream));
+    CK(qh_stream_sync(m->stream));
+    CK(qh_check_device_error(NULL));
+    if (h_next) memcpy(h_next, m->h_next, sizeof(int32_t) * m->B);
+    return QH_OK;
+}
+
+int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out) {
+    if (!m || !prompt || !out || n_prompt <= 0 || n_new < 0 || n_prompt + n_new > m->cfg.max_pos + 1)
+        return QH_ERR_INVALID;
+    const int32_t B = m->B;
+    int32_t *tok = (int32_t *)malloc(sizeof(int32_t) * B), *nxt = (int32_t *)malloc(sizeof(int32_t) * B);
+    if (!tok || !nxt) { free(tok); free(nxt); return QH_ERR_INVALID; }
+    int rc = QH_OK;
+    int32_t pos = 0;
+    for (int32_t i = 0; i < n_prompt && !rc; ++i, ++pos) {
+        for (int32_t b = 0; b < B; ++b) tok[b] = prompt[(int64_t)b * n_prompt + i];
+        rc = qh_slm_step(m, tok, pos, nxt, NULL);
+    }
+    for (int32_t j = 0; j < n_new && !rc; ++j) {
+        for (int32_t b = 0; b < B; ++b) out[(int64_t)b * n_new + j] = nxt[b];
+        if (j + 1 == n_new) break;
+        memcpy(tok, nxt, sizeof(int32_t) * B);
+        rc = qh_slm_step(m, tok, pos++, nxt, NULL);
+    }
+    free(tok);
+    free(nxt);
+    return rc;
+}
+
+int qh_slm_memory(const qh_slm *m, int64_t *weight_bytes, int64_t *state_bytes) {
+    if (!m) return QH_ERR_INVALID;
+    if (weight_bytes) *weight_bytes = m->weight_bytes;
+    if (state_bytes) *state_bytes = m->state_bytes;
+    return QH_OK;
+}

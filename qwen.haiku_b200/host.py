@@ -177,3 +177,92 @@ class MatvecPlan:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------------------
+# Model level (include/qh_slm.h)
+# ---------------------------------------------------------------------------
+from . import SlmConfig  # noqa: E402
+
+
+def slm_config(max_pos: int = 320, **over) -> SlmConfig:
+    """BASELINE config 4 shape (qh_slm_config_default) with field overrides."""
+    c = SlmConfig()
+    lib().qh_slm_config_default(C.byref(c), max_pos)
+    for k, v in over.items():
+        if k == "rope_sections":
+            for i, x in enumerate(v):
+                c.rope_sections[i] = x
+        else:
+            setattr(c, k, v)
+    return c
+
+
+class Blob:
+    """Synthetic weight blob (qh_blob_synthetic)."""
+
+    def __init__(self, cfg: SlmConfig, seed: int):
+        h = C.c_void_p()
+        check(lib().qh_blob_synthetic(C.byref(cfg), seed, C.byref(h)), "qh_blob_synthetic")
+        self.handle, self.cfg = h, cfg
+
+    def tensors(self):
+        """[(name, type, (shape0, shape1), data pointer, nbytes)]"""
+        L, out = lib(), []
+        for i in range(L.qh_blob_count(self.handle)):
+            name, typ, data, nb = C.c_char_p(), C.c_int32(), C.c_void_p(), C.c_int64()
+            shape = (C.c_int64 * 2)()
+            check(L.qh_blob_tensor(self.handle, i, C.byref(name), C.byref(typ), shape, C.byref(data),
+                                   C.byref(nb)), "qh_blob_tensor")
+            out.append((name.value.decode(), typ.value, (shape[0], shape[1]), data.value, nb.value))
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().qh_blob_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Slm:
+    """Device model with n_seq sequences (qh_slm_create)."""
+
+    def __init__(self, cfg: SlmConfig, blob: Blob, n_seq: int = 1):
+        _torch()
+        h = C.c_void_p()
+        check(lib().qh_slm_create(C.byref(cfg), blob.handle, n_seq, C.byref(h)), "qh_slm_create")
+        self.handle, self.cfg, self.n_seq = h, cfg, n_seq
+
+    def reset(self):
+        check(lib().qh_slm_reset(self.handle), "qh_slm_reset")
+
+    def step(self, tokens, pos: int, want_logits: bool = False):
+        toks = np.ascontiguousarray(tokens, np.int32).reshape(self.n_seq)
+        nxt = np.empty(self.n_seq, np.int32)
+        logits = np.empty((self.n_seq, self.cfg.vocab), np.float32) if want_logits else None
+        check(lib().qh_slm_step(self.handle, toks.ctypes.data, pos, nxt.ctypes.data,
+                                logits.ctypes.data if logits is not None else None), "qh_slm_step")
+        return (nxt, logits) if want_logits else nxt
+
+    def generate(self, prompt, n_new: int):
+        p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
+        out = np.empty((self.n_seq, n_new), np.int32)
+        check(lib().qh_slm_generate(self.handle, p.ctypes.data, p.shape[1], n_new, out.ctypes.data),
+              "qh_slm_generate")
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().qh_slm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

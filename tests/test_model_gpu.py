@@ -1,0 +1,166 @@
+# SPDX-License-Identifier: MIT
+"""GPU: the device forward pass (include/qh_slm.h) against the reference's
+own slm_forward_step + sample_argmax (oracle/_ref, compiled from its
+sources), on the same synthetic weights.
+
+Bar (north star): greedy token streams identical, except that a divergence
+is exempt at a step where the reference's top-2 logit gap is below 1e-3;
+comparison stops at the first exempt step.
+
+Two builds of the reference are used. `ref_cr` is the reference's sources
+with expf/logf correctly rounded, the arithmetic the device kernels
+implement: against it the bar above is asserted over the full BASELINE
+config-4 run. `ref` is the stock build on the host glibc, whose expf/logf
+are off by one ulp for ~6e-4 of inputs; the model's Q8_K activation
+quantization turns such ulps into int8 flips in later layers, so against
+it the test records where the streams part and asserts the start.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GAP = 1e-3
+
+
+def ref_run(ref, RefModel, cfg, tensors, prompt, n_new):
+    """Teacher-forced prompt then greedy; returns (predictions, top2 gaps, logits)."""
+    rm = RefModel(ref, cfg, tensors)
+    preds, gaps, logits = [], [], []
+    tok = prompt[0]
+    for pos in range(len(prompt) + n_new - 1):
+        a, lg = rm.step(tok, pos, want_logits=True)
+        s = np.sort(lg)[::-1]
+        preds.append(a)
+        gaps.append(float(s[0] - s[1]))
+        logits.append(lg)
+        tok = prompt[pos + 1] if pos + 1 < len(prompt) else a
+    rm.close()
+    return np.array(preds), np.array(gaps), logits
+
+
+def gpu_run(slm, prompts, n_new):
+    """Same schedule on the device for all sequences at once."""
+    B, n_prompt = prompts.shape
+    slm.reset()
+    preds, logits = [], []
+    tok = prompts[:, 0].copy()
+    for pos in range(n_prompt + n_new - 1):
+        nxt, lg = slm.step(tok, pos, want_logits=True)
+        preds.append(nxt.copy())
+        logits.append(lg.copy())
+        tok = prompts[:, pos + 1] if pos + 1 < n_prompt else nxt
+    return np.stack(preds, 1), np.stack(logits, 1)
+
+
+def check_stream(ref_preds, ref_gaps, gpu_preds, label):
+    mism = np.flatnonzero(ref_preds != gpu_preds)
+    if mism.size == 0:
+        return len(ref_preds)
+    i = mism[0]
+    assert ref_gaps[i] < GAP, (f"{label}: token {i} differs (ref {ref_preds[i]}, gpu {gpu_preds[i]}) "
+                               f"with a top-2 gap of {ref_gaps[i]:.3g} >= {GAP}")
+    return i
+
+
+@pytest.fixture(scope="module")
+def small(qh, cuda):
+    cfg = qh.host.slm_config(64, n_layers=4, vocab=4096)
+    blob = qh.host.Blob(cfg, 0x51A11)
+    return cfg, blob, blob.tensors()
+
+
+def test_small_model_batch1_parity(qh, cuda, ref_cr, small):
+    from oracle.oracle import RefModel
+    cfg, blob, tensors = small
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(0, cfg.vocab, 12).astype(np.int32)
+    rp, rg, rl = ref_run(ref_cr, RefModel, cfg, tensors, prompt, 20)
+    slm = qh.host.Slm(cfg, blob, 1)
+    gp, gl = gpu_run(slm, prompt[None, :], 20)
+    n = check_stream(rp, rg, gp[0], "small b1")
+    exact = sum(np.array_equal(gl[0, i].view(np.uint32), rl[i].view(np.uint32)) for i in range(n))
+    worst = max(float(np.abs(gl[0, i] - rl[i]).max() / np.abs(rl[i]).max()) for i in range(n))
+    print(f"small b1: {exact} of {n} steps bit-identical logits, worst rel diff {worst:.2e}")
+    assert worst < 1e-4, f"logits drift {worst:.3e}"
+    slm.close()
+
+
+def test_small_model_batched_sequences_independent(qh, cuda, ref_cr, small):
+    """8 sequences in one batch each match their own reference run."""
+    from oracle.oracle import RefModel
+    cfg, blob, tensors = small
+    B, n_prompt, n_new = 8, 10, 12
+    rng = np.random.default_rng(2)
+    prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
+    slm = qh.host.Slm(cfg, blob, B)
+    gp, _ = gpu_run(slm, prompts, n_new)
+    for b in range(B):
+        rp, rg, _ = ref_run(ref_cr, RefModel, cfg, tensors, prompts[b], n_new)
+        check_stream(rp, rg, gp[b], f"seq {b}")
+    slm.close()
+
+
+def test_batch16_matches_batch1(qh, cuda, small):
+    """B > 8 runs the matvecs in 8-row chunks; results equal B = 1 runs."""
+    cfg, blob, _ = small
+    B, n_prompt, n_new = 16, 6, 6
+    rng = np.random.default_rng(3)
+    prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
+    big = qh.host.Slm(cfg, blob, B)
+    gp, gl = gpu_run(big, prompts, n_new)
+    big.close()
+    one = qh.host.Slm(cfg, blob, 1)
+    for b in (0, 7, 8, 15):
+        p1, l1 = gpu_run(one, prompts[b:b + 1], n_new)
+        assert np.array_equal(p1[0], gp[b])
+        assert np.array_equal(l1[0].view(np.uint32), gl[b].view(np.uint32)), f"seq {b} logits differ"
+    one.close()
+
+
+def test_generate_api_matches_steps(qh, cuda, small):
+    cfg, blob, _ = small
+    rng = np.random.default_rng(4)
+    prompts = rng.integers(0, cfg.vocab, (2, 8)).astype(np.int32)
+    slm = qh.host.Slm(cfg, blob, 2)
+    gp, _ = gpu_run(slm, prompts, 10)
+    slm.reset()
+    out = slm.generate(prompts, 10)
+    assert np.array_equal(out, gp[:, 7:])
+    slm.close()
+
+
+@pytest.fixture(scope="module")
+def full(qh, cuda):
+    cfg = qh.host.slm_config(320)
+    blob = qh.host.Blob(cfg, 0xC0F16)
+    rng = np.random.default_rng(0xC4)
+    prompt = rng.integers(0, cfg.vocab, 64).astype(np.int32)
+    slm = qh.host.Slm(cfg, blob, 1)
+    gp, gl = gpu_run(slm, prompt[None, :], 256)
+    slm.close()
+    return cfg, blob, blob.tensors(), prompt, gp[0], gl[0]
+
+
+def test_full_model_greedy_parity_config4(qh, cuda, ref_cr, full):
+    """full-size model, 64-token prompt, 256 greedy tokens."""
+    from oracle.oracle import RefModel
+    cfg, blob, tensors, prompt, gp, gl = full
+    rp, rg, rl = ref_run(ref_cr, RefModel, cfg, tensors, prompt, 256)
+    n = check_stream(rp, rg, gp, "config 4")
+    exact = sum(np.array_equal(gl[i].view(np.uint32), rl[i].view(np.uint32)) for i in range(n))
+    print(f"config 4 vs correctly rounded libm: {n} of {len(rp)} predictions equal, "
+          f"{exact} steps with bit-identical logits")
+    assert n == len(rp) or rg[n] < GAP
+
+
+def test_full_model_vs_stock_libm_reference(qh, cuda, ref, full):
+    """Same run against the stock build: report where the streams part."""
+    from oracle.oracle import RefModel
+    cfg, blob, tensors, prompt, gp, gl = full
+    rp, rg, rl = ref_run(ref, RefModel, cfg, tensors, prompt, 256)
+    mism = np.flatnonzero(rp != gp)
+    first = int(mism[0]) if mism.size else len(rp)
+    print(f"config 4 vs stock glibc reference: first differing prediction at step {first} of {len(rp)}"
+          + (f" (top-2 gap there {rg[first]:.3g})" if mism.size else ""))
+    assert first >= 8, "the streams part before the libm can account for it"
