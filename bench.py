@@ -199,6 +199,134 @@ def run_reference_arm(args):
 
 
 # ---------------------------------------------------------------------------
+# decode of the synthetic Qwen3.5-0.8B-shaped model (configs 4 and 5)
+# ---------------------------------------------------------------------------
+MODEL_SEED = 0xC0F16
+
+
+class _DevInts:
+    """A device int32 vector seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+def decode_step_bytes(cfg, B: int, weight_bytes: int, n_prompt: int, n_new: int) -> float:
+    """Algorithmic HBM bytes of one decode step, averaged over the decode
+    positions: every weight once (the tied Q6_K LM head included; the
+    embedding row gather is negligible), the Gated DeltaNet state read and
+    written, the conv ring read and written, the fp16 KV cache rows read up
+    to the position plus the new row written."""
+    n_attn = sum(1 for l in range(cfg.n_layers) if (l + 1) % cfg.full_attn_interval == 0)
+    n_gdn = cfg.n_layers - n_attn
+    kdim = cfg.gdn_heads * cfg.gdn_head_dim
+    state = n_gdn * cfg.gdn_heads * cfg.gdn_head_dim * cfg.gdn_head_dim * 4
+    ring = n_gdn * cfg.conv_kernel * 3 * kdim * 4
+    avg_rows = n_prompt + (n_new - 1) / 2.0 + 1
+    kv = n_attn * avg_rows * 2 * cfg.n_kv_heads * cfg.head_dim * 2
+    return weight_bytes + B * (2 * state + 2 * ring + kv)
+
+
+def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_new: int):
+    """Greedy decode of B sequences per GPU: n_prompt teacher-forced steps,
+    then n_new steps timed with CUDA events on the model's stream; the
+    sampled tokens are gathered over NCCL after every step when world > 1.
+    Returns a dict for the JSON line (rank 0 fills it)."""
+    import numpy as np
+    h = qh.host
+    cfg = h.slm_config(n_prompt + n_new)
+    blob = h.Blob(cfg, MODEL_SEED)  # identical weights on every rank (replicated)
+    slm = h.Slm(cfg, blob, B)
+    import ctypes as C
+    wb, sb = C.c_int64(), C.c_int64()
+    qh.check(qh.lib().qh_slm_memory(slm.handle, C.byref(wb), C.byref(sb)), "qh_slm_memory")
+    rng = np.random.default_rng(0xD3C0 + 7919 * rank + B)
+    prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
+    stream = torch.cuda.ExternalStream(slm.stream)
+    nxt = torch.as_tensor(_DevInts(slm.device_next, B), device="cuda")
+    gathered = torch.empty(world * B, dtype=torch.int32, device="cuda")
+
+    def gather():
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gathered, nxt)
+
+    # warm-up: the first steps run directly, then the step is captured
+    slm.begin(prompts)
+    for _ in range(3):
+        slm.advance(1)
+        gather()
+    slm.picks(0, 3)
+    slm.reset()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    t0 = time.perf_counter()
+    slm.begin(prompts)
+    ev[0].record(stream)
+    slm.advance(n_prompt - 1)
+    ev[1].record(stream)
+    for _ in range(n_new):
+        slm.advance(1)
+        gather()
+    ev[2].record(stream)
+    picks = slm.picks(n_prompt - 1, n_new)  # synchronizes
+    wall = time.perf_counter() - t0
+    torch.cuda.synchronize()
+    prefill_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    if world > 1:
+        t = torch.tensor([prefill_ms, decode_ms, wall], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms, decode_ms, wall = (float(v) for v in t.tolist())
+    # consistency: the gathered picks of the last step are this rank's picks
+    if world > 1:
+        mine = gathered.view(world, B)[rank].cpu().numpy()
+        if not np.array_equal(mine, picks[:, -1]):
+            raise SystemExit("token gather disagrees with the rank's own picks")
+    step_bytes = decode_step_bytes(cfg, B, wb.value, n_prompt, n_new)
+    step_ms = decode_ms / n_new
+    out = {
+        "workload": f"{B} sequence(s)/GPU, {n_prompt}-token prompt, {n_new} greedy tokens",
+        "tok_s": round(world * B * n_new / (decode_ms / 1e3), 1),
+        "ms_per_step": round(step_ms, 4),
+        "prefill_tok_s": round(world * B * (n_prompt - 1) / (prefill_ms / 1e3), 1),
+        "e2e_tok_s": round(world * B * (n_prompt - 1 + n_new) / wall, 1),
+        "hbm_bytes_per_step": int(step_bytes), "weight_bytes": wb.value,
+        "hbm_gbs": round(step_bytes / (step_ms / 1e3) / 1e9, 1),
+        "picks_checksum": int(np.bitwise_xor.reduce(picks.ravel() * np.int64(2654435761) % (1 << 31))),
+    }
+    slm.close()
+    del blob
+    return out, cfg, prompts, picks
+
+
+def cpu_decode_baseline(qh, n_steps: int = 4):
+    """The reference's own slm_forward_step + sample_argmax (oracle/_ref,
+    single-threaded on Linux) on the full-size model: a bounded sample of
+    n_steps steps from position 0, tok/s."""
+    from oracle.oracle import Ref, RefModel
+    if not Ref.available():
+        return None
+    h = qh.host
+    cfg = h.slm_config(64)
+    blob = h.Blob(cfg, MODEL_SEED)
+    rm = RefModel(Ref(), cfg, blob.tensors())
+    rm.step(1, 0)
+    t0 = time.perf_counter()
+    tok = 2
+    for pos in range(1, n_steps + 1):
+        tok = rm.step(tok, pos)
+    dt = time.perf_counter() - t0
+    rm.close()
+    return {"value": round(n_steps / dt, 3), "unit": "tok/s", "cores": 1, "kind": "reference",
+            "sample": f"{n_steps} decode steps of the full-size model at batch 1 (slm_forward_step, "
+                      f"single-threaded on Linux)"}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def run_ours(args):
@@ -321,10 +449,31 @@ def run_ours(args):
     achieved = G * ALGO_BYTES / (kern_mean_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
 
+    plan.close()
+    del wdev
+    torch.cuda.empty_cache()
+
+    # ---- decode of the synthetic model (configs 4 and 5) ----
+    decode = None
+    if not args.no_decode:
+        dclk = ClockSampler(uuid)
+        dclk.start()
+        decode = {}
+        for B, n_prompt in ((1, 64), (args.decode_batch, args.decode_prompt)):
+            if args.decode_only_batch and B != args.decode_only_batch:
+                continue
+            decode[f"batch{B}"], _, _, _ = run_decode(qh, torch, dist, world, rank, B, n_prompt, args.decode_new)
+        runs = list(decode.values())
+        decode.update({"clocks": dclk.stop(),
+                  "data": "synthetic Qwen3.5-0.8B-shaped weights (Q4_K mix), seeded random prompts",
+                  "roofline_peak_gbs": peak, "parallelism": f"dp{world}, replicated weights, "
+                  "sampled tokens all-gathered over NCCL each step"})
+        for d in runs:
+            d["hbm_frac"] = round(d["hbm_gbs"] / peak, 4)
+
     if world > 1:
         dist.barrier()
     if rank != 0:
-        plan.close()
         if world > 1:
             dist.destroy_process_group()
         return 0
@@ -368,8 +517,11 @@ def run_ours(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if decode is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            decode["cpu_baseline"] = cpu_decode_baseline(qh)
+        line["decode"] = decode
     print(json.dumps(line), flush=True)
-    plan.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -384,6 +536,11 @@ def main():
     ap.add_argument("--pool", type=int, default=320)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the model decode measurement")
+    ap.add_argument("--decode-batch", type=int, default=64, help="sequences per GPU of the batched decode")
+    ap.add_argument("--decode-new", type=int, default=256, help="greedy tokens per decode run")
+    ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens of the batched decode")
+    ap.add_argument("--decode-only-batch", type=int, default=0, help="run only the decode of this batch size")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

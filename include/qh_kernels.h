@@ -42,13 +42,15 @@ int qh_swiglu(const float *d_gate, const float *d_up, float *d_out, int64_t n, v
  * (slm/qwen.c:357-475): push qkv into the conv ring slot pos % kk,
  * causal conv + SiLU, split into Q/K/V, per-head L2 norm of Q (scaled by
  * 1/sqrt(head_dim)) and K, beta = sigmoid(b), g = exp(ssm_a *
- * softplus(a + dt_bias)).
+ * softplus(a + dt_bias)). The position is read from device memory (*d_pos)
+ * here and in the attention kernels, so a whole step can be captured once
+ * in a CUDA graph and replayed for every position.
  *   qkv [B][conv_dim], ring [B][kk][conv_dim], conv_w [conv_dim][kk],
  *   b, a [B][heads]; out q, k, v [B][heads*hd], beta, g [B][heads]. */
 int qh_gdn_pre(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b,
                const float *d_a, const float *d_dt_bias, const float *d_ssm_a, int32_t B,
-               int32_t heads, int32_t hd, int32_t kk, int32_t pos, float *d_q, float *d_k, float *d_v,
-               float *d_beta, float *d_g, void *stream);
+               int32_t heads, int32_t hd, int32_t kk, const int32_t *d_pos, float *d_q, float *d_k,
+               float *d_v, float *d_beta, float *d_g, void *stream);
 
 /* Gated DeltaNet recurrence (slm/qwen.c:499-557) over state [B][heads][hd
  * k][hd v]: state *= g; kv = state^T K; delta = (V - kv) * beta;
@@ -65,24 +67,32 @@ int qh_gdn_gated_norm(const float *d_x, const float *d_z, const float *d_w, int3
 /* Attention pre-processing for one layer (slm/model.c:831-913): split the
  * head-interleaved Q/gate projection, per-head RMSNorm of Q and K, partial
  * interleaved-MRoPE with the host-built cos/sin table rope[pos][rope_dim/2][2],
- * append K (roped) and V as fp16 at row pos of the layer's caches
+ * append K (roped) and V as fp16 at row *d_pos (< max_pos) of the layer's caches
  * [B][max_pos][kvh][hd]. qraw [B][2*nh*hd], k, v [B][kvh*hd] in; q [B][nh][hd],
  * gate [B][nh*hd] out. */
 int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
                 const float *d_knorm_w, const float *d_rope, int32_t B, int32_t nh, int32_t kvh,
-                int32_t hd, int32_t rope_dim, float eps, int32_t pos, int32_t max_pos, float *d_q,
-                float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream);
+                int32_t hd, int32_t rope_dim, float eps, const int32_t *d_pos, int32_t max_pos,
+                float *d_q, float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream);
 
-/* Causal GQA attention of the new query over cache rows 0..pos, then the
+/* Causal GQA attention of the new query over cache rows 0..*d_pos, then the
  * sigmoid output gate (tensor_attention, slm/tensor.c:1049-1102;
  * slm/model.c:940-947). ctx [B][nh*hd]. */
 int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache,
-                   const float *d_gate, int32_t B, int32_t nh, int32_t kvh, int32_t hd, int32_t pos,
-                   int32_t max_pos, float *d_ctx, void *stream);
+                   const float *d_gate, int32_t B, int32_t nh, int32_t kvh, int32_t hd,
+                   const int32_t *d_pos, int32_t max_pos, float *d_ctx, void *stream);
 
 /* Greedy pick per row (sample_argmax, slm/model.c:401-412): index of the
  * first maximum of logits [B][vocab]. */
 int qh_argmax(const float *d_logits, int32_t B, int64_t vocab, int32_t *d_out, void *stream);
+
+/* End of a device-driven decode step (the loop of slm_generate,
+ * slm/model.c, kept on the device): with pos = ctl[0] and n_prompt = ctl[1],
+ * picks[b][pos] = next[b]; tokens[b] = prompt[b][pos + 1] while pos + 1 <
+ * n_prompt (teacher forcing through the prompt), else next[b]; then
+ * ctl[0] = pos + 1. prompt and picks are [B][stride]. */
+int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int32_t stride, int32_t *d_ctl,
+                 int32_t *d_tokens, int32_t *d_picks, void *stream);
 
 #ifdef __cplusplus
 }

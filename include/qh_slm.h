@@ -84,15 +84,38 @@ void qh_slm_destroy(qh_slm *m);
 /* Clears every sequence's KV cache, conv ring and recurrent state. */
 int qh_slm_reset(qh_slm *m);
 
-/* slm_forward_step + sample_argmax for all n_seq sequences at position pos:
- * h_tokens[n_seq] in, h_next[n_seq] (greedy argmax) out, optionally the
- * logits h_logits[n_seq][vocab]. Synchronous. */
+/* slm_forward_step + sample_argmax for all n_seq sequences at position pos
+ * (slm/qwen.c:874-981, slm/model.c:401-412): h_tokens[n_seq] in,
+ * h_next[n_seq] (greedy argmax) out, optionally the logits
+ * h_logits[n_seq][vocab]. Synchronous. The step is one CUDA graph launch
+ * (captured on the second call; the first runs the kernels directly). */
 int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next, float *h_logits);
 
-/* Greedy generation: feeds the n_prompt tokens of every sequence one step
- * at a time (as the reference's default prefill does), then n_new greedy
- * steps; out[s][i] is the i-th generated token of sequence s. */
+/* Device-driven decoding, no host round trip per token:
+ *   qh_slm_begin   uploads prompt[n_seq][n_prompt] and sets position 0;
+ *   qh_slm_advance launches n_steps steps (asynchronous on qh_slm_stream):
+ *                  step p feeds prompt[s][p] while p < n_prompt, else the
+ *                  greedy pick of step p - 1, and records its own pick;
+ *   qh_slm_picks   waits, then out[s][i] = pick of step from_pos + i.
+ * Positions stay below max_pos. */
+int qh_slm_begin(qh_slm *m, const int32_t *prompt, int32_t n_prompt);
+int qh_slm_advance(qh_slm *m, int32_t n_steps);
+int qh_slm_picks(qh_slm *m, int32_t from_pos, int32_t n, int32_t *out);
+
+/* Greedy generation, the per-step prefill path of slm_generate_raw
+ * (slm/slm.c:237-357) for every sequence: the n_prompt tokens are fed one
+ * step each and the pick of the last prompt step is the first of the n_new
+ * generated tokens; out[s][i] is the i-th generated token of sequence s.
+ * slm_generate_raw re-feeds the last prompt token once more at position
+ * n_prompt before its first sample; callers wanting that schedule pass the
+ * prompt with its last token repeated. */
 int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out);
+
+/* The model's CUDA stream (cudaStream_t) and the device buffer of the last
+ * greedy picks [n_seq], for callers that order their own work (events, a
+ * token gather over NCCL) after qh_slm_advance. */
+void *qh_slm_stream(const qh_slm *m);
+const int32_t *qh_slm_device_next(const qh_slm *m);
 
 /* Device memory held by the model (weights) and by the per-sequence state. */
 int qh_slm_memory(const qh_slm *m, int64_t *weight_bytes, int64_t *state_bytes);

@@ -112,6 +112,11 @@ SIGNATURES.update({
     "qh_slm_step": (_I, [_P, _P, C.c_int32, _P, _P]),
     "qh_slm_generate": (_I, [_P, _P, C.c_int32, C.c_int32, _P]),
     "qh_slm_memory": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64)]),
+    "qh_slm_begin": (_I, [_P, _P, C.c_int32]),
+    "qh_slm_advance": (_I, [_P, C.c_int32]),
+    "qh_slm_picks": (_I, [_P, C.c_int32, C.c_int32, _P]),
+    "qh_slm_stream": (_P, [_P]),
+    "qh_slm_device_next": (_P, [_P]),
 })
 
 _F32P = C.c_void_p
@@ -120,15 +125,16 @@ SIGNATURES.update({  # include/qh_kernels.h
     "qh_rmsnorm": (_I, [_P, _P, _I64, _I64, C.c_float, _P, _P]),
     "qh_add": (_I, [_P, _P, _I64, _P]),
     "qh_swiglu": (_I, [_P, _P, _P, _I64, _P]),
-    "qh_gdn_pre": (_I, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+    "qh_gdn_pre": (_I, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P,
                         _P, _P, _P, _P, _P, _P]),
     "qh_gdn_recurrence": (_I, [_P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, _P, _P]),
     "qh_gdn_gated_norm": (_I, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_float, _P, _P]),
     "qh_attn_pre": (_I, [_P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
-                         C.c_float, C.c_int32, C.c_int32, _P, _P, _P, _P, _P]),
-    "qh_attn_decode": (_I, [_P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                         C.c_float, _P, C.c_int32, _P, _P, _P, _P, _P]),
+    "qh_attn_decode": (_I, [_P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32,
                             _P, _P]),
     "qh_argmax": (_I, [_P, C.c_int32, _I64, _P, _P]),
+    "qh_feed_next": (_I, [_P, _P, C.c_int32, C.c_int32, _P, _P, _P, _P]),
 })
 
 _lib = None

@@ -119,12 +119,13 @@ __global__ void swiglu_kernel(const float *__restrict__ g, const float *__restri
 __global__ void gdn_pre_kernel(const float *__restrict__ qkv, float *__restrict__ ring,
                                const float *__restrict__ conv_w, const float *__restrict__ bb,
                                const float *__restrict__ aa, const float *__restrict__ dt_bias,
-                               const float *__restrict__ ssm_a, int heads, int hd, int kk, int pos,
-                               float *__restrict__ qo, float *__restrict__ ko, float *__restrict__ vo,
+                               const float *__restrict__ ssm_a, int heads, int hd, int kk,
+                               const int32_t *__restrict__ pos_ptr, float *__restrict__ qo, float *__restrict__ ko, float *__restrict__ vo,
                                float *__restrict__ beta, float *__restrict__ gout) {
     __shared__ double scratch[32];
     const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
     const int kdim = heads * hd, conv_dim = 3 * kdim;
+    const int pos = max(*pos_ptr, 0);
     const int slot = pos % kk, head_after = (pos + 1) % kk;
     const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
     float *rg = ring + static_cast<int64_t>(b) * kk * conv_dim;
@@ -218,12 +219,14 @@ __global__ void gdn_gated_norm_kernel(const float *__restrict__ x, const float *
 __global__ void attn_pre_kernel(const float *__restrict__ qraw, const float *__restrict__ kin,
                                 const float *__restrict__ vin, const float *__restrict__ qn_w,
                                 const float *__restrict__ kn_w, const float *__restrict__ rope, int nh,
-                                int kvh, int hd, int rope_dim, float eps, int pos, int max_pos,
+                                int kvh, int hd, int rope_dim, float eps,
+                                const int32_t *__restrict__ pos_ptr, int max_pos,
                                 float *__restrict__ qout, float *__restrict__ gate,
                                 __half *__restrict__ kcache, __half *__restrict__ vcache) {
     __shared__ double scratch[32];
     __shared__ float xs[512];
     const int b = blockIdx.x, j = blockIdx.y, t = threadIdx.x;
+    const int pos = min(max(*pos_ptr, 0), max_pos - 1);
     const bool is_q = j < nh;
     float x;
     if (is_q) {
@@ -263,11 +266,13 @@ __global__ void attn_pre_kernel(const float *__restrict__ qraw, const float *__r
 // ---------------------------------------------------------------------------
 __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__restrict__ kcache,
                                    const __half *__restrict__ vcache, const float *__restrict__ gate,
-                                   int nh, int kvh, int hd, int pos, int max_pos, float *__restrict__ ctx) {
-    extern __shared__ float sh[];  // [hd] query, [pos+1] scores, [32] scratch
+                                   int nh, int kvh, int hd, const int32_t *__restrict__ pos_ptr,
+                                   int max_pos, float *__restrict__ ctx) {
+    extern __shared__ float sh[];  // [hd] query, [max_pos] scores, [32] scratch
     float *qs = sh;
     float *sc = sh + hd;
-    float *scratch = sc + (pos + 1);
+    float *scratch = sc + max_pos;
+    const int pos = min(max(*pos_ptr, 0), max_pos - 1);
     __shared__ float total;
     const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
     const int kh = h / (nh / kvh);
@@ -333,6 +338,21 @@ __global__ void argmax_kernel(const float *__restrict__ logits, int64_t vocab, i
     }
 }
 
+// End of a decode step on the device: record the picks, choose the next
+// input (the prompt while inside it, else the pick) and advance the position.
+__global__ void feed_next_kernel(const int32_t *__restrict__ next, const int32_t *__restrict__ prompt, int32_t B,
+                                 int32_t stride, int32_t *__restrict__ ctl, int32_t *__restrict__ tokens,
+                                 int32_t *__restrict__ picks) {
+    const int pos = ctl[0], n_prompt = ctl[1];
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        const int32_t nx = next[b];
+        if (pos >= 0 && pos < stride) picks[static_cast<int64_t>(b) * stride + pos] = nx;
+        tokens[b] = (pos + 1 < n_prompt && pos + 1 < stride) ? prompt[static_cast<int64_t>(b) * stride + pos + 1] : nx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ctl[0] = pos + 1;
+}
+
 }  // namespace qh
 
 // ---------------------------------------------------------------------------
@@ -388,13 +408,13 @@ int qh_swiglu(const float *d_gate, const float *d_up, float *d_out, int64_t n, v
 
 int qh_gdn_pre(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b,
                const float *d_a, const float *d_dt_bias, const float *d_ssm_a, int32_t B,
-               int32_t heads, int32_t hd, int32_t kk, int32_t pos, float *d_q, float *d_k, float *d_v,
-               float *d_beta, float *d_g, void *stream) {
-    if (B <= 0 || heads <= 0 || hd <= 0 || hd % 32 || hd > 1024 || kk <= 0 || pos < 0)
+               int32_t heads, int32_t hd, int32_t kk, const int32_t *d_pos, float *d_q, float *d_k,
+               float *d_v, float *d_beta, float *d_g, void *stream) {
+    if (B <= 0 || heads <= 0 || hd <= 0 || hd % 32 || hd > 1024 || kk <= 0 || !d_pos)
         return bad("qh_gdn_pre: bad arguments");
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
     qh::gdn_pre_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(
-        d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, heads, hd, kk, pos, d_q, d_k, d_v, d_beta, d_g);
+        d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, heads, hd, kk, d_pos, d_q, d_k, d_v, d_beta, d_g);
     return launch_status("qh_gdn_pre");
 }
 
@@ -422,24 +442,24 @@ int qh_gdn_gated_norm(const float *d_x, const float *d_z, const float *d_w, int3
 
 int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
                 const float *d_knorm_w, const float *d_rope, int32_t B, int32_t nh, int32_t kvh,
-                int32_t hd, int32_t rope_dim, float eps, int32_t pos, int32_t max_pos, float *d_q,
-                float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream) {
+                int32_t hd, int32_t rope_dim, float eps, const int32_t *d_pos, int32_t max_pos,
+                float *d_q, float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream) {
     if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 512 || rope_dim > hd || rope_dim % 2 ||
-        pos < 0 || pos >= max_pos)
+        !d_pos || max_pos <= 0)
         return bad("qh_attn_pre: bad arguments");
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh + kvh));
     qh::attn_pre_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(
-        d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, nh, kvh, hd, rope_dim, eps, pos, max_pos, d_q, d_gate,
+        d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, nh, kvh, hd, rope_dim, eps, d_pos, max_pos, d_q, d_gate,
         reinterpret_cast<__half *>(d_kcache), reinterpret_cast<__half *>(d_vcache));
     return launch_status("qh_attn_pre");
 }
 
 int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache,
-                   const float *d_gate, int32_t B, int32_t nh, int32_t kvh, int32_t hd, int32_t pos,
-                   int32_t max_pos, float *d_ctx, void *stream) {
-    if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 1024 || pos < 0 || pos >= max_pos)
+                   const float *d_gate, int32_t B, int32_t nh, int32_t kvh, int32_t hd,
+                   const int32_t *d_pos, int32_t max_pos, float *d_ctx, void *stream) {
+    if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 1024 || !d_pos || max_pos <= 0)
         return bad("qh_attn_decode: bad arguments");
-    const size_t smem = sizeof(float) * (static_cast<size_t>(hd) + pos + 1 + 32);
+    const size_t smem = sizeof(float) * (static_cast<size_t>(hd) + max_pos + 32);
     if (smem > 200 * 1024) return bad("qh_attn_decode: context too long");
     static bool attr_done[64] = {false};
     int dev = 0;
@@ -451,7 +471,7 @@ int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh));
     qh::attn_decode_kernel<<<grid, hd, smem, static_cast<cudaStream_t>(stream)>>>(
         d_q, reinterpret_cast<const __half *>(d_kcache), reinterpret_cast<const __half *>(d_vcache), d_gate, nh,
-        kvh, hd, pos, max_pos, d_ctx);
+        kvh, hd, d_pos, max_pos, d_ctx);
     return launch_status("qh_attn_decode");
 }
 
@@ -459,6 +479,15 @@ int qh_argmax(const float *d_logits, int32_t B, int64_t vocab, int32_t *d_out, v
     if (!d_logits || !d_out || B <= 0 || vocab <= 0) return bad("qh_argmax: bad arguments");
     qh::argmax_kernel<<<static_cast<unsigned>(B), 1024, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, vocab, d_out);
     return launch_status("qh_argmax");
+}
+
+int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int32_t stride, int32_t *d_ctl,
+                 int32_t *d_tokens, int32_t *d_picks, void *stream) {
+    if (!d_next || !d_prompt || !d_ctl || !d_tokens || !d_picks || B <= 0 || stride <= 0)
+        return bad("qh_feed_next: bad arguments");
+    qh::feed_next_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_next, d_prompt, B, stride, d_ctl,
+                                                                          d_tokens, d_picks);
+    return launch_status("qh_feed_next");
 }
 
 }  // extern "C"

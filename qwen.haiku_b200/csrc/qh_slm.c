@@ -68,7 +68,17 @@ struct qh_slm {
     float *qraw, *kb, *vb, *aq, *agate, *actx, *fgate, *fup, *fact, *logits, *rope;
     void *xq_h, *xq_gdn, *xq_ffn;  // split Q8_K activations for K = hidden, gdn width, ffn
     int32_t *d_tok, *d_next;
-    int32_t *h_tok, *h_next;  // pinned
+    int32_t *d_ctl;                // [0] = position, [1] = prompt length
+    int32_t *d_prompt, *d_picks;   // [B][max_pos]: prompt tokens, greedy picks by position
+    int32_t *h_tok, *h_next, *h_ctl;  // pinned
+    int32_t host_pos;              // position of the next step
+    int32_t n_prompt;
+    // The whole step is captured once in a CUDA graph (after one direct run
+    // has set every kernel attribute) and replayed; position and tokens are
+    // read from device memory, so one graph serves every position.
+    cudaGraph_t graph;
+    cudaGraphExec_t graph_exec;
+    int steps_run;
     // caches
     float *ring, *state;
     uint16_t *kcache, *vcache;
@@ -251,8 +261,12 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         TRY(dev_alloc(m, &m->xq_ffn, (size_t)qh_q8k_bytes(F, B), NULL));
         TRY(dev_alloc(m, (void **)&m->d_tok, (size_t)B * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_next, (size_t)B * 4, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_ctl, 16, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_prompt, (size_t)B * cfg->max_pos * 4, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_picks, (size_t)B * cfg->max_pos * 4, NULL));
         if (cudaMallocHost((void **)&m->h_tok, (size_t)B * 4) != cudaSuccess ||
-            cudaMallocHost((void **)&m->h_next, (size_t)B * 4) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
+            cudaMallocHost((void **)&m->h_next, (size_t)B * 4) != cudaSuccess ||
+            cudaMallocHost((void **)&m->h_ctl, 16) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
         // caches
         const int64_t ng = m->n_gdn > 0 ? m->n_gdn : 1, na = m->n_attn > 0 ? m->n_attn : 1;
         TRY(dev_alloc(m, (void **)&m->ring, (size_t)(ng * B * cfg->conv_kernel * conv_dim * 4), &m->state_bytes));
@@ -328,10 +342,13 @@ void qh_slm_destroy(qh_slm *m) {
         free_plans(&m->L[l].p_down);
     }
     free_plans(&m->p_head);
+    if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
     for (int i = 0; i < m->nallocs; ++i) qh_free(m->allocs[i]);
     free(m->allocs);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->h_next) cudaFreeHost(m->h_next);
+    if (m->h_ctl) cudaFreeHost(m->h_ctl);
     if (m->stream) cudaStreamDestroy(m->stream);
     free(m);
 }
@@ -346,11 +363,17 @@ int qh_slm_reset(qh_slm *m) {
     CK(qh_memset(m->state, 0, (size_t)(ng * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim * 4), m->stream));
     CK(qh_memset(m->kcache, 0, (size_t)(na * B * c->max_pos * kvd * 2), m->stream));
     CK(qh_memset(m->vcache, 0, (size_t)(na * B * c->max_pos * kvd * 2), m->stream));
+    CK(qh_memset(m->d_picks, 0, (size_t)B * c->max_pos * 4, m->stream));
+    m->host_pos = 0;
+    m->n_prompt = 0;
     return qh_stream_sync(m->stream);
 }
 
-// One forward step for all sequences; tokens already in m->d_tok.
-static int forward(qh_slm *m, int32_t pos) {
+// One step for all sequences: the forward pass of tokens m->d_tok at
+// position d_ctl[0], the greedy picks, then the device-side feed of the next
+// inputs. Launches only (no allocation, no synchronization), so it is
+// captured in a CUDA graph.
+static int forward(qh_slm *m) {
     const qh_slm_config *c = &m->cfg;
     const int32_t B = m->B;
     const int64_t H = c->hidden, F = c->ffn, hd = c->head_dim;
@@ -368,8 +391,9 @@ static int forward(qh_slm *m, int32_t pos) {
             uint16_t *kc = m->kcache + ai * B * c->max_pos * kvd;
             uint16_t *vc = m->vcache + ai * B * c->max_pos * kvd;
             CK(qh_attn_pre(m->qraw, m->kb, m->vb, Ly->q_norm, Ly->k_norm, m->rope, B, c->n_heads, c->n_kv_heads,
-                           (int32_t)hd, c->rope_dim, c->norm_eps, pos, c->max_pos, m->aq, m->agate, kc, vc, s));
-            CK(qh_attn_decode(m->aq, kc, vc, m->agate, B, c->n_heads, c->n_kv_heads, (int32_t)hd, pos,
+                           (int32_t)hd, c->rope_dim, c->norm_eps, m->d_ctl, c->max_pos, m->aq, m->agate, kc, vc,
+                           s));
+            CK(qh_attn_decode(m->aq, kc, vc, m->agate, B, c->n_heads, c->n_kv_heads, (int32_t)hd, m->d_ctl,
                               c->max_pos, m->actx, s));
             CK(qh_quantize_q8k(m->actx, qdim, B, m->xq_h, s));
         } else {
@@ -377,7 +401,7 @@ static int forward(qh_slm *m, int32_t pos) {
             float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
             CK(qh_gdn_pre(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, B, c->gdn_heads,
-                          c->gdn_head_dim, c->conv_kernel, pos, m->gq, m->gk, m->gv, m->gbeta, m->gg, s));
+                          c->gdn_head_dim, c->conv_kernel, m->d_ctl, m->gq, m->gk, m->gv, m->gbeta, m->gg, s));
             CK(qh_gdn_recurrence(state, m->gq, m->gk, m->gv, m->gbeta, m->gg, B, c->gdn_heads, c->gdn_head_dim,
                                  m->gout, s));
             CK(qh_gdn_gated_norm(m->gout, m->z, Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->norm_eps,
@@ -398,7 +422,34 @@ static int forward(qh_slm *m, int32_t pos) {
     CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
     CK(run_plans(m, &m->p_head));
     CK(qh_argmax(m->logits, B, c->vocab, m->d_next, s));
+    CK(qh_feed_next(m->d_next, m->d_prompt, B, c->max_pos, m->d_ctl, m->d_tok, m->d_picks, s));
     return QH_OK;
+}
+
+static int launch_step(qh_slm *m) {
+    if (m->graph_exec) {
+        if (cudaGraphLaunch(m->graph_exec, m->stream) != cudaSuccess) return QH_ERR_CUDA;
+        return QH_OK;
+    }
+    if (m->steps_run++ == 0) return forward(m);  // first run sets kernel attributes
+    // capture the step once, then replay it
+    if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return forward(m);
+    int rc = forward(m);
+    cudaGraph_t g = NULL;
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc || e != cudaSuccess || g == NULL) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return rc ? rc : forward(m);
+    }
+    if (cudaGraphInstantiate(&m->graph_exec, g, 0) != cudaSuccess) {
+        cudaGraphDestroy(g);
+        m->graph_exec = NULL;
+        cudaGetLastError();
+        return forward(m);
+    }
+    m->graph = g;
+    return cudaGraphLaunch(m->graph_exec, m->stream) == cudaSuccess ? QH_OK : QH_ERR_CUDA;
 }
 
 int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next, float *h_logits) {
@@ -406,8 +457,13 @@ int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next
     memcpy(m->h_tok, h_tokens, sizeof(int32_t) * m->B);
     for (int32_t b = 0; b < m->B; ++b)
         if (m->h_tok[b] < 0 || m->h_tok[b] >= m->cfg.vocab) return QH_ERR_INVALID;
+    m->h_ctl[0] = pos;
+    m->h_ctl[1] = 0;
+    CK(qh_memcpy_h2d(m->d_ctl, m->h_ctl, 2 * sizeof(int32_t), m->stream));
     CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * m->B, m->stream));
-    CK(forward(m, pos));
+    CK(launch_step(m));
+    m->host_pos = pos + 1;
+    m->n_prompt = 0;
     CK(qh_memcpy_d2h(m->h_next, m->d_next, sizeof(int32_t) * m->B, m->stream));
     if (h_logits)
         CK(qh_memcpy_d2h(h_logits, m->logits, sizeof(float) * (size_t)m->B * m->cfg.vocab, m->stream));
@@ -417,28 +473,59 @@ int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next
     return QH_OK;
 }
 
-int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out) {
-    if (!m || !prompt || !out || n_prompt <= 0 || n_new < 0 || n_prompt + n_new > m->cfg.max_pos + 1)
-        return QH_ERR_INVALID;
-    const int32_t B = m->B;
-    int32_t *tok = (int32_t *)malloc(sizeof(int32_t) * B), *nxt = (int32_t *)malloc(sizeof(int32_t) * B);
-    if (!tok || !nxt) { free(tok); free(nxt); return QH_ERR_INVALID; }
-    int rc = QH_OK;
-    int32_t pos = 0;
-    for (int32_t i = 0; i < n_prompt && !rc; ++i, ++pos) {
-        for (int32_t b = 0; b < B; ++b) tok[b] = prompt[(int64_t)b * n_prompt + i];
-        rc = qh_slm_step(m, tok, pos, nxt, NULL);
-    }
-    for (int32_t j = 0; j < n_new && !rc; ++j) {
-        for (int32_t b = 0; b < B; ++b) out[(int64_t)b * n_new + j] = nxt[b];
-        if (j + 1 == n_new) break;
-        memcpy(tok, nxt, sizeof(int32_t) * B);
-        rc = qh_slm_step(m, tok, pos++, nxt, NULL);
-    }
-    free(tok);
-    free(nxt);
-    return rc;
+int qh_slm_begin(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
+    if (!m || !prompt || n_prompt <= 0 || n_prompt > m->cfg.max_pos) return QH_ERR_INVALID;
+    const int32_t B = m->B, P = m->cfg.max_pos;
+    for (int64_t i = 0; i < (int64_t)B * n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab) return QH_ERR_INVALID;
+    // prompt[s][i] -> d_prompt[s][i] (row pitch max_pos)
+    if (cudaMemcpy2DAsync(m->d_prompt, (size_t)P * 4, prompt, (size_t)n_prompt * 4, (size_t)n_prompt * 4,
+                          (size_t)B, cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
+        return QH_ERR_CUDA;
+    CK(qh_stream_sync(m->stream));  // the pinned staging buffers below are reused
+    for (int32_t b = 0; b < B; ++b) m->h_tok[b] = prompt[(int64_t)b * n_prompt];
+    m->h_ctl[0] = 0;
+    m->h_ctl[1] = n_prompt;
+    CK(qh_memcpy_h2d(m->d_ctl, m->h_ctl, 2 * sizeof(int32_t), m->stream));
+    CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * B, m->stream));
+    CK(qh_stream_sync(m->stream));
+    m->host_pos = 0;
+    m->n_prompt = n_prompt;
+    return QH_OK;
 }
+
+int qh_slm_advance(qh_slm *m, int32_t n_steps) {
+    if (!m || n_steps < 0 || m->host_pos + n_steps > m->cfg.max_pos) return QH_ERR_INVALID;
+    for (int32_t i = 0; i < n_steps; ++i) CK(launch_step(m));
+    m->host_pos += n_steps;
+    return QH_OK;
+}
+
+int qh_slm_picks(qh_slm *m, int32_t from_pos, int32_t n, int32_t *out) {
+    if (!m || !out || from_pos < 0 || n < 0 || from_pos + n > m->host_pos) return QH_ERR_INVALID;
+    if (n == 0) return QH_OK;
+    const size_t P = (size_t)m->cfg.max_pos;
+    if (cudaMemcpy2DAsync(out, (size_t)n * 4, m->d_picks + from_pos, P * 4, (size_t)n * 4, (size_t)m->B,
+                          cudaMemcpyDeviceToHost, m->stream) != cudaSuccess)
+        return QH_ERR_CUDA;
+    CK(qh_stream_sync(m->stream));
+    return qh_check_device_error(NULL);
+}
+
+int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out) {
+    if (!m || !prompt || !out || n_prompt <= 0 || n_new < 0 || n_prompt + n_new - 1 > m->cfg.max_pos)
+        return QH_ERR_INVALID;
+    CK(qh_slm_begin(m, prompt, n_prompt));
+    if (n_new == 0) return QH_OK;
+    // step p consumes the input at p and picks the token for p + 1: the
+    // pick of step n_prompt - 1 is the first generated token
+    CK(qh_slm_advance(m, n_prompt - 1 + n_new));
+    return qh_slm_picks(m, n_prompt - 1, n_new, out);
+}
+
+void *qh_slm_stream(const qh_slm *m) { return m ? (void *)m->stream : NULL; }
+
+const int32_t *qh_slm_device_next(const qh_slm *m) { return m ? m->d_next : NULL; }
 
 int qh_slm_memory(const qh_slm *m, int64_t *weight_bytes, int64_t *state_bytes) {
     if (!m) return QH_ERR_INVALID;

@@ -256,6 +256,26 @@ class Slm:
               "qh_slm_generate")
         return out
 
+    def begin(self, prompt):
+        p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
+        check(lib().qh_slm_begin(self.handle, p.ctypes.data, p.shape[1]), "qh_slm_begin")
+
+    def advance(self, n_steps: int):
+        check(lib().qh_slm_advance(self.handle, n_steps), "qh_slm_advance")
+
+    def picks(self, from_pos: int, n: int):
+        out = np.empty((self.n_seq, n), np.int32)
+        check(lib().qh_slm_picks(self.handle, from_pos, n, out.ctypes.data), "qh_slm_picks")
+        return out
+
+    @property
+    def stream(self) -> int:
+        return lib().qh_slm_stream(self.handle) or 0
+
+    @property
+    def device_next(self) -> int:
+        return lib().qh_slm_device_next(self.handle) or 0
+
     def close(self):
         if self.handle:
             lib().qh_slm_destroy(self.handle)

@@ -130,6 +130,25 @@ def test_generate_api_matches_steps(qh, cuda, small):
     slm.close()
 
 
+def test_device_driven_decode_matches_steps(qh, cuda, small):
+    """begin/advance/picks (graph replays, tokens fed on the device) give the
+    picks of the host-driven step loop at every position."""
+    cfg, blob, _ = small
+    rng = np.random.default_rng(5)
+    prompts = rng.integers(0, cfg.vocab, (3, 9)).astype(np.int32)
+    slm = qh.host.Slm(cfg, blob, 3)
+    gp, _ = gpu_run(slm, prompts, 14)
+    slm.reset()
+    slm.begin(prompts)
+    for n in (1, 4, 3, 8, 6):  # uneven chunks across the prompt/decode boundary
+        slm.advance(n)
+    got = slm.picks(0, 22)
+    assert np.array_equal(got, gp), "device-driven picks differ from the step loop"
+    with pytest.raises(qh.QHError):
+        slm.picks(0, 23)  # beyond the steps run
+    slm.close()
+
+
 @pytest.fixture(scope="module")
 def full(qh, cuda):
     cfg = qh.host.slm_config(320)
