@@ -94,6 +94,43 @@ int qh_argmax(const float *d_logits, int32_t B, int64_t vocab, int32_t *d_out, v
 int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int32_t stride, int32_t *d_ctl,
                  int32_t *d_tokens, int32_t *d_picks, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Fused forms used by the decode step. Same arithmetic as the chains they
+ * replace (bit-identical results), fewer launches and HBM round trips.
+ * ---------------------------------------------------------------------- */
+
+/* Optional residual add, RMSNorm and Q8_K quantization in one launch:
+ * if d_mix, h += mix (written back); xq = Q8_K(rmsnorm(h) * w) in the split
+ * layout of qh_backend.h for K = dim, n_tok = B (qh_add + qh_rmsnorm +
+ * qh_quantize_q8k; slm/tensor.c:285, 348-369, 683-720). dim a multiple of
+ * 256, at most 4096. */
+int qh_rmsnorm_q8k(float *d_h, const float *d_mix, const float *d_w, int64_t dim, int32_t B, float eps,
+                   void *d_xq, void *stream);
+
+/* xq = Q8_K(silu(gate) * up) for B rows of ffn values (qh_swiglu +
+ * qh_quantize_q8k; slm/qwen.c:952-955). */
+int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B, void *d_xq, void *stream);
+
+/* The whole Gated DeltaNet mixer between its projections for one token per
+ * sequence (slm/qwen.c:357-598): qh_gdn_pre + qh_gdn_recurrence +
+ * qh_gdn_gated_norm (z is the attn_gate projection [B][heads*hd], norm_w
+ * ssm_norm [hd]) + Q8_K of the result into xq (K = heads*hd, n_tok = B).
+ * hd must be 128, heads even. */
+int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
+                 const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
+                 const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
+                 const int32_t *d_pos, void *d_xq, void *stream);
+
+/* qh_argmax + qh_feed_next over a grid of CTAs per row (sample_argmax,
+ * slm/model.c:401-412). d_scratch holds per-slice partial maxima and ticket
+ * counters: qh_argmax_feed_scratch_bytes bytes, zero-filled before the first
+ * call (each call leaves the counters at zero). The size query returns -1
+ * for bad arguments. */
+int64_t qh_argmax_feed_scratch_bytes(int32_t B, int64_t vocab);
+int qh_argmax_feed(const float *d_logits, int32_t B, int64_t vocab, void *d_scratch, int32_t *d_next,
+                   const int32_t *d_prompt, int32_t stride, int32_t *d_ctl, int32_t *d_tokens, int32_t *d_picks,
+                   void *stream);
+
 #ifdef __cplusplus
 }
 #endif

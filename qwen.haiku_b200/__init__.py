@@ -135,6 +135,12 @@ SIGNATURES.update({  # include/qh_kernels.h
                             _P, _P]),
     "qh_argmax": (_I, [_P, C.c_int32, _I64, _P, _P]),
     "qh_feed_next": (_I, [_P, _P, C.c_int32, C.c_int32, _P, _P, _P, _P]),
+    "qh_rmsnorm_q8k": (_I, [_P, _P, _P, _I64, C.c_int32, C.c_float, _P, _P]),
+    "qh_swiglu_q8k": (_I, [_P, _P, _I64, C.c_int32, _P, _P]),
+    "qh_gdn_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                          C.c_float, _P, _P, _P]),
+    "qh_argmax_feed_scratch_bytes": (_I64, [C.c_int32, _I64]),
+    "qh_argmax_feed": (_I, [_P, C.c_int32, _I64, _P, _P, _P, C.c_int32, _P, _P, _P, _P]),
 })
 
 _lib = None

@@ -27,6 +27,17 @@ enum DeviceError : int {
 // far beyond any legitimate stall, short enough to return control.
 constexpr uint32_t kWaitLimit = 1u << 22;
 
+// Programmatic dependent launch. Every kernel of this library starts with
+// pdl_launch_dependents() (the next kernel on the stream may be scheduled
+// as soon as all CTAs of this one run) and calls pdl_wait() before it reads
+// or writes memory that an earlier kernel touches: pdl_wait returns once the
+// preceding grid has completed and its writes are visible. Both are no-ops
+// in a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -381,6 +381,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
     const int S = p.n_stages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -399,10 +400,30 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
     if (warp == kConsumerWarps) {
         // ----- producer warp (uniform control flow; lane 0 owns the barriers) -----
+        // The weight bytes of the first ring's worth of tiles are requested
+        // before pdl_wait() -- they do not depend on earlier kernels, so under
+        // programmatic launch they stream in while the previous kernel (the
+        // activation quantizer) finishes; the activation planes follow the wait.
+        const int n_pre = min(n_my, S);
+        auto issue_x = [&](int s) {
+            if (lane == 0) {
+                const GemvJob &jb = meta[s].job;
+                uint32_t xq_b, xb_b, xd_b;
+                x_plane_bytes(TYPE, jb, p.n_tok, &xq_b, &xb_b, &xd_b);
+                uint8_t *xdst = data + static_cast<int64_t>(s) * p.stage_bytes + p.x_offset;
+                bulk_copy_g2s(xdst, jb.xqs, xq_b, &full[s]);
+                if (xb_b) bulk_copy_g2s(xdst + xq_b, jb.xbs, xb_b, &full[s]);
+                bulk_copy_g2s(xdst + xq_b + xb_b, jb.xd, xd_b, &full[s]);
+            }
+        };
         int issued = 0;
         int j = n_my > 0 ? find_job(p, t_begin) : 0;
         GemvJob job = load_job(p, j);
         for (int i = 0; i < n_my; ++i) {
+            if (i == n_pre) {
+                pdl_wait();
+                for (int t = 0; t < n_pre; ++t) issue_x(t);
+            }
             // Every decision that ends the loop is made warp-uniform, so the
             // __syncwarp below never waits for a lane that has left.
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
@@ -424,7 +445,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             uint8_t *dst = data + static_cast<int64_t>(s) * p.stage_bytes;
             uint32_t xq_b, xb_b, xd_b;
             x_plane_bytes(TYPE, job, p.n_tok, &xq_b, &xb_b, &xd_b);
-            uint8_t *xdst = dst + p.x_offset;
             const uint8_t *g1 = g0 + static_cast<int64_t>(nrows) * job.row_bytes;
             const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g0) & ~uintptr_t(15));
             const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g1) & ~uintptr_t(15));
@@ -444,12 +464,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             }
             __syncwarp();
             if (lane == 0 && wbytes) bulk_copy_g2s(dst, a0, wbytes, &full[s]);
-            if (lane == 0) {
-                bulk_copy_g2s(xdst, job.xqs, xq_b, &full[s]);
-                if (xb_b) bulk_copy_g2s(xdst + xq_b, job.xbs, xb_b, &full[s]);
-                bulk_copy_g2s(xdst + xq_b + xb_b, job.xd, xd_b, &full[s]);
-            }
+            if (i >= n_pre) issue_x(s);
             ++issued;
+        }
+        if (issued == n_pre && n_pre > 0) {  // the loop ended inside the first ring
+            pdl_wait();
+            for (int t = 0; t < n_pre; ++t) issue_x(t);
         }
         // Drain: wait for this CTA's copies in flight before exiting.
         for (int i = max(0, issued - S); i < issued; ++i)
@@ -556,8 +576,7 @@ static cudaError_t launch_one(const GemvParams &p, const GemvGeometry &g, cudaSt
         if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
-    gemv_kernel<TYPE, NT><<<g.grid, kGemvThreads, g.smem_bytes, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(gemv_kernel<TYPE, NT>, dim3(g.grid), dim3(kGemvThreads), g.smem_bytes, stream, p);
 }
 
 template <int TYPE>

@@ -73,6 +73,25 @@ cudaError_t quantize_q8k_launch(const float *x, int64_t k, int64_t n_tok, void *
 cudaError_t quantize_q8_0_launch(const float *x, int64_t k, int64_t n_tok, void *q8_0,
                                  cudaStream_t stream);
 
+// Launch with programmatic stream serialization (the kernel may start
+// while the previous kernel on the stream finishes; it orders itself with
+// pdl_wait()). Captured into CUDA graphs as programmatic edges.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Device error word (lazily allocated per device) and its reset/read.
 int *device_error_word();
 

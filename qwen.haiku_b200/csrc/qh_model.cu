@@ -18,6 +18,7 @@
 // token streams drift. RoPE cos/sin come from a host-computed table so they
 // match the reference's libm bit for bit.
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -70,6 +71,8 @@ __device__ float block_max_f(float v, float *scratch) {
 // ---------------------------------------------------------------------------
 __global__ void embed_q6k_kernel(const uint8_t *__restrict__ table, int64_t hidden,
                                  const int32_t *__restrict__ tokens, float *__restrict__ h) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.y, sb = blockIdx.x, p = threadIdx.x;
     const int64_t nb = hidden / QH_QK;
     const uint8_t *blk = table + (static_cast<int64_t>(tokens[b]) * nb + sb) * QH_Q6K_BYTES;
@@ -88,6 +91,8 @@ __global__ void embed_q6k_kernel(const uint8_t *__restrict__ table, int64_t hidd
 // ---------------------------------------------------------------------------
 __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int64_t dim,
                                float eps, float *__restrict__ y) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ double scratch[32];
     const float *xr = x + blockIdx.x * dim;
     float *yr = y + blockIdx.x * dim;
@@ -102,12 +107,16 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 }
 
 __global__ void add_kernel(float *__restrict__ h, const float *__restrict__ mix, int64_t n) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i < n) h[i] = __fadd_rn(h[i], mix[i]);
 }
 
 __global__ void swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ o,
                               int64_t n) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i < n) o[i] = __fmul_rn(silu_f(g[i]), u[i]);
 }
@@ -122,6 +131,8 @@ __global__ void gdn_pre_kernel(const float *__restrict__ qkv, float *__restrict_
                                const float *__restrict__ ssm_a, int heads, int hd, int kk,
                                const int32_t *__restrict__ pos_ptr, float *__restrict__ qo, float *__restrict__ ko, float *__restrict__ vo,
                                float *__restrict__ beta, float *__restrict__ gout) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ double scratch[32];
     const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
     const int kdim = heads * hd, conv_dim = 3 * kdim;
@@ -173,6 +184,8 @@ __global__ void __launch_bounds__(HD) gdn_recurrence_kernel(float *__restrict__ 
                                                             const float *__restrict__ beta,
                                                             const float *__restrict__ g, int heads,
                                                             float *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float Ks[HD], Qs[HD];
     const int b = blockIdx.x, h = blockIdx.y, v = threadIdx.x;
     const int64_t vec = (static_cast<int64_t>(b) * heads + h) * HD;
@@ -202,6 +215,8 @@ __global__ void __launch_bounds__(HD) gdn_recurrence_kernel(float *__restrict__ 
 // Gated RMSNorm: one CTA (hd threads) per (sequence, head).
 __global__ void gdn_gated_norm_kernel(const float *__restrict__ x, const float *__restrict__ z,
                                       const float *__restrict__ w, int hd, float eps, float *__restrict__ y) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ double scratch[32];
     const int64_t base = (static_cast<int64_t>(blockIdx.x) * gridDim.y + blockIdx.y) * hd;
     const int t = threadIdx.x;
@@ -223,6 +238,8 @@ __global__ void attn_pre_kernel(const float *__restrict__ qraw, const float *__r
                                 const int32_t *__restrict__ pos_ptr, int max_pos,
                                 float *__restrict__ qout, float *__restrict__ gate,
                                 __half *__restrict__ kcache, __half *__restrict__ vcache) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ double scratch[32];
     __shared__ float xs[512];
     const int b = blockIdx.x, j = blockIdx.y, t = threadIdx.x;
@@ -268,6 +285,8 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
                                    const __half *__restrict__ vcache, const float *__restrict__ gate,
                                    int nh, int kvh, int hd, const int32_t *__restrict__ pos_ptr,
                                    int max_pos, float *__restrict__ ctx) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ float sh[];  // [hd] query, [max_pos] scores, [32] scratch
     float *qs = sh;
     float *sc = sh + hd;
@@ -312,6 +331,8 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
 
 // Greedy argmax: one CTA per row; ties keep the smaller index.
 __global__ void argmax_kernel(const float *__restrict__ logits, int64_t vocab, int32_t *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float *row = logits + static_cast<int64_t>(blockIdx.x) * vocab;
@@ -343,6 +364,8 @@ __global__ void argmax_kernel(const float *__restrict__ logits, int64_t vocab, i
 __global__ void feed_next_kernel(const int32_t *__restrict__ next, const int32_t *__restrict__ prompt, int32_t B,
                                  int32_t stride, int32_t *__restrict__ ctl, int32_t *__restrict__ tokens,
                                  int32_t *__restrict__ picks) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int pos = ctl[0], n_prompt = ctl[1];
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
         const int32_t nx = next[b];
@@ -359,8 +382,9 @@ __global__ void feed_next_kernel(const int32_t *__restrict__ next, const int32_t
 // C-ABI launchers
 // ---------------------------------------------------------------------------
 namespace {
-int launch_status(const char *what) {
-    cudaError_t e = cudaGetLastError();
+int launch_status(cudaError_t e, const char *what) {
+    const cudaError_t last = cudaGetLastError();
+    if (e == cudaSuccess) e = last;
     if (e == cudaSuccess) return QH_OK;
     char msg[256];
     snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(e));
@@ -379,31 +403,31 @@ int qh_embed_q6k(const void *d_table, int64_t hidden, const int32_t *d_tokens, i
                  void *stream) {
     if (!d_table || !d_tokens || !d_h || hidden % 256 || B <= 0) return bad("qh_embed_q6k: bad arguments");
     dim3 grid(static_cast<unsigned>(hidden / 256), static_cast<unsigned>(B));
-    qh::embed_q6k_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::embed_q6k_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), 
         static_cast<const uint8_t *>(d_table), hidden, d_tokens, d_h);
-    return launch_status("qh_embed_q6k");
+    return launch_status(le, "qh_embed_q6k");
 }
 
 int qh_rmsnorm(const float *d_x, const float *d_w, int64_t dim, int64_t rows, float eps, float *d_y,
                void *stream) {
     if (!d_x || !d_w || !d_y || dim <= 0 || rows <= 0 || rows > 0x7fffffff) return bad("qh_rmsnorm: bad arguments");
     const int threads = dim >= 256 ? 256 : 128;
-    qh::rmsnorm_kernel<<<static_cast<unsigned>(rows), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::rmsnorm_kernel, dim3(static_cast<unsigned>(rows)), dim3(threads), 0, static_cast<cudaStream_t>(stream), 
         d_x, d_w, dim, eps, d_y);
-    return launch_status("qh_rmsnorm");
+    return launch_status(le, "qh_rmsnorm");
 }
 
 int qh_add(float *d_h, const float *d_mix, int64_t n, void *stream) {
     if (!d_h || !d_mix || n <= 0) return bad("qh_add: bad arguments");
-    qh::add_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(d_h, d_mix, n);
-    return launch_status("qh_add");
+    const cudaError_t le = qh::launch_pdl(qh::add_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), d_h, d_mix, n);
+    return launch_status(le, "qh_add");
 }
 
 int qh_swiglu(const float *d_gate, const float *d_up, float *d_out, int64_t n, void *stream) {
     if (!d_gate || !d_up || !d_out || n <= 0) return bad("qh_swiglu: bad arguments");
-    qh::swiglu_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::swiglu_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
         d_gate, d_up, d_out, n);
-    return launch_status("qh_swiglu");
+    return launch_status(le, "qh_swiglu");
 }
 
 int qh_gdn_pre(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b,
@@ -413,9 +437,9 @@ int qh_gdn_pre(const float *d_qkv, float *d_ring, const float *d_conv_w, const f
     if (B <= 0 || heads <= 0 || hd <= 0 || hd % 32 || hd > 1024 || kk <= 0 || !d_pos)
         return bad("qh_gdn_pre: bad arguments");
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
-    qh::gdn_pre_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::gdn_pre_kernel, dim3(grid), dim3(hd), 0, static_cast<cudaStream_t>(stream), 
         d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, heads, hd, kk, d_pos, d_q, d_k, d_v, d_beta, d_g);
-    return launch_status("qh_gdn_pre");
+    return launch_status(le, "qh_gdn_pre");
 }
 
 int qh_gdn_recurrence(float *d_state, const float *d_q, const float *d_k, const float *d_v,
@@ -427,17 +451,17 @@ int qh_gdn_recurrence(float *d_state, const float *d_q, const float *d_k, const 
         return QH_ERR_UNSUPPORTED;
     }
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
-    qh::gdn_recurrence_kernel<128><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::gdn_recurrence_kernel<128>, dim3(grid), dim3(128), 0, static_cast<cudaStream_t>(stream), 
         d_state, d_q, d_k, d_v, d_beta, d_g, heads, d_out);
-    return launch_status("qh_gdn_recurrence");
+    return launch_status(le, "qh_gdn_recurrence");
 }
 
 int qh_gdn_gated_norm(const float *d_x, const float *d_z, const float *d_w, int32_t B, int32_t heads,
                       int32_t hd, float eps, float *d_y, void *stream) {
     if (B <= 0 || heads <= 0 || hd <= 0 || hd % 32 || hd > 1024) return bad("qh_gdn_gated_norm: bad arguments");
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(heads));
-    qh::gdn_gated_norm_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(d_x, d_z, d_w, hd, eps, d_y);
-    return launch_status("qh_gdn_gated_norm");
+    const cudaError_t le = qh::launch_pdl(qh::gdn_gated_norm_kernel, dim3(grid), dim3(hd), 0, static_cast<cudaStream_t>(stream), d_x, d_z, d_w, hd, eps, d_y);
+    return launch_status(le, "qh_gdn_gated_norm");
 }
 
 int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
@@ -448,10 +472,10 @@ int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const f
         !d_pos || max_pos <= 0)
         return bad("qh_attn_pre: bad arguments");
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh + kvh));
-    qh::attn_pre_kernel<<<grid, hd, 0, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::attn_pre_kernel, dim3(grid), dim3(hd), 0, static_cast<cudaStream_t>(stream), 
         d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, nh, kvh, hd, rope_dim, eps, d_pos, max_pos, d_q, d_gate,
         reinterpret_cast<__half *>(d_kcache), reinterpret_cast<__half *>(d_vcache));
-    return launch_status("qh_attn_pre");
+    return launch_status(le, "qh_attn_pre");
 }
 
 int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache,
@@ -469,25 +493,431 @@ int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d
         attr_done[dev] = true;
     }
     dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh));
-    qh::attn_decode_kernel<<<grid, hd, smem, static_cast<cudaStream_t>(stream)>>>(
+    const cudaError_t le = qh::launch_pdl(qh::attn_decode_kernel, dim3(grid), dim3(hd), smem, static_cast<cudaStream_t>(stream), 
         d_q, reinterpret_cast<const __half *>(d_kcache), reinterpret_cast<const __half *>(d_vcache), d_gate, nh,
         kvh, hd, d_pos, max_pos, d_ctx);
-    return launch_status("qh_attn_decode");
+    return launch_status(le, "qh_attn_decode");
 }
 
 int qh_argmax(const float *d_logits, int32_t B, int64_t vocab, int32_t *d_out, void *stream) {
     if (!d_logits || !d_out || B <= 0 || vocab <= 0) return bad("qh_argmax: bad arguments");
-    qh::argmax_kernel<<<static_cast<unsigned>(B), 1024, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, vocab, d_out);
-    return launch_status("qh_argmax");
+    const cudaError_t le = qh::launch_pdl(qh::argmax_kernel, dim3(static_cast<unsigned>(B)), dim3(1024), 0, static_cast<cudaStream_t>(stream), d_logits, vocab, d_out);
+    return launch_status(le, "qh_argmax");
 }
 
 int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int32_t stride, int32_t *d_ctl,
                  int32_t *d_tokens, int32_t *d_picks, void *stream) {
     if (!d_next || !d_prompt || !d_ctl || !d_tokens || !d_picks || B <= 0 || stride <= 0)
         return bad("qh_feed_next: bad arguments");
-    qh::feed_next_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_next, d_prompt, B, stride, d_ctl,
+    const cudaError_t le = qh::launch_pdl(qh::feed_next_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), d_next, d_prompt, B, stride, d_ctl,
                                                                           d_tokens, d_picks);
-    return launch_status("qh_feed_next");
+    return launch_status(le, "qh_feed_next");
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Fused kernels of the decode step. Each one replaces a chain of the kernels
+// above with identical arithmetic (same operations, same order, same
+// rounding), so results are bit-identical to the unfused chain; they exist
+// to cut launches and round trips through HBM per token.
+// ===========================================================================
+namespace qh {
+
+// Candidate for the Q8_K block maximum: |x| (NaN never wins), its index in
+// the block and its signed value; ties go to the smaller index, as the
+// reference's first-strictly-greater scan does.
+__device__ __forceinline__ void best_merge(float &a, int &i, float &v, float oa, int oi, float ov) {
+    if (oa > a || (oa == a && oi < i)) { a = oa; i = oi; v = ov; }
+}
+
+__device__ __forceinline__ void warp_best(float &a, int &i, float &v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, a, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, off);
+        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+        best_merge(a, i, v, oa, oi, ov);
+    }
+}
+
+// q = clamp(round_half_even(iscale * v)) through the 1.5*2^23 bias, as
+// quantize_q8k_kernel does (slm/tensor.c:673-678, 683-720).
+__device__ __forceinline__ int q8k_value(float v, float iscale) {
+    const float f = __fmul_rn(iscale, v);
+    const float biased = __fadd_rn(f, 12582912.0f);
+    int q = (__float_as_int(biased) & 0x007fffff) - 0x00400000;
+    if (f != f) q = 0;
+    return q > 127 ? 127 : (q < -128 ? -128 : q);
+}
+
+// Pointers into the split Q8_K layout (qh_formats.h) of row `tok`.
+struct Q8KRow {
+    int8_t *qs;
+    float *d;
+    int16_t *bs;
+};
+__device__ __forceinline__ Q8KRow q8k_row(uint8_t *base, int64_t k, int64_t n_tok, int64_t tok) {
+    Q8KRow r;
+    r.qs = reinterpret_cast<int8_t *>(base) + tok * k;
+    r.d = reinterpret_cast<float *>(base + qhf_q8k_d_offset(k, n_tok)) + tok * qhf_q8k_d_stride(k);
+    r.bs = reinterpret_cast<int16_t *>(base + qhf_q8k_bsums_offset(k, n_tok)) + tok * (k / QH_QK) * 16;
+    return r;
+}
+
+struct Q8KScratch {
+    float a[8], v[8];
+    int i[8];
+};
+
+// Q8_K quantization of one 256-value block held one value per thread by a
+// 256-thread CTA (thread t holds element t). qs/bs point at the block's
+// 256 quants / 16 group sums, d at its scale. Ends with a barrier, so the
+// scratch can be reused by the next block.
+__device__ void q8k_block256(float v, Q8KScratch &sc, int8_t *qs, float *d, int16_t *bs) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float a = (v == v) ? fabsf(v) : -1.0f, bv = v;
+    int bi = tid;
+    warp_best(a, bi, bv);
+    if (lane == 0) { sc.a[warp] = a; sc.i[warp] = bi; sc.v[warp] = bv; }
+    __syncthreads();
+    float ba = sc.a[0], xv = sc.v[0];
+    int ii = sc.i[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) best_merge(ba, ii, xv, sc.a[w], sc.i[w], sc.v[w]);
+    const float xmax = ba > 0.0f ? xv : 0.0f;
+    int q = 0;
+    if (xmax != 0.0f) {
+        const float iscale = __fdiv_rn(-127.0f, xmax);
+        q = q8k_value(v, iscale);
+        if (tid == 0) *d = __fdiv_rn(1.0f, iscale);
+    } else if (tid == 0) {
+        *d = 0.0f;
+    }
+    qs[tid] = static_cast<int8_t>(q);
+    int s = q;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if ((lane & 15) == 0) bs[warp * 2 + (lane >> 4)] = static_cast<int16_t>(s);
+    __syncthreads();
+}
+
+// (optional residual add) + RMSNorm + Q8_K: one 256-thread CTA per row.
+// Same sums as add_kernel, rmsnorm_kernel (256 threads) and
+// quantize_q8k_kernel in sequence.
+constexpr int kResNormMaxBlocks = 16;
+__global__ void __launch_bounds__(256) resnorm_q8k_kernel(float *__restrict__ h, const float *__restrict__ mix,
+                                                          const float *__restrict__ w, int dim, float eps,
+                                                          uint8_t *__restrict__ xq, int n_tok) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ double scratch[32];
+    __shared__ Q8KScratch sc;
+    const int row = blockIdx.x, tid = threadIdx.x, nb = dim / QH_QK;
+    float v[kResNormMaxBlocks];
+    double s = 0.0;
+#pragma unroll
+    for (int j = 0; j < kResNormMaxBlocks; ++j) {
+        if (j < nb) {
+            const int64_t i = static_cast<int64_t>(row) * dim + j * QH_QK + tid;
+            float x = h[i];
+            if (mix) {
+                x = __fadd_rn(x, mix[i]);
+                h[i] = x;
+            }
+            v[j] = x;
+            s += static_cast<double>(__fmul_rn(x, x));
+        }
+    }
+    const double ssq = block_sum_d(s, scratch);
+    const float rscale =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(dim)), eps)));
+    const Q8KRow r = q8k_row(xq, dim, n_tok, row);
+#pragma unroll
+    for (int j = 0; j < kResNormMaxBlocks; ++j) {
+        if (j < nb) {
+            const float y = __fmul_rn(__fmul_rn(v[j], rscale), w[j * QH_QK + tid]);
+            q8k_block256(y, sc, r.qs + j * QH_QK, r.d + j, r.bs + j * 16);
+        }
+    }
+}
+
+// SwiGLU + Q8_K: CTA (block, row), 256 threads.
+__global__ void __launch_bounds__(256) swiglu_q8k_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                                                         int ffn, uint8_t *__restrict__ xq, int n_tok) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ Q8KScratch sc;
+    const int blk = blockIdx.x, row = blockIdx.y, tid = threadIdx.x;
+    const int64_t i = static_cast<int64_t>(row) * ffn + blk * QH_QK + tid;
+    const float v = __fmul_rn(silu_f(g[i]), u[i]);
+    const Q8KRow r = q8k_row(xq, ffn, n_tok, row);
+    q8k_block256(v, sc, r.qs + blk * QH_QK, r.d + blk, r.bs + blk * 16);
+}
+
+// Whole Gated DeltaNet head for one token: CTA (sequence, head) of HD
+// threads runs gdn_pre_kernel, gdn_recurrence_kernel and
+// gdn_gated_norm_kernel in registers and shared memory, then quantizes the
+// gated-norm output to Q8_K. A Q8_K block (256) spans two heads, so CTAs
+// come in clusters of two along the head axis and agree on the block
+// maximum through distributed shared memory.
+template <int HD>
+__global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
+    gdn_fused_kernel(const float *__restrict__ qkv, float *__restrict__ ring, const float *__restrict__ conv_w,
+                     const float *__restrict__ bb, const float *__restrict__ aa, const float *__restrict__ dt_bias,
+                     const float *__restrict__ ssm_a, float *__restrict__ state, const float *__restrict__ z,
+                     const float *__restrict__ norm_w, int heads, int kk, float eps,
+                     const int32_t *__restrict__ pos_ptr, uint8_t *__restrict__ xq, int n_tok) {
+    static_assert(HD == 128, "a cluster pair of heads must form one 256-value Q8_K block");
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ double scratch[32];
+    __shared__ float Ks[HD], Qs[HD];
+    __shared__ float s_beta, s_g;
+    __shared__ float wa[HD / 32], wv[HD / 32];
+    __shared__ int wi[HD / 32];
+    __shared__ float c_a, c_v;
+    __shared__ int c_i;
+    const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int kdim = heads * HD, conv_dim = 3 * kdim;
+    // ---- conv ring + SiLU + L2 norms + beta/g (gdn_pre_kernel) ----
+    const int pos = max(*pos_ptr, 0);
+    const int slot = pos % kk, head_after = (pos + 1) % kk;
+    const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
+    float *rg = ring + static_cast<int64_t>(b) * kk * conv_dim;
+    float mixed[3];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+        rg[static_cast<int64_t>(slot) * conv_dim + ch] = src[ch];
+        float acc = 0.0f;
+        for (int k = 0; k < kk; ++k) {
+            const int sl = (head_after + k) % kk;
+            acc = __fadd_rn(acc, __fmul_rn(rg[static_cast<int64_t>(sl) * conv_dim + ch], conv_w[ch * kk + k]));
+        }
+        mixed[part] = silu_f(acc);
+    }
+    const double qss = block_sum_d(static_cast<double>(__fmul_rn(mixed[0], mixed[0])), scratch);
+    const double kss = block_sum_d(static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+    const float qrs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qss)), 1e-6f));
+    const float krs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(kss)), 1e-6f));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
+    Qs[t] = __fmul_rn(__fmul_rn(mixed[0], qrs), scale);
+    Ks[t] = __fmul_rn(mixed[1], krs);
+    const float vt = mixed[2];
+    if (t == 0) {
+        const int i = b * heads + h;
+        s_beta = sigmoid_f(bb[i]);
+        const float a = __fadd_rn(aa[i], dt_bias[h]);
+        const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
+        s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
+    }
+    __syncthreads();
+    // ---- recurrence (gdn_recurrence_kernel): thread v owns state column v ----
+    float *st = state + (static_cast<int64_t>(b) * heads + h) * HD * HD;
+    const float gh = s_g, bh = s_beta;
+    float s[HD];
+    double acc = 0.0;
+#pragma unroll
+    for (int k = 0; k < HD; ++k) {
+        s[k] = __fmul_rn(st[k * HD + t], gh);
+        acc += static_cast<double>(__fmul_rn(s[k], Ks[k]));
+    }
+    const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
+    double acc2 = 0.0;
+#pragma unroll
+    for (int k = 0; k < HD; ++k) {
+        s[k] = __fadd_rn(s[k], __fmul_rn(Ks[k], delta));
+        st[k * HD + t] = s[k];
+        acc2 += static_cast<double>(__fmul_rn(s[k], Qs[k]));
+    }
+    const float o = static_cast<float>(acc2);
+    // ---- gated RMSNorm (gdn_gated_norm_kernel) ----
+    const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
+    const float mean = static_cast<float>(ssq / static_cast<double>(HD));
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    const int64_t zi = static_cast<int64_t>(b) * kdim + h * HD + t;
+    const float y = __fmul_rn(__fmul_rn(__fmul_rn(o, rs), norm_w[t]), silu_f(z[zi]));
+    // ---- Q8_K over the head pair (quantize_q8k_kernel) ----
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int half = static_cast<int>(cluster.block_rank());  // == h & 1
+    float a = (y == y) ? fabsf(y) : -1.0f, bv = y;
+    int bi = half * HD + t;
+    warp_best(a, bi, bv);
+    if (lane == 0) { wa[warp] = a; wi[warp] = bi; wv[warp] = bv; }
+    __syncthreads();
+    if (t == 0) {
+        float ca = wa[0], cv = wv[0];
+        int ci = wi[0];
+        for (int w = 1; w < HD / 32; ++w) best_merge(ca, ci, cv, wa[w], wi[w], wv[w]);
+        c_a = ca; c_i = ci; c_v = cv;
+    }
+    cluster.sync();
+    float ba = c_a, xv = c_v;
+    int ii = c_i;
+    {
+        const float *pa = cluster.map_shared_rank(&c_a, half ^ 1);
+        const int *pi = cluster.map_shared_rank(&c_i, half ^ 1);
+        const float *pv = cluster.map_shared_rank(&c_v, half ^ 1);
+        best_merge(ba, ii, xv, *pa, *pi, *pv);
+    }
+    cluster.sync();  // the partner has read this CTA's candidate
+    const float xmax = ba > 0.0f ? xv : 0.0f;
+    const Q8KRow r = q8k_row(xq, kdim, n_tok, b);
+    const int blk = h >> 1;
+    int q = 0;
+    if (xmax != 0.0f) {
+        const float iscale = __fdiv_rn(-127.0f, xmax);
+        q = q8k_value(y, iscale);
+        if (half == 0 && t == 0) r.d[blk] = __fdiv_rn(1.0f, iscale);
+    } else if (half == 0 && t == 0) {
+        r.d[blk] = 0.0f;
+    }
+    r.qs[blk * QH_QK + half * HD + t] = static_cast<int8_t>(q);
+    int sum = q;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if ((lane & 15) == 0) r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+}
+
+// Greedy pick + device-side feed (argmax_kernel + feed_next_kernel) over a
+// grid of (parts, rows): each CTA scans one slice of the row, the last CTA
+// of a row (ticket counter) merges the slices in order, records the pick
+// and feeds the next input; the last row advances the position. Counters
+// are left at zero for the next launch.
+constexpr int kArgmaxThreads = 512;
+__global__ void __launch_bounds__(kArgmaxThreads)
+    argmax_feed_kernel(const float *__restrict__ logits, int64_t vocab, float *__restrict__ part_v,
+                       int *__restrict__ part_i, unsigned *__restrict__ tickets, int32_t *__restrict__ next,
+                       const int32_t *__restrict__ prompt, int B, int stride, int32_t *__restrict__ ctl,
+                       int32_t *__restrict__ tokens, int32_t *__restrict__ picks) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float sv[kArgmaxThreads / 32];
+    __shared__ int si[kArgmaxThreads / 32];
+    __shared__ bool last;
+    const int part = blockIdx.x, P = gridDim.x, row = blockIdx.y;
+    const int64_t chunk = (vocab + P - 1) / P;
+    const int64_t lo = part * chunk, hi = min(vocab, lo + chunk);
+    const float *lr = logits + static_cast<int64_t>(row) * vocab;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = lr[i];
+        if (v > best) { best = v; bi = static_cast<int>(i); }
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kArgmaxThreads / 32; ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+        part_v[row * P + part] = best;
+        part_i[row * P + part] = bi;
+        __threadfence();
+        last = atomicAdd(&tickets[row], 1u) == static_cast<unsigned>(P - 1);
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    float bv = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (int p = 0; p < P; ++p) {
+        const float v = __ldcg(part_v + row * P + p);
+        const int i = __ldcg(part_i + row * P + p);
+        if (v > bv || (v == bv && i < bidx)) { bv = v; bidx = i; }
+    }
+    // sample_argmax starts from element 0: a NaN there is never replaced
+    const float first = lr[0];
+    const int32_t nx = (first != first || bidx == 0x7fffffff) ? 0 : bidx;
+    next[row] = nx;
+    const int pos = ctl[0], n_prompt = ctl[1];
+    if (pos >= 0 && pos < stride) picks[static_cast<int64_t>(row) * stride + pos] = nx;
+    tokens[row] = (pos + 1 < n_prompt && pos + 1 < stride) ? prompt[static_cast<int64_t>(row) * stride + pos + 1] : nx;
+    tickets[row] = 0u;
+    __threadfence();
+    if (atomicAdd(&tickets[B], 1u) == static_cast<unsigned>(B - 1)) {
+        ctl[0] = pos + 1;
+        tickets[B] = 0u;
+    }
+}
+
+}  // namespace qh
+
+// ---------------------------------------------------------------------------
+// C-ABI launchers of the fused kernels
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int qh_rmsnorm_q8k(float *d_h, const float *d_mix, const float *d_w, int64_t dim, int32_t B, float eps,
+                   void *d_xq, void *stream) {
+    if (!d_h || !d_w || !d_xq || dim <= 0 || dim % QH_QK || dim > qh::kResNormMaxBlocks * QH_QK || B <= 0)
+        return bad("qh_rmsnorm_q8k: bad arguments");
+    const cudaError_t le = qh::launch_pdl(qh::resnorm_q8k_kernel, dim3(static_cast<unsigned>(B)), dim3(256), 0,
+                                          static_cast<cudaStream_t>(stream), d_h, d_mix, d_w,
+                                          static_cast<int>(dim), eps, static_cast<uint8_t *>(d_xq), B);
+    return launch_status(le, "qh_rmsnorm_q8k");
+}
+
+int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B, void *d_xq, void *stream) {
+    if (!d_gate || !d_up || !d_xq || ffn <= 0 || ffn % QH_QK || B <= 0 || B > 65535)
+        return bad("qh_swiglu_q8k: bad arguments");
+    const cudaError_t le = qh::launch_pdl(qh::swiglu_q8k_kernel, dim3(static_cast<unsigned>(ffn / QH_QK), B),
+                                          dim3(256), 0, static_cast<cudaStream_t>(stream), d_gate, d_up,
+                                          static_cast<int>(ffn), static_cast<uint8_t *>(d_xq), B);
+    return launch_status(le, "qh_swiglu_q8k");
+}
+
+int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
+                 const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
+                 const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
+                 const int32_t *d_pos, void *d_xq, void *stream) {
+    if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_state || !d_z ||
+        !d_norm_w || !d_pos || !d_xq || B <= 0 || heads <= 0 || heads % 2 || kk <= 0)
+        return bad("qh_gdn_fused: bad arguments");
+    if (hd != 128) {
+        qh::set_last_error_message("qh_gdn_fused: head dim must be 128");
+        return QH_ERR_UNSUPPORTED;
+    }
+    const cudaError_t le = qh::launch_pdl(qh::gdn_fused_kernel<128>, dim3(static_cast<unsigned>(B), heads),
+                                          dim3(128), 0, static_cast<cudaStream_t>(stream), d_qkv, d_ring,
+                                          d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, heads,
+                                          kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B);
+    return launch_status(le, "qh_gdn_fused");
+}
+
+static int argmax_parts(int64_t vocab) {
+    const int64_t p = (vocab + 4095) / 4096;
+    return static_cast<int>(p < 1 ? 1 : (p > 64 ? 64 : p));
+}
+
+int64_t qh_argmax_feed_scratch_bytes(int32_t B, int64_t vocab) {
+    if (B <= 0 || vocab <= 0) return -1;
+    const int64_t P = argmax_parts(vocab);
+    return (static_cast<int64_t>(B) * P * 8 + (static_cast<int64_t>(B) + 1) * 4 + 255) & ~int64_t(255);
+}
+
+int qh_argmax_feed(const float *d_logits, int32_t B, int64_t vocab, void *d_scratch, int32_t *d_next,
+                   const int32_t *d_prompt, int32_t stride, int32_t *d_ctl, int32_t *d_tokens, int32_t *d_picks,
+                   void *stream) {
+    if (!d_logits || !d_scratch || !d_next || !d_prompt || !d_ctl || !d_tokens || !d_picks || B <= 0 ||
+        B > 65535 || vocab <= 0 || vocab > 0x7ffffffe || stride <= 0)
+        return bad("qh_argmax_feed: bad arguments");
+    const int P = argmax_parts(vocab);
+    uint8_t *base = static_cast<uint8_t *>(d_scratch);
+    float *pv = reinterpret_cast<float *>(base);
+    int *pi = reinterpret_cast<int *>(base + static_cast<int64_t>(B) * P * 4);
+    unsigned *tickets = reinterpret_cast<unsigned *>(base + static_cast<int64_t>(B) * P * 8);
+    const cudaError_t le = qh::launch_pdl(qh::argmax_feed_kernel, dim3(P, B), dim3(qh::kArgmaxThreads), 0,
+                                          static_cast<cudaStream_t>(stream), d_logits, vocab, pv, pi, tickets,
+                                          d_next, d_prompt, B, stride, d_ctl, d_tokens, d_picks);
+    return launch_status(le, "qh_argmax_feed");
 }
 
 }  // extern "C"

@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float *__restri
                                                            int8_t *__restrict__ qs,
                                                            float *__restrict__ dv,
                                                            int16_t *__restrict__ bsums) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float s_abs[8];
     __shared__ int s_idx[8];
     __shared__ float s_xmax;
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restr
                                                             int64_t n_blocks,
                                                             int8_t *__restrict__ qs,
                                                             uint16_t *__restrict__ dbits) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t b = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     if (b >= n_blocks) return;
@@ -103,11 +107,11 @@ cudaError_t quantize_q8k_launch(const float *x, int64_t k, int64_t n_tok, void *
     if (k <= 0 || k % QH_QK || n_tok <= 0 || n_tok > 65535) return cudaErrorInvalidValue;
     uint8_t *base = static_cast<uint8_t *>(q8k);
     dim3 grid(static_cast<unsigned>(k / QH_QK), static_cast<unsigned>(n_tok));
-    quantize_q8k_kernel<<<grid, 256, 0, stream>>>(
+    const cudaError_t le = launch_pdl(quantize_q8k_kernel, dim3(grid), dim3(256), 0, stream, 
         x, k, reinterpret_cast<int8_t *>(base),
         reinterpret_cast<float *>(base + qhf_q8k_d_offset(k, n_tok)),
         reinterpret_cast<int16_t *>(base + qhf_q8k_bsums_offset(k, n_tok)));
-    return cudaGetLastError();
+    return le != cudaSuccess ? le : cudaGetLastError();
 }
 
 cudaError_t quantize_q8_0_launch(const float *x, int64_t k, int64_t n_tok, void *q8_0,
@@ -117,10 +121,10 @@ cudaError_t quantize_q8_0_launch(const float *x, int64_t k, int64_t n_tok, void 
     const int64_t n_blocks = (k / QH_QK8_0) * n_tok;
     const int64_t grid = (n_blocks + 7) / 8;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    quantize_q8_0_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+    const cudaError_t le = launch_pdl(quantize_q8_0_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, 
         x, k, n_blocks, reinterpret_cast<int8_t *>(base),
         reinterpret_cast<uint16_t *>(base + qhf_q8_0_d_offset(k, n_tok)));
-    return cudaGetLastError();
+    return le != cudaSuccess ? le : cudaGetLastError();
 }
 
 }  // namespace qh

@@ -69,6 +69,7 @@ struct qh_slm {
     void *xq_h, *xq_gdn, *xq_ffn;  // split Q8_K activations for K = hidden, gdn width, ffn
     int32_t *d_tok, *d_next;
     int32_t *d_ctl;                // [0] = position, [1] = prompt length
+    void *amax_scratch;            // qh_argmax_feed partials + tickets (kept zeroed)
     int32_t *d_prompt, *d_picks;   // [B][max_pos]: prompt tokens, greedy picks by position
     int32_t *h_tok, *h_next, *h_ctl;  // pinned
     int32_t host_pos;              // position of the next step
@@ -262,6 +263,12 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         TRY(dev_alloc(m, (void **)&m->d_tok, (size_t)B * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_next, (size_t)B * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_ctl, 16, NULL));
+        {
+            const int64_t ab = qh_argmax_feed_scratch_bytes(n_seq, cfg->vocab);
+            if (ab <= 0) { rc = QH_ERR_INVALID; goto fail; }
+            TRY(dev_alloc(m, &m->amax_scratch, (size_t)ab, NULL));
+            TRY(qh_memset(m->amax_scratch, 0, (size_t)ab, m->stream));
+        }
         TRY(dev_alloc(m, (void **)&m->d_prompt, (size_t)B * cfg->max_pos * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_picks, (size_t)B * cfg->max_pos * 4, NULL));
         if (cudaMallocHost((void **)&m->h_tok, (size_t)B * 4) != cudaSuccess ||
@@ -381,10 +388,10 @@ static int forward(qh_slm *m) {
     const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
     void *s = m->stream;
     CK(qh_embed_q6k(m->tok_embd, H, m->d_tok, B, m->h, s));
+    const float *pending = NULL;  // residual branch output not yet added to h
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        CK(qh_rmsnorm(m->h, Ly->attn_norm, H, B, c->norm_eps, m->hn, s));
-        CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
+        CK(qh_rmsnorm_q8k(m->h, pending, Ly->attn_norm, H, B, c->norm_eps, m->xq_h, s));
         CK(run_plans(m, &Ly->p_in));
         if (Ly->is_attn) {
             const int64_t ai = Ly->attn_index;
@@ -400,29 +407,21 @@ static int forward(qh_slm *m) {
             const int64_t gi = Ly->gdn_index;
             float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
-            CK(qh_gdn_pre(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, B, c->gdn_heads,
-                          c->gdn_head_dim, c->conv_kernel, m->d_ctl, m->gq, m->gk, m->gv, m->gbeta, m->gg, s));
-            CK(qh_gdn_recurrence(state, m->gq, m->gk, m->gv, m->gbeta, m->gg, B, c->gdn_heads, c->gdn_head_dim,
-                                 m->gout, s));
-            CK(qh_gdn_gated_norm(m->gout, m->z, Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->norm_eps,
-                                 m->gy, s));
-            CK(qh_quantize_q8k(m->gy, kdim, B, m->xq_gdn, s));
+            CK(qh_gdn_fused(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
+                            Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps, m->d_ctl,
+                            m->xq_gdn, s));
         }
         CK(run_plans(m, &Ly->p_out));
-        CK(qh_add(m->h, m->mix, B * H, s));
-        CK(qh_rmsnorm(m->h, Ly->ffn_norm, H, B, c->norm_eps, m->hn, s));
-        CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
+        CK(qh_rmsnorm_q8k(m->h, m->mix, Ly->ffn_norm, H, B, c->norm_eps, m->xq_h, s));
         CK(run_plans(m, &Ly->p_ffn));
-        CK(qh_swiglu(m->fgate, m->fup, m->fact, B * F, s));
-        CK(qh_quantize_q8k(m->fact, F, B, m->xq_ffn, s));
+        CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, s));
         CK(run_plans(m, &Ly->p_down));
-        CK(qh_add(m->h, m->mix, B * H, s));
+        pending = m->mix;
     }
-    CK(qh_rmsnorm(m->h, m->out_norm, H, B, c->norm_eps, m->hn, s));
-    CK(qh_quantize_q8k(m->hn, H, B, m->xq_h, s));
+    CK(qh_rmsnorm_q8k(m->h, pending, m->out_norm, H, B, c->norm_eps, m->xq_h, s));
     CK(run_plans(m, &m->p_head));
-    CK(qh_argmax(m->logits, B, c->vocab, m->d_next, s));
-    CK(qh_feed_next(m->d_next, m->d_prompt, B, c->max_pos, m->d_ctl, m->d_tok, m->d_picks, s));
+    CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
+                      m->d_tok, m->d_picks, s));
     return QH_OK;
 }
 
