@@ -190,6 +190,51 @@ int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, 
                         int *smem_bytes);
 int qh_matvec_plan_destroy(qh_matvec_plan plan);
 
+/* ------------------------------------------------------------------------
+ * Tensor-core matmul for many tokens (prefill, batched decode): the same
+ * results as tensor_matmul_{q4k,q5k,q6k}_f32 (slm/tensor.c:827-853, 898-919,
+ * 1012-1033) with n tokens, computed by tcgen05 int8 MMAs on sm_100a. The
+ * weights are read once per 64-token tile instead of once per token.
+ * Q4_K, Q5_K and Q6_K; other types return QH_ERR_UNSUPPORTED.
+ *
+ * Formats:
+ *   tiled weights  -- the GGUF blocks reordered as [row tile of 128][block]
+ *                     [128 rows][block bytes] (rows past out_f zero):
+ *                     qh_gemm_weight_bytes bytes, written by
+ *                     qh_gemm_pack_weights from the GGUF (k, out_f) blocks.
+ *   tiled Q8_K     -- the reference's quantize_row_q8_K per token
+ *                     (slm/tensor.c:683-720), quants laid out per 64-token
+ *                     tile as the MMA operand, then the fp32 scales
+ *                     [n_tok][ceil4(k/256)] at qh_q8kt_d_offset;
+ *                     qh_q8kt_bytes bytes, written by qh_quantize_q8kt.
+ * ---------------------------------------------------------------------- */
+int64_t qh_gemm_weight_bytes(int type, int64_t k, int64_t out_f);
+int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, void *d_wt, void *stream);
+int64_t qh_q8kt_bytes(int64_t k, int64_t n_tok);
+int64_t qh_q8kt_d_offset(int64_t k, int64_t n_tok);
+int qh_quantize_q8kt(const float *d_x, int64_t k, int64_t n_tok, void *d_q8kt, void *stream);
+
+/* One output of a grouped GEMM: d_out[t * ld_out + j] = row j of the tiled
+ * weights d_wt dotted with token t, for j < out_f, t < n_tok. */
+typedef struct qh_gemm_job {
+    const void *d_wt;
+    int64_t out_f;
+    float *d_out;
+    int64_t ld_out;
+} qh_gemm_job;
+
+/* Up to 8 jobs of one type sharing the tiled activations (k, n_tok) in one
+ * persistent launch. Allocates nothing; asynchronous on `stream`. */
+int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
+            void *stream);
+
+/* One-call form of tensor_matmul_*_f32 for n_tok tokens: packs the weights
+ * and quantizes the activations into d_work (qh_matmul_gemm_workspace_bytes)
+ * and runs qh_gemm. d_out fp32 [n_tok][out_f]. */
+int64_t qh_matmul_gemm_workspace_bytes(int type, int64_t k, int64_t out_f, int64_t n_tok);
+int qh_matmul_gemm(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x, int64_t n_tok,
+                   float *d_out, void *d_work, int64_t work_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -99,17 +99,22 @@ int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int3
  * replace (bit-identical results), fewer launches and HBM round trips.
  * ---------------------------------------------------------------------- */
 
+/* Every fused kernel below that ends in a Q8_K quantization writes xq for
+ * K values x n_tok = B rows in the layout chosen by layout_tile: 0 = the
+ * split layout of qh_backend.h (GEMV input), QH_Q8KT_TILE (64) = the tiled
+ * layout of qh_q8kt_bytes (tensor-core GEMM input). */
+
 /* Optional residual add, RMSNorm and Q8_K quantization in one launch:
- * if d_mix, h += mix (written back); xq = Q8_K(rmsnorm(h) * w) in the split
- * layout of qh_backend.h for K = dim, n_tok = B (qh_add + qh_rmsnorm +
- * qh_quantize_q8k; slm/tensor.c:285, 348-369, 683-720). dim a multiple of
- * 256, at most 4096. */
+ * if d_mix, h += mix (written back); xq = Q8_K(rmsnorm(h) * w)
+ * (qh_add + qh_rmsnorm + qh_quantize_q8k; slm/tensor.c:285, 348-369,
+ * 683-720). dim a multiple of 256, at most 4096. */
 int qh_rmsnorm_q8k(float *d_h, const float *d_mix, const float *d_w, int64_t dim, int32_t B, float eps,
-                   void *d_xq, void *stream);
+                   void *d_xq, int32_t layout_tile, void *stream);
 
 /* xq = Q8_K(silu(gate) * up) for B rows of ffn values (qh_swiglu +
  * qh_quantize_q8k; slm/qwen.c:952-955). */
-int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B, void *d_xq, void *stream);
+int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B, void *d_xq, int32_t layout_tile,
+                  void *stream);
 
 /* The whole Gated DeltaNet mixer between its projections for one token per
  * sequence (slm/qwen.c:357-598): qh_gdn_pre + qh_gdn_recurrence +
@@ -119,7 +124,7 @@ int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B
 int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
                  const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
                  const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
-                 const int32_t *d_pos, void *d_xq, void *stream);
+                 const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream);
 
 /* qh_argmax + qh_feed_next over a grid of CTAs per row (sample_argmax,
  * slm/model.c:401-412). d_scratch holds per-slice partial maxima and ticket

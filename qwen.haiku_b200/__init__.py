@@ -34,6 +34,11 @@ BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34}
 BLOCK_WEIGHTS = {Q4_K: 256, Q5_K: 256, Q6_K: 256, Q8_0: 32}
 
 
+class GemmJob(C.Structure):
+    """qh_gemm_job (include/qh_backend.h)."""
+    _fields_ = [("d_wt", C.c_void_p), ("out_f", C.c_int64), ("d_out", C.c_void_p), ("ld_out", C.c_int64)]
+
+
 class QHError(RuntimeError):
     """A libqh200 call returned a non-zero status."""
 
@@ -83,6 +88,14 @@ SIGNATURES = {
     "qh_matvec_plan_run": (_I, [_P, _P]),
     "qh_matvec_plan_info": (_I, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
     "qh_matvec_plan_destroy": (_I, [_P]),
+    "qh_gemm_weight_bytes": (_I64, [_I, _I64, _I64]),
+    "qh_gemm_pack_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
+    "qh_q8kt_bytes": (_I64, [_I64, _I64]),
+    "qh_q8kt_d_offset": (_I64, [_I64, _I64]),
+    "qh_quantize_q8kt": (_I, [_P, _I64, _I64, _P, _P]),
+    "qh_gemm": (_I, [_I, _P, _I, _I64, _P, _I64, _P]),
+    "qh_matmul_gemm_workspace_bytes": (_I64, [_I, _I64, _I64, _I64]),
+    "qh_matmul_gemm": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_synth_u64": (_U64, [_U64, _U64]),
     "qh_synth_normal": (_I, [_U64, _I64, _F, _F, _P]),
     "qh_synth_blocks": (_I, [_I, _I64, _U64, _P]),
@@ -135,10 +148,10 @@ SIGNATURES.update({  # include/qh_kernels.h
                             _P, _P]),
     "qh_argmax": (_I, [_P, C.c_int32, _I64, _P, _P]),
     "qh_feed_next": (_I, [_P, _P, C.c_int32, C.c_int32, _P, _P, _P, _P]),
-    "qh_rmsnorm_q8k": (_I, [_P, _P, _P, _I64, C.c_int32, C.c_float, _P, _P]),
-    "qh_swiglu_q8k": (_I, [_P, _P, _I64, C.c_int32, _P, _P]),
+    "qh_rmsnorm_q8k": (_I, [_P, _P, _P, _I64, C.c_int32, C.c_float, _P, C.c_int32, _P]),
+    "qh_swiglu_q8k": (_I, [_P, _P, _I64, C.c_int32, _P, C.c_int32, _P]),
     "qh_gdn_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
-                          C.c_float, _P, _P, _P]),
+                          C.c_float, _P, _P, C.c_int32, _P]),
     "qh_argmax_feed_scratch_bytes": (_I64, [C.c_int32, _I64]),
     "qh_argmax_feed": (_I, [_P, C.c_int32, _I64, _P, _P, _P, C.c_int32, _P, _P, _P, _P]),
 })

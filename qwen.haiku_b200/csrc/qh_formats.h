@@ -101,4 +101,19 @@ static inline QH_HD int64_t qhf_q8_0_total_bytes(int64_t k, int64_t n_tok) {
     return qhf_align16(qhf_q8_0_d_offset(k, n_tok) + qhf_q8_0_d_stride(k) * n_tok * 2);
 }
 
+// Q8_K tiled activation layout read by the tensor-core GEMM: the quants of
+// each 64-token tile and 256-value block form one 16 KB operand tile in the
+// no-swizzle K-major layout [16 chunks of 16 values][64 tokens][16 bytes];
+// tokens past n_tok in the last tile are padding. Then the scales as in the
+// split layout. No block sums (the GEMM derives the min terms itself).
+#define QH_Q8KT_TILE 64
+#define QH_Q8KT_BLOCK_BYTES (QH_Q8KT_TILE * QH_QK)
+static inline QH_HD int64_t qhf_q8kt_tiles(int64_t n_tok) { return (n_tok + QH_Q8KT_TILE - 1) / QH_Q8KT_TILE; }
+static inline QH_HD int64_t qhf_q8kt_d_offset(int64_t k, int64_t n_tok) {
+    return qhf_q8kt_tiles(n_tok) * (k / QH_QK) * QH_Q8KT_BLOCK_BYTES;
+}
+static inline QH_HD int64_t qhf_q8kt_total_bytes(int64_t k, int64_t n_tok) {
+    return qhf_align16(qhf_q8kt_d_offset(k, n_tok) + qhf_q8k_d_stride(k) * n_tok * 4);
+}
+
 #endif  // QH_FORMATS_H

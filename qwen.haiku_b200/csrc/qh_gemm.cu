@@ -1,0 +1,572 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_gemm.cu -- K-quant x Q8_K matmul for many tokens on the 5th-generation
+// tensor cores (tcgen05.mma kind::i8, accumulators in TMEM), bit-exact with
+// the reference's per-row dots (simd/quants.h:267-402) and its per-block
+// fp32 combination (the sequential sumf += ... of tensor_matmul_*_f32,
+// slm/tensor.c:827-1033).
+//
+// The integer part of one super-block (256 weights) is an exact integer dot
+// that the tensor core computes, once the weights are expanded in shared
+// memory into int8 "planes" whose dot with the int8 activations gives the
+// reference's integers:
+//   Q4_K / Q5_K: a_p = scale[sb(p)] * w_p  (<= 63 * 31) split as
+//                a_p = 128 * hi_p + lo_p  (hi, lo in [0, 127]); a third plane
+//                holds min[sb(p)], whose dot with the activations is
+//                sum_sb min[sb] * (bsums[2sb] + bsums[2sb+1]) = isum_mins.
+//                isum = 128 * (hi . x) + (lo . x).
+//   Q6_K:        a_p = scale[p/16] * (w_p - 32) split the same way (hi
+//                signed); 128 * (hi . x) + (lo . x) = isum - 32 * isum_mins,
+//                the integer the reference scales.
+// Per super-block the accumulators are read back from TMEM and combined in
+// fp32 exactly as the reference does, in block order.
+//
+// Operands (no-swizzle K-major canonical layout, see qh_tc.cuh):
+//   A  128 weight rows x 256 per plane, built by the CUDA cores from the
+//      raw GGUF blocks;
+//   B  64 tokens x 256 int8 activations, the tiled Q8_K layout
+//      (qh_formats.h) copied as one 16 KB bulk transfer per super-block.
+// Weights are read in the "tiled" order [row tile][block][128 rows][block
+// bytes] (qh_gemm_pack_weights), so one super-block of a row tile is one
+// contiguous bulk copy.
+//
+// CTA: 8 consumer warps (expansion, MMA issue by one thread, epilogue) and
+// 1 producer warp (bulk copies into a 3-stage ring), one CTA per SM,
+// persistent over (row tile, token tile) work items.
+
+#include <cuda_runtime.h>
+#include <stdio.h>
+
+#include <algorithm>
+
+#include "../../include/qh_backend.h"
+#include "qh_common.cuh"
+#include "qh_internal.h"
+#include "qh_q8k.cuh"
+#include "qh_tc.cuh"
+
+namespace qh {
+
+constexpr int kGemmRows = 128;             // MMA M
+constexpr int kGemmTok = QH_Q8KT_TILE;     // MMA N (64)
+constexpr int kGemmThreads = 288;          // 8 consumer warps + 1 producer warp
+constexpr int kGemmConsumers = 256;
+constexpr int kGemmMaxJobs = 8;
+constexpr int kGemmMaxStages = 6;
+constexpr int kPlaneBytes = kGemmRows * QH_QK;  // 32 KB
+constexpr int kXBytes = QH_Q8KT_BLOCK_BYTES;    // 16 KB
+constexpr int kGemmHeader = 1024;
+constexpr int kGemmSmemMax = 232448;            // 227 KB per CTA
+constexpr uint32_t kTmemCols = 256;
+
+struct GemmJob {
+    const uint8_t *wt;  // tiled weights
+    float *out;         // [n_tok][ldo]
+    int32_t n_rows;
+    int32_t m_tiles;
+    int32_t tile_begin;  // first global row tile of this job
+    int32_t ldo;
+};
+
+struct GemmParams {
+    int32_t n_jobs, total_items, nb, n_tok, t_tiles, d_stride, n_stages, stage_bytes;
+    const uint8_t *xq;  // tiled Q8_K quants
+    const float *xd;    // Q8_K scales [n_tok][d_stride]
+    int *err_flag;
+    GemmJob jobs[kGemmMaxJobs];
+};
+
+template <int TYPE>
+struct KQ;
+template <>
+struct KQ<QH_GGUF_Q4_K> {
+    static constexpr int kBytes = QH_Q4K_BYTES, kPlanes = 3;
+};
+template <>
+struct KQ<QH_GGUF_Q5_K> {
+    static constexpr int kBytes = QH_Q5K_BYTES, kPlanes = 3;
+};
+template <>
+struct KQ<QH_GGUF_Q6_K> {
+    static constexpr int kBytes = QH_Q6K_BYTES, kPlanes = 2;
+};
+
+__device__ __forceinline__ void put16(uint8_t *plane, int c, int r, uint32_t a, uint32_t b, uint32_t cc,
+                                      uint32_t d) {
+    *reinterpret_cast<uint4 *>(plane + c * (kGemmRows * 16) + r * 16) = make_uint4(a, b, cc, d);
+}
+
+// Q4_K/Q5_K scale and min of sub-block sb (q4k_get_scale_min,
+// simd/quants.h:215-224).
+__device__ __forceinline__ void scale_min(const uint8_t *s12, int sb, int &sc, int &mn) {
+    if (sb < 4) {
+        sc = s12[sb] & 0x3f;
+        mn = s12[sb + 4] & 0x3f;
+    } else {
+        sc = (s12[sb + 4] & 0x0f) | ((s12[sb - 4] >> 6) << 4);
+        mn = (s12[sb + 4] >> 4) | ((s12[sb] >> 6) << 4);
+    }
+}
+
+// 4 weights (bytes of w, each < 2^9 / scale so products fit 16 bits)
+// times a non-negative scale, split into lo = a & 127 and hi = a >> 7 bytes.
+__device__ __forceinline__ void split_pos(uint32_t w, uint32_t sc, uint32_t &hi, uint32_t &lo) {
+    const uint32_t p02 = (w & 0x00ff00ffu) * sc;
+    const uint32_t p13 = ((w >> 8) & 0x00ff00ffu) * sc;
+    lo = (p02 & 0x007f007fu) | ((p13 & 0x007f007fu) << 8);
+    hi = ((p02 >> 7) & 0x007f007fu) | (((p13 >> 7) & 0x007f007fu) << 8);
+}
+
+// Expansion of half h (weights 128h..128h+127) of row r's super-block.
+template <int TYPE>
+__device__ __forceinline__ void expand(const uint8_t *raw, int h, int r, uint8_t *planes);
+
+template <>
+__device__ __forceinline__ void expand<QH_GGUF_Q4_K>(const uint8_t *raw, int h, int r, uint8_t *planes) {
+    const uint8_t *s12 = raw + 4;
+#pragma unroll
+    for (int cl = 0; cl < 8; ++cl) {
+        const int c = 8 * h + cl, sb = c >> 1;
+        int sc, mn;
+        scale_min(s12, sb, sc, mn);
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + 16 + 32 * (c >> 2) + 16 * (c & 1));
+        const uint32_t sh = 4u * ((c >> 1) & 1);
+        uint32_t hi[4], lo[4];
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) split_pos((qw[k] >> sh) & 0x0f0f0f0fu, static_cast<uint32_t>(sc), hi[k], lo[k]);
+        const uint32_t m4 = static_cast<uint32_t>(mn) * 0x01010101u;
+        put16(planes, c, r, hi[0], hi[1], hi[2], hi[3]);
+        put16(planes + kPlaneBytes, c, r, lo[0], lo[1], lo[2], lo[3]);
+        put16(planes + 2 * kPlaneBytes, c, r, m4, m4, m4, m4);
+    }
+}
+
+template <>
+__device__ __forceinline__ void expand<QH_GGUF_Q5_K>(const uint8_t *raw, int h, int r, uint8_t *planes) {
+    const uint8_t *s12 = raw + 4;
+#pragma unroll
+    for (int cl = 0; cl < 8; ++cl) {
+        const int c = 8 * h + cl, sb = c >> 1;
+        int sc, mn;
+        scale_min(s12, sb, sc, mn);
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + 48 + 32 * (c >> 2) + 16 * (c & 1));
+        const uint4 qh = *reinterpret_cast<const uint4 *>(raw + 16 + 16 * (c & 1));
+        const uint32_t sh = 4u * ((c >> 1) & 1);
+        uint32_t hi[4], lo[4];
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t w = ((qw[k] >> sh) & 0x0f0f0f0fu) | (((hw[k] >> sb) & 0x01010101u) << 4);
+            split_pos(w, static_cast<uint32_t>(sc), hi[k], lo[k]);
+        }
+        const uint32_t m4 = static_cast<uint32_t>(mn) * 0x01010101u;
+        put16(planes, c, r, hi[0], hi[1], hi[2], hi[3]);
+        put16(planes + kPlaneBytes, c, r, lo[0], lo[1], lo[2], lo[3]);
+        put16(planes + 2 * kPlaneBytes, c, r, m4, m4, m4, m4);
+    }
+}
+
+// Q6_K: a = sc * (w - 32), computed as u = a + 4096 in non-negative 16-bit
+// lanes (no carries or borrows cross lanes for |sc| <= 128, w <= 63); then
+// lo = u & 127 and hi = (u >> 7) - 32 = floor(a / 128).
+template <>
+__device__ __forceinline__ void expand<QH_GGUF_Q6_K>(const uint8_t *raw, int h, int r, uint8_t *planes) {
+#pragma unroll
+    for (int cl = 0; cl < 8; ++cl) {
+        const int c = 8 * h + cl, rq = (c >> 1) & 3, l0 = 16 * (c & 1);
+        const uint4 ql = lds128_a2(raw + 64 * h + 32 * (rq & 1) + l0);
+        const uint4 qh = lds128_a2(raw + 128 + 32 * h + l0);
+        const int sc = static_cast<int8_t>(raw[192 + c]);
+        const uint32_t lsh = 4u * static_cast<uint32_t>(rq >> 1), hsh = 2u * static_cast<uint32_t>(rq);
+        const uint32_t a = static_cast<uint32_t>(sc < 0 ? -sc : sc);
+        const uint32_t cst = static_cast<uint32_t>(sc < 0 ? 4096 + 32 * (-sc) : 4096 - 32 * sc);
+        const uint32_t c2 = cst | (cst << 16);
+        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
+        const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t w = ((lw[k] >> lsh) & 0x0f0f0f0fu) | (((hw[k] >> hsh) & 0x03030303u) << 4);
+            const uint32_t w02 = (w & 0x00ff00ffu) * a, w13 = ((w >> 8) & 0x00ff00ffu) * a;
+            const uint32_t u02 = sc < 0 ? c2 - w02 : c2 + w02;
+            const uint32_t u13 = sc < 0 ? c2 - w13 : c2 + w13;
+            lo[k] = (u02 & 0x007f007fu) | ((u13 & 0x007f007fu) << 8);
+            const uint32_t hu = ((u02 >> 7) & 0x007f007fu) | (((u13 >> 7) & 0x007f007fu) << 8);
+            hi[k] = __vsub4(hu, 0x20202020u);
+        }
+        put16(planes, c, r, hi[0], hi[1], hi[2], hi[3]);
+        put16(planes + kPlaneBytes, c, r, lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+__device__ __forceinline__ void decode_item(const GemmParams &p, int item, GemmJob &job, int &mt, int &tt) {
+    const int g = item / p.t_tiles;
+    tt = item - g * p.t_tiles;
+    int j = 0;
+    while (j + 1 < p.n_jobs && g >= p.jobs[j + 1].tile_begin) ++j;
+    job = p.jobs[j];
+    mt = g - job.tile_begin;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+    constexpr int BB = KQ<TYPE>::kBytes, P = KQ<TYPE>::kPlanes;
+    constexpr int WB = kGemmRows * BB;  // weight bytes of one row tile's super-block
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kGemmMaxStages;
+    uint64_t *mma_bar = empty + kGemmMaxStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 256);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 260);
+    uint8_t *planes = smem + kGemmHeader;
+    uint8_t *stages = planes + P * kPlaneBytes;
+
+    const int S = p.n_stages;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_launch_dependents();
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(mma_bar, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    // Earlier kernels on the stream finish (and free their TMEM) first.
+    pdl_wait();
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kGemmConsumers / 32) {
+        // ----- producer: one thread streams (weights, activations) per super-block -----
+        if (lane == 0) {
+            int i = 0;
+            bool stop = false;
+            for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
+                GemmJob job;
+                int mt, tt;
+                decode_item(p, item, job, mt, tt);
+                const uint8_t *wsrc = job.wt + static_cast<int64_t>(mt) * p.nb * WB;
+                const uint8_t *xsrc = p.xq + static_cast<int64_t>(tt) * p.nb * kXBytes;
+                for (int b = 0; b < p.nb; ++b, ++i) {
+                    const int s = i % S;
+                    const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+                    if (*abort_flag || (i >= S && !mbar_wait(&empty[s], ph ^ 1u))) {
+                        report_error(p.err_flag, kDevWaitTimeout);
+                        *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    uint8_t *dst = stages + static_cast<int64_t>(s) * p.stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], WB + kXBytes);
+                    bulk_copy_g2s(dst, wsrc + static_cast<int64_t>(b) * WB, WB, &full[s]);
+                    bulk_copy_g2s(dst + WB, xsrc + static_cast<int64_t>(b) * kXBytes, kXBytes, &full[s]);
+                }
+            }
+            // Drain: no copy of this CTA stays in flight past its exit.
+            for (int j = max(0, i - S); j < i; ++j)
+                if (!mbar_wait(&full[j % S], static_cast<uint32_t>(j / S) & 1u)) report_error(p.err_flag, kDevWaitTimeout);
+        }
+    } else {
+        // ----- consumers -----
+        const int r = tid >> 1, h = tid & 1;             // expansion: row, half
+        const int er = 32 * (warp & 3) + lane;           // epilogue: row (TMEM lane)
+        const int eh = warp >> 2;                        // epilogue: token half
+        const uint32_t tcol = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + 32u * eh;
+        constexpr uint32_t idesc = tc::idesc_i8(kGemmRows, kGemmTok);
+        uint32_t mma_phase = 0;
+        int i = 0;
+        bool aborted = false;
+        for (int item = blockIdx.x; item < p.total_items && !aborted; item += gridDim.x) {
+            GemmJob job;
+            int mt, tt;
+            decode_item(p, item, job, mt, tt);
+            float acc[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+            const int t0 = tt * kGemmTok + 32 * eh;
+            for (int b = 0; b < p.nb; ++b, ++i) {
+                const int s = i % S;
+                const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+                const bool ok = mbar_wait(&full[s], ph);
+                const uint8_t *wst = stages + static_cast<int64_t>(s) * p.stage_bytes;
+                float dw = 0.0f, dmw = 0.0f;
+                if (ok) {
+                    expand<TYPE>(wst + r * BB, h, r, planes);
+                    const uint8_t *er_raw = wst + er * BB;
+                    if (TYPE == QH_GGUF_Q6_K) {
+                        dw = h2f_bits(static_cast<uint32_t>(er_raw[208]) | (static_cast<uint32_t>(er_raw[209]) << 8));
+                    } else {
+                        const uint32_t dd = *reinterpret_cast<const uint32_t *>(er_raw);
+                        dw = h2f_bits(dd);
+                        dmw = h2f_bits(dd >> 16);
+                    }
+                }
+                tc::fence_proxy_async_smem();
+                if (bar_any(1, kGemmConsumers, !ok)) {
+                    aborted = true;
+                    break;
+                }
+                if (tid == 0) {
+                    tc::fence_after_sync();
+                    const uint32_t a0 = smem_addr(planes), b0 = smem_addr(wst + WB);
+#pragma unroll
+                    for (int pl = 0; pl < P; ++pl)
+#pragma unroll
+                        for (int ks = 0; ks < QH_QK / 32; ++ks) {
+                            const uint64_t ad = tc::smem_desc(a0 + pl * kPlaneBytes + ks * 2 * (kGemmRows * 16),
+                                                              kGemmRows * 16, 128);
+                            const uint64_t bd = tc::smem_desc(b0 + ks * 2 * (kGemmTok * 16), kGemmTok * 16, 128);
+                            tc::mma_i8(tmem + pl * kGemmTok, ad, bd, idesc, ks > 0);
+                        }
+                    tc::commit(mma_bar);
+                    tc::commit(&empty[s]);
+                }
+                const bool ok2 = mbar_wait(mma_bar, mma_phase);
+                mma_phase ^= 1u;
+                if (bar_any(2, kGemmConsumers, !ok2)) {
+                    aborted = true;
+                    break;
+                }
+                tc::fence_after_sync();
+                uint32_t vhi[32], vlo[32], vmn[32];
+                tc::ld_32x32b_x32(tcol, vhi);
+                tc::ld_32x32b_x32(tcol + kGemmTok, vlo);
+                if (P == 3) tc::ld_32x32b_x32(tcol + 2 * kGemmTok, vmn);
+                tc::wait_ld();
+                tc::fence_before_sync();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + j;
+                    if (t < p.n_tok) {
+                        const float yd = __ldg(p.xd + static_cast<int64_t>(t) * p.d_stride + b);
+                        const int isum = static_cast<int>(vhi[j]) * 128 + static_cast<int>(vlo[j]);
+                        float term;
+                        if (TYPE == QH_GGUF_Q6_K) {
+                            term = __fmul_rn(__fmul_rn(dw, yd), __int2float_rn(isum));
+                        } else {
+                            const float d = __fmul_rn(yd, dw), dm = __fmul_rn(yd, dmw);
+                            term = __fsub_rn(__fmul_rn(d, __int2float_rn(isum)),
+                                             __fmul_rn(dm, __int2float_rn(static_cast<int>(vmn[j]))));
+                        }
+                        acc[j] = __fadd_rn(acc[j], term);
+                    }
+                }
+            }
+            if (aborted) break;
+            const int n = mt * kGemmRows + er;
+            if (n < job.n_rows) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (t0 + j < p.n_tok) job.out[static_cast<int64_t>(t0 + j) * job.ldo + n] = acc[j];
+            }
+        }
+        if (aborted && tid == 0) {
+            report_error(p.err_flag, kDevWaitTimeout);
+            *abort_flag = 1;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Weight repacking: GGUF rows -> [row tile][block][128 rows][block bytes],
+// rows past n_rows zero. CTA (row tile, block), one thread per row.
+__global__ void pack_tiles_kernel(const uint8_t *__restrict__ w, int64_t n_rows, int nb, int bb,
+                                  uint8_t *__restrict__ wt) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t mt = blockIdx.x;
+    const int b = blockIdx.y, r = threadIdx.x;
+    const int64_t row = mt * kGemmRows + r;
+    uint16_t *dst = reinterpret_cast<uint16_t *>(wt + ((mt * nb + b) * kGemmRows + r) * bb);
+    if (row < n_rows) {
+        const uint16_t *src = reinterpret_cast<const uint16_t *>(w + row * nb * bb + static_cast<int64_t>(b) * bb);
+        for (int i = 0; i < bb / 2; ++i) dst[i] = src[i];
+    } else {
+        for (int i = 0; i < bb / 2; ++i) dst[i] = 0;
+    }
+}
+
+// Q8_K quantization into the tiled layout: CTA (block, token).
+__global__ void __launch_bounds__(256) quantize_q8kt_kernel(const float *__restrict__ x, int k, int n_tok,
+                                                            uint8_t *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ Q8KScratch sc;
+    const int b = blockIdx.x, t = blockIdx.y;
+    const float v = x[static_cast<int64_t>(t) * k + b * QH_QK + threadIdx.x];
+    q8k_block256(v, sc, q8k_row(out, k, n_tok, t, QH_Q8KT_TILE), b);
+}
+
+template <int TYPE>
+static cudaError_t gemm_launch_t(const GemmParams &p0, int sm_count, cudaStream_t stream) {
+    constexpr int WB = kGemmRows * KQ<TYPE>::kBytes, P = KQ<TYPE>::kPlanes;
+    GemmParams p = p0;
+    p.stage_bytes = WB + kXBytes;
+    const int avail = kGemmSmemMax - kGemmHeader - P * kPlaneBytes;
+    p.n_stages = std::min(kGemmMaxStages, avail / p.stage_bytes);
+    if (p.n_stages < 2) return cudaErrorInvalidValue;
+    const int smem = kGemmHeader + P * kPlaneBytes + p.n_stages * p.stage_bytes;
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kGemmSmemMax);
+        if (e != cudaSuccess) return e;
+        attr_done[dev] = true;
+    }
+    const int grid = std::min(p.total_items, sm_count);
+    return launch_pdl(gemm_kernel<TYPE>, dim3(grid), dim3(kGemmThreads), smem, stream, p);
+}
+
+}  // namespace qh
+
+// ---------------------------------------------------------------------------
+// C-ABI
+// ---------------------------------------------------------------------------
+namespace {
+int gfail(int code, const char *msg) {
+    qh::set_last_error_message(msg);
+    return code;
+}
+int gcuda(cudaError_t e, const char *what) {
+    char msg[256];
+    snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(e));
+    qh::set_last_error_message(msg);
+    return QH_ERR_CUDA;
+}
+bool gemm_type_ok(int type) { return type == QH_TYPE_Q4_K || type == QH_TYPE_Q5_K || type == QH_TYPE_Q6_K; }
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+extern "C" {
+
+int64_t qh_gemm_weight_bytes(int type, int64_t k, int64_t out_f) {
+    if (!gemm_type_ok(type) || k <= 0 || k % 256 || out_f <= 0) return -1;
+    return ((out_f + qh::kGemmRows - 1) / qh::kGemmRows) * qh::kGemmRows * qhf_row_bytes(type, k);
+}
+
+int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, void *d_wt, void *stream) {
+    if (!gemm_type_ok(type)) return gfail(QH_ERR_UNSUPPORTED, "gemm_pack_weights: type must be Q4_K, Q5_K or Q6_K");
+    if (!d_w || !d_wt || k <= 0 || k % 256 || out_f <= 0 || k / 256 > 65535 || out_f > 0x7fffffffll)
+        return gfail(QH_ERR_INVALID, "gemm_pack_weights: bad arguments");
+    if ((reinterpret_cast<uintptr_t>(d_w) & 1u) || !al16(d_wt))
+        return gfail(QH_ERR_ALIGN, "gemm_pack_weights: misaligned pointer");
+    const int64_t mt = (out_f + qh::kGemmRows - 1) / qh::kGemmRows;
+    cudaError_t e = qh::launch_pdl(qh::pack_tiles_kernel, dim3(static_cast<unsigned>(mt), static_cast<unsigned>(k / 256)),
+                                   dim3(qh::kGemmRows), 0, static_cast<cudaStream_t>(stream),
+                                   static_cast<const uint8_t *>(d_w), out_f, static_cast<int>(k / 256),
+                                   static_cast<int>(qhf_block_bytes(type)), static_cast<uint8_t *>(d_wt));
+    if (e != cudaSuccess) return gcuda(e, "gemm_pack_weights launch");
+    return QH_OK;
+}
+
+int64_t qh_q8kt_bytes(int64_t k, int64_t n_tok) {
+    if (k <= 0 || k % 256 || n_tok <= 0) return -1;
+    return qhf_q8kt_total_bytes(k, n_tok);
+}
+int64_t qh_q8kt_d_offset(int64_t k, int64_t n_tok) {
+    if (k <= 0 || k % 256 || n_tok <= 0) return -1;
+    return qhf_q8kt_d_offset(k, n_tok);
+}
+
+int qh_quantize_q8kt(const float *d_x, int64_t k, int64_t n_tok, void *d_q8kt, void *stream) {
+    if (!d_x || !d_q8kt || k <= 0 || k % 256 || k / 256 > 65535 || n_tok <= 0 || n_tok > 65535)
+        return gfail(QH_ERR_INVALID, "quantize_q8kt: bad arguments");
+    if (!al16(d_q8kt)) return gfail(QH_ERR_ALIGN, "quantize_q8kt: output not 16-byte aligned");
+    cudaError_t e = qh::launch_pdl(qh::quantize_q8kt_kernel, dim3(static_cast<unsigned>(k / 256), static_cast<unsigned>(n_tok)),
+                                   dim3(256), 0, static_cast<cudaStream_t>(stream), d_x, static_cast<int>(k),
+                                   static_cast<int>(n_tok), static_cast<uint8_t *>(d_q8kt));
+    if (e != cudaSuccess) return gcuda(e, "quantize_q8kt launch");
+    return QH_OK;
+}
+
+int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
+            void *stream) {
+    if (!gemm_type_ok(type)) return gfail(QH_ERR_UNSUPPORTED, "gemm: type must be Q4_K, Q5_K or Q6_K");
+    if (!jobs || n_jobs <= 0 || n_jobs > qh::kGemmMaxJobs || !d_q8kt || k <= 0 || k % 256 || n_tok <= 0 ||
+        n_tok > 65535)
+        return gfail(QH_ERR_INVALID, "gemm: bad arguments");
+    if (!al16(d_q8kt)) return gfail(QH_ERR_ALIGN, "gemm: activations not 16-byte aligned");
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return gcuda(e, "gemm: device query");
+    qh::GemmParams p = {};
+    p.n_jobs = n_jobs;
+    p.nb = static_cast<int32_t>(k / 256);
+    p.n_tok = static_cast<int32_t>(n_tok);
+    p.t_tiles = static_cast<int32_t>(qhf_q8kt_tiles(n_tok));
+    p.d_stride = static_cast<int32_t>(qhf_q8k_d_stride(k));
+    p.xq = static_cast<const uint8_t *>(d_q8kt);
+    p.xd = reinterpret_cast<const float *>(static_cast<const uint8_t *>(d_q8kt) + qhf_q8kt_d_offset(k, n_tok));
+    p.err_flag = qh::device_error_word();
+    if (!p.err_flag) return gfail(QH_ERR_CUDA, "gemm: no device error word");
+    int64_t tiles = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+        const qh_gemm_job &jb = jobs[j];
+        if (!jb.d_wt || !jb.d_out || jb.out_f <= 0 || jb.out_f > 0x7fffffffll || jb.ld_out < jb.out_f ||
+            jb.ld_out > 0x7fffffffll)
+            return gfail(QH_ERR_INVALID, "gemm: bad job");
+        if (!al16(jb.d_wt)) return gfail(QH_ERR_ALIGN, "gemm: weights not 16-byte aligned");
+        qh::GemmJob g;
+        g.wt = static_cast<const uint8_t *>(jb.d_wt);
+        g.out = jb.d_out;
+        g.n_rows = static_cast<int32_t>(jb.out_f);
+        g.m_tiles = static_cast<int32_t>((jb.out_f + qh::kGemmRows - 1) / qh::kGemmRows);
+        g.tile_begin = static_cast<int32_t>(tiles);
+        g.ldo = static_cast<int32_t>(jb.ld_out);
+        tiles += g.m_tiles;
+        p.jobs[j] = g;
+    }
+    if (tiles * p.t_tiles > 0x7fffffffll) return gfail(QH_ERR_INVALID, "gemm: too many tiles");
+    p.total_items = static_cast<int32_t>(tiles * p.t_tiles);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (type) {
+        case QH_TYPE_Q4_K: e = qh::gemm_launch_t<QH_GGUF_Q4_K>(p, sms, s); break;
+        case QH_TYPE_Q5_K: e = qh::gemm_launch_t<QH_GGUF_Q5_K>(p, sms, s); break;
+        default: e = qh::gemm_launch_t<QH_GGUF_Q6_K>(p, sms, s); break;
+    }
+    if (e != cudaSuccess) return gcuda(e, "gemm launch");
+    return QH_OK;
+}
+
+int64_t qh_matmul_gemm_workspace_bytes(int type, int64_t k, int64_t out_f, int64_t n_tok) {
+    const int64_t w = qh_gemm_weight_bytes(type, k, out_f), x = qh_q8kt_bytes(k, n_tok);
+    if (w < 0 || x < 0) return -1;
+    return qhf_align16(w) + x;
+}
+
+int qh_matmul_gemm(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x, int64_t n_tok,
+                   float *d_out, void *d_work, int64_t work_bytes, void *stream) {
+    const int64_t need = qh_matmul_gemm_workspace_bytes(type, k, out_f, n_tok);
+    if (need < 0) return gemm_type_ok(type) ? gfail(QH_ERR_INVALID, "matmul_gemm: bad shape")
+                                            : gfail(QH_ERR_UNSUPPORTED, "matmul_gemm: type must be Q4_K, Q5_K or Q6_K");
+    if (!d_work || work_bytes < need) return gfail(QH_ERR_WORKSPACE, "matmul_gemm: workspace too small");
+    if (!al16(d_work)) return gfail(QH_ERR_ALIGN, "matmul_gemm: workspace not 16-byte aligned");
+    uint8_t *wt = static_cast<uint8_t *>(d_work);
+    uint8_t *xq = wt + qhf_align16(qh_gemm_weight_bytes(type, k, out_f));
+    int rc = qh_gemm_pack_weights(type, d_w, k, out_f, wt, stream);
+    if (rc) return rc;
+    rc = qh_quantize_q8kt(d_x, k, n_tok, xq, stream);
+    if (rc) return rc;
+    qh_gemm_job job = {wt, out_f, d_out, out_f};
+    return qh_gemm(type, &job, 1, k, xq, n_tok, stream);
+}
+
+}  // extern "C"

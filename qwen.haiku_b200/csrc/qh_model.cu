@@ -28,6 +28,7 @@
 #include "../../include/qh_kernels.h"
 #include "qh_common.cuh"
 #include "qh_internal.h"
+#include "qh_q8k.cuh"
 
 namespace qh {
 
@@ -524,91 +525,13 @@ int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int3
 // ===========================================================================
 namespace qh {
 
-// Candidate for the Q8_K block maximum: |x| (NaN never wins), its index in
-// the block and its signed value; ties go to the smaller index, as the
-// reference's first-strictly-greater scan does.
-__device__ __forceinline__ void best_merge(float &a, int &i, float &v, float oa, int oi, float ov) {
-    if (oa > a || (oa == a && oi < i)) { a = oa; i = oi; v = ov; }
-}
-
-__device__ __forceinline__ void warp_best(float &a, int &i, float &v) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const float oa = __shfl_xor_sync(0xffffffffu, a, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, i, off);
-        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
-        best_merge(a, i, v, oa, oi, ov);
-    }
-}
-
-// q = clamp(round_half_even(iscale * v)) through the 1.5*2^23 bias, as
-// quantize_q8k_kernel does (slm/tensor.c:673-678, 683-720).
-__device__ __forceinline__ int q8k_value(float v, float iscale) {
-    const float f = __fmul_rn(iscale, v);
-    const float biased = __fadd_rn(f, 12582912.0f);
-    int q = (__float_as_int(biased) & 0x007fffff) - 0x00400000;
-    if (f != f) q = 0;
-    return q > 127 ? 127 : (q < -128 ? -128 : q);
-}
-
-// Pointers into the split Q8_K layout (qh_formats.h) of row `tok`.
-struct Q8KRow {
-    int8_t *qs;
-    float *d;
-    int16_t *bs;
-};
-__device__ __forceinline__ Q8KRow q8k_row(uint8_t *base, int64_t k, int64_t n_tok, int64_t tok) {
-    Q8KRow r;
-    r.qs = reinterpret_cast<int8_t *>(base) + tok * k;
-    r.d = reinterpret_cast<float *>(base + qhf_q8k_d_offset(k, n_tok)) + tok * qhf_q8k_d_stride(k);
-    r.bs = reinterpret_cast<int16_t *>(base + qhf_q8k_bsums_offset(k, n_tok)) + tok * (k / QH_QK) * 16;
-    return r;
-}
-
-struct Q8KScratch {
-    float a[8], v[8];
-    int i[8];
-};
-
-// Q8_K quantization of one 256-value block held one value per thread by a
-// 256-thread CTA (thread t holds element t). qs/bs point at the block's
-// 256 quants / 16 group sums, d at its scale. Ends with a barrier, so the
-// scratch can be reused by the next block.
-__device__ void q8k_block256(float v, Q8KScratch &sc, int8_t *qs, float *d, int16_t *bs) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float a = (v == v) ? fabsf(v) : -1.0f, bv = v;
-    int bi = tid;
-    warp_best(a, bi, bv);
-    if (lane == 0) { sc.a[warp] = a; sc.i[warp] = bi; sc.v[warp] = bv; }
-    __syncthreads();
-    float ba = sc.a[0], xv = sc.v[0];
-    int ii = sc.i[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) best_merge(ba, ii, xv, sc.a[w], sc.i[w], sc.v[w]);
-    const float xmax = ba > 0.0f ? xv : 0.0f;
-    int q = 0;
-    if (xmax != 0.0f) {
-        const float iscale = __fdiv_rn(-127.0f, xmax);
-        q = q8k_value(v, iscale);
-        if (tid == 0) *d = __fdiv_rn(1.0f, iscale);
-    } else if (tid == 0) {
-        *d = 0.0f;
-    }
-    qs[tid] = static_cast<int8_t>(q);
-    int s = q;
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if ((lane & 15) == 0) bs[warp * 2 + (lane >> 4)] = static_cast<int16_t>(s);
-    __syncthreads();
-}
-
 // (optional residual add) + RMSNorm + Q8_K: one 256-thread CTA per row.
 // Same sums as add_kernel, rmsnorm_kernel (256 threads) and
 // quantize_q8k_kernel in sequence.
 constexpr int kResNormMaxBlocks = 16;
 __global__ void __launch_bounds__(256) resnorm_q8k_kernel(float *__restrict__ h, const float *__restrict__ mix,
                                                           const float *__restrict__ w, int dim, float eps,
-                                                          uint8_t *__restrict__ xq, int n_tok) {
+                                                          uint8_t *__restrict__ xq, int n_tok, int tile) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ double scratch[32];
@@ -632,27 +555,27 @@ __global__ void __launch_bounds__(256) resnorm_q8k_kernel(float *__restrict__ h,
     const double ssq = block_sum_d(s, scratch);
     const float rscale =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(dim)), eps)));
-    const Q8KRow r = q8k_row(xq, dim, n_tok, row);
+    const Q8KRow r = q8k_row(xq, dim, n_tok, row, tile);
 #pragma unroll
     for (int j = 0; j < kResNormMaxBlocks; ++j) {
         if (j < nb) {
             const float y = __fmul_rn(__fmul_rn(v[j], rscale), w[j * QH_QK + tid]);
-            q8k_block256(y, sc, r.qs + j * QH_QK, r.d + j, r.bs + j * 16);
+            q8k_block256(y, sc, r, j);
         }
     }
 }
 
 // SwiGLU + Q8_K: CTA (block, row), 256 threads.
 __global__ void __launch_bounds__(256) swiglu_q8k_kernel(const float *__restrict__ g, const float *__restrict__ u,
-                                                         int ffn, uint8_t *__restrict__ xq, int n_tok) {
+                                                         int ffn, uint8_t *__restrict__ xq, int n_tok, int tile) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ Q8KScratch sc;
     const int blk = blockIdx.x, row = blockIdx.y, tid = threadIdx.x;
     const int64_t i = static_cast<int64_t>(row) * ffn + blk * QH_QK + tid;
     const float v = __fmul_rn(silu_f(g[i]), u[i]);
-    const Q8KRow r = q8k_row(xq, ffn, n_tok, row);
-    q8k_block256(v, sc, r.qs + blk * QH_QK, r.d + blk, r.bs + blk * 16);
+    const Q8KRow r = q8k_row(xq, ffn, n_tok, row, tile);
+    q8k_block256(v, sc, r, blk);
 }
 
 // Whole Gated DeltaNet head for one token: CTA (sequence, head) of HD
@@ -667,7 +590,7 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
                      const float *__restrict__ bb, const float *__restrict__ aa, const float *__restrict__ dt_bias,
                      const float *__restrict__ ssm_a, float *__restrict__ state, const float *__restrict__ z,
                      const float *__restrict__ norm_w, int heads, int kk, float eps,
-                     const int32_t *__restrict__ pos_ptr, uint8_t *__restrict__ xq, int n_tok) {
+                     const int32_t *__restrict__ pos_ptr, uint8_t *__restrict__ xq, int n_tok, int tile) {
     static_assert(HD == 128, "a cluster pair of heads must form one 256-value Q8_K block");
     pdl_launch_dependents();
     pdl_wait();
@@ -764,7 +687,7 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     }
     cluster.sync();  // the partner has read this CTA's candidate
     const float xmax = ba > 0.0f ? xv : 0.0f;
-    const Q8KRow r = q8k_row(xq, kdim, n_tok, b);
+    const Q8KRow r = q8k_row(xq, kdim, n_tok, b, tile);
     const int blk = h >> 1;
     int q = 0;
     if (xmax != 0.0f) {
@@ -774,11 +697,14 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     } else if (half == 0 && t == 0) {
         r.d[blk] = 0.0f;
     }
-    r.qs[blk * QH_QK + half * HD + t] = static_cast<int8_t>(q);
-    int sum = q;
+    *q8k_elem(r, blk, half * HD + t) = static_cast<int8_t>(q);
+    if (r.bs) {
+        int sum = q;
 #pragma unroll
-    for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if ((lane & 15) == 0) r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+        for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if ((lane & 15) == 0)
+            r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+    }
 }
 
 // Greedy pick + device-side feed (argmax_kernel + feed_next_kernel) over a
@@ -855,31 +781,36 @@ __global__ void __launch_bounds__(kArgmaxThreads)
 // ---------------------------------------------------------------------------
 extern "C" {
 
+static bool tile_ok(int32_t t) { return t == 0 || t == QH_Q8KT_TILE; }
+
 int qh_rmsnorm_q8k(float *d_h, const float *d_mix, const float *d_w, int64_t dim, int32_t B, float eps,
-                   void *d_xq, void *stream) {
-    if (!d_h || !d_w || !d_xq || dim <= 0 || dim % QH_QK || dim > qh::kResNormMaxBlocks * QH_QK || B <= 0)
+                   void *d_xq, int32_t layout_tile, void *stream) {
+    if (!d_h || !d_w || !d_xq || dim <= 0 || dim % QH_QK || dim > qh::kResNormMaxBlocks * QH_QK || B <= 0 ||
+        !tile_ok(layout_tile))
         return bad("qh_rmsnorm_q8k: bad arguments");
     const cudaError_t le = qh::launch_pdl(qh::resnorm_q8k_kernel, dim3(static_cast<unsigned>(B)), dim3(256), 0,
                                           static_cast<cudaStream_t>(stream), d_h, d_mix, d_w,
-                                          static_cast<int>(dim), eps, static_cast<uint8_t *>(d_xq), B);
+                                          static_cast<int>(dim), eps, static_cast<uint8_t *>(d_xq), B,
+                                          layout_tile);
     return launch_status(le, "qh_rmsnorm_q8k");
 }
 
-int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B, void *d_xq, void *stream) {
-    if (!d_gate || !d_up || !d_xq || ffn <= 0 || ffn % QH_QK || B <= 0 || B > 65535)
+int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B, void *d_xq, int32_t layout_tile,
+                  void *stream) {
+    if (!d_gate || !d_up || !d_xq || ffn <= 0 || ffn % QH_QK || B <= 0 || B > 65535 || !tile_ok(layout_tile))
         return bad("qh_swiglu_q8k: bad arguments");
     const cudaError_t le = qh::launch_pdl(qh::swiglu_q8k_kernel, dim3(static_cast<unsigned>(ffn / QH_QK), B),
                                           dim3(256), 0, static_cast<cudaStream_t>(stream), d_gate, d_up,
-                                          static_cast<int>(ffn), static_cast<uint8_t *>(d_xq), B);
+                                          static_cast<int>(ffn), static_cast<uint8_t *>(d_xq), B, layout_tile);
     return launch_status(le, "qh_swiglu_q8k");
 }
 
 int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
                  const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
                  const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
-                 const int32_t *d_pos, void *d_xq, void *stream) {
+                 const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream) {
     if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_state || !d_z ||
-        !d_norm_w || !d_pos || !d_xq || B <= 0 || heads <= 0 || heads % 2 || kk <= 0)
+        !d_norm_w || !d_pos || !d_xq || B <= 0 || heads <= 0 || heads % 2 || kk <= 0 || !tile_ok(layout_tile))
         return bad("qh_gdn_fused: bad arguments");
     if (hd != 128) {
         qh::set_last_error_message("qh_gdn_fused: head dim must be 128");
@@ -888,7 +819,7 @@ int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const
     const cudaError_t le = qh::launch_pdl(qh::gdn_fused_kernel<128>, dim3(static_cast<unsigned>(B), heads),
                                           dim3(128), 0, static_cast<cudaStream_t>(stream), d_qkv, d_ring,
                                           d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, heads,
-                                          kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B);
+                                          kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B, layout_tile);
     return launch_status(le, "qh_gdn_fused");
 }
 

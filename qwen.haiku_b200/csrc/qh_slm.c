@@ -391,7 +391,7 @@ static int forward(qh_slm *m) {
     const float *pending = NULL;  // residual branch output not yet added to h
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        CK(qh_rmsnorm_q8k(m->h, pending, Ly->attn_norm, H, B, c->norm_eps, m->xq_h, s));
+        CK(qh_rmsnorm_q8k(m->h, pending, Ly->attn_norm, H, B, c->norm_eps, m->xq_h, 0, s));
         CK(run_plans(m, &Ly->p_in));
         if (Ly->is_attn) {
             const int64_t ai = Ly->attn_index;
@@ -409,16 +409,16 @@ static int forward(qh_slm *m) {
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
             CK(qh_gdn_fused(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
                             Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps, m->d_ctl,
-                            m->xq_gdn, s));
+                            m->xq_gdn, 0, s));
         }
         CK(run_plans(m, &Ly->p_out));
-        CK(qh_rmsnorm_q8k(m->h, m->mix, Ly->ffn_norm, H, B, c->norm_eps, m->xq_h, s));
+        CK(qh_rmsnorm_q8k(m->h, m->mix, Ly->ffn_norm, H, B, c->norm_eps, m->xq_h, 0, s));
         CK(run_plans(m, &Ly->p_ffn));
-        CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, s));
+        CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, 0, s));
         CK(run_plans(m, &Ly->p_down));
         pending = m->mix;
     }
-    CK(qh_rmsnorm_q8k(m->h, pending, m->out_norm, H, B, c->norm_eps, m->xq_h, s));
+    CK(qh_rmsnorm_q8k(m->h, pending, m->out_norm, H, B, c->norm_eps, m->xq_h, 0, s));
     CK(run_plans(m, &m->p_head));
     CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
                       m->d_tok, m->d_picks, s));

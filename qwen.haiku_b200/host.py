@@ -121,6 +121,44 @@ def matmul(gtype: int, w, k: int, out_f: int, x, n_tok: int = None, out=None, wo
     return out
 
 
+def matmul_gemm(gtype: int, w, k: int, out_f: int, x, n_tok: int = None, out=None):
+    """Tensor-core path of matmul (qh_matmul_gemm): same results, many tokens."""
+    torch = _torch()
+    if n_tok is None:
+        n_tok = x.numel() // k
+    if out is None:
+        out = torch.empty((n_tok, out_f), dtype=torch.float32, device="cuda")
+    need = int(lib().qh_matmul_gemm_workspace_bytes(gtype, k, out_f, n_tok))
+    if need < 0:
+        raise QHError(-2, "matmul_gemm", f"unsupported type {gtype} or shape")
+    work = torch.empty(need, dtype=torch.uint8, device="cuda")
+    check(lib().qh_matmul_gemm(gtype, dptr(w), k, out_f, dptr(x), n_tok, dptr(out), dptr(work), need, None),
+          "qh_matmul_gemm")
+    return out
+
+
+def gemm_pack(gtype: int, w, k: int, out_f: int):
+    """qh_gemm_pack_weights into a fresh device buffer."""
+    torch = _torch()
+    wt = torch.empty(int(lib().qh_gemm_weight_bytes(gtype, k, out_f)), dtype=torch.uint8, device="cuda")
+    check(lib().qh_gemm_pack_weights(gtype, dptr(w), k, out_f, dptr(wt), None), "qh_gemm_pack_weights")
+    return wt
+
+
+def quantize_q8kt(x, k: int, n_tok: int):
+    torch = _torch()
+    buf = torch.empty(int(lib().qh_q8kt_bytes(k, n_tok)), dtype=torch.uint8, device="cuda")
+    check(lib().qh_quantize_q8kt(dptr(x), k, n_tok, dptr(buf), None), "qh_quantize_q8kt")
+    return buf
+
+
+def gemm(gtype: int, jobs, k: int, xq, n_tok: int):
+    """qh_gemm over jobs [(wt, out_f, out, ld_out)] sharing tiled activations xq."""
+    from . import GemmJob
+    arr = (GemmJob * len(jobs))(*[GemmJob(wt.data_ptr(), out_f, out.data_ptr(), ld) for wt, out_f, out, ld in jobs])
+    check(lib().qh_gemm(gtype, C.cast(arr, C.c_void_p), len(jobs), k, dptr(xq), n_tok, None), "qh_gemm")
+
+
 def tensor_matmul_q4k_f32(w, out_f, k, x):
     return matmul(Q4_K, w, k, out_f, x)
 

@@ -1,0 +1,131 @@
+# SPDX-License-Identifier: MIT
+"""GPU: the tensor-core matmul (tcgen05 kind::i8, include/qh_backend.h
+qh_gemm*) against the oracle's restatement of tensor_matmul_*_f32
+(slm/tensor.c:827-1033) on the same seeded inputs. Bar: bit-exact fp32 --
+the integers come from the tensor core, the per-block fp32 combination
+follows the reference's order."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+Q8_0, Q4_K, Q5_K, Q6_K = 8, 12, 13, 14
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def assert_bitwise(got, want, what):
+    if not np.array_equal(bits(got), bits(want)):
+        bad = np.flatnonzero(bits(got).ravel() != bits(want).ravel())
+        i = bad[0]
+        raise AssertionError(f"{what}: {bad.size} of {got.size} differ, first at {np.unravel_index(i, got.shape)}: "
+                             f"got {got.ravel()[i]!r} want {want.ravel()[i]!r}")
+
+
+def run_gemm(qh, cuda, gt, w_np, k, out_f, x_np):
+    w = qh.host.to_device(w_np)
+    x = qh.host.to_device(np.ascontiguousarray(x_np, np.float32))
+    out = qh.host.matmul_gemm(gt, w, k, out_f, x, n_tok=x_np.shape[0])
+    cuda.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("gt", [Q4_K, Q5_K, Q6_K])
+@pytest.mark.parametrize("k,out_f,n_tok", [(256, 128, 64), (1024, 300, 70), (2048, 257, 1), (512, 1000, 129)])
+def test_gemm_bitexact_vs_oracle(qh, cuda, oracle, gt, k, out_f, n_tok):
+    w = qh.host.synth_blocks(gt, out_f * (k // 256), 0x6E44 + gt + k + out_f)
+    x = qh.host.synth_normal(n_tok * k, 77 + n_tok + k, 0.0, 1.0).reshape(n_tok, k)
+    got = run_gemm(qh, cuda, gt, w, k, out_f, x)
+    want = oracle.matmul(gt, w, out_f, k, x)
+    assert_bitwise(got, want.reshape(n_tok, out_f), f"type {gt} k={k} out_f={out_f} n={n_tok}")
+
+
+def test_gemm_matches_gemv_path(qh, cuda):
+    """Same inputs through the matvec kernel (qh_matmul) and the GEMM."""
+    k, out_f, n_tok = 1024, 2048, 96
+    w_np = qh.host.synth_blocks(Q4_K, out_f * 4, 0xA11)
+    x_np = qh.host.synth_normal(n_tok * k, 0xA12).reshape(n_tok, k)
+    w, x = qh.host.to_device(w_np), qh.host.to_device(x_np)
+    a = qh.host.matmul(Q4_K, w, k, out_f, x, n_tok=n_tok)
+    b = qh.host.matmul_gemm(Q4_K, w, k, out_f, x, n_tok=n_tok)
+    cuda.cuda.synchronize()
+    assert_bitwise(b.cpu().numpy(), a.cpu().numpy(), "gemm vs gemv")
+
+
+def test_grouped_gemm_with_row_stride(qh, cuda, oracle):
+    """Two jobs sharing one tiled activation buffer; outputs with ld_out > out_f."""
+    torch = cuda
+    k, n_tok = 1024, 65
+    shapes = [(384, Q6_K), (200, Q6_K)]
+    x_np = qh.host.synth_normal(n_tok * k, 5).reshape(n_tok, k)
+    xq = qh.host.quantize_q8kt(qh.host.to_device(x_np), k, n_tok)
+    jobs, ws, outs = [], [], []
+    for i, (out_f, gt) in enumerate(shapes):
+        w = qh.host.synth_blocks(gt, out_f * 4, 900 + i)
+        ws.append(w)
+        wt = qh.host.gemm_pack(gt, qh.host.to_device(w), k, out_f)
+        out = torch.full((n_tok, out_f + 13), -7.0, dtype=torch.float32, device="cuda")
+        outs.append((wt, out))
+        jobs.append((wt, out_f, out, out_f + 13))
+    qh.host.gemm(Q6_K, jobs, k, xq, n_tok)
+    cuda.cuda.synchronize()
+    for (out_f, gt), w, (_, out) in zip(shapes, ws, outs):
+        o = out.cpu().numpy()
+        assert_bitwise(o[:, :out_f], oracle.matmul(gt, w, out_f, k, x_np).reshape(n_tok, out_f), f"job {out_f}")
+        assert np.all(o[:, out_f:] == -7.0), "wrote past out_f"
+
+
+@pytest.mark.parametrize("cfg", ["3a", "3b"])
+def test_prefill_configs(qh, cuda, oracle, cfg):
+    """Benchmark config 3: M=512 K=1024 N=3584 Q4_K and M=2048 K=3584 N=1024
+    Q6_K, full size on the GPU; the oracle checks a seeded subset of tokens
+    (tokens are independent) bit for bit."""
+    m, k, n, gt = (512, 1024, 3584, Q4_K) if cfg == "3a" else (2048, 3584, 1024, Q6_K)
+    w = qh.host.synth_blocks(gt, n * (k // 256), 0x3A if cfg == "3a" else 0x3B)
+    x = qh.host.synth_normal(m * k, 0x33 + m).reshape(m, k)
+    got = run_gemm(qh, cuda, gt, w, k, n, x)
+    rows = np.random.default_rng(3).choice(m, 24, replace=False)
+    rows = np.unique(np.concatenate([rows, [0, 63, 64, m - 1]]))
+    want = oracle.matmul(gt, w, n, k, x[rows]).reshape(len(rows), n)
+    assert_bitwise(got[rows], want, f"config {cfg}")
+    assert np.all(np.isfinite(got))
+
+
+def test_gemm_rejects_q8_0_and_small_workspace(qh, cuda):
+    L = qh.lib()
+    assert L.qh_matmul_gemm_workspace_bytes(Q8_0, 1024, 64, 64) < 0
+    import ctypes as C
+    w = qh.host.to_device(qh.host.synth_blocks(Q4_K, 64 * 4, 1))
+    x = qh.host.to_device(qh.host.synth_normal(64 * 1024, 2))
+    out = cuda.empty((64, 64), dtype=cuda.float32, device="cuda")
+    need = int(L.qh_matmul_gemm_workspace_bytes(Q4_K, 1024, 64, 64))
+    work = cuda.empty(need, dtype=cuda.uint8, device="cuda")
+    rc = L.qh_matmul_gemm(Q4_K, C.c_void_p(w.data_ptr()), 1024, 64, C.c_void_p(x.data_ptr()), 64,
+                          C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()), need - 16, None)
+    assert rc == -5  # QH_ERR_WORKSPACE
+    rc = L.qh_matmul_gemm(Q8_0, C.c_void_p(w.data_ptr()), 1024, 64, C.c_void_p(x.data_ptr()), 64,
+                          C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()), need, None)
+    assert rc == -2  # QH_ERR_UNSUPPORTED
+
+
+def test_quantize_q8kt_matches_split_layout(qh, cuda):
+    """The tiled quantizer writes the same quants and scales as qh_quantize_q8k."""
+    k, n_tok = 1024, 70
+    x_np = qh.host.synth_normal(n_tok * k, 9, 0.0, 3.0).reshape(n_tok, k)
+    x = qh.host.to_device(x_np)
+    split = qh.host.quantize_q8k(x, k, n_tok)
+    tiled = qh.host.quantize_q8kt(x, k, n_tok)
+    cuda.cuda.synchronize()
+    qs, d, _ = qh.host.unpack_q8k(split.cpu().numpy(), k, n_tok)
+    t = tiled.cpu().numpy()
+    nb = k // 256
+    tiles = (n_tok + 63) // 64
+    q = t[:tiles * nb * 16384].view(np.int8).reshape(tiles, nb, 16, 64, 16)
+    q = q.transpose(0, 3, 1, 2, 4).reshape(tiles * 64, k)[:n_tok]
+    assert np.array_equal(q, qs)
+    off = int(qh.lib().qh_q8kt_d_offset(k, n_tok))
+    ds = ((nb + 3) // 4) * 4
+    dt = t[off:off + n_tok * ds * 4].view(np.float32).reshape(n_tok, ds)[:, :nb]
+    assert np.array_equal(dt.view(np.uint32), np.asarray(d, np.float32).reshape(n_tok, -1)[:, :nb].view(np.uint32))
