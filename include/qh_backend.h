@@ -199,19 +199,22 @@ int qh_matvec_plan_destroy(qh_matvec_plan plan);
  *
  * Formats:
  *   tiled weights  -- the GGUF blocks reordered as [row tile of 128][block]
- *                     [128 rows][block bytes] (rows past out_f zero):
+ *                     [128 rows][block bytes padded to 16: 144, 176, 224]
+ *                     (rows past out_f and padding zero):
  *                     qh_gemm_weight_bytes bytes, written by
  *                     qh_gemm_pack_weights from the GGUF (k, out_f) blocks.
  *   tiled Q8_K     -- the reference's quantize_row_q8_K per token
- *                     (slm/tensor.c:683-720), quants laid out per 64-token
- *                     tile as the MMA operand, then the fp32 scales
- *                     [n_tok][ceil4(k/256)] at qh_q8kt_d_offset;
+ *                     (slm/tensor.c:683-720); per (64-token tile, block)
+ *                     18,688 bytes: the quants as the MMA operand
+ *                     [16 chunks][64 tokens][16], the 64 fp32 scales, and
+ *                     the sub-block sums S_j as two int8 operand rows per
+ *                     token (S_j mod 128, floor(S_j / 128));
  *                     qh_q8kt_bytes bytes, written by qh_quantize_q8kt.
  * ---------------------------------------------------------------------- */
+#define QH_Q8KT_TILE_TOKENS 64  /* tokens per tile of the tiled Q8_K layout */
 int64_t qh_gemm_weight_bytes(int type, int64_t k, int64_t out_f);
 int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, void *d_wt, void *stream);
 int64_t qh_q8kt_bytes(int64_t k, int64_t n_tok);
-int64_t qh_q8kt_d_offset(int64_t k, int64_t n_tok);
 int qh_quantize_q8kt(const float *d_x, int64_t k, int64_t n_tok, void *d_q8kt, void *stream);
 
 /* One output of a grouped GEMM: d_out[t * ld_out + j] = row j of the tiled

@@ -91,7 +91,6 @@ SIGNATURES = {
     "qh_gemm_weight_bytes": (_I64, [_I, _I64, _I64]),
     "qh_gemm_pack_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
     "qh_q8kt_bytes": (_I64, [_I64, _I64]),
-    "qh_q8kt_d_offset": (_I64, [_I64, _I64]),
     "qh_quantize_q8kt": (_I, [_P, _I64, _I64, _P, _P]),
     "qh_gemm": (_I, [_I, _P, _I, _I64, _P, _I64, _P]),
     "qh_matmul_gemm_workspace_bytes": (_I64, [_I, _I64, _I64, _I64]),

@@ -101,19 +101,25 @@ static inline QH_HD int64_t qhf_q8_0_total_bytes(int64_t k, int64_t n_tok) {
     return qhf_align16(qhf_q8_0_d_offset(k, n_tok) + qhf_q8_0_d_stride(k) * n_tok * 2);
 }
 
-// Q8_K tiled activation layout read by the tensor-core GEMM: the quants of
-// each 64-token tile and 256-value block form one 16 KB operand tile in the
-// no-swizzle K-major layout [16 chunks of 16 values][64 tokens][16 bytes];
-// tokens past n_tok in the last tile are padding. Then the scales as in the
-// split layout. No block sums (the GEMM derives the min terms itself).
+// Q8_K tiled activation layout read by the tensor-core GEMM. Per 64-token
+// tile and 256-value block, one contiguous "tile block" of
+// QH_Q8KT_BLOCK_BYTES:
+//   [16384] quants in the no-swizzle K-major operand layout
+//           [16 chunks of 16 values][64 tokens][16 bytes];
+//   [  256] the 64 tokens' fp32 scales d;
+//   [ 2048] the min operand: 128 rows x 16 bytes; row t < 64 holds, for
+//           sub-blocks j = 0..7, S_j(t) mod 128 and row 64 + t holds
+//           floor(S_j(t) / 128), where S_j = bsums[2j] + bsums[2j+1] (the
+//           sum of the 32 quants of sub-block j); bytes 8..15 are zero.
+// Tokens past n_tok in the last tile are padding (never read as results).
 #define QH_Q8KT_TILE 64
-#define QH_Q8KT_BLOCK_BYTES (QH_Q8KT_TILE * QH_QK)
+#define QH_Q8KT_QS_BYTES (QH_Q8KT_TILE * QH_QK)
+#define QH_Q8KT_D_OFF QH_Q8KT_QS_BYTES
+#define QH_Q8KT_MIN_OFF (QH_Q8KT_QS_BYTES + QH_Q8KT_TILE * 4)
+#define QH_Q8KT_BLOCK_BYTES (QH_Q8KT_MIN_OFF + 2 * QH_Q8KT_TILE * 16)
 static inline QH_HD int64_t qhf_q8kt_tiles(int64_t n_tok) { return (n_tok + QH_Q8KT_TILE - 1) / QH_Q8KT_TILE; }
-static inline QH_HD int64_t qhf_q8kt_d_offset(int64_t k, int64_t n_tok) {
-    return qhf_q8kt_tiles(n_tok) * (k / QH_QK) * QH_Q8KT_BLOCK_BYTES;
-}
 static inline QH_HD int64_t qhf_q8kt_total_bytes(int64_t k, int64_t n_tok) {
-    return qhf_align16(qhf_q8kt_d_offset(k, n_tok) + qhf_q8k_d_stride(k) * n_tok * 4);
+    return qhf_q8kt_tiles(n_tok) * (k / QH_QK) * QH_Q8KT_BLOCK_BYTES;
 }
 
 #endif  // QH_FORMATS_H

@@ -30,7 +30,7 @@
 // bytes] (qh_gemm_pack_weights), so one super-block of a row tile is one
 // contiguous bulk copy.
 //
-// CTA: 8 consumer warps (expansion, MMA issue by one thread, epilogue) and
+// CTA: 4 expander warps (one also issues the MMAs), 4 epilogue warps and
 // 1 producer warp (bulk copies into a 3-stage ring), one CTA per SM,
 // persistent over (row tile, token tile) work items.
 
@@ -47,17 +47,21 @@
 
 namespace qh {
 
-constexpr int kGemmRows = 128;             // MMA M
-constexpr int kGemmTok = QH_Q8KT_TILE;     // MMA N (64)
-constexpr int kGemmThreads = 288;          // 8 consumer warps + 1 producer warp
-constexpr int kGemmConsumers = 256;
+constexpr int kGemmRows = 128;           // MMA M: weight rows per tile
+constexpr int kGemmTok = QH_Q8KT_TILE;   // MMA N: tokens per tile (64)
+constexpr int kExpWarps = 8;             // expanders: 2 threads per weight row
+constexpr int kEpiWarps = 8;             // epilogue: 4 lane groups x 2 token halves
+constexpr int kGemmThreads = 32 * (kExpWarps + kEpiWarps + 2);
+constexpr int kProducerWarp = kExpWarps + kEpiWarps;
+constexpr int kMmaWarp = kProducerWarp + 1;
 constexpr int kGemmMaxJobs = 8;
-constexpr int kGemmMaxStages = 6;
-constexpr int kPlaneBytes = kGemmRows * QH_QK;  // 32 KB
-constexpr int kXBytes = QH_Q8KT_BLOCK_BYTES;    // 16 KB
+constexpr int kGemmMaxStages = 4;
+constexpr int kPlaneBytes = kGemmRows * QH_QK;  // 32 KB: one int8 operand plane
+constexpr int kMinRowBytes = kGemmRows * 16;    // 2 KB: min operand (first K chunk)
 constexpr int kGemmHeader = 1024;
 constexpr int kGemmSmemMax = 232448;            // 227 KB per CTA
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kAccCols = 256;              // one accumulator set
+constexpr int kRing = 4;                        // scale ring depth (blocks)
 
 struct GemmJob {
     const uint8_t *wt;  // tiled weights
@@ -69,27 +73,33 @@ struct GemmJob {
 };
 
 struct GemmParams {
-    int32_t n_jobs, total_items, nb, n_tok, t_tiles, d_stride, n_stages, stage_bytes;
-    const uint8_t *xq;  // tiled Q8_K quants
-    const float *xd;    // Q8_K scales [n_tok][d_stride]
+    int32_t n_jobs, total_items, nb, n_tok, t_tiles, n_stages;
+    const uint8_t *xq;  // tiled Q8_K activations
     int *err_flag;
     GemmJob jobs[kGemmMaxJobs];
 };
 
+// Per type: GGUF block bytes, padded row-block bytes in the tiled weights
+// (16-byte multiple), operand planes (hi, lo) and whether the min operand
+// is used.
 template <int TYPE>
 struct KQ;
 template <>
 struct KQ<QH_GGUF_Q4_K> {
-    static constexpr int kBytes = QH_Q4K_BYTES, kPlanes = 3;
+    static constexpr int kBytes = QH_Q4K_BYTES, kPadded = 144, kMins = 1;
 };
 template <>
 struct KQ<QH_GGUF_Q5_K> {
-    static constexpr int kBytes = QH_Q5K_BYTES, kPlanes = 3;
+    static constexpr int kBytes = QH_Q5K_BYTES, kPadded = 176, kMins = 1;
 };
 template <>
 struct KQ<QH_GGUF_Q6_K> {
-    static constexpr int kBytes = QH_Q6K_BYTES, kPlanes = 2;
+    static constexpr int kBytes = QH_Q6K_BYTES, kPadded = 224, kMins = 0;
 };
+
+__host__ __device__ constexpr int padded_block_bytes(int type) {
+    return type == QH_GGUF_Q4_K ? 144 : type == QH_GGUF_Q5_K ? 176 : type == QH_GGUF_Q6_K ? 224 : 0;
+}
 
 __device__ __forceinline__ void put16(uint8_t *plane, int c, int r, uint32_t a, uint32_t b, uint32_t cc,
                                       uint32_t d) {
@@ -108,8 +118,8 @@ __device__ __forceinline__ void scale_min(const uint8_t *s12, int sb, int &sc, i
     }
 }
 
-// 4 weights (bytes of w, each < 2^9 / scale so products fit 16 bits)
-// times a non-negative scale, split into lo = a & 127 and hi = a >> 7 bytes.
+// 4 weights (bytes of w) times a non-negative scale (products < 2^16),
+// split into lo = a & 127 and hi = a >> 7 bytes.
 __device__ __forceinline__ void split_pos(uint32_t w, uint32_t sc, uint32_t &hi, uint32_t &lo) {
     const uint32_t p02 = (w & 0x00ff00ffu) * sc;
     const uint32_t p13 = ((w >> 8) & 0x00ff00ffu) * sc;
@@ -117,13 +127,15 @@ __device__ __forceinline__ void split_pos(uint32_t w, uint32_t sc, uint32_t &hi,
     hi = ((p02 >> 7) & 0x007f007fu) | (((p13 >> 7) & 0x007f007fu) << 8);
 }
 
-// Expansion of half h (weights 128h..128h+127) of row r's super-block.
+// Expansion of half h (weights 128h..128h+127) of row r's super-block into
+// the hi/lo planes (and, for h == 0, the row's min-operand entries).
 template <int TYPE>
 __device__ __forceinline__ void expand(const uint8_t *raw, int h, int r, uint8_t *planes);
 
 template <>
 __device__ __forceinline__ void expand<QH_GGUF_Q4_K>(const uint8_t *raw, int h, int r, uint8_t *planes) {
     const uint8_t *s12 = raw + 4;
+    uint32_t mins[2] = {0u, 0u};
 #pragma unroll
     for (int cl = 0; cl < 8; ++cl) {
         const int c = 8 * h + cl, sb = c >> 1;
@@ -135,16 +147,24 @@ __device__ __forceinline__ void expand<QH_GGUF_Q4_K>(const uint8_t *raw, int h, 
         const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) split_pos((qw[k] >> sh) & 0x0f0f0f0fu, static_cast<uint32_t>(sc), hi[k], lo[k]);
-        const uint32_t m4 = static_cast<uint32_t>(mn) * 0x01010101u;
         put16(planes, c, r, hi[0], hi[1], hi[2], hi[3]);
         put16(planes + kPlaneBytes, c, r, lo[0], lo[1], lo[2], lo[3]);
-        put16(planes + 2 * kPlaneBytes, c, r, m4, m4, m4, m4);
+    }
+    if (h == 0) {
+#pragma unroll
+        for (int sb = 0; sb < 8; ++sb) {
+            int sc, mn;
+            scale_min(s12, sb, sc, mn);
+            mins[sb >> 2] |= static_cast<uint32_t>(mn) << (8 * (sb & 3));
+        }
+        *reinterpret_cast<uint4 *>(planes + 2 * kPlaneBytes + r * 16) = make_uint4(mins[0], mins[1], 0u, 0u);
     }
 }
 
 template <>
 __device__ __forceinline__ void expand<QH_GGUF_Q5_K>(const uint8_t *raw, int h, int r, uint8_t *planes) {
     const uint8_t *s12 = raw + 4;
+    uint32_t mins[2] = {0u, 0u};
 #pragma unroll
     for (int cl = 0; cl < 8; ++cl) {
         const int c = 8 * h + cl, sb = c >> 1;
@@ -161,24 +181,34 @@ __device__ __forceinline__ void expand<QH_GGUF_Q5_K>(const uint8_t *raw, int h, 
             const uint32_t w = ((qw[k] >> sh) & 0x0f0f0f0fu) | (((hw[k] >> sb) & 0x01010101u) << 4);
             split_pos(w, static_cast<uint32_t>(sc), hi[k], lo[k]);
         }
-        const uint32_t m4 = static_cast<uint32_t>(mn) * 0x01010101u;
         put16(planes, c, r, hi[0], hi[1], hi[2], hi[3]);
         put16(planes + kPlaneBytes, c, r, lo[0], lo[1], lo[2], lo[3]);
-        put16(planes + 2 * kPlaneBytes, c, r, m4, m4, m4, m4);
+    }
+    if (h == 0) {
+#pragma unroll
+        for (int sb = 0; sb < 8; ++sb) {
+            int sc, mn;
+            scale_min(s12, sb, sc, mn);
+            mins[sb >> 2] |= static_cast<uint32_t>(mn) << (8 * (sb & 3));
+        }
+        *reinterpret_cast<uint4 *>(planes + 2 * kPlaneBytes + r * 16) = make_uint4(mins[0], mins[1], 0u, 0u);
     }
 }
 
 // Q6_K: a = sc * (w - 32), computed as u = a + 4096 in non-negative 16-bit
 // lanes (no carries or borrows cross lanes for |sc| <= 128, w <= 63); then
-// lo = u & 127 and hi = (u >> 7) - 32 = floor(a / 128).
+// lo = u & 127 and hi = (u >> 7) - 32 = floor(a / 128). Rows are padded to
+// 224 bytes in the tiled weights, so every field is 16-byte aligned.
 template <>
 __device__ __forceinline__ void expand<QH_GGUF_Q6_K>(const uint8_t *raw, int h, int r, uint8_t *planes) {
+    const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 192);
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
 #pragma unroll
     for (int cl = 0; cl < 8; ++cl) {
         const int c = 8 * h + cl, rq = (c >> 1) & 3, l0 = 16 * (c & 1);
-        const uint4 ql = lds128_a2(raw + 64 * h + 32 * (rq & 1) + l0);
-        const uint4 qh = lds128_a2(raw + 128 + 32 * h + l0);
-        const int sc = static_cast<int8_t>(raw[192 + c]);
+        const uint4 ql = *reinterpret_cast<const uint4 *>(raw + 64 * h + 32 * (rq & 1) + l0);
+        const uint4 qh = *reinterpret_cast<const uint4 *>(raw + 128 + 32 * h + l0);
+        const int sc = static_cast<int8_t>((scw[c >> 2] >> (8 * (c & 3))) & 0xffu);
         const uint32_t lsh = 4u * static_cast<uint32_t>(rq >> 1), hsh = 2u * static_cast<uint32_t>(rq);
         const uint32_t a = static_cast<uint32_t>(sc < 0 ? -sc : sc);
         const uint32_t cst = static_cast<uint32_t>(sc < 0 ? 4096 + 32 * (-sc) : 4096 - 32 * sc);
@@ -210,20 +240,62 @@ __device__ __forceinline__ void decode_item(const GemmParams &p, int item, GemmJ
     mt = g - job.tile_begin;
 }
 
+// Shared-memory plan of one CTA (offsets from the dynamic smem base).
+template <int TYPE>
+struct GemmSmem {
+    static constexpr int kWB = kGemmRows * KQ<TYPE>::kPadded;                   // weight tile block
+    static constexpr int kXB = KQ<TYPE>::kMins ? QH_Q8KT_BLOCK_BYTES : QH_Q8KT_MIN_OFF;  // activation bytes copied
+    static constexpr int kStage = kWB + kXB;
+    static constexpr int kABuf = 2 * kPlaneBytes + (KQ<TYPE>::kMins ? kMinRowBytes : 0);
+    static constexpr int kA = kGemmHeader;                                       // 2 A buffers
+    static constexpr int kScales = kA + 2 * kABuf;                               // ring of token scales
+    static constexpr int kRowScales = kScales + kRing * kGemmTok * 4;            // ring of row (d, dmin)
+    static constexpr int kStages = kRowScales + kRing * kGemmRows * 8;           // stage ring
+    static constexpr int kNStages = (kGemmSmemMax - kStages - kMinRowBytes) / kStage > kGemmMaxStages
+                                        ? kGemmMaxStages
+                                        : (kGemmSmemMax - kStages - kMinRowBytes) / kStage;
+    // 2 KB of zeros after the stages: the second K chunk of both min
+    // operands (a positive leading-dimension offset from either).
+    static constexpr int kZero = kStages + kNStages * kStage;
+    static constexpr int kTotal = kZero + kMinRowBytes;
+    static_assert(kNStages >= 2 && kTotal <= kGemmSmemMax, "shared memory plan");
+};
+
+// Warp roles (576 threads, one CTA per SM):
+//   warps 0-7   expanders: two threads per weight row build the A planes
+//               of a super-block into one of two A buffers and copy its
+//               scales to a small ring;
+//   warps 8-15  epilogue: thread = (weight row, half of the token tile);
+//               reads the accumulators, combines in fp32, stores;
+//   warp 16     producer: one bulk copy each of the weight tile block and
+//               the activation tile block per super-block;
+//   warp 17     one thread issues the MMAs of each block.
+// A buffers and TMEM accumulators are double-buffered, so the expansion of
+// block b+1, the MMAs of block b and the epilogue of block b-1 overlap.
+// mbarriers: full[s] (copies landed), empty[s] (block's MMAs done with the
+// stage), mma_done[2] (MMAs of a block completed: its A buffer is free, its
+// accumulators readable), acc_empty[2] (8 epilogue warps read them),
+// a_ready[2] (8 expander warps wrote a block's A buffer and scales),
+// scale_ready[2] (the MMA thread passes the scales on to the epilogue).
 template <int TYPE>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
-    constexpr int BB = KQ<TYPE>::kBytes, P = KQ<TYPE>::kPlanes;
-    constexpr int WB = kGemmRows * BB;  // weight bytes of one row tile's super-block
+    using L = GemmSmem<TYPE>;
+    constexpr int BBP = KQ<TYPE>::kPadded, MINS = KQ<TYPE>::kMins;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kGemmMaxStages;
-    uint64_t *mma_bar = empty + kGemmMaxStages;
+    uint64_t *mma_done = empty + kGemmMaxStages;
+    uint64_t *acc_empty = mma_done + 2;
+    uint64_t *scale_ready = acc_empty + 2;
+    uint64_t *a_ready = scale_ready + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 256);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 260);
-    uint8_t *planes = smem + kGemmHeader;
-    uint8_t *stages = planes + P * kPlaneBytes;
+    float *tok_scale = reinterpret_cast<float *>(smem + L::kScales);     // [kRing][64]
+    float2 *row_scale = reinterpret_cast<float2 *>(smem + L::kRowScales);  // [kRing][128]
+    uint8_t *zero = smem + L::kZero;
+    uint8_t *stages = smem + L::kStages;
 
-    const int S = p.n_stages;
+    constexpr int S = L::kNStages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_launch_dependents();
     if (tid == 0) {
@@ -231,14 +303,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(mma_bar, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&mma_done[b], 1);
+            mbar_init(&acc_empty[b], kEpiWarps);
+            mbar_init(&scale_ready[b], 1);
+            mbar_init(&a_ready[b], kExpWarps);
+        }
         *abort_flag = 0;
         mbar_fence_init();
     }
+    for (int i = tid; i < kMinRowBytes / 16; i += kGemmThreads)
+        reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0u, 0u, 0u, 0u);
     // Earlier kernels on the stream finish (and free their TMEM) first.
     pdl_wait();
     if (warp == 0) {
-        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_alloc(tmem_slot, 2 * kAccCols);
         tc::tmem_relinquish();
     }
     tc::fence_before_sync();
@@ -246,8 +325,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kGemmConsumers / 32) {
-        // ----- producer: one thread streams (weights, activations) per super-block -----
+    if (warp == kProducerWarp) {
+        // ----- producer -----
         if (lane == 0) {
             int i = 0;
             bool stop = false;
@@ -255,114 +334,170 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 GemmJob job;
                 int mt, tt;
                 decode_item(p, item, job, mt, tt);
-                const uint8_t *wsrc = job.wt + static_cast<int64_t>(mt) * p.nb * WB;
-                const uint8_t *xsrc = p.xq + static_cast<int64_t>(tt) * p.nb * kXBytes;
+                const uint8_t *wsrc = job.wt + static_cast<int64_t>(mt) * p.nb * L::kWB;
+                const uint8_t *xsrc = p.xq + static_cast<int64_t>(tt) * p.nb * QH_Q8KT_BLOCK_BYTES;
                 for (int b = 0; b < p.nb; ++b, ++i) {
                     const int s = i % S;
-                    const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-                    if (*abort_flag || (i >= S && !mbar_wait(&empty[s], ph ^ 1u))) {
+                    if (*abort_flag) { stop = true; break; }
+                    if (i >= S && !mbar_wait(&empty[s], (static_cast<uint32_t>(i / S) & 1u) ^ 1u)) {
                         report_error(p.err_flag, kDevWaitTimeout);
                         *abort_flag = 1;
                         stop = true;
                         break;
                     }
-                    uint8_t *dst = stages + static_cast<int64_t>(s) * p.stage_bytes;
-                    mbar_arrive_expect_tx(&full[s], WB + kXBytes);
-                    bulk_copy_g2s(dst, wsrc + static_cast<int64_t>(b) * WB, WB, &full[s]);
-                    bulk_copy_g2s(dst + WB, xsrc + static_cast<int64_t>(b) * kXBytes, kXBytes, &full[s]);
+                    uint8_t *dst = stages + static_cast<int64_t>(s) * L::kStage;
+                    mbar_arrive_expect_tx(&full[s], L::kWB + L::kXB);
+                    bulk_copy_g2s(dst, wsrc + static_cast<int64_t>(b) * L::kWB, L::kWB, &full[s]);
+                    bulk_copy_g2s(dst + L::kWB, xsrc + static_cast<int64_t>(b) * QH_Q8KT_BLOCK_BYTES, L::kXB,
+                                  &full[s]);
                 }
             }
             // Drain: no copy of this CTA stays in flight past its exit.
             for (int j = max(0, i - S); j < i; ++j)
                 if (!mbar_wait(&full[j % S], static_cast<uint32_t>(j / S) & 1u)) report_error(p.err_flag, kDevWaitTimeout);
         }
+    } else if (warp == kMmaWarp) {
+        // ----- MMA issue: one thread -----
+        if (lane == 0) {
+            constexpr uint32_t idesc64 = tc::idesc_i8(kGemmRows, kGemmTok);
+            constexpr uint32_t idesc128 = tc::idesc_i8(kGemmRows, 2 * kGemmTok);
+            int i = 0, ib = 0;
+            bool stop = false;
+            for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
+                for (int b = 0; b < p.nb; ++b, ++i, ++ib) {
+                    const int s = i % S, buf = ib & 1;
+                    const uint32_t ph = static_cast<uint32_t>(ib >> 1) & 1u;
+                    // expanders done with this block's A buffer and scales; the
+                    // epilogue done with the accumulators two blocks back
+                    const bool ok = !*abort_flag && mbar_wait(&a_ready[buf], ph) &&
+                                    (ib < 2 || mbar_wait(&acc_empty[buf], ph ^ 1u));
+                    if (!ok) {
+                        report_error(p.err_flag, kDevWaitTimeout);
+                        *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint8_t *xst = stages + static_cast<int64_t>(s) * L::kStage + L::kWB;
+                    const uint32_t a0 = smem_addr(smem + L::kA + buf * L::kABuf), b0 = smem_addr(xst);
+                    const uint32_t dcol = tmem + buf * kAccCols;
+                    const uint64_t ad0 = tc::smem_desc(a0, kGemmRows * 16, 128);
+                    const uint64_t bd0 = tc::smem_desc(b0, kGemmTok * 16, 128);
+#pragma unroll
+                    for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+                        for (int ks = 0; ks < QH_QK / 32; ++ks)
+                            tc::mma_i8(dcol + pl * kGemmTok,
+                                       ad0 + static_cast<uint64_t>((pl * kPlaneBytes + ks * 2 * kGemmRows * 16) >> 4),
+                                       bd0 + static_cast<uint64_t>((ks * 2 * kGemmTok * 16) >> 4), idesc64, ks > 0);
+                    if (MINS) {
+                        // [S mod 128 | floor(S/128)] (128 columns) = min row x min operand;
+                        // the second K chunk of both operands is the zero area.
+                        const uint32_t am = a0 + 2 * kPlaneBytes, bm = b0 + QH_Q8KT_MIN_OFF, z = smem_addr(zero);
+                        tc::mma_i8(dcol + 2 * kGemmTok, tc::smem_desc(am, z - am, 128), tc::smem_desc(bm, z - bm, 128),
+                                   idesc128, false);
+                    }
+                    tc::commit(&mma_done[buf]);
+                    tc::commit(&empty[s]);
+                    // release the block's scales (written before a_ready) to the epilogue
+                    mbar_arrive(&scale_ready[buf]);
+                }
+            }
+        }
+    } else if (warp < kExpWarps) {
+        // ----- expanders -----
+        const int r = tid >> 1, h = tid & 1;
+        int i = 0, ib = 0;
+        bool stop = false;
+        for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
+            for (int b = 0; b < p.nb; ++b, ++i, ++ib) {
+                const int s = i % S, buf = ib & 1, ring = ib % kRing;
+                // stage landed; the MMAs two blocks back are done with this A buffer
+                const bool ok = __all_sync(0xffffffffu,
+                                           !*abort_flag && mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u) &&
+                                               (ib < 2 || mbar_wait(&mma_done[buf], static_cast<uint32_t>((ib - 2) >> 1) & 1u)));
+                if (!ok) {
+                    stop = true;
+                    break;
+                }
+                const uint8_t *wst = stages + static_cast<int64_t>(s) * L::kStage;
+                const uint8_t *raw = wst + r * BBP;
+                expand<TYPE>(raw, h, r, smem + L::kA + buf * L::kABuf);
+                if (h == 0) {
+                    const uint32_t dd = *reinterpret_cast<const uint32_t *>(raw + (TYPE == QH_GGUF_Q6_K ? 208 : 0));
+                    row_scale[ring * kGemmRows + r] =
+                        make_float2(h2f_bits(dd), TYPE == QH_GGUF_Q6_K ? 0.0f : h2f_bits(dd >> 16));
+                }
+                if (tid < kGemmTok / 4)
+                    reinterpret_cast<uint4 *>(tok_scale + ring * kGemmTok)[tid] =
+                        reinterpret_cast<const uint4 *>(wst + L::kWB + QH_Q8KT_D_OFF)[tid];
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_ready[buf]);
+            }
+        }
+        if (stop && lane == 0) {
+            report_error(p.err_flag, kDevWaitTimeout);
+            *abort_flag = 1;
+        }
     } else {
-        // ----- consumers -----
-        const int r = tid >> 1, h = tid & 1;             // expansion: row, half
-        const int er = 32 * (warp & 3) + lane;           // epilogue: row (TMEM lane)
-        const int eh = warp >> 2;                        // epilogue: token half
-        const uint32_t tcol = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + 32u * eh;
-        constexpr uint32_t idesc = tc::idesc_i8(kGemmRows, kGemmTok);
-        uint32_t mma_phase = 0;
-        int i = 0;
-        bool aborted = false;
-        for (int item = blockIdx.x; item < p.total_items && !aborted; item += gridDim.x) {
+        // ----- epilogue -----
+        const int ew = warp - kExpWarps;
+        const int er = 32 * (ew & 3) + lane;  // weight row = TMEM lane
+        const int th = ew >> 2;               // token half of the tile
+        const uint32_t lane_base = static_cast<uint32_t>(32 * (ew & 3)) << 16;
+        int ib = 0;
+        bool stop = false;
+        for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
             GemmJob job;
             int mt, tt;
             decode_item(p, item, job, mt, tt);
             float acc[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-            const int t0 = tt * kGemmTok + 32 * eh;
-            for (int b = 0; b < p.nb; ++b, ++i) {
-                const int s = i % S;
-                const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-                const bool ok = mbar_wait(&full[s], ph);
-                const uint8_t *wst = stages + static_cast<int64_t>(s) * p.stage_bytes;
-                float dw = 0.0f, dmw = 0.0f;
-                if (ok) {
-                    expand<TYPE>(wst + r * BB, h, r, planes);
-                    const uint8_t *er_raw = wst + er * BB;
-                    if (TYPE == QH_GGUF_Q6_K) {
-                        dw = h2f_bits(static_cast<uint32_t>(er_raw[208]) | (static_cast<uint32_t>(er_raw[209]) << 8));
-                    } else {
-                        const uint32_t dd = *reinterpret_cast<const uint32_t *>(er_raw);
-                        dw = h2f_bits(dd);
-                        dmw = h2f_bits(dd >> 16);
-                    }
-                }
-                tc::fence_proxy_async_smem();
-                if (bar_any(1, kGemmConsumers, !ok)) {
-                    aborted = true;
-                    break;
-                }
-                if (tid == 0) {
-                    tc::fence_after_sync();
-                    const uint32_t a0 = smem_addr(planes), b0 = smem_addr(wst + WB);
-#pragma unroll
-                    for (int pl = 0; pl < P; ++pl)
-#pragma unroll
-                        for (int ks = 0; ks < QH_QK / 32; ++ks) {
-                            const uint64_t ad = tc::smem_desc(a0 + pl * kPlaneBytes + ks * 2 * (kGemmRows * 16),
-                                                              kGemmRows * 16, 128);
-                            const uint64_t bd = tc::smem_desc(b0 + ks * 2 * (kGemmTok * 16), kGemmTok * 16, 128);
-                            tc::mma_i8(tmem + pl * kGemmTok, ad, bd, idesc, ks > 0);
-                        }
-                    tc::commit(mma_bar);
-                    tc::commit(&empty[s]);
-                }
-                const bool ok2 = mbar_wait(mma_bar, mma_phase);
-                mma_phase ^= 1u;
-                if (bar_any(2, kGemmConsumers, !ok2)) {
-                    aborted = true;
+            const int t0 = tt * kGemmTok + 32 * th;
+            for (int b = 0; b < p.nb; ++b, ++ib) {
+                const int buf = ib & 1, ring = ib % kRing;
+                const uint32_t ph = static_cast<uint32_t>(ib >> 1) & 1u;
+                const bool ok = __all_sync(0xffffffffu, mbar_wait(&scale_ready[buf], ph) && mbar_wait(&mma_done[buf], ph));
+                if (!ok || *abort_flag) {
+                    stop = true;
                     break;
                 }
                 tc::fence_after_sync();
-                uint32_t vhi[32], vlo[32], vmn[32];
-                tc::ld_32x32b_x32(tcol, vhi);
-                tc::ld_32x32b_x32(tcol + kGemmTok, vlo);
-                if (P == 3) tc::ld_32x32b_x32(tcol + 2 * kGemmTok, vmn);
-                tc::wait_ld();
-                tc::fence_before_sync();
+                const float2 rs = row_scale[ring * kGemmRows + er];
+                const float *ts = tok_scale + ring * kGemmTok + 32 * th;
+                const uint32_t tcol = tmem + lane_base + buf * kAccCols + 32 * th;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = t0 + j;
-                    if (t < p.n_tok) {
-                        const float yd = __ldg(p.xd + static_cast<int64_t>(t) * p.d_stride + b);
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t vhi[16], vlo[16], vsl[16], vsh[16];
+                    tc::ld_32x32b_x16(tcol + 16 * c, vhi);
+                    tc::ld_32x32b_x16(tcol + kGemmTok + 16 * c, vlo);
+                    if (MINS) {
+                        tc::ld_32x32b_x16(tcol + 2 * kGemmTok + 16 * c, vsl);
+                        tc::ld_32x32b_x16(tcol + 3 * kGemmTok + 16 * c, vsh);
+                    }
+                    tc::wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float yd = ts[16 * c + j];
                         const int isum = static_cast<int>(vhi[j]) * 128 + static_cast<int>(vlo[j]);
                         float term;
-                        if (TYPE == QH_GGUF_Q6_K) {
-                            term = __fmul_rn(__fmul_rn(dw, yd), __int2float_rn(isum));
+                        if (!MINS) {
+                            term = __fmul_rn(__fmul_rn(rs.x, yd), __int2float_rn(isum));
                         } else {
-                            const float d = __fmul_rn(yd, dw), dm = __fmul_rn(yd, dmw);
-                            term = __fsub_rn(__fmul_rn(d, __int2float_rn(isum)),
-                                             __fmul_rn(dm, __int2float_rn(static_cast<int>(vmn[j]))));
+                            const int imin = static_cast<int>(vsl[j]) + 128 * static_cast<int>(vsh[j]);
+                            const float d = __fmul_rn(yd, rs.x), dm = __fmul_rn(yd, rs.y);
+                            term = __fsub_rn(__fmul_rn(d, __int2float_rn(isum)), __fmul_rn(dm, __int2float_rn(imin)));
                         }
-                        acc[j] = __fadd_rn(acc[j], term);
+                        acc[16 * c + j] = __fadd_rn(acc[16 * c + j], term);
                     }
                 }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
             }
-            if (aborted) break;
+            if (stop) break;
             const int n = mt * kGemmRows + er;
             if (n < job.n_rows) {
 #pragma unroll
@@ -370,7 +505,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     if (t0 + j < p.n_tok) job.out[static_cast<int64_t>(t0 + j) * job.ldo + n] = acc[j];
             }
         }
-        if (aborted && tid == 0) {
+        if (stop && lane == 0) {
             report_error(p.err_flag, kDevWaitTimeout);
             *abort_flag = 1;
         }
@@ -379,26 +514,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        tc::tmem_dealloc(tmem, 2 * kAccCols);
     }
 }
 
-// Weight repacking: GGUF rows -> [row tile][block][128 rows][block bytes],
-// rows past n_rows zero. CTA (row tile, block), one thread per row.
-__global__ void pack_tiles_kernel(const uint8_t *__restrict__ w, int64_t n_rows, int nb, int bb,
+// Weight repacking: GGUF rows -> [row tile][block][128 rows][padded block
+// bytes], padding and rows past n_rows zero. CTA (row tile, block), one
+// thread per row; 2-byte copies (GGUF rows are 2-byte aligned).
+__global__ void pack_tiles_kernel(const uint8_t *__restrict__ w, int64_t n_rows, int nb, int bb, int bbp,
                                   uint8_t *__restrict__ wt) {
     pdl_launch_dependents();
     pdl_wait();
     const int64_t mt = blockIdx.x;
     const int b = blockIdx.y, r = threadIdx.x;
     const int64_t row = mt * kGemmRows + r;
-    uint16_t *dst = reinterpret_cast<uint16_t *>(wt + ((mt * nb + b) * kGemmRows + r) * bb);
+    uint16_t *dst = reinterpret_cast<uint16_t *>(wt + ((mt * nb + b) * kGemmRows + r) * bbp);
+    int i = 0;
     if (row < n_rows) {
         const uint16_t *src = reinterpret_cast<const uint16_t *>(w + row * nb * bb + static_cast<int64_t>(b) * bb);
-        for (int i = 0; i < bb / 2; ++i) dst[i] = src[i];
-    } else {
-        for (int i = 0; i < bb / 2; ++i) dst[i] = 0;
+        for (; i < bb / 2; ++i) dst[i] = src[i];
     }
+    for (; i < bbp / 2; ++i) dst[i] = 0;
 }
 
 // Q8_K quantization into the tiled layout: CTA (block, token).
@@ -414,13 +550,10 @@ __global__ void __launch_bounds__(256) quantize_q8kt_kernel(const float *__restr
 
 template <int TYPE>
 static cudaError_t gemm_launch_t(const GemmParams &p0, int sm_count, cudaStream_t stream) {
-    constexpr int WB = kGemmRows * KQ<TYPE>::kBytes, P = KQ<TYPE>::kPlanes;
+    using L = GemmSmem<TYPE>;
     GemmParams p = p0;
-    p.stage_bytes = WB + kXBytes;
-    const int avail = kGemmSmemMax - kGemmHeader - P * kPlaneBytes;
-    p.n_stages = std::min(kGemmMaxStages, avail / p.stage_bytes);
-    if (p.n_stages < 2) return cudaErrorInvalidValue;
-    const int smem = kGemmHeader + P * kPlaneBytes + p.n_stages * p.stage_bytes;
+    p.n_stages = L::kNStages;
+    const int smem = L::kTotal;
     static bool attr_done[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -458,7 +591,7 @@ extern "C" {
 
 int64_t qh_gemm_weight_bytes(int type, int64_t k, int64_t out_f) {
     if (!gemm_type_ok(type) || k <= 0 || k % 256 || out_f <= 0) return -1;
-    return ((out_f + qh::kGemmRows - 1) / qh::kGemmRows) * qh::kGemmRows * qhf_row_bytes(type, k);
+    return ((out_f + qh::kGemmRows - 1) / qh::kGemmRows) * qh::kGemmRows * (k / 256) * qh::padded_block_bytes(type);
 }
 
 int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, void *d_wt, void *stream) {
@@ -471,7 +604,8 @@ int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, vo
     cudaError_t e = qh::launch_pdl(qh::pack_tiles_kernel, dim3(static_cast<unsigned>(mt), static_cast<unsigned>(k / 256)),
                                    dim3(qh::kGemmRows), 0, static_cast<cudaStream_t>(stream),
                                    static_cast<const uint8_t *>(d_w), out_f, static_cast<int>(k / 256),
-                                   static_cast<int>(qhf_block_bytes(type)), static_cast<uint8_t *>(d_wt));
+                                   static_cast<int>(qhf_block_bytes(type)), qh::padded_block_bytes(type),
+                                   static_cast<uint8_t *>(d_wt));
     if (e != cudaSuccess) return gcuda(e, "gemm_pack_weights launch");
     return QH_OK;
 }
@@ -479,10 +613,6 @@ int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, vo
 int64_t qh_q8kt_bytes(int64_t k, int64_t n_tok) {
     if (k <= 0 || k % 256 || n_tok <= 0) return -1;
     return qhf_q8kt_total_bytes(k, n_tok);
-}
-int64_t qh_q8kt_d_offset(int64_t k, int64_t n_tok) {
-    if (k <= 0 || k % 256 || n_tok <= 0) return -1;
-    return qhf_q8kt_d_offset(k, n_tok);
 }
 
 int qh_quantize_q8kt(const float *d_x, int64_t k, int64_t n_tok, void *d_q8kt, void *stream) {
@@ -512,9 +642,7 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
     p.nb = static_cast<int32_t>(k / 256);
     p.n_tok = static_cast<int32_t>(n_tok);
     p.t_tiles = static_cast<int32_t>(qhf_q8kt_tiles(n_tok));
-    p.d_stride = static_cast<int32_t>(qhf_q8k_d_stride(k));
     p.xq = static_cast<const uint8_t *>(d_q8kt);
-    p.xd = reinterpret_cast<const float *>(static_cast<const uint8_t *>(d_q8kt) + qhf_q8kt_d_offset(k, n_tok));
     p.err_flag = qh::device_error_word();
     if (!p.err_flag) return gfail(QH_ERR_CUDA, "gemm: no device error word");
     int64_t tiles = 0;

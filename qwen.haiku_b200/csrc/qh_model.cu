@@ -693,17 +693,20 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     if (xmax != 0.0f) {
         const float iscale = __fdiv_rn(-127.0f, xmax);
         q = q8k_value(y, iscale);
-        if (half == 0 && t == 0) r.d[blk] = __fdiv_rn(1.0f, iscale);
+        if (half == 0 && t == 0) *q8k_scale(r, blk) = __fdiv_rn(1.0f, iscale);
     } else if (half == 0 && t == 0) {
-        r.d[blk] = 0.0f;
+        *q8k_scale(r, blk) = 0.0f;
     }
     *q8k_elem(r, blk, half * HD + t) = static_cast<int8_t>(q);
-    if (r.bs) {
-        int sum = q;
+    int sum = q;
 #pragma unroll
-        for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (r.bs) {
         if ((lane & 15) == 0)
             r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+    } else {
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        if (lane == 0) q8k_put_min(r, blk, half * (HD / 32) + warp, sum);
     }
 }
 

@@ -45,14 +45,17 @@ __device__ __forceinline__ int q8k_value(float v, float iscale) {
 // Destination of the Q8_K quantization of row `tok` in either activation
 // layout (qh_formats.h):
 //   split  (tile == 0):  qs [n_tok][K], d [n_tok][d_stride], bsums;
-//   tiled  (tile == QH_Q8KT_TILE): qs in the tensor-core operand layout
-//          [tok/64][K/256][16 chunks][64 tokens][16 bytes], d as split, no bsums.
-// Element p (0..255) of block b sits at qs + b * bstride + (p / 16) * cstride + p % 16.
+//   tiled  (tile == QH_Q8KT_TILE): per (64-token tile, block) the operand
+//          quants, the scales and the min operand rows.
+// Element p (0..255) of block b sits at qs + b * bstride + (p / 16) * cstride
+// + p % 16; its scale at d + b * dstride.
 struct Q8KRow {
     int8_t *qs;
     int32_t bstride, cstride;
     float *d;
-    int16_t *bs;  // null in the tiled layout
+    int32_t dstride;
+    int16_t *bs;      // split layout only
+    int8_t *mins;     // tiled layout only: min-operand row of this token (block 0)
 };
 __device__ __forceinline__ Q8KRow q8k_row(uint8_t *base, int64_t k, int64_t n_tok, int64_t tok, int tile = 0) {
     Q8KRow r;
@@ -61,20 +64,38 @@ __device__ __forceinline__ Q8KRow q8k_row(uint8_t *base, int64_t k, int64_t n_to
         r.bstride = QH_QK;
         r.cstride = 16;
         r.d = reinterpret_cast<float *>(base + qhf_q8k_d_offset(k, n_tok)) + tok * qhf_q8k_d_stride(k);
+        r.dstride = 1;
         r.bs = reinterpret_cast<int16_t *>(base + qhf_q8k_bsums_offset(k, n_tok)) + tok * (k / QH_QK) * 16;
+        r.mins = nullptr;
     } else {
-        const int64_t nb = k / QH_QK;
-        r.qs = reinterpret_cast<int8_t *>(base) + (tok / QH_Q8KT_TILE) * nb * QH_Q8KT_BLOCK_BYTES +
-               (tok % QH_Q8KT_TILE) * 16;
+        const int64_t nb = k / QH_QK, tl = tok % QH_Q8KT_TILE;
+        uint8_t *tb = base + (tok / QH_Q8KT_TILE) * nb * QH_Q8KT_BLOCK_BYTES;
+        r.qs = reinterpret_cast<int8_t *>(tb) + tl * 16;
         r.bstride = QH_Q8KT_BLOCK_BYTES;
         r.cstride = QH_Q8KT_TILE * 16;
-        r.d = reinterpret_cast<float *>(base + qhf_q8kt_d_offset(k, n_tok)) + tok * qhf_q8k_d_stride(k);
+        r.d = reinterpret_cast<float *>(tb + QH_Q8KT_D_OFF) + tl;
+        r.dstride = QH_Q8KT_BLOCK_BYTES / 4;
         r.bs = nullptr;
+        r.mins = reinterpret_cast<int8_t *>(tb + QH_Q8KT_MIN_OFF) + tl * 16;
     }
     return r;
 }
 __device__ __forceinline__ int8_t *q8k_elem(const Q8KRow &r, int b, int p) {
     return r.qs + static_cast<int64_t>(b) * r.bstride + (p >> 4) * r.cstride + (p & 15);
+}
+__device__ __forceinline__ float *q8k_scale(const Q8KRow &r, int b) { return r.d + static_cast<int64_t>(b) * r.dstride; }
+
+// Tiled layout: the min operand entries of sub-block j (the 32 quants of
+// one warp-aligned group), given their sum S; bytes 8..15 of both rows are
+// zeroed by the caller for j == 0.
+__device__ __forceinline__ void q8k_put_min(const Q8KRow &r, int b, int j, int S) {
+    int8_t *m = r.mins + static_cast<int64_t>(b) * r.bstride;
+    m[j] = static_cast<int8_t>(S & 127);
+    m[QH_Q8KT_TILE * 16 + j] = static_cast<int8_t>(S >> 7);
+    if (j == 0) {
+        *reinterpret_cast<uint2 *>(m + 8) = make_uint2(0u, 0u);
+        *reinterpret_cast<uint2 *>(m + QH_Q8KT_TILE * 16 + 8) = make_uint2(0u, 0u);
+    }
 }
 
 struct Q8KScratch {
@@ -101,16 +122,19 @@ __device__ __forceinline__ void q8k_block256(float v, Q8KScratch &sc, const Q8KR
     if (xmax != 0.0f) {
         const float iscale = __fdiv_rn(-127.0f, xmax);
         q = q8k_value(v, iscale);
-        if (tid == 0) r.d[b] = __fdiv_rn(1.0f, iscale);
+        if (tid == 0) *q8k_scale(r, b) = __fdiv_rn(1.0f, iscale);
     } else if (tid == 0) {
-        r.d[b] = 0.0f;
+        *q8k_scale(r, b) = 0.0f;
     }
     *q8k_elem(r, b, tid) = static_cast<int8_t>(q);
-    if (r.bs) {
-        int s = q;
+    int s = q;
 #pragma unroll
-        for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (r.bs) {
         if ((lane & 15) == 0) r.bs[b * 16 + warp * 2 + (lane >> 4)] = static_cast<int16_t>(s);
+    } else {
+        s += __shfl_xor_sync(0xffffffffu, s, 16);  // sub-block (warp) sum
+        if (lane == 0) q8k_put_min(r, b, warp, s);
     }
     __syncthreads();
 }

@@ -33,9 +33,16 @@
 
 #define MAX_LAYERS 128
 
+// The projections sharing one activation buffer. B <= 8: one grouped
+// matvec plan (weights streamed once per step, GEMV kernel). B > 8: one
+// grouped tensor-core GEMM over tiled weights (qh_gemm).
 typedef struct {
-    qh_matvec_plan plan[8];  // one per 8-token chunk set (see make_plan)
+    qh_matvec_plan plan[1];
     int nplan;
+    int gemm, type, njobs;
+    int64_t k;
+    const void *xq;
+    qh_gemm_job jobs[8];
 } plan_set;
 
 typedef struct {
@@ -55,6 +62,8 @@ typedef struct {
 struct qh_slm {
     qh_slm_config cfg;
     int32_t B;
+    int use_gemm;   // B > 8: tensor-core GEMM over tiled weights and activations
+    int xq_tile;    // activation layout the fused quantizers write (0 split, 64 tiled)
     cudaStream_t stream;
     void **allocs;
     int nallocs, capallocs;
@@ -116,36 +125,50 @@ static int upload(qh_slm *m, const qh_blob *blob, const char *name, const void *
     return QH_OK;
 }
 
-// A plan over `nm` matrices of one type sharing the activation buffer xq
-// (quantized for B rows of k). B <= 8: one job per matrix with n_tok = B;
-// B > 8 (a multiple of 8): one job per (matrix, 8-row chunk).
+// A plan over `nm` (<= 8) matrices of one type sharing the activation
+// buffer xq (quantized for B rows of k; split layout for the GEMV, tiled
+// for the GEMM). The GEMM path packs each matrix into its tiled order here.
 static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *const *w,
                      const int64_t *out_f, float *const *out, const void *xq, int64_t k) {
     const int32_t B = m->B;
-    const int chunks = B <= 8 ? 1 : B / 8;
-    const int nt = B <= 8 ? B : 8;
-    qh_matvec_job *jobs = (qh_matvec_job *)calloc((size_t)nm * chunks, sizeof(qh_matvec_job));
-    if (!jobs) return QH_ERR_INVALID;
-    int n = 0;
-    for (int c = 0; c < chunks; ++c)
+    if (nm > 8) return QH_ERR_INVALID;
+    if (m->use_gemm) {
+        ps->gemm = 1;
+        ps->type = type;
+        ps->njobs = nm;
+        ps->k = k;
+        ps->xq = xq;
         for (int i = 0; i < nm; ++i) {
-            jobs[n].d_w = w[i];
-            jobs[n].d_xq = xq;
-            jobs[n].d_out = out[i] + (int64_t)c * nt * out_f[i];
-            jobs[n].k = k;
-            jobs[n].out_f = out_f[i];
-            jobs[n].xq_rows = B;
-            jobs[n].xq_row0 = (int64_t)c * nt;
-            ++n;
+            const int64_t wb = qh_gemm_weight_bytes(type, k, out_f[i]);
+            if (wb < 0) return QH_ERR_INVALID;
+            void *wt;
+            CK(dev_alloc(m, &wt, (size_t)wb, NULL));
+            CK(qh_gemm_pack_weights(type, w[i], k, out_f[i], wt, m->stream));
+            ps->jobs[i].d_wt = wt;
+            ps->jobs[i].out_f = out_f[i];
+            ps->jobs[i].d_out = out[i];
+            ps->jobs[i].ld_out = out_f[i];
         }
-    int rc = qh_matvec_plan_create(type, jobs, n, nt, &ps->plan[0]);
-    free(jobs);
-    if (rc) return rc;
+        return QH_OK;
+    }
+    qh_matvec_job jobs[8];
+    memset(jobs, 0, sizeof(jobs));
+    for (int i = 0; i < nm; ++i) {
+        jobs[i].d_w = w[i];
+        jobs[i].d_xq = xq;
+        jobs[i].d_out = out[i];
+        jobs[i].k = k;
+        jobs[i].out_f = out_f[i];
+        jobs[i].xq_rows = B;
+        jobs[i].xq_row0 = 0;
+    }
+    CK(qh_matvec_plan_create(type, jobs, nm, B, &ps->plan[0]));
     ps->nplan = 1;
     return QH_OK;
 }
 
 static int run_plans(qh_slm *m, plan_set *ps) {
+    if (ps->gemm) return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, m->B, m->stream);
     for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
     return QH_OK;
 }
@@ -214,7 +237,7 @@ static int bind_layers(qh_slm *m, const qh_blob *blob) {
 static int alloc_f(qh_slm *m, float **p, int64_t n) { return dev_alloc(m, (void **)p, (size_t)n * 4, NULL); }
 
 int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, qh_slm **out) {
-    if (!cfg || !blob || !out || n_seq <= 0 || (n_seq > 8 && n_seq % 8) || cfg->n_layers > MAX_LAYERS ||
+    if (!cfg || !blob || !out || n_seq <= 0 || n_seq > 65535 || cfg->n_layers > MAX_LAYERS ||
         cfg->n_heads % cfg->n_kv_heads || cfg->max_pos <= 0)
         return QH_ERR_INVALID;
     *out = NULL;
@@ -222,6 +245,8 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
     if (!m) return QH_ERR_INVALID;
     m->cfg = *cfg;
     m->B = n_seq;
+    m->use_gemm = n_seq > 8;
+    m->xq_tile = m->use_gemm ? QH_Q8KT_TILE_TOKENS : 0;
     int rc = QH_OK;
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
 #define TRY(x) do { rc = (x); if (rc) goto fail; } while (0)
@@ -257,9 +282,12 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         TRY(alloc_f(m, &m->fact, B * F));
         TRY(alloc_f(m, &m->logits, B * cfg->vocab));
         const int64_t max_in = H > qdim ? H : qdim;
-        TRY(dev_alloc(m, &m->xq_h, (size_t)qh_q8k_bytes(max_in, B), NULL));
-        TRY(dev_alloc(m, &m->xq_gdn, (size_t)qh_q8k_bytes(kdim, B), NULL));
-        TRY(dev_alloc(m, &m->xq_ffn, (size_t)qh_q8k_bytes(F, B), NULL));
+        {
+            int64_t (*xq_bytes)(int64_t, int64_t) = m->use_gemm ? qh_q8kt_bytes : qh_q8k_bytes;
+            TRY(dev_alloc(m, &m->xq_h, (size_t)xq_bytes(max_in, B), NULL));
+            TRY(dev_alloc(m, &m->xq_gdn, (size_t)xq_bytes(kdim, B), NULL));
+            TRY(dev_alloc(m, &m->xq_ffn, (size_t)xq_bytes(F, B), NULL));
+        }
         TRY(dev_alloc(m, (void **)&m->d_tok, (size_t)B * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_next, (size_t)B * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_ctl, 16, NULL));
@@ -391,7 +419,7 @@ static int forward(qh_slm *m) {
     const float *pending = NULL;  // residual branch output not yet added to h
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        CK(qh_rmsnorm_q8k(m->h, pending, Ly->attn_norm, H, B, c->norm_eps, m->xq_h, 0, s));
+        CK(qh_rmsnorm_q8k(m->h, pending, Ly->attn_norm, H, B, c->norm_eps, m->xq_h, m->xq_tile, s));
         CK(run_plans(m, &Ly->p_in));
         if (Ly->is_attn) {
             const int64_t ai = Ly->attn_index;
@@ -402,23 +430,24 @@ static int forward(qh_slm *m) {
                            s));
             CK(qh_attn_decode(m->aq, kc, vc, m->agate, B, c->n_heads, c->n_kv_heads, (int32_t)hd, m->d_ctl,
                               c->max_pos, m->actx, s));
-            CK(qh_quantize_q8k(m->actx, qdim, B, m->xq_h, s));
+            CK(m->use_gemm ? qh_quantize_q8kt(m->actx, qdim, B, m->xq_h, s)
+                           : qh_quantize_q8k(m->actx, qdim, B, m->xq_h, s));
         } else {
             const int64_t gi = Ly->gdn_index;
             float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
             CK(qh_gdn_fused(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
                             Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps, m->d_ctl,
-                            m->xq_gdn, 0, s));
+                            m->xq_gdn, m->xq_tile, s));
         }
         CK(run_plans(m, &Ly->p_out));
-        CK(qh_rmsnorm_q8k(m->h, m->mix, Ly->ffn_norm, H, B, c->norm_eps, m->xq_h, 0, s));
+        CK(qh_rmsnorm_q8k(m->h, m->mix, Ly->ffn_norm, H, B, c->norm_eps, m->xq_h, m->xq_tile, s));
         CK(run_plans(m, &Ly->p_ffn));
-        CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, 0, s));
+        CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, m->xq_tile, s));
         CK(run_plans(m, &Ly->p_down));
         pending = m->mix;
     }
-    CK(qh_rmsnorm_q8k(m->h, pending, m->out_norm, H, B, c->norm_eps, m->xq_h, 0, s));
+    CK(qh_rmsnorm_q8k(m->h, pending, m->out_norm, H, B, c->norm_eps, m->xq_h, m->xq_tile, s));
     CK(run_plans(m, &m->p_head));
     CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
                       m->d_tok, m->d_picks, s));

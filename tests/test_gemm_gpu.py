@@ -111,21 +111,28 @@ def test_gemm_rejects_q8_0_and_small_workspace(qh, cuda):
 
 
 def test_quantize_q8kt_matches_split_layout(qh, cuda):
-    """The tiled quantizer writes the same quants and scales as qh_quantize_q8k."""
+    """The tiled quantizer writes the same quants and scales as qh_quantize_q8k,
+    and min-operand rows that encode the sub-block sums of the bsums."""
     k, n_tok = 1024, 70
     x_np = qh.host.synth_normal(n_tok * k, 9, 0.0, 3.0).reshape(n_tok, k)
     x = qh.host.to_device(x_np)
     split = qh.host.quantize_q8k(x, k, n_tok)
     tiled = qh.host.quantize_q8kt(x, k, n_tok)
     cuda.cuda.synchronize()
-    qs, d, _ = qh.host.unpack_q8k(split.cpu().numpy(), k, n_tok)
+    qs, d, bs = qh.host.unpack_q8k(split.cpu().numpy(), k, n_tok)
     t = tiled.cpu().numpy()
-    nb = k // 256
-    tiles = (n_tok + 63) // 64
-    q = t[:tiles * nb * 16384].view(np.int8).reshape(tiles, nb, 16, 64, 16)
+    nb, tiles, TB = k // 256, (n_tok + 63) // 64, 18688
+    assert t.size == tiles * nb * TB
+    blk = t.reshape(tiles, nb, TB)
+    q = blk[:, :, :16384].view(np.int8).reshape(tiles, nb, 16, 64, 16)
     q = q.transpose(0, 3, 1, 2, 4).reshape(tiles * 64, k)[:n_tok]
     assert np.array_equal(q, qs)
-    off = int(qh.lib().qh_q8kt_d_offset(k, n_tok))
-    ds = ((nb + 3) // 4) * 4
-    dt = t[off:off + n_tok * ds * 4].view(np.float32).reshape(n_tok, ds)[:, :nb]
-    assert np.array_equal(dt.view(np.uint32), np.asarray(d, np.float32).reshape(n_tok, -1)[:, :nb].view(np.uint32))
+    dt = blk[:, :, 16384:16640].copy().view(np.float32).reshape(tiles, nb, 64).transpose(0, 2, 1)
+    dt = dt.reshape(tiles * 64, nb)[:n_tok]
+    assert np.array_equal(dt.view(np.uint32), np.asarray(d, np.float32).reshape(n_tok, nb).view(np.uint32))
+    mn = blk[:, :, 16640:].view(np.int8).reshape(tiles, nb, 2, 64, 16).astype(np.int64)
+    S = mn[:, :, 0, :, :8] + 128 * mn[:, :, 1, :, :8]               # [tiles, nb, 64, 8]
+    S = S.transpose(0, 2, 1, 3).reshape(tiles * 64, nb, 8)[:n_tok]
+    want = bs.reshape(n_tok, nb, 8, 2).astype(np.int64).sum(-1)
+    assert np.array_equal(S, want)
+    assert np.all(mn[:, :, :, :n_tok % 64 or 64, 8:] == 0)

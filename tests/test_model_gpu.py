@@ -101,17 +101,19 @@ def test_small_model_batched_sequences_independent(qh, cuda, ref_cr, small):
     slm.close()
 
 
-def test_batch16_matches_batch1(qh, cuda, small):
-    """B > 8 runs the matvecs in 8-row chunks; results equal B = 1 runs."""
+@pytest.mark.parametrize("B", [16, 70])
+def test_batched_gemm_matches_batch1(qh, cuda, small, B):
+    """B > 8 runs every projection on the tensor-core GEMM (B = 70: two
+    64-token tiles, the second ragged); logits equal B = 1 runs bit for bit."""
     cfg, blob, _ = small
-    B, n_prompt, n_new = 16, 6, 6
-    rng = np.random.default_rng(3)
+    n_prompt, n_new = 6, 6
+    rng = np.random.default_rng(3 + B)
     prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
     big = qh.host.Slm(cfg, blob, B)
     gp, gl = gpu_run(big, prompts, n_new)
     big.close()
     one = qh.host.Slm(cfg, blob, 1)
-    for b in (0, 7, 8, 15):
+    for b in sorted({0, 7, 8, B // 2, 63 % B, B - 1}):
         p1, l1 = gpu_run(one, prompts[b:b + 1], n_new)
         assert np.array_equal(p1[0], gp[b])
         assert np.array_equal(l1[0].view(np.uint32), gl[b].view(np.uint32)), f"seq {b} logits differ"
