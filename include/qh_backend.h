@@ -227,9 +227,16 @@ typedef struct qh_gemm_job {
 } qh_gemm_job;
 
 /* Up to 8 jobs of one type sharing the tiled activations (k, n_tok) in one
- * persistent launch. Allocates nothing; asynchronous on `stream`. */
+ * persistent launch; asynchronous on `stream`, allocates nothing. With a
+ * scratch of at least qh_gemm_scratch_bytes (its first 4 KB, the arrival
+ * counters, zero-filled before the first use; every call leaves them at
+ * zero, so one scratch serves calls of any shape), launches with few output
+ * tiles split each tile's super-blocks over several CTAs and add the
+ * per-block terms in block order at the end (same results); d_scratch may
+ * be NULL. Calls sharing a scratch must not overlap on the GPU. */
+int64_t qh_gemm_scratch_bytes(const qh_gemm_job *jobs, int n_jobs, int64_t k, int64_t n_tok);
 int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
-            void *stream);
+            void *d_scratch, int64_t scratch_bytes, void *stream);
 
 /* One-call form of tensor_matmul_*_f32 for n_tok tokens: packs the weights
  * and quantizes the activations into d_work (qh_matmul_gemm_workspace_bytes)

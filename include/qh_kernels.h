@@ -105,11 +105,12 @@ int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int3
  * layout of qh_q8kt_bytes (tensor-core GEMM input). */
 
 /* Optional residual add, RMSNorm and Q8_K quantization in one launch:
- * if d_mix, h += mix (written back); xq = Q8_K(rmsnorm(h) * w)
- * (qh_add + qh_rmsnorm + qh_quantize_q8k; slm/tensor.c:285, 348-369,
- * 683-720). dim a multiple of 256, at most 4096. */
-int qh_rmsnorm_q8k(float *d_h, const float *d_mix, const float *d_w, int64_t dim, int32_t B, float eps,
-                   void *d_xq, int32_t layout_tile, void *stream);
+ * with d_mix, h_out = h + mix and xq = Q8_K(rmsnorm(h_out) * w); without,
+ * xq = Q8_K(rmsnorm(h) * w) and h_out is not touched (qh_add + qh_rmsnorm
+ * + qh_quantize_q8k; slm/tensor.c:285, 348-369, 683-720). h_out must not
+ * alias h. dim a multiple of 256, at most 4096. */
+int qh_rmsnorm_q8k(const float *d_h, const float *d_mix, float *d_h_out, const float *d_w, int64_t dim, int32_t B,
+                   float eps, void *d_xq, int32_t layout_tile, void *stream);
 
 /* xq = Q8_K(silu(gate) * up) for B rows of ffn values (qh_swiglu +
  * qh_quantize_q8k; slm/qwen.c:952-955). */

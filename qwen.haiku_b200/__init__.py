@@ -92,7 +92,8 @@ SIGNATURES = {
     "qh_gemm_pack_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
     "qh_q8kt_bytes": (_I64, [_I64, _I64]),
     "qh_quantize_q8kt": (_I, [_P, _I64, _I64, _P, _P]),
-    "qh_gemm": (_I, [_I, _P, _I, _I64, _P, _I64, _P]),
+    "qh_gemm_scratch_bytes": (_I64, [_P, _I, _I64, _I64]),
+    "qh_gemm": (_I, [_I, _P, _I, _I64, _P, _I64, _P, _I64, _P]),
     "qh_matmul_gemm_workspace_bytes": (_I64, [_I, _I64, _I64, _I64]),
     "qh_matmul_gemm": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_synth_u64": (_U64, [_U64, _U64]),
@@ -147,7 +148,7 @@ SIGNATURES.update({  # include/qh_kernels.h
                             _P, _P]),
     "qh_argmax": (_I, [_P, C.c_int32, _I64, _P, _P]),
     "qh_feed_next": (_I, [_P, _P, C.c_int32, C.c_int32, _P, _P, _P, _P]),
-    "qh_rmsnorm_q8k": (_I, [_P, _P, _P, _I64, C.c_int32, C.c_float, _P, C.c_int32, _P]),
+    "qh_rmsnorm_q8k": (_I, [_P, _P, _P, _P, _I64, C.c_int32, C.c_float, _P, C.c_int32, _P]),
     "qh_swiglu_q8k": (_I, [_P, _P, _I64, C.c_int32, _P, C.c_int32, _P]),
     "qh_gdn_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                           C.c_float, _P, _P, C.c_int32, _P]),

@@ -92,6 +92,18 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
         : "memory");
 }
 
+// 1-D bulk copy shared -> global (bulk-group completion). Writers of the
+// shared source must have executed fence.proxy.async.shared::cta and
+// synchronized with the issuing thread first.
+__device__ __forceinline__ void bulk_copy_s2g(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_addr(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void report_error(int *flag, int code) {
     if (flag != nullptr) atomicCAS(flag, 0, code);
 }

@@ -74,7 +74,10 @@ struct GemmJob {
 
 struct GemmParams {
     int32_t n_jobs, total_items, nb, n_tok, t_tiles, n_stages;
-    const uint8_t *xq;  // tiled Q8_K activations
+    int32_t kchunks, kc_blocks;  // split of the super-blocks of one output tile over CTAs
+    const uint8_t *xq;           // tiled Q8_K activations
+    float *terms;                // split-K: per-block fp32 terms [tile][block][64 tokens][128 rows]
+    unsigned *tickets;           // split-K: arrivals per output tile (left at zero)
     int *err_flag;
     GemmJob jobs[kGemmMaxJobs];
 };
@@ -231,13 +234,25 @@ __device__ __forceinline__ void expand<QH_GGUF_Q6_K>(const uint8_t *raw, int h, 
     }
 }
 
-__device__ __forceinline__ void decode_item(const GemmParams &p, int item, GemmJob &job, int &mt, int &tt) {
-    const int g = item / p.t_tiles;
-    tt = item - g * p.t_tiles;
+// Work item -> (job, row tile mt, token tile tt, output tile index, block
+// range [b0, b1)). The k-chunks of one output tile are consecutive items.
+struct Item {
+    GemmJob job;
+    int mt, tt, tile, b0, b1;
+};
+__device__ __forceinline__ Item decode_item(const GemmParams &p, int item) {
+    Item it;
+    const int kc = item % p.kchunks;
+    it.tile = item / p.kchunks;
+    const int g = it.tile / p.t_tiles;
+    it.tt = it.tile - g * p.t_tiles;
     int j = 0;
     while (j + 1 < p.n_jobs && g >= p.jobs[j + 1].tile_begin) ++j;
-    job = p.jobs[j];
-    mt = g - job.tile_begin;
+    it.job = p.jobs[j];
+    it.mt = g - it.job.tile_begin;
+    it.b0 = kc * p.kc_blocks;
+    it.b1 = min(p.nb, it.b0 + p.kc_blocks);
+    return it;
 }
 
 // Shared-memory plan of one CTA (offsets from the dynamic smem base).
@@ -331,12 +346,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             int i = 0;
             bool stop = false;
             for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
-                GemmJob job;
-                int mt, tt;
-                decode_item(p, item, job, mt, tt);
-                const uint8_t *wsrc = job.wt + static_cast<int64_t>(mt) * p.nb * L::kWB;
-                const uint8_t *xsrc = p.xq + static_cast<int64_t>(tt) * p.nb * QH_Q8KT_BLOCK_BYTES;
-                for (int b = 0; b < p.nb; ++b, ++i) {
+                const Item it = decode_item(p, item);
+                const uint8_t *wsrc = it.job.wt + static_cast<int64_t>(it.mt) * p.nb * L::kWB;
+                const uint8_t *xsrc = p.xq + static_cast<int64_t>(it.tt) * p.nb * QH_Q8KT_BLOCK_BYTES;
+                for (int b = it.b0; b < it.b1; ++b, ++i) {
                     const int s = i % S;
                     if (*abort_flag) { stop = true; break; }
                     if (i >= S && !mbar_wait(&empty[s], (static_cast<uint32_t>(i / S) & 1u) ^ 1u)) {
@@ -364,7 +377,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             int i = 0, ib = 0;
             bool stop = false;
             for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
-                for (int b = 0; b < p.nb; ++b, ++i, ++ib) {
+                const Item it = decode_item(p, item);
+                for (int b = it.b0; b < it.b1; ++b, ++i, ++ib) {
                     const int s = i % S, buf = ib & 1;
                     const uint32_t ph = static_cast<uint32_t>(ib >> 1) & 1u;
                     // expanders done with this block's A buffer and scales; the
@@ -410,7 +424,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         int i = 0, ib = 0;
         bool stop = false;
         for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
-            for (int b = 0; b < p.nb; ++b, ++i, ++ib) {
+            const Item it = decode_item(p, item);
+            for (int b = it.b0; b < it.b1; ++b, ++i, ++ib) {
                 const int s = i % S, buf = ib & 1, ring = ib % kRing;
                 // stage landed; the MMAs two blocks back are done with this A buffer
                 const bool ok = __all_sync(0xffffffffu,
@@ -446,17 +461,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         const int er = 32 * (ew & 3) + lane;  // weight row = TMEM lane
         const int th = ew >> 2;               // token half of the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (ew & 3)) << 16;
+        volatile int &last_flag = *reinterpret_cast<volatile int *>(smem + 264);
+        const bool split = p.kchunks > 1;
         int ib = 0;
         bool stop = false;
         for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
-            GemmJob job;
-            int mt, tt;
-            decode_item(p, item, job, mt, tt);
+            const Item it = decode_item(p, item);
             float acc[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-            const int t0 = tt * kGemmTok + 32 * th;
-            for (int b = 0; b < p.nb; ++b, ++ib) {
+            const int t0 = it.tt * kGemmTok + 32 * th;
+            // split-K: this tile's per-block terms, [block][64 tokens][128 rows]
+            float *tterms = split ? p.terms + static_cast<int64_t>(it.tile) * p.nb * (kGemmTok * kGemmRows) : nullptr;
+            for (int b = it.b0; b < it.b1; ++b, ++ib) {
                 const int buf = ib & 1, ring = ib % kRing;
                 const uint32_t ph = static_cast<uint32_t>(ib >> 1) & 1u;
                 const bool ok = __all_sync(0xffffffffu, mbar_wait(&scale_ready[buf], ph) && mbar_wait(&mma_done[buf], ph));
@@ -490,19 +507,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                             const float d = __fmul_rn(yd, rs.x), dm = __fmul_rn(yd, rs.y);
                             term = __fsub_rn(__fmul_rn(d, __int2float_rn(isum)), __fmul_rn(dm, __int2float_rn(imin)));
                         }
-                        acc[16 * c + j] = __fadd_rn(acc[16 * c + j], term);
+                        if (split)
+                            tterms[(static_cast<int64_t>(b) * kGemmTok + 32 * th + 16 * c + j) * kGemmRows + er] = term;
+                        else
+                            acc[16 * c + j] = __fadd_rn(acc[16 * c + j], term);
                     }
                 }
                 tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[buf]);
             }
-            if (stop) break;
-            const int n = mt * kGemmRows + er;
-            if (n < job.n_rows) {
+            if (split) {
+                // The CTA that brings the tile's last chunk adds every block's
+                // term in block order (the reference's sequential sum). The
+                // barrier also makes a stop of any epilogue warp uniform.
+                __threadfence();
+                if (bar_any(2, 32 * kEpiWarps, stop)) {
+                    stop = true;
+                    break;
+                }
+                if (warp == kExpWarps && lane == 0) {
+                    const unsigned prev = atomicAdd(&p.tickets[it.tile], 1u);
+                    last_flag = prev == static_cast<unsigned>(p.kchunks - 1);
+                    if (last_flag) p.tickets[it.tile] = 0u;
+                }
+                asm volatile("bar.sync 2, %0;" ::"n"(32 * kEpiWarps) : "memory");
+                if (!last_flag) continue;
+                __threadfence();  // acquire the other chunks' terms
+                for (int b = 0; b < p.nb; ++b) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        acc[j] = __fadd_rn(acc[j], __ldcg(tterms + (static_cast<int64_t>(b) * kGemmTok + 32 * th + j) * kGemmRows + er));
+                }
+            } else if (stop) {
+                break;
+            }
+            const int n = it.mt * kGemmRows + er;
+            if (n < it.job.n_rows) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (t0 + j < p.n_tok) job.out[static_cast<int64_t>(t0 + j) * job.ldo + n] = acc[j];
+                    if (t0 + j < p.n_tok) it.job.out[static_cast<int64_t>(t0 + j) * it.job.ldo + n] = acc[j];
             }
         }
         if (stop && lane == 0) {
@@ -559,7 +603,7 @@ static cudaError_t gemm_launch_t(const GemmParams &p0, int sm_count, cudaStream_
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
         cudaError_t e = cudaFuncSetAttribute(gemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kGemmSmemMax);
+                                             L::kTotal);
         if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
@@ -626,13 +670,33 @@ int qh_quantize_q8kt(const float *d_x, int64_t k, int64_t n_tok, void *d_q8kt, v
     return QH_OK;
 }
 
+static int64_t gemm_tiles(const qh_gemm_job *jobs, int n_jobs, int64_t n_tok) {
+    int64_t t = 0;
+    for (int j = 0; j < n_jobs; ++j) t += (jobs[j].out_f + qh::kGemmRows - 1) / qh::kGemmRows;
+    return t * qhf_q8kt_tiles(n_tok);
+}
+
+// Scratch: a fixed area of arrival counters (one per output tile, so calls
+// of different shapes sharing one scratch never see another call's terms in
+// their counters), then the per-block terms.
+constexpr int64_t kMaxSplitTiles = 1024;
+constexpr int64_t kTicketBytes = kMaxSplitTiles * 4;
+
+int64_t qh_gemm_scratch_bytes(const qh_gemm_job *jobs, int n_jobs, int64_t k, int64_t n_tok) {
+    if (!jobs || n_jobs <= 0 || n_jobs > qh::kGemmMaxJobs || k <= 0 || k % 256 || n_tok <= 0) return -1;
+    for (int j = 0; j < n_jobs; ++j)
+        if (jobs[j].out_f <= 0) return -1;
+    const int64_t tiles = std::min(gemm_tiles(jobs, n_jobs, n_tok), kMaxSplitTiles);
+    return kTicketBytes + tiles * (k / 256) * qh::kGemmTok * qh::kGemmRows * 4;
+}
+
 int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
-            void *stream) {
+            void *d_scratch, int64_t scratch_bytes, void *stream) {
     if (!gemm_type_ok(type)) return gfail(QH_ERR_UNSUPPORTED, "gemm: type must be Q4_K, Q5_K or Q6_K");
     if (!jobs || n_jobs <= 0 || n_jobs > qh::kGemmMaxJobs || !d_q8kt || k <= 0 || k % 256 || n_tok <= 0 ||
         n_tok > 65535)
         return gfail(QH_ERR_INVALID, "gemm: bad arguments");
-    if (!al16(d_q8kt)) return gfail(QH_ERR_ALIGN, "gemm: activations not 16-byte aligned");
+    if (!al16(d_q8kt) || (d_scratch && !al16(d_scratch))) return gfail(QH_ERR_ALIGN, "gemm: buffer not 16-byte aligned");
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -662,8 +726,21 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
         tiles += g.m_tiles;
         p.jobs[j] = g;
     }
-    if (tiles * p.t_tiles > 0x7fffffffll) return gfail(QH_ERR_INVALID, "gemm: too many tiles");
-    p.total_items = static_cast<int32_t>(tiles * p.t_tiles);
+    const int64_t out_tiles = tiles * p.t_tiles;
+    // Split the super-blocks of each output tile over several CTAs when the
+    // tiles alone would leave most SMs idle (needs the scratch).
+    p.kchunks = 1;
+    p.kc_blocks = p.nb;
+    const int64_t need = qh_gemm_scratch_bytes(jobs, n_jobs, k, n_tok);
+    if (d_scratch && scratch_bytes >= need && out_tiles < sms / 2 && out_tiles <= kMaxSplitTiles && p.nb > 1) {
+        const int64_t want = std::min<int64_t>(p.nb, (sms + out_tiles - 1) / out_tiles);
+        p.kc_blocks = static_cast<int32_t>((p.nb + want - 1) / want);
+        p.kchunks = static_cast<int32_t>((p.nb + p.kc_blocks - 1) / p.kc_blocks);
+        p.tickets = static_cast<unsigned *>(d_scratch);
+        p.terms = reinterpret_cast<float *>(static_cast<uint8_t *>(d_scratch) + kTicketBytes);
+    }
+    if (out_tiles * p.kchunks > 0x7fffffffll) return gfail(QH_ERR_INVALID, "gemm: too many tiles");
+    p.total_items = static_cast<int32_t>(out_tiles * p.kchunks);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (type) {
         case QH_TYPE_Q4_K: e = qh::gemm_launch_t<QH_GGUF_Q4_K>(p, sms, s); break;
@@ -677,7 +754,8 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
 int64_t qh_matmul_gemm_workspace_bytes(int type, int64_t k, int64_t out_f, int64_t n_tok) {
     const int64_t w = qh_gemm_weight_bytes(type, k, out_f), x = qh_q8kt_bytes(k, n_tok);
     if (w < 0 || x < 0) return -1;
-    return qhf_align16(w) + x;
+    const qh_gemm_job job = {nullptr, out_f, nullptr, out_f};
+    return qhf_align16(w) + qhf_align16(x) + qh_gemm_scratch_bytes(&job, 1, k, n_tok);
 }
 
 int qh_matmul_gemm(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x, int64_t n_tok,
@@ -689,12 +767,17 @@ int qh_matmul_gemm(int type, const void *d_w, int64_t k, int64_t out_f, const fl
     if (!al16(d_work)) return gfail(QH_ERR_ALIGN, "matmul_gemm: workspace not 16-byte aligned");
     uint8_t *wt = static_cast<uint8_t *>(d_work);
     uint8_t *xq = wt + qhf_align16(qh_gemm_weight_bytes(type, k, out_f));
+    uint8_t *scratch = xq + qhf_align16(qh_q8kt_bytes(k, n_tok));
+    qh_gemm_job job = {wt, out_f, d_out, out_f};
+    const int64_t sb = qh_gemm_scratch_bytes(&job, 1, k, n_tok);
+    // the split-K arrival counters start at zero (the kernel leaves them so)
+    cudaError_t e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(kTicketBytes), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return gcuda(e, "matmul_gemm: clear counters");
     int rc = qh_gemm_pack_weights(type, d_w, k, out_f, wt, stream);
     if (rc) return rc;
     rc = qh_quantize_q8kt(d_x, k, n_tok, xq, stream);
     if (rc) return rc;
-    qh_gemm_job job = {wt, out_f, d_out, out_f};
-    return qh_gemm(type, &job, 1, k, xq, n_tok, stream);
+    return qh_gemm(type, &job, 1, k, xq, n_tok, scratch, sb, stream);
 }
 
 }  // extern "C"

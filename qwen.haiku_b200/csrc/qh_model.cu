@@ -525,30 +525,34 @@ int qh_feed_next(const int32_t *d_next, const int32_t *d_prompt, int32_t B, int3
 // ===========================================================================
 namespace qh {
 
-// (optional residual add) + RMSNorm + Q8_K: one 256-thread CTA per row.
-// Same sums as add_kernel, rmsnorm_kernel (256 threads) and
-// quantize_q8k_kernel in sequence.
+// (optional residual add) + RMSNorm + Q8_K. CTA (block j, row), 256
+// threads: every CTA of a row forms the row's sum of squares in the same
+// order (thread t sums elements t, t+256, ... in double, then the block
+// reduction of rmsnorm_kernel with 256 threads), then quantizes its own
+// block; with a residual, CTA j writes h_out's block j (h_out != h, so no
+// CTA reads a value another one has updated).
 constexpr int kResNormMaxBlocks = 16;
-__global__ void __launch_bounds__(256) resnorm_q8k_kernel(float *__restrict__ h, const float *__restrict__ mix,
-                                                          const float *__restrict__ w, int dim, float eps,
-                                                          uint8_t *__restrict__ xq, int n_tok, int tile) {
+__global__ void __launch_bounds__(256) resnorm_q8k_kernel(const float *__restrict__ h, const float *__restrict__ mix,
+                                                          float *__restrict__ h_out, const float *__restrict__ w,
+                                                          int dim, float eps, uint8_t *__restrict__ xq, int n_tok,
+                                                          int tile) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ double scratch[32];
     __shared__ Q8KScratch sc;
-    const int row = blockIdx.x, tid = threadIdx.x, nb = dim / QH_QK;
-    float v[kResNormMaxBlocks];
+    const int jb = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, nb = dim / QH_QK;
+    float mine = 0.0f;
     double s = 0.0;
 #pragma unroll
     for (int j = 0; j < kResNormMaxBlocks; ++j) {
         if (j < nb) {
             const int64_t i = static_cast<int64_t>(row) * dim + j * QH_QK + tid;
             float x = h[i];
-            if (mix) {
-                x = __fadd_rn(x, mix[i]);
-                h[i] = x;
+            if (mix) x = __fadd_rn(x, mix[i]);
+            if (j == jb) {
+                mine = x;
+                if (mix) h_out[i] = x;
             }
-            v[j] = x;
             s += static_cast<double>(__fmul_rn(x, x));
         }
     }
@@ -556,13 +560,7 @@ __global__ void __launch_bounds__(256) resnorm_q8k_kernel(float *__restrict__ h,
     const float rscale =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(dim)), eps)));
     const Q8KRow r = q8k_row(xq, dim, n_tok, row, tile);
-#pragma unroll
-    for (int j = 0; j < kResNormMaxBlocks; ++j) {
-        if (j < nb) {
-            const float y = __fmul_rn(__fmul_rn(v[j], rscale), w[j * QH_QK + tid]);
-            q8k_block256(y, sc, r, j);
-        }
-    }
+    q8k_block256(__fmul_rn(__fmul_rn(mine, rscale), w[jb * QH_QK + tid]), sc, r, jb);
 }
 
 // SwiGLU + Q8_K: CTA (block, row), 256 threads.
@@ -584,16 +582,23 @@ __global__ void __launch_bounds__(256) swiglu_q8k_kernel(const float *__restrict
 // gated-norm output to Q8_K. A Q8_K block (256) spans two heads, so CTAs
 // come in clusters of two along the head axis and agree on the block
 // maximum through distributed shared memory.
+constexpr int kMaxConvTaps = 8;
+
 template <int HD>
 __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     gdn_fused_kernel(const float *__restrict__ qkv, float *__restrict__ ring, const float *__restrict__ conv_w,
                      const float *__restrict__ bb, const float *__restrict__ aa, const float *__restrict__ dt_bias,
                      const float *__restrict__ ssm_a, float *__restrict__ state, const float *__restrict__ z,
                      const float *__restrict__ norm_w, int heads, int kk, float eps,
-                     const int32_t *__restrict__ pos_ptr, uint8_t *__restrict__ xq, int n_tok, int tile) {
+                     const int32_t *__restrict__ pos_ptr, uint8_t *__restrict__ xq, int n_tok, int tile,
+                     int *__restrict__ err_flag) {
     static_assert(HD == 128, "a cluster pair of heads must form one 256-value Q8_K block");
     pdl_launch_dependents();
     pdl_wait();
+    // The head's 64 KB state arrives by one bulk copy while the conv and
+    // norms run, is updated in shared memory and leaves by one bulk store.
+    extern __shared__ __align__(128) float st_s[];  // [HD k][HD v]
+    __shared__ uint64_t st_bar;
     __shared__ double scratch[32];
     __shared__ float Ks[HD], Qs[HD];
     __shared__ float s_beta, s_g;
@@ -603,21 +608,50 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     __shared__ int c_i;
     const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int kdim = heads * HD, conv_dim = 3 * kdim;
+    float *st = state + (static_cast<int64_t>(b) * heads + h) * HD * HD;
+    if (t == 0) {
+        mbar_init(&st_bar, 1);
+        mbar_fence_init();
+        mbar_arrive_expect_tx(&st_bar, HD * HD * 4);
+        bulk_copy_g2s(st_s, st, HD * HD * 4, &st_bar);
+    }
     // ---- conv ring + SiLU + L2 norms + beta/g (gdn_pre_kernel) ----
     const int pos = max(*pos_ptr, 0);
     const int slot = pos % kk, head_after = (pos + 1) % kk;
     const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
     float *rg = ring + static_cast<int64_t>(b) * kk * conv_dim;
+    // beta and g on another warp while the conv runs
+    if (t == 32) {
+        const int i = b * heads + h;
+        s_beta = sigmoid_f(bb[i]);
+        const float a = __fadd_rn(aa[i], dt_bias[h]);
+        const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
+        s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
+    }
+    // All loads first (the kk - 1 older taps from the ring; the newest tap
+    // is the new input itself), then the ring update, then the sums in tap
+    // order -- the same values and order as writing the slot and reading
+    // every tap back.
+    float xin[3], taps[3][kMaxConvTaps - 1], cw[3][kMaxConvTaps];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+        xin[part] = src[ch];
+#pragma unroll
+        for (int k = 0; k < kMaxConvTaps; ++k) {
+            if (k < kk) cw[part][k] = conv_w[ch * kk + k];
+            if (k < kk - 1) taps[part][k] = rg[static_cast<int64_t>((head_after + k) % kk) * conv_dim + ch];
+        }
+    }
     float mixed[3];
 #pragma unroll
     for (int part = 0; part < 3; ++part) {
         const int ch = part * kdim + h * HD + t;
-        rg[static_cast<int64_t>(slot) * conv_dim + ch] = src[ch];
+        rg[static_cast<int64_t>(slot) * conv_dim + ch] = xin[part];
         float acc = 0.0f;
-        for (int k = 0; k < kk; ++k) {
-            const int sl = (head_after + k) % kk;
-            acc = __fadd_rn(acc, __fmul_rn(rg[static_cast<int64_t>(sl) * conv_dim + ch], conv_w[ch * kk + k]));
-        }
+#pragma unroll
+        for (int k = 0; k < kMaxConvTaps; ++k)
+            if (k < kk) acc = __fadd_rn(acc, __fmul_rn(k < kk - 1 ? taps[part][k] : xin[part], cw[part][k]));
         mixed[part] = silu_f(acc);
     }
     const double qss = block_sum_d(static_cast<double>(__fmul_rn(mixed[0], mixed[0])), scratch);
@@ -628,33 +662,31 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     Qs[t] = __fmul_rn(__fmul_rn(mixed[0], qrs), scale);
     Ks[t] = __fmul_rn(mixed[1], krs);
     const float vt = mixed[2];
-    if (t == 0) {
-        const int i = b * heads + h;
-        s_beta = sigmoid_f(bb[i]);
-        const float a = __fadd_rn(aa[i], dt_bias[h]);
-        const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
-        s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
-    }
     __syncthreads();
     // ---- recurrence (gdn_recurrence_kernel): thread v owns state column v ----
-    float *st = state + (static_cast<int64_t>(b) * heads + h) * HD * HD;
+    if (!mbar_wait(&st_bar, 0)) report_error(err_flag, kDevWaitTimeout);
     const float gh = s_g, bh = s_beta;
-    float s[HD];
+    // The column is read from shared memory in both passes (the decayed
+    // value recomputed), which keeps registers low enough for several
+    // heads per SM.
     double acc = 0.0;
-#pragma unroll
-    for (int k = 0; k < HD; ++k) {
-        s[k] = __fmul_rn(st[k * HD + t], gh);
-        acc += static_cast<double>(__fmul_rn(s[k], Ks[k]));
-    }
+#pragma unroll 16
+    for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
     const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
     double acc2 = 0.0;
-#pragma unroll
+#pragma unroll 16
     for (int k = 0; k < HD; ++k) {
-        s[k] = __fadd_rn(s[k], __fmul_rn(Ks[k], delta));
-        st[k * HD + t] = s[k];
-        acc2 += static_cast<double>(__fmul_rn(s[k], Qs[k]));
+        const float sk = __fadd_rn(__fmul_rn(st_s[k * HD + t], gh), __fmul_rn(Ks[k], delta));
+        st_s[k * HD + t] = sk;
+        acc2 += static_cast<double>(__fmul_rn(sk, Qs[k]));
     }
     const float o = static_cast<float>(acc2);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (t == 0) {
+        bulk_copy_s2g(st, st_s, HD * HD * 4);
+        bulk_commit_group();
+    }
     // ---- gated RMSNorm (gdn_gated_norm_kernel) ----
     const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
     const float mean = static_cast<float>(ssq / static_cast<double>(HD));
@@ -708,6 +740,7 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
         sum += __shfl_xor_sync(0xffffffffu, sum, 16);
         if (lane == 0) q8k_put_min(r, blk, half * (HD / 32) + warp, sum);
     }
+    if (t == 0) bulk_wait_all();  // the state store has completed before the CTA exits
 }
 
 // Greedy pick + device-side feed (argmax_kernel + feed_next_kernel) over a
@@ -786,15 +819,14 @@ extern "C" {
 
 static bool tile_ok(int32_t t) { return t == 0 || t == QH_Q8KT_TILE; }
 
-int qh_rmsnorm_q8k(float *d_h, const float *d_mix, const float *d_w, int64_t dim, int32_t B, float eps,
-                   void *d_xq, int32_t layout_tile, void *stream) {
+int qh_rmsnorm_q8k(const float *d_h, const float *d_mix, float *d_h_out, const float *d_w, int64_t dim, int32_t B,
+                   float eps, void *d_xq, int32_t layout_tile, void *stream) {
     if (!d_h || !d_w || !d_xq || dim <= 0 || dim % QH_QK || dim > qh::kResNormMaxBlocks * QH_QK || B <= 0 ||
-        !tile_ok(layout_tile))
+        B > 65535 || !tile_ok(layout_tile) || (d_mix && (!d_h_out || d_h_out == d_h)))
         return bad("qh_rmsnorm_q8k: bad arguments");
-    const cudaError_t le = qh::launch_pdl(qh::resnorm_q8k_kernel, dim3(static_cast<unsigned>(B)), dim3(256), 0,
-                                          static_cast<cudaStream_t>(stream), d_h, d_mix, d_w,
-                                          static_cast<int>(dim), eps, static_cast<uint8_t *>(d_xq), B,
-                                          layout_tile);
+    const cudaError_t le = qh::launch_pdl(qh::resnorm_q8k_kernel, dim3(static_cast<unsigned>(dim / QH_QK), B),
+                                          dim3(256), 0, static_cast<cudaStream_t>(stream), d_h, d_mix, d_h_out, d_w,
+                                          static_cast<int>(dim), eps, static_cast<uint8_t *>(d_xq), B, layout_tile);
     return launch_status(le, "qh_rmsnorm_q8k");
 }
 
@@ -813,16 +845,27 @@ int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const
                  const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
                  const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream) {
     if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_state || !d_z ||
-        !d_norm_w || !d_pos || !d_xq || B <= 0 || heads <= 0 || heads % 2 || kk <= 0 || !tile_ok(layout_tile))
+        !d_norm_w || !d_pos || !d_xq || B <= 0 || heads <= 0 || heads % 2 || kk <= 0 || kk > qh::kMaxConvTaps ||
+        !tile_ok(layout_tile))
         return bad("qh_gdn_fused: bad arguments");
     if (hd != 128) {
         qh::set_last_error_message("qh_gdn_fused: head dim must be 128");
         return QH_ERR_UNSUPPORTED;
     }
+    if (reinterpret_cast<uintptr_t>(d_state) & 15) return bad("qh_gdn_fused: state not 16-byte aligned");
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaFuncSetAttribute(qh::gdn_fused_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
+        attr_done[dev] = true;
+    }
+    int *err = qh::device_error_word();
+    if (!err) return bad("qh_gdn_fused: no device error word");
     const cudaError_t le = qh::launch_pdl(qh::gdn_fused_kernel<128>, dim3(static_cast<unsigned>(B), heads),
-                                          dim3(128), 0, static_cast<cudaStream_t>(stream), d_qkv, d_ring,
-                                          d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, heads,
-                                          kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B, layout_tile);
+                                          dim3(128), 128 * 128 * 4, static_cast<cudaStream_t>(stream), d_qkv,
+                                          d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w,
+                                          heads, kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B, layout_tile, err);
     return launch_status(le, "qh_gdn_fused");
 }
 

@@ -64,6 +64,8 @@ struct qh_slm {
     int32_t B;
     int use_gemm;   // B > 8: tensor-core GEMM over tiled weights and activations
     int xq_tile;    // activation layout the fused quantizers write (0 split, 64 tiled)
+    void *gemm_scratch;            // split-K terms + counters shared by every GEMM of a step
+    int64_t gemm_scratch_bytes;
     cudaStream_t stream;
     void **allocs;
     int nallocs, capallocs;
@@ -73,7 +75,7 @@ struct qh_slm {
     layer L[MAX_LAYERS];
     int n_gdn, n_attn;
     // activations [B][...]
-    float *h, *hn, *mix, *qkv, *z, *bt, *at, *gq, *gk, *gv, *gbeta, *gg, *gout, *gy;
+    float *h, *h2, *hn, *mix, *qkv, *z, *bt, *at, *gq, *gk, *gv, *gbeta, *gg, *gout, *gy;
     float *qraw, *kb, *vb, *aq, *agate, *actx, *fgate, *fup, *fact, *logits, *rope;
     void *xq_h, *xq_gdn, *xq_ffn;  // split Q8_K activations for K = hidden, gdn width, ffn
     int32_t *d_tok, *d_next;
@@ -168,7 +170,9 @@ static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *cons
 }
 
 static int run_plans(qh_slm *m, plan_set *ps) {
-    if (ps->gemm) return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, m->B, m->stream);
+    if (ps->gemm)
+        return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, m->B, m->gemm_scratch, m->gemm_scratch_bytes,
+                       m->stream);
     for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
     return QH_OK;
 }
@@ -258,6 +262,7 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         const int64_t kdim = (int64_t)cfg->gdn_heads * cfg->gdn_head_dim, conv_dim = 3 * kdim;
         const int64_t qdim = (int64_t)cfg->n_heads * hd, kvd = (int64_t)cfg->n_kv_heads * hd;
         TRY(alloc_f(m, &m->h, B * H));
+        TRY(alloc_f(m, &m->h2, B * H));
         TRY(alloc_f(m, &m->hn, B * H));
         TRY(alloc_f(m, &m->mix, B * H));
         TRY(alloc_f(m, &m->qkv, B * conv_dim));
@@ -356,6 +361,31 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         const int64_t ofh[1] = {cfg->vocab};
         float *oh[1] = {m->logits};
         TRY(make_plan(m, &m->p_head, QH_TYPE_Q6_K, 1, wh, ofh, oh, m->xq_h, H));
+        if (m->use_gemm) {
+            int64_t need = 0;
+            plan_set *all[4 * MAX_LAYERS + 1];
+            int na_ = 0;
+            for (int l = 0; l < cfg->n_layers; ++l) {
+                all[na_++] = &m->L[l].p_in;
+                all[na_++] = &m->L[l].p_out;
+                all[na_++] = &m->L[l].p_ffn;
+                all[na_++] = &m->L[l].p_down;
+            }
+            all[na_++] = &m->p_head;
+            for (int i = 0; i < na_; ++i) {
+                // only launches with few output tiles split K (the LM head never does)
+                int64_t tiles = 0;
+                for (int j = 0; j < all[i]->njobs; ++j) tiles += (all[i]->jobs[j].out_f + 127) / 128;
+                tiles *= (B + QH_Q8KT_TILE_TOKENS - 1) / QH_Q8KT_TILE_TOKENS;
+                if (tiles >= 148) continue;
+                const int64_t b = qh_gemm_scratch_bytes(all[i]->jobs, all[i]->njobs, all[i]->k, B);
+                if (b > need) need = b;
+            }
+            if (need == 0) need = 256;
+            TRY(dev_alloc(m, &m->gemm_scratch, (size_t)need, NULL));
+            TRY(qh_memset(m->gemm_scratch, 0, (size_t)need, m->stream));
+            m->gemm_scratch_bytes = need;
+        }
     }
 #undef TRY
     rc = qh_slm_reset(m);
@@ -416,10 +446,19 @@ static int forward(qh_slm *m) {
     const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
     void *s = m->stream;
     CK(qh_embed_q6k(m->tok_embd, H, m->d_tok, B, m->h, s));
-    const float *pending = NULL;  // residual branch output not yet added to h
+    // The residual stream alternates between two buffers: each add writes
+    // h + mix into the other one (the fused kernel reads h from many CTAs).
+    float *hc = m->h, *hx = m->h2;
+    const float *pending = NULL;  // residual branch output not yet added to hc
+#define RESNORM(w, xq)                                                                                 \
+    do {                                                                                               \
+        CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, B, c->norm_eps, (xq), m->xq_tile, s)); \
+        if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                           \
+        pending = NULL;                                                                                \
+    } while (0)
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        CK(qh_rmsnorm_q8k(m->h, pending, Ly->attn_norm, H, B, c->norm_eps, m->xq_h, m->xq_tile, s));
+        RESNORM(Ly->attn_norm, m->xq_h);
         CK(run_plans(m, &Ly->p_in));
         if (Ly->is_attn) {
             const int64_t ai = Ly->attn_index;
@@ -441,13 +480,15 @@ static int forward(qh_slm *m) {
                             m->xq_gdn, m->xq_tile, s));
         }
         CK(run_plans(m, &Ly->p_out));
-        CK(qh_rmsnorm_q8k(m->h, m->mix, Ly->ffn_norm, H, B, c->norm_eps, m->xq_h, m->xq_tile, s));
+        pending = m->mix;
+        RESNORM(Ly->ffn_norm, m->xq_h);
         CK(run_plans(m, &Ly->p_ffn));
         CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, m->xq_tile, s));
         CK(run_plans(m, &Ly->p_down));
         pending = m->mix;
     }
-    CK(qh_rmsnorm_q8k(m->h, pending, m->out_norm, H, B, c->norm_eps, m->xq_h, m->xq_tile, s));
+    RESNORM(m->out_norm, m->xq_h);
+#undef RESNORM
     CK(run_plans(m, &m->p_head));
     CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
                       m->d_tok, m->d_picks, s));

@@ -152,11 +152,19 @@ def quantize_q8kt(x, k: int, n_tok: int):
     return buf
 
 
-def gemm(gtype: int, jobs, k: int, xq, n_tok: int):
-    """qh_gemm over jobs [(wt, out_f, out, ld_out)] sharing tiled activations xq."""
+def gemm(gtype: int, jobs, k: int, xq, n_tok: int, split: bool = True):
+    """qh_gemm over jobs [(wt, out_f, out, ld_out)] sharing tiled activations xq;
+    split=True passes a fresh zeroed scratch so small launches may split K."""
     from . import GemmJob
+    torch = _torch()
     arr = (GemmJob * len(jobs))(*[GemmJob(wt.data_ptr(), out_f, out.data_ptr(), ld) for wt, out_f, out, ld in jobs])
-    check(lib().qh_gemm(gtype, C.cast(arr, C.c_void_p), len(jobs), k, dptr(xq), n_tok, None), "qh_gemm")
+    scratch, nbytes = None, 0
+    if split:
+        nbytes = int(lib().qh_gemm_scratch_bytes(C.cast(arr, C.c_void_p), len(jobs), k, n_tok))
+        scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    check(lib().qh_gemm(gtype, C.cast(arr, C.c_void_p), len(jobs), k, dptr(xq), n_tok,
+                        dptr(scratch) if scratch is not None else None, nbytes, None), "qh_gemm")
+    return scratch
 
 
 def tensor_matmul_q4k_f32(w, out_f, k, x):

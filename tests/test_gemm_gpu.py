@@ -77,6 +77,36 @@ def test_grouped_gemm_with_row_stride(qh, cuda, oracle):
         assert np.all(o[:, out_f:] == -7.0), "wrote past out_f"
 
 
+@pytest.mark.parametrize("gt,k,out_f,n_tok", [(Q6_K, 3584, 1024, 64), (Q4_K, 2048, 1024, 64),
+                                               (Q5_K, 1024, 300, 130), (Q4_K, 256, 128, 1)])
+def test_split_k_equals_unsplit(qh, cuda, oracle, gt, k, out_f, n_tok):
+    """Few output tiles: the super-blocks are split over CTAs and the terms
+    added in block order by the last one -- bit-identical to one CTA per tile
+    and to the oracle. Run twice on one scratch (counters must return to 0)."""
+    w = qh.host.synth_blocks(gt, out_f * (k // 256), 0x5B + k + gt)
+    x_np = qh.host.synth_normal(n_tok * k, 0x5C + k).reshape(n_tok, k)
+    wt = qh.host.gemm_pack(gt, qh.host.to_device(w), k, out_f)
+    xq = qh.host.quantize_q8kt(qh.host.to_device(x_np), k, n_tok)
+    outs = []
+    for split in (False, True):
+        out = cuda.empty((n_tok, out_f), dtype=cuda.float32, device="cuda")
+        scratch = qh.host.gemm(gt, [(wt, out_f, out, out_f)], k, xq, n_tok, split=split)
+        if split:  # second call on the same scratch
+            out2 = cuda.empty_like(out)
+            from qwen_haiku_b200 import GemmJob
+            import ctypes as C
+            arr = (GemmJob * 1)(GemmJob(wt.data_ptr(), out_f, out2.data_ptr(), out_f))
+            qh.check(qh.lib().qh_gemm(gt, C.cast(arr, C.c_void_p), 1, k, C.c_void_p(xq.data_ptr()), n_tok,
+                                      C.c_void_p(scratch.data_ptr()), scratch.numel(), None), "qh_gemm")
+            cuda.cuda.synchronize()
+            assert np.array_equal(bits(out2.cpu().numpy()), bits(out.cpu().numpy()))
+            assert int(scratch[:4096].sum()) == 0, "split-K counters not reset"
+        cuda.cuda.synchronize()
+        outs.append(out.cpu().numpy())
+    assert_bitwise(outs[1], outs[0], "split vs unsplit")
+    assert_bitwise(outs[0], oracle.matmul(gt, w, out_f, k, x_np).reshape(n_tok, out_f), "oracle")
+
+
 @pytest.mark.parametrize("cfg", ["3a", "3b"])
 def test_prefill_configs(qh, cuda, oracle, cfg):
     """Benchmark config 3: M=512 K=1024 N=3584 Q4_K and M=2048 K=3584 N=1024
