@@ -228,6 +228,81 @@ def decode_step_bytes(cfg, B: int, weight_bytes: int, n_prompt: int, n_new: int)
     return weight_bytes + B * (2 * state + 2 * ring + kv)
 
 
+# ---------------------------------------------------------------------------
+# prefill GEMMs (config 3) on the tensor cores
+# ---------------------------------------------------------------------------
+GEMM_CONFIGS = {"3a": (512, 1024, 3584, 12), "3b": (2048, 3584, 1024, 14)}  # M, K, N, GGUF type
+
+
+def tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured bf16 dense (burst)"
+    except Exception:
+        return 1590.0, "fallback bf16 dense"
+
+
+def run_gemm(qh, torch, steps: int, warmup: int):
+    """Config 3: device-resident tiled weights and activations, qh_gemm
+    timed with CUDA events; e2e through qh_matmul_gemm (GGUF weights on the
+    device, fp32 activations from pinned host memory, outputs read back).
+    Ops count 2*M*N*K (int8 multiply-adds of the expanded operands)."""
+    import ctypes as C
+    h, L = qh.host, qh.lib()
+    peak, peak_kind = tensor_peak()
+    out = {}
+    for name, (m, k, n, gt) in GEMM_CONFIGS.items():
+        w = h.to_device(h.synth_blocks(gt, n * (k // 256), 0x3A00 + gt))
+        x_host = torch.from_numpy(h.synth_normal(m * k, 0x3B00 + m).reshape(m, k)).pin_memory()
+        x = x_host.to("cuda")
+        wt = h.gemm_pack(gt, w, k, n)
+        xq = h.quantize_q8kt(x, k, m)
+        o = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        for _ in range(warmup):
+            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        # end to end: host activations in, outputs out, GGUF weights packed per call
+        need = int(L.qh_matmul_gemm_workspace_bytes(gt, k, n, m))
+        work = torch.empty(need, dtype=torch.uint8, device="cuda")
+        o_host = torch.empty((m, n), dtype=torch.float32).pin_memory()
+        sh = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+        def e2e_once():
+            qh.check(L.qh_memcpy_h2d(C.c_void_p(x.data_ptr()), C.c_void_p(x_host.data_ptr()), m * k * 4, sh), "h2d")
+            qh.check(L.qh_matmul_gemm(gt, C.c_void_p(w.data_ptr()), k, n, C.c_void_p(x.data_ptr()), m,
+                                      C.c_void_p(o.data_ptr()), C.c_void_p(work.data_ptr()), need, sh), "matmul_gemm")
+            qh.check(L.qh_memcpy_d2h(C.c_void_p(o_host.data_ptr()), C.c_void_p(o.data_ptr()), m * n * 4, sh), "d2h")
+        for _ in range(2):
+            e2e_once()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            e2e_once()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / steps
+        ops = 2.0 * m * n * k
+        tops = ops / (ms / 1e3) / 1e12
+        out[name] = {"workload": f"M={m} K={k} N={n} {'Q4_K' if gt == 12 else 'Q6_K'} x Q8_K -> fp32",
+                     "ms": round(ms, 4), "tops": round(tops, 2), "tokens_per_s": round(m / (ms / 1e3), 1),
+                     "weight_gbs": round(w.numel() / (ms / 1e3) / 1e9, 1),
+                     "e2e": {"ms": round(ms_e2e, 4), "tokens_per_s": round(m / (ms_e2e / 1e3), 1),
+                             "h2d_bytes": m * k * 4, "d2h_bytes": m * n * 4},
+                     "roofline": {"bound": "tensor", "achieved": round(tops, 2), "peak": peak, "unit": "TOP/s",
+                                  "frac": round(tops / peak, 4), "peak_source": peak_kind + "; int8 MMA nominal is 2x bf16"}}
+        del w, x, wt, xq, o, work
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_new: int):
     """Greedy decode of B sequences per GPU: n_prompt teacher-forced steps,
     then n_new steps timed with CUDA events on the model's stream; the
@@ -454,6 +529,10 @@ def run_ours(args):
     torch.cuda.empty_cache()
 
     # ---- decode of the synthetic model (configs 4 and 5) ----
+    gemm = None
+    if not args.no_gemm and world == 1:
+        gemm = run_gemm(qh, torch, 20, 3)
+
     decode = None
     if not args.no_decode:
         dclk = ClockSampler(uuid)
@@ -517,6 +596,8 @@ def run_ours(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if gemm is not None:
+        line["gemm"] = gemm
     if decode is not None:
         if world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = cpu_decode_baseline(qh)
@@ -537,6 +618,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the model decode measurement")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the prefill GEMM measurement")
     ap.add_argument("--decode-batch", type=int, default=64, help="sequences per GPU of the batched decode")
     ap.add_argument("--decode-new", type=int, default=256, help="greedy tokens per decode run")
     ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens of the batched decode")

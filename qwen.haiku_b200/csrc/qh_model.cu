@@ -330,6 +330,110 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
     ctx[oi] = __fmul_rn(o, sigmoid_f(gate[oi]));
 }
 
+// Attention over the cache for a whole GQA group: CTA (sequence, KV head)
+// of HD threads serves the G query heads sharing that KV head, so every
+// cache row is read once for G heads. Per head the arithmetic and its order
+// are those of attn_decode_kernel (tensor_attention, slm/tensor.c:1049-1102):
+// sequential dot per position, max, exp, sequential sum, scaling, and a
+// sequential weighted sum of V rows per dimension.
+template <int G>
+__global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__restrict__ q, const __half *__restrict__ kcache,
+                                                              const __half *__restrict__ vcache,
+                                                              const float *__restrict__ gate, int nh, int kvh,
+                                                              const int32_t *__restrict__ pos_ptr, int max_pos,
+                                                              float *__restrict__ ctx) {
+    constexpr int HD = 128;
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ float sh[];  // [G][HD] queries, [G][max_pos] scores
+    float *qs = sh;
+    float *sc = sh + G * HD;
+    __shared__ float red[G][32];
+    __shared__ float s_inv[G];
+    const int pos = min(max(*pos_ptr, 0), max_pos - 1);
+    const int b = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int n = pos + 1;
+#pragma unroll
+    for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(static_cast<int64_t>(b) * nh + kh * G + g) * HD + t];
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
+    const int64_t rstride = static_cast<int64_t>(kvh) * HD;
+    const __half *kb = kcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
+    const __half *vb = vcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
+    float lmax[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) lmax[g] = -INFINITY;
+    for (int i = t; i < n; i += blockDim.x) {
+        const uint4 *kr = reinterpret_cast<const uint4 *>(kb + i * rstride);
+        float dot[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) dot[g] = 0.0f;
+#pragma unroll 4
+        for (int c = 0; c < HD / 8; ++c) {
+            const uint4 u = kr[c];
+            const __half2 *hp = reinterpret_cast<const __half2 *>(&u);
+            float kf[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(hp[e]);
+                kf[2 * e] = f.x;
+                kf[2 * e + 1] = f.y;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+#pragma unroll
+                for (int g = 0; g < G; ++g) dot[g] = __fadd_rn(dot[g], __fmul_rn(qs[g * HD + 8 * c + e], kf[e]));
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float s = __fmul_rn(dot[g], scale);
+            sc[g * max_pos + i] = s;
+            lmax[g] = fmaxf(lmax[g], s);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float v = lmax[g];
+        for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) red[g][warp] = v;
+    }
+    __syncthreads();
+    float m[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = red[g][0];
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m[g] = fmaxf(m[g], red[g][w]);
+    }
+    for (int i = t; i < n; i += blockDim.x)
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g * max_pos + i] = expf_cr(__fsub_rn(sc[g * max_pos + i], m[g]));
+    __syncthreads();
+    if (t < G) {  // sequential sums, one head per thread
+        float s = 0.0f;
+        for (int i = 0; i < n; ++i) s = __fadd_rn(s, sc[t * max_pos + i]);
+        s_inv[t] = __fdiv_rn(1.0f, s);
+    }
+    __syncthreads();
+    for (int i = t; i < n; i += blockDim.x)
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g * max_pos + i] = __fmul_rn(sc[g * max_pos + i], s_inv[g]);
+    __syncthreads();
+    float o[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) o[g] = 0.0f;
+#pragma unroll 4
+    for (int i = 0; i < n; ++i) {
+        const float v = __half2float(vb[i * rstride + t]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + i], v));
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int64_t oi = static_cast<int64_t>(b) * nh * HD + (kh * G + g) * HD + t;
+        ctx[oi] = __fmul_rn(o[g], sigmoid_f(gate[oi]));
+    }
+}
+
 // Greedy argmax: one CTA per row; ties keep the smaller index.
 __global__ void argmax_kernel(const float *__restrict__ logits, int64_t vocab, int32_t *__restrict__ out) {
     pdl_launch_dependents();
@@ -484,6 +588,31 @@ int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d
                    const int32_t *d_pos, int32_t max_pos, float *d_ctx, void *stream) {
     if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 1024 || !d_pos || max_pos <= 0)
         return bad("qh_attn_decode: bad arguments");
+    const int G = nh / kvh;
+    if (hd == 128 && (G == 1 || G == 2 || G == 4 || G == 8) && (reinterpret_cast<uintptr_t>(d_kcache) & 15) == 0) {
+        // GQA-group kernel: one CTA per (sequence, KV head)
+        const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + static_cast<size_t>(max_pos));
+        if (smem > 200 * 1024) return bad("qh_attn_decode: context too long");
+        static bool gattr[64][4] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+        void (*kern)(const float *, const __half *, const __half *, const float *, int, int, const int32_t *, int,
+                     float *) = G == 1   ? qh::attn_decode_gqa_kernel<1>
+                                : G == 2 ? qh::attn_decode_gqa_kernel<2>
+                                : G == 4 ? qh::attn_decode_gqa_kernel<4>
+                                         : qh::attn_decode_gqa_kernel<8>;
+        if (dev >= 0 && dev < 64 && !gattr[dev][gi]) {
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            gattr[dev][gi] = true;
+        }
+        const cudaError_t le = qh::launch_pdl(kern, dim3(static_cast<unsigned>(B), kvh), dim3(128), smem,
+                                              static_cast<cudaStream_t>(stream), d_q,
+                                              reinterpret_cast<const __half *>(d_kcache),
+                                              reinterpret_cast<const __half *>(d_vcache), d_gate, nh, kvh, d_pos,
+                                              max_pos, d_ctx);
+        return launch_status(le, "qh_attn_decode");
+    }
     const size_t smem = sizeof(float) * (static_cast<size_t>(hd) + max_pos + 32);
     if (smem > 200 * 1024) return bad("qh_attn_decode: context too long");
     static bool attr_done[64] = {false};
