@@ -229,6 +229,31 @@ def decode_step_bytes(cfg, B: int, weight_bytes: int, n_prompt: int, n_new: int)
 
 
 # ---------------------------------------------------------------------------
+# data-parallel plumbing (one process per GPU; also exercised on CPU/gloo)
+# ---------------------------------------------------------------------------
+def max_over_ranks(dist, values, device):
+    """Element-wise max of a list of floats over all ranks (the job's time is
+    its slowest rank's)."""
+    import torch
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def gather_tokens(dist, local, out):
+    """All-gather of each rank's sampled tokens (int32 [B]) into out
+    [world * B], rank-major. NCCL: one all_gather_into_tensor; other
+    backends: all_gather into views of out."""
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(out, local)
+    else:
+        dist.all_gather(list(out.view(dist.get_world_size(), -1).unbind(0)), local)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # prefill GEMMs (config 3) on the tensor cores
 # ---------------------------------------------------------------------------
 GEMM_CONFIGS = {"3a": (512, 1024, 3584, 12), "3b": (2048, 3584, 1024, 14)}  # M, K, N, GGUF type
@@ -325,7 +350,7 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     def gather():
         if world > 1:
             with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(gathered, nxt)
+                gather_tokens(dist, nxt, gathered)
 
     # warm-up: the first steps run directly, then the step is captured
     slm.begin(prompts)
@@ -352,10 +377,7 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     wall = time.perf_counter() - t0
     torch.cuda.synchronize()
     prefill_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
-    if world > 1:
-        t = torch.tensor([prefill_ms, decode_ms, wall], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        prefill_ms, decode_ms, wall = (float(v) for v in t.tolist())
+    prefill_ms, decode_ms, wall = max_over_ranks(dist, [prefill_ms, decode_ms, wall], "cuda")
     # consistency: the gathered picks of the last step are this rank's picks
     if world > 1:
         mine = gathered.view(world, B)[rank].cpu().numpy()
@@ -465,12 +487,8 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    def max_time(v: float) -> float:
+        return max_over_ranks(dist, [v], "cuda")[0]
 
     # ---- device-resident timing ----
     for _ in range(args.warmup):
@@ -495,7 +513,7 @@ def run_ours(args):
         kev[i][1].record(stream)
     ev1.record(stream)
     barrier()
-    elapsed_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    elapsed_ms = max_time(ev0.elapsed_time(ev1))
     kern_ms = [a.elapsed_time(b) for a, b in kev]
     # ---- end to end through the C-ABI with host buffers ----
     for _ in range(2):
@@ -513,7 +531,7 @@ def run_ours(args):
         qh.check(L.qh_memcpy_d2h(C.c_void_p(out_pin.data_ptr()), C.c_void_p(out.data_ptr()), out.numel() * 4, sh), "d2h")
     e1.record(stream)
     barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_ms = max_time(e0.elapsed_time(e1))
     clk = clocks.stop()
     qh.check(L.qh_check_device_error(None), "device error word")
 

@@ -1,0 +1,69 @@
+# SPDX-License-Identifier: MIT
+"""CPU (gloo, world size 2): the data-parallel plumbing of bench.py --
+max-over-ranks timing, the per-step all-gather of sampled tokens, and the
+reference arm's rank-0-only rule -- without a GPU."""
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        import bench
+        # slowest rank's time wins, element-wise
+        got = bench.max_over_ranks(dist, [1.0 + rank, 10.0 - rank], "cpu")
+        assert got == [float(world), 10.0], got
+        # token gather: rank-major concatenation, repeated over steps
+        B = 5
+        out = torch.empty(world * B, dtype=torch.int32)
+        for step in range(3):
+            local = torch.arange(B, dtype=torch.int32) + 100 * rank + 1000 * step
+            bench.gather_tokens(dist, local, out)
+            want = torch.cat([torch.arange(B, dtype=torch.int32) + 100 * r + 1000 * step for r in range(world)])
+            assert torch.equal(out, want), (out, want)
+        q.put((rank, "ok"))
+    except Exception as e:  # report to the parent instead of hanging the peer
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_collectives_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world, port = 2, _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: "ok", 1: "ok"}, results
+
+
+def test_reference_arm_only_rank0_works(monkeypatch):
+    """Under torchrun the reference arm's non-zero ranks exit 0 at once."""
+    sys.path.insert(0, ROOT)
+    import bench
+    monkeypatch.setenv("RANK", "1")
+
+    class Args:
+        gpus, steps, warmup = 2, 1, 3
+    assert bench.run_reference_arm(Args()) == 0
