@@ -284,13 +284,14 @@ def run_gemm(qh, torch, steps: int, warmup: int):
         wt = h.gemm_pack(gt, w, k, n)
         xq = h.quantize_q8kt(x, k, m)
         o = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()  # packed weights complete: they may stream in early (QH_GEMM_WEIGHTS_READY)
         for _ in range(warmup):
-            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False)
+            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False, flags=1)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False)
+            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False, flags=1)
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / steps

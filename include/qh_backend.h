@@ -235,8 +235,11 @@ typedef struct qh_gemm_job {
  * per-block terms in block order at the end (same results); d_scratch may
  * be NULL. Calls sharing a scratch must not overlap on the GPU. */
 int64_t qh_gemm_scratch_bytes(const qh_gemm_job *jobs, int n_jobs, int64_t k, int64_t n_tok);
+#define QH_GEMM_WEIGHTS_READY 1 /* flags: the tiled weights were complete before the previous
+                                   kernel on the stream started (e.g. packed, then synchronized):
+                                   the kernel streams them in while that kernel finishes */
 int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
-            void *d_scratch, int64_t scratch_bytes, void *stream);
+            void *d_scratch, int64_t scratch_bytes, int32_t flags, void *stream);
 
 /* One-call form of tensor_matmul_*_f32 for n_tok tokens: packs the weights
  * and quantizes the activations into d_work (qh_matmul_gemm_workspace_bytes)

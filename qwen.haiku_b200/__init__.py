@@ -93,7 +93,7 @@ SIGNATURES = {
     "qh_q8kt_bytes": (_I64, [_I64, _I64]),
     "qh_quantize_q8kt": (_I, [_P, _I64, _I64, _P, _P]),
     "qh_gemm_scratch_bytes": (_I64, [_P, _I, _I64, _I64]),
-    "qh_gemm": (_I, [_I, _P, _I, _I64, _P, _I64, _P, _I64, _P]),
+    "qh_gemm": (_I, [_I, _P, _I, _I64, _P, _I64, _P, _I64, C.c_int32, _P]),
     "qh_matmul_gemm_workspace_bytes": (_I64, [_I, _I64, _I64, _I64]),
     "qh_matmul_gemm": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_synth_u64": (_U64, [_U64, _U64]),

@@ -75,6 +75,7 @@ struct GemmJob {
 struct GemmParams {
     int32_t n_jobs, total_items, nb, n_tok, t_tiles, n_stages;
     int32_t kchunks, kc_blocks;  // split of the super-blocks of one output tile over CTAs
+    int32_t w_early;             // weights complete before the previous kernel: stream them before pdl_wait
     const uint8_t *xq;           // tiled Q8_K activations
     float *terms;                // split-K: per-block fp32 terms [tile][block][64 tokens][128 rows]
     unsigned *tickets;           // split-K: arrivals per output tile (left at zero)
@@ -303,6 +304,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     uint64_t *acc_empty = mma_done + 2;
     uint64_t *scale_ready = acc_empty + 2;
     uint64_t *a_ready = scale_ready + 2;
+    uint64_t *xfull = a_ready + 2;  // activation part of a stage landed (full[] covers the weights)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 256);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 260);
     float *tok_scale = reinterpret_cast<float *>(smem + L::kScales);     // [kRing][64]
@@ -316,6 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&xfull[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -329,8 +332,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     }
     for (int i = tid; i < kMinRowBytes / 16; i += kGemmThreads)
         reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0u, 0u, 0u, 0u);
-    // Earlier kernels on the stream finish (and free their TMEM) first.
-    pdl_wait();
+    // A CTA of this kernel never shares an SM with another one (shared
+    // memory), so the TMEM it allocates is free even while the previous
+    // kernel runs. Only the producer waits for earlier kernels (before the
+    // first activation copy, or before any copy unless p.w_early); every other
+    // global access of the kernel follows an activation copy.
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, 2 * kAccCols);
         tc::tmem_relinquish();
@@ -344,13 +350,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         // ----- producer -----
         if (lane == 0) {
             int i = 0;
-            bool stop = false;
+            bool stop = false, waited = !p.w_early;
+            if (waited) pdl_wait();
+            const uint8_t *xpend[kGemmMaxStages];  // activation blocks of the first ring, issued after the wait
+            auto issue_x = [&](int s2, const uint8_t *src) {
+                mbar_arrive_expect_tx(&xfull[s2], L::kXB);
+                bulk_copy_g2s(stages + static_cast<int64_t>(s2) * L::kStage + L::kWB, src, L::kXB, &xfull[s2]);
+            };
             for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
                 const Item it = decode_item(p, item);
                 const uint8_t *wsrc = it.job.wt + static_cast<int64_t>(it.mt) * p.nb * L::kWB;
                 const uint8_t *xsrc = p.xq + static_cast<int64_t>(it.tt) * p.nb * QH_Q8KT_BLOCK_BYTES;
                 for (int b = it.b0; b < it.b1; ++b, ++i) {
                     const int s = i % S;
+                    if (!waited && i == S) {
+                        pdl_wait();
+                        waited = true;
+                        for (int j = 0; j < S; ++j) issue_x(j, xpend[j]);
+                    }
                     if (*abort_flag) { stop = true; break; }
                     if (i >= S && !mbar_wait(&empty[s], (static_cast<uint32_t>(i / S) & 1u) ^ 1u)) {
                         report_error(p.err_flag, kDevWaitTimeout);
@@ -359,40 +376,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                         break;
                     }
                     uint8_t *dst = stages + static_cast<int64_t>(s) * L::kStage;
-                    mbar_arrive_expect_tx(&full[s], L::kWB + L::kXB);
+                    mbar_arrive_expect_tx(&full[s], L::kWB);
                     bulk_copy_g2s(dst, wsrc + static_cast<int64_t>(b) * L::kWB, L::kWB, &full[s]);
-                    bulk_copy_g2s(dst + L::kWB, xsrc + static_cast<int64_t>(b) * QH_Q8KT_BLOCK_BYTES, L::kXB,
-                                  &full[s]);
+                    const uint8_t *xb = xsrc + static_cast<int64_t>(b) * QH_Q8KT_BLOCK_BYTES;
+                    if (waited) issue_x(s, xb);
+                    else xpend[s] = xb;
                 }
             }
+            if (!waited) {  // ended inside the first ring
+                pdl_wait();
+                for (int j = 0; j < i; ++j) issue_x(j, xpend[j]);
+            }
             // Drain: no copy of this CTA stays in flight past its exit.
-            for (int j = max(0, i - S); j < i; ++j)
-                if (!mbar_wait(&full[j % S], static_cast<uint32_t>(j / S) & 1u)) report_error(p.err_flag, kDevWaitTimeout);
+            for (int j = max(0, i - S); j < i; ++j) {
+                const uint32_t ph = static_cast<uint32_t>(j / S) & 1u;
+                if (!mbar_wait(&full[j % S], ph) || !mbar_wait(&xfull[j % S], ph)) report_error(p.err_flag, kDevWaitTimeout);
+            }
         }
     } else if (warp == kMmaWarp) {
-        // ----- MMA issue: one thread -----
-        if (lane == 0) {
-            constexpr uint32_t idesc64 = tc::idesc_i8(kGemmRows, kGemmTok);
-            constexpr uint32_t idesc128 = tc::idesc_i8(kGemmRows, 2 * kGemmTok);
-            int i = 0, ib = 0;
-            bool stop = false;
-            for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
-                const Item it = decode_item(p, item);
-                for (int b = it.b0; b < it.b1; ++b, ++i, ++ib) {
-                    const int s = i % S, buf = ib & 1;
-                    const uint32_t ph = static_cast<uint32_t>(ib >> 1) & 1u;
-                    // expanders done with this block's A buffer and scales; the
-                    // epilogue done with the accumulators two blocks back
-                    const bool ok = !*abort_flag && mbar_wait(&a_ready[buf], ph) &&
-                                    (ib < 2 || mbar_wait(&acc_empty[buf], ph ^ 1u));
-                    if (!ok) {
+        // ----- MMA issue: lane 0; lanes 0-15 also move the token scales -----
+        constexpr uint32_t idesc64 = tc::idesc_i8(kGemmRows, kGemmTok);
+        constexpr uint32_t idesc128 = tc::idesc_i8(kGemmRows, 2 * kGemmTok);
+        int i = 0, ib = 0;
+        bool stop = false;
+        for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
+            const Item it = decode_item(p, item);
+            for (int b = it.b0; b < it.b1; ++b, ++i, ++ib) {
+                const int s = i % S, buf = ib & 1, ring = ib % kRing;
+                const uint32_t ph = static_cast<uint32_t>(ib >> 1) & 1u;
+                // expanders done with this block's A buffer and row scales; the
+                // activations landed; the epilogue done with the accumulators
+                // two blocks back
+                bool ok = true;
+                if (lane == 0)
+                    ok = !*abort_flag && mbar_wait(&a_ready[buf], ph) &&
+                         mbar_wait(&xfull[s], static_cast<uint32_t>(i / S) & 1u) &&
+                         (ib < 2 || mbar_wait(&acc_empty[buf], ph ^ 1u));
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) {
+                    if (lane == 0) {
                         report_error(p.err_flag, kDevWaitTimeout);
                         *abort_flag = 1;
-                        stop = true;
-                        break;
                     }
+                    stop = true;
+                    break;
+                }
+                const uint8_t *xst = stages + static_cast<int64_t>(s) * L::kStage + L::kWB;
+                if (lane < kGemmTok / 4)
+                    reinterpret_cast<uint4 *>(tok_scale + ring * kGemmTok)[lane] =
+                        reinterpret_cast<const uint4 *>(xst + QH_Q8KT_D_OFF)[lane];
+                __syncwarp();
+                if (lane == 0) {
                     tc::fence_after_sync();
-                    const uint8_t *xst = stages + static_cast<int64_t>(s) * L::kStage + L::kWB;
                     const uint32_t a0 = smem_addr(smem + L::kA + buf * L::kABuf), b0 = smem_addr(xst);
                     const uint32_t dcol = tmem + buf * kAccCols;
                     const uint64_t ad0 = tc::smem_desc(a0, kGemmRows * 16, 128);
@@ -413,7 +448,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     }
                     tc::commit(&mma_done[buf]);
                     tc::commit(&empty[s]);
-                    // release the block's scales (written before a_ready) to the epilogue
+                    // release the block's scales (row scales from the expanders,
+                    // token scales from this warp) to the epilogue
                     mbar_arrive(&scale_ready[buf]);
                 }
             }
@@ -443,9 +479,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     row_scale[ring * kGemmRows + r] =
                         make_float2(h2f_bits(dd), TYPE == QH_GGUF_Q6_K ? 0.0f : h2f_bits(dd >> 16));
                 }
-                if (tid < kGemmTok / 4)
-                    reinterpret_cast<uint4 *>(tok_scale + ring * kGemmTok)[tid] =
-                        reinterpret_cast<const uint4 *>(wst + L::kWB + QH_Q8KT_D_OFF)[tid];
                 tc::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&a_ready[buf]);
@@ -691,7 +724,7 @@ int64_t qh_gemm_scratch_bytes(const qh_gemm_job *jobs, int n_jobs, int64_t k, in
 }
 
 int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
-            void *d_scratch, int64_t scratch_bytes, void *stream) {
+            void *d_scratch, int64_t scratch_bytes, int32_t flags, void *stream) {
     if (!gemm_type_ok(type)) return gfail(QH_ERR_UNSUPPORTED, "gemm: type must be Q4_K, Q5_K or Q6_K");
     if (!jobs || n_jobs <= 0 || n_jobs > qh::kGemmMaxJobs || !d_q8kt || k <= 0 || k % 256 || n_tok <= 0 ||
         n_tok > 65535)
@@ -707,6 +740,7 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
     p.n_tok = static_cast<int32_t>(n_tok);
     p.t_tiles = static_cast<int32_t>(qhf_q8kt_tiles(n_tok));
     p.xq = static_cast<const uint8_t *>(d_q8kt);
+    p.w_early = (flags & QH_GEMM_WEIGHTS_READY) ? 1 : 0;
     p.err_flag = qh::device_error_word();
     if (!p.err_flag) return gfail(QH_ERR_CUDA, "gemm: no device error word");
     int64_t tiles = 0;
@@ -777,7 +811,7 @@ int qh_matmul_gemm(int type, const void *d_w, int64_t k, int64_t out_f, const fl
     if (rc) return rc;
     rc = qh_quantize_q8kt(d_x, k, n_tok, xq, stream);
     if (rc) return rc;
-    return qh_gemm(type, &job, 1, k, xq, n_tok, scratch, sb, stream);
+    return qh_gemm(type, &job, 1, k, xq, n_tok, scratch, sb, 0, stream);
 }
 
 }  // extern "C"

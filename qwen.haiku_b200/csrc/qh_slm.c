@@ -172,7 +172,7 @@ static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *cons
 static int run_plans(qh_slm *m, plan_set *ps) {
     if (ps->gemm)
         return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, m->B, m->gemm_scratch, m->gemm_scratch_bytes,
-                       m->stream);
+                       QH_GEMM_WEIGHTS_READY, m->stream);  /* packed at create, then synchronized */
     for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
     return QH_OK;
 }

@@ -152,7 +152,7 @@ def quantize_q8kt(x, k: int, n_tok: int):
     return buf
 
 
-def gemm(gtype: int, jobs, k: int, xq, n_tok: int, split: bool = True):
+def gemm(gtype: int, jobs, k: int, xq, n_tok: int, split: bool = True, flags: int = 0):
     """qh_gemm over jobs [(wt, out_f, out, ld_out)] sharing tiled activations xq;
     split=True passes a fresh zeroed scratch so small launches may split K."""
     from . import GemmJob
@@ -163,7 +163,7 @@ def gemm(gtype: int, jobs, k: int, xq, n_tok: int, split: bool = True):
         nbytes = int(lib().qh_gemm_scratch_bytes(C.cast(arr, C.c_void_p), len(jobs), k, n_tok))
         scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     check(lib().qh_gemm(gtype, C.cast(arr, C.c_void_p), len(jobs), k, dptr(xq), n_tok,
-                        dptr(scratch) if scratch is not None else None, nbytes, None), "qh_gemm")
+                        dptr(scratch) if scratch is not None else None, nbytes, flags, None), "qh_gemm")
     return scratch
 
 

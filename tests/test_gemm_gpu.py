@@ -96,8 +96,9 @@ def test_split_k_equals_unsplit(qh, cuda, oracle, gt, k, out_f, n_tok):
             from qwen_haiku_b200 import GemmJob
             import ctypes as C
             arr = (GemmJob * 1)(GemmJob(wt.data_ptr(), out_f, out2.data_ptr(), out_f))
+            cuda.cuda.synchronize()  # weights and activations complete: the early weight stream is allowed
             qh.check(qh.lib().qh_gemm(gt, C.cast(arr, C.c_void_p), 1, k, C.c_void_p(xq.data_ptr()), n_tok,
-                                      C.c_void_p(scratch.data_ptr()), scratch.numel(), None), "qh_gemm")
+                                      C.c_void_p(scratch.data_ptr()), scratch.numel(), 1, None), "qh_gemm")
             cuda.cuda.synchronize()
             assert np.array_equal(bits(out2.cpu().numpy()), bits(out.cpu().numpy()))
             assert int(scratch[:4096].sum()) == 0, "split-K counters not reset"
