@@ -364,14 +364,17 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
 #pragma unroll
     for (int g = 0; g < G; ++g) lmax[g] = -INFINITY;
     for (int i = t; i < n; i += blockDim.x) {
+        // the whole 256-byte row first (16 loads in flight), then the sums
         const uint4 *kr = reinterpret_cast<const uint4 *>(kb + i * rstride);
+        uint4 row[HD / 8];
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c) row[c] = __ldg(kr + c);
         float dot[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) dot[g] = 0.0f;
-#pragma unroll 4
+#pragma unroll
         for (int c = 0; c < HD / 8; ++c) {
-            const uint4 u = kr[c];
-            const __half2 *hp = reinterpret_cast<const __half2 *>(&u);
+            const __half2 *hp = reinterpret_cast<const __half2 *>(&row[c]);
             float kf[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -421,8 +424,20 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     float o[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) o[g] = 0.0f;
-#pragma unroll 4
-    for (int i = 0; i < n; ++i) {
+    // V rows in chunks of 16 positions: the 16 loads are issued together,
+    // the sums stay sequential in position order
+    constexpr int VC = 16;
+    int i0 = 0;
+    for (; i0 + VC <= n; i0 += VC) {
+        float v[VC];
+#pragma unroll
+        for (int j = 0; j < VC; ++j) v[j] = __half2float(vb[(i0 + j) * rstride + t]);
+#pragma unroll
+        for (int j = 0; j < VC; ++j)
+#pragma unroll
+            for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + i0 + j], v[j]));
+    }
+    for (int i = i0; i < n; ++i) {
         const float v = __half2float(vb[i * rstride + t]);
 #pragma unroll
         for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + i], v));
@@ -802,13 +817,14 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
 #pragma unroll 16
     for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
     const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
+    // update the column first (independent per k), then the output sum
+    // (the sequential double chain) over the updated values
+#pragma unroll 16
+    for (int k = 0; k < HD; ++k)
+        st_s[k * HD + t] = __fadd_rn(__fmul_rn(st_s[k * HD + t], gh), __fmul_rn(Ks[k], delta));
     double acc2 = 0.0;
 #pragma unroll 16
-    for (int k = 0; k < HD; ++k) {
-        const float sk = __fadd_rn(__fmul_rn(st_s[k * HD + t], gh), __fmul_rn(Ks[k], delta));
-        st_s[k * HD + t] = sk;
-        acc2 += static_cast<double>(__fmul_rn(sk, Qs[k]));
-    }
+    for (int k = 0; k < HD; ++k) acc2 += static_cast<double>(__fmul_rn(st_s[k * HD + t], Qs[k]));
     const float o = static_cast<float>(acc2);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
