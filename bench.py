@@ -353,12 +353,12 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
             with torch.cuda.stream(stream):
                 gather_tokens(dist, nxt, gathered)
 
-    # warm-up: the first steps run directly, then the step is captured
-    slm.begin(prompts)
+    # warm-up: the first steps run directly, then the step is captured; a
+    # short prefill allocates the prompt-chunk buffers and tiled weights
+    slm.prefill(prompts[:, :min(n_prompt, 9)])
     for _ in range(3):
         slm.advance(1)
         gather()
-    slm.picks(0, 3)
     slm.reset()
     torch.cuda.synchronize()
     if world > 1:
@@ -366,9 +366,8 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     t0 = time.perf_counter()
-    slm.begin(prompts)
     ev[0].record(stream)
-    slm.advance(n_prompt - 1)
+    slm.prefill(prompts)  # prompt in chunks: tensor-core projections, per-chunk recurrence/attention
     ev[1].record(stream)
     for _ in range(n_new):
         slm.advance(1)

@@ -127,6 +127,35 @@ int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const
                  const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
                  const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Prompt chunks: n_tok tokens of each of n_seq sequences at once, rows
+ * sequence-major (row = s * n_tok + j, position *d_pos + j). Each kernel
+ * performs the per-token arithmetic of its decode counterpart, in the same
+ * order, so a prompt run in chunks leaves the same caches and produces the
+ * same activations as the prompt fed one token per step (the reference's
+ * default prefill in slm_generate_raw, slm/slm.c:280-287).
+ * ---------------------------------------------------------------------- */
+
+/* qh_attn_pre for every prompt row: q/k norms, MRoPE at the row's position,
+ * K and V appended to the caches at rows *d_pos .. *d_pos + n_tok - 1. */
+int qh_attn_prefill_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
+                        const float *d_knorm_w, const float *d_rope, int32_t n_seq, int32_t n_tok, int32_t nh,
+                        int32_t kvh, int32_t hd, int32_t rope_dim, float eps, const int32_t *d_pos, int32_t max_pos,
+                        float *d_q, float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream);
+
+/* Causal attention of every prompt row over cache rows 0 .. its position
+ * (qh_attn_decode per row; needs hd 128 and a query group of 1, 2, 4 or 8). */
+int qh_attn_prefill(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache, const float *d_gate,
+                    int32_t n_seq, int32_t n_tok, int32_t nh, int32_t kvh, int32_t hd, const int32_t *d_pos,
+                    int32_t max_pos, float *d_ctx, void *stream);
+
+/* qh_gdn_fused for n_tok consecutive tokens of each sequence, in token
+ * order, inside one launch (hd 128, conv kernel 4). */
+int qh_gdn_prefill(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
+                   const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
+                   const float *d_norm_w, int32_t n_seq, int32_t n_tok, int32_t heads, int32_t hd, int32_t kk,
+                   float eps, const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream);
+
 /* qh_argmax + qh_feed_next over a grid of CTAs per row (sample_argmax,
  * slm/model.c:401-412). d_scratch holds per-slice partial maxima and ticket
  * counters: qh_argmax_feed_scratch_bytes bytes, zero-filled before the first

@@ -102,10 +102,23 @@ int qh_slm_begin(qh_slm *m, const int32_t *prompt, int32_t n_prompt);
 int qh_slm_advance(qh_slm *m, int32_t n_steps);
 int qh_slm_picks(qh_slm *m, int32_t from_pos, int32_t n, int32_t *out);
 
+/* Prompt in chunks (batched prefill): the same result as qh_slm_begin +
+ * qh_slm_advance(n_prompt - 1) -- the same caches, bit for bit -- with the
+ * projections of many prompt tokens as tensor-core GEMMs and the recurrence
+ * and attention of a chunk in one launch per layer. The last prompt token is
+ * left as the input of the next qh_slm_advance step (position n_prompt - 1);
+ * the picks of the prompt positions are not computed. Needs head dim 128 and
+ * conv kernel 4 (QH_ERR_UNSUPPORTED otherwise). Synchronous. */
+int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt);
+
+/* Tokens per sequence in one prompt chunk (0 = the default: 8192 rows over
+ * all sequences); only before the first qh_slm_prefill. */
+int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq);
+
 /* Greedy generation, the per-step prefill path of slm_generate_raw
- * (slm/slm.c:237-357) for every sequence: the n_prompt tokens are fed one
- * step each and the pick of the last prompt step is the first of the n_new
- * generated tokens; out[s][i] is the i-th generated token of sequence s.
+ * (slm/slm.c:237-357) for every sequence: the prompt runs through
+ * qh_slm_prefill (the same caches as feeding one token per step) and the
+ * pick of the last prompt step is the first of the n_new generated tokens; out[s][i] is the i-th generated token of sequence s.
  * slm_generate_raw re-feeds the last prompt token once more at position
  * n_prompt before its first sample; callers wanting that schedule pass the
  * prompt with its last token repeated. */

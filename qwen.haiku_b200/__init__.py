@@ -126,6 +126,8 @@ SIGNATURES.update({
     "qh_slm_generate": (_I, [_P, _P, C.c_int32, C.c_int32, _P]),
     "qh_slm_memory": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64)]),
     "qh_slm_begin": (_I, [_P, _P, C.c_int32]),
+    "qh_slm_prefill": (_I, [_P, _P, C.c_int32]),
+    "qh_slm_set_prefill_chunk": (_I, [_P, C.c_int32]),
     "qh_slm_advance": (_I, [_P, C.c_int32]),
     "qh_slm_picks": (_I, [_P, C.c_int32, C.c_int32, _P]),
     "qh_slm_stream": (_P, [_P]),
@@ -153,6 +155,12 @@ SIGNATURES.update({  # include/qh_kernels.h
     "qh_gdn_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                           C.c_float, _P, _P, C.c_int32, _P]),
     "qh_argmax_feed_scratch_bytes": (_I64, [C.c_int32, _I64]),
+    "qh_attn_prefill_pre": (_I, [_P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                 C.c_int32, C.c_float, _P, C.c_int32, _P, _P, _P, _P, _P]),
+    "qh_attn_prefill": (_I, [_P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32,
+                             _P, _P]),
+    "qh_gdn_prefill": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                            C.c_int32, C.c_float, _P, _P, C.c_int32, _P]),
     "qh_argmax_feed": (_I, [_P, C.c_int32, _I64, _P, _P, _P, C.c_int32, _P, _P, _P, _P]),
 })
 

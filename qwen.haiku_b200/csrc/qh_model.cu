@@ -238,13 +238,16 @@ __global__ void attn_pre_kernel(const float *__restrict__ qraw, const float *__r
                                 int kvh, int hd, int rope_dim, float eps,
                                 const int32_t *__restrict__ pos_ptr, int max_pos,
                                 float *__restrict__ qout, float *__restrict__ gate,
-                                __half *__restrict__ kcache, __half *__restrict__ vcache) {
+                                __half *__restrict__ kcache, __half *__restrict__ vcache, int rows_per_seq) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ double scratch[32];
     __shared__ float xs[512];
+    // row b holds token (b % rows_per_seq) of sequence b / rows_per_seq, at
+    // position *pos_ptr + b % rows_per_seq (decode: one row per sequence)
     const int b = blockIdx.x, j = blockIdx.y, t = threadIdx.x;
-    const int pos = min(max(*pos_ptr, 0), max_pos - 1);
+    const int seq = b / rows_per_seq;
+    const int pos = min(max(*pos_ptr + b % rows_per_seq, 0), max_pos - 1);
     const bool is_q = j < nh;
     float x;
     if (is_q) {
@@ -273,7 +276,7 @@ __global__ void attn_pre_kernel(const float *__restrict__ qraw, const float *__r
         qout[(static_cast<int64_t>(b) * nh + j) * hd + t] = y;
     } else {
         const int kh = j - nh;
-        const int64_t row = ((static_cast<int64_t>(b) * max_pos + pos) * kvh + kh) * hd + t;
+        const int64_t row = ((static_cast<int64_t>(seq) * max_pos + pos) * kvh + kh) * hd + t;
         kcache[row] = __float2half_rn(y);
         vcache[row] = __float2half_rn(vin[static_cast<int64_t>(b) * kvh * hd + kh * hd + t]);
     }
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
                                                               const __half *__restrict__ vcache,
                                                               const float *__restrict__ gate, int nh, int kvh,
                                                               const int32_t *__restrict__ pos_ptr, int max_pos,
-                                                              float *__restrict__ ctx) {
+                                                              float *__restrict__ ctx, int rows_per_seq) {
     constexpr int HD = 128;
     pdl_launch_dependents();
     pdl_wait();
@@ -350,11 +353,14 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     float *sc = sh + G * HD;
     __shared__ float red[G][32];
     __shared__ float s_inv[G];
-    const int pos = min(max(*pos_ptr, 0), max_pos - 1);
+    // CTA (sequence b, KV head kh, query j): the query row b * rows_per_seq + j
+    // at position *pos_ptr + j (decode: j = 0, one row per sequence)
     const int b = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int64_t qrow = static_cast<int64_t>(b) * rows_per_seq + blockIdx.z;
+    const int pos = min(max(*pos_ptr + static_cast<int>(blockIdx.z), 0), max_pos - 1);
     const int n = pos + 1;
 #pragma unroll
-    for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(static_cast<int64_t>(b) * nh + kh * G + g) * HD + t];
+    for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(qrow * nh + kh * G + g) * HD + t];
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
     const int64_t rstride = static_cast<int64_t>(kvh) * HD;
@@ -444,7 +450,7 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const int64_t oi = static_cast<int64_t>(b) * nh * HD + (kh * G + g) * HD + t;
+        const int64_t oi = qrow * nh * HD + (kh * G + g) * HD + t;
         ctx[oi] = __fmul_rn(o[g], sigmoid_f(gate[oi]));
     }
 }
@@ -584,18 +590,92 @@ int qh_gdn_gated_norm(const float *d_x, const float *d_z, const float *d_w, int3
     return launch_status(le, "qh_gdn_gated_norm");
 }
 
+}  // extern "C"
+
+namespace {
+// rows = n_seq * rows_per_seq query rows (sequence-major), positions
+// *d_pos + (row % rows_per_seq).
+int attn_pre_impl(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
+                  const float *d_knorm_w, const float *d_rope, int32_t rows, int32_t rows_per_seq, int32_t nh,
+                  int32_t kvh, int32_t hd, int32_t rope_dim, float eps, const int32_t *d_pos, int32_t max_pos,
+                  float *d_q, float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream, const char *what) {
+    if (rows <= 0 || rows_per_seq <= 0 || rows % rows_per_seq || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 ||
+        hd > 512 || rope_dim > hd || rope_dim % 2 || !d_pos || max_pos <= 0)
+        return bad(what);
+    dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(nh + kvh));
+    const cudaError_t le = qh::launch_pdl(qh::attn_pre_kernel, dim3(grid), dim3(hd), 0, static_cast<cudaStream_t>(stream),
+        d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, nh, kvh, hd, rope_dim, eps, d_pos, max_pos, d_q, d_gate,
+        reinterpret_cast<__half *>(d_kcache), reinterpret_cast<__half *>(d_vcache), rows_per_seq);
+    return launch_status(le, what);
+}
+
+bool gqa_ok(int32_t nh, int32_t kvh, int32_t hd, const void *kc) {
+    const int G = nh / kvh;
+    return hd == 128 && (G == 1 || G == 2 || G == 4 || G == 8) && (reinterpret_cast<uintptr_t>(kc) & 15) == 0;
+}
+
+int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache, const float *d_gate,
+                  int32_t n_seq, int32_t rows_per_seq, int32_t nh, int32_t kvh, const int32_t *d_pos,
+                  int32_t max_pos, float *d_ctx, void *stream, const char *what) {
+    const int G = nh / kvh;
+    const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + static_cast<size_t>(max_pos));
+    if (smem > 200 * 1024) return bad("attention: context too long");
+    if (rows_per_seq > 65535) return bad(what);
+    static bool gattr[64][4] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+    void (*kern)(const float *, const __half *, const __half *, const float *, int, int, const int32_t *, int, float *,
+                 int) = G == 1   ? qh::attn_decode_gqa_kernel<1>
+                        : G == 2 ? qh::attn_decode_gqa_kernel<2>
+                        : G == 4 ? qh::attn_decode_gqa_kernel<4>
+                                 : qh::attn_decode_gqa_kernel<8>;
+    if (dev >= 0 && dev < 64 && !gattr[dev][gi]) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        gattr[dev][gi] = true;
+    }
+    const cudaError_t le = qh::launch_pdl(kern, dim3(static_cast<unsigned>(n_seq), kvh, rows_per_seq), dim3(128), smem,
+                                          static_cast<cudaStream_t>(stream), d_q,
+                                          reinterpret_cast<const __half *>(d_kcache),
+                                          reinterpret_cast<const __half *>(d_vcache), d_gate, nh, kvh, d_pos, max_pos,
+                                          d_ctx, rows_per_seq);
+    return launch_status(le, what);
+}
+}  // namespace
+
+extern "C" {
+
 int qh_attn_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
                 const float *d_knorm_w, const float *d_rope, int32_t B, int32_t nh, int32_t kvh,
                 int32_t hd, int32_t rope_dim, float eps, const int32_t *d_pos, int32_t max_pos,
                 float *d_q, float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream) {
-    if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 512 || rope_dim > hd || rope_dim % 2 ||
-        !d_pos || max_pos <= 0)
-        return bad("qh_attn_pre: bad arguments");
-    dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>(nh + kvh));
-    const cudaError_t le = qh::launch_pdl(qh::attn_pre_kernel, dim3(grid), dim3(hd), 0, static_cast<cudaStream_t>(stream), 
-        d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, nh, kvh, hd, rope_dim, eps, d_pos, max_pos, d_q, d_gate,
-        reinterpret_cast<__half *>(d_kcache), reinterpret_cast<__half *>(d_vcache));
-    return launch_status(le, "qh_attn_pre");
+    return attn_pre_impl(d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, B, 1, nh, kvh, hd, rope_dim, eps, d_pos,
+                         max_pos, d_q, d_gate, d_kcache, d_vcache, stream, "qh_attn_pre: bad arguments");
+}
+
+int qh_attn_prefill_pre(const float *d_qraw, const float *d_k, const float *d_v, const float *d_qnorm_w,
+                        const float *d_knorm_w, const float *d_rope, int32_t n_seq, int32_t n_tok, int32_t nh,
+                        int32_t kvh, int32_t hd, int32_t rope_dim, float eps, const int32_t *d_pos, int32_t max_pos,
+                        float *d_q, float *d_gate, uint16_t *d_kcache, uint16_t *d_vcache, void *stream) {
+    if (n_seq <= 0 || n_tok <= 0 || static_cast<int64_t>(n_seq) * n_tok > 0x7fffffff)
+        return bad("qh_attn_prefill_pre: bad arguments");
+    return attn_pre_impl(d_qraw, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope, n_seq * n_tok, n_tok, nh, kvh, hd, rope_dim,
+                         eps, d_pos, max_pos, d_q, d_gate, d_kcache, d_vcache, stream,
+                         "qh_attn_prefill_pre: bad arguments");
+}
+
+int qh_attn_prefill(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache, const float *d_gate,
+                    int32_t n_seq, int32_t n_tok, int32_t nh, int32_t kvh, int32_t hd, const int32_t *d_pos,
+                    int32_t max_pos, float *d_ctx, void *stream) {
+    if (n_seq <= 0 || n_tok <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || !d_pos || max_pos <= 0 || !d_q ||
+        !d_kcache || !d_vcache || !d_gate || !d_ctx)
+        return bad("qh_attn_prefill: bad arguments");
+    if (!gqa_ok(nh, kvh, hd, d_kcache)) {
+        qh::set_last_error_message("qh_attn_prefill: needs head dim 128 and a query group of 1, 2, 4 or 8");
+        return QH_ERR_UNSUPPORTED;
+    }
+    return attn_gqa_impl(d_q, d_kcache, d_vcache, d_gate, n_seq, n_tok, nh, kvh, d_pos, max_pos, d_ctx, stream,
+                         "qh_attn_prefill");
 }
 
 int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache,
@@ -603,31 +683,9 @@ int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d
                    const int32_t *d_pos, int32_t max_pos, float *d_ctx, void *stream) {
     if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 1024 || !d_pos || max_pos <= 0)
         return bad("qh_attn_decode: bad arguments");
-    const int G = nh / kvh;
-    if (hd == 128 && (G == 1 || G == 2 || G == 4 || G == 8) && (reinterpret_cast<uintptr_t>(d_kcache) & 15) == 0) {
-        // GQA-group kernel: one CTA per (sequence, KV head)
-        const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + static_cast<size_t>(max_pos));
-        if (smem > 200 * 1024) return bad("qh_attn_decode: context too long");
-        static bool gattr[64][4] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
-        void (*kern)(const float *, const __half *, const __half *, const float *, int, int, const int32_t *, int,
-                     float *) = G == 1   ? qh::attn_decode_gqa_kernel<1>
-                                : G == 2 ? qh::attn_decode_gqa_kernel<2>
-                                : G == 4 ? qh::attn_decode_gqa_kernel<4>
-                                         : qh::attn_decode_gqa_kernel<8>;
-        if (dev >= 0 && dev < 64 && !gattr[dev][gi]) {
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            gattr[dev][gi] = true;
-        }
-        const cudaError_t le = qh::launch_pdl(kern, dim3(static_cast<unsigned>(B), kvh), dim3(128), smem,
-                                              static_cast<cudaStream_t>(stream), d_q,
-                                              reinterpret_cast<const __half *>(d_kcache),
-                                              reinterpret_cast<const __half *>(d_vcache), d_gate, nh, kvh, d_pos,
-                                              max_pos, d_ctx);
-        return launch_status(le, "qh_attn_decode");
-    }
+    if (gqa_ok(nh, kvh, hd, d_kcache))  // one CTA per (sequence, KV head)
+        return attn_gqa_impl(d_q, d_kcache, d_vcache, d_gate, B, 1, nh, kvh, d_pos, max_pos, d_ctx, stream,
+                             "qh_attn_decode");
     const size_t smem = sizeof(float) * (static_cast<size_t>(hd) + max_pos + 32);
     if (smem > 200 * 1024) return bad("qh_attn_decode: context too long");
     static bool attr_done[64] = {false};
@@ -888,6 +946,167 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     if (t == 0) bulk_wait_all();  // the state store has completed before the CTA exits
 }
 
+// Gated DeltaNet over a chunk of n_tok prompt tokens per sequence: CTA
+// (sequence, head) runs, token after token, exactly the per-token work of
+// gdn_fused_kernel (same operations and order), with the head's state in
+// shared memory for the whole chunk and the conv history in registers, so
+// a prompt costs one launch per layer and chunk instead of one per token.
+// Rows are sequence-major: row = sequence * n_tok + j at position *pos_ptr + j.
+template <int HD, int KK>
+__global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
+    gdn_prefill_kernel(const float *__restrict__ qkv, float *__restrict__ ring, const float *__restrict__ conv_w,
+                       const float *__restrict__ bb, const float *__restrict__ aa, const float *__restrict__ dt_bias,
+                       const float *__restrict__ ssm_a, float *__restrict__ state, const float *__restrict__ z,
+                       const float *__restrict__ norm_w, int heads, float eps, const int32_t *__restrict__ pos_ptr,
+                       int n_tok, uint8_t *__restrict__ xq, int n_rows, int tile, int *__restrict__ err_flag) {
+    static_assert(HD == 128, "a cluster pair of heads must form one 256-value Q8_K block");
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ __align__(128) float st_s[];  // [HD k][HD v]
+    __shared__ uint64_t st_bar;
+    __shared__ double scratch[32];
+    __shared__ float Ks[HD], Qs[HD];
+    __shared__ float s_beta, s_g;
+    __shared__ float wa[HD / 32], wv[HD / 32];
+    __shared__ int wi[HD / 32];
+    __shared__ float c_a, c_v;
+    __shared__ int c_i;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int half = static_cast<int>(cluster.block_rank());
+    const int kdim = heads * HD, conv_dim = 3 * kdim;
+    float *st = state + (static_cast<int64_t>(b) * heads + h) * HD * HD;
+    if (t == 0) {
+        mbar_init(&st_bar, 1);
+        mbar_fence_init();
+        mbar_arrive_expect_tx(&st_bar, HD * HD * 4);
+        bulk_copy_g2s(st_s, st, HD * HD * 4, &st_bar);
+    }
+    const int pos0 = max(*pos_ptr, 0);
+    float *rg = ring + static_cast<int64_t>(b) * KK * conv_dim;
+    // conv history of this thread's 3 channels, oldest first: positions
+    // pos0-(KK-1) .. pos0-1, which the ring holds in slots (pos0+1+k) % KK
+    float hist[3][KK - 1], cw[3][KK];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+#pragma unroll
+        for (int k = 0; k < KK; ++k) cw[part][k] = conv_w[ch * KK + k];
+#pragma unroll
+        for (int k = 0; k < KK - 1; ++k) hist[part][k] = rg[static_cast<int64_t>((pos0 + 1 + k) % KK) * conv_dim + ch];
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
+    bool have_state = false;
+    for (int j = 0; j < n_tok; ++j) {
+        const int64_t row = static_cast<int64_t>(b) * n_tok + j;
+        if (t == 32) {
+            const int64_t i = row * heads + h;
+            s_beta = sigmoid_f(bb[i]);
+            const float a = __fadd_rn(aa[i], dt_bias[h]);
+            const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
+            s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
+        }
+        float mixed[3];
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const float x = qkv[row * conv_dim + part * kdim + h * HD + t];
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < KK; ++k)
+                acc = __fadd_rn(acc, __fmul_rn(k < KK - 1 ? hist[part][k] : x, cw[part][k]));
+#pragma unroll
+            for (int k = 0; k < KK - 2; ++k) hist[part][k] = hist[part][k + 1];
+            hist[part][KK - 2] = x;
+            mixed[part] = silu_f(acc);
+        }
+        const double qss = block_sum_d(static_cast<double>(__fmul_rn(mixed[0], mixed[0])), scratch);
+        const double kss = block_sum_d(static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+        const float qrs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qss)), 1e-6f));
+        const float krs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(kss)), 1e-6f));
+        Qs[t] = __fmul_rn(__fmul_rn(mixed[0], qrs), scale);
+        Ks[t] = __fmul_rn(mixed[1], krs);
+        const float vt = mixed[2];
+        __syncthreads();
+        if (!have_state) {
+            if (!mbar_wait(&st_bar, 0)) report_error(err_flag, kDevWaitTimeout);
+            have_state = true;
+        }
+        const float gh = s_g, bh = s_beta;
+        double acc = 0.0;
+#pragma unroll 16
+        for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
+        const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
+#pragma unroll 16
+        for (int k = 0; k < HD; ++k)
+            st_s[k * HD + t] = __fadd_rn(__fmul_rn(st_s[k * HD + t], gh), __fmul_rn(Ks[k], delta));
+        double acc2 = 0.0;
+#pragma unroll 16
+        for (int k = 0; k < HD; ++k) acc2 += static_cast<double>(__fmul_rn(st_s[k * HD + t], Qs[k]));
+        const float o = static_cast<float>(acc2);
+        const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
+        const float mean = static_cast<float>(ssq / static_cast<double>(HD));
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        const float y = __fmul_rn(__fmul_rn(__fmul_rn(o, rs), norm_w[t]), silu_f(z[row * kdim + h * HD + t]));
+        float a = (y == y) ? fabsf(y) : -1.0f, bv = y;
+        int bi = half * HD + t;
+        warp_best(a, bi, bv);
+        if (lane == 0) { wa[warp] = a; wi[warp] = bi; wv[warp] = bv; }
+        __syncthreads();
+        if (t == 0) {
+            float ca = wa[0], cv = wv[0];
+            int ci = wi[0];
+            for (int w = 1; w < HD / 32; ++w) best_merge(ca, ci, cv, wa[w], wi[w], wv[w]);
+            c_a = ca; c_i = ci; c_v = cv;
+        }
+        cluster.sync();
+        float ba = c_a, xv = c_v;
+        int ii = c_i;
+        best_merge(ba, ii, xv, *cluster.map_shared_rank(&c_a, half ^ 1), *cluster.map_shared_rank(&c_i, half ^ 1),
+                   *cluster.map_shared_rank(&c_v, half ^ 1));
+        cluster.sync();  // the partner has read this CTA's candidate; Ks/Qs/scales free for the next token
+        const float xmax = ba > 0.0f ? xv : 0.0f;
+        const Q8KRow r = q8k_row(xq, kdim, n_rows, row, tile);
+        const int blk = h >> 1;
+        int q = 0;
+        if (xmax != 0.0f) {
+            const float iscale = __fdiv_rn(-127.0f, xmax);
+            q = q8k_value(y, iscale);
+            if (half == 0 && t == 0) *q8k_scale(r, blk) = __fdiv_rn(1.0f, iscale);
+        } else if (half == 0 && t == 0) {
+            *q8k_scale(r, blk) = 0.0f;
+        }
+        *q8k_elem(r, blk, half * HD + t) = static_cast<int8_t>(q);
+        int sum = q;
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if (r.bs) {
+            if ((lane & 15) == 0)
+                r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+        } else {
+            sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+            if (lane == 0) q8k_put_min(r, blk, half * (HD / 32) + warp, sum);
+        }
+    }
+    if (!have_state && t == 0 && !mbar_wait(&st_bar, 0)) report_error(err_flag, kDevWaitTimeout);
+    // conv history back to the ring slots of the last KK-1 positions
+    const int last = pos0 + n_tok - 1;
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+#pragma unroll
+        for (int k = 0; k < KK - 1; ++k)
+            rg[static_cast<int64_t>(((last - (KK - 2) + k) % KK + KK) % KK) * conv_dim + ch] = hist[part][k];
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (t == 0) {
+        bulk_copy_s2g(st, st_s, HD * HD * 4);
+        bulk_commit_group();
+        bulk_wait_all();
+    }
+}
+
 // Greedy pick + device-side feed (argmax_kernel + feed_next_kernel) over a
 // grid of (parts, rows): each CTA scans one slice of the row, the last CTA
 // of a row (ticket counter) merges the slices in order, records the pick
@@ -1012,6 +1231,35 @@ int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const
                                           d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w,
                                           heads, kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B, layout_tile, err);
     return launch_status(le, "qh_gdn_fused");
+}
+
+int qh_gdn_prefill(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
+                   const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
+                   const float *d_norm_w, int32_t n_seq, int32_t n_tok, int32_t heads, int32_t hd, int32_t kk,
+                   float eps, const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream) {
+    if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_state || !d_z ||
+        !d_norm_w || !d_pos || !d_xq || n_seq <= 0 || n_tok <= 0 || static_cast<int64_t>(n_seq) * n_tok > 0x7fffffff ||
+        heads <= 0 || heads % 2 || !tile_ok(layout_tile))
+        return bad("qh_gdn_prefill: bad arguments");
+    if (hd != 128 || kk != 4) {
+        qh::set_last_error_message("qh_gdn_prefill: head dim must be 128 and the conv kernel 4");
+        return QH_ERR_UNSUPPORTED;
+    }
+    if (reinterpret_cast<uintptr_t>(d_state) & 15) return bad("qh_gdn_prefill: state not 16-byte aligned");
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaFuncSetAttribute(qh::gdn_prefill_kernel<128, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
+        attr_done[dev] = true;
+    }
+    int *err = qh::device_error_word();
+    if (!err) return bad("qh_gdn_prefill: no device error word");
+    const cudaError_t le = qh::launch_pdl(qh::gdn_prefill_kernel<128, 4>, dim3(static_cast<unsigned>(n_seq), heads),
+                                          dim3(128), 128 * 128 * 4, static_cast<cudaStream_t>(stream), d_qkv, d_ring,
+                                          d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, heads, eps,
+                                          d_pos, n_tok, static_cast<uint8_t *>(d_xq), n_seq * n_tok, layout_tile, err);
+    return launch_status(le, "qh_gdn_prefill");
 }
 
 static int argmax_parts(int64_t vocab) {

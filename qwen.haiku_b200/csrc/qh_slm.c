@@ -85,6 +85,16 @@ struct qh_slm {
     int32_t *h_tok, *h_next, *h_ctl;  // pinned
     int32_t host_pos;              // position of the next step
     int32_t n_prompt;
+    // tiled copies of the weights (tensor-core path), by raw pointer
+    struct { const void *raw; void *wt; } tiled[4 * MAX_LAYERS * 4 + 8];
+    int ntiled;
+    // prompt chunks (qh_slm_prefill), allocated on first use
+    int32_t pf_chunk, pf_chunk_max;
+    float *pf_h, *pf_h2, *pf_mix, *pf_qkv, *pf_z, *pf_bt, *pf_at, *pf_qraw, *pf_kb, *pf_vb, *pf_aq, *pf_agate,
+        *pf_actx, *pf_fgate, *pf_fup;
+    void *pf_xq_h, *pf_xq_gdn, *pf_xq_ffn;
+    int32_t *pf_tok, *pf_pos;
+    plan_set pf_in[MAX_LAYERS], pf_out[MAX_LAYERS], pf_ffn[MAX_LAYERS], pf_down[MAX_LAYERS];
     // The whole step is captured once in a CUDA graph (after one direct run
     // has set every kernel attribute) and replayed; position and tokens are
     // read from device memory, so one graph serves every position.
@@ -127,6 +137,44 @@ static int upload(qh_slm *m, const qh_blob *blob, const char *name, const void *
     return QH_OK;
 }
 
+// Tiled copy of a weight matrix for the tensor-core GEMM, packed on first
+// request and shared by the decode and prompt plans.
+static int get_tiled(qh_slm *m, const void *raw, int type, int64_t k, int64_t out_f, const void **wt) {
+    for (int i = 0; i < m->ntiled; ++i)
+        if (m->tiled[i].raw == raw) { *wt = m->tiled[i].wt; return QH_OK; }
+    if (m->ntiled >= (int)(sizeof(m->tiled) / sizeof(m->tiled[0]))) return QH_ERR_INVALID;
+    const int64_t wb = qh_gemm_weight_bytes(type, k, out_f);
+    if (wb < 0) return QH_ERR_INVALID;
+    void *d;
+    CK(dev_alloc(m, &d, (size_t)wb, NULL));
+    CK(qh_gemm_pack_weights(type, raw, k, out_f, d, m->stream));
+    m->tiled[m->ntiled].raw = raw;
+    m->tiled[m->ntiled].wt = d;
+    m->ntiled++;
+    *wt = d;
+    return QH_OK;
+}
+
+// GEMM job set over tiled weights (outputs [rows][out_f]).
+static int make_gemm_set(qh_slm *m, plan_set *ps, int type, int nm, const void *const *w, const int64_t *out_f,
+                         float *const *out, const void *xq, int64_t k) {
+    if (nm > 8) return QH_ERR_INVALID;
+    ps->gemm = 1;
+    ps->type = type;
+    ps->njobs = nm;
+    ps->k = k;
+    ps->xq = xq;
+    for (int i = 0; i < nm; ++i) {
+        const void *wt;
+        CK(get_tiled(m, w[i], type, k, out_f[i], &wt));
+        ps->jobs[i].d_wt = wt;
+        ps->jobs[i].out_f = out_f[i];
+        ps->jobs[i].d_out = out[i];
+        ps->jobs[i].ld_out = out_f[i];
+    }
+    return QH_OK;
+}
+
 // A plan over `nm` (<= 8) matrices of one type sharing the activation
 // buffer xq (quantized for B rows of k; split layout for the GEMV, tiled
 // for the GEMM). The GEMM path packs each matrix into its tiled order here.
@@ -134,25 +182,7 @@ static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *cons
                      const int64_t *out_f, float *const *out, const void *xq, int64_t k) {
     const int32_t B = m->B;
     if (nm > 8) return QH_ERR_INVALID;
-    if (m->use_gemm) {
-        ps->gemm = 1;
-        ps->type = type;
-        ps->njobs = nm;
-        ps->k = k;
-        ps->xq = xq;
-        for (int i = 0; i < nm; ++i) {
-            const int64_t wb = qh_gemm_weight_bytes(type, k, out_f[i]);
-            if (wb < 0) return QH_ERR_INVALID;
-            void *wt;
-            CK(dev_alloc(m, &wt, (size_t)wb, NULL));
-            CK(qh_gemm_pack_weights(type, w[i], k, out_f[i], wt, m->stream));
-            ps->jobs[i].d_wt = wt;
-            ps->jobs[i].out_f = out_f[i];
-            ps->jobs[i].d_out = out[i];
-            ps->jobs[i].ld_out = out_f[i];
-        }
-        return QH_OK;
-    }
+    if (m->use_gemm) return make_gemm_set(m, ps, type, nm, w, out_f, out, xq, k);
     qh_matvec_job jobs[8];
     memset(jobs, 0, sizeof(jobs));
     for (int i = 0; i < nm; ++i) {
@@ -581,14 +611,187 @@ int qh_slm_picks(qh_slm *m, int32_t from_pos, int32_t n, int32_t *out) {
     return qh_check_device_error(NULL);
 }
 
+// ---------------------------------------------------------------------------
+// Prompt chunks: every projection of B x C prompt tokens as one tensor-core
+// GEMM, the recurrence and attention per token inside one launch per layer.
+// Bit-identical to feeding the prompt one token per step.
+// ---------------------------------------------------------------------------
+#define PF_MAX_ROWS 8192
+
+static int ensure_prefill(qh_slm *m) {
+    if (m->pf_chunk) return QH_OK;
+    const qh_slm_config *c = &m->cfg;
+    const int64_t B = m->B;
+    int64_t C = m->pf_chunk_max > 0 ? m->pf_chunk_max : PF_MAX_ROWS / B;
+    if (C < 1) C = 1;
+    if (C > c->max_pos) C = c->max_pos;
+    const int64_t M = B * C, H = c->hidden, F = c->ffn, hd = c->head_dim;
+    const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
+    const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
+    CK(alloc_f(m, &m->pf_h, M * H));
+    CK(alloc_f(m, &m->pf_h2, M * H));
+    CK(alloc_f(m, &m->pf_mix, M * H));
+    CK(alloc_f(m, &m->pf_qkv, M * conv_dim));
+    CK(alloc_f(m, &m->pf_z, M * kdim));
+    CK(alloc_f(m, &m->pf_bt, M * c->gdn_heads));
+    CK(alloc_f(m, &m->pf_at, M * c->gdn_heads));
+    CK(alloc_f(m, &m->pf_qraw, M * 2 * qdim));
+    CK(alloc_f(m, &m->pf_kb, M * kvd));
+    CK(alloc_f(m, &m->pf_vb, M * kvd));
+    CK(alloc_f(m, &m->pf_aq, M * qdim));
+    CK(alloc_f(m, &m->pf_agate, M * qdim));
+    CK(alloc_f(m, &m->pf_actx, M * qdim));
+    CK(alloc_f(m, &m->pf_fgate, M * F));
+    CK(alloc_f(m, &m->pf_fup, M * F));
+    const int64_t max_in = H > qdim ? H : qdim;
+    CK(dev_alloc(m, &m->pf_xq_h, (size_t)qh_q8kt_bytes(max_in, M), NULL));
+    CK(dev_alloc(m, &m->pf_xq_gdn, (size_t)qh_q8kt_bytes(kdim, M), NULL));
+    CK(dev_alloc(m, &m->pf_xq_ffn, (size_t)qh_q8kt_bytes(F, M), NULL));
+    CK(dev_alloc(m, (void **)&m->pf_tok, (size_t)M * 4, NULL));
+    CK(dev_alloc(m, (void **)&m->pf_pos, 16, NULL));
+    for (int l = 0; l < c->n_layers; ++l) {
+        layer *Ly = &m->L[l];
+        if (Ly->is_attn) {
+            const void *w[3] = {Ly->wq, Ly->wk, Ly->wv};
+            const int64_t of[3] = {2 * qdim, kvd, kvd};
+            float *o[3] = {m->pf_qraw, m->pf_kb, m->pf_vb};
+            CK(make_gemm_set(m, &m->pf_in[l], QH_TYPE_Q4_K, 3, w, of, o, m->pf_xq_h, H));
+            const void *w2[1] = {Ly->wo};
+            const int64_t of2[1] = {H};
+            float *o2[1] = {m->pf_mix};
+            CK(make_gemm_set(m, &m->pf_out[l], QH_TYPE_Q4_K, 1, w2, of2, o2, m->pf_xq_h, qdim));
+        } else {
+            const void *w[4] = {Ly->qkv, Ly->gate, Ly->beta, Ly->alpha};
+            const int64_t of[4] = {conv_dim, kdim, c->gdn_heads, c->gdn_heads};
+            float *o[4] = {m->pf_qkv, m->pf_z, m->pf_bt, m->pf_at};
+            CK(make_gemm_set(m, &m->pf_in[l], QH_TYPE_Q4_K, 4, w, of, o, m->pf_xq_h, H));
+            const void *w2[1] = {Ly->ssm_out};
+            const int64_t of2[1] = {H};
+            float *o2[1] = {m->pf_mix};
+            CK(make_gemm_set(m, &m->pf_out[l], QH_TYPE_Q4_K, 1, w2, of2, o2, m->pf_xq_gdn, kdim));
+        }
+        const void *wf[2] = {Ly->ffn_gate, Ly->ffn_up};
+        const int64_t off[2] = {F, F};
+        float *of_[2] = {m->pf_fgate, m->pf_fup};
+        CK(make_gemm_set(m, &m->pf_ffn[l], QH_TYPE_Q4_K, 2, wf, off, of_, m->pf_xq_h, H));
+        const void *wd[1] = {Ly->ffn_down};
+        const int64_t ofd[1] = {H};
+        float *od[1] = {m->pf_mix};
+        CK(make_gemm_set(m, &m->pf_down[l], QH_TYPE_Q6_K, 1, wd, ofd, od, m->pf_xq_ffn, F));
+    }
+    CK(qh_stream_sync(m->stream));  // tiled weights complete before any early weight stream
+    m->pf_chunk = (int32_t)C;
+    return QH_OK;
+}
+
+static int run_pf(qh_slm *m, plan_set *ps, int64_t rows) {
+    return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, rows, NULL, 0, QH_GEMM_WEIGHTS_READY, m->stream);
+}
+
+// One chunk of cn tokens per sequence at positions *pf_pos .. + cn - 1;
+// tokens in pf_tok (row = s * cn + j). Leaves caches, ring and state as cn
+// decode steps would; computes no logits.
+static int forward_prefill(qh_slm *m, int32_t cn) {
+    const qh_slm_config *c = &m->cfg;
+    const int32_t B = m->B;
+    const int64_t M = (int64_t)B * cn, H = c->hidden, F = c->ffn, hd = c->head_dim;
+    const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
+    const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
+    void *s = m->stream;
+    const int32_t T = QH_Q8KT_TILE_TOKENS;
+    CK(qh_embed_q6k(m->tok_embd, H, m->pf_tok, (int32_t)M, m->pf_h, s));
+    float *hc = m->pf_h, *hx = m->pf_h2;
+    const float *pending = NULL;
+#define PF_RESNORM(w, xq)                                                                                  \
+    do {                                                                                                   \
+        CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, (int32_t)M, c->norm_eps, (xq), T, s)); \
+        if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                               \
+        pending = NULL;                                                                                    \
+    } while (0)
+    for (int l = 0; l < c->n_layers; ++l) {
+        layer *Ly = &m->L[l];
+        PF_RESNORM(Ly->attn_norm, m->pf_xq_h);
+        CK(run_pf(m, &m->pf_in[l], M));
+        if (Ly->is_attn) {
+            const int64_t ai = Ly->attn_index;
+            uint16_t *kc = m->kcache + ai * B * c->max_pos * kvd;
+            uint16_t *vc = m->vcache + ai * B * c->max_pos * kvd;
+            CK(qh_attn_prefill_pre(m->pf_qraw, m->pf_kb, m->pf_vb, Ly->q_norm, Ly->k_norm, m->rope, B, cn,
+                                   c->n_heads, c->n_kv_heads, (int32_t)hd, c->rope_dim, c->norm_eps, m->pf_pos,
+                                   c->max_pos, m->pf_aq, m->pf_agate, kc, vc, s));
+            CK(qh_attn_prefill(m->pf_aq, kc, vc, m->pf_agate, B, cn, c->n_heads, c->n_kv_heads, (int32_t)hd,
+                               m->pf_pos, c->max_pos, m->pf_actx, s));
+            CK(qh_quantize_q8kt(m->pf_actx, qdim, M, m->pf_xq_h, s));
+        } else {
+            const int64_t gi = Ly->gdn_index;
+            float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
+            float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
+            CK(qh_gdn_prefill(m->pf_qkv, ring, Ly->conv_w, m->pf_bt, m->pf_at, Ly->dt_bias, Ly->ssm_a, state,
+                              m->pf_z, Ly->ssm_norm, B, cn, c->gdn_heads, c->gdn_head_dim, c->conv_kernel,
+                              c->norm_eps, m->pf_pos, m->pf_xq_gdn, T, s));
+        }
+        CK(run_pf(m, &m->pf_out[l], M));
+        pending = m->pf_mix;
+        PF_RESNORM(Ly->ffn_norm, m->pf_xq_h);
+        CK(run_pf(m, &m->pf_ffn[l], M));
+        CK(qh_swiglu_q8k(m->pf_fgate, m->pf_fup, F, (int32_t)M, m->pf_xq_ffn, T, s));
+        CK(run_pf(m, &m->pf_down[l], M));
+        pending = m->pf_mix;
+    }
+#undef PF_RESNORM
+    return QH_OK;
+}
+
+int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq) {
+    if (!m || max_tokens_per_seq < 0) return QH_ERR_INVALID;
+    if (m->pf_chunk) return max_tokens_per_seq == 0 || max_tokens_per_seq == m->pf_chunk ? QH_OK : QH_ERR_INVALID;
+    m->pf_chunk_max = max_tokens_per_seq;
+    return QH_OK;
+}
+
+int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
+    CK(qh_slm_begin(m, prompt, n_prompt));
+    const int32_t n_ctx = n_prompt - 1;  // the last prompt token is the next step's input
+    if (n_ctx == 0) return QH_OK;
+    const qh_slm_config *c = &m->cfg;
+    if (c->head_dim != 128 || c->gdn_head_dim != 128 || c->conv_kernel != 4) return QH_ERR_UNSUPPORTED;
+    CK(ensure_prefill(m));
+    const int32_t B = m->B, C = m->pf_chunk;
+    int32_t *tok = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * C);
+    if (!tok) return QH_ERR_INVALID;
+    int rc = QH_OK;
+    for (int32_t p0 = 0; p0 < n_ctx && !rc; p0 += C) {
+        const int32_t cn = n_ctx - p0 < C ? n_ctx - p0 : C;
+        for (int32_t b = 0; b < B; ++b)
+            for (int32_t j = 0; j < cn; ++j) tok[(int64_t)b * cn + j] = prompt[(int64_t)b * n_prompt + p0 + j];
+        // pageable sources: the copies are staged before these calls return
+        rc = qh_memcpy_h2d(m->pf_tok, tok, sizeof(int32_t) * (size_t)B * cn, m->stream);
+        if (!rc) rc = qh_memcpy_h2d(m->pf_pos, &p0, sizeof(int32_t), m->stream);
+        if (!rc) rc = forward_prefill(m, cn);
+    }
+    free(tok);
+    if (rc) return rc;
+    // next step: position n_ctx, input the last prompt token
+    for (int32_t b = 0; b < B; ++b) m->h_tok[b] = prompt[(int64_t)b * n_prompt + n_ctx];
+    m->h_ctl[0] = n_ctx;
+    m->h_ctl[1] = n_prompt;
+    CK(qh_memcpy_h2d(m->d_ctl, m->h_ctl, 2 * sizeof(int32_t), m->stream));
+    CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * B, m->stream));
+    CK(qh_stream_sync(m->stream));
+    CK(qh_check_device_error(NULL));
+    m->host_pos = n_ctx;
+    return QH_OK;
+}
+
 int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out) {
     if (!m || !prompt || !out || n_prompt <= 0 || n_new < 0 || n_prompt + n_new - 1 > m->cfg.max_pos)
         return QH_ERR_INVALID;
-    CK(qh_slm_begin(m, prompt, n_prompt));
+    // the prompt in chunks (all but its last token), then one step per
+    // token: the step at n_prompt - 1 consumes the last prompt token and
+    // picks the first generated one
+    CK(qh_slm_prefill(m, prompt, n_prompt));
     if (n_new == 0) return QH_OK;
-    // step p consumes the input at p and picks the token for p + 1: the
-    // pick of step n_prompt - 1 is the first generated token
-    CK(qh_slm_advance(m, n_prompt - 1 + n_new));
+    CK(qh_slm_advance(m, n_new));
     return qh_slm_picks(m, n_prompt - 1, n_new, out);
 }
 

@@ -306,6 +306,12 @@ class Slm:
         p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
         check(lib().qh_slm_begin(self.handle, p.ctypes.data, p.shape[1]), "qh_slm_begin")
 
+    def prefill(self, prompt, chunk: int = 0):
+        p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
+        if chunk:
+            check(lib().qh_slm_set_prefill_chunk(self.handle, chunk), "qh_slm_set_prefill_chunk")
+        check(lib().qh_slm_prefill(self.handle, p.ctypes.data, p.shape[1]), "qh_slm_prefill")
+
     def advance(self, n_steps: int):
         check(lib().qh_slm_advance(self.handle, n_steps), "qh_slm_advance")
 

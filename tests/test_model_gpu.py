@@ -151,6 +151,36 @@ def test_device_driven_decode_matches_steps(qh, cuda, small):
     slm.close()
 
 
+@pytest.mark.parametrize("B,chunk", [(1, 0), (3, 4), (16, 5), (70, 0)])
+def test_prefill_matches_step_by_step(qh, cuda, small, B, chunk):
+    """The prompt in chunks (tensor-core projections, recurrence and attention
+    per chunk) leaves the caches of one token per step: the greedy picks and
+    logits that follow are bit-identical."""
+    cfg, blob, _ = small
+    n_prompt, n_new = 13, 6
+    rng = np.random.default_rng(40 + B)
+    prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
+    a = qh.host.Slm(cfg, blob, B)
+    a.begin(prompts)
+    a.advance(n_prompt - 1 + n_new)
+    want = a.picks(n_prompt - 1, n_new)
+    a.close()
+    b = qh.host.Slm(cfg, blob, B)
+    b.prefill(prompts, chunk)
+    b.advance(n_new)
+    got = b.picks(n_prompt - 1, n_new)
+    # the logits of the next step too
+    nxt, lg = b.step(got[:, -1], n_prompt - 1 + n_new, want_logits=True)
+    b.close()
+    assert np.array_equal(got, want), "picks after prefill differ from the step-by-step prompt"
+    c = qh.host.Slm(cfg, blob, B)
+    c.begin(prompts)
+    c.advance(n_prompt - 1 + n_new)
+    nxt2, lg2 = c.step(want[:, -1], n_prompt - 1 + n_new, want_logits=True)
+    c.close()
+    assert np.array_equal(lg.view(np.uint32), lg2.view(np.uint32)), "logits after prefill differ"
+
+
 @pytest.fixture(scope="module")
 def full(qh, cuda):
     cfg = qh.host.slm_config(320)
