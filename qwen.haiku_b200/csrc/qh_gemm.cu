@@ -124,11 +124,13 @@ __device__ __forceinline__ void scale_min(const uint8_t *s12, int sb, int &sc, i
 
 // 4 weights (bytes of w) times a non-negative scale (products < 2^16),
 // split into lo = a & 127 and hi = a >> 7 bytes.
+// Products a < 2^11, so (a >> 7) fits the low byte of each lane and the
+// byte interleave (byte_perm) needs no masking for hi.
 __device__ __forceinline__ void split_pos(uint32_t w, uint32_t sc, uint32_t &hi, uint32_t &lo) {
     const uint32_t p02 = (w & 0x00ff00ffu) * sc;
     const uint32_t p13 = ((w >> 8) & 0x00ff00ffu) * sc;
-    lo = (p02 & 0x007f007fu) | ((p13 & 0x007f007fu) << 8);
-    hi = ((p02 >> 7) & 0x007f007fu) | (((p13 >> 7) & 0x007f007fu) << 8);
+    lo = __byte_perm(p02, p13, 0x6240u) & 0x7f7f7f7fu;
+    hi = __byte_perm(p02 >> 7, p13 >> 7, 0x6240u);
 }
 
 // Expansion of half h (weights 128h..128h+127) of row r's super-block into
@@ -226,9 +228,9 @@ __device__ __forceinline__ void expand<QH_GGUF_Q6_K>(const uint8_t *raw, int h, 
             const uint32_t w02 = (w & 0x00ff00ffu) * a, w13 = ((w >> 8) & 0x00ff00ffu) * a;
             const uint32_t u02 = sc < 0 ? c2 - w02 : c2 + w02;
             const uint32_t u13 = sc < 0 ? c2 - w13 : c2 + w13;
-            lo[k] = (u02 & 0x007f007fu) | ((u13 & 0x007f007fu) << 8);
-            const uint32_t hu = ((u02 >> 7) & 0x007f007fu) | (((u13 >> 7) & 0x007f007fu) << 8);
-            hi[k] = __vsub4(hu, 0x20202020u);
+            // u < 2^14: (u >> 7) fits the low byte of each lane
+            lo[k] = __byte_perm(u02, u13, 0x6240u) & 0x7f7f7f7fu;
+            hi[k] = __vsub4(__byte_perm(u02 >> 7, u13 >> 7, 0x6240u), 0x20202020u);
         }
         put16(planes, c, r, hi[0], hi[1], hi[2], hi[3]);
         put16(planes + kPlaneBytes, c, r, lo[0], lo[1], lo[2], lo[3]);
