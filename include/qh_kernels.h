@@ -156,6 +156,15 @@ int qh_gdn_prefill(const float *d_qkv, float *d_ring, const float *d_conv_w, con
                    const float *d_norm_w, int32_t n_seq, int32_t n_tok, int32_t heads, int32_t hd, int32_t kk,
                    float eps, const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream);
 
+/* qh_gdn_fused without the quantization: the gated-norm output y fp32
+ * [B][heads*hd] for qh_quantize_q8k / qh_quantize_q8kt. The heads are then
+ * independent CTAs (no cluster pairs), which keeps more of them resident
+ * when many sequences run. */
+int qh_gdn_fused_y(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
+                   const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
+                   const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
+                   const int32_t *d_pos, float *d_y, void *stream);
+
 /* qh_argmax + qh_feed_next over a grid of CTAs per row (sample_argmax,
  * slm/model.c:401-412). d_scratch holds per-slice partial maxima and ticket
  * counters: qh_argmax_feed_scratch_bytes bytes, zero-filled before the first

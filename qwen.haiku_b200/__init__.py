@@ -155,6 +155,8 @@ SIGNATURES.update({  # include/qh_kernels.h
     "qh_gdn_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                           C.c_float, _P, _P, C.c_int32, _P]),
     "qh_argmax_feed_scratch_bytes": (_I64, [C.c_int32, _I64]),
+    "qh_gdn_fused_y": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                            C.c_float, _P, _P, _P]),
     "qh_attn_prefill_pre": (_I, [_P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                  C.c_int32, C.c_float, _P, C.c_int32, _P, _P, _P, _P, _P]),
     "qh_attn_prefill": (_I, [_P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32,

@@ -786,14 +786,17 @@ __global__ void __launch_bounds__(256) swiglu_q8k_kernel(const float *__restrict
 // maximum through distributed shared memory.
 constexpr int kMaxConvTaps = 8;
 
-template <int HD>
-__global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
+// QUANT = false: no cluster; the gated-norm output goes to y_out (fp32
+// [B][heads*HD]) for a separate quantizer -- more heads per SM when many
+// sequences run (cluster pairs limit how many CTAs are resident).
+template <int HD, bool QUANT>
+__global__ void __launch_bounds__(HD)
     gdn_fused_kernel(const float *__restrict__ qkv, float *__restrict__ ring, const float *__restrict__ conv_w,
                      const float *__restrict__ bb, const float *__restrict__ aa, const float *__restrict__ dt_bias,
                      const float *__restrict__ ssm_a, float *__restrict__ state, const float *__restrict__ z,
                      const float *__restrict__ norm_w, int heads, int kk, float eps,
                      const int32_t *__restrict__ pos_ptr, uint8_t *__restrict__ xq, int n_tok, int tile,
-                     int *__restrict__ err_flag) {
+                     int *__restrict__ err_flag, float *__restrict__ y_out) {
     static_assert(HD == 128, "a cluster pair of heads must form one 256-value Q8_K block");
     pdl_launch_dependents();
     pdl_wait();
@@ -896,52 +899,56 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     const int64_t zi = static_cast<int64_t>(b) * kdim + h * HD + t;
     const float y = __fmul_rn(__fmul_rn(__fmul_rn(o, rs), norm_w[t]), silu_f(z[zi]));
-    // ---- Q8_K over the head pair (quantize_q8k_kernel) ----
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int half = static_cast<int>(cluster.block_rank());  // == h & 1
-    float a = (y == y) ? fabsf(y) : -1.0f, bv = y;
-    int bi = half * HD + t;
-    warp_best(a, bi, bv);
-    if (lane == 0) { wa[warp] = a; wi[warp] = bi; wv[warp] = bv; }
-    __syncthreads();
-    if (t == 0) {
-        float ca = wa[0], cv = wv[0];
-        int ci = wi[0];
-        for (int w = 1; w < HD / 32; ++w) best_merge(ca, ci, cv, wa[w], wi[w], wv[w]);
-        c_a = ca; c_i = ci; c_v = cv;
-    }
-    cluster.sync();
-    float ba = c_a, xv = c_v;
-    int ii = c_i;
-    {
-        const float *pa = cluster.map_shared_rank(&c_a, half ^ 1);
-        const int *pi = cluster.map_shared_rank(&c_i, half ^ 1);
-        const float *pv = cluster.map_shared_rank(&c_v, half ^ 1);
-        best_merge(ba, ii, xv, *pa, *pi, *pv);
-    }
-    cluster.sync();  // the partner has read this CTA's candidate
-    const float xmax = ba > 0.0f ? xv : 0.0f;
-    const Q8KRow r = q8k_row(xq, kdim, n_tok, b, tile);
-    const int blk = h >> 1;
-    int q = 0;
-    if (xmax != 0.0f) {
-        const float iscale = __fdiv_rn(-127.0f, xmax);
-        q = q8k_value(y, iscale);
-        if (half == 0 && t == 0) *q8k_scale(r, blk) = __fdiv_rn(1.0f, iscale);
-    } else if (half == 0 && t == 0) {
-        *q8k_scale(r, blk) = 0.0f;
-    }
-    *q8k_elem(r, blk, half * HD + t) = static_cast<int8_t>(q);
-    int sum = q;
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (r.bs) {
-        if ((lane & 15) == 0)
-            r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+    if constexpr (!QUANT) {
+        y_out[zi] = y;
     } else {
-        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-        if (lane == 0) q8k_put_min(r, blk, half * (HD / 32) + warp, sum);
+        // ---- Q8_K over the head pair (quantize_q8k_kernel) ----
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        const int half = static_cast<int>(cluster.block_rank());  // == h & 1
+        float a = (y == y) ? fabsf(y) : -1.0f, bv = y;
+        int bi = half * HD + t;
+        warp_best(a, bi, bv);
+        if (lane == 0) { wa[warp] = a; wi[warp] = bi; wv[warp] = bv; }
+        __syncthreads();
+        if (t == 0) {
+            float ca = wa[0], cv = wv[0];
+            int ci = wi[0];
+            for (int w = 1; w < HD / 32; ++w) best_merge(ca, ci, cv, wa[w], wi[w], wv[w]);
+            c_a = ca; c_i = ci; c_v = cv;
+        }
+        cluster.sync();
+        float ba = c_a, xv = c_v;
+        int ii = c_i;
+        {
+            const float *pa = cluster.map_shared_rank(&c_a, half ^ 1);
+            const int *pi = cluster.map_shared_rank(&c_i, half ^ 1);
+            const float *pv = cluster.map_shared_rank(&c_v, half ^ 1);
+            best_merge(ba, ii, xv, *pa, *pi, *pv);
+        }
+        cluster.sync();  // the partner has read this CTA's candidate
+        const float xmax = ba > 0.0f ? xv : 0.0f;
+        const Q8KRow r = q8k_row(xq, kdim, n_tok, b, tile);
+        const int blk = h >> 1;
+        int q = 0;
+        if (xmax != 0.0f) {
+            const float iscale = __fdiv_rn(-127.0f, xmax);
+            q = q8k_value(y, iscale);
+            if (half == 0 && t == 0) *q8k_scale(r, blk) = __fdiv_rn(1.0f, iscale);
+        } else if (half == 0 && t == 0) {
+            *q8k_scale(r, blk) = 0.0f;
+        }
+        *q8k_elem(r, blk, half * HD + t) = static_cast<int8_t>(q);
+        int sum = q;
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if (r.bs) {
+            if ((lane & 15) == 0)
+                r.bs[blk * 16 + half * (HD / 16) + warp * 2 + (lane >> 4)] = static_cast<int16_t>(sum);
+        } else {
+            sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+            if (lane == 0) q8k_put_min(r, blk, half * (HD / 32) + warp, sum);
+        }
     }
     if (t == 0) bulk_wait_all();  // the state store has completed before the CTA exits
 }
@@ -1204,33 +1211,63 @@ int qh_swiglu_q8k(const float *d_gate, const float *d_up, int64_t ffn, int32_t B
     return launch_status(le, "qh_swiglu_q8k");
 }
 
+static int gdn_fused_impl(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b,
+                          const float *d_a, const float *d_dt_bias, const float *d_ssm_a, float *d_state,
+                          const float *d_z, const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk,
+                          float eps, const int32_t *d_pos, void *d_xq, int32_t layout_tile, float *d_y, void *stream,
+                          const char *what) {
+    if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_state || !d_z ||
+        !d_norm_w || !d_pos || (!d_xq && !d_y) || B <= 0 || heads <= 0 || heads % 2 || kk <= 0 ||
+        kk > qh::kMaxConvTaps || !tile_ok(layout_tile))
+        return bad(what);
+    if (hd != 128) {
+        qh::set_last_error_message("gdn: head dim must be 128");
+        return QH_ERR_UNSUPPORTED;
+    }
+    if (reinterpret_cast<uintptr_t>(d_state) & 15) return bad(what);
+    static bool attr_done[64][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev][d_y != nullptr]) {
+        if (d_y)
+            cudaFuncSetAttribute(qh::gdn_fused_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
+        else
+            cudaFuncSetAttribute(qh::gdn_fused_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
+        attr_done[dev][d_y != nullptr] = true;
+    }
+    int *err = qh::device_error_word();
+    if (!err) return bad("gdn: no device error word");
+    const dim3 grid(static_cast<unsigned>(B), heads);
+    cudaError_t le;
+    if (d_y)
+        le = qh::launch_pdl(qh::gdn_fused_kernel<128, false>, grid, dim3(128), 128 * 128 * 4,
+                            static_cast<cudaStream_t>(stream), d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a,
+                            d_state, d_z, d_norm_w, heads, kk, eps, d_pos, static_cast<uint8_t *>(nullptr), B, 0, err,
+                            d_y);
+    else
+        le = qh::launch_pdl_cluster(qh::gdn_fused_kernel<128, true>, grid, dim3(128), 128 * 128 * 4,
+                                    static_cast<cudaStream_t>(stream), dim3(1, 2, 1), d_qkv, d_ring, d_conv_w, d_b, d_a,
+                                    d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, heads, kk, eps, d_pos,
+                                    static_cast<uint8_t *>(d_xq), B, layout_tile, err, static_cast<float *>(nullptr));
+    return launch_status(le, what);
+}
+
 int qh_gdn_fused(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
                  const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
                  const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
                  const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream) {
-    if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_state || !d_z ||
-        !d_norm_w || !d_pos || !d_xq || B <= 0 || heads <= 0 || heads % 2 || kk <= 0 || kk > qh::kMaxConvTaps ||
-        !tile_ok(layout_tile))
-        return bad("qh_gdn_fused: bad arguments");
-    if (hd != 128) {
-        qh::set_last_error_message("qh_gdn_fused: head dim must be 128");
-        return QH_ERR_UNSUPPORTED;
-    }
-    if (reinterpret_cast<uintptr_t>(d_state) & 15) return bad("qh_gdn_fused: state not 16-byte aligned");
-    static bool attr_done[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaFuncSetAttribute(qh::gdn_fused_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
-        attr_done[dev] = true;
-    }
-    int *err = qh::device_error_word();
-    if (!err) return bad("qh_gdn_fused: no device error word");
-    const cudaError_t le = qh::launch_pdl(qh::gdn_fused_kernel<128>, dim3(static_cast<unsigned>(B), heads),
-                                          dim3(128), 128 * 128 * 4, static_cast<cudaStream_t>(stream), d_qkv,
-                                          d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w,
-                                          heads, kk, eps, d_pos, static_cast<uint8_t *>(d_xq), B, layout_tile, err);
-    return launch_status(le, "qh_gdn_fused");
+    if (!d_xq) return bad("qh_gdn_fused: bad arguments");
+    return gdn_fused_impl(d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, B, heads, hd,
+                          kk, eps, d_pos, d_xq, layout_tile, nullptr, stream, "qh_gdn_fused: bad arguments");
+}
+
+int qh_gdn_fused_y(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,
+                   const float *d_dt_bias, const float *d_ssm_a, float *d_state, const float *d_z,
+                   const float *d_norm_w, int32_t B, int32_t heads, int32_t hd, int32_t kk, float eps,
+                   const int32_t *d_pos, float *d_y, void *stream) {
+    if (!d_y) return bad("qh_gdn_fused_y: bad arguments");
+    return gdn_fused_impl(d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a, d_state, d_z, d_norm_w, B, heads, hd,
+                          kk, eps, d_pos, nullptr, 0, d_y, stream, "qh_gdn_fused_y: bad arguments");
 }
 
 int qh_gdn_prefill(const float *d_qkv, float *d_ring, const float *d_conv_w, const float *d_b, const float *d_a,

@@ -505,9 +505,16 @@ static int forward(qh_slm *m) {
             const int64_t gi = Ly->gdn_index;
             float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
-            CK(qh_gdn_fused(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
-                            Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps, m->d_ctl,
-                            m->xq_gdn, m->xq_tile, s));
+            if (m->use_gemm) {  /* many sequences: heads as independent CTAs, then the quantizer */
+                CK(qh_gdn_fused_y(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
+                                  Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps,
+                                  m->d_ctl, m->gy, s));
+                CK(qh_quantize_q8kt(m->gy, kdim, B, m->xq_gdn, s));
+            } else {
+                CK(qh_gdn_fused(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
+                                Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps,
+                                m->d_ctl, m->xq_gdn, m->xq_tile, s));
+            }
         }
         CK(run_plans(m, &Ly->p_out));
         pending = m->mix;
