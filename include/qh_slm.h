@@ -71,6 +71,13 @@ int qh_blob_tensor(const qh_blob *blob, int i, const char **name, int32_t *type,
 int qh_blob_find(const qh_blob *blob, const char *name);
 void qh_blob_free(qh_blob *blob);
 
+/* A blob built from the caller's tensors (e.g. a GGUF file's, with the GGUF
+ * names and shapes, shape[0] = input dim): qh_blob_add copies the bytes.
+ * Types F32 (0), Q8_0, Q4_K, Q5_K, Q6_K; nbytes must match the shape. */
+int qh_blob_create(qh_blob **out);
+int qh_blob_add(qh_blob *blob, const char *name, int32_t type, const int64_t shape[2], const void *data,
+                int64_t nbytes);
+
 /* ------------------------------------------------------------------------
  * Device model + n_seq sequences
  * ---------------------------------------------------------------------- */

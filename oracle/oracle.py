@@ -260,15 +260,39 @@ class Ref:
 
 
 class RefModel:
-    """The reference's slm_forward_step over a synthetic blob's tensors."""
+    """The reference's slm_forward_step over a synthetic blob's tensors, or
+    over a GGUF file read by the reference's own loader (RefModel.from_gguf:
+    gguf_open slm/gguf.c:172, slm_load_config slm/qwen.c:59,
+    slm_load_weights slm/qwen.c:174)."""
 
-    def __init__(self, ref: "Ref", cfg, tensors):
-        L = ref.L
+    @staticmethod
+    def _bind(L):
         L.ref_model_create.restype = C.c_void_p
         L.ref_model_create.argtypes = [_P, _P, _I, _P, _P, _P, _P]
+        L.ref_model_from_gguf.restype = C.c_void_p
+        L.ref_model_from_gguf.argtypes = [C.c_char_p, _P, _P]
         L.ref_model_step.argtypes = [_P, C.c_int32, C.c_int32, _P]
         L.ref_model_step.restype = C.c_int
         L.ref_model_destroy.argtypes = [_P]
+
+    @classmethod
+    def from_gguf(cls, ref: "Ref", path: str):
+        """Returns (model, ic[17], fc[2]): the reference's config as read
+        from the file (ic: layers, hidden, ffn, vocab, heads, kv heads,
+        head dim, rope dim, sections[4], gdn heads, gdn head dim, conv,
+        full-attention interval, max position; fc: rope theta, eps)."""
+        cls._bind(ref.L)
+        ic, fc = np.zeros(17, np.int32), np.zeros(2, np.float32)
+        h = ref.L.ref_model_from_gguf(path.encode(), _ptr(ic), _ptr(fc))
+        if not h:
+            raise RuntimeError(f"reference gguf load failed: {path}")
+        m = cls.__new__(cls)
+        m.L, m.vocab, m.h, m._keep = ref.L, int(ic[3]), h, ()
+        return m, ic, fc
+
+    def __init__(self, ref: "Ref", cfg, tensors):
+        L = ref.L
+        self._bind(L)
         ic = np.array([cfg.n_layers, cfg.hidden, cfg.ffn, cfg.vocab, cfg.n_heads, cfg.n_kv_heads,
                        cfg.head_dim, cfg.rope_dim, *list(cfg.rope_sections), cfg.gdn_heads,
                        cfg.gdn_head_dim, cfg.conv_kernel, cfg.full_attn_interval, cfg.max_pos], np.int32)

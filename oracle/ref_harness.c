@@ -344,9 +344,40 @@ int ref_model_step(void *h, int32_t tok, int32_t pos, float *logits) {
     return sample_argmax(lg);
 }
 
+// The reference's own GGUF path: gguf_open (slm/gguf.c:172), slm_load_config
+// (slm/qwen.c:59) and slm_load_weights (slm/qwen.c:174) on a file, then the
+// caches as above. ic/fc receive the config in ref_model_create's order.
+// NULL if any step fails.
+void *ref_model_from_gguf(const char *path, int32_t *ic, float *fc) {
+    simd_init();
+    struct ref_model *r = (struct ref_model *)calloc(1, sizeof(*r));
+    if (gguf_open(&r->m.gguf, path) != 0) { free(r); return NULL; }
+    struct slm_config *cfg = &r->m.cfg;
+    if (slm_load_config(&r->m.gguf, cfg) != 0 || slm_load_weights(&r->m.gguf, cfg, &r->m.W) != 0) {
+        gguf_close(&r->m.gguf);
+        free(r->m.W.layers);
+        free(r);
+        return NULL;
+    }
+    ic[0] = cfg->n_layers; ic[1] = cfg->hidden_dim; ic[2] = cfg->ffn_dim; ic[3] = cfg->vocab_size;
+    ic[4] = cfg->n_heads; ic[5] = cfg->n_kv_heads; ic[6] = cfg->head_dim; ic[7] = cfg->rope_dim;
+    for (int i = 0; i < 4; i++) ic[8 + i] = cfg->rope_sections[i];
+    ic[12] = cfg->linear_n_heads; ic[13] = cfg->linear_k_head_dim; ic[14] = cfg->linear_conv_kernel;
+    ic[15] = cfg->full_attn_interval; ic[16] = cfg->max_position;
+    fc[0] = cfg->rope_theta; fc[1] = cfg->norm_eps;
+    r->m.loaded = 1;
+    r->c.model = &r->m;
+    r->c.ctrl = slm_ctrl_defaults();
+    kv_init(&r->c.kv, cfg->n_layers, cfg->n_kv_heads, cfg->head_dim, cfg->max_position);
+    ssm_cache_init(&r->c.ssm, cfg);
+    r->c.arena = arena_new(64 * 1024 * 1024);
+    return r;
+}
+
 void ref_model_destroy(void *h) {
     struct ref_model *r = (struct ref_model *)h;
     if (!r) return;
+    if (r->m.gguf.base) gguf_close(&r->m.gguf);
     ssm_cache_free(&r->c.ssm);
     kv_free(&r->c.kv);
     arena_free(r->c.arena);

@@ -119,6 +119,10 @@ SIGNATURES.update({
                            C.POINTER(C.c_void_p), C.POINTER(_I64)]),
     "qh_blob_find": (_I, [_P, C.c_char_p]),
     "qh_blob_free": (None, [_P]),
+    "qh_blob_create": (_I, [C.POINTER(C.c_void_p)]),
+    "qh_blob_add": (_I, [_P, C.c_char_p, C.c_int32, C.POINTER(_I64), _P, _I64]),
+    "qh_gguf_load": (_I, [C.c_char_p, C.c_int32, C.POINTER(SlmConfig), C.POINTER(C.c_void_p)]),
+    "qh_gguf_write": (_I, [C.c_char_p, C.POINTER(SlmConfig), _P]),
     "qh_slm_create": (_I, [C.POINTER(SlmConfig), _P, C.c_int32, C.POINTER(C.c_void_p)]),
     "qh_slm_destroy": (None, [_P]),
     "qh_slm_reset": (_I, [_P]),

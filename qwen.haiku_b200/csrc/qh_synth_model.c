@@ -222,6 +222,27 @@ fail:
     return rc;
 }
 
+int qh_blob_create(qh_blob **out) {
+    if (!out) return QH_ERR_INVALID;
+    *out = (qh_blob *)calloc(1, sizeof(qh_blob));
+    return *out ? QH_OK : QH_ERR_INVALID;
+}
+
+int qh_blob_add(qh_blob *b, const char *name, int32_t type, const int64_t shape[2], const void *data,
+                int64_t nbytes) {
+    if (!b || !name || !shape || !data || strlen(name) >= sizeof(((blob_tensor *)0)->name) || shape[0] <= 0 ||
+        shape[1] <= 0 || qh_blob_find(b, name) >= 0)
+        return QH_ERR_INVALID;
+    if (type != QH_GGUF_F32 && (qhf_block_bytes(type) == 0 || shape[0] % qhf_block_weights(type)))
+        return QH_ERR_UNSUPPORTED;
+    const int64_t want = type == QH_GGUF_F32 ? shape[0] * shape[1] * 4 : qhf_row_bytes(type, shape[0]) * shape[1];
+    if (nbytes != want) return QH_ERR_INVALID;
+    blob_tensor *t = blob_add(b, name, type, shape[0], shape[1]);
+    if (!t) return QH_ERR_INVALID;
+    memcpy(t->data, data, (size_t)nbytes);
+    return QH_OK;
+}
+
 int qh_blob_count(const qh_blob *b) { return b ? b->count : 0; }
 
 int qh_blob_tensor(const qh_blob *b, int i, const char **name, int32_t *type, int64_t shape[2],

@@ -245,12 +245,24 @@ def slm_config(max_pos: int = 320, **over) -> SlmConfig:
 
 
 class Blob:
-    """Synthetic weight blob (qh_blob_synthetic)."""
+    """Weight blob: synthetic (qh_blob_synthetic) or read from a GGUF file
+    (Blob.from_gguf, qh_gguf_load)."""
 
-    def __init__(self, cfg: SlmConfig, seed: int):
-        h = C.c_void_p()
-        check(lib().qh_blob_synthetic(C.byref(cfg), seed, C.byref(h)), "qh_blob_synthetic")
-        self.handle, self.cfg = h, cfg
+    def __init__(self, cfg: SlmConfig, seed: int = None, handle=None):
+        if handle is None:
+            h = C.c_void_p()
+            check(lib().qh_blob_synthetic(C.byref(cfg), seed, C.byref(h)), "qh_blob_synthetic")
+            handle = h
+        self.handle, self.cfg = handle, cfg
+
+    @classmethod
+    def from_gguf(cls, path: str, max_pos_cap: int = 0):
+        cfg, h = SlmConfig(), C.c_void_p()
+        check(lib().qh_gguf_load(path.encode(), max_pos_cap, C.byref(cfg), C.byref(h)), "qh_gguf_load")
+        return cls(cfg, handle=h)
+
+    def write_gguf(self, path: str, cfg: SlmConfig = None):
+        check(lib().qh_gguf_write(path.encode(), C.byref(cfg or self.cfg), self.handle), "qh_gguf_write")
 
     def tensors(self):
         """[(name, type, (shape0, shape1), data pointer, nbytes)]"""
