@@ -15,6 +15,8 @@
 
 #include <stdint.h>
 
+#include "qh_sampler.h"
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -174,6 +176,27 @@ int64_t qh_argmax_feed_scratch_bytes(int32_t B, int64_t vocab);
 int qh_argmax_feed(const float *d_logits, int32_t B, int64_t vocab, void *d_scratch, int32_t *d_next,
                    const int32_t *d_prompt, int32_t stride, int32_t *d_ctl, int32_t *d_tokens, int32_t *d_picks,
                    void *stream);
+
+/* Sampler settings of a sampled decode step, read from device memory so a
+ * captured step serves any settings: the chain (qh_sampler.h) plus the
+ * eos/eot masking of slm_generate_raw (slm/slm.c:303-322) -- while
+ * pos - gen0 < min_new (tokens generated so far), logits[eos_id] and
+ * logits[eot_id] are -inf during sampling and restored after (-1: none). */
+typedef struct qh_sample_ctl {
+    qh_sampler sp;
+    int32_t eos_id, eot_id;
+    int32_t min_new;
+    int32_t gen0;  /* position of the first sampled step */
+} qh_sample_ctl;
+
+/* qh_sample + the device-side feed of a sampled decode step: per row the
+ * pick goes to d_next, d_picks[row][pos], d_tokens (the next input) and is
+ * appended to the row's history (d_hist [B][hist_stride], lengths d_hist_n);
+ * the last row to finish advances d_ctl[0]. *d_ticket starts at zero and is
+ * left at zero. */
+int qh_sample_feed(float *d_logits, int32_t B, int64_t vocab, const qh_sample_ctl *d_sctl, int32_t *d_hist,
+                   int32_t hist_stride, int32_t *d_hist_n, uint64_t *d_rng, int32_t *d_next, int32_t stride,
+                   int32_t *d_ctl, int32_t *d_tokens, int32_t *d_picks, unsigned *d_ticket, void *stream);
 
 #ifdef __cplusplus
 }

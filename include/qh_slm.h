@@ -11,8 +11,9 @@
  *     slm_forward_ssm (GDN layer)        slm/qwen.c:318-611
  *     slm_forward_attn (attention layer) slm/model.c:766-953
  *   sample_argmax (greedy pick)          slm/model.c:401-412
- * The reference's text layer (tokenizer, chat template, sampler chain,
- * agent) is not part of this path: these entry points take token ids.
+ *   slm_generate_raw (generation loop)   slm/slm.c:237-357
+ * The reference's text layer (tokenizer, chat template, agent) is not part
+ * of this path: these entry points take token ids.
  *
  * One qh_slm holds the weights of one model on one GPU plus the decode
  * state of n_seq independent sequences (the reference's slm_ctx, one per
@@ -24,6 +25,8 @@
 #define QH_SLM_H
 
 #include <stdint.h>
+
+#include "qh_sampler.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -99,7 +102,8 @@ int qh_slm_reset(qh_slm *m);
 int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next, float *h_logits);
 
 /* Device-driven decoding, no host round trip per token:
- *   qh_slm_begin   uploads prompt[n_seq][n_prompt] and sets position 0;
+ *   qh_slm_begin   uploads prompt[n_seq][n_prompt], clears the caches
+ *                  (qh_slm_reset) and sets position 0;
  *   qh_slm_advance launches n_steps steps (asynchronous on qh_slm_stream):
  *                  step p feeds prompt[s][p] while p < n_prompt, else the
  *                  greedy pick of step p - 1, and records its own pick;
@@ -130,6 +134,25 @@ int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq);
  * n_prompt before its first sample; callers wanting that schedule pass the
  * prompt with its last token repeated. */
 int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out);
+
+/* Sampled generation, slm_generate_raw (slm/slm.c:237-357) with the sampler
+ * chain of qh_sampler.h, for every sequence at once; the whole loop stays on
+ * the device (one captured step per token, the sample and the token feed
+ * inside it). Starts each sequence afresh at position 0 (like qh_slm_begin):
+ * prompt[s][0..n_prompt) at positions 0..n_prompt-1, then the decode loop
+ * from position n_prompt, whose first input is the last prompt token again,
+ * as in the reference. Per step: logits, eos_id/eot_id masked to -inf while
+ * fewer than min_new tokens were generated, sample_with over the history
+ * (this call's prompt plus the tokens generated so far) with the sequence's
+ * generator. seeds[s] != 0 re-seeds sequence s (rng_seed); 0, or seeds ==
+ * NULL, continues its generator (each starts seeded with s + 1). Up to
+ * max_new tokens (fewer if the positions run out: the loop runs while the
+ * position is below max_pos); a sequence ends at its first eos_id, eot_id
+ * or stop_ids token, which is included. out[s][i] (row pitch max_new) for
+ * i < n_out[s]; later entries are unspecified. n_prompt < max_pos. */
+int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t max_new, int32_t min_new,
+                            const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
+                            const int32_t *stop_ids, int32_t n_stop, int32_t *out, int32_t *n_out);
 
 /* The model's CUDA stream (cudaStream_t) and the device buffer of the last
  * greedy picks [n_seq], for callers that order their own work (events, a

@@ -97,7 +97,19 @@ class Oracle:
         L.orc_dequant_block.argtypes = [_I, _P, _P]
         L.orc_matmul.argtypes = [_I, _P, _I64, _I64, _P, _I64, _P, _P, _P, _P]
         L.orc_matmul.restype = _I
+        L.orc_sample_with.argtypes = [_P, _I64, _P, _P, _P, _P, C.c_int32]
+        L.orc_sample_with.restype = C.c_int32
         self.L = L
+
+    def sample_with(self, logits: np.ndarray, sp: dict, st: np.ndarray, hist) -> int:
+        """Restated sample_with on `logits` (float32, penalized in place) with
+        the generator words `st` (uint64[2], advanced in place)."""
+        assert logits.dtype == np.float32 and logits.flags.c_contiguous
+        fp = np.array([sp["temperature"], sp["top_p"], sp["min_p"], sp["repetition_penalty"]], np.float32)
+        ip = np.array([sp["top_k"], sp["repetition_window"]], np.int32)
+        h = np.ascontiguousarray(hist, np.int32)
+        return int(self.L.orc_sample_with(_ptr(logits), logits.size, _ptr(fp), _ptr(ip), _ptr(st),
+                                          _ptr(h) if h.size else None, int(h.size)))
 
     def quantize_q8k(self, x: np.ndarray):
         x = np.ascontiguousarray(x, dtype=np.float32)
@@ -196,8 +208,34 @@ class Ref:
         L.ref_matvec_mt.restype = _I
         L.ref_matvec_pool_mt.argtypes = [_I, _P, _I, _I64, _I64, _P, _P, _I]
         L.ref_matvec_pool_mt.restype = _I
+        L.ref_sample_with.argtypes = [_P, _I64, _P, _P, _P, _P, C.c_int32]
+        L.ref_sample_with.restype = C.c_int32
+        L.ref_rng_seed.argtypes = [C.c_uint64, _P]
+        L.ref_sampler_defaults.argtypes = [_P, _P]
         self.L = L
         self.label = L.ref_dispatch_label().decode()
+
+    # -- sampler chain (slm/sampler.c:134-180, slm/model.c:414-447) --------
+    def rng_seed(self, seed: int) -> np.ndarray:
+        st = np.zeros(2, np.uint64)
+        self.L.ref_rng_seed(seed, _ptr(st))
+        return st
+
+    def sampler_defaults(self):
+        fp, ip = np.zeros(4, np.float32), np.zeros(2, np.int32)
+        self.L.ref_sampler_defaults(_ptr(fp), _ptr(ip))
+        return {"temperature": float(fp[0]), "top_p": float(fp[1]), "min_p": float(fp[2]),
+                "repetition_penalty": float(fp[3]), "top_k": int(ip[0]), "repetition_window": int(ip[1])}
+
+    def sample_with(self, logits: np.ndarray, sp: dict, st: np.ndarray, hist) -> int:
+        """sample_with on `logits` (float32, modified in place) with the
+        generator words `st` (uint64[2], advanced in place)."""
+        assert logits.dtype == np.float32 and logits.flags.c_contiguous
+        fp = np.array([sp["temperature"], sp["top_p"], sp["min_p"], sp["repetition_penalty"]], np.float32)
+        ip = np.array([sp["top_k"], sp["repetition_window"]], np.int32)
+        h = np.ascontiguousarray(hist, np.int32)
+        return int(self.L.ref_sample_with(_ptr(logits), logits.size, _ptr(fp), _ptr(ip), _ptr(st),
+                                          _ptr(h) if h.size else None, int(h.size)))
 
     def quantize_q8k(self, x: np.ndarray):
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, x.shape[-1])

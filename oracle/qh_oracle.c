@@ -15,6 +15,8 @@
 //     Q5_K 176 B  [0]fp16 d [2]fp16 dmin [4]u8 scales[12] [16]u8 qh[32] [48]u8 qs[128]
 //     Q6_K 210 B  [0]u8 ql[128] [128]u8 qh[64] [192]i8 scales[16] [208]fp16 d
 //     Q8_0  34 B  [0]fp16 d [2]i8 qs[32]
+//   Sampler chain sample_with (slm/sampler.c:134-180), generator
+//   (slm/model.c:414-447): orc_sample_with at the end of this file.
 //   Activation rows are handed over split into planes (qs int8[K], d float[K/256],
 //   bsums int16[K/16]) -- the same numbers as the reference's q8k_block array.
 //
@@ -356,4 +358,119 @@ int orc_matmul(int type, const uint8_t *w, int64_t out_f, int64_t k,
                                      scratch_bs);
     }
     return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Sampler chain: sample_with (slm/sampler.c:134-180) with the generator of
+// slm/model.c:414-447. fp = {temperature, top_p, min_p, repetition_penalty},
+// ip = {top_k, repetition_window}, st = generator words (advanced in place).
+// Logits are penalized in place. The exponential is exp in double rounded
+// once to float (correctly rounded expf), like the device kernel.
+// ---------------------------------------------------------------------------
+
+static uint64_t orc_rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+// rng_next + rng_uniform (slm/model.c:420-428, 444-447)
+static float orc_uniform(uint64_t *st) {
+    const uint64_t a = st[0];
+    uint64_t b = st[1];
+    const uint64_t out = orc_rotl64(a * 5u, 7) * 9u;
+    b ^= a;
+    st[0] = orc_rotl64(a, 24) ^ b ^ (b << 16);
+    st[1] = orc_rotl64(b, 37);
+    return (float)(uint32_t)(out >> 40) / 16777216.0f;
+}
+
+#define ORC_TOPK_MAX 256
+
+// First slot holding the smallest value among slot[0..k).
+static int orc_first_min(const float *val, int k) {
+    int w = 0;
+    for (int j = 1; j < k; j++)
+        if (val[j] < val[w]) w = j;
+    return w;
+}
+
+int32_t orc_sample_with(float *lg, int64_t n, const float *fp, const int32_t *ip, uint64_t *st,
+                        const int32_t *hist, int32_t hn) {
+    const float temp = fp[0], top_p = fp[1], min_p = fp[2], pen = fp[3];
+    // repetition penalty: each occurrence in the window scales its logit
+    // once more (slm/sampler.c:49-63)
+    if (pen != 1.0f && hn != 0) {
+        const int32_t win = ip[1];
+        for (int32_t i = (win > 0 && win < hn) ? hn - win : 0; i < hn; i++) {
+            const int32_t t = hist[i];
+            if (t < 0 || (int64_t)t >= n) continue;
+            lg[t] = lg[t] > 0.0f ? lg[t] / pen : lg[t] * pen;
+        }
+    }
+    if (temp <= 0.0f) {  // sample_argmax (slm/model.c:401-412)
+        int32_t best = 0;
+        for (int64_t i = 1; i < n; i++)
+            if (lg[i] > lg[best]) best = (int32_t)i;
+        return best;
+    }
+    int k = ip[0] > 0 ? ip[0] : ORC_TOPK_MAX;
+    if (k > ORC_TOPK_MAX) k = ORC_TOPK_MAX;
+    // top-k slots: fill the first k, then each logit above the current
+    // first minimum takes that slot (slm/sampler.c:70-93)
+    float val[ORC_TOPK_MAX];
+    int32_t idx[ORC_TOPK_MAX];
+    int filled = 0;
+    int w = 0;
+    for (int64_t i = 0; i < n; i++) {
+        if (filled < k) {
+            val[filled] = lg[i];
+            idx[filled] = (int32_t)i;
+            if (++filled == k) w = orc_first_min(val, k);
+        } else if (lg[i] > val[w]) {
+            val[w] = lg[i];
+            idx[w] = (int32_t)i;
+            w = orc_first_min(val, k);
+        }
+    }
+    // softmax over the slots in slot order (slm/sampler.c:97-112)
+    float m = val[0];
+    for (int j = 1; j < filled; j++)
+        if (val[j] > m) m = val[j];
+    float sum = 0.0f;
+    for (int j = 0; j < filled; j++) {
+        val[j] = (float)exp((double)((val[j] - m) / temp));
+        sum += val[j];
+    }
+    if (sum > 0.0f)
+        for (int j = 0; j < filled; j++) val[j] /= sum;
+    // stable descending order (slm/sampler.c:117-130)
+    float sv[ORC_TOPK_MAX];
+    int32_t si[ORC_TOPK_MAX];
+    for (int j = 0; j < filled; j++) {
+        int r = 0;
+        for (int i = 0; i < filled; i++) r += (val[i] > val[j]) || (val[i] == val[j] && i < j);
+        sv[r] = val[j];
+        si[r] = idx[j];
+    }
+    int cutoff = filled;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        float acc = 0.0f;
+        for (int j = 0; j < filled; j++) {
+            acc += sv[j];
+            if (acc >= top_p) { cutoff = j + 1; break; }
+        }
+    }
+    if (min_p > 0.0f) {
+        const float thresh = min_p * sv[0];
+        int j = 1;
+        while (j < cutoff && sv[j] >= thresh) j++;
+        cutoff = j;
+    }
+    float tot = 0.0f;
+    for (int j = 0; j < cutoff; j++) tot += sv[j];
+    const float u = orc_uniform(st) * tot;
+    float c = 0.0f;
+    int picked = 0;
+    for (int j = 0; j < cutoff; j++) {
+        c += sv[j];
+        if (u <= c) { picked = j; break; }
+    }
+    return si[picked];
 }

@@ -19,6 +19,7 @@
 //   matmul_dispatch                            slm/model.c:220-264
 //   q{4k,5k,6k}_dequant_block                  slm/tensor.c:800, 867, 988
 //   slm_forward_step + sample_argmax           slm/qwen.c:874-981, slm/model.c:401
+//   sample_with, rng_seed, rng_uniform         slm/sampler.c:134, slm/model.c:431-447
 
 // Built twice by oracle/Makefile: libqhref.so is the reference as shipped;
 // libqhref_crlibm.so (-DQH_CR_LIBM) is the same sources with expf/logf
@@ -383,4 +384,49 @@ void ref_model_destroy(void *h) {
     arena_free(r->c.arena);
     free(r->m.W.layers);
     free(r);
+}
+
+// The sampler chain, sample_with (slm/sampler.c:134-180), on caller
+// logits (modified in place as the reference does). fp = {temperature,
+// top_p, min_p, repetition_penalty}, ip = {top_k, repetition_window}; st =
+// the generator's two words, advanced in place.
+int32_t ref_sample_with(float *logits, int64_t n, const float *fp, const int32_t *ip, uint64_t *st,
+                        const int32_t *hist, int32_t hist_n) {
+    struct tensor t;
+    memset(&t, 0, sizeof(t));
+    t.ne[0] = n;
+    t.ne[1] = t.ne[2] = t.ne[3] = 1;
+    t.ndim = 1;
+    t.data = logits;
+    struct slm_sampler sp;
+    sp.temperature = fp[0];
+    sp.top_p = fp[1];
+    sp.min_p = fp[2];
+    sp.repetition_penalty = fp[3];
+    sp.top_k = ip[0];
+    sp.repetition_window = ip[1];
+    struct rng r = {st[0], st[1]};
+    int32_t pick = sample_with(&t, &sp, &r, hist, hist_n);
+    st[0] = r.s0;
+    st[1] = r.s1;
+    return pick;
+}
+
+// rng_seed (slm/model.c:431) into st[2].
+void ref_rng_seed(uint64_t seed, uint64_t *st) {
+    struct rng r;
+    rng_seed(&r, seed);
+    st[0] = r.s0;
+    st[1] = r.s1;
+}
+
+// slm_sampler_defaults (slm/sampler.c:22): fp/ip in ref_sample_with's order.
+void ref_sampler_defaults(float *fp, int32_t *ip) {
+    struct slm_sampler s = slm_sampler_defaults();
+    fp[0] = s.temperature;
+    fp[1] = s.top_p;
+    fp[2] = s.min_p;
+    fp[3] = s.repetition_penalty;
+    ip[0] = s.top_k;
+    ip[1] = s.repetition_window;
 }

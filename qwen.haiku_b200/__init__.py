@@ -55,6 +55,15 @@ class MatvecJob(C.Structure):
 
 _P, _I, _I64, _U64, _F, _SZ = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_float, C.c_size_t
 
+
+class Sampler(C.Structure):
+    """qh_sampler (include/qh_sampler.h) = struct slm_sampler."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("repetition_window", C.c_int32)]
+
+    def as_dict(self):
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
 # name -> (restype, argtypes); every declaration of include/qh_backend.h and
 # include/qh_synth.h.
 SIGNATURES = {
@@ -168,6 +177,12 @@ SIGNATURES.update({  # include/qh_kernels.h
     "qh_gdn_prefill": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                             C.c_int32, C.c_float, _P, _P, C.c_int32, _P]),
     "qh_argmax_feed": (_I, [_P, C.c_int32, _I64, _P, _P, _P, C.c_int32, _P, _P, _P, _P]),
+    "qh_sampler_defaults": (None, [_P]),
+    "qh_rng_seed": (None, [_U64, _P]),
+    "qh_sample": (_I, [_P, _P, C.c_int32, _I64, _P, C.c_int32, _P, _P, _P, _P]),
+    "qh_sample_feed": (_I, [_P, C.c_int32, _I64, _P, _P, C.c_int32, _P, _P, _P, C.c_int32, _P, _P, _P, _P, _P]),
+    "qh_slm_generate_sampled": (_I, [_P, _P, C.c_int32, C.c_int32, C.c_int32, _P, _P, C.c_int32, C.c_int32, _P,
+                                     C.c_int32, _P, _P]),
 })
 
 _lib = None

@@ -97,10 +97,17 @@ struct qh_slm {
     plan_set pf_in[MAX_LAYERS], pf_out[MAX_LAYERS], pf_ffn[MAX_LAYERS], pf_down[MAX_LAYERS];
     // The whole step is captured once in a CUDA graph (after one direct run
     // has set every kernel attribute) and replayed; position and tokens are
-    // read from device memory, so one graph serves every position.
-    cudaGraph_t graph;
-    cudaGraphExec_t graph_exec;
-    int steps_run;
+    // read from device memory, so one graph serves every position. Two
+    // graphs: [0] ends in the greedy pick, [1] in the sampler chain.
+    cudaGraph_t graph[2];
+    cudaGraphExec_t graph_exec[2];
+    int steps_run[2];
+    int sampling;                  // the step ends in qh_sample_feed
+    // sampled decoding (qh_slm_generate_sampled)
+    qh_sample_ctl *d_sctl;
+    int32_t *d_hist, *d_hist_n;    // [B][max_pos + 1] prompt + generated tokens, lengths
+    uint64_t *d_rng;               // [B][2] generator words
+    unsigned *d_sticket;
     // caches
     float *ring, *state;
     uint16_t *kcache, *vcache;
@@ -334,6 +341,23 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         }
         TRY(dev_alloc(m, (void **)&m->d_prompt, (size_t)B * cfg->max_pos * 4, NULL));
         TRY(dev_alloc(m, (void **)&m->d_picks, (size_t)B * cfg->max_pos * 4, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_sctl, sizeof(qh_sample_ctl), NULL));
+        TRY(dev_alloc(m, (void **)&m->d_hist, (size_t)B * (cfg->max_pos + 1) * 4, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_hist_n, (size_t)B * 4, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_rng, (size_t)B * 16, NULL));
+        TRY(dev_alloc(m, (void **)&m->d_sticket, 16, NULL));
+        TRY(qh_memset(m->d_sticket, 0, 16, m->stream));
+        TRY(qh_memset(m->d_hist_n, 0, (size_t)B * 4, m->stream));
+        {
+            // each sequence's generator starts seeded with its index + 1
+            uint64_t *st = (uint64_t *)malloc((size_t)B * 16);
+            if (!st) { rc = QH_ERR_INVALID; goto fail; }
+            for (int64_t b = 0; b < B; ++b) qh_rng_seed((uint64_t)b + 1, st + 2 * b);
+            rc = qh_memcpy_h2d(m->d_rng, st, (size_t)B * 16, m->stream);
+            if (!rc) rc = qh_stream_sync(m->stream);
+            free(st);
+            if (rc) goto fail;
+        }
         if (cudaMallocHost((void **)&m->h_tok, (size_t)B * 4) != cudaSuccess ||
             cudaMallocHost((void **)&m->h_next, (size_t)B * 4) != cudaSuccess ||
             cudaMallocHost((void **)&m->h_ctl, 16) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
@@ -437,8 +461,10 @@ void qh_slm_destroy(qh_slm *m) {
         free_plans(&m->L[l].p_down);
     }
     free_plans(&m->p_head);
-    if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
-    if (m->graph) cudaGraphDestroy(m->graph);
+    for (int i = 0; i < 2; ++i) {
+        if (m->graph_exec[i]) cudaGraphExecDestroy(m->graph_exec[i]);
+        if (m->graph[i]) cudaGraphDestroy(m->graph[i]);
+    }
     for (int i = 0; i < m->nallocs; ++i) qh_free(m->allocs[i]);
     free(m->allocs);
     if (m->h_tok) cudaFreeHost(m->h_tok);
@@ -527,17 +553,22 @@ static int forward(qh_slm *m) {
     RESNORM(m->out_norm, m->xq_h);
 #undef RESNORM
     CK(run_plans(m, &m->p_head));
-    CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
-                      m->d_tok, m->d_picks, s));
+    if (m->sampling)
+        CK(qh_sample_feed(m->logits, B, c->vocab, m->d_sctl, m->d_hist, c->max_pos + 1, m->d_hist_n, m->d_rng,
+                          m->d_next, c->max_pos, m->d_ctl, m->d_tok, m->d_picks, m->d_sticket, s));
+    else
+        CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
+                          m->d_tok, m->d_picks, s));
     return QH_OK;
 }
 
 static int launch_step(qh_slm *m) {
-    if (m->graph_exec) {
-        if (cudaGraphLaunch(m->graph_exec, m->stream) != cudaSuccess) return QH_ERR_CUDA;
+    const int gi = m->sampling ? 1 : 0;
+    if (m->graph_exec[gi]) {
+        if (cudaGraphLaunch(m->graph_exec[gi], m->stream) != cudaSuccess) return QH_ERR_CUDA;
         return QH_OK;
     }
-    if (m->steps_run++ == 0) return forward(m);  // first run sets kernel attributes
+    if (m->steps_run[gi]++ == 0) return forward(m);  // first run sets kernel attributes
     // capture the step once, then replay it
     if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return forward(m);
     int rc = forward(m);
@@ -548,14 +579,14 @@ static int launch_step(qh_slm *m) {
         cudaGetLastError();
         return rc ? rc : forward(m);
     }
-    if (cudaGraphInstantiate(&m->graph_exec, g, 0) != cudaSuccess) {
+    if (cudaGraphInstantiate(&m->graph_exec[gi], g, 0) != cudaSuccess) {
         cudaGraphDestroy(g);
-        m->graph_exec = NULL;
+        m->graph_exec[gi] = NULL;
         cudaGetLastError();
         return forward(m);
     }
-    m->graph = g;
-    return cudaGraphLaunch(m->graph_exec, m->stream) == cudaSuccess ? QH_OK : QH_ERR_CUDA;
+    m->graph[gi] = g;
+    return cudaGraphLaunch(m->graph_exec[gi], m->stream) == cudaSuccess ? QH_OK : QH_ERR_CUDA;
 }
 
 int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next, float *h_logits) {
@@ -584,6 +615,9 @@ int qh_slm_begin(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
     const int32_t B = m->B, P = m->cfg.max_pos;
     for (int64_t i = 0; i < (int64_t)B * n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab) return QH_ERR_INVALID;
+    // position 0 starts every sequence afresh: the conv ring and recurrent
+    // state are read before they are written, so they are cleared
+    CK(qh_slm_reset(m));
     // prompt[s][i] -> d_prompt[s][i] (row pitch max_pos)
     if (cudaMemcpy2DAsync(m->d_prompt, (size_t)P * 4, prompt, (size_t)n_prompt * 4, (size_t)n_prompt * 4,
                           (size_t)B, cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
@@ -800,6 +834,83 @@ int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t 
     if (n_new == 0) return QH_OK;
     CK(qh_slm_advance(m, n_new));
     return qh_slm_picks(m, n_prompt - 1, n_new, out);
+}
+
+int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t max_new, int32_t min_new,
+                            const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
+                            const int32_t *stop_ids, int32_t n_stop, int32_t *out, int32_t *n_out) {
+    if (!m || !prompt || !sp || !out || !n_out || n_prompt <= 0 || max_new < 0 || n_stop < 0 ||
+        (n_stop > 0 && !stop_ids) || n_prompt >= m->cfg.max_pos)
+        return QH_ERR_INVALID;
+    const int32_t B = m->B, P = m->cfg.max_pos, n = n_prompt;
+    // slm_generate_raw's decode loop runs while pos < max_position
+    const int32_t n_gen = max_new < P - n ? max_new : P - n;
+    // prompt at positions 0..n-1, then the decode loop re-feeds the last
+    // prompt token at position n: a prefill of the prompt plus that token
+    // leaves exactly this state with the token pending at position n
+    int32_t *ext = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * (n + 1));
+    int32_t *hn = (int32_t *)malloc(sizeof(int32_t) * (size_t)B);
+    uint64_t *st = (uint64_t *)malloc(16 * (size_t)B);
+    int32_t *picks = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * (n_gen > 0 ? n_gen : 1));
+    int rc = (ext && hn && st && picks) ? QH_OK : QH_ERR_INVALID;
+    if (!rc) {
+        for (int32_t b = 0; b < B; ++b) {
+            memcpy(ext + (int64_t)b * (n + 1), prompt + (int64_t)b * n, sizeof(int32_t) * (size_t)n);
+            ext[(int64_t)b * (n + 1) + n] = prompt[(int64_t)b * n + n - 1];
+            hn[b] = n;
+        }
+        rc = qh_slm_prefill(m, ext, n + 1);
+    }
+    // the repetition-penalty history starts as this call's prompt (slm/slm.c:257-263)
+    if (!rc && cudaMemcpy2DAsync(m->d_hist, (size_t)(P + 1) * 4, prompt, (size_t)n * 4, (size_t)n * 4, (size_t)B,
+                                 cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
+        rc = QH_ERR_CUDA;
+    if (!rc) rc = qh_memcpy_h2d(m->d_hist_n, hn, sizeof(int32_t) * (size_t)B, m->stream);
+    // a non-zero seed re-seeds a sequence's generator; zero continues it
+    if (!rc && seeds) {
+        rc = qh_memcpy_d2h(st, m->d_rng, 16 * (size_t)B, m->stream);
+        if (!rc) rc = qh_stream_sync(m->stream);
+        for (int32_t b = 0; b < B && !rc; ++b)
+            if (seeds[b] != 0) qh_rng_seed(seeds[b], st + 2 * b);
+        if (!rc) rc = qh_memcpy_h2d(m->d_rng, st, 16 * (size_t)B, m->stream);
+    }
+    if (!rc) {
+        qh_sample_ctl sc;
+        memset(&sc, 0, sizeof(sc));
+        sc.sp = *sp;
+        sc.eos_id = eos_id;
+        sc.eot_id = eot_id;
+        sc.min_new = min_new;
+        sc.gen0 = n;
+        rc = qh_memcpy_h2d(m->d_sctl, &sc, sizeof(sc), m->stream);
+        if (!rc) rc = qh_stream_sync(m->stream);
+    }
+    if (!rc && n_gen > 0) {
+        m->sampling = 1;
+        rc = qh_slm_advance(m, n_gen);
+        m->sampling = 0;
+        if (!rc) rc = qh_slm_picks(m, n, n_gen, picks);
+    }
+    if (!rc) {
+        // a sequence ends at its first eos, eot or stop token, which is
+        // counted (slm/slm.c:330-341)
+        for (int32_t b = 0; b < B; ++b) {
+            int32_t cnt = n_gen;
+            for (int32_t i = 0; i < n_gen; ++i) {
+                const int32_t t = picks[(int64_t)b * n_gen + i];
+                int stop = t == eos_id || t == eot_id;
+                for (int32_t j = 0; j < n_stop && !stop; ++j) stop = t == stop_ids[j];
+                out[(int64_t)b * max_new + i] = t;
+                if (stop) { cnt = i + 1; break; }
+            }
+            n_out[b] = cnt;
+        }
+    }
+    free(ext);
+    free(hn);
+    free(st);
+    free(picks);
+    return rc;
 }
 
 void *qh_slm_stream(const qh_slm *m) { return m ? (void *)m->stream : NULL; }

@@ -287,6 +287,33 @@ class Blob:
             pass
 
 
+def sampler_defaults():
+    """qh_sampler_defaults (slm_sampler_defaults)."""
+    from . import Sampler
+    sp = Sampler()
+    lib().qh_sampler_defaults(C.byref(sp))
+    return sp
+
+
+def rng_seed(seed: int) -> np.ndarray:
+    """qh_rng_seed: the generator's two words for `seed`."""
+    st = np.zeros(2, np.uint64)
+    lib().qh_rng_seed(seed, st.ctypes.data)
+    return st
+
+
+def sample(sp, logits, hist, hist_n, rng):
+    """qh_sample on device tensors: logits float32 [B][vocab] (penalized in
+    place), hist int32 [B][stride], hist_n int32 [B], rng uint64-as-int64
+    [B][2] (advanced in place). Returns the int32 [B] picks (device)."""
+    torch = _torch()
+    B, vocab = logits.shape
+    out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    check(lib().qh_sample(C.byref(sp), dptr(logits), B, vocab, dptr(hist), hist.shape[1], dptr(hist_n), dptr(rng),
+                          dptr(out), stream_handle()), "qh_sample")
+    return out
+
+
 class Slm:
     """Device model with n_seq sequences (qh_slm_create)."""
 
@@ -313,6 +340,22 @@ class Slm:
         check(lib().qh_slm_generate(self.handle, p.ctypes.data, p.shape[1], n_new, out.ctypes.data),
               "qh_slm_generate")
         return out
+
+    def generate_sampled(self, prompt, max_new: int, sampler=None, seeds=None, min_new: int = 0,
+                         eos_id: int = -1, eot_id: int = -1, stop_ids=()):
+        """qh_slm_generate_sampled: returns a list of n_seq int32 arrays
+        (each sequence's tokens up to and including its first stop)."""
+        p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
+        sp = sampler if sampler is not None else sampler_defaults()
+        sd = None if seeds is None else np.ascontiguousarray(seeds, np.uint64).reshape(self.n_seq)
+        st = np.ascontiguousarray(list(stop_ids), np.int32)
+        out = np.zeros((self.n_seq, max(max_new, 1)), np.int32)
+        n_out = np.zeros(self.n_seq, np.int32)
+        check(lib().qh_slm_generate_sampled(self.handle, p.ctypes.data, p.shape[1], max_new, min_new, C.byref(sp),
+                                            sd.ctypes.data if sd is not None else None, eos_id, eot_id,
+                                            st.ctypes.data if st.size else None, int(st.size), out.ctypes.data,
+                                            n_out.ctypes.data), "qh_slm_generate_sampled")
+        return [out[b, :n_out[b]].copy() for b in range(self.n_seq)]
 
     def begin(self, prompt):
         p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
