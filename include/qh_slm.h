@@ -12,6 +12,8 @@
  *     slm_forward_attn (attention layer) slm/model.c:766-953
  *   sample_argmax (greedy pick)          slm/model.c:401-412
  *   slm_generate_raw (generation loop)   slm/slm.c:237-357
+ *   slm_ctx_snapshot / slm_ctx_restore   slm/model.c:1262-1371
+ *   JSONL parity tracer (slm_trace_*)    slm/model.c:585-727
  * The reference's text layer (tokenizer, chat template, agent) is not part
  * of this path: these entry points take token ids.
  *
@@ -153,6 +155,40 @@ int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t 
 int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t max_new, int32_t min_new,
                             const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
                             const int32_t *stop_ids, int32_t n_stop, int32_t *out, int32_t *n_out);
+
+/* Snapshot / restore of every sequence's decode state (slm_ctx_snapshot,
+ * slm_ctx_restore, slm_snapshot_free; slm/model.c:1262-1371), held in device
+ * memory: the position and pending input tokens, generator words, KV rows
+ * 0..pos-1 of every attention layer (sized to the position, as the
+ * reference's), the conv rings and recurrent states (full), plus prompts,
+ * picks by position and the sampler history. qh_slm_restore puts them back
+ * into the model they came from (QH_ERR_INVALID for another one); the next
+ * step continues from the snapshot's position. Synchronous. */
+typedef struct qh_slm_snap qh_slm_snap;
+int qh_slm_snapshot(qh_slm *m, qh_slm_snap **out);
+int qh_slm_restore(qh_slm *m, const qh_slm_snap *s);
+void qh_slm_snapshot_free(qh_slm_snap *s);
+/* Device bytes the snapshot holds; its position. -1 for NULL. */
+int64_t qh_slm_snapshot_bytes(const qh_slm_snap *s);
+int32_t qh_slm_snapshot_pos(const qh_slm_snap *s);
+
+/* Parity tracer (slm_trace_open / slm_trace_f32, slm/model.c:585-727):
+ * the next qh_slm_step writes one JSON line per traced tensor of sequence
+ * `seq` to `path` (truncated), in the reference's schema and number
+ * formatting (name, op, type, ne, nb, nbytes, fnv64 of the raw bytes, first
+ * and last 8 values as %.9g and as fp32 hex, sum, n_nan, n_inf), so a line
+ * is textually identical to the reference's line of the same name when the
+ * tensor is bit-identical. Names follow the reference's (inp_embd,
+ * attn_norm-L, attn_qkv-L, alpha-L, beta-L, V_raw-L, Q_l2norm-L, K_l2norm-L,
+ * beta_in-L, attn_output-L, y_norm-L, ssm_out-L, Qfull-L, Kcur-L, Vcur-L,
+ * attn_out-L, mix-L, mix_residual-L, ffn_norm-L, ffn_out-L, l_out-L,
+ * result_norm, result_output); intermediates that the device never holds
+ * (conv_raw, Q_raw, K_raw, a_softplus, g_in, conv_silu) are not written.
+ * The traced step runs its kernels one by one (the Gated DeltaNet layers as
+ * the unfused pre/recurrence/gated-norm chain, whose results are the same)
+ * and synchronizes after each traced tensor; the file is closed when the
+ * step ends. */
+int qh_slm_trace(qh_slm *m, int32_t seq, const char *path);
 
 /* The model's CUDA stream (cudaStream_t) and the device buffer of the last
  * greedy picks [n_seq], for callers that order their own work (events, a

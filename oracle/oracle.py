@@ -312,6 +312,12 @@ class RefModel:
         L.ref_model_step.argtypes = [_P, C.c_int32, C.c_int32, _P]
         L.ref_model_step.restype = C.c_int
         L.ref_model_destroy.argtypes = [_P]
+        L.ref_model_snapshot.argtypes = [_P, C.c_int32]
+        L.ref_model_snapshot.restype = C.c_void_p
+        L.ref_model_restore.argtypes = [_P, _P]
+        L.ref_snapshot_free.argtypes = [_P]
+        L.ref_trace_begin.argtypes = [C.c_char_p]
+        L.ref_trace_begin.restype = C.c_int
 
     @classmethod
     def from_gguf(cls, ref: "Ref", path: str):
@@ -349,6 +355,25 @@ class RefModel:
         logits = np.empty(self.vocab, np.float32) if want_logits else None
         a = self.L.ref_model_step(self.h, int(tok), int(pos), _ptr(logits) if logits is not None else None)
         return (a, logits) if want_logits else a
+
+    def snapshot(self, pos: int):
+        """slm_ctx_snapshot at position pos; free with free_snapshot."""
+        return self.L.ref_model_snapshot(self.h, pos)
+
+    def restore(self, snap):
+        self.L.ref_model_restore(self.h, snap)
+
+    def free_snapshot(self, snap):
+        self.L.ref_snapshot_free(snap)
+
+    def trace_step(self, path: str, tok: int, pos: int):
+        """One slm_forward_step with the reference's JSONL tracer writing to path."""
+        if self.L.ref_trace_begin(path.encode()) != 0:
+            raise RuntimeError(f"cannot open {path}")
+        try:
+            return self.step(tok, pos)
+        finally:
+            self.L.ref_trace_end()
 
     def close(self):
         if self.h:

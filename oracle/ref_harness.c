@@ -20,6 +20,8 @@
 //   q{4k,5k,6k}_dequant_block                  slm/tensor.c:800, 867, 988
 //   slm_forward_step + sample_argmax           slm/qwen.c:874-981, slm/model.c:401
 //   sample_with, rng_seed, rng_uniform         slm/sampler.c:134, slm/model.c:431-447
+//   slm_ctx_snapshot / restore / free           slm/model.c:1262-1371
+//   JSONL tracer (g_qh_trace_fp, slm_trace_close) slm/model.c:585-727
 
 // Built twice by oracle/Makefile: libqhref.so is the reference as shipped;
 // libqhref_crlibm.so (-DQH_CR_LIBM) is the same sources with expf/logf
@@ -430,3 +432,28 @@ void ref_sampler_defaults(float *fp, int32_t *ip) {
     ip[0] = s.top_k;
     ip[1] = s.repetition_window;
 }
+
+// slm_ctx_snapshot / slm_ctx_restore / slm_snapshot_free (slm/model.c:
+// 1262-1371) on a ref_model's context; pos = the context's position (the
+// number of KV rows written), which ref_model_step does not track itself.
+void *ref_model_snapshot(void *h, int32_t pos) {
+    struct ref_model *r = (struct ref_model *)h;
+    r->c.pos = pos;
+    return slm_ctx_snapshot(&r->c);
+}
+void ref_model_restore(void *h, void *snap) {
+    struct ref_model *r = (struct ref_model *)h;
+    slm_ctx_restore(&r->c, (const struct slm_snapshot *)snap);
+}
+void ref_snapshot_free(void *snap) { slm_snapshot_free((struct slm_snapshot *)snap); }
+
+// The reference's JSONL parity tracer (slm/model.c:585-727): records of
+// the forward steps run between ref_trace_begin and ref_trace_end go to
+// `path` (slm_trace_open reads the path from QH_TRACE_OUT; this sets the
+// same file handle directly).
+int ref_trace_begin(const char *path) {
+    if (g_qh_trace_fp) fclose(g_qh_trace_fp);
+    g_qh_trace_fp = fopen(path, "w");
+    return g_qh_trace_fp ? 0 : -1;
+}
+void ref_trace_end(void) { slm_trace_close(); }

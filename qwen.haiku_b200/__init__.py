@@ -177,6 +177,12 @@ SIGNATURES.update({  # include/qh_kernels.h
     "qh_gdn_prefill": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                             C.c_int32, C.c_float, _P, _P, C.c_int32, _P]),
     "qh_argmax_feed": (_I, [_P, C.c_int32, _I64, _P, _P, _P, C.c_int32, _P, _P, _P, _P]),
+    "qh_slm_trace": (_I, [_P, C.c_int32, C.c_char_p]),
+    "qh_slm_snapshot": (_I, [_P, _P]),
+    "qh_slm_restore": (_I, [_P, _P]),
+    "qh_slm_snapshot_free": (None, [_P]),
+    "qh_slm_snapshot_bytes": (_I64, [_P]),
+    "qh_slm_snapshot_pos": (C.c_int32, [_P]),
     "qh_sampler_defaults": (None, [_P]),
     "qh_rng_seed": (None, [_U64, _P]),
     "qh_sample": (_I, [_P, _P, C.c_int32, _I64, _P, C.c_int32, _P, _P, _P, _P]),

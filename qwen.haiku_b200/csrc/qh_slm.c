@@ -20,6 +20,7 @@
 // tensor_matmul_* wrappers compute per call.
 
 #include <math.h>
+#include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -108,6 +109,11 @@ struct qh_slm {
     int32_t *d_hist, *d_hist_n;    // [B][max_pos + 1] prompt + generated tokens, lengths
     uint64_t *d_rng;               // [B][2] generator words
     unsigned *d_sticket;
+    // parity tracer (qh_slm_trace): armed for the next qh_slm_step
+    FILE *trace_fp;
+    int32_t trace_seq;
+    float *trace_buf;              // host copy of one traced row
+    int64_t trace_cap;
     // caches
     float *ring, *state;
     uint16_t *kcache, *vcache;
@@ -467,6 +473,8 @@ void qh_slm_destroy(qh_slm *m) {
     }
     for (int i = 0; i < m->nallocs; ++i) qh_free(m->allocs[i]);
     free(m->allocs);
+    if (m->trace_fp) fclose(m->trace_fp);
+    free(m->trace_buf);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->h_next) cudaFreeHost(m->h_next);
     if (m->h_ctl) cudaFreeHost(m->h_ctl);
@@ -490,6 +498,87 @@ int qh_slm_reset(qh_slm *m) {
     return qh_stream_sync(m->stream);
 }
 
+// ---------------------------------------------------------------------------
+// Parity tracer: one JSONL record per traced tensor, the schema and number
+// formatting of the reference's slm_trace_f32 (slm/model.c:585-727) so the
+// lines of bit-identical tensors are identical text. Rows of sequence
+// m->trace_seq are copied to the host after a stream synchronization.
+// ---------------------------------------------------------------------------
+static uint64_t fnv1a64(const uint8_t *p, size_t n) {
+    uint64_t h = 0xcbf29ce484222325ULL;
+    for (size_t i = 0; i < n; ++i) h = (h ^ p[i]) * 0x100000001b3ULL;
+    return h;
+}
+
+static void trace_floats(FILE *f, const char *key, const float *v, int n) {
+    fprintf(f, ",\"%s\":[", key);
+    for (int i = 0; i < n; ++i) {
+        if (i) fputc(',', f);
+        if (isnan(v[i])) fputs("\"nan\"", f);
+        else if (isinf(v[i])) fputs(v[i] < 0.0f ? "\"-inf\"" : "\"inf\"", f);
+        else fprintf(f, "%.9g", v[i]);
+    }
+    fprintf(f, "],\"%s_hex\":[", key);
+    for (int i = 0; i < n; ++i) {
+        uint32_t u;
+        memcpy(&u, &v[i], 4);
+        fprintf(f, "%s\"%08x\"", i ? "," : "", u);
+    }
+    fputc(']', f);
+}
+
+static int trace_row(qh_slm *m, const char *op, const float *d_rows, int64_t n, const char *fmt, ...) {
+    char name[64];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(name, sizeof(name), fmt, ap);
+    va_end(ap);
+    if (n > m->trace_cap) return QH_ERR_INVALID;
+    CK(qh_stream_sync(m->stream));
+    CK(qh_memcpy_d2h(m->trace_buf, d_rows + (int64_t)m->trace_seq * n, (size_t)n * 4, m->stream));
+    CK(qh_stream_sync(m->stream));
+    const float *v = m->trace_buf;
+    FILE *f = m->trace_fp;
+    const int k = n < 8 ? (int)n : 8;
+    float sum = 0.0f;
+    int n_nan = 0, n_inf = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        if (isnan(v[i])) ++n_nan;
+        else if (isinf(v[i])) ++n_inf;
+        else sum += v[i];
+    }
+    fprintf(f,
+            "{\"name\":\"%s\",\"op\":\"%s\",\"type\":\"f32\",\"ne\":[%lld,1,1,1],\"nb\":[4,%lld,%lld,%lld],"
+            "\"nbytes\":%zu,\"fnv64\":\"%016llx\"",
+            name, op, (long long)n, (long long)(n * 4), (long long)(n * 4), (long long)(n * 4), (size_t)n * 4,
+            (unsigned long long)fnv1a64((const uint8_t *)v, (size_t)n * 4));
+    trace_floats(f, "head", v, k);
+    trace_floats(f, "tail", v + (n - k), k);
+    fprintf(f, ",\"sum\":%.9g,\"n_nan\":%d,\"n_inf\":%d}\n", sum, n_nan, n_inf);
+    return ferror(f) ? QH_ERR_INVALID : QH_OK;
+}
+
+int qh_slm_trace(qh_slm *m, int32_t seq, const char *path) {
+    if (!m || !path || seq < 0 || seq >= m->B) return QH_ERR_INVALID;
+    const qh_slm_config *c = &m->cfg;
+    int64_t cap = c->vocab;
+    const int64_t conv_dim = 3 * (int64_t)c->gdn_heads * c->gdn_head_dim;
+    if (conv_dim > cap) cap = conv_dim;
+    if (2 * (int64_t)c->n_heads * c->head_dim > cap) cap = 2 * (int64_t)c->n_heads * c->head_dim;
+    if (c->ffn > cap) cap = c->ffn;
+    if (cap > m->trace_cap) {
+        float *b = (float *)realloc(m->trace_buf, (size_t)cap * 4);
+        if (!b) return QH_ERR_INVALID;
+        m->trace_buf = b;
+        m->trace_cap = cap;
+    }
+    if (m->trace_fp) fclose(m->trace_fp);
+    m->trace_fp = fopen(path, "w");
+    if (!m->trace_fp) return QH_ERR_INVALID;
+    m->trace_seq = seq;
+    return QH_OK;
+}
+
 // One step for all sequences: the forward pass of tokens m->d_tok at
 // position d_ctl[0], the greedy picks, then the device-side feed of the next
 // inputs. Launches only (no allocation, no synchronization), so it is
@@ -501,22 +590,39 @@ static int forward(qh_slm *m) {
     const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
     const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
     void *s = m->stream;
+    // tracing (qh_slm_trace) records the reference's named intermediates
+    // (slm/qwen.c:318-981, slm/model.c:766-953); the normalized rows, which
+    // the fused kernels only quantize, are recomputed with qh_rmsnorm
+#define TR(op, ptr, n, ...)                                            \
+    do {                                                               \
+        if (m->trace_fp) CK(trace_row(m, (op), (ptr), (n), __VA_ARGS__)); \
+    } while (0)
     CK(qh_embed_q6k(m->tok_embd, H, m->d_tok, B, m->h, s));
+    TR("GET_ROWS", m->h, H, "inp_embd");
     // The residual stream alternates between two buffers: each add writes
     // h + mix into the other one (the fused kernel reads h from many CTAs).
     float *hc = m->h, *hx = m->h2;
     const float *pending = NULL;  // residual branch output not yet added to hc
-#define RESNORM(w, xq)                                                                                 \
+#define RESNORM(w, xq, ADD_NAME, ADD_L, NORM_NAME, NORM_L)                                            \
     do {                                                                                               \
+        const int added_ = pending != NULL;                                                            \
         CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, B, c->norm_eps, (xq), m->xq_tile, s)); \
         if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                           \
         pending = NULL;                                                                                \
+        if (m->trace_fp) {                                                                             \
+            if (added_) TR("ADD", hc, H, ADD_NAME, ADD_L);                                             \
+            CK(qh_rmsnorm(hc, (w), H, B, c->norm_eps, m->hn, s));                                      \
+            TR("RMS_NORM", m->hn, H, NORM_NAME, NORM_L);                                               \
+        }                                                                                              \
     } while (0)
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        RESNORM(Ly->attn_norm, m->xq_h);
+        RESNORM(Ly->attn_norm, m->xq_h, "l_out-%d", l - 1, "attn_norm-%d", l);
         CK(run_plans(m, &Ly->p_in));
         if (Ly->is_attn) {
+            TR("MUL_MAT", m->qraw, 2 * qdim, "Qfull-%d", l);
+            TR("MUL_MAT", m->kb, kvd, "Kcur-%d", l);
+            TR("MUL_MAT", m->vb, kvd, "Vcur-%d", l);
             const int64_t ai = Ly->attn_index;
             uint16_t *kc = m->kcache + ai * B * c->max_pos * kvd;
             uint16_t *vc = m->vcache + ai * B * c->max_pos * kvd;
@@ -528,10 +634,28 @@ static int forward(qh_slm *m) {
             CK(m->use_gemm ? qh_quantize_q8kt(m->actx, qdim, B, m->xq_h, s)
                            : qh_quantize_q8k(m->actx, qdim, B, m->xq_h, s));
         } else {
+            TR("MUL_MAT", m->qkv, conv_dim, "attn_qkv-%d", l);
+            TR("MUL_MAT", m->at, c->gdn_heads, "alpha-%d", l);
+            TR("MUL_MAT", m->bt, c->gdn_heads, "beta-%d", l);
             const int64_t gi = Ly->gdn_index;
             float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
-            if (m->use_gemm) {  /* many sequences: heads as independent CTAs, then the quantizer */
+            if (m->trace_fp) {  /* the unfused chain, whose intermediates are traced */
+                CK(qh_gdn_pre(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, B, c->gdn_heads,
+                              c->gdn_head_dim, c->conv_kernel, m->d_ctl, m->gq, m->gk, m->gv, m->gbeta, m->gg, s));
+                TR("VIEW", m->gv, kdim, "V_raw-%d", l);
+                TR("L2_NORM_SCALE", m->gq, kdim, "Q_l2norm-%d", l);
+                TR("L2_NORM", m->gk, kdim, "K_l2norm-%d", l);
+                TR("SIGMOID", m->gbeta, c->gdn_heads, "beta_in-%d", l);
+                CK(qh_gdn_recurrence(state, m->gq, m->gk, m->gv, m->gbeta, m->gg, B, c->gdn_heads, c->gdn_head_dim,
+                                     m->gout, s));
+                TR("RECURRENT", m->gout, kdim, "attn_output-%d", l);
+                CK(qh_gdn_gated_norm(m->gout, m->z, Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->norm_eps,
+                                     m->gy, s));
+                TR("RMS_NORM_GATED", m->gy, kdim, "y_norm-%d", l);
+                CK(m->use_gemm ? qh_quantize_q8kt(m->gy, kdim, B, m->xq_gdn, s)
+                               : qh_quantize_q8k(m->gy, kdim, B, m->xq_gdn, s));
+            } else if (m->use_gemm) {  /* many sequences: heads as independent CTAs, then the quantizer */
                 CK(qh_gdn_fused_y(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
                                   Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps,
                                   m->d_ctl, m->gy, s));
@@ -543,16 +667,24 @@ static int forward(qh_slm *m) {
             }
         }
         CK(run_plans(m, &Ly->p_out));
+        if (Ly->is_attn)
+            TR("MUL_MAT", m->mix, H, "attn_out-%d", l);
+        else
+            TR("MUL_MAT", m->mix, H, "ssm_out-%d", l);
+        TR(Ly->is_attn ? "ATTN" : "SSM", m->mix, H, "mix-%d", l);
         pending = m->mix;
-        RESNORM(Ly->ffn_norm, m->xq_h);
+        RESNORM(Ly->ffn_norm, m->xq_h, "mix_residual-%d", l, "ffn_norm-%d", l);
         CK(run_plans(m, &Ly->p_ffn));
         CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, m->xq_tile, s));
         CK(run_plans(m, &Ly->p_down));
+        TR("MUL_MAT", m->mix, H, "ffn_out-%d", l);
         pending = m->mix;
     }
-    RESNORM(m->out_norm, m->xq_h);
+    RESNORM(m->out_norm, m->xq_h, "l_out-%d", c->n_layers - 1, "result_norm", 0);
 #undef RESNORM
     CK(run_plans(m, &m->p_head));
+    TR("MUL_MAT", m->logits, c->vocab, "result_output");
+#undef TR
     if (m->sampling)
         CK(qh_sample_feed(m->logits, B, c->vocab, m->d_sctl, m->d_hist, c->max_pos + 1, m->d_hist_n, m->d_rng,
                           m->d_next, c->max_pos, m->d_ctl, m->d_tok, m->d_picks, m->d_sticket, s));
@@ -598,7 +730,14 @@ int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next
     m->h_ctl[1] = 0;
     CK(qh_memcpy_h2d(m->d_ctl, m->h_ctl, 2 * sizeof(int32_t), m->stream));
     CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * m->B, m->stream));
-    CK(launch_step(m));
+    if (m->trace_fp) {  // a traced step runs its kernels directly
+        const int rc = forward(m);
+        fclose(m->trace_fp);
+        m->trace_fp = NULL;
+        CK(rc);
+    } else {
+        CK(launch_step(m));
+    }
     m->host_pos = pos + 1;
     m->n_prompt = 0;
     CK(qh_memcpy_d2h(m->h_next, m->d_next, sizeof(int32_t) * m->B, m->stream));
@@ -912,6 +1051,126 @@ int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, 
     free(picks);
     return rc;
 }
+
+// ---------------------------------------------------------------------------
+// Snapshot / restore (slm_ctx_snapshot / slm_ctx_restore, slm/model.c:1262-
+// 1371): a device-memory copy of everything a step reads and writes --
+// position and feed state, generator words, KV rows 0..pos-1 of every
+// attention layer, conv rings and recurrent states, prompts, picks and the
+// sampler history.
+// ---------------------------------------------------------------------------
+struct qh_slm_snap {
+    const qh_slm *owner;
+    int32_t host_pos, n_prompt, kv_rows;
+    int64_t bytes;
+    void *ctl, *tok, *next, *rng, *picks, *prompt, *hist, *hist_n, *ring, *state, *k, *v;
+};
+
+typedef struct {
+    void **snap_field;
+    void *model_buf;
+    size_t bytes;
+} snap_part;
+
+static int snap_parts(const qh_slm *m, qh_slm_snap *s, snap_part *parts) {
+    const qh_slm_config *c = &m->cfg;
+    const int64_t B = m->B, kdim = (int64_t)c->gdn_heads * c->gdn_head_dim;
+    const int64_t ng = m->n_gdn > 0 ? m->n_gdn : 1;
+    int n = 0;
+#define PART(field, buf, nb) parts[n++] = (snap_part){(void **)&s->field, (void *)(buf), (size_t)(nb)}
+    PART(ctl, m->d_ctl, 16);
+    PART(tok, m->d_tok, B * 4);
+    PART(next, m->d_next, B * 4);
+    PART(rng, m->d_rng, B * 16);
+    PART(picks, m->d_picks, B * c->max_pos * 4);
+    PART(prompt, m->d_prompt, B * c->max_pos * 4);
+    PART(hist, m->d_hist, B * (c->max_pos + 1) * 4);
+    PART(hist_n, m->d_hist_n, B * 4);
+    PART(ring, m->ring, ng * B * c->conv_kernel * 3 * kdim * 4);
+    PART(state, m->state, ng * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim * 4);
+#undef PART
+    return n;
+}
+
+int qh_slm_snapshot(qh_slm *m, qh_slm_snap **out) {
+    if (!m || !out) return QH_ERR_INVALID;
+    *out = NULL;
+    const qh_slm_config *c = &m->cfg;
+    qh_slm_snap *s = (qh_slm_snap *)calloc(1, sizeof(qh_slm_snap));
+    if (!s) return QH_ERR_INVALID;
+    s->owner = m;
+    s->host_pos = m->host_pos;
+    s->n_prompt = m->n_prompt;
+    s->kv_rows = m->host_pos;
+    snap_part parts[16];
+    const int np = snap_parts(m, s, parts);
+    int rc = QH_OK;
+    for (int i = 0; i < np && !rc; ++i) {
+        rc = qh_malloc(parts[i].snap_field, parts[i].bytes);
+        if (!rc && cudaMemcpyAsync(*parts[i].snap_field, parts[i].model_buf, parts[i].bytes, cudaMemcpyDeviceToDevice,
+                                   m->stream) != cudaSuccess)
+            rc = QH_ERR_CUDA;
+        s->bytes += (int64_t)parts[i].bytes;
+    }
+    // KV rows 0..pos-1: the (layer, sequence) rows of a cache share one pitch
+    const int64_t kvd = (int64_t)c->n_kv_heads * c->head_dim, rows = (int64_t)m->n_attn * m->B;
+    if (!rc && s->kv_rows > 0 && rows > 0) {
+        const size_t w = (size_t)s->kv_rows * kvd * 2, pitch = (size_t)c->max_pos * kvd * 2;
+        rc = qh_malloc(&s->k, w * rows);
+        if (!rc) rc = qh_malloc(&s->v, w * rows);
+        if (!rc && (cudaMemcpy2DAsync(s->k, w, m->kcache, pitch, w, (size_t)rows, cudaMemcpyDeviceToDevice,
+                                      m->stream) != cudaSuccess ||
+                    cudaMemcpy2DAsync(s->v, w, m->vcache, pitch, w, (size_t)rows, cudaMemcpyDeviceToDevice,
+                                      m->stream) != cudaSuccess))
+            rc = QH_ERR_CUDA;
+        s->bytes += 2 * (int64_t)(w * rows);
+    }
+    if (!rc) rc = qh_stream_sync(m->stream);
+    if (rc) {
+        qh_slm_snapshot_free(s);
+        return rc;
+    }
+    *out = s;
+    return QH_OK;
+}
+
+int qh_slm_restore(qh_slm *m, const qh_slm_snap *s) {
+    if (!m || !s || s->owner != m) return QH_ERR_INVALID;
+    const qh_slm_config *c = &m->cfg;
+    qh_slm_snap view = *s;
+    snap_part parts[16];
+    const int np = snap_parts(m, &view, parts);
+    for (int i = 0; i < np; ++i)
+        if (cudaMemcpyAsync(parts[i].model_buf, *parts[i].snap_field, parts[i].bytes, cudaMemcpyDeviceToDevice,
+                            m->stream) != cudaSuccess)
+            return QH_ERR_CUDA;
+    const int64_t kvd = (int64_t)c->n_kv_heads * c->head_dim, rows = (int64_t)m->n_attn * m->B;
+    if (s->kv_rows > 0 && rows > 0) {
+        const size_t w = (size_t)s->kv_rows * kvd * 2, pitch = (size_t)c->max_pos * kvd * 2;
+        if (cudaMemcpy2DAsync(m->kcache, pitch, s->k, w, w, (size_t)rows, cudaMemcpyDeviceToDevice, m->stream) !=
+                cudaSuccess ||
+            cudaMemcpy2DAsync(m->vcache, pitch, s->v, w, w, (size_t)rows, cudaMemcpyDeviceToDevice, m->stream) !=
+                cudaSuccess)
+            return QH_ERR_CUDA;
+    }
+    CK(qh_stream_sync(m->stream));
+    m->host_pos = s->host_pos;
+    m->n_prompt = s->n_prompt;
+    return QH_OK;
+}
+
+void qh_slm_snapshot_free(qh_slm_snap *s) {
+    if (!s) return;
+    void *bufs[] = {s->ctl, s->tok, s->next, s->rng, s->picks, s->prompt, s->hist, s->hist_n, s->ring, s->state,
+                    s->k, s->v};
+    for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); ++i)
+        if (bufs[i]) qh_free(bufs[i]);
+    free(s);
+}
+
+int64_t qh_slm_snapshot_bytes(const qh_slm_snap *s) { return s ? s->bytes : -1; }
+
+int32_t qh_slm_snapshot_pos(const qh_slm_snap *s) { return s ? s->host_pos : -1; }
 
 void *qh_slm_stream(const qh_slm *m) { return m ? (void *)m->stream : NULL; }
 

@@ -314,6 +314,32 @@ def sample(sp, logits, hist, hist_n, rng):
     return out
 
 
+class Snapshot:
+    """A qh_slm_snap (device memory), freed with the object."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    @property
+    def nbytes(self) -> int:
+        return int(lib().qh_slm_snapshot_bytes(self.handle))
+
+    @property
+    def pos(self) -> int:
+        return int(lib().qh_slm_snapshot_pos(self.handle))
+
+    def close(self):
+        if self.handle:
+            lib().qh_slm_snapshot_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Slm:
     """Device model with n_seq sequences (qh_slm_create)."""
 
@@ -356,6 +382,19 @@ class Slm:
                                             st.ctypes.data if st.size else None, int(st.size), out.ctypes.data,
                                             n_out.ctypes.data), "qh_slm_generate_sampled")
         return [out[b, :n_out[b]].copy() for b in range(self.n_seq)]
+
+    def trace(self, seq: int, path: str):
+        """qh_slm_trace: the next step writes sequence seq's JSONL trace to path."""
+        check(lib().qh_slm_trace(self.handle, seq, path.encode()), "qh_slm_trace")
+
+    def snapshot(self) -> "Snapshot":
+        """qh_slm_snapshot: the decode state of every sequence."""
+        s = C.c_void_p()
+        check(lib().qh_slm_snapshot(self.handle, C.byref(s)), "qh_slm_snapshot")
+        return Snapshot(s)
+
+    def restore(self, snap: "Snapshot"):
+        check(lib().qh_slm_restore(self.handle, snap.handle), "qh_slm_restore")
 
     def begin(self, prompt):
         p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
