@@ -329,7 +329,8 @@ def run_gemm(qh, torch, steps: int, warmup: int):
     return out
 
 
-def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_new: int):
+def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_new: int,
+               profile_step: bool = False):
     """Greedy decode of B sequences per GPU: n_prompt teacher-forced steps,
     then n_new steps timed with CUDA events on the model's stream; the
     sampled tokens are gathered over NCCL after every step when world > 1.
@@ -375,6 +376,14 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     ev[2].record(stream)
     picks = slm.picks(n_prompt - 1, n_new)  # synchronizes
     wall = time.perf_counter() - t0
+    if profile_step and rank == 0:
+        # one more decode step between cudaProfilerStart/Stop, outside the
+        # timed region, for `ncu --profile-from-start off` launch lists
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        slm.advance(1)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
     torch.cuda.synchronize()
     prefill_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
     prefill_ms, decode_ms, wall = max_over_ranks(dist, [prefill_ms, decode_ms, wall], "cuda")
@@ -559,7 +568,8 @@ def run_ours(args):
         for B, n_prompt in ((1, 64), (args.decode_batch, args.decode_prompt)):
             if args.decode_only_batch and B != args.decode_only_batch:
                 continue
-            decode[f"batch{B}"], _, _, _ = run_decode(qh, torch, dist, world, rank, B, n_prompt, args.decode_new)
+            decode[f"batch{B}"], _, _, _ = run_decode(qh, torch, dist, world, rank, B, n_prompt, args.decode_new,
+                                                      args.profile_step)
         runs = list(decode.values())
         decode.update({"clocks": dclk.stop(),
                   "data": "synthetic Qwen3.5-0.8B-shaped weights (Q4_K mix), seeded random prompts",
@@ -641,6 +651,9 @@ def main():
     ap.add_argument("--decode-new", type=int, default=256, help="greedy tokens per decode run")
     ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens of the batched decode")
     ap.add_argument("--decode-only-batch", type=int, default=0, help="run only the decode of this batch size")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after the timed decode, run one more step between cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

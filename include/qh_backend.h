@@ -184,6 +184,27 @@ typedef struct qh_matvec_plan_s *qh_matvec_plan;
 /* n_tok in [1, 8]. */
 int qh_matvec_plan_create(int type, const qh_matvec_job *h_jobs, int n_jobs, int64_t n_tok,
                           qh_matvec_plan *out_plan);
+/* Fused input: instead of reading the jobs' shared Q8_K activation (d_xq of
+ * the jobs), every CTA of the launch forms it itself from fp32 rows
+ * [n_tok][k] -- the step that otherwise runs as its own kernel just before
+ * the projections (one launch fewer, no activation round trip through
+ * memory), with the same arithmetic bit for bit:
+ *   QH_FUSE_RMSNORM  residual add + RMSNorm (tensor_add + tensor_rms_norm,
+ *                    slm/tensor.c:285, 348-369): rows d_a (+ d_b when
+ *                    given), weight d_w, eps; with d_b the sum h = a + b is
+ *                    also written to d_h_out (the updated residual stream);
+ *   QH_FUSE_SWIGLU   silu(d_a) * d_b (slm/qwen.c:952-955);
+ *   QH_FUSE_QUANT    d_a as is;
+ *   0                back to d_xq.
+ * All jobs must share k (<= 4096 for RMSNorm); K-quant plans only. The
+ * pointers are captured by the plan: qh_matvec_plan_run launches with them.
+ * The outputs equal those of quantizing first (qh_rmsnorm_q8k,
+ * qh_swiglu_q8k, qh_quantize_q8k) and running the plan on that activation. */
+#define QH_FUSE_RMSNORM 1
+#define QH_FUSE_SWIGLU 2
+#define QH_FUSE_QUANT 3
+int qh_matvec_plan_fuse_input(qh_matvec_plan plan, int mode, const float *d_a, const float *d_b, const float *d_w,
+                              float eps, float *d_h_out);
 int qh_matvec_plan_run(qh_matvec_plan plan, void *stream);
 /* Rows per tile, pipeline stages, grid size and shared memory chosen. */
 int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, int *grid,
@@ -238,8 +259,21 @@ int64_t qh_gemm_scratch_bytes(const qh_gemm_job *jobs, int n_jobs, int64_t k, in
 #define QH_GEMM_WEIGHTS_READY 1 /* flags: the tiled weights were complete before the previous
                                    kernel on the stream started (e.g. packed, then synchronized):
                                    the kernel streams them in while that kernel finishes */
+#define QH_GEMM_EXPANDED 2      /* flags: jobs[].d_wt are expanded weights (qh_gemm_expand_weights):
+                                   the kernel streams the MMA operands directly, no expansion */
 int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void *d_q8kt, int64_t n_tok,
             void *d_scratch, int64_t scratch_bytes, int32_t flags, void *stream);
+
+/* Expanded weights: the tiled weights (qh_gemm_pack_weights) turned once
+ * into the tensor-core operand image of every 128-row tile and super-block
+ * -- the int8 planes whose dots with the Q8_K activations are the
+ * reference's block integers (hi/lo planes of scale * weight, the min row
+ * for Q4_K/Q5_K), plus the rows' fp16 d/dmin as fp32 -- so a qh_gemm with
+ * QH_GEMM_EXPANDED only streams and multiplies: the form for decoding many
+ * sequences, where each weight is used by one 64-token tile per step.
+ * 2.09 (Q4_K/Q5_K) or 2.03 (Q6_K) bytes per weight; bit-identical results. */
+int64_t qh_gemm_expanded_bytes(int type, int64_t k, int64_t out_f);
+int qh_gemm_expand_weights(int type, const void *d_wt, int64_t k, int64_t out_f, void *d_we, void *stream);
 
 /* One-call form of tensor_matmul_*_f32 for n_tok tokens: packs the weights
  * and quantizes the activations into d_work (qh_matmul_gemm_workspace_bytes)

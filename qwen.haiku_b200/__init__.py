@@ -99,6 +99,9 @@ SIGNATURES = {
     "qh_matvec_plan_destroy": (_I, [_P]),
     "qh_gemm_weight_bytes": (_I64, [_I, _I64, _I64]),
     "qh_gemm_pack_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
+    "qh_gemm_expanded_bytes": (_I64, [_I, _I64, _I64]),
+    "qh_matvec_plan_fuse_input": (_I, [_P, _I, _P, _P, _P, C.c_float, _P]),
+    "qh_gemm_expand_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
     "qh_q8kt_bytes": (_I64, [_I64, _I64]),
     "qh_quantize_q8kt": (_I, [_P, _I64, _I64, _P, _P]),
     "qh_gemm_scratch_bytes": (_I64, [_P, _I, _I64, _I64]),

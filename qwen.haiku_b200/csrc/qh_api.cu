@@ -169,6 +169,8 @@ int *device_error_word() {
 struct qh_matvec_plan_s {
     int type;
     int device;
+    int n_tok, sms;
+    std::vector<qh::GemvJob> jobs;  // as planned (for re-planning with a fused input)
     qh::GemvParams params;
     qh::GemvGeometry geom;
     qh::GemvJob *d_table;
@@ -339,6 +341,9 @@ int qh_matvec_plan_create(int type, const qh_matvec_job *h_jobs, int n_jobs, int
     }
     qh_matvec_plan p = new qh_matvec_plan_s{};
     p->type = type;
+    p->n_tok = static_cast<int>(n_tok);
+    p->sms = sms;
+    p->jobs = jobs;
     cudaGetDevice(&p->device);
     cudaError_t e = qh::gemv_plan(type, jobs.data(), n_jobs, static_cast<int>(n_tok), sms, &p->params, &p->geom);
     if (e != cudaSuccess) {
@@ -360,6 +365,45 @@ int qh_matvec_plan_create(int type, const qh_matvec_job *h_jobs, int n_jobs, int
         p->params.table = p->d_table;
     }
     *out_plan = p;
+    return QH_OK;
+}
+
+int qh_matvec_plan_fuse_input(qh_matvec_plan plan, int mode, const float *d_a, const float *d_b, const float *d_w,
+                              float eps, float *d_h_out) {
+    if (!plan) return fail(QH_ERR_INVALID, "plan_fuse_input: null plan");
+    if (mode < 0 || mode > QH_FUSE_QUANT) return fail(QH_ERR_INVALID, "plan_fuse_input: unknown mode %d", mode);
+    if (mode != 0 && plan->type == QH_GGUF_Q8_0)
+        return fail(QH_ERR_UNSUPPORTED, "plan_fuse_input: Q8_0 weights take Q8_0 activations");
+    const int64_t k = plan->jobs[0].k;
+    for (const qh::GemvJob &j : plan->jobs)
+        if (j.k != k) return fail(QH_ERR_INVALID, "plan_fuse_input: the jobs read inputs of different sizes");
+    if (mode != 0 && !d_a) return fail(QH_ERR_INVALID, "plan_fuse_input: null input");
+    if (mode == QH_FUSE_SWIGLU && !d_b) return fail(QH_ERR_INVALID, "plan_fuse_input: SwiGLU needs gate and up");
+    if (mode == QH_FUSE_RMSNORM && (!d_w || (d_b && !d_h_out) || (d_h_out && (d_h_out == d_a || d_h_out == d_b))))
+        return fail(QH_ERR_INVALID, "plan_fuse_input: RMSNorm needs a weight, and h_out (not an input) with a residual");
+    if (mode == QH_FUSE_RMSNORM && k > 16 * QH_QK)
+        return fail(QH_ERR_UNSUPPORTED, "plan_fuse_input: RMSNorm rows longer than 4096");
+    std::vector<qh::GemvJob> jobs = plan->jobs;
+    qh::GemvParams p{};
+    qh::GemvGeometry g{};
+    cudaError_t e = qh::gemv_plan(plan->type, jobs.data(), static_cast<int>(jobs.size()), plan->n_tok, plan->sms, &p, &g,
+                                  mode);
+    if (e != cudaSuccess) return fail(QH_ERR_INVALID, "plan_fuse_input: cannot tile these rows (%s)", cudaGetErrorString(e));
+    p.err_flag = plan->params.err_flag;
+    p.table = plan->params.table;
+    if (mode) {
+        p.xa = d_a;
+        p.xb = d_b;
+        p.xw = d_w;
+        p.eps = eps;
+        p.xh_out = mode == QH_FUSE_RMSNORM ? d_h_out : nullptr;
+    }
+    if (plan->d_table) {  // tile ranges of the table follow the new tiling
+        e = cudaMemcpy(plan->d_table, jobs.data(), sizeof(qh::GemvJob) * jobs.size(), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, "plan_fuse_input: job table");
+    }
+    plan->params = p;
+    plan->geom = g;
     return QH_OK;
 }
 

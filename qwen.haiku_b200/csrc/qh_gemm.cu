@@ -51,9 +51,10 @@ constexpr int kGemmRows = 128;           // MMA M: weight rows per tile
 constexpr int kGemmTok = QH_Q8KT_TILE;   // MMA N: tokens per tile (64)
 constexpr int kExpWarps = 8;             // expanders: 2 threads per weight row
 constexpr int kEpiWarps = 8;             // epilogue: 4 lane groups x 2 token halves
-constexpr int kGemmThreads = 32 * (kExpWarps + kEpiWarps + 2);
-constexpr int kProducerWarp = kExpWarps + kEpiWarps;
-constexpr int kMmaWarp = kProducerWarp + 1;
+// Warp roles: [expanders][epilogue][producer][MMA]; with expanded weights
+// there are no expanders and the CTA is 10 warps.
+__host__ __device__ constexpr int gemm_exp_warps(bool exp) { return exp ? 0 : kExpWarps; }
+__host__ __device__ constexpr int gemm_threads(bool exp) { return 32 * (gemm_exp_warps(exp) + kEpiWarps + 2); }
 constexpr int kGemmMaxJobs = 8;
 constexpr int kGemmMaxStages = 4;
 constexpr int kPlaneBytes = kGemmRows * QH_QK;  // 32 KB: one int8 operand plane
@@ -258,15 +259,29 @@ __device__ __forceinline__ Item decode_item(const GemmParams &p, int item) {
     return it;
 }
 
-// Shared-memory plan of one CTA (offsets from the dynamic smem base).
+// Expanded weights (qh_gemm_expand_weights): per (row tile, block) the A
+// operand exactly as the expander warps build it -- hi plane, lo plane, min
+// rows (Q4_K/Q5_K) -- followed by the rows' (d, dmin) as float2[128].
 template <int TYPE>
+struct ExpBlock {
+    static constexpr int kA = 2 * kPlaneBytes + (KQ<TYPE>::kMins ? kMinRowBytes : 0);
+    static constexpr int kBytes = kA + kGemmRows * 8;
+};
+__host__ __device__ constexpr int expanded_block_bytes(int type) {
+    return type == QH_GGUF_Q6_K ? 2 * kPlaneBytes + kGemmRows * 8 : 2 * kPlaneBytes + kMinRowBytes + kGemmRows * 8;
+}
+
+// Shared-memory plan of one CTA (offsets from the dynamic smem base). EXP:
+// the stages hold expanded weights and the MMAs read A from the stage (no
+// A buffers, no expansion).
+template <int TYPE, bool EXP = false>
 struct GemmSmem {
-    static constexpr int kWB = kGemmRows * KQ<TYPE>::kPadded;                   // weight tile block
+    static constexpr int kWB = EXP ? ExpBlock<TYPE>::kBytes : kGemmRows * KQ<TYPE>::kPadded;  // weight tile block
     static constexpr int kXB = KQ<TYPE>::kMins ? QH_Q8KT_BLOCK_BYTES : QH_Q8KT_MIN_OFF;  // activation bytes copied
     static constexpr int kStage = kWB + kXB;
     static constexpr int kABuf = 2 * kPlaneBytes + (KQ<TYPE>::kMins ? kMinRowBytes : 0);
-    static constexpr int kA = kGemmHeader;                                       // 2 A buffers
-    static constexpr int kScales = kA + 2 * kABuf;                               // ring of token scales
+    static constexpr int kA = kGemmHeader;                                       // 2 A buffers (not EXP)
+    static constexpr int kScales = kA + (EXP ? 0 : 2 * kABuf);                   // ring of token scales
     static constexpr int kRowScales = kScales + kRing * kGemmTok * 4;            // ring of row (d, dmin)
     static constexpr int kStages = kRowScales + kRing * kGemmRows * 8;           // stage ring
     static constexpr int kNStages = (kGemmSmemMax - kStages - kMinRowBytes) / kStage > kGemmMaxStages
@@ -279,7 +294,10 @@ struct GemmSmem {
     static_assert(kNStages >= 2 && kTotal <= kGemmSmemMax, "shared memory plan");
 };
 
-// Warp roles (576 threads, one CTA per SM):
+// Warp roles (576 threads, one CTA per SM; with expanded weights, EXP, the
+// expanders are absent -- 320 threads, epilogue warps 0-7, producer 8, MMA 9 --
+// and the MMAs read A straight from the stage, whose row scales the MMA warp
+// moves to the ring before the stage is released):
 //   warps 0-7   expanders: two threads per weight row build the A planes
 //               of a super-block into one of two A buffers and copy its
 //               scales to a small ring;
@@ -295,9 +313,11 @@ struct GemmSmem {
 // accumulators readable), acc_empty[2] (8 epilogue warps read them),
 // a_ready[2] (8 expander warps wrote a block's A buffer and scales),
 // scale_ready[2] (the MMA thread passes the scales on to the epilogue).
-template <int TYPE>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
-    using L = GemmSmem<TYPE>;
+template <int TYPE, bool EXP>
+__global__ void __launch_bounds__(gemm_threads(EXP), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+    using L = GemmSmem<TYPE, EXP>;
+    constexpr int XW = gemm_exp_warps(EXP), kProducerWarp = XW + kEpiWarps, kMmaWarp = kProducerWarp + 1;
+    constexpr int kGemmThreads = gemm_threads(EXP);
     constexpr int BBP = KQ<TYPE>::kPadded, MINS = KQ<TYPE>::kMins;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -411,7 +431,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 // two blocks back
                 bool ok = true;
                 if (lane == 0)
-                    ok = !*abort_flag && mbar_wait(&a_ready[buf], ph) &&
+                    ok = !*abort_flag &&
+                         (EXP ? mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u) : mbar_wait(&a_ready[buf], ph)) &&
                          mbar_wait(&xfull[s], static_cast<uint32_t>(i / S) & 1u) &&
                          (ib < 2 || mbar_wait(&acc_empty[buf], ph ^ 1u));
                 ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -423,14 +444,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     stop = true;
                     break;
                 }
-                const uint8_t *xst = stages + static_cast<int64_t>(s) * L::kStage + L::kWB;
+                const uint8_t *wst = stages + static_cast<int64_t>(s) * L::kStage;
+                const uint8_t *xst = wst + L::kWB;
                 if (lane < kGemmTok / 4)
                     reinterpret_cast<uint4 *>(tok_scale + ring * kGemmTok)[lane] =
                         reinterpret_cast<const uint4 *>(xst + QH_Q8KT_D_OFF)[lane];
+                if (EXP) {
+                    // the rows' (d, dmin) leave the stage before it is released
+                    const uint4 *src = reinterpret_cast<const uint4 *>(wst + L::kABuf);
+                    uint4 *dst = reinterpret_cast<uint4 *>(row_scale + ring * kGemmRows);
+                    dst[lane] = src[lane];
+                    dst[lane + 32] = src[lane + 32];
+                }
                 __syncwarp();
                 if (lane == 0) {
                     tc::fence_after_sync();
-                    const uint32_t a0 = smem_addr(smem + L::kA + buf * L::kABuf), b0 = smem_addr(xst);
+                    const uint32_t a0 = EXP ? smem_addr(wst) : smem_addr(smem + L::kA + buf * L::kABuf);
+                    const uint32_t b0 = smem_addr(xst);
                     const uint32_t dcol = tmem + buf * kAccCols;
                     const uint64_t ad0 = tc::smem_desc(a0, kGemmRows * 16, 128);
                     const uint64_t bd0 = tc::smem_desc(b0, kGemmTok * 16, 128);
@@ -456,43 +486,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 }
             }
         }
-    } else if (warp < kExpWarps) {
-        // ----- expanders -----
-        const int r = tid >> 1, h = tid & 1;
-        int i = 0, ib = 0;
-        bool stop = false;
-        for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
-            const Item it = decode_item(p, item);
-            for (int b = it.b0; b < it.b1; ++b, ++i, ++ib) {
-                const int s = i % S, buf = ib & 1, ring = ib % kRing;
-                // stage landed; the MMAs two blocks back are done with this A buffer
-                const bool ok = __all_sync(0xffffffffu,
-                                           !*abort_flag && mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u) &&
-                                               (ib < 2 || mbar_wait(&mma_done[buf], static_cast<uint32_t>((ib - 2) >> 1) & 1u)));
-                if (!ok) {
-                    stop = true;
-                    break;
+    } else if (warp < XW) {
+        // ----- expanders (idle with expanded weights) -----
+        if constexpr (!EXP) {
+            const int r = tid >> 1, h = tid & 1;
+            int i = 0, ib = 0;
+            bool stop = false;
+            for (int item = blockIdx.x; item < p.total_items && !stop; item += gridDim.x) {
+                const Item it = decode_item(p, item);
+                for (int b = it.b0; b < it.b1; ++b, ++i, ++ib) {
+                    const int s = i % S, buf = ib & 1, ring = ib % kRing;
+                    // stage landed; the MMAs two blocks back are done with this A buffer
+                    const bool ok = __all_sync(0xffffffffu,
+                                               !*abort_flag && mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u) &&
+                                                   (ib < 2 || mbar_wait(&mma_done[buf], static_cast<uint32_t>((ib - 2) >> 1) & 1u)));
+                    if (!ok) {
+                        stop = true;
+                        break;
+                    }
+                    const uint8_t *wst = stages + static_cast<int64_t>(s) * L::kStage;
+                    const uint8_t *raw = wst + r * BBP;
+                    expand<TYPE>(raw, h, r, smem + L::kA + buf * L::kABuf);
+                    if (h == 0) {
+                        const uint32_t dd = *reinterpret_cast<const uint32_t *>(raw + (TYPE == QH_GGUF_Q6_K ? 208 : 0));
+                        row_scale[ring * kGemmRows + r] =
+                            make_float2(h2f_bits(dd), TYPE == QH_GGUF_Q6_K ? 0.0f : h2f_bits(dd >> 16));
+                    }
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_ready[buf]);
                 }
-                const uint8_t *wst = stages + static_cast<int64_t>(s) * L::kStage;
-                const uint8_t *raw = wst + r * BBP;
-                expand<TYPE>(raw, h, r, smem + L::kA + buf * L::kABuf);
-                if (h == 0) {
-                    const uint32_t dd = *reinterpret_cast<const uint32_t *>(raw + (TYPE == QH_GGUF_Q6_K ? 208 : 0));
-                    row_scale[ring * kGemmRows + r] =
-                        make_float2(h2f_bits(dd), TYPE == QH_GGUF_Q6_K ? 0.0f : h2f_bits(dd >> 16));
-                }
-                tc::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&a_ready[buf]);
             }
-        }
-        if (stop && lane == 0) {
-            report_error(p.err_flag, kDevWaitTimeout);
-            *abort_flag = 1;
+            if (stop && lane == 0) {
+                report_error(p.err_flag, kDevWaitTimeout);
+                *abort_flag = 1;
+            }
         }
     } else {
         // ----- epilogue -----
-        const int ew = warp - kExpWarps;
+        const int ew = warp - XW;
         const int er = 32 * (ew & 3) + lane;  // weight row = TMEM lane
         const int th = ew >> 2;               // token half of the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (ew & 3)) << 16;
@@ -561,7 +593,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     stop = true;
                     break;
                 }
-                if (warp == kExpWarps && lane == 0) {
+                if (warp == XW && lane == 0) {
                     const unsigned prev = atomicAdd(&p.tickets[it.tile], 1u);
                     last_flag = prev == static_cast<unsigned>(p.kchunks - 1);
                     if (last_flag) p.tickets[it.tile] = 0u;
@@ -616,6 +648,27 @@ __global__ void pack_tiles_kernel(const uint8_t *__restrict__ w, int64_t n_rows,
     for (; i < bbp / 2; ++i) dst[i] = 0;
 }
 
+// Expansion of tiled weights into the A-operand image of every (row tile,
+// block) (ExpBlock): CTA (row tile, block), two threads per row running the
+// expander warps' code into global memory, plus the rows' (d, dmin).
+template <int TYPE>
+__global__ void __launch_bounds__(256) expand_tiles_kernel(const uint8_t *__restrict__ wt, int nb,
+                                                           uint8_t *__restrict__ we) {
+    pdl_launch_dependents();
+    pdl_wait();
+    constexpr int BBP = KQ<TYPE>::kPadded;
+    const int64_t tb = static_cast<int64_t>(blockIdx.x) * nb + blockIdx.y;
+    const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
+    const uint8_t *raw = wt + (tb * kGemmRows + r) * BBP;
+    uint8_t *dst = we + tb * ExpBlock<TYPE>::kBytes;
+    expand<TYPE>(raw, h, r, dst);
+    if (h == 0) {
+        const uint32_t dd = *reinterpret_cast<const uint32_t *>(raw + (TYPE == QH_GGUF_Q6_K ? 208 : 0));
+        reinterpret_cast<float2 *>(dst + ExpBlock<TYPE>::kA)[r] =
+            make_float2(h2f_bits(dd), TYPE == QH_GGUF_Q6_K ? 0.0f : h2f_bits(dd >> 16));
+    }
+}
+
 // Q8_K quantization into the tiled layout: CTA (block, token).
 __global__ void __launch_bounds__(256) quantize_q8kt_kernel(const float *__restrict__ x, int k, int n_tok,
                                                             uint8_t *__restrict__ out) {
@@ -627,9 +680,9 @@ __global__ void __launch_bounds__(256) quantize_q8kt_kernel(const float *__restr
     q8k_block256(v, sc, q8k_row(out, k, n_tok, t, QH_Q8KT_TILE), b);
 }
 
-template <int TYPE>
+template <int TYPE, bool EXP>
 static cudaError_t gemm_launch_t(const GemmParams &p0, int sm_count, cudaStream_t stream) {
-    using L = GemmSmem<TYPE>;
+    using L = GemmSmem<TYPE, EXP>;
     GemmParams p = p0;
     p.n_stages = L::kNStages;
     const int smem = L::kTotal;
@@ -637,13 +690,13 @@ static cudaError_t gemm_launch_t(const GemmParams &p0, int sm_count, cudaStream_
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<TYPE, EXP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              L::kTotal);
         if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
     const int grid = std::min(p.total_items, sm_count);
-    return launch_pdl(gemm_kernel<TYPE>, dim3(grid), dim3(kGemmThreads), smem, stream, p);
+    return launch_pdl(gemm_kernel<TYPE, EXP>, dim3(grid), dim3(gemm_threads(EXP)), smem, stream, p);
 }
 
 }  // namespace qh
@@ -686,6 +739,31 @@ int qh_gemm_pack_weights(int type, const void *d_w, int64_t k, int64_t out_f, vo
                                    static_cast<int>(qhf_block_bytes(type)), qh::padded_block_bytes(type),
                                    static_cast<uint8_t *>(d_wt));
     if (e != cudaSuccess) return gcuda(e, "gemm_pack_weights launch");
+    return QH_OK;
+}
+
+int64_t qh_gemm_expanded_bytes(int type, int64_t k, int64_t out_f) {
+    if (!gemm_type_ok(type) || k <= 0 || k % 256 || out_f <= 0) return -1;
+    return ((out_f + qh::kGemmRows - 1) / qh::kGemmRows) * (k / 256) * qh::expanded_block_bytes(type);
+}
+
+int qh_gemm_expand_weights(int type, const void *d_wt, int64_t k, int64_t out_f, void *d_we, void *stream) {
+    if (!gemm_type_ok(type)) return gfail(QH_ERR_UNSUPPORTED, "gemm_expand_weights: type must be Q4_K, Q5_K or Q6_K");
+    if (!d_wt || !d_we || k <= 0 || k % 256 || out_f <= 0 || k / 256 > 65535 || out_f > 0x7fffffffll)
+        return gfail(QH_ERR_INVALID, "gemm_expand_weights: bad arguments");
+    if (!al16(d_wt) || !al16(d_we)) return gfail(QH_ERR_ALIGN, "gemm_expand_weights: misaligned pointer");
+    const dim3 grid(static_cast<unsigned>((out_f + qh::kGemmRows - 1) / qh::kGemmRows), static_cast<unsigned>(k / 256));
+    const uint8_t *wt = static_cast<const uint8_t *>(d_wt);
+    uint8_t *we = static_cast<uint8_t *>(d_we);
+    const int nb = static_cast<int>(k / 256);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    switch (type) {
+        case QH_TYPE_Q4_K: e = qh::launch_pdl(qh::expand_tiles_kernel<QH_GGUF_Q4_K>, grid, dim3(256), 0, s, wt, nb, we); break;
+        case QH_TYPE_Q5_K: e = qh::launch_pdl(qh::expand_tiles_kernel<QH_GGUF_Q5_K>, grid, dim3(256), 0, s, wt, nb, we); break;
+        default: e = qh::launch_pdl(qh::expand_tiles_kernel<QH_GGUF_Q6_K>, grid, dim3(256), 0, s, wt, nb, we); break;
+    }
+    if (e != cudaSuccess) return gcuda(e, "gemm_expand_weights launch");
     return QH_OK;
 }
 
@@ -768,7 +846,10 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
     p.kchunks = 1;
     p.kc_blocks = p.nb;
     const int64_t need = qh_gemm_scratch_bytes(jobs, n_jobs, k, n_tok);
-    if (d_scratch && scratch_bytes >= need && out_tiles < sms / 2 && out_tiles <= kMaxSplitTiles && p.nb > 1) {
+    // Expanded weights stream at the memory rate, so a split (whose last CTA
+    // re-reads every block's terms) pays only for very few tiles.
+    const int64_t split_below = (flags & QH_GEMM_EXPANDED) ? sms / 4 : sms / 2;
+    if (d_scratch && scratch_bytes >= need && out_tiles < split_below && out_tiles <= kMaxSplitTiles && p.nb > 1) {
         const int64_t want = std::min<int64_t>(p.nb, (sms + out_tiles - 1) / out_tiles);
         p.kc_blocks = static_cast<int32_t>((p.nb + want - 1) / want);
         p.kchunks = static_cast<int32_t>((p.nb + p.kc_blocks - 1) / p.kc_blocks);
@@ -778,10 +859,14 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
     if (out_tiles * p.kchunks > 0x7fffffffll) return gfail(QH_ERR_INVALID, "gemm: too many tiles");
     p.total_items = static_cast<int32_t>(out_tiles * p.kchunks);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool xp = (flags & QH_GEMM_EXPANDED) != 0;
     switch (type) {
-        case QH_TYPE_Q4_K: e = qh::gemm_launch_t<QH_GGUF_Q4_K>(p, sms, s); break;
-        case QH_TYPE_Q5_K: e = qh::gemm_launch_t<QH_GGUF_Q5_K>(p, sms, s); break;
-        default: e = qh::gemm_launch_t<QH_GGUF_Q6_K>(p, sms, s); break;
+        case QH_TYPE_Q4_K: e = xp ? qh::gemm_launch_t<QH_GGUF_Q4_K, true>(p, sms, s)
+                                  : qh::gemm_launch_t<QH_GGUF_Q4_K, false>(p, sms, s); break;
+        case QH_TYPE_Q5_K: e = xp ? qh::gemm_launch_t<QH_GGUF_Q5_K, true>(p, sms, s)
+                                  : qh::gemm_launch_t<QH_GGUF_Q5_K, false>(p, sms, s); break;
+        default: e = xp ? qh::gemm_launch_t<QH_GGUF_Q6_K, true>(p, sms, s)
+                        : qh::gemm_launch_t<QH_GGUF_Q6_K, false>(p, sms, s); break;
     }
     if (e != cudaSuccess) return gcuda(e, "gemm launch");
     return QH_OK;

@@ -32,6 +32,8 @@
 
 #include "qh_common.cuh"
 #include "qh_internal.h"
+#include "qh_q8k.cuh"
+#include "qh_tc.cuh"
 
 namespace qh {
 
@@ -41,6 +43,10 @@ constexpr int kGemvThreads = 32 * (kConsumerWarps + 1);
 // Two CTAs fit on one SM (228 KiB per SM, 1 KiB reserved per CTA).
 constexpr int kSmemHeader = 2048;
 constexpr int kSmemDataBudget = 110 * 1024;  // per CTA at 2 CTAs/SM
+// Per-block terms of split tiles (two buffers), after the stage ring and
+// inside the data budget.
+constexpr int kTermsBytes = 4096;
+constexpr int kTermsFloats = kTermsBytes / 8;  // per buffer
 
 // Per-stage metadata written by the producer: the tile's job descriptor
 // (so consumers never touch the global job table) and its row range.
@@ -124,6 +130,31 @@ __device__ __forceinline__ KScales unpack_kscales(const uint4 &h, uint32_t sh) {
     return s;
 }
 
+// Where a group's per-block fp32 terms go. Whole rows: added in block order
+// into registers (the reference's sequential row sum). Split tiles (the
+// blocks of a row spread over several warps): stored to shared memory
+// terms[t][row][block] (by the lane of quarter 0, which holds the 4-lane
+// total), summed in block order once every warp is done.
+template <int NT>
+struct Sink {
+    float acc[NT];
+    float *terms;  // nullptr: accumulate
+    int nb;
+    __device__ __forceinline__ void init(float *t, int n) {
+#pragma unroll
+        for (int i = 0; i < NT; ++i) acc[i] = 0.0f;
+        terms = t;
+        nb = n;
+    }
+    __device__ __forceinline__ void put(int t, int r, int b, bool writer, float term) {
+        if (terms) {
+            if (writer) terms[(t * 8 + r) * nb + b] = term;
+        } else {
+            acc[t] = __fadd_rn(acc[t], term);
+        }
+    }
+};
+
 // Shared tail of Q4_K/Q5_K: integer dots with the four activation slices,
 // scale, mins via dp2a, 4-lane reduction, fp32 combination.
 template <int NT>
@@ -131,7 +162,7 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
                                                   const uint32_t (&wc)[4], const uint32_t (&wd)[4],
                                                   const KScales &s, float dw, float dmw,
                                                   const GemvJob &job, const XView &x, int b, int j0,
-                                                  int r0, int n_tok, float (&acc)[NT]) {
+                                                  int r0, int n_tok, Sink<NT> &acc, int r, bool writer) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
         if (t < n_tok) {
@@ -161,23 +192,22 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
             const float yd = reinterpret_cast<const float *>(x.d)[t * job.d_stride + b];
             const float d = __fmul_rn(yd, dw);
             const float dmin = __fmul_rn(yd, dmw);
-            acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d, static_cast<float>(isum)),
-                                                 __fmul_rn(dmin, static_cast<float>(mins))));
+            acc.put(t, r, b, writer,
+                    __fsub_rn(__fmul_rn(d, static_cast<float>(isum)), __fmul_rn(dmin, static_cast<float>(mins))));
         }
     }
 }
 
 template <int NT>
 __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
-                                          int nvalid, int n_tok) {
+                                          int nvalid, int n_tok, int b_first, int b_step, float *terms) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, q = lane & 3, j0 = q >> 1, r0 = (q & 1) << 4;
     const uint8_t *row = grp + r * job.box_pitch;
     const uint32_t sh = 16u * static_cast<uint32_t>(j0);
-    float acc[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-    for (int b = 0; b < job.nb; ++b) {
+    Sink<NT> acc;
+    acc.init(terms, job.nb);
+    for (int b = b_first; b < job.nb; b += b_step) {
         const uint8_t *blk = row + b * QH_Q4K_BYTES;
         const uint4 h = lds128(blk);
         const uint4 qa = lds128(blk + 16 + 16 * q);  // qs[32*j0 + r0 .. +16]
@@ -189,18 +219,18 @@ __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job
         const uint32_t wc[4] = {qc.x & m4, qc.y & m4, qc.z & m4, qc.w & m4};
         const uint32_t wd[4] = {(qc.x >> 4) & m4, (qc.y >> 4) & m4, (qc.z >> 4) & m4, (qc.w >> 4) & m4};
         kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, x, b, j0,
-                              r0, n_tok, acc);
+                              r0, n_tok, acc, r, q == 0);
     }
-    if (q == 0 && r < nvalid) {
+    if (!terms && q == 0 && r < nvalid) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
-            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc[t];
+            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc.acc[t];
     }
 }
 
 template <int NT>
 __device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
-                                          int nvalid, int n_tok) {
+                                          int nvalid, int n_tok, int b_first, int b_step, float *terms) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, q = lane & 3, j0 = q >> 1, r0 = (q & 1) << 4;
     const uint8_t *row = grp + r * job.box_pitch;
@@ -208,10 +238,9 @@ __device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job
     // 5th bit of sub-block s sits in bit s of qh[l]; move it to bit 4.
     const uint32_t up_a = 4u - 2u * j0, up_b = 3u - 2u * j0;  // s = 2j0, 2j0+1
     const uint32_t dn_c = 2u * j0, dn_d = 2u * j0 + 1u;       // s = 2j0+4, 2j0+5
-    float acc[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-    for (int b = 0; b < job.nb; ++b) {
+    Sink<NT> acc;
+    acc.init(terms, job.nb);
+    for (int b = b_first; b < job.nb; b += b_step) {
         const uint8_t *blk = row + b * QH_Q5K_BYTES;
         const uint4 h = lds128(blk);
         const uint4 hv = lds128(blk + 16 + r0);       // qh[r0 .. r0+16)
@@ -231,26 +260,25 @@ __device__ __forceinline__ void group_q5k(const uint8_t *grp, const GemvJob &job
             wd[i] = ((lc[i] >> 4) & m4) | ((qh[i] >> dn_d) & b4);
         }
         kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, x, b, j0,
-                              r0, n_tok, acc);
+                              r0, n_tok, acc, r, q == 0);
     }
-    if (q == 0 && r < nvalid) {
+    if (!terms && q == 0 && r < nvalid) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
-            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc[t];
+            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc.acc[t];
     }
 }
 
 template <int NT>
 __device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
-                                          int nvalid, int n_tok) {
+                                          int nvalid, int n_tok, int b_first, int b_step, float *terms) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, q = lane & 3, n = q >> 1, l0 = (q & 1) << 4;
     const uint8_t *row = grp + r * job.box_pitch;
     const uint32_t bs_shift = 16u * static_cast<uint32_t>(q & 1);
-    float acc[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-    for (int b = 0; b < job.nb; ++b) {
+    Sink<NT> acc;
+    acc.init(terms, job.nb);
+    for (int b = b_first; b < job.nb; b += b_step) {
         const uint8_t *blk = row + b * QH_Q6K_BYTES;
         const uint4 qa = lds128_a2(blk + 64 * n + l0);        // ql, quarters 0 (low) / 2 (high)
         const uint4 qb = lds128_a2(blk + 64 * n + 32 + l0);   // ql, quarters 1 (low) / 3 (high)
@@ -289,14 +317,14 @@ __device__ __forceinline__ void group_q6k(const uint8_t *grp, const GemvJob &job
                 tot += __shfl_xor_sync(0xffffffffu, tot, 1);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 2);
                 const float yd = reinterpret_cast<const float *>(x.d)[t * job.d_stride + b];
-                acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, yd), static_cast<float>(tot)));
+                acc.put(t, r, b, q == 0, __fmul_rn(__fmul_rn(dw, yd), static_cast<float>(tot)));
             }
         }
     }
-    if (q == 0 && r < nvalid) {
+    if (!terms && q == 0 && r < nvalid) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
-            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc[t];
+            if (t < n_tok) job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc.acc[t];
     }
 }
 
@@ -344,14 +372,16 @@ __device__ __forceinline__ void group_q8_0(const uint8_t *grp, const GemvJob &jo
     }
 }
 
+// One 8-row group: blocks b_first, b_first + b_step, ... of its rows; with
+// terms == nullptr whole rows (b_first 0, b_step 1) summed and stored.
 template <int TYPE, int NT>
 __device__ __forceinline__ void process_group(const uint8_t *wbase, int tile_rows, int trow,
                                               const GemvJob &job, const XView &x, int row0, int nvalid,
-                                              int n_tok) {
+                                              int n_tok, int b_first = 0, int b_step = 1, float *terms = nullptr) {
     const uint8_t *grp = wbase + trow * job.box_pitch;
-    if constexpr (TYPE == QH_GGUF_Q4_K) group_q4k<NT>(grp, job, x, row0, nvalid, n_tok);
-    else if constexpr (TYPE == QH_GGUF_Q5_K) group_q5k<NT>(grp, job, x, row0, nvalid, n_tok);
-    else if constexpr (TYPE == QH_GGUF_Q6_K) group_q6k<NT>(grp, job, x, row0, nvalid, n_tok);
+    if constexpr (TYPE == QH_GGUF_Q4_K) group_q4k<NT>(grp, job, x, row0, nvalid, n_tok, b_first, b_step, terms);
+    else if constexpr (TYPE == QH_GGUF_Q5_K) group_q5k<NT>(grp, job, x, row0, nvalid, n_tok, b_first, b_step, terms);
+    else if constexpr (TYPE == QH_GGUF_Q6_K) group_q6k<NT>(grp, job, x, row0, nvalid, n_tok, b_first, b_step, terms);
     else group_q8_0<NT>(grp, job, x, row0, nvalid, n_tok);
 }
 
@@ -364,6 +394,116 @@ __host__ __device__ __forceinline__ void x_plane_bytes(int type, const GemvJob &
     *qs = static_cast<uint32_t>(n_tok) * static_cast<uint32_t>(job.k);
     *bs = type == QH_GGUF_Q8_0 ? 0u : static_cast<uint32_t>(n_tok * job.nb * 32);
     *d = static_cast<uint32_t>(n_tok * job.d_stride * (type == QH_GGUF_Q8_0 ? 2 : 4));
+}
+
+// ---------------------------------------------------------------------------
+// Fused input: the 256 consumer threads form the jobs' shared Q8_K
+// activation in the CTA's fixed planes ([qs][bsums][d], as staged ones),
+// with the operations and order of resnorm_q8k_kernel (double sum of
+// squares: thread t over elements t, t+256, ..., then the warp tree and the
+// warps in order), swiglu_q8k_kernel or quantize_q8k_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kFuseMaxBlocks = 16;  // residual + RMSNorm rows up to 4096
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ double consumers_sum_d(double v, double *scratch) {
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    consumers_sync();
+    if (lane == 0) scratch[warp] = v;
+    consumers_sync();
+    double t = 0.0;
+    for (int w = 0; w < kConsumerWarps; ++w) t += scratch[w];
+    return t;
+}
+
+// One Q8_K block quantized by one warp (quantize_row_q8_K, slm/tensor.c:
+// 673-720): lane l holds elements 8l..8l+7; the maximum magnitude with the
+// first-index tie rule, the round-half-even quants, 1 / iscale and the 16
+// sums of 16 quants -- the bytes q8k_block256 writes, without CTA barriers.
+__device__ __forceinline__ void q8k_block_warp(const float (&v)[8], int8_t *qs, int16_t *bsums, float *d) {
+    const int lane = threadIdx.x & 31;
+    float a = -1.0f, bv = 0.0f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const float ax = (v[e] == v[e]) ? fabsf(v[e]) : -1.0f;
+        if (ax > a) { a = ax; bv = v[e]; bi = 8 * lane + e; }
+    }
+    warp_best(a, bi, bv);
+    const float xmax = a > 0.0f ? bv : 0.0f;
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (xmax != 0.0f) {
+        const float iscale = __fdiv_rn(-127.0f, xmax);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = q8k_value(v[e], iscale);
+        if (lane == 0) *d = __fdiv_rn(1.0f, iscale);
+    } else if (lane == 0) {
+        *d = 0.0f;
+    }
+    uint32_t lo = 0u, hi = 0u;
+    int sum = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        lo |= (static_cast<uint32_t>(q[e]) & 0xffu) << (8 * e);
+        hi |= (static_cast<uint32_t>(q[e + 4]) & 0xffu) << (8 * e);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sum += q[e];
+    *reinterpret_cast<uint2 *>(qs + 8 * lane) = make_uint2(lo, hi);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    if ((lane & 1) == 0) bsums[lane >> 1] = static_cast<int16_t>(sum);
+}
+
+// Fused input into the CTA's planes. RMSNorm first forms the row's double
+// sum of squares over the 256 consumer threads (thread t: elements t,
+// t + 256, ...); then every consumer warp quantizes whole Q8_K blocks (warp
+// w: blocks w, w + 8, ...), re-reading its elements (cache hits).
+__device__ __noinline__ void fuse_input(const GemvParams &p, uint8_t *xs, double *dscr) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.xk, nb = K / QH_QK, nt = p.n_tok;
+    const int dstride = static_cast<int>(qhf_q8k_d_stride(K));
+    for (int t = 0; t < nt; ++t) {
+        int8_t *qs = reinterpret_cast<int8_t *>(xs) + t * K;
+        int16_t *bs = reinterpret_cast<int16_t *>(xs + nt * K) + t * nb * 16;
+        float *dd = reinterpret_cast<float *>(xs + nt * K + nt * nb * 32) + t * dstride;
+        const int64_t row = static_cast<int64_t>(t) * K;
+        float rscale = 0.0f;
+        if (p.xform == 1) {
+            double s = 0.0;
+#pragma unroll
+            for (int j = 0; j < kFuseMaxBlocks; ++j) {
+                if (j < nb) {
+                    const int64_t i = row + j * QH_QK + tid;
+                    float x = p.xa[i];
+                    if (p.xb) x = __fadd_rn(x, p.xb[i]);
+                    if (p.xh_out && blockIdx.x == 0) p.xh_out[i] = x;
+                    s += static_cast<double>(__fmul_rn(x, x));
+                }
+            }
+            const double ssq = consumers_sum_d(s, dscr);
+            rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(K)), p.eps)));
+        }
+        for (int b = warp; b < nb; b += kConsumerWarps) {
+            const int64_t e0 = row + b * QH_QK + 8 * lane;
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int64_t i = e0 + e;
+                if (p.xform == 1) {
+                    float x = p.xa[i];
+                    if (p.xb) x = __fadd_rn(x, p.xb[i]);
+                    v[e] = __fmul_rn(__fmul_rn(x, rscale), p.xw[b * QH_QK + 8 * lane + e]);
+                } else if (p.xform == 2) {
+                    v[e] = __fmul_rn(silu_f(p.xa[i]), p.xb[i]);
+                } else {
+                    v[e] = p.xa[i];
+                }
+            }
+            q8k_block_warp(v, qs + b * QH_QK, bs + b * 16, dd + b);
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -406,7 +546,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         // activation quantizer) finishes; the activation planes follow the wait.
         const int n_pre = min(n_my, S);
         auto issue_x = [&](int s) {
-            if (lane == 0) {
+            if (lane == 0 && !p.xform) {
                 const GemvJob &jb = meta[s].job;
                 uint32_t xq_b, xb_b, xd_b;
                 x_plane_bytes(TYPE, jb, p.n_tok, &xq_b, &xb_b, &xd_b);
@@ -420,7 +560,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         int j = n_my > 0 ? find_job(p, t_begin) : 0;
         GemvJob job = load_job(p, j);
         for (int i = 0; i < n_my; ++i) {
-            if (i == n_pre) {
+            if (i == n_pre && !p.xform) {
                 pdl_wait();
                 for (int t = 0; t < n_pre; ++t) issue_x(t);
             }
@@ -443,8 +583,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             const int nrows = min(p.rows_per_tile, job.n_rows - row0);
             const uint8_t *g0 = job.w + static_cast<int64_t>(row0) * job.row_bytes;
             uint8_t *dst = data + static_cast<int64_t>(s) * p.stage_bytes;
-            uint32_t xq_b, xb_b, xd_b;
-            x_plane_bytes(TYPE, job, p.n_tok, &xq_b, &xb_b, &xd_b);
+            uint32_t xq_b = 0, xb_b = 0, xd_b = 0;
+            if (!p.xform) x_plane_bytes(TYPE, job, p.n_tok, &xq_b, &xb_b, &xd_b);
             const uint8_t *g1 = g0 + static_cast<int64_t>(nrows) * job.row_bytes;
             const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g0) & ~uintptr_t(15));
             const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(g1) & ~uintptr_t(15));
@@ -467,7 +607,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             if (i >= n_pre) issue_x(s);
             ++issued;
         }
-        if (issued == n_pre && n_pre > 0) {  // the loop ended inside the first ring
+        if (issued == n_pre && n_pre > 0 && !p.xform) {  // the loop ended inside the first ring
             pdl_wait();
             for (int t = 0; t < n_pre; ++t) issue_x(t);
         }
@@ -479,6 +619,66 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
 
     // ----- consumers -----
+    // The activation planes: per stage, or (fused input) formed here once.
+    uint8_t *xfix = data + p.x_fixed;
+    if (p.xform) {
+        __shared__ double fscr[kConsumerWarps];
+        pdl_wait();
+        fuse_input(p, xfix, fscr);
+        consumers_sync();
+    }
+    auto xview = [&](const uint8_t *stage, const GemvJob &job) {
+        const uint8_t *xb = p.xform ? xfix : stage + p.x_offset;
+        XView x;
+        x.qs = reinterpret_cast<const int8_t *>(xb);
+        x.bs = reinterpret_cast<const int16_t *>(xb + p.n_tok * job.k);
+        x.d = xb + p.n_tok * job.k + (TYPE == QH_GGUF_Q8_0 ? 0 : p.n_tok * job.nb * 32);
+        return x;
+    };
+    if (p.split) {
+        // One 8-row group per tile (the planner's condition), its blocks
+        // spread over the 8 warps: warp w takes blocks w, w + 8, ...; the
+        // terms meet in shared memory and warp 0 adds them in block order.
+        // Every wait outcome is agreed on by all consumer warps first, so
+        // the named barriers never wait for a warp that has left.
+        float *terms = reinterpret_cast<float *>(data + p.terms_off);
+        for (int i = 0; i < n_my; ++i) {
+            const int s = i % S;
+            const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+            const bool ok = !*abort_flag && mbar_wait(&full[s], ph);
+            if (bar_any(1, 32 * kConsumerWarps, !ok)) {
+                if (!ok) {
+                    report_error(p.err_flag, kDevWaitTimeout);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            const GemvJob job = meta[s].job;
+            const int row0 = meta[s].row0, nrows = meta[s].nrows;
+            const uint8_t *stage = data + static_cast<int64_t>(s) * p.stage_bytes;
+            const XView x = xview(stage, job);
+            float *tb = terms + (i & 1) * kTermsFloats;
+            const int nvalid = min(GR, nrows);
+            if (warp < job.nb)
+                process_group<TYPE, NT>(stage + meta[s].offset, p.rows_per_tile, 0, job, x, row0, nvalid, p.n_tok,
+                                        warp, kConsumerWarps, tb);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumerWarps) : "memory");
+            if (warp == 0 && (lane & 3) == 0 && (lane >> 2) < nvalid) {
+                const int r = lane >> 2;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t < p.n_tok) {
+                        float acc = 0.0f;
+                        for (int b = 0; b < job.nb; ++b) acc = __fadd_rn(acc, tb[(t * GR + r) * job.nb + b]);
+                        job.out[static_cast<int64_t>(t) * job.n_rows + row0 + r] = acc;
+                    }
+                }
+            }
+        }
+        return;
+    }
     int group_base = 0;
     for (int i = 0; i < n_my; ++i) {
         const int s = i % S;
@@ -495,10 +695,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         if (g < 0) g += kConsumerWarps;
         const uint8_t *stage = data + static_cast<int64_t>(s) * p.stage_bytes;
         const uint8_t *base = stage + meta[s].offset;
-        XView x;
-        x.qs = reinterpret_cast<const int8_t *>(stage + p.x_offset);
-        x.bs = reinterpret_cast<const int16_t *>(stage + p.x_offset + p.n_tok * job.k);
-        x.d = stage + p.x_offset + p.n_tok * job.k + (TYPE == QH_GGUF_Q8_0 ? 0 : p.n_tok * job.nb * 32);
+        const XView x = xview(stage, job);
         for (; g < ngroups; g += kConsumerWarps)
             process_group<TYPE, NT>(base, p.rows_per_tile, GR * g, job, x, row0 + GR * g,
                                     min(GR, nrows - GR * g), p.n_tok);
@@ -514,13 +711,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 
 cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_count,
-                      GemvParams *p, GemvGeometry *g) {
+                      GemvParams *p, GemvGeometry *g, int xform) {
     if (n_jobs <= 0 || n_tok < 1 || n_tok > 8 || qhf_block_bytes(type) == 0)
         return cudaErrorInvalidValue;
+    if (xform && type == QH_GGUF_Q8_0) return cudaErrorInvalidValue;
     const int GR = kGroupRows;
     int64_t max_pitch = 0, total_rows = 0, max_x = 0;
     for (int j = 0; j < n_jobs; ++j) {
         if (jobs[j].n_rows <= 0 || jobs[j].row_bytes <= 0) return cudaErrorInvalidValue;
+        if (xform && jobs[j].k != jobs[0].k) return cudaErrorInvalidValue;
         jobs[j].box_blocks = jobs[j].nb;
         jobs[j].box_pitch = jobs[j].row_bytes;
         max_pitch = std::max<int64_t>(max_pitch, jobs[j].row_bytes);
@@ -529,19 +728,22 @@ cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_cou
         x_plane_bytes(type, jobs[j], n_tok, &a, &b, &c);
         max_x = std::max<int64_t>(max_x, static_cast<int64_t>(a) + b + c);
     }
-    const int64_t budget = kSmemDataBudget;
-    const int max_ctas = 2 * sm_count;
     const int64_t x_bytes = (max_x + 127) / 128 * 128;
+    // With a fused input the activation planes live once per CTA, not per stage.
+    const int64_t x_stage = xform ? 0 : x_bytes, x_fixed = xform ? x_bytes : 0;
+    const int64_t budget = kSmemDataBudget - x_fixed;
+    if (budget <= 0) return cudaErrorInvalidValue;
+    const int max_ctas = 2 * sm_count;
     // Rows per tile: a multiple of the group size, at most 64, small enough
     // that the launch has ~2 tiles per CTA, and shrunk until the ring holds
     // at least 3 stages (2 at the very least).
     const int64_t r_max = 64;
     const int64_t r_bal = (total_rows / (2 * static_cast<int64_t>(max_ctas))) / GR * GR;
     int64_t R = std::max<int64_t>(GR, std::min<int64_t>(r_bal, r_max));
-    auto stage_of = [&](int64_t r) { return (r * max_pitch + 32 + 127) / 128 * 128 + x_bytes; };
+    auto stage_of = [&](int64_t r) { return (r * max_pitch + 32 + 127) / 128 * 128 + x_stage; };
     while (R > GR && budget / stage_of(R) < 3) R -= GR;
     const int64_t w_bytes = (R * max_pitch + 32 + 127) / 128 * 128;
-    const int64_t stage_bytes = w_bytes + x_bytes;
+    const int64_t stage_bytes = w_bytes + x_stage;
     const int64_t stages = std::min<int64_t>(kGemvMaxStages, budget / stage_bytes);
     if (stages < 2) return cudaErrorInvalidValue;  // a row (+ activations) too long to stage
     int64_t tiles = 0;
@@ -558,9 +760,24 @@ cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_cou
     p->stage_bytes = static_cast<int32_t>(stage_bytes);
     p->n_tok = n_tok;
     p->x_offset = static_cast<int32_t>(w_bytes);
+    p->xform = xform;
+    p->xk = xform ? jobs[0].k : 0;
     for (int j = 0; j < kGemvInlineJobs; ++j) p->jobs[j] = j < n_jobs ? jobs[j] : GemvJob{};
     g->grid = static_cast<int>(std::min<int64_t>(tiles, max_ctas));
-    g->smem_bytes = static_cast<int>(kSmemHeader + stages * stage_bytes);
+    // Split tiles: when every CTA holds at most one 8-row tile, one warp per
+    // tile would walk all blocks of its rows alone; spread them instead
+    // (needs the terms area next to at least two stages).
+    int64_t max_nb = 0;
+    for (int j = 0; j < n_jobs; ++j) max_nb = std::max<int64_t>(max_nb, jobs[j].nb);
+    const int64_t split_stages = std::min<int64_t>(stages, (budget - kTermsBytes) / stage_bytes);
+    p->split = (type != QH_GGUF_Q8_0 && R == GR && tiles <= g->grid && max_nb > 1 && split_stages >= 2 &&
+                static_cast<int64_t>(n_tok) * GR * max_nb <= kTermsFloats)
+                   ? 1
+                   : 0;
+    if (p->split) p->n_stages = static_cast<int32_t>(split_stages);
+    p->x_fixed = static_cast<int32_t>(p->n_stages * stage_bytes);
+    p->terms_off = static_cast<int32_t>(p->x_fixed + x_fixed);
+    g->smem_bytes = static_cast<int>(kSmemHeader + p->terms_off + (p->split ? kTermsBytes : 0));
     return cudaSuccess;
 }
 

@@ -45,6 +45,21 @@ struct GemvParams {
     int32_t stage_bytes;
     int32_t n_tok;
     int32_t x_offset;      // byte offset of the staged activation planes inside a stage
+    int32_t split;         // one 8-row tile per CTA: the tile's blocks spread over the consumer warps
+    int32_t terms_off;     // split: byte offset of the terms area from the stage ring base
+    // Fused input (xform != 0): every CTA forms the jobs' shared Q8_K
+    // activation itself from fp32 rows into a fixed shared-memory area at
+    // x_fixed (the same split-plane layout as a staged one) instead of
+    // copying it per stage:
+    //   1 residual + RMSNorm: a = h, b = branch output (or null), w = norm
+    //     weight, h_out = h + b (written by CTA 0 when b is given);
+    //   2 SwiGLU: a = gate, b = up;   3 plain quantization of a.
+    int32_t xform;
+    int32_t x_fixed;
+    int32_t xk;            // K of the fused input (every job's k)
+    float eps;
+    const float *xa, *xb, *xw;
+    float *xh_out;
     const GemvJob *table;  // device copy of all jobs when n_jobs > kGemvInlineJobs
     int *err_flag;         // device error word
     GemvJob jobs[kGemvInlineJobs];
@@ -61,7 +76,7 @@ struct GemvGeometry {
 // cudaErrorInvalidValue if a row is too long to stage. `sm_count` is the
 // device's multiprocessor count.
 cudaError_t gemv_plan(int type, GemvJob *jobs, int n_jobs, int n_tok, int sm_count,
-                      GemvParams *p, GemvGeometry *g);
+                      GemvParams *p, GemvGeometry *g, int xform = 0);
 
 // Launches the grouped GEMV kernel for `type`; p.n_tok in [1, 8].
 cudaError_t gemv_launch(int type, const GemvParams &p, const GemvGeometry &g,

@@ -32,16 +32,6 @@
 
 namespace qh {
 
-__device__ __forceinline__ float expf_cr(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
-__device__ __forceinline__ float logf_cr(float x) { return static_cast<float>(log(static_cast<double>(x))); }
-
-__device__ __forceinline__ float silu_f(float x) {
-    return __fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x)));
-}
-
-__device__ __forceinline__ float sigmoid_f(float x) {
-    return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-x)));
-}
 
 // Block-wide double sum (blockDim.x multiple of 32, <= 1024); all threads
 // get the result.
@@ -339,42 +329,66 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
 // are those of attn_decode_kernel (tensor_attention, slm/tensor.c:1049-1102):
 // sequential dot per position, max, exp, sequential sum, scaling, and a
 // sequential weighted sum of V rows per dimension.
+constexpr int kAttnVChunk = 32;  // V rows per bulk-copied chunk
 template <int G>
 __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__restrict__ q, const __half *__restrict__ kcache,
                                                               const __half *__restrict__ vcache,
                                                               const float *__restrict__ gate, int nh, int kvh,
                                                               const int32_t *__restrict__ pos_ptr, int max_pos,
-                                                              float *__restrict__ ctx, int rows_per_seq) {
+                                                              float *__restrict__ ctx, int rows_per_seq,
+                                                              int *__restrict__ err_flag) {
     constexpr int HD = 128;
     pdl_launch_dependents();
     pdl_wait();
-    extern __shared__ float sh[];  // [G][HD] queries, [G][max_pos] scores
+    // [G][HD] queries, [G][max_pos] scores, then two V chunks of
+    // kAttnVChunk rows (16-byte aligned: max_pos rounded up to 4)
+    extern __shared__ __align__(16) float sh[];
     float *qs = sh;
     float *sc = sh + G * HD;
+    __half *vbuf = reinterpret_cast<__half *>(sc + G * ((max_pos + 3) & ~3));
     __shared__ float red[G][32];
     __shared__ float s_inv[G];
+    __shared__ uint64_t vbar[2];
     // CTA (sequence b, KV head kh, query j): the query row b * rows_per_seq + j
     // at position *pos_ptr + j (decode: j = 0, one row per sequence)
     const int b = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t qrow = static_cast<int64_t>(b) * rows_per_seq + blockIdx.z;
     const int pos = min(max(*pos_ptr + static_cast<int>(blockIdx.z), 0), max_pos - 1);
     const int n = pos + 1;
+    const int64_t rstride = static_cast<int64_t>(kvh) * HD;
+    const __half *kb = kcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
+    const __half *vb = vcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
+    const int n_chunks = (n + kAttnVChunk - 1) / kAttnVChunk;
+    // V rows of chunk c (one bulk copy per 256-byte row) into buffer c & 1
+    auto issue_v = [&](int c) {
+        const int r0 = c * kAttnVChunk, rows = min(kAttnVChunk, n - r0);
+        uint64_t *bar = &vbar[c & 1];
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rows) * HD * 2);
+        __half *dst = vbuf + (c & 1) * kAttnVChunk * HD;
+        for (int j = 0; j < rows; ++j) bulk_copy_g2s(dst + j * HD, vb + (r0 + j) * rstride, HD * 2, bar);
+    };
+    if (t == 0) {
+        mbar_init(&vbar[0], 1);
+        mbar_init(&vbar[1], 1);
+        mbar_fence_init();
+        // the first V chunk streams in while the scores are formed
+        issue_v(0);
+    }
 #pragma unroll
     for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(qrow * nh + kh * G + g) * HD + t];
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
-    const int64_t rstride = static_cast<int64_t>(kvh) * HD;
-    const __half *kb = kcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
-    const __half *vb = vcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
     float lmax[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) lmax[g] = -INFINITY;
-    for (int i = t; i < n; i += blockDim.x) {
-        // the whole 256-byte row first (16 loads in flight), then the sums
+    // scores: thread t takes positions t, t + 128, ...; the next row's 256
+    // bytes are loaded while the current one is summed
+    auto load_row = [&](int i, uint4 (&row)[HD / 8]) {
         const uint4 *kr = reinterpret_cast<const uint4 *>(kb + i * rstride);
-        uint4 row[HD / 8];
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c) row[c] = __ldg(kr + c);
+    };
+    auto score = [&](int i, const uint4 (&row)[HD / 8]) {
         float dot[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) dot[g] = 0.0f;
@@ -399,6 +413,18 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
             sc[g * max_pos + i] = s;
             lmax[g] = fmaxf(lmax[g], s);
         }
+    };
+    {
+        uint4 ra[HD / 8], rb[HD / 8];
+        int i = t;
+        if (i < n) load_row(i, ra);
+        for (; i < n; i += 2 * blockDim.x) {
+            if (i + blockDim.x < n) load_row(i + blockDim.x, rb);
+            score(i, ra);
+            if (i + blockDim.x >= n) break;
+            if (i + 2 * blockDim.x < n) load_row(i + 2 * blockDim.x, ra);
+            score(i + blockDim.x, rb);
+        }
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -418,8 +444,17 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
         for (int g = 0; g < G; ++g) sc[g * max_pos + i] = expf_cr(__fsub_rn(sc[g * max_pos + i], m[g]));
     __syncthreads();
     if (t < G) {  // sequential sums, one head per thread
+        const float *st = sc + t * max_pos;
         float s = 0.0f;
-        for (int i = 0; i < n; ++i) s = __fadd_rn(s, sc[t * max_pos + i]);
+        int i = 0;
+        for (; i + 8 <= n; i += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = st[i + j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[j]);
+        }
+        for (; i < n; ++i) s = __fadd_rn(s, st[i]);
         s_inv[t] = __fdiv_rn(1.0f, s);
     }
     __syncthreads();
@@ -427,26 +462,39 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
 #pragma unroll
         for (int g = 0; g < G; ++g) sc[g * max_pos + i] = __fmul_rn(sc[g * max_pos + i], s_inv[g]);
     __syncthreads();
+    // weighted V sum: chunks of V rows arrive in shared memory by bulk copies
+    // (the next chunk in flight while this one is summed); per dimension the
+    // sum stays sequential in position order
     float o[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) o[g] = 0.0f;
-    // V rows in chunks of 16 positions: the 16 loads are issued together,
-    // the sums stay sequential in position order
-    constexpr int VC = 16;
-    int i0 = 0;
-    for (; i0 + VC <= n; i0 += VC) {
-        float v[VC];
+    bool ok = true;
+    int c = 0;
+    for (; c < n_chunks; ++c) {
+        if (t == 0 && c + 1 < n_chunks) issue_v(c + 1);
+        ok = mbar_wait(&vbar[c & 1], static_cast<uint32_t>(c >> 1) & 1u);
+        if (__syncthreads_or(!ok)) {
+            ok = false;
+            break;
+        }
+        const __half *vc = vbuf + (c & 1) * kAttnVChunk * HD;
+        const int r0 = c * kAttnVChunk, rows = min(kAttnVChunk, n - r0);
+        for (int j = 0; j < rows; ++j) {
+            const float v = __half2float(vc[j * HD + t]);
 #pragma unroll
-        for (int j = 0; j < VC; ++j) v[j] = __half2float(vb[(i0 + j) * rstride + t]);
-#pragma unroll
-        for (int j = 0; j < VC; ++j)
-#pragma unroll
-            for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + i0 + j], v[j]));
+            for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + r0 + j], v));
+        }
+        __syncthreads();  // buffer c & 1 is refilled by the issue of chunk c + 2
     }
-    for (int i = i0; i < n; ++i) {
-        const float v = __half2float(vb[i * rstride + t]);
-#pragma unroll
-        for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + i], v));
+    if (!ok) {
+        // a chunk that never arrived: report it, and give this CTA's copies
+        // still in flight (chunks c and c + 1) a bounded wait before exiting
+        if (t == 0) {
+            report_error(err_flag, kDevWaitTimeout);
+            for (int cc = c; cc < n_chunks && cc <= c + 1; ++cc)
+                mbar_wait(&vbar[cc & 1], static_cast<uint32_t>(cc >> 1) & 1u);
+        }
+        return;
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -618,15 +666,18 @@ int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_
                   int32_t n_seq, int32_t rows_per_seq, int32_t nh, int32_t kvh, const int32_t *d_pos,
                   int32_t max_pos, float *d_ctx, void *stream, const char *what) {
     const int G = nh / kvh;
-    const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + static_cast<size_t>(max_pos));
+    const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + ((static_cast<size_t>(max_pos) + 3) & ~size_t(3))) +
+                        2 * qh::kAttnVChunk * 128 * sizeof(__half);
     if (smem > 200 * 1024) return bad("attention: context too long");
+    int *err = qh::device_error_word();
+    if (!err) return bad("attention: no device error word");
     if (rows_per_seq > 65535) return bad(what);
     static bool gattr[64][4] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
     void (*kern)(const float *, const __half *, const __half *, const float *, int, int, const int32_t *, int, float *,
-                 int) = G == 1   ? qh::attn_decode_gqa_kernel<1>
+                 int, int *) = G == 1   ? qh::attn_decode_gqa_kernel<1>
                         : G == 2 ? qh::attn_decode_gqa_kernel<2>
                         : G == 4 ? qh::attn_decode_gqa_kernel<4>
                                  : qh::attn_decode_gqa_kernel<8>;
@@ -638,7 +689,7 @@ int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_
                                           static_cast<cudaStream_t>(stream), d_q,
                                           reinterpret_cast<const __half *>(d_kcache),
                                           reinterpret_cast<const __half *>(d_vcache), d_gate, nh, kvh, d_pos, max_pos,
-                                          d_ctx, rows_per_seq);
+                                          d_ctx, rows_per_seq, err);
     return launch_status(le, what);
 }
 }  // namespace

@@ -103,16 +103,26 @@ struct Q8KScratch {
     int i[8];
 };
 
-// Q8_K quantization of block b of row r held one value per thread by a
-// 256-thread CTA (thread t holds element t). Ends with a barrier, so the
-// scratch can be reused by the next block.
+// Barrier over the threads of a q8k_block256 call: the whole CTA, or (NAMED)
+// threads 0..255 of a larger CTA on named barrier 1.
+template <bool NAMED>
+__device__ __forceinline__ void q8k_sync() {
+    if constexpr (NAMED) asm volatile("bar.sync 1, 256;" ::: "memory");
+    else __syncthreads();
+}
+
+// Q8_K quantization of block b of row r held one value per thread by 256
+// threads (thread t holds element t): a 256-thread CTA, or with NAMED
+// threads 0..255 of a larger one. Ends with a barrier, so the scratch can be
+// reused by the next block.
+template <bool NAMED = false>
 __device__ __forceinline__ void q8k_block256(float v, Q8KScratch &sc, const Q8KRow &r, int b) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float a = (v == v) ? fabsf(v) : -1.0f, bv = v;
     int bi = tid;
     warp_best(a, bi, bv);
     if (lane == 0) { sc.a[warp] = a; sc.i[warp] = bi; sc.v[warp] = bv; }
-    __syncthreads();
+    q8k_sync<NAMED>();
     float ba = sc.a[0], xv = sc.v[0];
     int ii = sc.i[0];
 #pragma unroll
@@ -136,7 +146,7 @@ __device__ __forceinline__ void q8k_block256(float v, Q8KScratch &sc, const Q8KR
         s += __shfl_xor_sync(0xffffffffu, s, 16);  // sub-block (warp) sum
         if (lane == 0) q8k_put_min(r, b, warp, s);
     }
-    __syncthreads();
+    q8k_sync<NAMED>();
 }
 
 }  // namespace qh

@@ -52,8 +52,6 @@ constexpr int kChunk = kThreads * kPerThread;  // logits filtered per round
 constexpr int kTopK = QH_SAMPLE_TOPK_MAX;
 constexpr unsigned kFull = 0xffffffffu;
 
-__device__ __forceinline__ float expf_cr(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
-
 __device__ __forceinline__ uint64_t rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
 
 // rng_next + rng_uniform (slm/model.c:420-447)

@@ -150,17 +150,25 @@ static int upload(qh_slm *m, const qh_blob *blob, const char *name, const void *
     return QH_OK;
 }
 
-// Tiled copy of a weight matrix for the tensor-core GEMM, packed on first
-// request and shared by the decode and prompt plans.
+// Expanded copy of a weight matrix for the tensor-core GEMM (the MMA
+// operand image of every 128-row tile and super-block, qh_gemm_expand_weights),
+// made on first request through a temporary tiled copy and shared by the
+// decode and prompt plans. Each weight is used by few token tiles per
+// launch, so streaming the stored operands beats expanding them per launch.
 static int get_tiled(qh_slm *m, const void *raw, int type, int64_t k, int64_t out_f, const void **wt) {
     for (int i = 0; i < m->ntiled; ++i)
         if (m->tiled[i].raw == raw) { *wt = m->tiled[i].wt; return QH_OK; }
     if (m->ntiled >= (int)(sizeof(m->tiled) / sizeof(m->tiled[0]))) return QH_ERR_INVALID;
-    const int64_t wb = qh_gemm_weight_bytes(type, k, out_f);
-    if (wb < 0) return QH_ERR_INVALID;
-    void *d;
-    CK(dev_alloc(m, &d, (size_t)wb, NULL));
-    CK(qh_gemm_pack_weights(type, raw, k, out_f, d, m->stream));
+    const int64_t tb = qh_gemm_weight_bytes(type, k, out_f), eb = qh_gemm_expanded_bytes(type, k, out_f);
+    if (tb < 0 || eb < 0) return QH_ERR_INVALID;
+    void *tiled = NULL, *d;
+    CK(dev_alloc(m, &d, (size_t)eb, NULL));
+    CK(qh_malloc(&tiled, (size_t)tb));
+    int rc = qh_gemm_pack_weights(type, raw, k, out_f, tiled, m->stream);
+    if (!rc) rc = qh_gemm_expand_weights(type, tiled, k, out_f, d, m->stream);
+    if (!rc) rc = qh_stream_sync(m->stream);
+    qh_free(tiled);
+    if (rc) return rc;
     m->tiled[m->ntiled].raw = raw;
     m->tiled[m->ntiled].wt = d;
     m->ntiled++;
@@ -168,7 +176,7 @@ static int get_tiled(qh_slm *m, const void *raw, int type, int64_t k, int64_t ou
     return QH_OK;
 }
 
-// GEMM job set over tiled weights (outputs [rows][out_f]).
+// GEMM job set over expanded weights (outputs [rows][out_f]).
 static int make_gemm_set(qh_slm *m, plan_set *ps, int type, int nm, const void *const *w, const int64_t *out_f,
                          float *const *out, const void *xq, int64_t k) {
     if (nm > 8) return QH_ERR_INVALID;
@@ -215,7 +223,7 @@ static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *cons
 static int run_plans(qh_slm *m, plan_set *ps) {
     if (ps->gemm)
         return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, m->B, m->gemm_scratch, m->gemm_scratch_bytes,
-                       QH_GEMM_WEIGHTS_READY, m->stream);  /* packed at create, then synchronized */
+                       QH_GEMM_WEIGHTS_READY | QH_GEMM_EXPANDED, m->stream);  /* made at create, then synchronized */
     for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
     return QH_OK;
 }
@@ -603,22 +611,27 @@ static int forward(qh_slm *m) {
     // h + mix into the other one (the fused kernel reads h from many CTAs).
     float *hc = m->h, *hx = m->h2;
     const float *pending = NULL;  // residual branch output not yet added to hc
-#define RESNORM(w, xq, ADD_NAME, ADD_L, NORM_NAME, NORM_L)                                            \
-    do {                                                                                               \
-        const int added_ = pending != NULL;                                                            \
-        CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, B, c->norm_eps, (xq), m->xq_tile, s)); \
-        if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                           \
-        pending = NULL;                                                                                \
-        if (m->trace_fp) {                                                                             \
-            if (added_) TR("ADD", hc, H, ADD_NAME, ADD_L);                                             \
-            CK(qh_rmsnorm(hc, (w), H, B, c->norm_eps, m->hn, s));                                      \
-            TR("RMS_NORM", m->hn, H, NORM_NAME, NORM_L);                                               \
-        }                                                                                              \
+    // Residual add + RMSNorm + Q8_K (one fused kernel), then the plan that
+    // reads the quantized row. (The GEMV plans can also form this input
+    // themselves, qh_matvec_plan_fuse_input; in the captured step that is
+    // slower, because two GEMV launches in a row cannot share SMs the way a
+    // small norm kernel and a GEMV do under programmatic launch.)
+#define NORMED(ps, w, ADD_NAME, ADD_L, NORM_NAME, NORM_L)                                                  \
+    do {                                                                                                   \
+        const int added_ = pending != NULL;                                                                \
+        CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, B, c->norm_eps, m->xq_h, m->xq_tile, s)); \
+        CK(run_plans(m, (ps)));                                                                            \
+        if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                               \
+        pending = NULL;                                                                                    \
+        if (m->trace_fp) {                                                                                 \
+            if (added_) TR("ADD", hc, H, ADD_NAME, ADD_L);                                                 \
+            CK(qh_rmsnorm(hc, (w), H, B, c->norm_eps, m->hn, s));                                          \
+            TR("RMS_NORM", m->hn, H, NORM_NAME, NORM_L);                                                   \
+        }                                                                                                  \
     } while (0)
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        RESNORM(Ly->attn_norm, m->xq_h, "l_out-%d", l - 1, "attn_norm-%d", l);
-        CK(run_plans(m, &Ly->p_in));
+        NORMED(&Ly->p_in, Ly->attn_norm, "l_out-%d", l - 1, "attn_norm-%d", l);
         if (Ly->is_attn) {
             TR("MUL_MAT", m->qraw, 2 * qdim, "Qfull-%d", l);
             TR("MUL_MAT", m->kb, kvd, "Kcur-%d", l);
@@ -673,16 +686,14 @@ static int forward(qh_slm *m) {
             TR("MUL_MAT", m->mix, H, "ssm_out-%d", l);
         TR(Ly->is_attn ? "ATTN" : "SSM", m->mix, H, "mix-%d", l);
         pending = m->mix;
-        RESNORM(Ly->ffn_norm, m->xq_h, "mix_residual-%d", l, "ffn_norm-%d", l);
-        CK(run_plans(m, &Ly->p_ffn));
+        NORMED(&Ly->p_ffn, Ly->ffn_norm, "mix_residual-%d", l, "ffn_norm-%d", l);
         CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, m->xq_tile, s));
         CK(run_plans(m, &Ly->p_down));
         TR("MUL_MAT", m->mix, H, "ffn_out-%d", l);
         pending = m->mix;
     }
-    RESNORM(m->out_norm, m->xq_h, "l_out-%d", c->n_layers - 1, "result_norm", 0);
-#undef RESNORM
-    CK(run_plans(m, &m->p_head));
+    NORMED(&m->p_head, m->out_norm, "l_out-%d", c->n_layers - 1, "result_norm", 0);
+#undef NORMED
     TR("MUL_MAT", m->logits, c->vocab, "result_output");
 #undef TR
     if (m->sampling)
@@ -865,7 +876,8 @@ static int ensure_prefill(qh_slm *m) {
 }
 
 static int run_pf(qh_slm *m, plan_set *ps, int64_t rows) {
-    return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, rows, NULL, 0, QH_GEMM_WEIGHTS_READY, m->stream);
+    return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, rows, NULL, 0, QH_GEMM_WEIGHTS_READY | QH_GEMM_EXPANDED,
+                   m->stream);
 }
 
 // One chunk of cn tokens per sequence at positions *pf_pos .. + cn - 1;

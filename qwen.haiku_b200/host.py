@@ -145,6 +145,15 @@ def gemm_pack(gtype: int, w, k: int, out_f: int):
     return wt
 
 
+def gemm_expand(gtype: int, wt, k: int, out_f: int):
+    """qh_gemm_expand_weights of tiled weights into a fresh device buffer
+    (use with qh_gemm flags QH_GEMM_EXPANDED)."""
+    torch = _torch()
+    we = torch.empty(int(lib().qh_gemm_expanded_bytes(gtype, k, out_f)), dtype=torch.uint8, device="cuda")
+    check(lib().qh_gemm_expand_weights(gtype, dptr(wt), k, out_f, dptr(we), None), "qh_gemm_expand_weights")
+    return we
+
+
 def quantize_q8kt(x, k: int, n_tok: int):
     torch = _torch()
     buf = torch.empty(int(lib().qh_q8kt_bytes(k, n_tok)), dtype=torch.uint8, device="cuda")
@@ -206,6 +215,14 @@ class MatvecPlan:
     def run(self, stream=None):
         check(lib().qh_matvec_plan_run(self.handle, stream if stream is not None else stream_handle()),
               "qh_matvec_plan_run")
+
+    def fuse_input(self, mode: int, a=None, b=None, w=None, eps: float = 0.0, h_out=None):
+        """qh_matvec_plan_fuse_input (QH_FUSE_RMSNORM 1, SWIGLU 2, QUANT 3; 0 = off)."""
+        self._fused = (a, b, w, h_out)
+        check(lib().qh_matvec_plan_fuse_input(self.handle, mode, *(dptr(t) if t is not None else None
+                                                                  for t in (a, b, w)),
+                                              eps, dptr(h_out) if h_out is not None else None),
+              "qh_matvec_plan_fuse_input")
 
     def info(self):
         r, s, g, m = C.c_int(), C.c_int(), C.c_int(), C.c_int()

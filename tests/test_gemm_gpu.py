@@ -108,6 +108,52 @@ def test_split_k_equals_unsplit(qh, cuda, oracle, gt, k, out_f, n_tok):
     assert_bitwise(outs[0], oracle.matmul(gt, w, out_f, k, x_np).reshape(n_tok, out_f), "oracle")
 
 
+QH_GEMM_EXPANDED = 2
+
+
+@pytest.mark.parametrize("gt", [Q4_K, Q5_K, Q6_K])
+@pytest.mark.parametrize("k,out_f,n_tok", [(256, 128, 64), (1024, 300, 70), (2048, 257, 1), (3584, 1024, 64)])
+@pytest.mark.parametrize("split", [False, True])
+def test_expanded_weights_bitexact(qh, cuda, oracle, gt, k, out_f, n_tok, split):
+    """qh_gemm on expanded weights (QH_GEMM_EXPANDED: the MMA operands
+    streamed as stored, no expansion in the kernel) equals the oracle bit
+    for bit, with and without split-K, and the tiled path."""
+    w = qh.host.synth_blocks(gt, out_f * (k // 256), 0xE0 + gt + k + out_f)
+    x_np = qh.host.synth_normal(n_tok * k, 0xE1 + k + n_tok).reshape(n_tok, k)
+    wt = qh.host.gemm_pack(gt, qh.host.to_device(w), k, out_f)
+    we = qh.host.gemm_expand(gt, wt, k, out_f)
+    assert we.numel() == qh.lib().qh_gemm_expanded_bytes(gt, k, out_f)
+    xq = qh.host.quantize_q8kt(qh.host.to_device(x_np), k, n_tok)
+    a = cuda.empty((n_tok, out_f), dtype=cuda.float32, device="cuda")
+    b = cuda.empty((n_tok, out_f), dtype=cuda.float32, device="cuda")
+    qh.host.gemm(gt, [(wt, out_f, a, out_f)], k, xq, n_tok, split=split)
+    qh.host.gemm(gt, [(we, out_f, b, out_f)], k, xq, n_tok, split=split, flags=QH_GEMM_EXPANDED)
+    cuda.cuda.synchronize()
+    want = oracle.matmul(gt, w, out_f, k, x_np).reshape(n_tok, out_f)
+    assert_bitwise(b.cpu().numpy(), want, f"expanded type {gt} k={k} out_f={out_f} n={n_tok}")
+    assert_bitwise(b.cpu().numpy(), a.cpu().numpy(), "expanded vs tiled")
+
+
+def test_expanded_grouped_jobs(qh, cuda, oracle):
+    """Three expanded Q4_K matrices in one launch, 130 tokens (3 token tiles)."""
+    k, n_tok = 1024, 130
+    x_np = qh.host.synth_normal(n_tok * k, 0xE7).reshape(n_tok, k)
+    xq = qh.host.quantize_q8kt(qh.host.to_device(x_np), k, n_tok)
+    jobs, ws, outs = [], [], []
+    for i, out_f in enumerate((2048, 256, 16)):
+        w = qh.host.synth_blocks(Q4_K, out_f * 4, 0xE8 + i)
+        we = qh.host.gemm_expand(Q4_K, qh.host.gemm_pack(Q4_K, qh.host.to_device(w), k, out_f), k, out_f)
+        out = cuda.empty((n_tok, out_f), dtype=cuda.float32, device="cuda")
+        ws.append(w)
+        outs.append((we, out))
+        jobs.append((we, out_f, out, out_f))
+    qh.host.gemm(Q4_K, jobs, k, xq, n_tok, flags=QH_GEMM_EXPANDED)
+    cuda.cuda.synchronize()
+    for (out_f, w, (_, out)) in zip((2048, 256, 16), ws, outs):
+        assert_bitwise(out.cpu().numpy(), oracle.matmul(Q4_K, w, out_f, k, x_np).reshape(n_tok, out_f),
+                       f"job {out_f}")
+
+
 @pytest.mark.parametrize("cfg", ["3a", "3b"])
 def test_prefill_configs(qh, cuda, oracle, cfg):
     """Benchmark config 3: M=512 K=1024 N=3584 Q4_K and M=2048 K=3584 N=1024

@@ -196,3 +196,57 @@ def test_misaligned_weight_rejected(qh, cuda):
 
 def test_no_device_error_reported(qh, cuda):
     assert qh.lib().qh_check_device_error(None) == 0
+
+
+@pytest.mark.parametrize("gt,k", [(Q4_K, 1024), (Q5_K, 2048), (Q6_K, 3584), (Q4_K, 4096)])
+@pytest.mark.parametrize("n_tok", [1, 3, 8])
+def test_fused_input_equals_separate_kernels(qh, cuda, gt, k, n_tok):
+    """qh_matvec_plan_fuse_input: the plan forming its own Q8_K input (residual
+    + RMSNorm, SwiGLU, plain quantization) gives the same outputs, bit for bit,
+    as the separate kernel followed by the plan; RMSNorm also writes h + b.
+    Small and large launches (the split-tile path and the pipelined one)."""
+    import ctypes as C
+    torch = cuda
+    h = qh.host
+    L = qh.lib()
+    outs = (40, 3000)  # 40 rows: one tile per CTA (split); 3000: several tiles per CTA
+    a = h.to_device(h.synth_normal(n_tok * k, 0xF1 + k).reshape(n_tok, k))
+    b = h.to_device(h.synth_normal(n_tok * k, 0xF2 + k, 0.0, 0.5).reshape(n_tok, k))
+    w = h.to_device(h.synth_normal(k, 0xF3, 1.0, 0.02))
+    ws = [h.to_device(h.synth_blocks(gt, n * (k // 256), 0xF4 + n)) for n in outs]
+    xq = torch.empty(int(L.qh_q8k_bytes(k, n_tok)), dtype=torch.uint8, device="cuda")
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for mode in (1, 2, 3, 4):  # 4: RMSNorm without a residual
+        ref = [torch.empty((n_tok, n), dtype=torch.float32, device="cuda") for n in outs]
+        got = [torch.empty((n_tok, n), dtype=torch.float32, device="cuda") for n in outs]
+        h_ref = torch.empty_like(a)
+        h_got = torch.full_like(a, 7.0)
+        if mode == 1:
+            qh.check(L.qh_rmsnorm_q8k(h.dptr(a), h.dptr(b), h.dptr(h_ref), h.dptr(w), k, n_tok, 1e-6, h.dptr(xq), 0, s),
+                     "rmsnorm_q8k")
+        elif mode == 2:
+            qh.check(L.qh_swiglu_q8k(h.dptr(a), h.dptr(b), k, n_tok, h.dptr(xq), 0, s), "swiglu_q8k")
+        elif mode == 3:
+            qh.check(L.qh_quantize_q8k(h.dptr(a), k, n_tok, h.dptr(xq), s), "quantize_q8k")
+        else:
+            qh.check(L.qh_rmsnorm_q8k(h.dptr(a), None, None, h.dptr(w), k, n_tok, 1e-6, h.dptr(xq), 0, s),
+                     "rmsnorm_q8k")
+        plan_ref = h.MatvecPlan(gt, [(ws[i], xq, ref[i], k, n) for i, n in enumerate(outs)], n_tok)
+        plan_ref.run()
+        plan = h.MatvecPlan(gt, [(ws[i], xq, got[i], k, n) for i, n in enumerate(outs)], n_tok)
+        if mode == 1:
+            plan.fuse_input(1, a, b, w, 1e-6, h_got)
+        elif mode == 2:
+            plan.fuse_input(2, a, b)
+        elif mode == 3:
+            plan.fuse_input(3, a)
+        else:
+            plan.fuse_input(1, a, None, w, 1e-6, None)
+        plan.run()
+        torch.cuda.synchronize()
+        for i in range(len(outs)):
+            assert torch.equal(got[i].view(torch.int32), ref[i].view(torch.int32)), f"mode {mode} job {i}"
+        if mode == 1:
+            assert torch.equal(h_got.view(torch.int32), h_ref.view(torch.int32)), "residual h + b"
+        plan.close()
+        plan_ref.close()
