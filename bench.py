@@ -10,10 +10,13 @@ the G activation rows to Q8_K (one launch) + the G matvecs (one grouped
 persistent launch). GB/s counts algorithmic bytes per matvec: weights
 1,769,472 + Q8_K activation 1,168 + fp32 output 12,288 = 1,782,928.
 
-  value  -- device-resident inputs, CUDA-event time of K steps (max over ranks)
+  value  -- device-resident inputs, CUDA-event time of K steps (max over ranks);
+            activations and outputs are double-buffered, so step i + 1's
+            quantization (its own stream) overlaps step i's matvec launch
   e2e    -- the same work through the C-ABI with HOST buffers: per step the
             activations are copied from pinned host memory and the outputs
-            read back, inside the timed region
+            read back, inside the timed region (copies on their own streams,
+            overlapping the neighbouring steps' compute)
   roofline -- the grouped matvec kernel alone: algorithmic bytes / its mean
             launch time (events around each launch on its stream) vs the
             measured HBM copy bandwidth in MEASURED_PEAKS.json
@@ -282,19 +285,26 @@ def run_gemm(qh, torch, steps: int, warmup: int):
         x_host = torch.from_numpy(h.synth_normal(m * k, 0x3B00 + m).reshape(m, k)).pin_memory()
         x = x_host.to("cuda")
         wt = h.gemm_pack(gt, w, k, n)
+        we = h.gemm_expand(gt, wt, k, n)
         xq = h.quantize_q8kt(x, k, m)
         o = torch.empty((m, n), dtype=torch.float32, device="cuda")
         torch.cuda.synchronize()  # packed weights complete: they may stream in early (QH_GEMM_WEIGHTS_READY)
-        for _ in range(warmup):
-            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False, flags=1)
-        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            h.gemm(gt, [(wt, n, o, n)], k, xq, m, split=False, flags=1)
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
+        # tiled weights (expanded per launch on the CUDA cores) and expanded
+        # weights (the MMA operands stored once, QH_GEMM_EXPANDED)
+        mode_ms = {}
+        for mode, wbuf, flags in (("tiled", wt, 1), ("expanded", we, 3)):
+            for _ in range(warmup):
+                h.gemm(gt, [(wbuf, n, o, n)], k, xq, m, split=False, flags=flags)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(steps):
+                h.gemm(gt, [(wbuf, n, o, n)], k, xq, m, split=False, flags=flags)
+            e1.record()
+            torch.cuda.synchronize()
+            mode_ms[mode] = e0.elapsed_time(e1) / steps
+        best_mode = min(mode_ms, key=mode_ms.get)
+        ms = mode_ms[best_mode]
         # end to end: host activations in, outputs out, GGUF weights packed per call
         need = int(L.qh_matmul_gemm_workspace_bytes(gt, k, n, m))
         work = torch.empty(need, dtype=torch.uint8, device="cuda")
@@ -318,13 +328,15 @@ def run_gemm(qh, torch, steps: int, warmup: int):
         ops = 2.0 * m * n * k
         tops = ops / (ms / 1e3) / 1e12
         out[name] = {"workload": f"M={m} K={k} N={n} {'Q4_K' if gt == 12 else 'Q6_K'} x Q8_K -> fp32",
-                     "ms": round(ms, 4), "tops": round(tops, 2), "tokens_per_s": round(m / (ms / 1e3), 1),
+                     "ms": round(ms, 4), "weights": best_mode,
+                     "ms_by_weights": {kk: round(v, 4) for kk, v in mode_ms.items()},
+                     "tops": round(tops, 2), "tokens_per_s": round(m / (ms / 1e3), 1),
                      "weight_gbs": round(w.numel() / (ms / 1e3) / 1e9, 1),
                      "e2e": {"ms": round(ms_e2e, 4), "tokens_per_s": round(m / (ms_e2e / 1e3), 1),
                              "h2d_bytes": m * k * 4, "d2h_bytes": m * n * 4},
                      "roofline": {"bound": "tensor", "achieved": round(tops, 2), "peak": peak, "unit": "TOP/s",
                                   "frac": round(tops / peak, 4), "peak_source": peak_kind + "; int8 MMA nominal is 2x bf16"}}
-        del w, x, wt, xq, o, work
+        del w, x, wt, we, xq, o, work
     torch.cuda.empty_cache()
     return out
 
@@ -466,28 +478,36 @@ def run_ours(args):
     for g in range(G):
         wdev[g].copy_(torch.from_numpy(host_w[g % n_distinct]), non_blocking=False)
     x_host = h.synth_normal(G * K_IN, 0xABC + rank).reshape(G, K_IN)
+    # Two of everything the step touches (activations fp32 and Q8_K, outputs,
+    # host staging), so step i + 1's quantization -- and in the end-to-end
+    # run its host->device copy -- overlaps step i's matvecs on other streams.
     x_pin = torch.from_numpy(x_host).pin_memory()
-    x_dev = x_pin.to("cuda")
-    xq = torch.empty(int(L.qh_q8k_bytes(K_IN, G)), dtype=torch.uint8, device="cuda")
-    out = torch.empty((G, N_OUT), dtype=torch.float32, device="cuda")
-    out_pin = torch.empty((G, N_OUT), dtype=torch.float32).pin_memory()
-    jobs = [(wdev[g], xq, out[g], K_IN, N_OUT, G, g) for g in range(G)]
-    plan = h.MatvecPlan(qh.Q4_K, jobs, 1)
+    xbytes = int(L.qh_q8k_bytes(K_IN, G))
+    x_dev = [x_pin.to("cuda") for _ in range(2)]
+    xq = [torch.empty(xbytes, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    out = [torch.empty((G, N_OUT), dtype=torch.float32, device="cuda") for _ in range(2)]
+    out_pin = [torch.empty((G, N_OUT), dtype=torch.float32).pin_memory() for _ in range(2)]
+    plans = [h.MatvecPlan(qh.Q4_K, [(wdev[g], xq[b], out[b][g], K_IN, N_OUT, G, g) for g in range(G)], 1)
+             for b in range(2)]
+    plan = plans[0]
     info = plan.info()
+    s_q = torch.cuda.Stream()      # quantization of the next step
+    s_in = torch.cuda.Stream()     # host -> device copies
+    s_out = torch.cuda.Stream()    # device -> host copies
 
-    def quantize():
-        qh.check(L.qh_quantize_q8k(C.c_void_p(x_dev.data_ptr()), K_IN, G, C.c_void_p(xq.data_ptr()), sh),
-                 "qh_quantize_q8k")
+    def quantize(b, st):
+        qh.check(L.qh_quantize_q8k(C.c_void_p(x_dev[b].data_ptr()), K_IN, G, C.c_void_p(xq[b].data_ptr()),
+                                   C.c_void_p(st.cuda_stream)), "qh_quantize_q8k")
 
     # parity spot check of the benchmarked path (not timed)
-    quantize()
+    quantize(0, stream)
     plan.run(sh)
     torch.cuda.synchronize()
     from oracle.oracle import Oracle
     orc = Oracle()
     for g in (0, G - 1):
         want = orc.matmul(qh.Q4_K, host_w[g % n_distinct], N_OUT, K_IN, x_host[g:g + 1])
-        if not np.array_equal(out[g].cpu().numpy().view(np.uint32), want.view(np.uint32).ravel()):
+        if not np.array_equal(out[0][g].cpu().numpy().view(np.uint32), want.view(np.uint32).ravel()):
             raise SystemExit(f"bench parity check failed for matrix {g}")
 
     def barrier():
@@ -499,10 +519,53 @@ def run_ours(args):
     def max_time(v: float) -> float:
         return max_over_ranks(dist, [v], "cuda")[0]
 
+    def pipelined_steps(n, e2e, kev=None):
+        """n steps: step i = (e2e: copy activations in) + quantize into buffer
+        i % 2 + the grouped matvecs (+ e2e: copy the outputs out). Quantize /
+        copy-in of step i + 1 run on side streams while step i's matvecs run;
+        events order every reuse of a buffer."""
+        q_done = [torch.cuda.Event() for _ in range(n)]
+        g_done = [torch.cuda.Event() for _ in range(n)]
+        o_done = [torch.cuda.Event() for _ in range(n)]
+
+        def prepare(i):
+            b = i % 2
+            if i >= 2:  # buffer b was last read by step i - 2's matvecs
+                s_q.wait_event(g_done[i - 2])
+            if e2e:
+                s_in.wait_stream(s_q)
+                with torch.cuda.stream(s_in):
+                    qh.check(L.qh_memcpy_h2d(C.c_void_p(x_dev[b].data_ptr()), C.c_void_p(x_pin.data_ptr()),
+                                             x_pin.numel() * 4, C.c_void_p(s_in.cuda_stream)), "h2d")
+                s_q.wait_stream(s_in)
+            quantize(b, s_q)
+            q_done[i].record(s_q)
+
+        prepare(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                prepare(i + 1)
+            stream.wait_event(q_done[i])
+            if e2e and i >= 2:  # outputs of step i - 2 copied out before they are overwritten
+                stream.wait_event(o_done[i - 2])
+            if kev is not None:
+                kev[i][0].record(stream)
+            plans[b].run(sh)
+            if kev is not None:
+                kev[i][1].record(stream)
+            g_done[i].record(stream)
+            if e2e:
+                s_out.wait_event(g_done[i])
+                qh.check(L.qh_memcpy_d2h(C.c_void_p(out_pin[b].data_ptr()), C.c_void_p(out[b].data_ptr()),
+                                         out[b].numel() * 4, C.c_void_p(s_out.cuda_stream)), "d2h")
+                o_done[i].record(s_out)
+        if e2e:
+            stream.wait_stream(s_out)
+        stream.wait_stream(s_q)
+
     # ---- device-resident timing ----
-    for _ in range(args.warmup):
-        quantize()
-        plan.run(sh)
+    pipelined_steps(args.warmup, False)
     uuid = ""
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
@@ -515,34 +578,25 @@ def run_ours(args):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     ev0.record(stream)
-    for i in range(args.steps):
-        quantize()
-        kev[i][0].record(stream)
-        plan.run(sh)
-        kev[i][1].record(stream)
+    pipelined_steps(args.steps, False, kev)
     ev1.record(stream)
     barrier()
     elapsed_ms = max_time(ev0.elapsed_time(ev1))
     kern_ms = [a.elapsed_time(b) for a, b in kev]
     # ---- end to end through the C-ABI with host buffers ----
-    for _ in range(2):
-        qh.check(L.qh_memcpy_h2d(C.c_void_p(x_dev.data_ptr()), C.c_void_p(x_pin.data_ptr()), x_pin.numel() * 4, sh), "h2d")
-        quantize()
-        plan.run(sh)
-        qh.check(L.qh_memcpy_d2h(C.c_void_p(out_pin.data_ptr()), C.c_void_p(out.data_ptr()), out.numel() * 4, sh), "d2h")
+    pipelined_steps(2, True)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        qh.check(L.qh_memcpy_h2d(C.c_void_p(x_dev.data_ptr()), C.c_void_p(x_pin.data_ptr()), x_pin.numel() * 4, sh), "h2d")
-        quantize()
-        plan.run(sh)
-        qh.check(L.qh_memcpy_d2h(C.c_void_p(out_pin.data_ptr()), C.c_void_p(out.data_ptr()), out.numel() * 4, sh), "d2h")
+    pipelined_steps(args.steps, True)
     e1.record(stream)
     barrier()
     e2e_ms = max_time(e0.elapsed_time(e1))
     clk = clocks.stop()
     qh.check(L.qh_check_device_error(None), "device error word")
+    if not np.array_equal(out_pin[(args.steps - 1) % 2][G - 1].numpy().view(np.uint32),
+                          out[0][G - 1].cpu().numpy().view(np.uint32)):
+        raise SystemExit("end-to-end outputs differ from the device-resident run")
 
     total_bytes = world * G * args.steps * ALGO_BYTES
     value = total_bytes / (elapsed_ms / 1e3) / 1e9
@@ -551,7 +605,8 @@ def run_ours(args):
     achieved = G * ALGO_BYTES / (kern_mean_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
 
-    plan.close()
+    for pl in plans:
+        pl.close()
     del wdev
     torch.cuda.empty_cache()
 
@@ -620,6 +675,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": G * K_IN * 4, "d2h_bytes_per_step": G * N_OUT * 4,
                 "ms_per_step": round(e2e_ms / args.steps, 4)},
         "gpu_launches": 2 * args.steps,
+        "pipelining": "two activation/output buffers: quantize (and e2e copy-in) of step i+1 and copy-out of step i-1 overlap step i's matvecs",
         "clocks": clk,
     }
     if cpu is not None:

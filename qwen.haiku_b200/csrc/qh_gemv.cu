@@ -91,6 +91,17 @@ __device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint
     return acc;
 }
 
+// Same with unsigned weight bytes (dp4a.u32.s32): the Q4_K high nibbles are
+// used in place (16 * w, masked, not shifted) and the sum divided by 16 after
+// -- an exact shift, the sum being a multiple of 16.
+__device__ __forceinline__ int dot16_u(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, const int4 &x, int acc) {
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w0), "r"(x.x));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w1), "r"(x.y));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w2), "r"(x.z));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w3), "r"(x.w));
+    return acc;
+}
+
 // The job's activation planes as staged in shared memory next to the
 // weight tile (same split layout as in global memory, rows [t0, t0+n_tok)).
 struct XView {
@@ -157,7 +168,8 @@ struct Sink {
 
 // Shared tail of Q4_K/Q5_K: integer dots with the four activation slices,
 // scale, mins via dp2a, 4-lane reduction, fp32 combination.
-template <int NT>
+// HI16: wb and wd hold the high-nibble sub-blocks as 16 * w (Q4_K).
+template <int NT, bool HI16 = false>
 __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const uint32_t (&wb)[4],
                                                   const uint32_t (&wc)[4], const uint32_t (&wd)[4],
                                                   const KScales &s, float dw, float dmw,
@@ -172,9 +184,15 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
             const int4 xc = lds128i(xq + 128);
             const int4 xd = lds128i(xq + 160);
             const int da = dot16(wa[0], wa[1], wa[2], wa[3], xa, 0);
-            const int db = dot16(wb[0], wb[1], wb[2], wb[3], xb, 0);
             const int dc = dot16(wc[0], wc[1], wc[2], wc[3], xc, 0);
-            const int dd = dot16(wd[0], wd[1], wd[2], wd[3], xd, 0);
+            int db, dd;
+            if constexpr (HI16) {
+                db = dot16_u(wb[0], wb[1], wb[2], wb[3], xb, 0) >> 4;
+                dd = dot16_u(wd[0], wd[1], wd[2], wd[3], xd, 0) >> 4;
+            } else {
+                db = dot16(wb[0], wb[1], wb[2], wb[3], xb, 0);
+                dd = dot16(wd[0], wd[1], wd[2], wd[3], xd, 0);
+            }
             int isum = da * s.sc_a + db * s.sc_b + dc * s.sc_c + dd * s.sc_d;
             // Lanes q and q^1 share the four sub-blocks (each holds 16 of their
             // 32 weights), so the min terms are split between them: the lane
@@ -213,13 +231,13 @@ __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job
         const uint4 qa = lds128(blk + 16 + 16 * q);  // qs[32*j0 + r0 .. +16]
         const uint4 qc = lds128(blk + 80 + 16 * q);  // qs[32*(j0+2) + r0 .. +16]
         const KScales s = unpack_kscales(h, sh);
-        const uint32_t m4 = 0x0f0f0f0fu;
+        const uint32_t m4 = 0x0f0f0f0fu, h4 = 0xf0f0f0f0u;
         const uint32_t wa[4] = {qa.x & m4, qa.y & m4, qa.z & m4, qa.w & m4};
-        const uint32_t wb[4] = {(qa.x >> 4) & m4, (qa.y >> 4) & m4, (qa.z >> 4) & m4, (qa.w >> 4) & m4};
+        const uint32_t wb[4] = {qa.x & h4, qa.y & h4, qa.z & h4, qa.w & h4};  // 16 * w
         const uint32_t wc[4] = {qc.x & m4, qc.y & m4, qc.z & m4, qc.w & m4};
-        const uint32_t wd[4] = {(qc.x >> 4) & m4, (qc.y >> 4) & m4, (qc.z >> 4) & m4, (qc.w >> 4) & m4};
-        kquant_accumulate<NT>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, x, b, j0,
-                              r0, n_tok, acc, r, q == 0);
+        const uint32_t wd[4] = {qc.x & h4, qc.y & h4, qc.z & h4, qc.w & h4};  // 16 * w
+        kquant_accumulate<NT, true>(wa, wb, wc, wd, s, h2f_bits(h.x), h2f_bits(h.x >> 16), job, x, b, j0,
+                                    r0, n_tok, acc, r, q == 0);
     }
     if (!terms && q == 0 && r < nvalid) {
 #pragma unroll

@@ -330,17 +330,17 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
 // sequential dot per position, max, exp, sequential sum, scaling, and a
 // sequential weighted sum of V rows per dimension.
 constexpr int kAttnVChunk = 32;  // V rows per bulk-copied chunk
+constexpr int kAttnVBufs = 4;    // chunk buffers: up to kAttnVBufs - 1 chunks in flight ahead
 template <int G>
 __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__restrict__ q, const __half *__restrict__ kcache,
                                                               const __half *__restrict__ vcache,
                                                               const float *__restrict__ gate, int nh, int kvh,
                                                               const int32_t *__restrict__ pos_ptr, int max_pos,
-                                                              float *__restrict__ ctx, int rows_per_seq,
-                                                              int *__restrict__ err_flag) {
+                                                              float *__restrict__ ctx, int rows_per_seq) {
     constexpr int HD = 128;
     pdl_launch_dependents();
     pdl_wait();
-    // [G][HD] queries, [G][max_pos] scores, then two V chunks of
+    // [G][HD] queries, [G][max_pos] scores, then kAttnVBufs V chunks of
     // kAttnVChunk rows (16-byte aligned: max_pos rounded up to 4)
     extern __shared__ __align__(16) float sh[];
     float *qs = sh;
@@ -348,7 +348,6 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     __half *vbuf = reinterpret_cast<__half *>(sc + G * ((max_pos + 3) & ~3));
     __shared__ float red[G][32];
     __shared__ float s_inv[G];
-    __shared__ uint64_t vbar[2];
     // CTA (sequence b, KV head kh, query j): the query row b * rows_per_seq + j
     // at position *pos_ptr + j (decode: j = 0, one row per sequence)
     const int b = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -359,21 +358,24 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     const __half *kb = kcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
     const __half *vb = vcache + (static_cast<int64_t>(b) * max_pos * kvh + kh) * HD;
     const int n_chunks = (n + kAttnVChunk - 1) / kAttnVChunk;
-    // V rows of chunk c (one bulk copy per 256-byte row) into buffer c & 1
+    // V rows of chunk c into buffer c % kAttnVBufs: every thread copies 16-byte
+    // pieces with cp.async (16 pieces per 256-byte row), one commit group per
+    // chunk (an empty group past the last chunk keeps the group count fixed)
     auto issue_v = [&](int c) {
-        const int r0 = c * kAttnVChunk, rows = min(kAttnVChunk, n - r0);
-        uint64_t *bar = &vbar[c & 1];
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rows) * HD * 2);
-        __half *dst = vbuf + (c & 1) * kAttnVChunk * HD;
-        for (int j = 0; j < rows; ++j) bulk_copy_g2s(dst + j * HD, vb + (r0 + j) * rstride, HD * 2, bar);
+        if (c < n_chunks) {
+            const int r0 = c * kAttnVChunk, rows = min(kAttnVChunk, n - r0);
+            __half *dst = vbuf + (c % kAttnVBufs) * kAttnVChunk * HD;
+            for (int piece = t; piece < rows * (HD / 8); piece += blockDim.x) {
+                const int j = piece / (HD / 8), q16 = piece % (HD / 8);
+                const uint32_t sa = smem_addr(dst + j * HD + q16 * 8);
+                const __half *ga = vb + (r0 + j) * rstride + q16 * 8;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(ga) : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    if (t == 0) {
-        mbar_init(&vbar[0], 1);
-        mbar_init(&vbar[1], 1);
-        mbar_fence_init();
-        // the first V chunk streams in while the scores are formed
-        issue_v(0);
-    }
+    // the first V chunks stream in while the scores are formed
+    for (int c = 0; c < kAttnVBufs - 1; ++c) issue_v(c);
 #pragma unroll
     for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(qrow * nh + kh * G + g) * HD + t];
     __syncthreads();
@@ -468,34 +470,22 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     float o[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) o[g] = 0.0f;
-    bool ok = true;
-    int c = 0;
-    for (; c < n_chunks; ++c) {
-        if (t == 0 && c + 1 < n_chunks) issue_v(c + 1);
-        ok = mbar_wait(&vbar[c & 1], static_cast<uint32_t>(c >> 1) & 1u);
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
-        }
-        const __half *vc = vbuf + (c & 1) * kAttnVChunk * HD;
+    for (int c = 0; c < n_chunks; ++c) {
+        issue_v(c + kAttnVBufs - 1);
+        // this thread's pieces of chunk c have landed; the barrier makes
+        // every thread's pieces visible
+        asm volatile("cp.async.wait_group %0;" ::"n"(kAttnVBufs - 1) : "memory");
+        __syncthreads();
+        const __half *vc = vbuf + (c % kAttnVBufs) * kAttnVChunk * HD;
         const int r0 = c * kAttnVChunk, rows = min(kAttnVChunk, n - r0);
         for (int j = 0; j < rows; ++j) {
             const float v = __half2float(vc[j * HD + t]);
 #pragma unroll
             for (int g = 0; g < G; ++g) o[g] = __fadd_rn(o[g], __fmul_rn(sc[g * max_pos + r0 + j], v));
         }
-        __syncthreads();  // buffer c & 1 is refilled by the issue of chunk c + 2
+        __syncthreads();  // this buffer is refilled by the issue of chunk c + kAttnVBufs
     }
-    if (!ok) {
-        // a chunk that never arrived: report it, and give this CTA's copies
-        // still in flight (chunks c and c + 1) a bounded wait before exiting
-        if (t == 0) {
-            report_error(err_flag, kDevWaitTimeout);
-            for (int cc = c; cc < n_chunks && cc <= c + 1; ++cc)
-                mbar_wait(&vbar[cc & 1], static_cast<uint32_t>(cc >> 1) & 1u);
-        }
-        return;
-    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const int64_t oi = qrow * nh * HD + (kh * G + g) * HD + t;
@@ -667,17 +657,15 @@ int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_
                   int32_t max_pos, float *d_ctx, void *stream, const char *what) {
     const int G = nh / kvh;
     const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + ((static_cast<size_t>(max_pos) + 3) & ~size_t(3))) +
-                        2 * qh::kAttnVChunk * 128 * sizeof(__half);
+                        qh::kAttnVBufs * qh::kAttnVChunk * 128 * sizeof(__half);
     if (smem > 200 * 1024) return bad("attention: context too long");
-    int *err = qh::device_error_word();
-    if (!err) return bad("attention: no device error word");
     if (rows_per_seq > 65535) return bad(what);
     static bool gattr[64][4] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
     void (*kern)(const float *, const __half *, const __half *, const float *, int, int, const int32_t *, int, float *,
-                 int, int *) = G == 1   ? qh::attn_decode_gqa_kernel<1>
+                 int) = G == 1   ? qh::attn_decode_gqa_kernel<1>
                         : G == 2 ? qh::attn_decode_gqa_kernel<2>
                         : G == 4 ? qh::attn_decode_gqa_kernel<4>
                                  : qh::attn_decode_gqa_kernel<8>;
@@ -689,7 +677,7 @@ int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_
                                           static_cast<cudaStream_t>(stream), d_q,
                                           reinterpret_cast<const __half *>(d_kcache),
                                           reinterpret_cast<const __half *>(d_vcache), d_gate, nh, kvh, d_pos, max_pos,
-                                          d_ctx, rows_per_seq, err);
+                                          d_ctx, rows_per_seq);
     return launch_status(le, what);
 }
 }  // namespace
