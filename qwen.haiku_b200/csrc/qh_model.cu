@@ -46,6 +46,28 @@ __device__ double block_sum_d(double v, double *scratch) {
     return t;
 }
 
+// Two block-wide double sums at once, each with block_sum_d's order (warp
+// tree, then the warps in order); scratch holds 2 * 32 doubles.
+__device__ double2 block_sum_d2(double a, double b, double *scratch) {
+    for (int off = 16; off > 0; off >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, off);
+        b += __shfl_xor_sync(0xffffffffu, b, off);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) {
+        scratch[warp] = a;
+        scratch[32 + warp] = b;
+    }
+    __syncthreads();
+    double ta = 0.0, tb = 0.0;
+    for (int w = 0; w < nw; ++w) {
+        ta += scratch[w];
+        tb += scratch[32 + w];
+    }
+    return make_double2(ta, tb);
+}
+
 __device__ float block_max_f(float v, float *scratch) {
     for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -838,12 +860,22 @@ __global__ void __launch_bounds__(HD)
                      int *__restrict__ err_flag, float *__restrict__ y_out) {
     static_assert(HD == 128, "a cluster pair of heads must form one 256-value Q8_K block");
     pdl_launch_dependents();
+    // the conv taps' weights are constant: loaded while the previous kernel finishes
+    float cw[3][kMaxConvTaps];
+    {
+        const int ch0 = blockIdx.y * HD + threadIdx.x, kd = heads * HD;
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+#pragma unroll
+            for (int k = 0; k < kMaxConvTaps; ++k)
+                if (k < kk) cw[part][k] = conv_w[(part * kd + ch0) * kk + k];
+    }
     pdl_wait();
     // The head's 64 KB state arrives by one bulk copy while the conv and
     // norms run, is updated in shared memory and leaves by one bulk store.
     extern __shared__ __align__(128) float st_s[];  // [HD k][HD v]
     __shared__ uint64_t st_bar;
-    __shared__ double scratch[32];
+    __shared__ double scratch[64];
     __shared__ float Ks[HD], Qs[HD];
     __shared__ float s_beta, s_g;
     __shared__ float wa[HD / 32], wv[HD / 32];
@@ -860,10 +892,21 @@ __global__ void __launch_bounds__(HD)
         bulk_copy_g2s(st_s, st, HD * HD * 4, &st_bar);
     }
     // ---- conv ring + SiLU + L2 norms + beta/g (gdn_pre_kernel) ----
-    const int pos = max(*pos_ptr, 0);
-    const int slot = pos % kk, head_after = (pos + 1) % kk;
+    // Every load is issued before the position arrives: the new input and
+    // all kk rows of the ring (the taps are picked once the position is known).
     const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
     float *rg = ring + static_cast<int64_t>(b) * kk * conv_dim;
+    float xin[3], rows[3][kMaxConvTaps];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+        xin[part] = src[ch];
+#pragma unroll
+        for (int r = 0; r < kMaxConvTaps; ++r)
+            if (r < kk) rows[part][r] = rg[static_cast<int64_t>(r) * conv_dim + ch];
+    }
+    const int pos = max(*pos_ptr, 0);
+    const int slot = pos % kk, head_after = (pos + 1) % kk;
     // beta and g on another warp while the conv runs
     if (t == 32) {
         const int i = b * heads + h;
@@ -872,21 +915,21 @@ __global__ void __launch_bounds__(HD)
         const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
         s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
     }
-    // All loads first (the kk - 1 older taps from the ring; the newest tap
-    // is the new input itself), then the ring update, then the sums in tap
-    // order -- the same values and order as writing the slot and reading
-    // every tap back.
-    float xin[3], taps[3][kMaxConvTaps - 1], cw[3][kMaxConvTaps];
+    // The kk - 1 older taps from the ring (the newest tap is the new input
+    // itself), then the ring update, then the sums in tap order -- the same
+    // values and order as writing the slot and reading every tap back.
+    float taps[3][kMaxConvTaps - 1];
 #pragma unroll
-    for (int part = 0; part < 3; ++part) {
-        const int ch = part * kdim + h * HD + t;
-        xin[part] = src[ch];
+    for (int part = 0; part < 3; ++part)
 #pragma unroll
-        for (int k = 0; k < kMaxConvTaps; ++k) {
-            if (k < kk) cw[part][k] = conv_w[ch * kk + k];
-            if (k < kk - 1) taps[part][k] = rg[static_cast<int64_t>((head_after + k) % kk) * conv_dim + ch];
+        for (int k = 0; k < kMaxConvTaps - 1; ++k) {
+            const int rsel = (head_after + k) % kk;
+            float v = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kMaxConvTaps; ++r)
+                if (r == rsel) v = rows[part][r];
+            taps[part][k] = v;
         }
-    }
     float mixed[3];
 #pragma unroll
     for (int part = 0; part < 3; ++part) {
@@ -898,8 +941,9 @@ __global__ void __launch_bounds__(HD)
             if (k < kk) acc = __fadd_rn(acc, __fmul_rn(k < kk - 1 ? taps[part][k] : xin[part], cw[part][k]));
         mixed[part] = silu_f(acc);
     }
-    const double qss = block_sum_d(static_cast<double>(__fmul_rn(mixed[0], mixed[0])), scratch);
-    const double kss = block_sum_d(static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+    const double2 qkss = block_sum_d2(static_cast<double>(__fmul_rn(mixed[0], mixed[0])),
+                                      static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+    const double qss = qkss.x, kss = qkss.y;
     const float qrs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qss)), 1e-6f));
     const float krs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(kss)), 1e-6f));
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
@@ -917,14 +961,21 @@ __global__ void __launch_bounds__(HD)
 #pragma unroll 16
     for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
     const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
-    // update the column first (independent per k), then the output sum
-    // (the sequential double chain) over the updated values
-#pragma unroll 16
-    for (int k = 0; k < HD; ++k)
-        st_s[k * HD + t] = __fadd_rn(__fmul_rn(st_s[k * HD + t], gh), __fmul_rn(Ks[k], delta));
+    // one pass over the column: update each entry (independent per k) and
+    // add its product with Q to the output sum -- the sequential double
+    // chain runs over the updated values in k order, as in the reference
     double acc2 = 0.0;
+    {
+        float *__restrict__ sc = st_s + t;
+        const float *__restrict__ kv = Ks;
+        const float *__restrict__ qv = Qs;
 #pragma unroll 16
-    for (int k = 0; k < HD; ++k) acc2 += static_cast<double>(__fmul_rn(st_s[k * HD + t], Qs[k]));
+        for (int k = 0; k < HD; ++k) {
+            const float sn = __fadd_rn(__fmul_rn(sc[k * HD], gh), __fmul_rn(kv[k], delta));
+            sc[k * HD] = sn;
+            acc2 += static_cast<double>(__fmul_rn(sn, qv[k]));
+        }
+    }
     const float o = static_cast<float>(acc2);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -1083,12 +1134,19 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
 #pragma unroll 16
         for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
         const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
-#pragma unroll 16
-        for (int k = 0; k < HD; ++k)
-            st_s[k * HD + t] = __fadd_rn(__fmul_rn(st_s[k * HD + t], gh), __fmul_rn(Ks[k], delta));
+        // update and output sum in one pass (see gdn_fused_kernel)
         double acc2 = 0.0;
+        {
+            float *__restrict__ sc = st_s + t;
+            const float *__restrict__ kv = Ks;
+            const float *__restrict__ qv = Qs;
 #pragma unroll 16
-        for (int k = 0; k < HD; ++k) acc2 += static_cast<double>(__fmul_rn(st_s[k * HD + t], Qs[k]));
+            for (int k = 0; k < HD; ++k) {
+                const float sn = __fadd_rn(__fmul_rn(sc[k * HD], gh), __fmul_rn(kv[k], delta));
+                sc[k * HD] = sn;
+                acc2 += static_cast<double>(__fmul_rn(sn, qv[k]));
+            }
+        }
         const float o = static_cast<float>(acc2);
         const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
         const float mean = static_cast<float>(ssq / static_cast<double>(HD));
