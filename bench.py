@@ -421,6 +421,35 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     return out, cfg, prompts, picks
 
 
+def run_sampled(qh, torch, B: int, n_prompt: int, n_new: int):
+    """Sampled generation (qh_slm_generate_sampled, the reference's default
+    sampler chain: T 0.7, top-k 40, top-p 0.9, min-p 0.05, repetition
+    penalty 1.25 over 64 tokens) of B sequences: decode tok/s from the time
+    of an n_new-token call minus a 1-token call (the prompt part of both)."""
+    import numpy as np
+    h = qh.host
+    cfg = h.slm_config(n_prompt + n_new + 1)
+    blob = h.Blob(cfg, MODEL_SEED)
+    slm = h.Slm(cfg, blob, B)
+    rng = np.random.default_rng(0x5A3 + B)
+    prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
+    seeds = np.arange(1, B + 1, dtype=np.uint64)
+    sp = h.sampler_defaults()
+    slm.generate_sampled(prompts, 4, sp, seeds)  # warm-up: captures the sampled step
+    times = {}
+    for n in (1, n_new):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = slm.generate_sampled(prompts, n, sp, seeds)
+        times[n] = time.perf_counter() - t0
+    slm.close()
+    dt = times[n_new] - times[1]
+    return {"workload": f"{B} sequence(s)/GPU, {n_prompt}-token prompt, {n_new} sampled tokens",
+            "sampler": "T 0.7, top-k 40, top-p 0.9, min-p 0.05, repetition penalty 1.25 / 64",
+            "tok_s": round(B * (n_new - 1) / dt, 1), "ms_per_step": round(dt / (n_new - 1) * 1e3, 4),
+            "tokens_checksum": int(sum(int(np.sum(o.astype(np.int64) * 2654435761 % (1 << 31))) for o in out) % (1 << 31))}
+
+
 def cpu_decode_baseline(qh, n_steps: int = 4):
     """The reference's own slm_forward_step + sample_argmax (oracle/_ref,
     single-threaded on Linux) on the full-size model: a bounded sample of
@@ -625,7 +654,12 @@ def run_ours(args):
                 continue
             decode[f"batch{B}"], _, _, _ = run_decode(qh, torch, dist, world, rank, B, n_prompt, args.decode_new,
                                                       args.profile_step)
-        runs = list(decode.values())
+        if args.sampled:
+            for B, n_prompt in ((1, 64), (args.decode_batch, args.decode_prompt)):
+                if args.decode_only_batch and B != args.decode_only_batch:
+                    continue
+                decode[f"sampled_batch{B}"] = run_sampled(qh, torch, B, n_prompt, args.decode_new)
+        runs = [v for key, v in decode.items() if key.startswith("batch")]
         decode.update({"clocks": dclk.stop(),
                   "data": "synthetic Qwen3.5-0.8B-shaped weights (Q4_K mix), seeded random prompts",
                   "roofline_peak_gbs": peak, "parallelism": f"dp{world}, replicated weights, "
@@ -707,6 +741,8 @@ def main():
     ap.add_argument("--decode-new", type=int, default=256, help="greedy tokens per decode run")
     ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens of the batched decode")
     ap.add_argument("--decode-only-batch", type=int, default=0, help="run only the decode of this batch size")
+    ap.add_argument("--sampled", action="store_true",
+                    help="also time sampled generation (the reference's default sampler chain)")
     ap.add_argument("--profile-step", action="store_true",
                     help="after the timed decode, run one more step between cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off)")
