@@ -135,18 +135,26 @@ __global__ void __launch_bounds__(kThreads)
         }
     }
 
-    // 1. repetition penalty
+    // 1. repetition penalty: the window is staged in shared memory (the
+    // candidate buffer is free here) unless it is longer than the buffer
     if (sp.repetition_penalty != 1.0f && hn != 0) {
         const int32_t start = (sp.repetition_window > 0 && sp.repetition_window < hn) ? hn - sp.repetition_window : 0;
-        for (int32_t i = start + tid; i < hn; i += kThreads) {
-            const int32_t t = h[i];
+        const int32_t W = hn - start;
+        const int32_t *win = h + start;
+        if (W <= kChunk) {
+            for (int32_t i = tid; i < W; i += kThreads) cand_i[i] = h[start + i];
+            __syncthreads();
+            win = cand_i;
+        }
+        for (int32_t i = tid; i < W; i += kThreads) {
+            const int32_t t = win[i];
             if (t < 0 || static_cast<int64_t>(t) >= vocab) continue;
             bool first = true;
-            for (int32_t j = start; j < i; ++j)
-                if (h[j] == t) { first = false; break; }
+            for (int32_t j = 0; j < i; ++j)
+                if (win[j] == t) { first = false; break; }
             if (!first) continue;
             int32_t n = 1;
-            for (int32_t j = i + 1; j < hn; ++j) n += (h[j] == t);
+            for (int32_t j = i + 1; j < W; ++j) n += (win[j] == t);
             float lv = lr[t];
             for (int32_t r = 0; r < n; ++r)
                 lv = (lv > 0.0f) ? __fdiv_rn(lv, sp.repetition_penalty) : __fmul_rn(lv, sp.repetition_penalty);
@@ -185,33 +193,60 @@ __global__ void __launch_bounds__(kThreads)
         if (tid < filled) { sh.val[tid] = lr[tid]; sh.idx[tid] = tid; }
         __syncthreads();
         if (vocab > k) {
-            // warp 0 keeps the current first minimum (mval, mslot); lane l
-            // owns slots [8l, 8l + 8)
-            float mval = 0.0f, lmin = INFINITY;
+            // warp 0 keeps the slots in registers -- lane l holds slots
+            // 8l .. 8l+7 (values rv, token ids ri) -- and the current first
+            // minimum (mval, mslot); lmin/lslot are the lane's own first
+            // minimum
+            float rv[8], mval = 0.0f, lmin = INFINITY;
+            int32_t ri[8];
             int mslot = 0, lslot = 0x7fffffff;
-            if (warp == 0) {
-                for (int j = 0; j < 8; ++j) {
-                    const int s = lane * 8 + j;
-                    if (s < k && (lslot == 0x7fffffff || sh.val[s] < lmin)) { lmin = sh.val[s]; lslot = s; }
-                }
+            auto lane_min = [&]() {
+                lmin = INFINITY;
+                lslot = 0x7fffffff;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (lane * 8 + j < k && (lslot == 0x7fffffff || rv[j] < lmin)) { lmin = rv[j]; lslot = lane * 8 + j; }
+            };
+            auto warp_min = [&]() {
                 const uint32_t key = lslot == 0x7fffffff ? 0xffffffffu : order_key(lmin);
                 const uint32_t mk = __reduce_min_sync(kFull, key);
                 const int wl = __ffs(__ballot_sync(kFull, key == mk)) - 1;
                 mval = __shfl_sync(kFull, lmin, wl);
                 mslot = __shfl_sync(kFull, lslot, wl);
+            };
+            if (warp == 0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int slot = lane * 8 + j;
+                    rv[j] = slot < k ? sh.val[slot] : INFINITY;
+                    ri[j] = slot < k ? sh.idx[slot] : 0;
+                }
+                lane_min();
+                warp_min();
                 if (lane == 0) sh.mval = mval;
             }
             __syncthreads();
-            for (int64_t base = k; base < vocab; base += kChunk) {
-                const float thr = sh.mval;
-                const int64_t i0 = base + static_cast<int64_t>(tid) * kPerThread;
-                float v[kPerThread];
-                unsigned pass = 0;
+            // Rounds: the first covers kThreads logits (one per thread), the
+            // others kChunk; each thread's logits of the next round are loaded
+            // while warp 0 replays this one.
+            int64_t base = k;
+            int per = 1;
+            float v[kPerThread];
+            auto load_round = [&](int64_t b0, int pt) {
 #pragma unroll
                 for (int r = 0; r < kPerThread; ++r) {
-                    v[r] = (i0 + r < vocab) ? lr[i0 + r] : -INFINITY;
-                    if (i0 + r < vocab && v[r] > thr) pass |= 1u << r;
+                    const int64_t i = b0 + static_cast<int64_t>(tid) * pt + r;
+                    v[r] = (r < pt && i < vocab) ? lr[i] : -INFINITY;
                 }
+            };
+            load_round(base, per);
+            while (base < vocab) {
+                const float thr = sh.mval;
+                const int64_t i0 = base + static_cast<int64_t>(tid) * per;
+                unsigned pass = 0;
+#pragma unroll
+                for (int r = 0; r < kPerThread; ++r)
+                    if (r < per && i0 + r < vocab && v[r] > thr) pass |= 1u << r;
                 const int cnt = __popc(pass);
                 int incl = cnt;
 #pragma unroll
@@ -238,6 +273,9 @@ __global__ void __launch_bounds__(kThreads)
                 for (int r = 0; r < kPerThread; ++r)
                     if (pass & (1u << r)) { cand_v[o] = v[r]; cand_i[o] = static_cast<int32_t>(i0 + r); ++o; }
                 __syncthreads();
+                const int64_t next = base + static_cast<int64_t>(kThreads) * per;
+                per = kPerThread;
+                if (next < vocab) load_round(next, per);
                 if (warp == 0) {
                     const int ncand = sh.ncand;
                     for (int g = 0; g < ncand; g += 32) {
@@ -252,27 +290,29 @@ __global__ void __launch_bounds__(kThreads)
                             const float nv = __shfl_sync(kFull, cv, src);
                             const int32_t ni = __shfl_sync(kFull, ci, src);
                             if (lane == (mslot >> 3)) {
-                                sh.val[mslot] = nv;
-                                sh.idx[mslot] = ni;
-                                lmin = INFINITY;
-                                lslot = 0x7fffffff;
-                                for (int j = 0; j < 8; ++j) {
-                                    const int s = lane * 8 + j;
-                                    if (s < k && (lslot == 0x7fffffff || sh.val[s] < lmin)) { lmin = sh.val[s]; lslot = s; }
-                                }
+                                const int jj = mslot & 7;
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    if (j == jj) { rv[j] = nv; ri[j] = ni; }
+                                lane_min();
                             }
-                            const uint32_t key = lslot == 0x7fffffff ? 0xffffffffu : order_key(lmin);
-                            const uint32_t mk = __reduce_min_sync(kFull, key);
-                            const int wl = __ffs(__ballot_sync(kFull, key == mk)) - 1;
-                            mval = __shfl_sync(kFull, lmin, wl);
-                            mslot = __shfl_sync(kFull, lslot, wl);
+                            warp_min();
                             live &= src == 31 ? 0u : (kFull << (src + 1));
                         }
                     }
                     if (lane == 0) sh.mval = mval;
                 }
                 __syncthreads();
+                base = next;
             }
+            if (warp == 0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int slot = lane * 8 + j;
+                    if (slot < k) { sh.val[slot] = rv[j]; sh.idx[slot] = ri[j]; }
+                }
+            }
+            __syncthreads();
         }
         // 4. softmax with temperature over the slots, in slot order
         if (tid < 32) {
