@@ -404,6 +404,23 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
         mine = gathered.view(world, B)[rank].cpu().numpy()
         if not np.array_equal(mine, picks[:, -1]):
             raise SystemExit("token gather disagrees with the rank's own picks")
+    slm.close()
+    # the same prompts through the reference's batched prefill path
+    # (LLM_USE_FORWARD_BATCH: chunked DeltaNet algebra, QH_PREFILL_CHUNKED)
+    ch = h.Slm(cfg, blob, B)
+    ch.prefill(prompts[:, :min(n_prompt, 9)], mode=qh.PREFILL_CHUNKED)
+    ch.reset()
+    cstream = torch.cuda.ExternalStream(ch.stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    cev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    cev[0].record(cstream)
+    ch.prefill(prompts)
+    cev[1].record(cstream)
+    torch.cuda.synchronize()
+    chunked_ms = max_over_ranks(dist, [cev[0].elapsed_time(cev[1])], "cuda")[0]
+    ch.close()
     step_bytes = decode_step_bytes(cfg, B, wb.value, n_prompt, n_new)
     step_ms = decode_ms / n_new
     out = {
@@ -411,12 +428,12 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
         "tok_s": round(world * B * n_new / (decode_ms / 1e3), 1),
         "ms_per_step": round(step_ms, 4),
         "prefill_tok_s": round(world * B * (n_prompt - 1) / (prefill_ms / 1e3), 1),
+        "prefill_chunked_tok_s": round(world * B * (n_prompt - 1) / (chunked_ms / 1e3), 1),
         "e2e_tok_s": round(world * B * (n_prompt - 1 + n_new) / wall, 1),
         "hbm_bytes_per_step": int(step_bytes), "weight_bytes": wb.value,
         "hbm_gbs": round(step_bytes / (step_ms / 1e3) / 1e9, 1),
         "picks_checksum": int(np.bitwise_xor.reduce(picks.ravel() * np.int64(2654435761) % (1 << 31))),
     }
-    slm.close()
     del blob
     return out, cfg, prompts, picks
 

@@ -158,6 +158,34 @@ int qh_gdn_prefill(const float *d_qkv, float *d_ring, const float *d_conv_w, con
                    const float *d_norm_w, int32_t n_seq, int32_t n_tok, int32_t heads, int32_t hd, int32_t kk,
                    float eps, const int32_t *d_pos, void *d_xq, int32_t layout_tile, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Chunked prefill (the reference's batched prompt path, slm_forward_batch,
+ * slm/qwen.c:1018-1106, taken under LLM_USE_FORWARD_BATCH): its DeltaNet
+ * layers (slm_forward_ssm_batch, slm/qwen.c:627-806) run the 64-token chunk
+ * algebra of chunked_ssm_step_f32 (slm/chunked.c:287-523), which is not
+ * bit-equal to the per-token recurrence; these two kernels reproduce it bit
+ * for bit. Rows are sequence-major (row = s * n_tok + j, position
+ * *d_pos + j); chunks of 64 start at each call's first token.
+ * ---------------------------------------------------------------------- */
+
+/* Conv ring, SiLU, per-head L2 norms, beta and g_log for n_tok tokens per
+ * sequence (slm/qwen.c:652-715), in place: the head slices of each row of
+ * qkv [rows][3*heads*hd] become Q * (qrs / sqrt(hd)), K * krs and silu(conv
+ * V); b and a [rows][heads] become beta = sigmoid(b) and g_log = ssm_a *
+ * softplus(a + dt_bias). The ring [n_seq][kk][3*heads*hd] is read at and
+ * left for the chunk's positions, as qh_gdn_prefill. hd 128, kk 4. */
+int qh_gdn_chunk_prep(float *d_qkv, float *d_ring, const float *d_conv_w, float *d_b, float *d_a,
+                      const float *d_dt_bias, const float *d_ssm_a, int32_t n_seq, int32_t n_tok, int32_t heads,
+                      int32_t hd, int32_t kk, const int32_t *d_pos, void *stream);
+
+/* The chunked delta rule over n_tok tokens per sequence: for each head and
+ * each chunk of <= 64 tokens, chunked_ssm_step_f32 (slm/chunked.c:287-523)
+ * on qh_gdn_chunk_prep's rows, the state [n_seq][heads][hd k][hd v] (16-byte
+ * aligned) carried across chunks. out [rows][heads*hd] receives the
+ * per-token outputs before the gated norm (qh_gdn_gated_norm). hd 128. */
+int qh_gdn_chunked(const float *d_qkv, const float *d_beta, const float *d_glog, float *d_state, int32_t n_seq,
+                   int32_t n_tok, int32_t heads, int32_t hd, float *d_out, void *stream);
+
 /* qh_gdn_fused without the quantization: the gated-norm output y fp32
  * [B][heads*hd] for qh_quantize_q8k / qh_quantize_q8kt. The heads are then
  * independent CTAs (no cluster pairs), which keeps more of them resident

@@ -128,6 +128,22 @@ int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt);
  * all sequences); only before the first qh_slm_prefill. */
 int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq);
 
+/* How qh_slm_prefill runs the Gated DeltaNet layers:
+ *   QH_PREFILL_STEPWISE (default) -- the per-token recurrence, the same
+ *     caches as feeding the prompt one token per step (slm_generate_raw's
+ *     default prefill, slm/slm.c:280-287);
+ *   QH_PREFILL_CHUNKED -- the reference's batched prefill taken under
+ *     LLM_USE_FORWARD_BATCH (slm_forward_batch, slm/qwen.c:1018-1106): the
+ *     64-token chunk algebra of chunked_ssm_step_f32 (slm/chunked.c:287),
+ *     bit-identical to it, not to the per-token recurrence. Attention and
+ *     FFN layers are the same in both. Chunks of 64 tokens count from
+ *     position 0, so a prompt chunk (qh_slm_set_prefill_chunk) is rounded
+ *     down to a multiple of 64 (at least 64) in this mode.
+ * Only before the first qh_slm_prefill. */
+#define QH_PREFILL_STEPWISE 0
+#define QH_PREFILL_CHUNKED 1
+int qh_slm_set_prefill_mode(qh_slm *m, int32_t mode);
+
 /* Greedy generation, the per-step prefill path of slm_generate_raw
  * (slm/slm.c:237-357) for every sequence: the prompt runs through
  * qh_slm_prefill (the same caches as feeding one token per step) and the

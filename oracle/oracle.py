@@ -99,7 +99,16 @@ class Oracle:
         L.orc_matmul.restype = _I
         L.orc_sample_with.argtypes = [_P, _I64, _P, _P, _P, _P, C.c_int32]
         L.orc_sample_with.restype = C.c_int32
+        L.orc_chunked_step.argtypes = [_I, _I, _P, _P, _P, _P, _P, _P, _P, _I]
+        L.orc_chunked_step.restype = _I
         self.L = L
+
+    def chunked_prefill(self, q, k, v, g_log, beta, state, cr: bool = True):
+        """slm_forward_ssm_batch's chunk loop (slm/qwen.c:777-806) for one head:
+        q, k, v [n][hd], g_log, beta [n]; state [hd][hd] is updated in place.
+        Returns out [n][hd]. cr selects correctly rounded expf (the device's)."""
+        return _chunked_loop(lambda *a: self.L.orc_chunked_step(*a, 1 if cr else 0),
+                             q, k, v, g_log, beta, state)
 
     def sample_with(self, logits: np.ndarray, sp: dict, st: np.ndarray, hist) -> int:
         """Restated sample_with on `logits` (float32, penalized in place) with
@@ -177,6 +186,24 @@ class Oracle:
         return y
 
 
+def _chunked_loop(step, q, k, v, g_log, beta, state):
+    """Runs `step` (a chunked_ssm_step_f32 of <= 64 tokens) over the tokens in
+    64-token chunks with the state carried, as slm_forward_ssm_batch does."""
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    g_log, beta = (np.ascontiguousarray(a, np.float32) for a in (g_log, beta))
+    assert state.dtype == np.float32 and state.flags.c_contiguous
+    n, hd = q.shape
+    out = np.empty((n, hd), np.float32)
+    for c0 in range(0, n, 64):
+        cn = min(64, n - c0)
+        o = np.empty((cn, hd), np.float32)
+        sl = [np.ascontiguousarray(a[c0:c0 + cn]) for a in (q, k, v, g_log, beta)]
+        rc = step(cn, hd, *[_ptr(a) for a in sl[:3]], _ptr(sl[3]), _ptr(sl[4]), _ptr(state), _ptr(o))
+        assert rc == 0, "chunked step rejected its arguments"
+        out[c0:c0 + cn] = o
+    return out
+
+
 class Ref:
     """The reference's own C code (oracle/_ref/libqhref.so)."""
 
@@ -212,6 +239,8 @@ class Ref:
         L.ref_sample_with.restype = C.c_int32
         L.ref_rng_seed.argtypes = [C.c_uint64, _P]
         L.ref_sampler_defaults.argtypes = [_P, _P]
+        L.ref_chunked_step.argtypes = [C.c_int32] * 3 + [_P] * 7
+        L.ref_chunked_step.restype = _I
         self.L = L
         self.label = L.ref_dispatch_label().decode()
 
@@ -291,6 +320,11 @@ class Ref:
         ptrs = (C.c_void_p * len(pool))(*[w.ctypes.data for w in pool])
         self.L.ref_matvec_pool_mt(gtype, ptrs, len(pool), out_f, k, _ptr(xq_blocks), _ptr(out), nthreads)
 
+    def chunked_prefill(self, q, k, v, g_log, beta, state):
+        """The reference's own chunked_ssm_step_f32 in slm_forward_ssm_batch's
+        chunk loop; same arguments as Oracle.chunked_prefill."""
+        return _chunked_loop(lambda n, hd, *a: self.L.ref_chunked_step(n, hd, hd, *a), q, k, v, g_log, beta, state)
+
     def dequant_block(self, gtype, blk: np.ndarray) -> np.ndarray:
         y = np.empty(256, np.float32)
         self.L.ref_dequant_block(gtype, _ptr(np.ascontiguousarray(blk, np.uint8)), _ptr(y))
@@ -318,6 +352,8 @@ class RefModel:
         L.ref_snapshot_free.argtypes = [_P]
         L.ref_trace_begin.argtypes = [C.c_char_p]
         L.ref_trace_begin.restype = C.c_int
+        L.ref_model_forward_batch.argtypes = [_P, _P, C.c_int32, C.c_int32, _P]
+        L.ref_model_forward_batch.restype = C.c_int
 
     @classmethod
     def from_gguf(cls, ref: "Ref", path: str):
@@ -354,6 +390,15 @@ class RefModel:
     def step(self, tok: int, pos: int, want_logits: bool = False):
         logits = np.empty(self.vocab, np.float32) if want_logits else None
         a = self.L.ref_model_step(self.h, int(tok), int(pos), _ptr(logits) if logits is not None else None)
+        return (a, logits) if want_logits else a
+
+    def forward_batch(self, toks, pos_start: int, want_logits: bool = False):
+        """slm_forward_batch (the LLM_USE_FORWARD_BATCH prefill) over `toks` at
+        positions pos_start..; returns the last token's argmax (and logits)."""
+        t = np.ascontiguousarray(toks, np.int32)
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        a = self.L.ref_model_forward_batch(self.h, _ptr(t), len(t), int(pos_start),
+                                           _ptr(logits) if logits is not None else None)
         return (a, logits) if want_logits else a
 
     def snapshot(self, pos: int):

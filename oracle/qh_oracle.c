@@ -474,3 +474,109 @@ int32_t orc_sample_with(float *lg, int64_t n, const float *fp, const int32_t *ip
     }
     return si[picked];
 }
+
+// ---------------------------------------------------------------------------
+// Chunked Gated DeltaNet step (slm/chunked.c:287-523, chunked_ssm_step_f32),
+// the prompt path of slm_forward_ssm_batch (slm/qwen.c:772-806): one head,
+// n <= 64 tokens, state [hd k][hd v] carried in place, out [n][hd v].
+//
+// Written as the device kernel computes it: every matrix entry is a single
+// float chain, terms added in the reference's index order, products and
+// sums rounded separately (no FMA). Terms the reference adds that are
+// products with an exact zero (the masked upper triangles, the zero rows of
+// the forward substitution) leave a finite running sum unchanged and are
+// skipped. K*beta, V*beta, K*beta*gexp and Q*gexp are recomputed where used
+// (the same rounded products the reference stores).
+//
+// cr = 0: expf from the host libm (as the reference built here);
+// cr = 1: correctly rounded expf (double exp rounded once), as the device.
+// ---------------------------------------------------------------------------
+#define ORC_CH 64
+#define ORC_HD 128
+
+static float orc_expf(float x, int cr) { return cr ? (float)exp((double)x) : expf(x); }
+
+int orc_chunked_step(int n, int hd, const float *q, const float *k, const float *v, const float *g_log,
+                     const float *beta, float *state, float *out, int cr) {
+    if (n < 1 || n > ORC_CH || hd < 1 || hd > ORC_HD) return -1;
+    static float gcs[ORC_CH], gexp[ORC_CH], diff[ORC_CH];
+    static float kk[ORC_CH][ORC_CH], A[ORC_CH][ORC_CH], kq[ORC_CH][ORC_CH];
+    static float veff[ORC_CH][ORC_HD], kcd[ORC_CH][ORC_HD], vnew[ORC_CH][ORC_HD];
+    static float inter[ORC_CH][ORC_HD], kgd[ORC_HD][ORC_HD];
+    // running log-decay and its exponentials (chunked.c:311-320)
+    float acc = 0.0f;
+    for (int t = 0; t < n; t++) {
+        acc += g_log[t];
+        gcs[t] = acc;
+        gexp[t] = orc_expf(acc, cr);
+    }
+    // kk[i][j] = (K_j . (K_i*beta_i)) * exp(gcs_i - gcs_j), j < i (chunked.c:340-358)
+    for (int i = 0; i < n; i++)
+        for (int j = 0; j < i; j++) {
+            float s = 0.0f;
+            for (int d = 0; d < hd; d++) s += k[j * hd + d] * (k[i * hd + d] * beta[i]);
+            kk[i][j] = s * orc_expf(gcs[i] - gcs[j], cr);
+        }
+    // forward substitution (I + kk) X = -kk, then A = X + I on and below the
+    // diagonal (chunked.c:224-238, 364-386): column j, rows i > j, terms
+    // t = j+1 .. i-1 in order
+    for (int j = 0; j < n; j++) {
+        A[j][j] = 1.0f;
+        for (int i = j + 1; i < n; i++) {
+            float s = 0.0f;
+            for (int t = j + 1; t < i; t++) s += kk[i][t] * A[t][j];
+            A[i][j] = -kk[i][j] - s;
+        }
+    }
+    // V_eff = A (V*beta); k_cumdecay = A (K*beta*gexp) (chunked.c:391-426)
+    for (int i = 0; i < n; i++)
+        for (int e = 0; e < hd; e++) {
+            float s = 0.0f, c = 0.0f;
+            for (int j = 0; j <= i; j++) {
+                if (A[i][j] != 0.0f) {
+                    s += A[i][j] * (v[j * hd + e] * beta[j]);
+                    c += A[i][j] * ((k[j * hd + e] * beta[j]) * gexp[j]);
+                }
+            }
+            veff[i][e] = s;
+            kcd[i][e] = c;
+        }
+    // kq[i][j] = (K_j . Q_i) * decay, j <= i, decay 1 on the diagonal (chunked.c:430-443)
+    for (int i = 0; i < n; i++)
+        for (int j = 0; j <= i; j++) {
+            float s = 0.0f;
+            for (int d = 0; d < hd; d++) s += k[j * hd + d] * q[i * hd + d];
+            kq[i][j] = s * (i == j ? 1.0f : orc_expf(gcs[i] - gcs[j], cr));
+        }
+    // attn_inter = (Q*gexp) S; v_new = V_eff - k_cumdecay S (chunked.c:445-484)
+    for (int t = 0; t < n; t++)
+        for (int e = 0; e < hd; e++) {
+            float si = 0.0f, sp = 0.0f;
+            for (int d = 0; d < hd; d++) {
+                const float qg = q[t * hd + d] * gexp[t];
+                if (qg != 0.0f) si += qg * state[d * hd + e];
+                if (kcd[t][d] != 0.0f) sp += kcd[t][d] * state[d * hd + e];
+            }
+            inter[t][e] = si;
+            vnew[t][e] = veff[t][e] - sp;
+        }
+    // out = attn_inter + kq v_new (chunked.c:486-501)
+    for (int t = 0; t < n; t++)
+        for (int e = 0; e < hd; e++) {
+            float s = 0.0f;
+            for (int u = 0; u <= t; u++) s += kq[t][u] * vnew[u][e];
+            out[t * hd + e] = inter[t][e] + s;
+        }
+    // S = S * exp(gcs_last) + (K * exp(gcs_last - gcs))^T v_new (chunked.c:503-522)
+    const float gl = gcs[n - 1], gle = orc_expf(gl, cr);
+    for (int t = 0; t < n; t++) diff[t] = orc_expf(gl - gcs[t], cr);
+    for (int d = 0; d < hd; d++)
+        for (int e = 0; e < hd; e++) {
+            float s = 0.0f;
+            for (int t = 0; t < n; t++) s += (k[t * hd + d] * diff[t]) * vnew[t][e];
+            kgd[d][e] = s;
+        }
+    for (int d = 0; d < hd; d++)
+        for (int e = 0; e < hd; e++) state[d * hd + e] = state[d * hd + e] * gle + kgd[d][e];
+    return 0;
+}

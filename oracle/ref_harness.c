@@ -22,6 +22,8 @@
 //   sample_with, rng_seed, rng_uniform         slm/sampler.c:134, slm/model.c:431-447
 //   slm_ctx_snapshot / restore / free           slm/model.c:1262-1371
 //   JSONL tracer (g_qh_trace_fp, slm_trace_close) slm/model.c:585-727
+//   slm_forward_batch (chunked prefill)          slm/qwen.c:1018-1106
+//   chunked_ssm_step_f32                        slm/chunked.c:287-523
 
 // Built twice by oracle/Makefile: libqhref.so is the reference as shipped;
 // libqhref_crlibm.so (-DQH_CR_LIBM) is the same sources with expf/logf
@@ -457,3 +459,38 @@ int ref_trace_begin(const char *path) {
     return g_qh_trace_fp ? 0 : -1;
 }
 void ref_trace_end(void) { slm_trace_close(); }
+
+// The batched prefill the reference runs under LLM_USE_FORWARD_BATCH
+// (slm/slm.c:274-283): slm_forward_batch (slm/qwen.c:1018-1106) over n
+// tokens at positions pos_start.. -- chunked Gated DeltaNet layers
+// (slm_forward_ssm_batch, slm/qwen.c:627-806) and batched attention
+// (slm_forward_attn_batch, slm/model.c:955-1120). Copies the last token's
+// logits out (if non-null) and returns their sample_argmax.
+int ref_model_forward_batch(void *h, const int32_t *toks, int32_t n, int32_t pos_start, float *logits) {
+    struct ref_model *r = (struct ref_model *)h;
+    struct tensor *lg = slm_forward_batch(&r->c, toks, n, pos_start);
+    if (logits) memcpy(logits, lg->data, (size_t)r->m.cfg.vocab_size * sizeof(float));
+    return sample_argmax(lg);
+}
+
+// One chunked_ssm_step_f32 (slm/chunked.c:287-523) on caller arrays: n
+// (<= 64) tokens of one head, state [k_hd][v_hd] updated in place, out
+// [n][v_hd]. The kernel's scratch is allocated here.
+int ref_chunked_step(int32_t n, int32_t k_hd, int32_t v_hd, const float *q, const float *k, const float *v,
+                     const float *g_log, const float *beta, float *state, float *out) {
+    if (n < 1 || n > CHUNK_SIZE) return -1;
+    const size_t C = CHUNK_SIZE, kd = (size_t)k_hd, vd = (size_t)v_hd;
+    const size_t sizes[19] = {C, C, C * C, C * kd, C * vd, C * C, C * C, C * C, C * vd, C * kd,
+                              C * kd, C * C, C * kd, C * vd, C * vd, C * vd, C * vd, C * kd, kd * vd};
+    float *s[19];
+    int ok = 1;
+    for (int i = 0; i < 19; i++) {
+        s[i] = (float *)calloc(sizes[i] > C * C ? sizes[i] : C * C, sizeof(float));
+        ok &= s[i] != NULL;
+    }
+    if (ok)
+        chunked_ssm_step_f32(n, k_hd, v_hd, q, k, v, g_log, beta, state, out, s[0], s[1], s[2], s[3], s[4], s[5],
+                             s[6], s[7], s[8], s[9], s[10], s[11], s[12], s[13], s[14], s[15], s[16], s[17], s[18]);
+    for (int i = 0; i < 19; i++) free(s[i]);
+    return ok ? 0 : -1;
+}

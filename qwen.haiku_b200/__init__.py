@@ -27,6 +27,9 @@ STATUS_NAMES = {
     -4: "QH_ERR_ALIGN", -5: "QH_ERR_WORKSPACE", -6: "QH_ERR_DEVICE",
 }
 
+# qh_slm_set_prefill_mode (include/qh_slm.h)
+PREFILL_STEPWISE, PREFILL_CHUNKED = 0, 1
+
 # GGUF tensor types (slm/gguf.c:52-59).
 F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
 TYPE_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
@@ -144,6 +147,7 @@ SIGNATURES.update({
     "qh_slm_begin": (_I, [_P, _P, C.c_int32]),
     "qh_slm_prefill": (_I, [_P, _P, C.c_int32]),
     "qh_slm_set_prefill_chunk": (_I, [_P, C.c_int32]),
+    "qh_slm_set_prefill_mode": (_I, [_P, C.c_int32]),
     "qh_slm_advance": (_I, [_P, C.c_int32]),
     "qh_slm_picks": (_I, [_P, C.c_int32, C.c_int32, _P]),
     "qh_slm_stream": (_P, [_P]),
@@ -179,6 +183,9 @@ SIGNATURES.update({  # include/qh_kernels.h
                              _P, _P]),
     "qh_gdn_prefill": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                             C.c_int32, C.c_float, _P, _P, C.c_int32, _P]),
+    "qh_gdn_chunk_prep": (_I, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                               _P, _P]),
+    "qh_gdn_chunked": (_I, [_P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _P]),
     "qh_argmax_feed": (_I, [_P, C.c_int32, _I64, _P, _P, _P, C.c_int32, _P, _P, _P, _P]),
     "qh_slm_trace": (_I, [_P, C.c_int32, C.c_char_p]),
     "qh_slm_snapshot": (_I, [_P, _P]),

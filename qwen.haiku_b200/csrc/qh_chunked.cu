@@ -1,0 +1,469 @@
+// SPDX-License-Identifier: MIT
+//
+// qh_chunked.cu -- the chunked Gated DeltaNet prefill on sm_100a: the
+// reference's batched prompt path (slm_forward_batch, slm/qwen.c:1018-1106,
+// taken by slm_generate_raw under LLM_USE_FORWARD_BATCH, slm/slm.c:274-283),
+// whose DeltaNet layers run slm_forward_ssm_batch (slm/qwen.c:627-806) and
+// its 64-token chunk kernel chunked_ssm_step_f32 (slm/chunked.c:287-523).
+//
+// That path is not bit-equal to the per-token recurrence (the chunk algebra
+// sums in float, in another order); these kernels reproduce IT, bit for bit:
+//
+//   gdn_chunk_prep_kernel  conv ring + SiLU + per-head L2 norms + beta and
+//                          g_log for every prompt token (slm/qwen.c:652-715),
+//                          in place over the projections.
+//   gdn_chunked_kernel     one CTA per (sequence, head), the head's state in
+//                          shared memory; per 64-token chunk every matrix of
+//                          chunked_ssm_step_f32 as float chains in the
+//                          reference's index order (products and sums rounded
+//                          separately, never contracted), the forward
+//                          substitution as a wavefront over the rows.
+//
+// Every entry of every matrix is one thread's sequential sum, so the
+// arithmetic is the reference's; the work is spread by giving threads whole
+// entries (512 threads: a column e and every fourth row). The chunk algebra
+// has more multiply-adds per token than the recurrence, and with float
+// sums that must stay sequential it cannot move to the tensor cores, so on
+// this device it is about as fast as the per-token prefill -- it exists to
+// reproduce the reference's batched path.
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+
+#include "../../include/qh_backend.h"
+#include "../../include/qh_kernels.h"
+#include "qh_common.cuh"
+#include "qh_internal.h"
+
+namespace qh {
+namespace {
+
+constexpr int kChunk = 64;   // CHUNK_SIZE (slm/chunked.c:116)
+constexpr int kHd = 128;     // key = value head dim (asserted by the reference, slm/qwen.c:413)
+constexpr int kLdk = 132;    // row stride of the q/k tiles: 16-byte rows, float4 column walks conflict-free
+constexpr int kRowGroups = 4;
+constexpr int kThreads = kHd * kRowGroups;  // 512: thread (e = t % 128, rows t / 128 + 4r)
+constexpr int kRows = kChunk / kRowGroups;  // 16 rows per thread
+
+// shared-memory layout of gdn_chunked_kernel, in floats
+constexpr int kOffSt = 0;                          // state [hd k][hd v]
+constexpr int kOffK = kOffSt + kHd * kHd;          // K rows, later K * exp(gcs_last - gcs)
+constexpr int kOffQ = kOffK + kChunk * kLdk;       // Q rows, later Q*gexp, K*beta*gexp, k_cumdecay
+constexpr int kOffV = kOffQ + kChunk * kLdk;       // V rows, later V*beta, v_eff, v_new
+constexpr int kOffM1 = kOffV + kChunk * kHd;       // K.K_beta * decay, later K.Q * decay
+constexpr int kOffM2 = kOffM1 + kChunk * kChunk;   // the substitution's X, then attn
+constexpr int kOffVec = kOffM2 + kChunk * kChunk;  // g_log, gcs, gexp, beta, diff [64] each
+constexpr int kSmemFloats = kOffVec + 5 * kChunk;
+constexpr int kSmemBytes = kSmemFloats * 4;
+static_assert(kSmemBytes <= 227 * 1024, "chunk kernel shared memory");
+
+__device__ double sum2_d(double &a, double b, double *scratch) {
+    // two block-wide double sums: warp xor tree, then the warps in order
+    for (int off = 16; off > 0; off >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, off);
+        b += __shfl_xor_sync(0xffffffffu, b, off);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) {
+        scratch[warp] = a;
+        scratch[32 + warp] = b;
+    }
+    __syncthreads();
+    double ta = 0.0, tb = 0.0;
+    for (int w = 0; w < nw; ++w) {
+        ta += scratch[w];
+        tb += scratch[32 + w];
+    }
+    a = ta;
+    return tb;
+}
+
+// Conv ring, SiLU, per-head L2 norms, beta and g_log for n_tok consecutive
+// tokens of each sequence (slm_forward_ssm_batch steps 3-8,
+// slm/qwen.c:652-715). CTA (sequence, head), hd threads; thread t owns
+// channel t of the head in each of Q, K, V and walks the tokens in order
+// with the conv history in registers. Rewrites, per row, the head's slice of
+// qkv [rows][3*heads*hd] as Q * (qrs * scale), K * krs, silu(conv V), and
+// bb / aa [rows][heads] as beta and g_log. Rows are sequence-major; the
+// chunk starts at position *pos_ptr; the ring slots of the chunk's last
+// KK-1 positions receive their raw projections, as the reference's ring.
+template <int HD, int KK>
+__global__ void __launch_bounds__(HD) gdn_chunk_prep_kernel(float *__restrict__ qkv, float *__restrict__ ring,
+                                                            const float *__restrict__ conv_w, float *__restrict__ bb,
+                                                            float *__restrict__ aa, const float *__restrict__ dt_bias,
+                                                            const float *__restrict__ ssm_a, int heads,
+                                                            const int32_t *__restrict__ pos_ptr, int n_tok) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ double scratch[64];
+    const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+    const int kdim = heads * HD, conv_dim = 3 * kdim;
+    const int pos0 = max(*pos_ptr, 0);
+    float *rg = ring + static_cast<int64_t>(b) * KK * conv_dim;
+    float hist[3][KK - 1], cw[3][KK];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+#pragma unroll
+        for (int k = 0; k < KK; ++k) cw[part][k] = conv_w[ch * KK + k];
+#pragma unroll
+        for (int k = 0; k < KK - 1; ++k) hist[part][k] = rg[static_cast<int64_t>((pos0 + 1 + k) % KK) * conv_dim + ch];
+    }
+    // 1 / sqrtf((float)k_hd)
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
+    for (int j = 0; j < n_tok; ++j) {
+        const int64_t row = static_cast<int64_t>(b) * n_tok + j;
+        float *x = qkv + row * conv_dim + h * HD + t;
+        float mixed[3];
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const float xin = x[part * kdim];
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < KK; ++k)
+                acc = __fadd_rn(acc, __fmul_rn(k < KK - 1 ? hist[part][k] : xin, cw[part][k]));
+#pragma unroll
+            for (int k = 0; k < KK - 2; ++k) hist[part][k] = hist[part][k + 1];
+            hist[part][KK - 2] = xin;
+            mixed[part] = silu_f(acc);
+        }
+        double qss = static_cast<double>(__fmul_rn(mixed[0], mixed[0]));
+        const double kss = sum2_d(qss, static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+        const float qrs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qss)), 1e-6f));
+        const float krs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(kss)), 1e-6f));
+        // Q_all *= qrs * scale; K_all *= krs (slm/qwen.c:692-695)
+        x[0] = __fmul_rn(mixed[0], __fmul_rn(qrs, scale));
+        x[kdim] = __fmul_rn(mixed[1], krs);
+        x[2 * kdim] = mixed[2];
+        if (t == 0) {
+            const int64_t i = row * heads + h;
+            const float bv = bb[i];
+            const float a = __fadd_rn(aa[i], dt_bias[h]);
+            const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
+            bb[i] = sigmoid_f(bv);
+            aa[i] = __fmul_rn(ssm_a[h], sp);
+        }
+    }
+    const int last = pos0 + n_tok - 1;
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * kdim + h * HD + t;
+#pragma unroll
+        for (int k = 0; k < KK - 1; ++k)
+            rg[static_cast<int64_t>(((last - (KK - 2) + k) % KK + KK) % KK) * conv_dim + ch] = hist[part][k];
+    }
+}
+
+__device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+
+// s += a.x*b.x; s += a.y*b.y; ... in that order, each product and sum rounded
+__device__ __forceinline__ float dot4(float s, const float4 &a, const float4 &b) {
+    s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+    s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+    s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+    s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+    return s;
+}
+
+// acc[r] = sum_d A[row_r][d] * st[d][e], d = 0..hd-1 in order, for the
+// thread's rows row_r = rg + 4r < cn (A: a [64][kLdk] tile).
+__device__ __forceinline__ void rows_times_state(const float *__restrict__ A, const float *__restrict__ st, int e, int rg,
+                                                 int cn, float (&acc)[kRows]) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) acc[r] = 0.0f;
+    const int nr = (cn - rg + kRowGroups - 1) / kRowGroups;  // rows of this thread inside the chunk
+    for (int d = 0; d < kHd; d += 4) {
+        const float4 s = make_float4(st[d * kHd + e], st[(d + 1) * kHd + e], st[(d + 2) * kHd + e],
+                                     st[(d + 3) * kHd + e]);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+            if (r < nr) acc[r] = dot4(acc[r], lds4(A + (rg + kRowGroups * r) * kLdk + d), s);
+    }
+}
+
+// acc[r] = sum_{j <= row_r} M[row_r][j] * B[j][e], j in order (M: [64][64],
+// B: column e of a tile with row stride ldb).
+__device__ __forceinline__ void lower_times_tile(const float *__restrict__ M, const float *__restrict__ B, int ldb,
+                                                 int e, int rg, int cn, float (&acc)[kRows]) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+        const int i = rg + kRowGroups * r;
+        float s = 0.0f;
+        if (i < cn) {
+            const float *mi = M + i * kChunk;
+            for (int j = 0; j <= i; ++j) s = __fadd_rn(s, __fmul_rn(mi[j], B[j * ldb + e]));
+        }
+        acc[r] = s;
+    }
+}
+
+// Chunked Gated DeltaNet over n_tok tokens per sequence (slm/qwen.c:772-806
+// driving slm/chunked.c:287-523): CTA (sequence, head), 512 threads, the
+// head's state [hd k][hd v] in shared memory for all chunks. Inputs are the
+// prep kernel's rows (qkv, beta, g_log); out [rows][heads*hd] receives the
+// per-token outputs before the gated norm.
+__global__ void __launch_bounds__(kThreads, 1)
+    gdn_chunked_kernel(const float *__restrict__ qkv, const float *__restrict__ beta_in,
+                       const float *__restrict__ glog_in, float *__restrict__ state, int heads, int n_tok,
+                       float *__restrict__ out, int *__restrict__ err_flag) {
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ __align__(128) float sm[];
+    __shared__ uint64_t st_bar;
+    float *const st = sm + kOffSt, *const kc = sm + kOffK, *const qc = sm + kOffQ, *const vb = sm + kOffV;
+    float *const m1 = sm + kOffM1, *const m2 = sm + kOffM2;
+    float *const glg = sm + kOffVec, *const gcs = glg + kChunk, *const gex = gcs + kChunk, *const bet = gex + kChunk,
+                 *const dif = bet + kChunk;
+    const int s = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+    const int e = t & (kHd - 1), rg = t >> 7;
+    const int kdim = heads * kHd, ld = 3 * kdim;
+    float *const stg = state + (static_cast<int64_t>(s) * heads + h) * kHd * kHd;
+    if (t == 0) {
+        mbar_init(&st_bar, 1);
+        mbar_fence_init();
+        mbar_arrive_expect_tx(&st_bar, kHd * kHd * 4);
+        bulk_copy_g2s(st, stg, kHd * kHd * 4, &st_bar);
+    }
+    bool waited = false;
+    for (int c0 = 0; c0 < n_tok; c0 += kChunk) {
+        const int cn = min(kChunk, n_tok - c0);
+        const int64_t row0 = static_cast<int64_t>(s) * n_tok + c0;
+        // ---- chunk rows: q, k, v of this head; beta, g_log
+        for (int i = rg; i < cn; i += kRowGroups) {
+            const float *src = qkv + (row0 + i) * ld + h * kHd + e;
+            qc[i * kLdk + e] = src[0];
+            kc[i * kLdk + e] = src[kdim];
+            vb[i * kHd + e] = src[2 * kdim];
+        }
+        if (t < cn) {
+            bet[t] = beta_in[(row0 + t) * heads + h];
+            glg[t] = glog_in[(row0 + t) * heads + h];
+        }
+        __syncthreads();
+        // g_cumsum (slm/chunked.c:311-315): token t's running sum, in order
+        if (t < cn) {
+            float acc = 0.0f;
+            for (int i = 0; i <= t; ++i) acc = __fadd_rn(acc, glg[i]);
+            gcs[t] = acc;
+        }
+        __syncthreads();
+        if (t < cn) {
+            gex[t] = expf_cr(gcs[t]);
+            dif[t] = expf_cr(__fsub_rn(gcs[cn - 1], gcs[t]));
+        }
+        // ---- kk[i][j] = (K_j . (K_i * beta_i)) * exp(gcs_i - gcs_j), j < i (slm/chunked.c:340-358)
+        for (int idx = t; idx < kChunk * kChunk; idx += kThreads) {
+            const int i = idx >> 6, j = idx & (kChunk - 1);
+            if (j < i && i < cn) {
+                const float *ki = kc + i * kLdk, *kj = kc + j * kLdk;
+                const float bi = bet[i];
+                float acc = 0.0f;
+#pragma unroll 4
+                for (int d = 0; d < kHd; d += 4) {
+                    const float4 a = lds4(kj + d), bq = lds4(ki + d);
+                    acc = dot4(acc, a, make_float4(__fmul_rn(bq.x, bi), __fmul_rn(bq.y, bi), __fmul_rn(bq.z, bi),
+                                                   __fmul_rn(bq.w, bi)));
+                }
+                m1[i * kChunk + j] = __fmul_rn(acc, expf_cr(__fsub_rn(gcs[i], gcs[j])));
+            }
+        }
+        if (!waited) {
+            if (t == 0 && !mbar_wait(&st_bar, 0)) report_error(err_flag, kDevWaitTimeout);
+            waited = true;
+        }
+        __syncthreads();
+        // ---- forward substitution (I + kk) X = -kk (slm/chunked.c:224-238, 364-386), as a
+        // wavefront: after step s every X[s+1][j] is final. Thread: column j, rows i0 + 8m.
+        {
+            const int j = t & (kChunk - 1), i0 = t >> 6;
+            float acc[kChunk / 8];
+#pragma unroll
+            for (int m = 0; m < kChunk / 8; ++m) acc[m] = 0.0f;
+            for (int st_i = 0; st_i + 1 < cn; ++st_i) {
+                // terms t = st_i of rows i > st_i in column j < st_i: kk[i][st_i] * X[st_i][j]
+                if (j < st_i) {
+                    const float x = m2[st_i * kChunk + j];
+#pragma unroll
+                    for (int m = 0; m < kChunk / 8; ++m) {
+                        const int i = i0 + 8 * m;
+                        if (i > st_i && i < cn) acc[m] = __fadd_rn(acc[m], __fmul_rn(m1[i * kChunk + st_i], x));
+                    }
+                }
+                // row st_i + 1 is complete: X = -kk - sum (the reference's (B - sum) / 1)
+                const int rn = st_i + 1;
+                if ((rn & 7) == i0 && j < rn) {
+#pragma unroll
+                    for (int m = 0; m < kChunk / 8; ++m)
+                        if (i0 + 8 * m == rn) m2[rn * kChunk + j] = __fsub_rn(-m1[rn * kChunk + j], acc[m]);
+                }
+                __syncthreads();
+            }
+            if (t < cn) m2[t * kChunk + t] = 1.0f;  // attn = X + I on and below the diagonal
+        }
+        __syncthreads();
+        // ---- kq[i][j] = (K_j . Q_i) * decay, j <= i, 1 on the diagonal (slm/chunked.c:430-443)
+        for (int idx = t; idx < kChunk * kChunk; idx += kThreads) {
+            const int i = idx >> 6, j = idx & (kChunk - 1);
+            if (j <= i && i < cn) {
+                const float *qi = qc + i * kLdk, *kj = kc + j * kLdk;
+                float acc = 0.0f;
+#pragma unroll 4
+                for (int d = 0; d < kHd; d += 4) acc = dot4(acc, lds4(kj + d), lds4(qi + d));
+                m1[i * kChunk + j] = __fmul_rn(acc, i == j ? 1.0f : expf_cr(__fsub_rn(gcs[i], gcs[j])));
+            }
+        }
+        __syncthreads();
+        // ---- Q * gexp in place (q_g_exp, slm/chunked.c:447-450)
+        for (int i = rg; i < cn; i += kRowGroups) qc[i * kLdk + e] = __fmul_rn(qc[i * kLdk + e], gex[i]);
+        __syncthreads();
+        // ---- attn_inter = (Q * gexp) S (slm/chunked.c:451-463), kept in registers
+        float inter[kRows];
+        rows_times_state(qc, st, e, rg, cn, inter);
+        __syncthreads();
+        // ---- K * beta * gexp over the Q rows, V * beta in place (slm/chunked.c:323-332, 409-414)
+        for (int i = rg; i < cn; i += kRowGroups) {
+            qc[i * kLdk + e] = __fmul_rn(__fmul_rn(kc[i * kLdk + e], bet[i]), gex[i]);
+            vb[i * kHd + e] = __fmul_rn(vb[i * kHd + e], bet[i]);
+        }
+        __syncthreads();
+        // ---- k_cumdecay = attn (K * beta * gexp) (slm/chunked.c:415-426)
+        float acc[kRows];
+        lower_times_tile(m2, qc, kLdk, e, rg, cn, acc);
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int i = rg + kRowGroups * r;
+            if (i < cn) qc[i * kLdk + e] = acc[r];
+        }
+        // ---- v_eff = attn (V * beta) (slm/chunked.c:391-408)
+        lower_times_tile(m2, vb, kHd, e, rg, cn, acc);
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int i = rg + kRowGroups * r;
+            if (i < cn) vb[i * kHd + e] = acc[r];
+        }
+        __syncthreads();
+        // ---- v_new = v_eff - k_cumdecay S (slm/chunked.c:464-484)
+        rows_times_state(qc, st, e, rg, cn, acc);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int i = rg + kRowGroups * r;
+            if (i < cn) vb[i * kHd + e] = __fsub_rn(vb[i * kHd + e], acc[r]);
+        }
+        // key_gdiff = K * exp(gcs_last - gcs) in place (slm/chunked.c:503-510)
+        for (int i = rg; i < cn; i += kRowGroups) kc[i * kLdk + e] = __fmul_rn(kc[i * kLdk + e], dif[i]);
+        __syncthreads();
+        // ---- out = attn_inter + kq v_new (slm/chunked.c:486-501)
+        lower_times_tile(m1, vb, kHd, e, rg, cn, acc);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int i = rg + kRowGroups * r;
+            if (i < cn) out[(row0 + i) * kdim + h * kHd + e] = __fadd_rn(inter[r], acc[r]);
+        }
+        // ---- S = S * exp(gcs_last) + key_gdiff^T v_new (slm/chunked.c:511-522);
+        // thread: column e, rows d = 32 rg .. 32 rg + 31 in two groups of 16
+        {
+            const float gle = gex[cn - 1];
+#pragma unroll 1
+            for (int g = 0; g < 2; ++g) {
+                const int d0 = 32 * rg + 16 * g;
+                float a[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) a[q] = 0.0f;
+                for (int u = 0; u < cn; ++u) {
+                    const float vn = vb[u * kHd + e];
+                    const float *kr = kc + u * kLdk + d0;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 kv = lds4(kr + 4 * q4);
+                        a[4 * q4 + 0] = __fadd_rn(a[4 * q4 + 0], __fmul_rn(kv.x, vn));
+                        a[4 * q4 + 1] = __fadd_rn(a[4 * q4 + 1], __fmul_rn(kv.y, vn));
+                        a[4 * q4 + 2] = __fadd_rn(a[4 * q4 + 2], __fmul_rn(kv.z, vn));
+                        a[4 * q4 + 3] = __fadd_rn(a[4 * q4 + 3], __fmul_rn(kv.w, vn));
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    float *p = st + (d0 + q) * kHd + e;
+                    *p = __fadd_rn(__fmul_rn(*p, gle), a[q]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (!waited && t == 0 && !mbar_wait(&st_bar, 0)) report_error(err_flag, kDevWaitTimeout);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (t == 0) {
+        bulk_copy_s2g(stg, st, kHd * kHd * 4);
+        bulk_commit_group();
+        bulk_wait_all();
+    }
+}
+
+int launch_status(cudaError_t e, const char *what) {
+    const cudaError_t last = cudaGetLastError();
+    if (e == cudaSuccess) e = last;
+    if (e == cudaSuccess) return QH_OK;
+    char msg[256];
+    snprintf(msg, sizeof(msg), "%s: %s", what, cudaGetErrorString(e));
+    set_last_error_message(msg);
+    return QH_ERR_CUDA;
+}
+
+int bad(const char *what) {
+    set_last_error_message(what);
+    return QH_ERR_INVALID;
+}
+
+}  // namespace
+}  // namespace qh
+
+extern "C" {
+
+int qh_gdn_chunk_prep(float *d_qkv, float *d_ring, const float *d_conv_w, float *d_b, float *d_a,
+                      const float *d_dt_bias, const float *d_ssm_a, int32_t n_seq, int32_t n_tok, int32_t heads,
+                      int32_t hd, int32_t kk, const int32_t *d_pos, void *stream) {
+    if (!d_qkv || !d_ring || !d_conv_w || !d_b || !d_a || !d_dt_bias || !d_ssm_a || !d_pos || n_seq <= 0 ||
+        n_tok <= 0 || static_cast<int64_t>(n_seq) * n_tok > 0x7fffffff || heads <= 0 || heads > 65535 ||
+        n_seq > 0x7fffffff)
+        return qh::bad("qh_gdn_chunk_prep: bad arguments");
+    if (hd != 128 || kk != 4) {
+        qh::set_last_error_message("qh_gdn_chunk_prep: head dim must be 128 and the conv kernel 4");
+        return QH_ERR_UNSUPPORTED;
+    }
+    const cudaError_t le = qh::launch_pdl(qh::gdn_chunk_prep_kernel<128, 4>, dim3(static_cast<unsigned>(n_seq), heads),
+                                          dim3(128), 0, static_cast<cudaStream_t>(stream), d_qkv, d_ring, d_conv_w,
+                                          d_b, d_a, d_dt_bias, d_ssm_a, heads, d_pos, n_tok);
+    return qh::launch_status(le, "qh_gdn_chunk_prep");
+}
+
+int qh_gdn_chunked(const float *d_qkv, const float *d_beta, const float *d_glog, float *d_state, int32_t n_seq,
+                   int32_t n_tok, int32_t heads, int32_t hd, float *d_out, void *stream) {
+    if (!d_qkv || !d_beta || !d_glog || !d_state || !d_out || n_seq <= 0 || n_tok <= 0 ||
+        static_cast<int64_t>(n_seq) * n_tok > 0x7fffffff || heads <= 0 || heads > 65535)
+        return qh::bad("qh_gdn_chunked: bad arguments");
+    if (hd != 128) {
+        qh::set_last_error_message("qh_gdn_chunked: head dim must be 128");
+        return QH_ERR_UNSUPPORTED;
+    }
+    if (reinterpret_cast<uintptr_t>(d_state) & 15) return qh::bad("qh_gdn_chunked: state not 16-byte aligned");
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaFuncSetAttribute(qh::gdn_chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qh::kSmemBytes);
+        attr_done[dev] = true;
+    }
+    int *err = qh::device_error_word();
+    if (!err) return qh::bad("qh_gdn_chunked: no device error word");
+    const cudaError_t le = qh::launch_pdl(qh::gdn_chunked_kernel, dim3(static_cast<unsigned>(n_seq), heads),
+                                          dim3(qh::kThreads), qh::kSmemBytes, static_cast<cudaStream_t>(stream),
+                                          d_qkv, d_beta, d_glog, d_state, heads, n_tok, d_out, err);
+    return qh::launch_status(le, "qh_gdn_chunked");
+}
+
+}  // extern "C"

@@ -91,6 +91,8 @@ struct qh_slm {
     int ntiled;
     // prompt chunks (qh_slm_prefill), allocated on first use
     int32_t pf_chunk, pf_chunk_max;
+    int32_t pf_mode;               // QH_PREFILL_STEPWISE or QH_PREFILL_CHUNKED
+    float *pf_o;                   // chunked mode: DeltaNet outputs [rows][gdn width]
     float *pf_h, *pf_h2, *pf_mix, *pf_qkv, *pf_z, *pf_bt, *pf_at, *pf_qraw, *pf_kb, *pf_vb, *pf_aq, *pf_agate,
         *pf_actx, *pf_fgate, *pf_fup;
     void *pf_xq_h, *pf_xq_gdn, *pf_xq_ffn;
@@ -816,6 +818,13 @@ static int ensure_prefill(qh_slm *m) {
     int64_t C = m->pf_chunk_max > 0 ? m->pf_chunk_max : PF_MAX_ROWS / B;
     if (C < 1) C = 1;
     if (C > c->max_pos) C = c->max_pos;
+    if (m->pf_mode == QH_PREFILL_CHUNKED) {
+        // launches start on the 64-token chunk grid counted from position 0
+        // (slm/qwen.c:777-780); a prompt shorter than max_pos fits one launch
+        // when max_pos < 64
+        C = C < 64 ? 64 : C / 64 * 64;
+        if (C > c->max_pos) C = c->max_pos;
+    }
     const int64_t M = B * C, H = c->hidden, F = c->ffn, hd = c->head_dim;
     const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
     const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
@@ -834,6 +843,7 @@ static int ensure_prefill(qh_slm *m) {
     CK(alloc_f(m, &m->pf_actx, M * qdim));
     CK(alloc_f(m, &m->pf_fgate, M * F));
     CK(alloc_f(m, &m->pf_fup, M * F));
+    if (m->pf_mode == QH_PREFILL_CHUNKED) CK(alloc_f(m, &m->pf_o, M * kdim));
     const int64_t max_in = H > qdim ? H : qdim;
     CK(dev_alloc(m, &m->pf_xq_h, (size_t)qh_q8kt_bytes(max_in, M), NULL));
     CK(dev_alloc(m, &m->pf_xq_gdn, (size_t)qh_q8kt_bytes(kdim, M), NULL));
@@ -918,9 +928,21 @@ static int forward_prefill(qh_slm *m, int32_t cn) {
             const int64_t gi = Ly->gdn_index;
             float *ring = m->ring + gi * B * c->conv_kernel * conv_dim;
             float *state = m->state + gi * B * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
-            CK(qh_gdn_prefill(m->pf_qkv, ring, Ly->conv_w, m->pf_bt, m->pf_at, Ly->dt_bias, Ly->ssm_a, state,
-                              m->pf_z, Ly->ssm_norm, B, cn, c->gdn_heads, c->gdn_head_dim, c->conv_kernel,
-                              c->norm_eps, m->pf_pos, m->pf_xq_gdn, T, s));
+            if (m->pf_mode == QH_PREFILL_CHUNKED) {
+                // slm_forward_ssm_batch (slm/qwen.c:627-806): conv, norms, beta, g_log;
+                // the chunk algebra; gated RMSNorm; then Q8_K for ssm_out
+                CK(qh_gdn_chunk_prep(m->pf_qkv, ring, Ly->conv_w, m->pf_bt, m->pf_at, Ly->dt_bias, Ly->ssm_a, B, cn,
+                                     c->gdn_heads, c->gdn_head_dim, c->conv_kernel, m->pf_pos, s));
+                CK(qh_gdn_chunked(m->pf_qkv, m->pf_bt, m->pf_at, state, B, cn, c->gdn_heads, c->gdn_head_dim,
+                                  m->pf_o, s));
+                CK(qh_gdn_gated_norm(m->pf_o, m->pf_z, Ly->ssm_norm, (int32_t)M, c->gdn_heads, c->gdn_head_dim,
+                                     c->norm_eps, m->pf_o, s));
+                CK(qh_quantize_q8kt(m->pf_o, kdim, M, m->pf_xq_gdn, s));
+            } else {
+                CK(qh_gdn_prefill(m->pf_qkv, ring, Ly->conv_w, m->pf_bt, m->pf_at, Ly->dt_bias, Ly->ssm_a, state,
+                                  m->pf_z, Ly->ssm_norm, B, cn, c->gdn_heads, c->gdn_head_dim, c->conv_kernel,
+                                  c->norm_eps, m->pf_pos, m->pf_xq_gdn, T, s));
+            }
         }
         CK(run_pf(m, &m->pf_out[l], M));
         pending = m->pf_mix;
@@ -938,6 +960,13 @@ int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq) {
     if (!m || max_tokens_per_seq < 0) return QH_ERR_INVALID;
     if (m->pf_chunk) return max_tokens_per_seq == 0 || max_tokens_per_seq == m->pf_chunk ? QH_OK : QH_ERR_INVALID;
     m->pf_chunk_max = max_tokens_per_seq;
+    return QH_OK;
+}
+
+int qh_slm_set_prefill_mode(qh_slm *m, int32_t mode) {
+    if (!m || (mode != QH_PREFILL_STEPWISE && mode != QH_PREFILL_CHUNKED)) return QH_ERR_INVALID;
+    if (m->pf_chunk) return mode == m->pf_mode ? QH_OK : QH_ERR_INVALID;
+    m->pf_mode = mode;
     return QH_OK;
 }
 

@@ -417,10 +417,14 @@ class Slm:
         p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
         check(lib().qh_slm_begin(self.handle, p.ctypes.data, p.shape[1]), "qh_slm_begin")
 
-    def prefill(self, prompt, chunk: int = 0):
+    def prefill(self, prompt, chunk: int = 0, mode: int = None):
+        """qh_slm_prefill; chunk and mode (PREFILL_STEPWISE / PREFILL_CHUNKED)
+        apply from the first call on."""
         p = np.ascontiguousarray(prompt, np.int32).reshape(self.n_seq, -1)
         if chunk:
             check(lib().qh_slm_set_prefill_chunk(self.handle, chunk), "qh_slm_set_prefill_chunk")
+        if mode is not None:
+            check(lib().qh_slm_set_prefill_mode(self.handle, mode), "qh_slm_set_prefill_mode")
         check(lib().qh_slm_prefill(self.handle, p.ctypes.data, p.shape[1]), "qh_slm_prefill")
 
     def advance(self, n_steps: int):

@@ -1,0 +1,56 @@
+# SPDX-License-Identifier: MIT
+"""CPU: pins the oracle's chunked Gated DeltaNet step (orc_chunked_step in
+oracle/qh_oracle.c) to the reference's own chunked_ssm_step_f32
+(slm/chunked.c:287-523, compiled from its sources into oracle/_ref), run in
+slm_forward_ssm_batch's 64-token chunk loop with the state carried
+(slm/qwen.c:777-806). Bit-exact, outputs and final state, with the host
+libm (ref) and with correctly rounded expf (ref_cr, the device's)."""
+import numpy as np
+import pytest
+
+from tests.chunked_cases import chunk_inputs
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("n", [1, 2, 17, 63, 64, 65, 130, 200])
+@pytest.mark.parametrize("which", ["ref", "ref_cr"])
+def test_oracle_chunked_matches_reference(n, which, oracle, request):
+    r = request.getfixturevalue(which)
+    q, k, v, g, b, s0 = chunk_inputs(n, 128, 1000 + n)
+    s_ref, s_orc = s0.copy(), s0.copy()
+    o_ref = r.chunked_prefill(q, k, v, g, b, s_ref)
+    o_orc = oracle.chunked_prefill(q, k, v, g, b, s_orc, cr=(which == "ref_cr"))
+    assert np.array_equal(bits(o_orc), bits(o_ref)), "chunk outputs differ from the reference"
+    assert np.array_equal(bits(s_orc), bits(s_ref)), "carried state differs from the reference"
+
+
+def test_oracle_chunked_small_head_and_zero_state(oracle, ref):
+    q, k, v, g, b, _ = chunk_inputs(70, 32, 7)
+    s_ref = np.zeros((32, 32), np.float32)
+    s_orc = s_ref.copy()
+    o_ref = ref.chunked_prefill(q, k, v, g, b, s_ref)
+    o_orc = oracle.chunked_prefill(q, k, v, g, b, s_orc, cr=False)
+    assert np.array_equal(bits(o_orc), bits(o_ref)) and np.array_equal(bits(s_orc), bits(s_ref))
+
+
+def test_chunked_close_to_recurrent_update(oracle):
+    """The chunked algebra is the delta rule: against a float64 token-by-token
+    recurrence S <- g S + k (beta (v - S^T k g))^T, out = S^T q, it agrees to
+    float rounding (the reference's chunked-test bar is 1e-5 relative)."""
+    n, hd = 130, 128
+    q, k, v, g, b, s0 = chunk_inputs(n, hd, 3)
+    s = s0.copy()
+    out = oracle.chunked_prefill(q, k, v, g, b, s, cr=True)
+    S = s0.astype(np.float64)
+    want = np.empty((n, hd))
+    for t in range(n):
+        S *= np.exp(np.float64(g[t]))
+        delta = b[t] * (v[t] - S.T @ k[t])
+        S += np.outer(k[t], delta)
+        want[t] = S.T @ q[t]
+    rel = np.abs(out - want).max() / np.abs(want).max()
+    assert rel < 1e-5, f"chunked vs recurrent relative difference {rel:.2e}"
+    assert np.abs(s - S).max() / np.abs(S).max() < 1e-5
