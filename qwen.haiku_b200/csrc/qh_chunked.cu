@@ -22,10 +22,11 @@
 // Every entry of every matrix is one thread's sequential sum, so the
 // arithmetic is the reference's; the work is spread by giving threads whole
 // entries (512 threads: a column e and every fourth row). The chunk algebra
-// has more multiply-adds per token than the recurrence, and with float
-// sums that must stay sequential it cannot move to the tensor cores, so on
-// this device it is about as fast as the per-token prefill -- it exists to
-// reproduce the reference's batched path.
+// has more multiply-adds per token than the recurrence, and with float sums
+// that must stay sequential it cannot move to the tensor cores; it still
+// beats the per-token prefill, whose per-token double-precision dependency
+// chains leave the SMs idle (64-token prompt at batch 1: 9.4 k against
+// 5.1 k tokens/s; 64 x 512 tokens: 96.6 k against 71.1 k).
 
 #include <cuda_runtime.h>
 #include <math.h>
