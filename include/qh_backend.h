@@ -205,6 +205,19 @@ int qh_matvec_plan_create(int type, const qh_matvec_job *h_jobs, int n_jobs, int
 #define QH_FUSE_QUANT 3
 int qh_matvec_plan_fuse_input(qh_matvec_plan plan, int mode, const float *d_a, const float *d_b, const float *d_w,
                               float eps, float *d_h_out);
+/* Output tail: after the plan's matvecs, the launch's last CTA to finish
+ * forms the next layer's Q8_K input (split layout, qh_q8k_bytes(k, n_tok)
+ * bytes at d_xq) from fp32 rows [n_tok][k] -- typically this plan's own
+ * outputs -- with the same modes and operations as qh_matvec_plan_fuse_input
+ * (QH_FUSE_RMSNORM: h_out = a + b, RMSNorm with w and eps, as qh_rmsnorm_q8k;
+ * QH_FUSE_SWIGLU: silu(a) * b, as qh_swiglu_q8k; QH_FUSE_QUANT: a, as
+ * qh_quantize_q8k; 0 removes the tail). It replaces the separate
+ * normalization / activation kernel between two projections of the
+ * reference's step (slm/qwen.c:939-957, slm/model.c:949 to the next
+ * layer's tensor_rms_norm), bit for bit. Allocates a 4-byte arrival counter
+ * on the first call; launches of one plan must not overlap. */
+int qh_matvec_plan_fuse_output(qh_matvec_plan plan, int mode, int64_t k, const float *d_a, const float *d_b,
+                               const float *d_w, float eps, float *d_h_out, void *d_xq);
 int qh_matvec_plan_run(qh_matvec_plan plan, void *stream);
 /* Rows per tile, pipeline stages, grid size and shared memory chosen. */
 int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, int *grid,

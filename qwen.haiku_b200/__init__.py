@@ -104,6 +104,7 @@ SIGNATURES = {
     "qh_gemm_pack_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
     "qh_gemm_expanded_bytes": (_I64, [_I, _I64, _I64]),
     "qh_matvec_plan_fuse_input": (_I, [_P, _I, _P, _P, _P, C.c_float, _P]),
+    "qh_matvec_plan_fuse_output": (_I, [_P, _I, _I64, _P, _P, _P, C.c_float, _P, _P]),
     "qh_gemm_expand_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
     "qh_q8kt_bytes": (_I64, [_I64, _I64]),
     "qh_quantize_q8kt": (_I, [_P, _I64, _I64, _P, _P]),

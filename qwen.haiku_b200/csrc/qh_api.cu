@@ -174,6 +174,7 @@ struct qh_matvec_plan_s {
     qh::GemvParams params;
     qh::GemvGeometry geom;
     qh::GemvJob *d_table;
+    unsigned *d_ticket;             // output tail's arrival counter (qh_matvec_plan_fuse_output)
 };
 
 extern "C" {
@@ -391,6 +392,16 @@ int qh_matvec_plan_fuse_input(qh_matvec_plan plan, int mode, const float *d_a, c
     if (e != cudaSuccess) return fail(QH_ERR_INVALID, "plan_fuse_input: cannot tile these rows (%s)", cudaGetErrorString(e));
     p.err_flag = plan->params.err_flag;
     p.table = plan->params.table;
+    // an output tail set earlier stays
+    p.tform = plan->params.tform;
+    p.tk = plan->params.tk;
+    p.teps = plan->params.teps;
+    p.ta = plan->params.ta;
+    p.tb = plan->params.tb;
+    p.tw = plan->params.tw;
+    p.th_out = plan->params.th_out;
+    p.txq = plan->params.txq;
+    p.ticket = plan->params.ticket;
     if (mode) {
         p.xa = d_a;
         p.xb = d_b;
@@ -404,6 +415,44 @@ int qh_matvec_plan_fuse_input(qh_matvec_plan plan, int mode, const float *d_a, c
     }
     plan->params = p;
     plan->geom = g;
+    return QH_OK;
+}
+
+int qh_matvec_plan_fuse_output(qh_matvec_plan plan, int mode, int64_t k, const float *d_a, const float *d_b,
+                               const float *d_w, float eps, float *d_h_out, void *d_xq) {
+    if (!plan) return fail(QH_ERR_INVALID, "plan_fuse_output: null plan");
+    if (mode < 0 || mode > QH_FUSE_QUANT) return fail(QH_ERR_INVALID, "plan_fuse_output: unknown mode %d", mode);
+    if (mode == 0) {
+        plan->params.tform = 0;
+        return QH_OK;
+    }
+    if (k <= 0 || k % QH_QK) return fail(QH_ERR_INVALID, "plan_fuse_output: k=%lld", (long long)k);
+    if (!d_a || !d_xq) return fail(QH_ERR_INVALID, "plan_fuse_output: null input or output");
+    if (!aligned16(d_xq)) return fail(QH_ERR_ALIGN, "plan_fuse_output: output not 16-byte aligned");
+    if (mode == QH_FUSE_SWIGLU && !d_b) return fail(QH_ERR_INVALID, "plan_fuse_output: SwiGLU needs gate and up");
+    if (mode == QH_FUSE_RMSNORM && (!d_w || (d_b && !d_h_out) || (d_h_out && (d_h_out == d_a || d_h_out == d_b))))
+        return fail(QH_ERR_INVALID, "plan_fuse_output: RMSNorm needs a weight, and h_out (not an input) with a residual");
+    if (mode == QH_FUSE_RMSNORM && k > 16 * QH_QK)
+        return fail(QH_ERR_UNSUPPORTED, "plan_fuse_output: RMSNorm rows longer than 4096");
+    if (!plan->d_ticket) {
+        cudaError_t e = cudaMalloc(&plan->d_ticket, sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemset(plan->d_ticket, 0, sizeof(unsigned));
+        if (e != cudaSuccess) {
+            if (plan->d_ticket) cudaFree(plan->d_ticket);
+            plan->d_ticket = nullptr;
+            return cuda_fail(e, "plan_fuse_output: ticket");
+        }
+    }
+    qh::GemvParams &p = plan->params;
+    p.tform = mode;
+    p.tk = static_cast<int32_t>(k);
+    p.teps = eps;
+    p.ta = d_a;
+    p.tb = mode == QH_FUSE_QUANT ? nullptr : d_b;
+    p.tw = mode == QH_FUSE_RMSNORM ? d_w : nullptr;
+    p.th_out = mode == QH_FUSE_RMSNORM ? d_h_out : nullptr;
+    p.txq = static_cast<uint8_t *>(d_xq);
+    p.ticket = plan->d_ticket;
     return QH_OK;
 }
 
@@ -426,6 +475,7 @@ int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, 
 int qh_matvec_plan_destroy(qh_matvec_plan plan) {
     if (!plan) return QH_OK;
     if (plan->d_table) cudaFree(plan->d_table);
+    if (plan->d_ticket) cudaFree(plan->d_ticket);
     delete plan;
     return QH_OK;
 }

@@ -524,6 +524,69 @@ __device__ __noinline__ void fuse_input(const GemvParams &p, uint8_t *xs, double
     }
 }
 
+// Output tail: every consumer thread fences its outputs, the CTA takes a
+// ticket, and the last CTA of the launch forms the next Q8_K input -- the
+// operations and order of fuse_input (and so of resnorm_q8k_kernel,
+// swiglu_q8k_kernel, quantize_q8k_kernel), reading the other CTAs' outputs
+// from L2 and writing the split layout to global memory. The ticket is left
+// at zero for the next launch.
+__device__ __noinline__ void gemv_tail(const GemvParams &p) {
+    __shared__ double tscr[kConsumerWarps];
+    __shared__ int t_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __threadfence();
+    consumers_sync();
+    if (tid == 0) t_last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
+    consumers_sync();
+    if (!t_last) return;
+    __threadfence();
+    pdl_wait();  // a CTA without tiles has not waited for the previous kernel yet
+    const int K = p.tk, nb = K / QH_QK, nt = p.n_tok;
+    const int64_t d_off = qhf_q8k_d_offset(K, nt), b_off = qhf_q8k_bsums_offset(K, nt);
+    const int dstride = static_cast<int>(qhf_q8k_d_stride(K));
+    for (int t = 0; t < nt; ++t) {
+        int8_t *qs = reinterpret_cast<int8_t *>(p.txq) + static_cast<int64_t>(t) * K;
+        float *dd = reinterpret_cast<float *>(p.txq + d_off) + t * dstride;
+        int16_t *bs = reinterpret_cast<int16_t *>(p.txq + b_off) + t * nb * 16;
+        const int64_t row = static_cast<int64_t>(t) * K;
+        float rscale = 0.0f;
+        if (p.tform == 1) {
+            double s = 0.0;
+#pragma unroll
+            for (int j = 0; j < kFuseMaxBlocks; ++j) {
+                if (j < nb) {
+                    const int64_t i = row + j * QH_QK + tid;
+                    float x = __ldcg(p.ta + i);
+                    if (p.tb) x = __fadd_rn(x, __ldcg(p.tb + i));
+                    if (p.th_out) p.th_out[i] = x;
+                    s += static_cast<double>(__fmul_rn(x, x));
+                }
+            }
+            const double ssq = consumers_sum_d(s, tscr);
+            rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(K)), p.teps)));
+        }
+        for (int b = warp; b < nb; b += kConsumerWarps) {
+            const int64_t e0 = row + b * QH_QK + 8 * lane;
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int64_t i = e0 + e;
+                if (p.tform == 1) {
+                    float x = __ldcg(p.ta + i);
+                    if (p.tb) x = __fadd_rn(x, __ldcg(p.tb + i));
+                    v[e] = __fmul_rn(__fmul_rn(x, rscale), p.tw[b * QH_QK + 8 * lane + e]);
+                } else if (p.tform == 2) {
+                    v[e] = __fmul_rn(silu_f(__ldcg(p.ta + i)), __ldcg(p.tb + i));
+                } else {
+                    v[e] = __ldcg(p.ta + i);
+                }
+            }
+            q8k_block_warp(v, qs + b * QH_QK, bs + b * 16, dd + b);
+        }
+    }
+    if (tid == 0) *p.ticket = 0u;
+}
+
 // ---------------------------------------------------------------------------
 // The kernel: producer lane + 8 consumer warps over a ring of stages.
 // ---------------------------------------------------------------------------
@@ -695,6 +758,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 }
             }
         }
+        if (p.tform) gemv_tail(p);
         return;
     }
     int group_base = 0;
@@ -722,6 +786,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         if (lane == 0) mbar_arrive(&empty[s]);
         if (*abort_flag) break;
     }
+    if (p.tform) gemv_tail(p);
 }
 
 // ---------------------------------------------------------------------------

@@ -61,6 +61,18 @@ struct GemvParams {
     const float *xa, *xb, *xw;
     float *xh_out;
     const GemvJob *table;  // device copy of all jobs when n_jobs > kGemvInlineJobs
+    // Output tail (tform != 0): after its matvecs the launch's last CTA
+    // (ticket counter) forms a Q8_K row set in the split layout at txq from
+    // fp32 rows of tk values, with the operations of xform's modes:
+    // 1 residual + RMSNorm (ta = h, tb = branch or null, tw = weight, th_out =
+    // h + b), 2 SwiGLU (ta = gate, tb = up), 3 plain quantization of ta.
+    int32_t tform;
+    int32_t tk;
+    float teps;
+    const float *ta, *tb, *tw;
+    float *th_out;
+    uint8_t *txq;
+    unsigned *ticket;      // zero between launches
     int *err_flag;         // device error word
     GemvJob jobs[kGemvInlineJobs];
 };

@@ -431,6 +431,12 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         const int64_t ofh[1] = {cfg->vocab};
         float *oh[1] = {m->logits};
         TRY(make_plan(m, &m->p_head, QH_TYPE_Q6_K, 1, wh, ofh, oh, m->xq_h, H));
+        // (Output tails, qh_matvec_plan_fuse_output, could form each next
+        // Q8_K input inside the projection before it; measured in the
+        // captured step at batch 1 they are slower -- 1.51 against 1.04 ms
+        // per step -- because one CTA then runs the norm serially after the
+        // grid's arrival counter, where the separate kernel spreads it over
+        // the row's blocks and overlaps its launch.)
         if (m->use_gemm) {
             int64_t need = 0;
             plan_set *all[4 * MAX_LAYERS + 1];

@@ -224,6 +224,16 @@ class MatvecPlan:
                                               eps, dptr(h_out) if h_out is not None else None),
               "qh_matvec_plan_fuse_input")
 
+    def fuse_output(self, mode: int, k: int, xq, a=None, b=None, w=None, eps: float = 0.0, h_out=None):
+        """qh_matvec_plan_fuse_output: the launch's last CTA forms the Q8_K rows
+        xq (split layout) from a/b (same modes as fuse_input; 0 = off)."""
+        self._tail = (xq, a, b, w, h_out)
+        check(lib().qh_matvec_plan_fuse_output(self.handle, mode, k, *(dptr(t) if t is not None else None
+                                                                       for t in (a, b, w)),
+                                               eps, dptr(h_out) if h_out is not None else None,
+                                               dptr(xq) if xq is not None else None),
+              "qh_matvec_plan_fuse_output")
+
     def info(self):
         r, s, g, m = C.c_int(), C.c_int(), C.c_int(), C.c_int()
         check(lib().qh_matvec_plan_info(self.handle, C.byref(r), C.byref(s), C.byref(g), C.byref(m)),

@@ -250,3 +250,62 @@ def test_fused_input_equals_separate_kernels(qh, cuda, gt, k, n_tok):
             assert torch.equal(h_got.view(torch.int32), h_ref.view(torch.int32)), "residual h + b"
         plan.close()
         plan_ref.close()
+
+
+@pytest.mark.parametrize("gt,no", [(Q4_K, 256), (Q4_K, 3072), (Q6_K, 1024)])
+@pytest.mark.parametrize("n_tok", [1, 3])
+def test_fused_output_tail_equals_separate_kernels(qh, cuda, gt, no, n_tok):
+    """qh_matvec_plan_fuse_output: the launch's last CTA forms the next Q8_K
+    rows from the plan's own outputs (residual + RMSNorm, SwiGLU of two jobs,
+    plain quantization): the bytes equal the separate kernel's after the plan,
+    the residual sum too; two launches in a row (the arrival counter is left
+    at zero)."""
+    import ctypes as C
+    torch = cuda
+    h = qh.host
+    L = qh.lib()
+    k = 1024
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    x = h.to_device(h.synth_normal(n_tok * k, 0xA1 + no).reshape(n_tok, k))
+    xq_in = h.quantize_q8k(x, k, n_tok)
+    ws = [h.to_device(h.synth_blocks(gt, no * (k // 256), 0xA2 + i)) for i in range(2)]
+    hbase = h.to_device(h.synth_normal(n_tok * no, 0xA3 + no).reshape(n_tok, no))
+    w = h.to_device(h.synth_normal(no, 0xA4, 1.0, 0.02))
+    nbytes = int(L.qh_q8k_bytes(no, n_tok))
+    for mode in (1, 2, 3):
+        outs = [torch.empty((n_tok, no), dtype=torch.float32, device="cuda") for _ in range(2)]
+        jobs = [(ws[i], xq_in, outs[i], k, no) for i in range(2 if mode == 2 else 1)]
+        plan = h.MatvecPlan(gt, jobs, n_tok)
+        xq_got = torch.full((nbytes,), 0x5A, dtype=torch.uint8, device="cuda")
+        h_got = torch.full_like(hbase, 7.0)
+        if mode == 1:
+            plan.fuse_output(1, no, xq_got, hbase, outs[0], w, 1e-6, h_got)
+        elif mode == 2:
+            plan.fuse_output(2, no, xq_got, outs[0], outs[1])
+        else:
+            plan.fuse_output(3, no, xq_got, outs[0])
+        for rep in range(2):
+            xq_got.fill_(0x5A)
+            plan.run()
+            torch.cuda.synchronize()
+            xq_ref = torch.full((nbytes,), 0x5A, dtype=torch.uint8, device="cuda")
+            h_ref = torch.empty_like(hbase)
+            if mode == 1:
+                qh.check(L.qh_rmsnorm_q8k(h.dptr(hbase), h.dptr(outs[0]), h.dptr(h_ref), h.dptr(w), no, n_tok, 1e-6,
+                                          h.dptr(xq_ref), 0, s), "rmsnorm_q8k")
+            elif mode == 2:
+                qh.check(L.qh_swiglu_q8k(h.dptr(outs[0]), h.dptr(outs[1]), no, n_tok, h.dptr(xq_ref), 0, s),
+                         "swiglu_q8k")
+            else:
+                qh.check(L.qh_quantize_q8k(h.dptr(outs[0]), no, n_tok, h.dptr(xq_ref), s), "quantize_q8k")
+            torch.cuda.synchronize()
+            # compare the planes the quantizers define (the scale rows' padding aside)
+            qs_ref, d_ref, bs_ref = h.unpack_q8k(xq_ref.cpu().numpy(), no, n_tok)
+            qs_got, d_got, bs_got = h.unpack_q8k(xq_got.cpu().numpy(), no, n_tok)
+            assert np.array_equal(qs_got, qs_ref), f"mode {mode} launch {rep}: quants"
+            assert np.array_equal(d_got.view(np.uint32), d_ref.view(np.uint32)), f"mode {mode} launch {rep}: scales"
+            assert np.array_equal(bs_got, bs_ref), f"mode {mode} launch {rep}: block sums"
+            if mode == 1:
+                assert torch.equal(h_got.view(torch.int32), h_ref.view(torch.int32)), "residual h + b"
+        assert L.qh_check_device_error(None) == 0
+        plan.close()
