@@ -159,6 +159,18 @@ __global__ void __launch_bounds__(HD) gdn_chunk_prep_kernel(float *__restrict__ 
 
 __device__ __forceinline__ float4 lds4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 
+// Entry L of a row-major lower triangle: (i, j) with L = i(i+1)/2 + j, j <= i
+// (strict = false), or L = i(i-1)/2 + j, j < i (strict = true).
+__device__ __forceinline__ void tri_entry(int L, bool strict, int &i, int &j) {
+    // row r of the non-strict triangle (float estimate, then exact), j within it;
+    // the strict triangle is the same walk one row down
+    int r = static_cast<int>((__fsqrt_rn(8.0f * static_cast<float>(L) + 1.0f) - 1.0f) * 0.5f);
+    while (r * (r + 1) / 2 > L) --r;
+    while ((r + 1) * (r + 2) / 2 <= L) ++r;
+    j = L - r * (r + 1) / 2;
+    i = strict ? r + 1 : r;
+}
+
 // s += a.x*b.x; s += a.y*b.y; ... in that order, each product and sum rounded
 __device__ __forceinline__ float dot4(float s, const float4 &a, const float4 &b) {
     s = __fadd_rn(s, __fmul_rn(a.x, b.x));
@@ -194,7 +206,15 @@ __device__ __forceinline__ void lower_times_tile(const float *__restrict__ M, co
         float s = 0.0f;
         if (i < cn) {
             const float *mi = M + i * kChunk;
-            for (int j = 0; j <= i; ++j) s = __fadd_rn(s, __fmul_rn(mi[j], B[j * ldb + e]));
+            int j = 0;
+            for (; j + 3 <= i; j += 4) {
+                const float4 m4 = lds4(mi + j);
+                s = __fadd_rn(s, __fmul_rn(m4.x, B[j * ldb + e]));
+                s = __fadd_rn(s, __fmul_rn(m4.y, B[(j + 1) * ldb + e]));
+                s = __fadd_rn(s, __fmul_rn(m4.z, B[(j + 2) * ldb + e]));
+                s = __fadd_rn(s, __fmul_rn(m4.w, B[(j + 3) * ldb + e]));
+            }
+            for (; j <= i; ++j) s = __fadd_rn(s, __fmul_rn(mi[j], B[j * ldb + e]));
         }
         acc[r] = s;
     }
@@ -255,9 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             dif[t] = expf_cr(__fsub_rn(gcs[cn - 1], gcs[t]));
         }
         // ---- kk[i][j] = (K_j . (K_i * beta_i)) * exp(gcs_i - gcs_j), j < i (slm/chunked.c:340-358)
-        for (int idx = t; idx < kChunk * kChunk; idx += kThreads) {
-            const int i = idx >> 6, j = idx & (kChunk - 1);
-            if (j < i && i < cn) {
+        for (int L = t; L < cn * (cn - 1) / 2; L += kThreads) {
+            int i, j;
+            tri_entry(L, true, i, j);
+            {
                 const float *ki = kc + i * kLdk, *kj = kc + j * kLdk;
                 const float bi = bet[i];
                 float acc = 0.0f;
@@ -305,9 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncthreads();
         // ---- kq[i][j] = (K_j . Q_i) * decay, j <= i, 1 on the diagonal (slm/chunked.c:430-443)
-        for (int idx = t; idx < kChunk * kChunk; idx += kThreads) {
-            const int i = idx >> 6, j = idx & (kChunk - 1);
-            if (j <= i && i < cn) {
+        for (int L = t; L < cn * (cn + 1) / 2; L += kThreads) {
+            int i, j;
+            tri_entry(L, false, i, j);
+            {
                 const float *qi = qc + i * kLdk, *kj = kc + j * kLdk;
                 float acc = 0.0f;
 #pragma unroll 4

@@ -225,6 +225,9 @@ __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job
     const uint32_t sh = 16u * static_cast<uint32_t>(j0);
     Sink<NT> acc;
     acc.init(terms, job.nb);
+    // unrolled: the loads and integer work of neighbouring blocks overlap
+    // (the row sum still adds the blocks' terms in order)
+#pragma unroll 4
     for (int b = b_first; b < job.nb; b += b_step) {
         const uint8_t *blk = row + b * QH_Q4K_BYTES;
         const uint4 h = lds128(blk);
