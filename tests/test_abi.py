@@ -111,3 +111,18 @@ def test_synth_quantizer_roundtrip(qh, oracle, gt):
         deq = np.stack([oracle.dequant_block(gt, blocks[i * bb:(i + 1) * bb]) for i in range(4)])
     err = np.abs(deq - w).max() / np.abs(w).max()
     assert err < {12: 0.12, 13: 0.06, 14: 0.04, 8: 0.01}[gt], err
+
+
+def test_chunked_prefill_entry_points_reject_bad_arguments_on_host(qh):
+    """The chunked DeltaNet launchers and the prefill-mode switch check their
+    arguments before any device work (status codes, no abort)."""
+    L = qh.lib()
+    INVALID, UNSUPPORTED = -1, -2
+    fake = C.c_void_p(0x1000)  # never dereferenced: the checks fail first
+    assert L.qh_gdn_chunked(None, None, None, None, 1, 1, 1, 128, None, None) == INVALID
+    assert L.qh_gdn_chunked(fake, fake, fake, fake, 1, 0, 1, 128, fake, None) == INVALID  # no tokens
+    assert L.qh_gdn_chunked(fake, fake, fake, fake, 1, 1, 1, 64, fake, None) == UNSUPPORTED  # head dim
+    assert L.qh_gdn_chunk_prep(None, None, None, None, None, None, None, 1, 1, 1, 128, 4, None, None) == INVALID
+    assert L.qh_gdn_chunk_prep(fake, fake, fake, fake, fake, fake, fake, 1, 1, 1, 128, 3, fake, None) == UNSUPPORTED
+    assert L.qh_slm_set_prefill_mode(None, qh.PREFILL_CHUNKED) == INVALID
+    assert L.qh_matvec_plan_fuse_output(None, 1, 1024, None, None, None, 0.0, None, None) == INVALID

@@ -54,3 +54,18 @@ def test_chunked_close_to_recurrent_update(oracle):
     rel = np.abs(out - want).max() / np.abs(want).max()
     assert rel < 1e-5, f"chunked vs recurrent relative difference {rel:.2e}"
     assert np.abs(s - S).max() / np.abs(S).max() < 1e-5
+
+
+@pytest.mark.parametrize("n", [0, 65])
+def test_chunk_step_rejects_sizes_outside_one_chunk(n, oracle, ref):
+    """Both the reference wrapper and the oracle take 1..64 tokens per call
+    (CHUNK_SIZE, slm/chunked.c:116); larger prompts go through the chunk loop."""
+    import ctypes as C
+    hd = 128
+    a = np.zeros((max(n, 1), hd), np.float32)
+    v = np.zeros(max(n, 1), np.float32)
+    s = np.zeros((hd, hd), np.float32)
+    o = np.zeros((max(n, 1), hd), np.float32)
+    P = lambda x: C.c_void_p(x.ctypes.data)
+    assert oracle.L.orc_chunked_step(n, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o), 1) == -1
+    assert ref.L.ref_chunked_step(n, hd, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o)) == -1
