@@ -5,6 +5,8 @@ oracle/qh_oracle.c) to the reference's own chunked_ssm_step_f32
 slm_forward_ssm_batch's 64-token chunk loop with the state carried
 (slm/qwen.c:777-806). Bit-exact, outputs and final state, with the host
 libm (ref) and with correctly rounded expf (ref_cr, the device's)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -69,3 +71,22 @@ def test_chunk_step_rejects_sizes_outside_one_chunk(n, oracle, ref):
     P = lambda x: C.c_void_p(x.ctypes.data)
     assert oracle.L.orc_chunked_step(n, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o), 1) == -1
     assert ref.L.ref_chunked_step(n, hd, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o)) == -1
+
+
+GOLDEN_CHUNKED = os.path.join(os.path.dirname(__file__), "golden", "chunked", "chunked.npz")
+
+
+@pytest.mark.parametrize("name", ["c70_hd64", "c9_hd128"])
+@pytest.mark.parametrize("tag", ["libm", "cr"])
+def test_oracle_chunked_matches_golden(name, tag, oracle):
+    """Against fixtures the reference's own chunk step wrote
+    (tests/golden/chunked/make_chunked_golden.py): runs without the
+    reference library, here and on the GPU box."""
+    import hashlib
+    g = np.load(GOLDEN_CHUNKED)
+    q, k, v, gl, b = (g[f"{name}_{x}"] for x in ("q", "k", "v", "g", "beta"))
+    hd = q.shape[1]
+    st = np.zeros((hd, hd), np.float32)
+    out = oracle.chunked_prefill(q, k, v, gl, b, st, cr=(tag == "cr"))
+    assert np.array_equal(bits(out), bits(g[f"{name}_out_{tag}"])), "outputs differ from the reference's"
+    assert hashlib.sha256(st.tobytes()).hexdigest() == str(g[f"{name}_state_sha_{tag}"]), "final state differs"
