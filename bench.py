@@ -498,7 +498,7 @@ def cpu_decode_baseline(qh, n_steps: int = 4):
     run(rm, 2)
     one = n_steps / (time.perf_counter() - t0)
     rm.close()
-    cores = len(os.sched_getaffinity(0))
+    cores = min(len(os.sched_getaffinity(0)), 64)  # bounded host memory: ~85 MB of caches per context
     models = [RefModel(ref, cfg, tensors) for _ in range(cores)]
     for i, m in enumerate(models):
         m.step(1 + i, 0)
