@@ -126,3 +126,10 @@ def test_chunked_prefill_entry_points_reject_bad_arguments_on_host(qh):
     assert L.qh_gdn_chunk_prep(fake, fake, fake, fake, fake, fake, fake, 1, 1, 1, 128, 3, fake, None) == UNSUPPORTED
     assert L.qh_slm_set_prefill_mode(None, qh.PREFILL_CHUNKED) == INVALID
     assert L.qh_matvec_plan_fuse_output(None, 1, 1024, None, None, None, 0.0, None, None) == INVALID
+
+
+def test_bad_device_id_is_a_status(qh):
+    """A device id the machine does not have is reported, not aborted on."""
+    L = qh.lib()
+    assert L.qh_set_device(4096) != 0
+    assert len(L.qh_last_error()) > 0

@@ -67,3 +67,50 @@ def test_reference_arm_only_rank0_works(monkeypatch):
     class Args:
         gpus, steps, warmup = 2, 1, 3
     assert bench.run_reference_arm(Args()) == 0
+
+
+def _leaver(rank, world, port, q):
+    """Rank 1 leaves between steps (after one token gather) without taking
+    part in the next; rank 0's next gather must end with an error within the
+    process group's short timeout instead of waiting for good."""
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import time
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    import bench
+    B = 4
+    out = torch.empty(world * B, dtype=torch.int32)
+    bench.gather_tokens(dist, torch.full((B,), rank, dtype=torch.int32), out)
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # the message is out before the process ends
+        os._exit(0)  # leaves between steps: nothing of it is in flight
+    t0 = time.monotonic()
+    try:
+        bench.gather_tokens(dist, torch.zeros(B, dtype=torch.int32), out)
+        q.put((rank, "no error"))
+    except Exception as e:
+        q.put((rank, f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_leaving_is_detected_by_the_next_collective():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world, port = 2, _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == "left"
+    assert results[0].startswith("error after"), results[0]
+    import re
+    assert float(re.match(r"error after ([0-9.]+)s", results[0]).group(1)) < 30.0, results[0]
