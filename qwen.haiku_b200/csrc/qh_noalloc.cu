@@ -20,10 +20,12 @@
 //   * All calls share it and it keeps the last call's contents, so two calls
 //     whose work overlaps on the GPU (different streams, or different host
 //     threads on one device) race on it. Serialize them on one stream.
-//   * The quantized rows are rewritten completely by every call; the only
-//     part that must start at zero -- the kernel error word in the first
-//     256 bytes -- is cleared on the caller's stream at the start of each
-//     call.
+//   * The quantized rows are rewritten completely by every call. The only
+//     part that must start at zero is the kernel error word in the first
+//     256 bytes: it is zero when the library loads, a kernel whose bounded
+//     wait runs out sets it (first error wins), and qh_check_device_error
+//     reads and clears it together with the library's other error word, so
+//     a timeout in this path reaches the caller like one anywhere else.
 //   * Host code cannot use the array's name as a device address, so the
 //     first call on each device (with that device current) looks the
 //     address up with cudaGetSymbolAddress and caches it. Make that first
@@ -111,32 +113,16 @@ extern "C" int qh_matmul_q4k_f32_noalloc(const void *d_w, int64_t out_f, int64_t
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int *err_word = static_cast<int *>(base);
     uint8_t *xq = static_cast<uint8_t *>(base) + kNoallocControlBytes;
-    cudaError_t e = cudaMemsetAsync(err_word, 0, sizeof(int), s);
-    if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "clear error word: %s", cudaGetErrorString(e));
-    e = qh::quantize_q8k_launch(d_x, k, n_tok, xq, s);
+    cudaError_t e = qh::quantize_q8k_launch(d_x, k, n_tok, xq, s);
     if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "quantize launch: %s", cudaGetErrorString(e));
-    const int nb = static_cast<int>(k / QH_QK);
-    for (int64_t t0 = 0; t0 < n_tok; t0 += 8) {
-        const int nt = static_cast<int>(n_tok - t0 < 8 ? n_tok - t0 : 8);
-        qh::GemvJob job{};
-        job.w = static_cast<const uint8_t *>(d_w);
-        job.k = static_cast<int32_t>(k);
-        job.nb = nb;
-        job.row_bytes = nb * QH_Q4K_BYTES;
-        job.n_rows = static_cast<int32_t>(out_f);
-        job.xqs = reinterpret_cast<const int8_t *>(xq) + t0 * k;
-        job.d_stride = static_cast<int32_t>(qhf_q8k_d_stride(k));
-        job.xd = xq + qhf_q8k_d_offset(k, n_tok) + t0 * job.d_stride * 4;
-        job.xbs = reinterpret_cast<const int16_t *>(xq + qhf_q8k_bsums_offset(k, n_tok)) + t0 * nb * 16;
-        job.out = d_out + t0 * out_f;
-        qh::GemvParams p{};
-        qh::GemvGeometry g{};
-        e = qh::gemv_plan(QH_GGUF_Q4_K, &job, 1, nt, sms, &p, &g);
-        if (e != cudaSuccess) return noalloc_fail(QH_ERR_INVALID, "cannot tile rows of k=%lld", (long long)k);
-        p.err_flag = err_word;
-        p.table = nullptr;
-        e = qh::gemv_launch(QH_GGUF_Q4_K, p, g, s);
-        if (e != cudaSuccess) return noalloc_fail(QH_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
-    }
-    return QH_OK;
+    // the same launches (and token chunking) as qh_matmul_q4k_f32
+    return qh::matmul_preq_launch(QH_GGUF_Q4_K, d_w, k, out_f, xq, n_tok, d_out, s, sms, err_word);
 }
+
+namespace qh {
+int *noalloc_error_word(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mu);
+    return static_cast<int *>(g_scratch_addr[dev]);
+}
+}  // namespace qh
