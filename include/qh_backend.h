@@ -134,6 +134,13 @@ int qh_matmul_q8_0_f32(const void *d_w, int64_t out_f, int64_t k, const float *d
                        int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes,
                        void *stream);
 
+/* tensor_matmul_f32 (slm/tensor.c:517), the F32 case of matmul_dispatch
+ * (slm/model.c:227): out[t][j] = sum_i w[j][i] * x[t][i] with one float
+ * multiply and one float add per i in index order, as the reference's loop.
+ * Weights fp32 [out_f][k] (GGUF shape (k, out_f)); no workspace. */
+int qh_matmul_f32(const float *d_w, int64_t out_f, int64_t k, const float *d_x, int64_t n_tok, float *d_out,
+                  void *stream);
+
 /* No counterpart in the reference (its CPU matmuls take their scratch from
  * the context arena). Same computation and results as qh_matmul_q4k_f32,
  * for callers that are not allowed to allocate device memory -- e.g. a host
@@ -151,7 +158,10 @@ int qh_matmul_q4k_f32_noalloc(const void *d_w, int64_t out_f, int64_t k, const f
                               int64_t n_tok, float *d_out, void *stream);
 
 /* matmul_dispatch (slm/model.c:220): dispatch on the GGUF weight type with
- * the GGUF shape order (k = shape[0], out_f = shape[1]). */
+ * the GGUF shape order (k = shape[0], out_f = shape[1]): F32, Q8_0, Q4_K,
+ * Q5_K, Q6_K. F32 needs no workspace (qh_matmul_workspace_bytes returns 0);
+ * any other type returns QH_ERR_UNSUPPORTED where the reference aborts
+ * (slm/model.c:259-261). */
 int qh_matmul(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x,
               int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes, void *stream);
 

@@ -27,6 +27,11 @@ extern "C" {
 int qh_embed_q6k(const void *d_table, int64_t hidden, const int32_t *d_tokens, int32_t B, float *d_h,
                  void *stream);
 
+/* Token embedding from an F32 table of shape (hidden, vocab): h[b] = row
+ * tokens[b] (tensor_get_rows on the fp32 view, slm/qwen.c:885-889). */
+int qh_embed_f32(const float *d_table, int64_t hidden, const int32_t *d_tokens, int32_t B, float *d_h,
+                 void *stream);
+
 /* RMSNorm over rows of `dim` (tensor_rms_norm, slm/tensor.c:348-369):
  * y = x * (1 / sqrtf(float(sum(x*x) / dim) + eps)) * w, the sum of squares
  * accumulated in double. */
@@ -225,6 +230,14 @@ typedef struct qh_sample_ctl {
 int qh_sample_feed(float *d_logits, int32_t B, int64_t vocab, const qh_sample_ctl *d_sctl, int32_t *d_hist,
                    int32_t hist_stride, int32_t *d_hist_n, uint64_t *d_rng, int32_t *d_next, int32_t stride,
                    int32_t *d_ctl, int32_t *d_tokens, int32_t *d_picks, unsigned *d_ticket, void *stream);
+
+/* expf (fn 0) or logf (fn 1) of the floats whose bit patterns are
+ * first, first + 1, ..., first + n - 1 (wrapping at 2^32), as the device
+ * kernels evaluate them (the host C library's values, bit for bit: the
+ * reference calls expf/logf at slm/qwen.c:464-470, slm/model.c:943,
+ * slm/tensor.c:315/491/1086, simd/simd.c:264-277, slm/sampler.c:105). For
+ * checking those functions against the host library. */
+int qh_libm_eval(int fn, uint32_t first, int64_t n, float *d_out, void *stream);
 
 #ifdef __cplusplus
 }

@@ -101,7 +101,17 @@ class Oracle:
         L.orc_sample_with.restype = C.c_int32
         L.orc_chunked_step.argtypes = [_I, _I, _P, _P, _P, _P, _P, _P, _P, _I]
         L.orc_chunked_step.restype = _I
+        L.orc_libm_mismatches.argtypes = [_I, C.c_uint32, _I64, _P, C.POINTER(C.c_uint32)]
+        L.orc_libm_mismatches.restype = _I64
         self.L = L
+
+    def libm_mismatches(self, fn: int, first: int, vals: np.ndarray):
+        """(count, first differing bit pattern or None) of vals[j] against the
+        host expf (fn 0) / logf (fn 1) at bit pattern first + j."""
+        vals = np.ascontiguousarray(vals, np.float32)
+        bad = C.c_uint32(0)
+        n = self.L.orc_libm_mismatches(fn, first, vals.size, vals.ctypes.data, C.byref(bad))
+        return int(n), (int(bad.value) if n else None)
 
     def chunked_prefill(self, q, k, v, g_log, beta, state, cr: bool = True):
         """slm_forward_ssm_batch's chunk loop (slm/qwen.c:777-806) for one head:

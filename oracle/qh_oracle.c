@@ -27,8 +27,10 @@
 // not contract a*b-c*d into an FMA; neither may this file).
 
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <string.h>
+#include <unistd.h>
 
 #define QK 256
 
@@ -322,13 +324,23 @@ void orc_dequant_block(int type, const uint8_t *blk, float *y) {
 // Matmul wrappers: tensor_matmul_{q4k,q5k,q8_0,q6k}_f32, slm/tensor.c:827-853,
 // 898-919, 952-981, 1012-1033. For each of n tokens (x is [n][k] fp32):
 // quantize the row, then out[t*out_f + j] = row_dot(weight row j).
-// type follows the GGUF enum (slm/gguf.c:52-59): 8 Q8_0, 12 Q4_K, 13 Q5_K,
-// 14 Q6_K. Scratch comes from the caller (q8 buffers sized for k).
+// type follows the GGUF enum (slm/gguf.c:52-59): 0 F32 (tensor_matmul_f32,
+// slm/tensor.c:517), 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K. Scratch comes from the caller (q8 buffers sized for k).
 // Returns 0, or -1 for an unsupported type / k.
 // ---------------------------------------------------------------------------
 int orc_matmul(int type, const uint8_t *w, int64_t out_f, int64_t k,
                const float *x, int64_t n, float *out,
                int8_t *scratch_qs, float *scratch_d, int16_t *scratch_bs) {
+    if (type == 0) {  // F32: tensor_matmul_f32, slm/tensor.c:517-535
+        const float *wf = (const float *)w;
+        for (int64_t t = 0; t < n; t++)
+            for (int64_t j = 0; j < out_f; j++) {
+                float acc = 0.0f;
+                for (int64_t i = 0; i < k; i++) acc += wf[j * k + i] * x[t * k + i];
+                out[t * out_f + j] = acc;
+            }
+        return 0;
+    }
     if (type == 8) {
         if (k % 32) return -1;
         uint16_t *dbits = (uint16_t *)scratch_d;
@@ -579,4 +591,65 @@ int orc_chunked_step(int n, int hd, const float *q, const float *k, const float 
     for (int d = 0; d < hd; d++)
         for (int e = 0; e < hd; e++) state[d * hd + e] = state[d * hd + e] * gle + kgd[d][e];
     return 0;
+}
+
+// ---- host C library expf / logf --------------------------------------------
+// The reference evaluates expf/logf with the host C library (slm/qwen.c:464-470,
+// slm/model.c:943, slm/tensor.c:315/491/1086, simd/simd.c:264-277,
+// slm/sampler.c:105). Counts how many of vals[j] (a device evaluation of
+// expf (fn 0) or logf (fn 1) at the float with bit pattern first + j) differ
+// from the host's value; NaN results compare equal to any NaN. *first_bad
+// gets the first differing bit pattern (unchanged if none).
+static int orc_same_f32(float a, float b) {
+    uint32_t ua, ub;
+    memcpy(&ua, &a, 4);
+    memcpy(&ub, &b, 4);
+    return ua == ub || (a != a && b != b);
+}
+
+typedef struct {
+    int fn;
+    uint32_t first;
+    int64_t j0, j1;
+    const float *vals;
+    int64_t mis, bad_j;
+} orc_libm_part;
+
+static void *orc_libm_worker(void *arg) {
+    orc_libm_part *p = (orc_libm_part *)arg;
+    p->mis = 0;
+    p->bad_j = -1;
+    for (int64_t j = p->j0; j < p->j1; j++) {
+        uint32_t u = p->first + (uint32_t)j;
+        float x;
+        memcpy(&x, &u, 4);
+        float want = p->fn == 0 ? expf(x) : logf(x);
+        if (!orc_same_f32(want, p->vals[j])) {
+            if (p->bad_j < 0) p->bad_j = j;
+            p->mis++;
+        }
+    }
+    return NULL;
+}
+
+int64_t orc_libm_mismatches(int fn, uint32_t first, int64_t n, const float *vals, uint32_t *first_bad) {
+    enum { kMaxThreads = 64 };
+    long nc = sysconf(_SC_NPROCESSORS_ONLN);
+    int nt = nc < 1 ? 1 : nc > kMaxThreads ? kMaxThreads : (int)nc;
+    if (n < 1 << 20) nt = 1;
+    orc_libm_part parts[kMaxThreads];
+    pthread_t th[kMaxThreads];
+    for (int t = 0; t < nt; t++) {
+        parts[t] = (orc_libm_part){fn, first, n * t / nt, n * (t + 1) / nt, vals, 0, -1};
+        if (t > 0 && pthread_create(&th[t], NULL, orc_libm_worker, &parts[t]) != 0) orc_libm_worker(&parts[t]), th[t] = 0;
+    }
+    orc_libm_worker(&parts[0]);
+    int64_t mis = 0, bad_j = -1;
+    for (int t = 0; t < nt; t++) {
+        if (t > 0 && th[t]) pthread_join(th[t], NULL);
+        mis += parts[t].mis;
+        if (bad_j < 0 && parts[t].bad_j >= 0) bad_j = parts[t].bad_j;
+    }
+    if (mis && first_bad) *first_bad = first + (uint32_t)bad_j;
+    return mis;
 }

@@ -94,6 +94,7 @@ SIGNATURES = {
     "qh_matmul_q6k_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_matmul_q8_0_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_matmul_q4k_f32_noalloc": (_I, [_P, _I64, _I64, _P, _I64, _P, _P]),
+    "qh_matmul_f32": (_I, [_P, _I64, _I64, _P, _I64, _P, _P]),
     "qh_matmul": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qh_matmul_preq": (_I, [_I, _P, _I64, _I64, _P, _I64, _P, _P]),
     "qh_matvec_plan_create": (_I, [_I, C.POINTER(MatvecJob), _I, _I64, C.POINTER(C.c_void_p)]),
@@ -157,7 +158,9 @@ SIGNATURES.update({
 
 _F32P = C.c_void_p
 SIGNATURES.update({  # include/qh_kernels.h
+    "qh_libm_eval": (_I, [_I, C.c_uint32, _I64, _P, _P]),
     "qh_embed_q6k": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
+    "qh_embed_f32": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
     "qh_rmsnorm": (_I, [_P, _P, _I64, _I64, C.c_float, _P, _P]),
     "qh_add": (_I, [_P, _P, _I64, _P]),
     "qh_swiglu": (_I, [_P, _P, _P, _I64, _P]),

@@ -115,30 +115,24 @@ int run_preq(int type, const void *d_w, int64_t k, int64_t out_f, const void *d_
     int *err;
     int rc = device_state(&sms, &err);
     if (rc) return rc;
-    int chunk = 8;  // tokens per launch; halved while a stage cannot hold them
-    for (int64_t t0 = 0; t0 < n_tok; t0 += chunk) {
-        qh::GemvParams p{};
-        qh::GemvGeometry g{};
-        cudaError_t e;
-        for (;;) {
-            const int nt = static_cast<int>(n_tok - t0 < chunk ? n_tok - t0 : chunk);
-            qh::GemvJob job = make_job(type, d_w, k, out_f, d_xq, n_tok, t0, d_out);
-            e = qh::gemv_plan(type, &job, 1, nt, sms, &p, &g);
-            if (e == cudaSuccess || chunk == 1) break;
-            chunk >>= 1;
-        }
-        if (e != cudaSuccess) return fail(QH_ERR_INVALID, "matmul: cannot tile rows of %lld bytes (%s)",
-                                          (long long)qhf_row_bytes(type, k), cudaGetErrorString(e));
-        p.err_flag = err;
-        p.table = nullptr;
-        e = qh::gemv_launch(type, p, g, s);
-        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
-    }
+    return qh::matmul_preq_launch(type, d_w, k, out_f, d_xq, n_tok, d_out, s, sms, err);
+}
+
+int matmul_f32_impl(const float *d_w, int64_t k, int64_t out_f, const float *d_x, int64_t n_tok, float *d_out,
+                    void *stream) {
+    if (k <= 0 || out_f <= 0 || out_f > (1ll << 30) || n_tok <= 0 || n_tok > 65535 || k > (1ll << 28))
+        return fail(QH_ERR_INVALID, "matmul f32: bad shape k=%lld out_f=%lld n_tok=%lld", (long long)k,
+                    (long long)out_f, (long long)n_tok);
+    if (!d_w || !d_x || !d_out) return fail(QH_ERR_INVALID, "matmul f32: null pointer");
+    cudaError_t e = qh::matmul_f32_launch(d_w, k, out_f, d_x, n_tok, d_out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "matmul f32 launch");
     return QH_OK;
 }
 
 int matmul_impl(int type, const void *d_w, int64_t k, int64_t out_f, const float *d_x,
                 int64_t n_tok, float *d_out, void *d_work, int64_t work_bytes, void *stream) {
+    if (type == QH_GGUF_F32)  // no quantization, no workspace
+        return matmul_f32_impl(static_cast<const float *>(d_w), k, out_f, d_x, n_tok, d_out, stream);
     int rc = check_shape(type, k, out_f, n_tok);
     if (rc) return rc;
     if (!d_w || !d_x || !d_out) return fail(QH_ERR_INVALID, "matmul: null pointer");
@@ -163,6 +157,34 @@ int *device_error_word() {
     int *w = nullptr;
     device_state(nullptr, &w);
     return w;
+}
+
+int matmul_preq_launch(int type, const void *d_w, int64_t k, int64_t out_f, const void *d_xq, int64_t n_tok,
+                       float *d_out, cudaStream_t s, int sm_count, int *err_word) {
+    if (type == QH_GGUF_Q8_0 && n_tok > 8) {  // one launch over all tokens (same lane arithmetic)
+        cudaError_t e = matmul_q8_0_many_launch(d_w, k, out_f, d_xq, n_tok, 0, n_tok, d_out, s);
+        return e == cudaSuccess ? QH_OK : cuda_fail(e, "q8_0 matmul launch");
+    }
+    int chunk = 8;  // tokens per launch; halved while a stage cannot hold them
+    for (int64_t t0 = 0; t0 < n_tok; t0 += chunk) {
+        GemvParams p{};
+        GemvGeometry g{};
+        cudaError_t e;
+        for (;;) {
+            const int nt = static_cast<int>(n_tok - t0 < chunk ? n_tok - t0 : chunk);
+            GemvJob job = make_job(type, d_w, k, out_f, d_xq, n_tok, t0, d_out);
+            e = gemv_plan(type, &job, 1, nt, sm_count, &p, &g);
+            if (e == cudaSuccess || chunk == 1) break;
+            chunk >>= 1;
+        }
+        if (e != cudaSuccess) return fail(QH_ERR_INVALID, "matmul: cannot tile rows of %lld bytes (%s)",
+                                          (long long)qhf_row_bytes(type, k), cudaGetErrorString(e));
+        p.err_flag = err_word;
+        p.table = nullptr;
+        e = gemv_launch(type, p, g, s);
+        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    }
+    return QH_OK;
 }
 }  // namespace qh
 
@@ -239,17 +261,32 @@ int qh_stream_sync(void *stream) {
 }
 
 int qh_check_device_error(int *code) {
-    int *w = nullptr;
-    int rc = device_state(nullptr, &w);
+    // Reads (and clears) the words the kernels report to on the current
+    // device: the library's own, and the no-allocation entry point's. Only
+    // words that already exist are read, so this call allocates nothing.
+    int dev;
+    int rc = current_device(&dev);
     if (rc) return rc;
-    int v = 0;
-    cudaError_t e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(e, "read device error word");
-    if (code) *code = v;
-    if (v != 0) {
-        cudaMemset(w, 0, sizeof(int));
-        return fail(QH_ERR_DEVICE, "device error %d (a bounded wait timed out)", v);
+    int *words[2];
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        words[0] = g_err_words[dev];
     }
+    words[1] = qh::noalloc_error_word(dev);
+    int first = 0;
+    for (int *w : words) {
+        if (!w) continue;
+        int v = 0;
+        cudaError_t e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+        if (v != 0) {
+            e = cudaMemset(w, 0, sizeof(int));
+            if (e != cudaSuccess) return cuda_fail(e, "clear device error word");
+            if (!first) first = v;
+        }
+    }
+    if (code) *code = first;
+    if (first != 0) return fail(QH_ERR_DEVICE, "device error %d (a bounded wait timed out)", first);
     return QH_OK;
 }
 
@@ -280,6 +317,7 @@ int qh_quantize_q8_0(const float *d_x, int64_t k, int64_t n_tok, void *d_q8_0, v
 }
 
 int64_t qh_matmul_workspace_bytes(int type, int64_t k, int64_t n_tok) {
+    if (type == QH_GGUF_F32 && k > 0 && n_tok > 0) return 0;
     if (qhf_block_bytes(type) == 0 || k <= 0 || n_tok <= 0) return -1;
     return act_bytes(type, k, n_tok);
 }
@@ -304,6 +342,11 @@ int qh_matmul_q6k_f32(const void *d_w, int64_t out_f, int64_t k, const float *d_
 int qh_matmul_q8_0_f32(const void *d_w, int64_t out_f, int64_t k, const float *d_x, int64_t n_tok,
                        float *d_out, void *d_work, int64_t work_bytes, void *stream) {
     return matmul_impl(QH_GGUF_Q8_0, d_w, k, out_f, d_x, n_tok, d_out, d_work, work_bytes, stream);
+}
+
+int qh_matmul_f32(const float *d_w, int64_t out_f, int64_t k, const float *d_x, int64_t n_tok, float *d_out,
+                  void *stream) {
+    return matmul_f32_impl(d_w, k, out_f, d_x, n_tok, d_out, stream);
 }
 
 int qh_matmul_preq(int type, const void *d_w, int64_t k, int64_t out_f, const void *d_xq,

@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(HD) gdn_chunk_prep_kernel(float *__restrict__ 
             const int64_t i = row * heads + h;
             const float bv = bb[i];
             const float a = __fadd_rn(aa[i], dt_bias[h]);
-            const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
+            const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
             bb[i] = sigmoid_f(bv);
             aa[i] = __fmul_rn(ssm_a[h], sp);
         }
@@ -271,8 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncthreads();
         if (t < cn) {
-            gex[t] = expf_cr(gcs[t]);
-            dif[t] = expf_cr(__fsub_rn(gcs[cn - 1], gcs[t]));
+            gex[t] = expf_ref(gcs[t]);
+            dif[t] = expf_ref(__fsub_rn(gcs[cn - 1], gcs[t]));
         }
         // ---- kk[i][j] = (K_j . (K_i * beta_i)) * exp(gcs_i - gcs_j), j < i (slm/chunked.c:340-358)
         for (int L = t; L < cn * (cn - 1) / 2; L += kThreads) {
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc = dot4(acc, a, make_float4(__fmul_rn(bq.x, bi), __fmul_rn(bq.y, bi), __fmul_rn(bq.z, bi),
                                                    __fmul_rn(bq.w, bi)));
                 }
-                m1[i * kChunk + j] = __fmul_rn(acc, expf_cr(__fsub_rn(gcs[i], gcs[j])));
+                m1[i * kChunk + j] = __fmul_rn(acc, expf_ref(__fsub_rn(gcs[i], gcs[j])));
             }
         }
         if (!waited) {
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float acc = 0.0f;
 #pragma unroll 4
                 for (int d = 0; d < kHd; d += 4) acc = dot4(acc, lds4(kj + d), lds4(qi + d));
-                m1[i * kChunk + j] = __fmul_rn(acc, i == j ? 1.0f : expf_cr(__fsub_rn(gcs[i], gcs[j])));
+                m1[i * kChunk + j] = __fmul_rn(acc, i == j ? 1.0f : expf_ref(__fsub_rn(gcs[i], gcs[j])));
             }
         }
         __syncthreads();

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include "qh_formats.h"
+#include "qh_libm.cuh"
 
 namespace qh {
 
@@ -141,14 +142,10 @@ __device__ __forceinline__ int4 ldg128(const void *p) {
     return __ldg(reinterpret_cast<const int4 *>(p));
 }
 
-// expf / logf evaluated in double precision and rounded once to float
-// (correctly rounded except within ~1e-16 relative of a rounding boundary),
-// the values the reference's host libm returns; and the SiLU / sigmoid the
-// reference builds from expf.
-__device__ __forceinline__ float expf_cr(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
-__device__ __forceinline__ float logf_cr(float x) { return static_cast<float>(log(static_cast<double>(x))); }
-__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x))); }
-__device__ __forceinline__ float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-x))); }
+// expf / logf: the host C library's values, bit for bit (qh_libm.cuh); and
+// the SiLU / sigmoid the reference builds from expf.
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-x))); }
 
 __device__ __forceinline__ float h2f_bits(uint32_t bits16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));

@@ -143,6 +143,22 @@ cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
 // Device error word (lazily allocated per device) and its reset/read.
 int *device_error_word();
 
+// Quantized-input matmul through the grouped GEMV kernel: tokens in launches
+// of up to 8, halved while a stage cannot hold them. Bounded-wait timeouts
+// go to `err_word`. Returns a QH_ status and sets qh_last_error() on failure.
+int matmul_preq_launch(int type, const void *d_w, int64_t k, int64_t out_f, const void *d_xq, int64_t n_tok,
+                       float *d_out, cudaStream_t s, int sm_count, int *err_word);
+
+// F32 weights (tensor_matmul_f32) and many-token Q8_0 (qh_small.cu).
+cudaError_t matmul_f32_launch(const float *w, int64_t k, int64_t out_f, const float *x, int64_t n_tok, float *out,
+                              cudaStream_t s);
+cudaError_t matmul_q8_0_many_launch(const void *w, int64_t k, int64_t out_f, const void *xq, int64_t xq_rows,
+                                    int64_t row0, int64_t n_tok, float *out, cudaStream_t s);
+
+// The no-allocation entry point's own error word on device `dev`, or null
+// while that entry point has not run there (qh_noalloc.cu).
+int *noalloc_error_word(int dev);
+
 // Sets the calling thread's qh_last_error() message.
 void set_last_error_message(const char *msg);
 

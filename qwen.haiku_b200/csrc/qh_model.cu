@@ -9,14 +9,12 @@
 // the reference does in float over a short axis stay sequential in one
 // thread (attention dot products, softmax sum, value accumulation), and its
 // double-precision sums stay double (norms, the DeltaNet kv/out products).
-// Transcendentals are evaluated in double precision and rounded once to
-// float (expf_cr/logf_cr below): that is the correctly rounded float result
-// except when the exact value lies within ~1e-16 (relative) of a float
-// rounding boundary, which is what the reference's host libm returns as
-// well -- single-precision device expf/logf differ from it by an ulp often
-// enough that the next layer's Q8_K quantization flips int8 values and the
-// token streams drift. RoPE cos/sin come from a host-computed table so they
-// match the reference's libm bit for bit.
+// Transcendentals are the host C library's expf/logf, reproduced bit for
+// bit (expf_ref/logf_ref, qh_libm.cuh): the device's own single-precision
+// expf/logf differ from them by an ulp often enough that the next layer's
+// Q8_K quantization flips int8 values and the token streams drift. RoPE
+// cos/sin come from a host-computed table so they match the reference's
+// libm bit for bit.
 
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
@@ -99,6 +97,18 @@ __global__ void embed_q6k_kernel(const uint8_t *__restrict__ table, int64_t hidd
     h[static_cast<int64_t>(b) * hidden + sb * QH_QK + p] = __fmul_rn(__fmul_rn(d, sc), static_cast<float>(q));
 }
 
+// F32 table (tensor_get_rows on the fp32 view, slm/qwen.c:885-889).
+__global__ void embed_f32_kernel(const float *__restrict__ table, int64_t hidden, const int32_t *__restrict__ tokens,
+                                 float *__restrict__ h) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.y;
+    const float *row = table + static_cast<int64_t>(tokens[b]) * hidden;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hidden;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        h[static_cast<int64_t>(b) * hidden + i] = row[i];
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm: one CTA per row.
 // ---------------------------------------------------------------------------
@@ -179,8 +189,8 @@ __global__ void gdn_pre_kernel(const float *__restrict__ qkv, float *__restrict_
         const int i = b * heads + h;
         beta[i] = sigmoid_f(bb[i]);
         const float a = __fadd_rn(aa[i], dt_bias[h]);
-        const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
-        gout[i] = expf_cr(__fmul_rn(ssm_a[h], sp));
+        const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
+        gout[i] = expf_ref(__fmul_rn(ssm_a[h], sp));
     }
 }
 
@@ -328,7 +338,7 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
         lmax = fmaxf(lmax, s);
     }
     const float m = block_max_f(lmax, scratch);
-    for (int i = t; i < n; i += blockDim.x) sc[i] = expf_cr(__fsub_rn(sc[i], m));
+    for (int i = t; i < n; i += blockDim.x) sc[i] = expf_ref(__fsub_rn(sc[i], m));
     __syncthreads();
     if (t == 0) {
         float s = 0.0f;
@@ -465,7 +475,7 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     }
     for (int i = t; i < n; i += blockDim.x)
 #pragma unroll
-        for (int g = 0; g < G; ++g) sc[g * max_pos + i] = expf_cr(__fsub_rn(sc[g * max_pos + i], m[g]));
+        for (int g = 0; g < G; ++g) sc[g * max_pos + i] = expf_ref(__fsub_rn(sc[g * max_pos + i], m[g]));
     __syncthreads();
     if (t < G) {  // sequential sums, one head per thread
         const float *st = sc + t * max_pos;
@@ -592,6 +602,15 @@ int qh_embed_q6k(const void *d_table, int64_t hidden, const int32_t *d_tokens, i
     const cudaError_t le = qh::launch_pdl(qh::embed_q6k_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), 
         static_cast<const uint8_t *>(d_table), hidden, d_tokens, d_h);
     return launch_status(le, "qh_embed_q6k");
+}
+
+int qh_embed_f32(const float *d_table, int64_t hidden, const int32_t *d_tokens, int32_t B, float *d_h,
+                 void *stream) {
+    if (!d_table || !d_tokens || !d_h || hidden <= 0 || B <= 0) return bad("qh_embed_f32: bad arguments");
+    dim3 grid(static_cast<unsigned>((hidden + 255) / 256 < 8 ? (hidden + 255) / 256 : 8), static_cast<unsigned>(B));
+    const cudaError_t le = qh::launch_pdl(qh::embed_f32_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                          d_table, hidden, d_tokens, d_h);
+    return launch_status(le, "qh_embed_f32");
 }
 
 int qh_rmsnorm(const float *d_x, const float *d_w, int64_t dim, int64_t rows, float eps, float *d_y,
@@ -912,8 +931,8 @@ __global__ void __launch_bounds__(HD)
         const int i = b * heads + h;
         s_beta = sigmoid_f(bb[i]);
         const float a = __fadd_rn(aa[i], dt_bias[h]);
-        const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
-        s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
+        const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
+        s_g = expf_ref(__fmul_rn(ssm_a[h], sp));
     }
     // The kk - 1 older taps from the ring (the newest tap is the new input
     // itself), then the ring update, then the sums in tap order -- the same
@@ -1101,8 +1120,8 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
             const int64_t i = row * heads + h;
             s_beta = sigmoid_f(bb[i]);
             const float a = __fadd_rn(aa[i], dt_bias[h]);
-            const float sp = a > 20.0f ? a : logf_cr(__fadd_rn(1.0f, expf_cr(a)));
-            s_g = expf_cr(__fmul_rn(ssm_a[h], sp));
+            const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
+            s_g = expf_ref(__fmul_rn(ssm_a[h], sp));
         }
         float mixed[3];
 #pragma unroll

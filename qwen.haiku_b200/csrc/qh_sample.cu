@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kThreads)
         }
         __syncthreads();
         const float m = sh.sum;
-        if (tid < filled) sh.val[tid] = expf_cr(__fdiv_rn(__fsub_rn(sh.val[tid], m), sp.temperature));
+        if (tid < filled) sh.val[tid] = expf_ref(__fdiv_rn(__fsub_rn(sh.val[tid], m), sp.temperature));
         __syncthreads();
         if (tid == 0) {
             float s = 0.0f;

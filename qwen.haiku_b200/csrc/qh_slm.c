@@ -34,27 +34,54 @@
 
 #define MAX_LAYERS 128
 
-// The projections sharing one activation buffer. B <= 8: one grouped
-// matvec plan (weights streamed once per step, GEMV kernel). B > 8: one
-// grouped tensor-core GEMM over tiled weights (qh_gemm).
+// A weight matrix as the GGUF file stores it: type, shape (k = input dim,
+// out_f = output dim) and the device copy of its bytes.
 typedef struct {
-    qh_matvec_plan plan[1];
-    int nplan;
-    int gemm, type, njobs;
+    const void *d;
+    int type;
+    int64_t k, out_f;
+} wref;
+
+// The projections that read one input (q/k/v; qkv/gate/beta/alpha; gate/up;
+// one output projection). Each weight is computed by its own GGUF type, as
+// matmul_dispatch does (slm/model.c:220-264):
+//   * K-quant weights (Q4_K, Q5_K, Q6_K) read the input's Q8_K rows, which
+//     the kernel before the set writes: one grouped matvec plan per type
+//     (GEMV kernel; rows <= 8) or one tensor-core GEMM launch per type over
+//     expanded weights (more rows);
+//   * Q8_0 weights read Q8_0 rows of the fp32 input (tensor_quantize_row_q8_0
+//     per token, as tensor_matmul_q8_0_f32), F32 weights the fp32 input
+//     itself (tensor_matmul_f32); the step forms that fp32 input (x32) only
+//     for sets that hold such weights.
+#define PS_MAX 8
+typedef struct {
+    int n;
+    const wref *w[PS_MAX];
+    float *out[PS_MAX];
     int64_t k;
+    int gemm;
     const void *xq;
-    qh_gemm_job jobs[8];
+    qh_matvec_plan plan[3];
+    int nplan;
+    struct {
+        int type, njobs;
+        qh_gemm_job jobs[PS_MAX];
+    } gg[3];
+    int ngg;
+    int n32, has_q8_0;
+    const float *x32;
+    void *xq80;
 } plan_set;
 
 typedef struct {
     int is_attn;
     const float *attn_norm, *ffn_norm;
-    const void *ffn_gate, *ffn_up, *ffn_down;
+    wref ffn_gate, ffn_up, ffn_down;
     // GDN
-    const void *qkv, *gate, *alpha, *beta, *ssm_out;
+    wref qkv, gate, alpha, beta, ssm_out;
     const float *ssm_a, *conv_w, *dt_bias, *ssm_norm;
     // attention
-    const void *wq, *wk, *wv, *wo;
+    wref wq, wk, wv, wo;
     const float *q_norm, *k_norm;
     int gdn_index, attn_index;
     plan_set p_in, p_out, p_ffn, p_down;
@@ -71,7 +98,7 @@ struct qh_slm {
     void **allocs;
     int nallocs, capallocs;
     int64_t weight_bytes, state_bytes;
-    const void *tok_embd;
+    wref tok_embd;
     const float *out_norm;
     layer L[MAX_LAYERS];
     int n_gdn, n_attn;
@@ -95,6 +122,7 @@ struct qh_slm {
     float *pf_o;                   // chunked mode: DeltaNet outputs [rows][gdn width]
     float *pf_h, *pf_h2, *pf_mix, *pf_qkv, *pf_z, *pf_bt, *pf_at, *pf_qraw, *pf_kb, *pf_vb, *pf_aq, *pf_agate,
         *pf_actx, *pf_fgate, *pf_fup;
+    float *pf_hn, *pf_fact;        // fp32 rows for Q8_0/F32 weights (allocated when a set has them)
     void *pf_xq_h, *pf_xq_gdn, *pf_xq_ffn;
     int32_t *pf_tok, *pf_pos;
     plan_set pf_in[MAX_LAYERS], pf_out[MAX_LAYERS], pf_ffn[MAX_LAYERS], pf_down[MAX_LAYERS];
@@ -139,16 +167,52 @@ static int dev_alloc(qh_slm *m, void **p, size_t bytes, int64_t *counter) {
 
 #define CK(x) do { int rc_ = (x); if (rc_) return rc_; } while (0)
 
-static int upload(qh_slm *m, const qh_blob *blob, const char *name, const void **out) {
+// Device copy of the blob's matrix `name`, checked against the shape the
+// model needs (GGUF order: k = input dim, out_f = output dim): a type the
+// matmuls compute -- F32, Q8_0, Q4_K, Q5_K, Q6_K, the cases of
+// matmul_dispatch (slm/model.c:220-264) -- else QH_ERR_UNSUPPORTED; a
+// different shape, QH_ERR_INVALID. (The reference aborts on an unknown type
+// and trusts the shapes; here a file whose tensors do not fit the model is
+// refused before any kernel reads past a weight buffer.)
+static int upload_w(qh_slm *m, const qh_blob *blob, const char *name, int64_t k, int64_t out_f, wref *out) {
+    int i = qh_blob_find(blob, name);
+    if (i < 0) return QH_ERR_INVALID;
+    const void *data;
+    int64_t nbytes, shape[2];
+    int32_t type;
+    CK(qh_blob_tensor(blob, i, NULL, &type, shape, &data, &nbytes));
+    if (type != QH_GGUF_F32 && type != QH_GGUF_Q8_0 && type != QH_GGUF_Q4_K && type != QH_GGUF_Q5_K &&
+        type != QH_GGUF_Q6_K)
+        return QH_ERR_UNSUPPORTED;
+    if (shape[0] != k || shape[1] != out_f) return QH_ERR_INVALID;
+    const int64_t want = type == QH_GGUF_F32 ? 4 * k * out_f : qhf_row_bytes(type, k) * out_f;
+    if (type != QH_GGUF_F32 && k % qhf_block_weights(type)) return QH_ERR_INVALID;
+    if (nbytes != want) return QH_ERR_INVALID;
+    void *d;
+    CK(dev_alloc(m, &d, (size_t)nbytes, &m->weight_bytes));
+    CK(qh_memcpy_h2d(d, data, (size_t)nbytes, m->stream));
+    out->d = d;
+    out->type = type;
+    out->k = k;
+    out->out_f = out_f;
+    return QH_OK;
+}
+
+// Device copy of an fp32 vector of n values (norm weights, conv kernel,
+// ssm_a, dt bias).
+static int upload_vec(qh_slm *m, const qh_blob *blob, const char *name, int64_t n, const float **out) {
     int i = qh_blob_find(blob, name);
     if (i < 0) return QH_ERR_INVALID;
     const void *data;
     int64_t nbytes;
-    CK(qh_blob_tensor(blob, i, NULL, NULL, NULL, &data, &nbytes));
+    int32_t type;
+    CK(qh_blob_tensor(blob, i, NULL, &type, NULL, &data, &nbytes));
+    if (type != QH_GGUF_F32) return QH_ERR_UNSUPPORTED;
+    if (nbytes != 4 * n) return QH_ERR_INVALID;
     void *d;
     CK(dev_alloc(m, &d, (size_t)nbytes, &m->weight_bytes));
     CK(qh_memcpy_h2d(d, data, (size_t)nbytes, m->stream));
-    *out = d;
+    *out = (const float *)d;
     return QH_OK;
 }
 
@@ -178,56 +242,92 @@ static int get_tiled(qh_slm *m, const void *raw, int type, int64_t k, int64_t ou
     return QH_OK;
 }
 
-// GEMM job set over expanded weights (outputs [rows][out_f]).
-static int make_gemm_set(qh_slm *m, plan_set *ps, int type, int nm, const void *const *w, const int64_t *out_f,
-                         float *const *out, const void *xq, int64_t k) {
-    if (nm > 8) return QH_ERR_INVALID;
-    ps->gemm = 1;
-    ps->type = type;
-    ps->njobs = nm;
+static int is_kquant(int type) { return type == QH_GGUF_Q4_K || type == QH_GGUF_Q5_K || type == QH_GGUF_Q6_K; }
+
+// A set over `nm` (<= 8) weights that read one input of k values per row:
+// xq its Q8_K rows (split layout for the GEMV at `rows` <= 8, tiled for the
+// GEMM), rows the rows per launch. gemm: K-quant weights on the tensor-core
+// GEMM (their expanded copies are made here). Q8_0/F32 weights get a Q8_0
+// buffer; the caller points x32 at the fp32 input before the set runs.
+static int make_set(qh_slm *m, plan_set *ps, int nm, const wref *const *w, float *const *out, const void *xq,
+                    int64_t k, int64_t rows, int gemm) {
+    if (nm > PS_MAX) return QH_ERR_INVALID;
+    memset(ps, 0, sizeof(*ps));
+    ps->n = nm;
     ps->k = k;
+    ps->gemm = gemm;
     ps->xq = xq;
+    static const int kq[3] = {QH_GGUF_Q4_K, QH_GGUF_Q5_K, QH_GGUF_Q6_K};
     for (int i = 0; i < nm; ++i) {
-        const void *wt;
-        CK(get_tiled(m, w[i], type, k, out_f[i], &wt));
-        ps->jobs[i].d_wt = wt;
-        ps->jobs[i].out_f = out_f[i];
-        ps->jobs[i].d_out = out[i];
-        ps->jobs[i].ld_out = out_f[i];
+        if (w[i]->k != k) return QH_ERR_INVALID;
+        ps->w[i] = w[i];
+        ps->out[i] = out[i];
+        if (!is_kquant(w[i]->type)) {
+            ps->n32++;
+            if (w[i]->type == QH_GGUF_Q8_0) ps->has_q8_0 = 1;
+        }
     }
+    for (int t = 0; t < 3; ++t) {
+        qh_matvec_job jobs[PS_MAX];
+        int nj = 0;
+        memset(jobs, 0, sizeof(jobs));
+        for (int i = 0; i < nm; ++i) {
+            if (w[i]->type != kq[t]) continue;
+            if (gemm) {
+                const void *wt;
+                CK(get_tiled(m, w[i]->d, kq[t], k, w[i]->out_f, &wt));
+                qh_gemm_job *j = &ps->gg[ps->ngg].jobs[nj];
+                j->d_wt = wt;
+                j->out_f = w[i]->out_f;
+                j->d_out = out[i];
+                j->ld_out = w[i]->out_f;
+            } else {
+                jobs[nj].d_w = w[i]->d;
+                jobs[nj].d_xq = xq;
+                jobs[nj].d_out = out[i];
+                jobs[nj].k = k;
+                jobs[nj].out_f = w[i]->out_f;
+                jobs[nj].xq_rows = rows;
+                jobs[nj].xq_row0 = 0;
+            }
+            nj++;
+        }
+        if (!nj) continue;
+        if (gemm) {
+            ps->gg[ps->ngg].type = kq[t];
+            ps->gg[ps->ngg].njobs = nj;
+            ps->ngg++;
+        } else {
+            CK(qh_matvec_plan_create(kq[t], jobs, nj, rows, &ps->plan[ps->nplan]));
+            ps->nplan++;
+        }
+    }
+    if (ps->has_q8_0) CK(dev_alloc(m, &ps->xq80, (size_t)qh_q8_0_bytes(k, rows), NULL));
     return QH_OK;
 }
 
-// A plan over `nm` (<= 8) matrices of one type sharing the activation
-// buffer xq (quantized for B rows of k; split layout for the GEMV, tiled
-// for the GEMM). The GEMM path packs each matrix into its tiled order here.
-static int make_plan(qh_slm *m, plan_set *ps, int type, int nm, const void *const *w,
-                     const int64_t *out_f, float *const *out, const void *xq, int64_t k) {
-    const int32_t B = m->B;
-    if (nm > 8) return QH_ERR_INVALID;
-    if (m->use_gemm) return make_gemm_set(m, ps, type, nm, w, out_f, out, xq, k);
-    qh_matvec_job jobs[8];
-    memset(jobs, 0, sizeof(jobs));
-    for (int i = 0; i < nm; ++i) {
-        jobs[i].d_w = w[i];
-        jobs[i].d_xq = xq;
-        jobs[i].d_out = out[i];
-        jobs[i].k = k;
-        jobs[i].out_f = out_f[i];
-        jobs[i].xq_rows = B;
-        jobs[i].xq_row0 = 0;
+// Runs a set for `rows` input rows (the fp32 input, when the set needs it,
+// at ps->x32); scratch: split-K terms of the GEMM (may be null).
+static int run_set(qh_slm *m, plan_set *ps, int64_t rows, void *scratch, int64_t scratch_bytes) {
+    for (int g = 0; g < ps->ngg; ++g)  /* expanded weights made at create, then synchronized */
+        CK(qh_gemm(ps->gg[g].type, ps->gg[g].jobs, ps->gg[g].njobs, ps->k, ps->xq, rows, scratch, scratch_bytes,
+                   QH_GEMM_WEIGHTS_READY | QH_GEMM_EXPANDED, m->stream));
+    for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
+    if (!ps->n32) return QH_OK;
+    if (!ps->x32) return QH_ERR_INVALID;
+    if (ps->has_q8_0) CK(qh_quantize_q8_0(ps->x32, ps->k, rows, ps->xq80, m->stream));
+    for (int i = 0; i < ps->n; ++i) {
+        const wref *w = ps->w[i];
+        if (w->type == QH_GGUF_Q8_0)
+            CK(qh_matmul_preq(QH_GGUF_Q8_0, w->d, ps->k, w->out_f, ps->xq80, rows, ps->out[i], m->stream));
+        else if (w->type == QH_GGUF_F32)
+            CK(qh_matmul_f32((const float *)w->d, w->out_f, ps->k, ps->x32, rows, ps->out[i], m->stream));
     }
-    CK(qh_matvec_plan_create(type, jobs, nm, B, &ps->plan[0]));
-    ps->nplan = 1;
     return QH_OK;
 }
 
 static int run_plans(qh_slm *m, plan_set *ps) {
-    if (ps->gemm)
-        return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, m->B, m->gemm_scratch, m->gemm_scratch_bytes,
-                       QH_GEMM_WEIGHTS_READY | QH_GEMM_EXPANDED, m->stream);  /* made at create, then synchronized */
-    for (int i = 0; i < ps->nplan; ++i) CK(qh_matvec_plan_run(ps->plan[i], m->stream));
-    return QH_OK;
+    return run_set(m, ps, m->B, m->gemm_scratch, m->gemm_scratch_bytes);
 }
 
 static void free_plans(plan_set *ps) {
@@ -255,39 +355,44 @@ static void rope_table(const qh_slm_config *c, float *tab) {
 
 static int bind_layers(qh_slm *m, const qh_blob *blob) {
     const qh_slm_config *c = &m->cfg;
+    const int64_t H = c->hidden, F = c->ffn, hd = c->head_dim;
+    const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
+    const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
     char nm[96];
-#define W(field, fmt) do { snprintf(nm, sizeof(nm), fmt, l); CK(upload(m, blob, nm, (const void **)&Ly->field)); } while (0)
+#define W(field, fmt, k_, out_f_) do { snprintf(nm, sizeof(nm), fmt, l); CK(upload_w(m, blob, nm, (k_), (out_f_), &Ly->field)); } while (0)
+#define V(field, fmt, n_) do { snprintf(nm, sizeof(nm), fmt, l); CK(upload_vec(m, blob, nm, (n_), &Ly->field)); } while (0)
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
         snprintf(nm, sizeof(nm), "blk.%d.ssm_a", l);
         Ly->is_attn = qh_blob_find(blob, nm) < 0;
-        W(attn_norm, "blk.%d.attn_norm.weight");
-        W(ffn_norm, "blk.%d.post_attention_norm.weight");
-        W(ffn_gate, "blk.%d.ffn_gate.weight");
-        W(ffn_up, "blk.%d.ffn_up.weight");
-        W(ffn_down, "blk.%d.ffn_down.weight");
+        V(attn_norm, "blk.%d.attn_norm.weight", H);
+        V(ffn_norm, "blk.%d.post_attention_norm.weight", H);
+        W(ffn_gate, "blk.%d.ffn_gate.weight", H, F);
+        W(ffn_up, "blk.%d.ffn_up.weight", H, F);
+        W(ffn_down, "blk.%d.ffn_down.weight", F, H);
         if (Ly->is_attn) {
-            W(wq, "blk.%d.attn_q.weight");
-            W(wk, "blk.%d.attn_k.weight");
-            W(wv, "blk.%d.attn_v.weight");
-            W(wo, "blk.%d.attn_output.weight");
-            W(q_norm, "blk.%d.attn_q_norm.weight");
-            W(k_norm, "blk.%d.attn_k_norm.weight");
+            W(wq, "blk.%d.attn_q.weight", H, 2 * qdim);
+            W(wk, "blk.%d.attn_k.weight", H, kvd);
+            W(wv, "blk.%d.attn_v.weight", H, kvd);
+            W(wo, "blk.%d.attn_output.weight", qdim, H);
+            V(q_norm, "blk.%d.attn_q_norm.weight", hd);
+            V(k_norm, "blk.%d.attn_k_norm.weight", hd);
             Ly->attn_index = m->n_attn++;
         } else {
-            W(qkv, "blk.%d.attn_qkv.weight");
-            W(gate, "blk.%d.attn_gate.weight");
-            W(alpha, "blk.%d.ssm_alpha.weight");
-            W(beta, "blk.%d.ssm_beta.weight");
-            W(ssm_out, "blk.%d.ssm_out.weight");
-            W(ssm_a, "blk.%d.ssm_a");
-            W(conv_w, "blk.%d.ssm_conv1d.weight");
-            W(dt_bias, "blk.%d.ssm_dt.bias");
-            W(ssm_norm, "blk.%d.ssm_norm.weight");
+            W(qkv, "blk.%d.attn_qkv.weight", H, conv_dim);
+            W(gate, "blk.%d.attn_gate.weight", H, kdim);
+            W(alpha, "blk.%d.ssm_alpha.weight", H, c->gdn_heads);
+            W(beta, "blk.%d.ssm_beta.weight", H, c->gdn_heads);
+            W(ssm_out, "blk.%d.ssm_out.weight", kdim, H);
+            V(ssm_a, "blk.%d.ssm_a", c->gdn_heads);
+            V(conv_w, "blk.%d.ssm_conv1d.weight", (int64_t)c->conv_kernel * conv_dim);
+            V(dt_bias, "blk.%d.ssm_dt.bias", c->gdn_heads);
+            V(ssm_norm, "blk.%d.ssm_norm.weight", c->gdn_head_dim);
             Ly->gdn_index = m->n_gdn++;
         }
     }
 #undef W
+#undef V
     return QH_OK;
 }
 
@@ -307,8 +412,10 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
     int rc = QH_OK;
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) { rc = QH_ERR_CUDA; goto fail; }
 #define TRY(x) do { rc = (x); if (rc) goto fail; } while (0)
-    TRY(upload(m, blob, "token_embd.weight", &m->tok_embd));
-    TRY(upload(m, blob, "output_norm.weight", (const void **)&m->out_norm));
+    TRY(upload_w(m, blob, "token_embd.weight", cfg->hidden, cfg->vocab, &m->tok_embd));
+    // the embedding row reader takes the two types the reference's does (slm/qwen.c:885-907)
+    if (m->tok_embd.type != QH_GGUF_Q6_K && m->tok_embd.type != QH_GGUF_F32) { rc = QH_ERR_UNSUPPORTED; goto fail; }
+    TRY(upload_vec(m, blob, "output_norm.weight", cfg->hidden, &m->out_norm));
     TRY(bind_layers(m, blob));
     {
         const int64_t B = n_seq, H = cfg->hidden, F = cfg->ffn, hd = cfg->head_dim;
@@ -396,41 +503,41 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
         if (!rc) rc = qh_stream_sync(m->stream);
         free(tab);
         if (rc) goto fail;
-        // matvec plans
+        // projection sets, each weight by its own type
+        const int g = m->use_gemm;
         for (int l = 0; l < cfg->n_layers; ++l) {
             layer *Ly = &m->L[l];
             if (Ly->is_attn) {
-                const void *w[3] = {Ly->wq, Ly->wk, Ly->wv};
-                const int64_t of[3] = {2 * qdim, kvd, kvd};
+                const wref *w[3] = {&Ly->wq, &Ly->wk, &Ly->wv};
                 float *o[3] = {m->qraw, m->kb, m->vb};
-                TRY(make_plan(m, &Ly->p_in, QH_TYPE_Q4_K, 3, w, of, o, m->xq_h, H));
-                const void *w2[1] = {Ly->wo};
-                const int64_t of2[1] = {H};
+                TRY(make_set(m, &Ly->p_in, 3, w, o, m->xq_h, H, B, g));
+                const wref *w2[1] = {&Ly->wo};
                 float *o2[1] = {m->mix};
-                TRY(make_plan(m, &Ly->p_out, QH_TYPE_Q4_K, 1, w2, of2, o2, m->xq_h, qdim));
+                TRY(make_set(m, &Ly->p_out, 1, w2, o2, m->xq_h, qdim, B, g));
+                Ly->p_out.x32 = m->actx;
             } else {
-                const void *w[4] = {Ly->qkv, Ly->gate, Ly->beta, Ly->alpha};
-                const int64_t of[4] = {conv_dim, kdim, cfg->gdn_heads, cfg->gdn_heads};
+                const wref *w[4] = {&Ly->qkv, &Ly->gate, &Ly->beta, &Ly->alpha};
                 float *o[4] = {m->qkv, m->z, m->bt, m->at};
-                TRY(make_plan(m, &Ly->p_in, QH_TYPE_Q4_K, 4, w, of, o, m->xq_h, H));
-                const void *w2[1] = {Ly->ssm_out};
-                const int64_t of2[1] = {H};
+                TRY(make_set(m, &Ly->p_in, 4, w, o, m->xq_h, H, B, g));
+                const wref *w2[1] = {&Ly->ssm_out};
                 float *o2[1] = {m->mix};
-                TRY(make_plan(m, &Ly->p_out, QH_TYPE_Q4_K, 1, w2, of2, o2, m->xq_gdn, kdim));
+                TRY(make_set(m, &Ly->p_out, 1, w2, o2, m->xq_gdn, kdim, B, g));
+                Ly->p_out.x32 = m->gy;
             }
-            const void *wf[2] = {Ly->ffn_gate, Ly->ffn_up};
-            const int64_t off[2] = {F, F};
+            Ly->p_in.x32 = m->hn;
+            const wref *wf[2] = {&Ly->ffn_gate, &Ly->ffn_up};
             float *of_[2] = {m->fgate, m->fup};
-            TRY(make_plan(m, &Ly->p_ffn, QH_TYPE_Q4_K, 2, wf, off, of_, m->xq_h, H));
-            const void *wd[1] = {Ly->ffn_down};
-            const int64_t ofd[1] = {H};
+            TRY(make_set(m, &Ly->p_ffn, 2, wf, of_, m->xq_h, H, B, g));
+            Ly->p_ffn.x32 = m->hn;
+            const wref *wd[1] = {&Ly->ffn_down};
             float *od[1] = {m->mix};
-            TRY(make_plan(m, &Ly->p_down, QH_TYPE_Q6_K, 1, wd, ofd, od, m->xq_ffn, F));
+            TRY(make_set(m, &Ly->p_down, 1, wd, od, m->xq_ffn, F, B, g));
+            Ly->p_down.x32 = m->fact;
         }
-        const void *wh[1] = {m->tok_embd};
-        const int64_t ofh[1] = {cfg->vocab};
+        const wref *wh[1] = {&m->tok_embd};
         float *oh[1] = {m->logits};
-        TRY(make_plan(m, &m->p_head, QH_TYPE_Q6_K, 1, wh, ofh, oh, m->xq_h, H));
+        TRY(make_set(m, &m->p_head, 1, wh, oh, m->xq_h, H, B, g));
+        m->p_head.x32 = m->hn;
         // (Output tails, qh_matvec_plan_fuse_output, could form each next
         // Q8_K input inside the projection before it; measured in the
         // captured step at batch 1 they are slower -- 1.51 against 1.04 ms
@@ -448,15 +555,16 @@ int qh_slm_create(const qh_slm_config *cfg, const qh_blob *blob, int32_t n_seq, 
                 all[na_++] = &m->L[l].p_down;
             }
             all[na_++] = &m->p_head;
-            for (int i = 0; i < na_; ++i) {
-                // only launches with few output tiles split K (the LM head never does)
-                int64_t tiles = 0;
-                for (int j = 0; j < all[i]->njobs; ++j) tiles += (all[i]->jobs[j].out_f + 127) / 128;
-                tiles *= (B + QH_Q8KT_TILE_TOKENS - 1) / QH_Q8KT_TILE_TOKENS;
-                if (tiles >= 148) continue;
-                const int64_t b = qh_gemm_scratch_bytes(all[i]->jobs, all[i]->njobs, all[i]->k, B);
-                if (b > need) need = b;
-            }
+            for (int i = 0; i < na_; ++i)
+                for (int q = 0; q < all[i]->ngg; ++q) {
+                    // only launches with few output tiles split K (the LM head never does)
+                    int64_t tiles = 0;
+                    for (int j = 0; j < all[i]->gg[q].njobs; ++j) tiles += (all[i]->gg[q].jobs[j].out_f + 127) / 128;
+                    tiles *= (B + QH_Q8KT_TILE_TOKENS - 1) / QH_Q8KT_TILE_TOKENS;
+                    if (tiles >= 148) continue;
+                    const int64_t b = qh_gemm_scratch_bytes(all[i]->gg[q].jobs, all[i]->gg[q].njobs, all[i]->k, B);
+                    if (b > need) need = b;
+                }
             if (need == 0) need = 256;
             TRY(dev_alloc(m, &m->gemm_scratch, (size_t)need, NULL));
             TRY(qh_memset(m->gemm_scratch, 0, (size_t)need, m->stream));
@@ -613,7 +721,8 @@ static int forward(qh_slm *m) {
     do {                                                               \
         if (m->trace_fp) CK(trace_row(m, (op), (ptr), (n), __VA_ARGS__)); \
     } while (0)
-    CK(qh_embed_q6k(m->tok_embd, H, m->d_tok, B, m->h, s));
+    CK(m->tok_embd.type == QH_GGUF_F32 ? qh_embed_f32((const float *)m->tok_embd.d, H, m->d_tok, B, m->h, s)
+                                       : qh_embed_q6k(m->tok_embd.d, H, m->d_tok, B, m->h, s));
     TR("GET_ROWS", m->h, H, "inp_embd");
     // The residual stream alternates between two buffers: each add writes
     // h + mix into the other one (the fused kernel reads h from many CTAs).
@@ -628,9 +737,10 @@ static int forward(qh_slm *m) {
     do {                                                                                                   \
         const int added_ = pending != NULL;                                                                \
         CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, B, c->norm_eps, m->xq_h, m->xq_tile, s)); \
-        CK(run_plans(m, (ps)));                                                                            \
         if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                               \
         pending = NULL;                                                                                    \
+        if ((ps)->n32) CK(qh_rmsnorm(hc, (w), H, B, c->norm_eps, m->hn, s)); /* fp32 rows for Q8_0/F32 */ \
+        CK(run_plans(m, (ps)));                                                                            \
         if (m->trace_fp) {                                                                                 \
             if (added_) TR("ADD", hc, H, ADD_NAME, ADD_L);                                                 \
             CK(qh_rmsnorm(hc, (w), H, B, c->norm_eps, m->hn, s));                                          \
@@ -676,11 +786,14 @@ static int forward(qh_slm *m) {
                 TR("RMS_NORM_GATED", m->gy, kdim, "y_norm-%d", l);
                 CK(m->use_gemm ? qh_quantize_q8kt(m->gy, kdim, B, m->xq_gdn, s)
                                : qh_quantize_q8k(m->gy, kdim, B, m->xq_gdn, s));
-            } else if (m->use_gemm) {  /* many sequences: heads as independent CTAs, then the quantizer */
+            } else if (m->use_gemm || Ly->p_out.n32) {
+                /* many sequences: heads as independent CTAs, then the quantizer; also when
+                   ssm_out reads the fp32 rows (Q8_0 / F32 weights) */
                 CK(qh_gdn_fused_y(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
                                   Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps,
                                   m->d_ctl, m->gy, s));
-                CK(qh_quantize_q8kt(m->gy, kdim, B, m->xq_gdn, s));
+                CK(m->use_gemm ? qh_quantize_q8kt(m->gy, kdim, B, m->xq_gdn, s)
+                               : qh_quantize_q8k(m->gy, kdim, B, m->xq_gdn, s));
             } else {
                 CK(qh_gdn_fused(m->qkv, ring, Ly->conv_w, m->bt, m->at, Ly->dt_bias, Ly->ssm_a, state, m->z,
                                 Ly->ssm_norm, B, c->gdn_heads, c->gdn_head_dim, c->conv_kernel, c->norm_eps,
@@ -696,6 +809,7 @@ static int forward(qh_slm *m) {
         pending = m->mix;
         NORMED(&Ly->p_ffn, Ly->ffn_norm, "mix_residual-%d", l, "ffn_norm-%d", l);
         CK(qh_swiglu_q8k(m->fgate, m->fup, F, B, m->xq_ffn, m->xq_tile, s));
+        if (Ly->p_down.n32) CK(qh_swiglu(m->fgate, m->fup, m->fact, B * F, s));
         CK(run_plans(m, &Ly->p_down));
         TR("MUL_MAT", m->mix, H, "ffn_out-%d", l);
         pending = m->mix;
@@ -856,45 +970,51 @@ static int ensure_prefill(qh_slm *m) {
     CK(dev_alloc(m, &m->pf_xq_ffn, (size_t)qh_q8kt_bytes(F, M), NULL));
     CK(dev_alloc(m, (void **)&m->pf_tok, (size_t)M * 4, NULL));
     CK(dev_alloc(m, (void **)&m->pf_pos, 16, NULL));
+    // Q8_0/F32 weights read fp32 rows: normalized inputs and the SwiGLU output
+    int need_hn = m->p_head.n32, need_fact = 0;
+    for (int l = 0; l < c->n_layers; ++l) {
+        need_hn |= m->L[l].p_in.n32 | m->L[l].p_ffn.n32;
+        need_fact |= m->L[l].p_down.n32;
+        // the step-wise DeltaNet prompt kernel writes only the Q8_K rows of its output
+        if (!m->L[l].is_attn && m->L[l].p_out.n32 && m->pf_mode != QH_PREFILL_CHUNKED) return QH_ERR_UNSUPPORTED;
+    }
+    if (need_hn) CK(alloc_f(m, &m->pf_hn, M * H));
+    if (need_fact) CK(alloc_f(m, &m->pf_fact, M * F));
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
         if (Ly->is_attn) {
-            const void *w[3] = {Ly->wq, Ly->wk, Ly->wv};
-            const int64_t of[3] = {2 * qdim, kvd, kvd};
+            const wref *w[3] = {&Ly->wq, &Ly->wk, &Ly->wv};
             float *o[3] = {m->pf_qraw, m->pf_kb, m->pf_vb};
-            CK(make_gemm_set(m, &m->pf_in[l], QH_TYPE_Q4_K, 3, w, of, o, m->pf_xq_h, H));
-            const void *w2[1] = {Ly->wo};
-            const int64_t of2[1] = {H};
+            CK(make_set(m, &m->pf_in[l], 3, w, o, m->pf_xq_h, H, M, 1));
+            const wref *w2[1] = {&Ly->wo};
             float *o2[1] = {m->pf_mix};
-            CK(make_gemm_set(m, &m->pf_out[l], QH_TYPE_Q4_K, 1, w2, of2, o2, m->pf_xq_h, qdim));
+            CK(make_set(m, &m->pf_out[l], 1, w2, o2, m->pf_xq_h, qdim, M, 1));
+            m->pf_out[l].x32 = m->pf_actx;
         } else {
-            const void *w[4] = {Ly->qkv, Ly->gate, Ly->beta, Ly->alpha};
-            const int64_t of[4] = {conv_dim, kdim, c->gdn_heads, c->gdn_heads};
+            const wref *w[4] = {&Ly->qkv, &Ly->gate, &Ly->beta, &Ly->alpha};
             float *o[4] = {m->pf_qkv, m->pf_z, m->pf_bt, m->pf_at};
-            CK(make_gemm_set(m, &m->pf_in[l], QH_TYPE_Q4_K, 4, w, of, o, m->pf_xq_h, H));
-            const void *w2[1] = {Ly->ssm_out};
-            const int64_t of2[1] = {H};
+            CK(make_set(m, &m->pf_in[l], 4, w, o, m->pf_xq_h, H, M, 1));
+            const wref *w2[1] = {&Ly->ssm_out};
             float *o2[1] = {m->pf_mix};
-            CK(make_gemm_set(m, &m->pf_out[l], QH_TYPE_Q4_K, 1, w2, of2, o2, m->pf_xq_gdn, kdim));
+            CK(make_set(m, &m->pf_out[l], 1, w2, o2, m->pf_xq_gdn, kdim, M, 1));
+            m->pf_out[l].x32 = m->pf_o;
         }
-        const void *wf[2] = {Ly->ffn_gate, Ly->ffn_up};
-        const int64_t off[2] = {F, F};
+        m->pf_in[l].x32 = m->pf_hn;
+        const wref *wf[2] = {&Ly->ffn_gate, &Ly->ffn_up};
         float *of_[2] = {m->pf_fgate, m->pf_fup};
-        CK(make_gemm_set(m, &m->pf_ffn[l], QH_TYPE_Q4_K, 2, wf, off, of_, m->pf_xq_h, H));
-        const void *wd[1] = {Ly->ffn_down};
-        const int64_t ofd[1] = {H};
+        CK(make_set(m, &m->pf_ffn[l], 2, wf, of_, m->pf_xq_h, H, M, 1));
+        m->pf_ffn[l].x32 = m->pf_hn;
+        const wref *wd[1] = {&Ly->ffn_down};
         float *od[1] = {m->pf_mix};
-        CK(make_gemm_set(m, &m->pf_down[l], QH_TYPE_Q6_K, 1, wd, ofd, od, m->pf_xq_ffn, F));
+        CK(make_set(m, &m->pf_down[l], 1, wd, od, m->pf_xq_ffn, F, M, 1));
+        m->pf_down[l].x32 = m->pf_fact;
     }
     CK(qh_stream_sync(m->stream));  // tiled weights complete before any early weight stream
     m->pf_chunk = (int32_t)C;
     return QH_OK;
 }
 
-static int run_pf(qh_slm *m, plan_set *ps, int64_t rows) {
-    return qh_gemm(ps->type, ps->jobs, ps->njobs, ps->k, ps->xq, rows, NULL, 0, QH_GEMM_WEIGHTS_READY | QH_GEMM_EXPANDED,
-                   m->stream);
-}
+static int run_pf(qh_slm *m, plan_set *ps, int64_t rows) { return run_set(m, ps, rows, NULL, 0); }
 
 // One chunk of cn tokens per sequence at positions *pf_pos .. + cn - 1;
 // tokens in pf_tok (row = s * cn + j). Leaves caches, ring and state as cn
@@ -907,18 +1027,21 @@ static int forward_prefill(qh_slm *m, int32_t cn) {
     const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
     void *s = m->stream;
     const int32_t T = QH_Q8KT_TILE_TOKENS;
-    CK(qh_embed_q6k(m->tok_embd, H, m->pf_tok, (int32_t)M, m->pf_h, s));
+    CK(m->tok_embd.type == QH_GGUF_F32
+           ? qh_embed_f32((const float *)m->tok_embd.d, H, m->pf_tok, (int32_t)M, m->pf_h, s)
+           : qh_embed_q6k(m->tok_embd.d, H, m->pf_tok, (int32_t)M, m->pf_h, s));
     float *hc = m->pf_h, *hx = m->pf_h2;
     const float *pending = NULL;
-#define PF_RESNORM(w, xq)                                                                                  \
+#define PF_RESNORM(w, xq, ps)                                                                              \
     do {                                                                                                   \
         CK(qh_rmsnorm_q8k(hc, pending, pending ? hx : NULL, (w), H, (int32_t)M, c->norm_eps, (xq), T, s)); \
         if (pending) { float *t_ = hc; hc = hx; hx = t_; }                                               \
         pending = NULL;                                                                                    \
+        if ((ps)->n32) CK(qh_rmsnorm(hc, (w), H, M, c->norm_eps, m->pf_hn, s));                          \
     } while (0)
     for (int l = 0; l < c->n_layers; ++l) {
         layer *Ly = &m->L[l];
-        PF_RESNORM(Ly->attn_norm, m->pf_xq_h);
+        PF_RESNORM(Ly->attn_norm, m->pf_xq_h, &m->pf_in[l]);
         CK(run_pf(m, &m->pf_in[l], M));
         if (Ly->is_attn) {
             const int64_t ai = Ly->attn_index;
@@ -952,9 +1075,10 @@ static int forward_prefill(qh_slm *m, int32_t cn) {
         }
         CK(run_pf(m, &m->pf_out[l], M));
         pending = m->pf_mix;
-        PF_RESNORM(Ly->ffn_norm, m->pf_xq_h);
+        PF_RESNORM(Ly->ffn_norm, m->pf_xq_h, &m->pf_ffn[l]);
         CK(run_pf(m, &m->pf_ffn[l], M));
         CK(qh_swiglu_q8k(m->pf_fgate, m->pf_fup, F, (int32_t)M, m->pf_xq_ffn, T, s));
+        if (m->pf_down[l].n32) CK(qh_swiglu(m->pf_fgate, m->pf_fup, m->pf_fact, M * F, s));
         CK(run_pf(m, &m->pf_down[l], M));
         pending = m->pf_mix;
     }

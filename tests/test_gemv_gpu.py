@@ -309,3 +309,24 @@ def test_fused_output_tail_equals_separate_kernels(qh, cuda, gt, no, n_tok):
                 assert torch.equal(h_got.view(torch.int32), h_ref.view(torch.int32)), "residual h + b"
         assert L.qh_check_device_error(None) == 0
         plan.close()
+
+
+@pytest.mark.parametrize("k,out_f,n_tok", [(64, 16, 1), (1024, 300, 3), (100, 33, 11)])
+def test_f32_weights_match_reference(qh, cuda, oracle, ref, k, out_f, n_tok):
+    """matmul_dispatch's F32 case (tensor_matmul_f32, slm/tensor.c:517):
+    float product and float add per element in index order."""
+    rng = np.random.default_rng(k + out_f)
+    w = rng.standard_normal((out_f, k)).astype(np.float32)
+    x = rng.standard_normal((n_tok, k)).astype(np.float32)
+    out = gpu_matmul(qh, cuda, 0, w.view(np.uint8).ravel(), k, out_f, x)
+    assert_bitwise(out, ref.matmul(0, w.view(np.uint8).ravel(), out_f, k, x), "f32 vs reference")
+    assert_bitwise(out, oracle.matmul(0, w.view(np.uint8).ravel(), out_f, k, x), "f32 vs oracle")
+
+
+@pytest.mark.parametrize("n_tok", [9, 17, 64, 70])
+def test_q8_0_many_tokens_bitexact(qh, cuda, oracle, n_tok):
+    """Q8_0 weights for more than 8 tokens (one launch over every token)."""
+    k, out_f = 1024, 48
+    w = qh.host.synth_blocks(Q8_0, out_f * (k // 32), 0x80 + n_tok)
+    x = qh.host.synth_normal(n_tok * k, 0x81 + n_tok).reshape(n_tok, k)
+    assert_bitwise(gpu_matmul(qh, cuda, Q8_0, w, k, out_f, x), oracle.matmul(Q8_0, w, out_f, k, x), "q8_0 many")
