@@ -67,6 +67,16 @@ void qh_slm_config_default(qh_slm_config *cfg, int32_t max_pos);
 typedef struct qh_blob qh_blob;
 
 int qh_blob_synthetic(const qh_slm_config *cfg, uint64_t seed, qh_blob **out);
+/* The same model with the weight types of a mix: QH_MIX_BASELINE (the one
+ * above), QH_MIX_Q4_K_M (the released Qwen3.5-0.8B Q4_K_M file's types,
+ * docs/DESIGN.md:96-119 of the reference: Q5_K attn_q / attn_qkv / ssm_out,
+ * Q6_K attn_v / ffn_down / token_embd, Q8_0 ssm_alpha / ssm_beta, Q4_K the
+ * rest) or QH_MIX_ALL_TYPES (F32, Q8_0, Q5_K, Q6_K matrices in roles where
+ * the released file has none, to exercise every matmul case of the model). */
+#define QH_MIX_BASELINE 0
+#define QH_MIX_Q4_K_M 1
+#define QH_MIX_ALL_TYPES 2
+int qh_blob_synthetic_mix(const qh_slm_config *cfg, uint64_t seed, int32_t mix, qh_blob **out);
 int qh_blob_count(const qh_blob *blob);
 /* Tensor i: GGUF name, GGUF type id, shape (shape[1] = 1 for vectors), host
  * data and byte size. Pointers stay valid until qh_blob_free. */

@@ -54,10 +54,14 @@ def _lib(build_dir):
     L.exp_rows.argtypes = [p, p, p, p, p, i64, C.POINTER(i64)]
     L.log_rows.restype = i64
     L.log_rows.argtypes = [p, C.c_uint, p, p, p, p, i64, C.POINTER(i64)]
+    L.log_rows_near.restype = i64
+    L.log_rows_near.argtypes = [p, C.c_uint, C.c_double, p, p, p, p, i64, C.POINTER(i64)]
     L.exp_count_all.restype = i64
     L.exp_count_all.argtypes = [p, p]
     L.log_count_all.restype = i64
     L.log_count_all.argtypes = [p]
+    L.set_log_exceptions.restype = None
+    L.set_log_exceptions.argtypes = [p, p, C.c_int]
     return L
 
 
@@ -143,12 +147,12 @@ def log_init():
     return th
 
 
-def log_collect(L, th, mask, maxn=2_000_000):
+def log_collect(L, th, mask, maxn=2_000_000, margin=0.0):
     I, K = np.zeros(maxn, np.int32), np.zeros(maxn, np.int32)
     Z, G = np.zeros(maxn), np.zeros(maxn, np.float32)
     n = C.c_int64()
-    mis = L.log_rows(th.ctypes.data, mask, I.ctypes.data, K.ctypes.data, Z.ctypes.data, G.ctypes.data, maxn,
-                     C.byref(n))
+    mis = L.log_rows_near(th.ctypes.data, mask, margin, I.ctypes.data, K.ctypes.data, Z.ctypes.data,
+                          G.ctypes.data, maxn, C.byref(n))
     k = min(n.value, maxn)
     return mis, (I[:k], K[:k], Z[:k], G[:k])
 
@@ -228,33 +232,69 @@ def log_scan_c(L, th, i, log):
     return th
 
 
+def log_joint_near(L, th, log, margin=2e-6, iters=30):
+    """All parameters at once against the mismatching inputs AND the matching
+    ones within `margin` ulps of a rounding boundary, so that a step cannot
+    break what it does not see; the trust region shrinks on rejection."""
+    var = np.array([i for i in range(16) if i != 9] + [16 + i for i in range(16) if i != 9] + [32, 33, 34])
+    scale = np.zeros(36)
+    scale[:16], scale[16:32] = 1e-12 * th[:16], 1e-12
+    scale[32], scale[33], scale[34] = 1e-8, 1e-9, 1e-10
+    scale *= 2.0 ** 60
+    mis, rows = log_collect(L, th, 0xffff, margin=margin)
+    for it in range(iters):
+        log(f"logf joint+near it {it}: {mis} mismatches, {len(rows[0])} rows")
+        if mis == 0:
+            break
+        th2 = log_step(th, rows, var, scale)
+        if th2 is None:
+            scale = scale * 0.5
+            continue
+        mis2, rows2 = log_collect(L, th2, 0xffff, margin=margin)
+        if mis2 >= mis:
+            scale = scale * 0.5
+            continue
+        th, mis, rows = th2, mis2, rows2
+    return th
+
+
 def _ulp_move(x, n):
     return float(np.nextafter(x, np.inf if n > 0 else -np.inf)) if n else x
 
 
 def log_polish(L, th, log):
-    """Single-ulp moves of logc_i (and the polynomial) while they remove mismatches."""
-    mis, rows = log_collect(L, th, 0xffff)
-    for rnd in range(50):
-        if mis == 0:
+    """Single-ulp moves while they remove mismatches: each table pair checked
+    on its own subinterval, then the polynomial on all of them."""
+    total, rows = log_collect(L, th, 0xffff)
+    for rnd in range(20):
+        if total == 0:
             break
-        subs = sorted(set(int(i) for i in rows[0]))
-        improved = False
-        for i in subs:
-            for j in (16 + i, i, 32, 33, 34):
+        before = total
+        for i in sorted(set(int(v) for v in rows[0])):
+            mis, _ = log_collect(L, th, 1 << i, maxn=1)
+            for j in (16 + i, i):
                 for step in (1, -1):
-                    t2 = th.copy()
-                    for _ in range(8):
+                    while mis:
+                        t2 = th.copy()
                         t2[j] = _ulp_move(t2[j], step)
-                        m2, r2 = log_collect(L, t2, 0xffff)
-                        if m2 < mis:
-                            th, mis, rows, improved = t2.copy(), m2, r2, True
-                        else:
+                        m2, _ = log_collect(L, t2, 1 << i, maxn=1)
+                        if m2 >= mis:
                             break
-        log(f"logf polish round {rnd}: {mis} mismatches")
-        if not improved:
+                        th, mis = t2, m2
+        total, rows = log_collect(L, th, 0xffff)
+        for j in (32, 33, 34):
+            for step in (1, -1):
+                while total:
+                    t2 = th.copy()
+                    t2[j] = _ulp_move(t2[j], step)
+                    m2, r2 = log_collect(L, t2, 0xffff)
+                    if m2 >= total:
+                        break
+                    th, total, rows = t2, m2, r2
+        log(f"logf polish round {rnd}: {total} mismatches")
+        if total >= before:
             break
-    return th, mis
+    return th, total
 
 
 def fit_logf(L, th=None, stage=0, save=None, log=print):
@@ -282,18 +322,51 @@ def fit_logf(L, th=None, stage=0, save=None, log=print):
         scale[32], scale[33], scale[34] = 1e-6, 1e-7, 1e-8
         th, m = log_fit(L, th, 0xffff, var, scale * 2.0 ** 60, 150, "joint", log, 3000, 60000)
         save and save(th, 3)
+    if stage <= 3:
+        th = log_joint_near(L, th, log)
+        save and save(th, 4)
     th, m = log_polish(L, th, log)
-    save and save(th, 4)
+    save and save(th, 5)
+    # What the fit leaves (inputs whose unrounded value lies within ~1e-6 ulp
+    # of a rounding boundary, where no parameter set near this one rounds
+    # every such input as the host does) is listed with the host's results.
+    exc = _log_exception_list(L, th)
+    log(f"logf: {len(exc)} inputs listed with the host's results")
+    ein = np.array([e[0] for e in exc], np.uint32)
+    eout = np.array([e[1] for e in exc], np.uint32)
+    L.set_log_exceptions(ein.ctypes.data, eout.ctypes.data, len(exc))
     total = L.log_count_all(th.ctypes.data)
     log(f"logf: {total} of 2^32 inputs differ from the host library")
+    save and save(th, 5, log_exceptions=[[hex(a), hex(b)] for a, b in exc])
     return th, total
+
+
+def _log_exception_list(L, th):
+    """(input bits, host result bits) of every positive finite input where the
+    candidate differs from the host library, sorted by input."""
+    import ctypes.util
+    libm = C.CDLL(ctypes.util.find_library("m"))
+    libm.logf.restype, libm.logf.argtypes = C.c_float, [C.c_float]
+    I, K, Z, G = log_collect(L, th, 0xffff)[1]
+    out = []
+    for z, k, g in zip(Z, K, G):
+        # the input is z * 2^k (z in [0x3f330000, 0x3f330000 + 2^23) as bits)
+        zb = int(np.float32(z).view(np.uint32))
+        if -126 <= int(k) + ((zb >> 23) - 127) <= 127:
+            xb = zb + (int(k) << 23)
+        else:  # subnormal input: z * 2^k is exact in float
+            xb = int(np.float32(np.float64(z) * 2.0 ** int(k)).view(np.uint32))
+        x = np.uint32(xb).view(np.float32)
+        assert np.float32(libm.logf(float(x))).view(np.uint32) == np.float32(g).view(np.uint32)
+        out.append((xb, int(np.float32(g).view(np.uint32))))
+    return sorted(out)
 
 
 def _hex(x):
     return float(x).hex()
 
 
-def write_header(p, tab, th):
+def write_header(p, tab, th, exc):
     lines = [
         "// SPDX-License-Identifier: MIT",
         "//",
@@ -333,6 +406,13 @@ def write_header(p, tab, th):
         "// logf: log(1 + r) ~ r + r^2 (kLogA2 + kLogA1 r + kLogA0 r^2).",
         f"constexpr double kLogA0 = {_hex(th[32])}, kLogA1 = {_hex(th[33])}, kLogA2 = {_hex(th[34])};",
         f"constexpr double kLn2 = {_hex(th[35])};",
+        "// logf: inputs (bits, ascending) whose result the fitted evaluation rounds",
+        "// the other way than the host library, and the host's results.",
+        f"constexpr int kLogExcN = {len(exc)};",
+        "static __device__ const uint32_t kLogExcIn[kLogExcN > 0 ? kLogExcN : 1] = {"
+        + ", ".join(f"0x{a:08x}u" for a, _ in exc) + "};",
+        "static __device__ const uint32_t kLogExcOut[kLogExcN > 0 ? kLogExcN : 1] = {"
+        + ", ".join(f"0x{b:08x}u" for _, b in exc) + "};",
         "",
         "}  // namespace libm",
         "}  // namespace qh",
@@ -359,7 +439,8 @@ def main():
     st = json.load(open(args.state)) if os.path.exists(args.state) else {}
     if args.write_only:
         write_header(np.array([float.fromhex(v) for v in st["expf"]]), exp2_table(),
-                     np.array([float.fromhex(v) for v in st["th"]]))
+                     np.array([float.fromhex(v) for v in st["th"]]),
+                     [(int(a, 16), int(b, 16)) for a, b in st.get("log_exceptions", [])])
         print("wrote", OUT)
         return
     L = _lib(args.build_dir)
@@ -385,7 +466,7 @@ def main():
     th, total = fit_logf(L, th, st.get("log_stage", 0), save, log)
     if total:
         sys.exit(f"logf: {total} inputs still differ; header not written")
-    write_header(p, tab, th)
+    write_header(p, tab, th, [(int(a, 16), int(b, 16)) for a, b in st.get("log_exceptions", [])])
     print("wrote", OUT)
 
 

@@ -114,8 +114,35 @@ static inline int log_split(uint32_t ix, int *i, int *k, double *z) {
     return 1;
 }
 
+static double log_eval(uint32_t ix, const double *th) {
+    int i, k;
+    double z;
+    log_split(ix, &i, &k, &z);
+    double r = fma(z, th[i], -1.0);
+    double y0 = fma((double)k, th[35], th[16 + i]);
+    double r2 = r * r;
+    double y = fma(th[33], r, th[34]);
+    y = fma(th[32], r2, y);
+    return fma(y, r2, y0 + r);
+}
+
+// Inputs where the fitted evaluation rounds the other way than the host
+// library, with the host's results (sorted by input bits); see fit.py.
+static const uint32_t *g_exc_in, *g_exc_out;
+static int g_exc_n;
+void set_log_exceptions(const uint32_t *in, const uint32_t *out, int n) {
+    g_exc_in = in;
+    g_exc_out = out;
+    g_exc_n = n;
+}
+
 float cand_logf(float x, const double *th) {
     uint32_t ix = asu(x);
+    for (int lo = 0, hi = g_exc_n; lo < hi;) {
+        int mid = (lo + hi) / 2;
+        if (g_exc_in[mid] == ix) return asf(g_exc_out[mid]);
+        if (g_exc_in[mid] < ix) lo = mid + 1; else hi = mid;
+    }
     if (ix == 0x3f800000u) return 0.0f;
     if (ix - 0x00800000u >= 0x7f800000u - 0x00800000u) {
         if (ix * 2u == 0) return -INFINITY;
@@ -134,9 +161,19 @@ float cand_logf(float x, const double *th) {
     return (float)y;
 }
 
-// Mismatching positive finite inputs whose subinterval is in `mask`.
+// Mismatching positive finite inputs whose subinterval is in `mask`; with
+// margin > 0 also the matching ones whose unrounded candidate lies within
+// margin ulps of a rounding boundary (the constraints a small parameter
+// change could break).
+int64_t log_rows_near(const double *th, unsigned mask, double margin, int *I, int *K, double *Z, float *G,
+                      int64_t maxn, int64_t *nrows);
 int64_t log_rows(const double *th, unsigned mask, int *I, int *K, double *Z, float *G, int64_t maxn,
                  int64_t *nrows) {
+    return log_rows_near(th, mask, 0.0, I, K, Z, G, maxn, nrows);
+}
+
+int64_t log_rows_near(const double *th, unsigned mask, double margin, int *I, int *K, double *Z, float *G,
+                      int64_t maxn, int64_t *nrows) {
     int64_t mis = 0, cnt = 0;
 #pragma omp parallel for reduction(+ : mis) schedule(dynamic, 1)
     for (int64_t hi = 0; hi < (1 << 15); hi++) {
@@ -148,8 +185,17 @@ int64_t log_rows(const double *th, unsigned mask, int *I, int *K, double *Z, flo
             log_split(ix, &i, &k, &z);
             if (!((mask >> i) & 1)) continue;
             float g = logf(asf(ix));
-            if (asu(g) == asu(cand_logf(asf(ix), th))) continue;
-            mis++;
+            if (asu(g) == asu(cand_logf(asf(ix), th))) {
+                if (margin <= 0) continue;
+                double y = log_eval(ix, th);
+                float f = (float)y;
+                double up = nextafterf(f, INFINITY), dn = nextafterf(f, -INFINITY);
+                double ulp = up - (double)f;
+                double dist = fmin(fabs(y - ((double)f + up) / 2), fabs(y - ((double)f + dn) / 2));
+                if (dist > margin * ulp) continue;
+            } else {
+                mis++;
+            }
             int64_t n;
 #pragma omp atomic capture
             n = cnt++;

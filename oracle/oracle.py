@@ -25,7 +25,6 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libqhref.so")
-REF_CR_SO = os.path.join(HERE, "_ref", "libqhref_crlibm.so")
 
 Q8_0, Q4_K, Q5_K, Q6_K = 8, 12, 13, 14
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210, Q8_0: 34}
@@ -34,10 +33,21 @@ BLOCK_WEIGHTS = {Q4_K: 256, Q5_K: 256, Q6_K: 256, Q8_0: 32}
 _P, _I, _I64, _F = C.c_void_p, C.c_int, C.c_int64, C.c_float
 
 
+def reference_root():
+    """The reference's source tree: $QH_REF_ROOT, else a directory named
+    `reference` beside this repository; None when neither exists (test
+    machines use the prebuilt _ref/ libraries)."""
+    for cand in (os.environ.get("QH_REF_ROOT"), os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")):
+        if cand and os.path.isdir(os.path.join(cand, "slm")):
+            return cand
+    return None
+
+
 def build(force: bool = False) -> None:
     """make -C oracle (liboracle.so; _ref/libqhref.so when the reference exists)."""
     if force or not os.path.exists(ORACLE_SO):
-        subprocess.run(["make", "-s", "-C", HERE], check=True)
+        root = reference_root()
+        subprocess.run(["make", "-s", "-C", HERE] + ([f"REF_ROOT={root}"] if root else []), check=True)
 
 
 def _ptr(a: np.ndarray) -> C.c_void_p:
@@ -99,7 +109,7 @@ class Oracle:
         L.orc_matmul.restype = _I
         L.orc_sample_with.argtypes = [_P, _I64, _P, _P, _P, _P, C.c_int32]
         L.orc_sample_with.restype = C.c_int32
-        L.orc_chunked_step.argtypes = [_I, _I, _P, _P, _P, _P, _P, _P, _P, _I]
+        L.orc_chunked_step.argtypes = [_I, _I, _P, _P, _P, _P, _P, _P, _P]
         L.orc_chunked_step.restype = _I
         L.orc_libm_mismatches.argtypes = [_I, C.c_uint32, _I64, _P, C.POINTER(C.c_uint32)]
         L.orc_libm_mismatches.restype = _I64
@@ -113,12 +123,11 @@ class Oracle:
         n = self.L.orc_libm_mismatches(fn, first, vals.size, vals.ctypes.data, C.byref(bad))
         return int(n), (int(bad.value) if n else None)
 
-    def chunked_prefill(self, q, k, v, g_log, beta, state, cr: bool = True):
+    def chunked_prefill(self, q, k, v, g_log, beta, state):
         """slm_forward_ssm_batch's chunk loop (slm/qwen.c:777-806) for one head:
         q, k, v [n][hd], g_log, beta [n]; state [hd][hd] is updated in place.
-        Returns out [n][hd]. cr selects correctly rounded expf (the device's)."""
-        return _chunked_loop(lambda *a: self.L.orc_chunked_step(*a, 1 if cr else 0),
-                             q, k, v, g_log, beta, state)
+        Returns out [n][hd]."""
+        return _chunked_loop(lambda *a: self.L.orc_chunked_step(*a), q, k, v, g_log, beta, state)
 
     def sample_with(self, logits: np.ndarray, sp: dict, st: np.ndarray, hist) -> int:
         """Restated sample_with on `logits` (float32, penalized in place) with
@@ -218,12 +227,11 @@ class Ref:
     """The reference's own C code (oracle/_ref/libqhref.so)."""
 
     @staticmethod
-    def available(crlibm: bool = False) -> bool:
-        return os.path.exists(REF_CR_SO if crlibm else REF_SO)
+    def available() -> bool:
+        return os.path.exists(REF_SO)
 
-    def __init__(self, crlibm: bool = False):
-        """crlibm=True loads the build whose expf/logf are correctly rounded."""
-        path = REF_CR_SO if crlibm else REF_SO
+    def __init__(self):
+        path = REF_SO
         if not os.path.exists(path):
             build(force=True)
         L = C.CDLL(path)

@@ -376,8 +376,8 @@ int orc_matmul(int type, const uint8_t *w, int64_t out_f, int64_t k,
 // Sampler chain: sample_with (slm/sampler.c:134-180) with the generator of
 // slm/model.c:414-447. fp = {temperature, top_p, min_p, repetition_penalty},
 // ip = {top_k, repetition_window}, st = generator words (advanced in place).
-// Logits are penalized in place. The exponential is exp in double rounded
-// once to float (correctly rounded expf), like the device kernel.
+// Logits are penalized in place. The exponential is the host C library's
+// expf, as the reference's (and the device kernel's, bit for bit).
 // ---------------------------------------------------------------------------
 
 static uint64_t orc_rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
@@ -447,7 +447,7 @@ int32_t orc_sample_with(float *lg, int64_t n, const float *fp, const int32_t *ip
         if (val[j] > m) m = val[j];
     float sum = 0.0f;
     for (int j = 0; j < filled; j++) {
-        val[j] = (float)exp((double)((val[j] - m) / temp));
+        val[j] = expf((val[j] - m) / temp);
         sum += val[j];
     }
     if (sum > 0.0f)
@@ -499,17 +499,13 @@ int32_t orc_sample_with(float *lg, int64_t n, const float *fp, const int32_t *ip
 // the forward substitution) leave a finite running sum unchanged and are
 // skipped. K*beta, V*beta, K*beta*gexp and Q*gexp are recomputed where used
 // (the same rounded products the reference stores).
-//
-// cr = 0: expf from the host libm (as the reference built here);
-// cr = 1: correctly rounded expf (double exp rounded once), as the device.
+// expf is the host C library's, as the reference's.
 // ---------------------------------------------------------------------------
 #define ORC_CH 64
 #define ORC_HD 128
 
-static float orc_expf(float x, int cr) { return cr ? (float)exp((double)x) : expf(x); }
-
 int orc_chunked_step(int n, int hd, const float *q, const float *k, const float *v, const float *g_log,
-                     const float *beta, float *state, float *out, int cr) {
+                     const float *beta, float *state, float *out) {
     if (n < 1 || n > ORC_CH || hd < 1 || hd > ORC_HD) return -1;
     static float gcs[ORC_CH], gexp[ORC_CH], diff[ORC_CH];
     static float kk[ORC_CH][ORC_CH], A[ORC_CH][ORC_CH], kq[ORC_CH][ORC_CH];
@@ -520,14 +516,14 @@ int orc_chunked_step(int n, int hd, const float *q, const float *k, const float 
     for (int t = 0; t < n; t++) {
         acc += g_log[t];
         gcs[t] = acc;
-        gexp[t] = orc_expf(acc, cr);
+        gexp[t] = expf(acc);
     }
     // kk[i][j] = (K_j . (K_i*beta_i)) * exp(gcs_i - gcs_j), j < i (chunked.c:340-358)
     for (int i = 0; i < n; i++)
         for (int j = 0; j < i; j++) {
             float s = 0.0f;
             for (int d = 0; d < hd; d++) s += k[j * hd + d] * (k[i * hd + d] * beta[i]);
-            kk[i][j] = s * orc_expf(gcs[i] - gcs[j], cr);
+            kk[i][j] = s * expf(gcs[i] - gcs[j]);
         }
     // forward substitution (I + kk) X = -kk, then A = X + I on and below the
     // diagonal (chunked.c:224-238, 364-386): column j, rows i > j, terms
@@ -558,7 +554,7 @@ int orc_chunked_step(int n, int hd, const float *q, const float *k, const float 
         for (int j = 0; j <= i; j++) {
             float s = 0.0f;
             for (int d = 0; d < hd; d++) s += k[j * hd + d] * q[i * hd + d];
-            kq[i][j] = s * (i == j ? 1.0f : orc_expf(gcs[i] - gcs[j], cr));
+            kq[i][j] = s * (i == j ? 1.0f : expf(gcs[i] - gcs[j]));
         }
     // attn_inter = (Q*gexp) S; v_new = V_eff - k_cumdecay S (chunked.c:445-484)
     for (int t = 0; t < n; t++)
@@ -580,8 +576,8 @@ int orc_chunked_step(int n, int hd, const float *q, const float *k, const float 
             out[t * hd + e] = inter[t][e] + s;
         }
     // S = S * exp(gcs_last) + (K * exp(gcs_last - gcs))^T v_new (chunked.c:503-522)
-    const float gl = gcs[n - 1], gle = orc_expf(gl, cr);
-    for (int t = 0; t < n; t++) diff[t] = orc_expf(gl - gcs[t], cr);
+    const float gl = gcs[n - 1], gle = expf(gl);
+    for (int t = 0; t < n; t++) diff[t] = expf(gl - gcs[t]);
     for (int d = 0; d < hd; d++)
         for (int e = 0; e < hd; e++) {
             float s = 0.0f;

@@ -25,20 +25,6 @@
 //   slm_forward_batch (chunked prefill)          slm/qwen.c:1018-1106
 //   chunked_ssm_step_f32                        slm/chunked.c:287-523
 
-// Built twice by oracle/Makefile: libqhref.so is the reference as shipped;
-// libqhref_crlibm.so (-DQH_CR_LIBM) is the same sources with expf/logf
-// resolved to correctly rounded versions (double-precision exp/log rounded
-// once to float). The host glibc's expf/logf are not correctly rounded for
-// ~6e-4 of inputs; the device kernels evaluate them correctly rounded, so
-// the second build isolates that libm difference from everything else.
-#ifdef QH_CR_LIBM
-#include <math.h>
-static float qh_cr_expf(float x) { return (float)exp((double)x); }
-static float qh_cr_logf(float x) { return (float)log((double)x); }
-#define expf qh_cr_expf
-#define logf qh_cr_logf
-#endif
-
 #include "slm/qwen.c"
 #include "slm/sampler.c"
 

@@ -131,6 +131,7 @@ class SlmConfig(C.Structure):
 SIGNATURES.update({
     "qh_slm_config_default": (None, [C.POINTER(SlmConfig), C.c_int32]),
     "qh_blob_synthetic": (_I, [C.POINTER(SlmConfig), _U64, C.POINTER(C.c_void_p)]),
+    "qh_blob_synthetic_mix": (_I, [C.POINTER(SlmConfig), _U64, C.c_int32, C.POINTER(C.c_void_p)]),
     "qh_blob_count": (_I, [_P]),
     "qh_blob_tensor": (_I, [_P, _I, C.POINTER(C.c_char_p), C.POINTER(C.c_int32), C.POINTER(_I64),
                            C.POINTER(C.c_void_p), C.POINTER(_I64)]),

@@ -25,7 +25,10 @@
 // 2^(i/32) table is computed from its definition, and the polynomials and the
 // log table were measured against the host library by oracle/libm/fit.py,
 // which moves textbook starting values until the result equals the host's
-// on every float input. tests/test_libm_gpu.py compares these device
+// on every float input. For logf a handful of inputs remain whose unrounded
+// value lies within ~1e-6 ulp of a rounding boundary and which no nearby
+// parameter set rounds as the host does; they are listed with the host's
+// results and looked up first. tests/test_libm_gpu.py compares these device
 // functions with the host library over all 2^32 inputs.
 //
 // Every double operation is an explicit round-to-nearest intrinsic, so the
@@ -71,6 +74,16 @@ __device__ __forceinline__ float logf_ref(float x) {
         if (ix == 0x7f800000u) return x;                                // +inf
         if ((ix & 0x80000000u) || ix * 2u >= 0xff000000u) return __uint_as_float(0xffc00000u);  // < 0, nan
         ix = __float_as_uint(__fmul_rn(x, 0x1p23f)) - (23u << 23);      // subnormal
+    }
+    if (kLogExcN > 0) {  // the measured inputs the evaluation below rounds the other way
+        const uint32_t xb = __float_as_uint(x);
+        int lo = 0, hi = kLogExcN;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            const uint32_t v = __ldg(&kLogExcIn[mid]);
+            if (v == xb) return __uint_as_float(__ldg(&kLogExcOut[mid]));
+            if (v < xb) lo = mid + 1; else hi = mid;
+        }
     }
     const uint32_t tmp = ix - 0x3f330000u;
     const int i = static_cast<int>((tmp >> 19) & 15u);

@@ -172,8 +172,35 @@ static int add_vector(qh_blob *b, uint64_t seed, const char *name, int64_t s0, i
     return QH_OK;
 }
 
+// Weight types of the mixes (roles in the order of the table below).
+enum { R_EMBD, R_FFN_GATE, R_FFN_UP, R_FFN_DOWN, R_Q, R_K, R_V, R_O, R_QKV, R_GATE, R_ALPHA, R_BETA, R_SSM_OUT, R_N };
+static const int32_t k_mix[3][R_N] = {
+    // Q4_K mostly, Q6_K for ffn_down and the tied embedding / head
+    {QH_GGUF_Q6_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q6_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K,
+     QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K},
+    // the released Q4_K_M file's types (Qwen3.5-0.8B): Q5_K attn_q / attn_qkv / ssm_out, Q6_K attn_v,
+    // Q8_0 ssm_alpha / ssm_beta
+    {QH_GGUF_Q6_K, QH_GGUF_Q4_K, QH_GGUF_Q4_K, QH_GGUF_Q6_K, QH_GGUF_Q5_K, QH_GGUF_Q4_K, QH_GGUF_Q6_K,
+     QH_GGUF_Q4_K, QH_GGUF_Q5_K, QH_GGUF_Q4_K, QH_GGUF_Q8_0, QH_GGUF_Q8_0, QH_GGUF_Q5_K},
+    // every computed type in some role, including fp32 matrices and Q8_0 outputs
+    {QH_GGUF_F32, QH_GGUF_Q5_K, QH_GGUF_Q6_K, QH_GGUF_Q5_K, QH_GGUF_Q6_K, QH_GGUF_F32, QH_GGUF_Q8_0,
+     QH_GGUF_Q8_0, QH_GGUF_Q6_K, QH_GGUF_Q5_K, QH_GGUF_F32, QH_GGUF_Q8_0, QH_GGUF_Q8_0},
+};
+
+static int add_weight(qh_blob *b, uint64_t seed, const char *name, int32_t type, int64_t k, int64_t n) {
+    if (type != QH_GGUF_F32) return add_matrix(b, seed, name, type, k, n);
+    blob_tensor *t = blob_add(b, name, QH_GGUF_F32, k, n);
+    if (!t) return QH_ERR_INVALID;
+    return qh_synth_normal(seed ^ name_hash(name), k * n, 0.0f, 0.02f, (float *)t->data);
+}
+
 int qh_blob_synthetic(const qh_slm_config *c, uint64_t seed, qh_blob **out) {
-    if (!c || !out) return QH_ERR_INVALID;
+    return qh_blob_synthetic_mix(c, seed, QH_MIX_BASELINE, out);
+}
+
+int qh_blob_synthetic_mix(const qh_slm_config *c, uint64_t seed, int32_t mix, qh_blob **out) {
+    if (!c || !out || mix < 0 || mix > 2) return QH_ERR_INVALID;
+    const int32_t *ty = k_mix[mix];
     *out = NULL;
     if (c->hidden % 256 || c->ffn % 256 || c->n_layers <= 0 || c->vocab <= 0 || c->head_dim <= 0)
         return QH_ERR_INVALID;
@@ -184,33 +211,33 @@ int qh_blob_synthetic(const qh_slm_config *c, uint64_t seed, qh_blob **out) {
     char nm[64];
     int rc = 0;
 #define CHK(x) do { rc = (x); if (rc) goto fail; } while (0)
-    CHK(add_matrix(b, seed, "token_embd.weight", QH_GGUF_Q6_K, H, c->vocab));
+    CHK(add_weight(b, seed, "token_embd.weight", ty[R_EMBD], H, c->vocab));
     CHK(add_vector(b, seed, "output_norm.weight", H, 1, VEC_NORM, 0.02f));
     for (int L = 0; L < c->n_layers; ++L) {
         const int attn = (L % c->full_attn_interval) == c->full_attn_interval - 1;
 #define NAME(s) (snprintf(nm, sizeof(nm), "blk.%d." s, L), nm)
         CHK(add_vector(b, seed, NAME("attn_norm.weight"), H, 1, VEC_NORM, 0.02f));
         CHK(add_vector(b, seed, NAME("post_attention_norm.weight"), H, 1, VEC_NORM, 0.02f));
-        CHK(add_matrix(b, seed, NAME("ffn_gate.weight"), QH_GGUF_Q4_K, H, F));
-        CHK(add_matrix(b, seed, NAME("ffn_up.weight"), QH_GGUF_Q4_K, H, F));
-        CHK(add_matrix(b, seed, NAME("ffn_down.weight"), QH_GGUF_Q6_K, F, H));
+        CHK(add_weight(b, seed, NAME("ffn_gate.weight"), ty[R_FFN_GATE], H, F));
+        CHK(add_weight(b, seed, NAME("ffn_up.weight"), ty[R_FFN_UP], H, F));
+        CHK(add_weight(b, seed, NAME("ffn_down.weight"), ty[R_FFN_DOWN], F, H));
         if (attn) {
-            CHK(add_matrix(b, seed, NAME("attn_q.weight"), QH_GGUF_Q4_K, H, 2 * c->n_heads * hd));
-            CHK(add_matrix(b, seed, NAME("attn_k.weight"), QH_GGUF_Q4_K, H, c->n_kv_heads * hd));
-            CHK(add_matrix(b, seed, NAME("attn_v.weight"), QH_GGUF_Q4_K, H, c->n_kv_heads * hd));
+            CHK(add_weight(b, seed, NAME("attn_q.weight"), ty[R_Q], H, 2 * c->n_heads * hd));
+            CHK(add_weight(b, seed, NAME("attn_k.weight"), ty[R_K], H, c->n_kv_heads * hd));
+            CHK(add_weight(b, seed, NAME("attn_v.weight"), ty[R_V], H, c->n_kv_heads * hd));
             CHK(add_vector(b, seed, NAME("attn_q_norm.weight"), hd, 1, VEC_NORM, 0.02f));
             CHK(add_vector(b, seed, NAME("attn_k_norm.weight"), hd, 1, VEC_NORM, 0.02f));
-            CHK(add_matrix(b, seed, NAME("attn_output.weight"), QH_GGUF_Q4_K, c->n_heads * hd, H));
+            CHK(add_weight(b, seed, NAME("attn_output.weight"), ty[R_O], c->n_heads * hd, H));
         } else {
-            CHK(add_matrix(b, seed, NAME("attn_qkv.weight"), QH_GGUF_Q4_K, H, conv_dim));
-            CHK(add_matrix(b, seed, NAME("attn_gate.weight"), QH_GGUF_Q4_K, H, kdim));
+            CHK(add_weight(b, seed, NAME("attn_qkv.weight"), ty[R_QKV], H, conv_dim));
+            CHK(add_weight(b, seed, NAME("attn_gate.weight"), ty[R_GATE], H, kdim));
             CHK(add_vector(b, seed, NAME("ssm_a"), c->gdn_heads, 1, VEC_NEG_EXP, 0.02f));
-            CHK(add_matrix(b, seed, NAME("ssm_alpha.weight"), QH_GGUF_Q4_K, H, c->gdn_heads));
-            CHK(add_matrix(b, seed, NAME("ssm_beta.weight"), QH_GGUF_Q4_K, H, c->gdn_heads));
+            CHK(add_weight(b, seed, NAME("ssm_alpha.weight"), ty[R_ALPHA], H, c->gdn_heads));
+            CHK(add_weight(b, seed, NAME("ssm_beta.weight"), ty[R_BETA], H, c->gdn_heads));
             CHK(add_vector(b, seed, NAME("ssm_conv1d.weight"), c->conv_kernel, conv_dim, VEC_NORMAL, 0.5f));
             CHK(add_vector(b, seed, NAME("ssm_dt.bias"), c->gdn_heads, 1, VEC_NORMAL, 0.02f));
             CHK(add_vector(b, seed, NAME("ssm_norm.weight"), c->gdn_head_dim, 1, VEC_NORM, 0.02f));
-            CHK(add_matrix(b, seed, NAME("ssm_out.weight"), QH_GGUF_Q4_K, kdim, H));
+            CHK(add_weight(b, seed, NAME("ssm_out.weight"), ty[R_SSM_OUT], kdim, H));
         }
 #undef NAME
     }

@@ -275,12 +275,25 @@ class Blob:
     """Weight blob: synthetic (qh_blob_synthetic) or read from a GGUF file
     (Blob.from_gguf, qh_gguf_load)."""
 
-    def __init__(self, cfg: SlmConfig, seed: int = None, handle=None):
+    def __init__(self, cfg: SlmConfig, seed: int = None, handle=None, mix: int = 0):
+        """mix: 0 BASELINE types, 1 the released Q4_K_M file's types, 2 every type (qh_blob_synthetic_mix)."""
         if handle is None:
             h = C.c_void_p()
-            check(lib().qh_blob_synthetic(C.byref(cfg), seed, C.byref(h)), "qh_blob_synthetic")
+            check(lib().qh_blob_synthetic_mix(C.byref(cfg), seed, mix, C.byref(h)), "qh_blob_synthetic_mix")
             handle = h
         self.handle, self.cfg = handle, cfg
+
+    @classmethod
+    def empty(cls, cfg: SlmConfig):
+        """An empty blob to fill with add() (qh_blob_create)."""
+        h = C.c_void_p()
+        check(lib().qh_blob_create(C.byref(h)), "qh_blob_create")
+        return cls(cfg, handle=h)
+
+    def add(self, name: str, gtype: int, shape, data: bytes):
+        """qh_blob_add: copies the tensor's bytes."""
+        sh = (C.c_int64 * 2)(*shape)
+        check(lib().qh_blob_add(self.handle, name.encode(), gtype, sh, data, len(data)), "qh_blob_add")
 
     @classmethod
     def from_gguf(cls, path: str, max_pos_cap: int = 0):

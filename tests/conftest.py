@@ -48,15 +48,6 @@ def ref():
 
 
 @pytest.fixture(scope="session")
-def ref_cr():
-    """The reference built with correctly rounded expf/logf (oracle/Makefile)."""
-    from oracle.oracle import Ref
-    if not Ref.available(crlibm=True):
-        pytest.skip("oracle/_ref/libqhref_crlibm.so not built (reference sources absent)")
-    return Ref(crlibm=True)
-
-
-@pytest.fixture(scope="session")
 def cuda(qh):
     import torch
     if not torch.cuda.is_available():

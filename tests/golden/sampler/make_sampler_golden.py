@@ -4,9 +4,9 @@ sampler chain.
 
     python tests/golden/sampler/make_sampler_golden.py
 
-Runs in the build container, where oracle/_ref/libqhref_crlibm.so is the
-reference compiled from its sources (oracle/Makefile) with a correctly
-rounded expf -- the exponential the device kernel and the oracle evaluate.
+Runs in the build container, where oracle/_ref/libqhref.so is the
+reference compiled from its sources (oracle/Makefile), its expf the host C
+library's -- the exponential the device kernel and the oracle evaluate too.
 For every case of tests/sampler_cases.py it stores the reference's picks,
 generator words and penalized-logits digests (sample_with,
 slm/sampler.c:134-180; rng_seed / rng_uniform, slm/model.c:431-447). The
@@ -31,7 +31,7 @@ import sampler_cases as sc  # noqa: E402
 
 def main():
     host = load_pkg().host
-    ref = Ref(crlibm=True)
+    ref = Ref()
     picks, states, digests, names = [], [], [], []
     for name, vocab, rows in sc.cases():
         p, s, d = sc.run(ref.sample_with, ref.rng_seed, host, name, vocab, rows)

@@ -11,7 +11,7 @@ QH_PREFILL_CHUNKED) against the reference's batched prompt path.
 3. The model with QH_PREFILL_CHUNKED against the reference's own
    slm_forward_batch (the LLM_USE_FORWARD_BATCH prefill, slm/qwen.c:1018)
    followed by slm_forward_step: greedy picks and every logit vector
-   bit-identical (ref_cr: expf/logf correctly rounded, as the device).
+   bit-identical (the stock build: the device's expf/logf are the host library's).
 """
 import ctypes as C
 
@@ -80,7 +80,7 @@ def test_chunked_kernel_matches_oracle(qh, cuda, oracle, n_seq, heads, n_tok, sp
     out, st = run_chunked(qh, qkv, beta, glog, state, n_seq, n_tok, heads, splits)
     for (s, h), (q, k, v, g, b, s0) in per.items():
         s_want = s0.copy()
-        want = oracle.chunked_prefill(q, k, v, g, b, s_want, cr=True)
+        want = oracle.chunked_prefill(q, k, v, g, b, s_want)
         got = out[s * n_tok:(s + 1) * n_tok, h * HD:(h + 1) * HD]
         assert np.array_equal(bits(got), bits(want)), f"outputs of sequence {s} head {h} differ from the oracle"
         assert np.array_equal(bits(st[s, h]), bits(s_want)), f"state of sequence {s} head {h} differs"
@@ -148,11 +148,11 @@ def test_chunk_prep_matches_restatement(qh, cuda):
             assert np.array_equal(got_ring[s, p % kk], qkv[s * n_tok + (p - pos0)]), "ring slot not left raw"
 
 
-def ref_batch_then_steps(ref_cr, cfg, tensors, prompt, n_new):
+def ref_batch_then_steps(ref, cfg, tensors, prompt, n_new):
     """slm_forward_batch over prompt[:-1], then greedy slm_forward_step from
     the last prompt token: picks and logits of every step."""
     from oracle.oracle import RefModel
-    rm = RefModel(ref_cr, cfg, tensors)
+    rm = RefModel(ref, cfg, tensors)
     n = len(prompt)
     rm.forward_batch(prompt[:-1], 0)
     picks, logits = [], []
@@ -185,14 +185,14 @@ def small200(qh, cuda):
 
 
 @pytest.mark.parametrize("B,n_prompt,chunk", [(1, 13, 0), (3, 150, 0), (2, 150, 5), (1, 66, 64)])
-def test_chunked_prefill_matches_reference_forward_batch(qh, cuda, ref_cr, small200, B, n_prompt, chunk):
+def test_chunked_prefill_matches_reference_forward_batch(qh, cuda, ref, small200, B, n_prompt, chunk):
     cfg, blob, tensors = small200
     n_new = 6
     rng = np.random.default_rng(60 + n_prompt + B)
     prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
     got, lg = chunked_device_run(qh, cfg, blob, prompts, n_new, chunk)
     for b in range(B):
-        want, wl = ref_batch_then_steps(ref_cr, cfg, tensors, prompts[b], n_new)
+        want, wl = ref_batch_then_steps(ref, cfg, tensors, prompts[b], n_new)
         assert np.array_equal(got[b], want[:n_new]), f"seq {b}: greedy picks after the chunked prefill differ"
         assert np.array_equal(bits(lg[b]), bits(wl[n_new])), f"seq {b}: logits after the chunked prefill differ"
 
@@ -213,7 +213,7 @@ def test_chunked_prefill_differs_from_stepwise(qh, cuda, small200):
     assert not np.array_equal(bits(lc), bits(ls))
 
 
-def test_chunked_prefill_full_model(qh, cuda, ref_cr):
+def test_chunked_prefill_full_model(qh, cuda, ref):
     """BASELINE config-4 shape (24 layers, vocab 151936), 64-token prompt:
     the chunked prefill then 8 greedy steps, logits bit-identical to the
     reference's slm_forward_batch + slm_forward_step."""
@@ -222,7 +222,7 @@ def test_chunked_prefill_full_model(qh, cuda, ref_cr):
     rng = np.random.default_rng(0xC5)
     prompt = rng.integers(0, cfg.vocab, 64).astype(np.int32)
     got, lg = chunked_device_run(qh, cfg, blob, prompt[None, :], 8)
-    want, wl = ref_batch_then_steps(ref_cr, cfg, blob.tensors(), prompt, 8)
+    want, wl = ref_batch_then_steps(ref, cfg, blob.tensors(), prompt, 8)
     blob.close()
     assert np.array_equal(got[0], want[:8])
     assert np.array_equal(bits(lg[0]), bits(wl[8]))

@@ -3,8 +3,8 @@
 oracle/qh_oracle.c) to the reference's own chunked_ssm_step_f32
 (slm/chunked.c:287-523, compiled from its sources into oracle/_ref), run in
 slm_forward_ssm_batch's 64-token chunk loop with the state carried
-(slm/qwen.c:777-806). Bit-exact, outputs and final state, with the host
-libm (ref) and with correctly rounded expf (ref_cr, the device's)."""
+(slm/qwen.c:777-806). Bit-exact, outputs and final state, both on the
+host C library's expf."""
 import os
 
 import numpy as np
@@ -18,13 +18,11 @@ def bits(a):
 
 
 @pytest.mark.parametrize("n", [1, 2, 17, 63, 64, 65, 130, 200])
-@pytest.mark.parametrize("which", ["ref", "ref_cr"])
-def test_oracle_chunked_matches_reference(n, which, oracle, request):
-    r = request.getfixturevalue(which)
+def test_oracle_chunked_matches_reference(n, oracle, ref):
     q, k, v, g, b, s0 = chunk_inputs(n, 128, 1000 + n)
     s_ref, s_orc = s0.copy(), s0.copy()
-    o_ref = r.chunked_prefill(q, k, v, g, b, s_ref)
-    o_orc = oracle.chunked_prefill(q, k, v, g, b, s_orc, cr=(which == "ref_cr"))
+    o_ref = ref.chunked_prefill(q, k, v, g, b, s_ref)
+    o_orc = oracle.chunked_prefill(q, k, v, g, b, s_orc)
     assert np.array_equal(bits(o_orc), bits(o_ref)), "chunk outputs differ from the reference"
     assert np.array_equal(bits(s_orc), bits(s_ref)), "carried state differs from the reference"
 
@@ -34,7 +32,7 @@ def test_oracle_chunked_small_head_and_zero_state(oracle, ref):
     s_ref = np.zeros((32, 32), np.float32)
     s_orc = s_ref.copy()
     o_ref = ref.chunked_prefill(q, k, v, g, b, s_ref)
-    o_orc = oracle.chunked_prefill(q, k, v, g, b, s_orc, cr=False)
+    o_orc = oracle.chunked_prefill(q, k, v, g, b, s_orc)
     assert np.array_equal(bits(o_orc), bits(o_ref)) and np.array_equal(bits(s_orc), bits(s_ref))
 
 
@@ -45,7 +43,7 @@ def test_chunked_close_to_recurrent_update(oracle):
     n, hd = 130, 128
     q, k, v, g, b, s0 = chunk_inputs(n, hd, 3)
     s = s0.copy()
-    out = oracle.chunked_prefill(q, k, v, g, b, s, cr=True)
+    out = oracle.chunked_prefill(q, k, v, g, b, s)
     S = s0.astype(np.float64)
     want = np.empty((n, hd))
     for t in range(n):
@@ -69,7 +67,7 @@ def test_chunk_step_rejects_sizes_outside_one_chunk(n, oracle, ref):
     s = np.zeros((hd, hd), np.float32)
     o = np.zeros((max(n, 1), hd), np.float32)
     P = lambda x: C.c_void_p(x.ctypes.data)
-    assert oracle.L.orc_chunked_step(n, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o), 1) == -1
+    assert oracle.L.orc_chunked_step(n, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o)) == -1
     assert ref.L.ref_chunked_step(n, hd, hd, P(a), P(a), P(a), P(v), P(v), P(s), P(o)) == -1
 
 
@@ -77,8 +75,7 @@ GOLDEN_CHUNKED = os.path.join(os.path.dirname(__file__), "golden", "chunked", "c
 
 
 @pytest.mark.parametrize("name", ["c70_hd64", "c9_hd128"])
-@pytest.mark.parametrize("tag", ["libm", "cr"])
-def test_oracle_chunked_matches_golden(name, tag, oracle):
+def test_oracle_chunked_matches_golden(name, oracle):
     """Against fixtures the reference's own chunk step wrote
     (tests/golden/chunked/make_chunked_golden.py): runs without the
     reference library, here and on the GPU box."""
@@ -87,6 +84,6 @@ def test_oracle_chunked_matches_golden(name, tag, oracle):
     q, k, v, gl, b = (g[f"{name}_{x}"] for x in ("q", "k", "v", "g", "beta"))
     hd = q.shape[1]
     st = np.zeros((hd, hd), np.float32)
-    out = oracle.chunked_prefill(q, k, v, gl, b, st, cr=(tag == "cr"))
-    assert np.array_equal(bits(out), bits(g[f"{name}_out_{tag}"])), "outputs differ from the reference's"
-    assert hashlib.sha256(st.tobytes()).hexdigest() == str(g[f"{name}_state_sha_{tag}"]), "final state differs"
+    out = oracle.chunked_prefill(q, k, v, gl, b, st)
+    assert np.array_equal(bits(out), bits(g[f"{name}_out"])), "outputs differ from the reference's"
+    assert hashlib.sha256(st.tobytes()).hexdigest() == str(g[f"{name}_state_sha"]), "final state differs"

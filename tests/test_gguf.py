@@ -134,3 +134,111 @@ def test_device_model_from_gguf(qh, cuda, written):
         slm.close()
     back.close()
     assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.fixture(scope="module", params=[1, 2], ids=["q4_k_m_mix", "all_types"])
+def written_mix(qh, tmp_path_factory, request):
+    """A GGUF whose weights carry the released Q4_K_M file's types (Q5_K,
+    Q6_K, Q8_0 beside Q4_K), or every type the matmuls compute (F32 too)."""
+    cfg = qh.host.slm_config(48, n_layers=4, vocab=1024)
+    blob = qh.host.Blob(cfg, 0x6612F + request.param, mix=request.param)
+    path = str(tmp_path_factory.mktemp("gguf") / f"mix{request.param}.gguf")
+    blob.write_gguf(path)
+    return cfg, blob, path, request.param
+
+
+def test_mix_types_written_and_read_back(qh, written_mix):
+    cfg, blob, path, mix = written_mix
+    types = {n: t for n, t, *_ in blob.tensors()}
+    if mix == 1:
+        assert types["blk.0.attn_qkv.weight"] == 13 and types["blk.0.ssm_alpha.weight"] == 8
+        assert types["blk.3.attn_v.weight"] == 14 and types["blk.3.attn_q.weight"] == 13
+    else:
+        assert types["token_embd.weight"] == 0 and types["blk.3.attn_k.weight"] == 0
+    back = qh.host.Blob.from_gguf(path)
+    assert [x[:3] for x in tensor_bytes(back)] == [x[:3] for x in tensor_bytes(blob)]
+    back.close()
+
+
+def test_reference_loader_reads_mix(ref, written_mix):
+    """The reference's loader binds the mixed-type file; its steps equal the
+    reference over the in-memory tensors (matmul_dispatch per type)."""
+    from oracle.oracle import RefModel
+    cfg, blob, path, _ = written_mix
+    rg, _, _ = RefModel.from_gguf(ref, path)
+    rm = RefModel(ref, cfg, blob.tensors())
+    tok = 11
+    for pos in range(8):
+        a0, l0 = rm.step(tok, pos, want_logits=True)
+        a1, l1 = rg.step(tok, pos, want_logits=True)
+        assert a0 == a1 and np.array_equal(l0, l1), pos
+        tok = a0
+    rm.close()
+    rg.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [1, 3, 12])
+def test_device_model_mix_matches_reference_gguf(qh, cuda, ref, written_mix, B):
+    """The device model over the loaded mixed-type file (every projection by
+    its own GGUF type; B = 12 runs the K-quants on the tensor-core GEMM) gives
+    the logits, bit for bit, of the stock reference loading the same file."""
+    from oracle.oracle import RefModel
+    cfg, _, path, _ = written_mix
+    back = qh.host.Blob.from_gguf(path)
+    rng = np.random.default_rng(B)
+    n_prompt, n_new = 6, 10
+    prompts = rng.integers(0, cfg.vocab, (B, n_prompt)).astype(np.int32)
+    slm = qh.host.Slm(back.cfg, back, B)
+    gl = []
+    tok = prompts[:, 0].copy()
+    preds = []
+    for pos in range(n_prompt + n_new - 1):
+        nxt, lg = slm.step(tok, pos, want_logits=True)
+        preds.append(nxt.copy())
+        gl.append(lg.copy())
+        tok = prompts[:, pos + 1] if pos + 1 < n_prompt else nxt
+    slm.close()
+    preds = np.stack(preds, 1)
+    for b in sorted({0, B - 1}):
+        rg, _, _ = RefModel.from_gguf(ref, path)
+        t = prompts[b, 0]
+        for pos in range(n_prompt + n_new - 1):
+            a, lr = rg.step(int(t), pos, want_logits=True)
+            assert a == preds[b, pos], f"seq {b} step {pos}: pick {preds[b, pos]} vs reference {a}"
+            assert np.array_equal(gl[pos][b].view(np.uint32), lr.view(np.uint32)), f"seq {b} step {pos} logits"
+            t = prompts[b, pos + 1] if pos + 1 < n_prompt else a
+        rg.close()
+    back.close()
+
+
+@pytest.mark.gpu
+def test_model_rejects_a_type_it_does_not_compute(qh, cuda):
+    """Tensors are checked when the model is created: an embedding table of
+    a type the row reader does not take (Q4_K; the reference reads only Q6_K
+    or F32 rows there, slm/qwen.c:885-907) is QH_ERR_UNSUPPORTED, a matrix of
+    another shape QH_ERR_INVALID; a tensor of a type no matmul computes (F16)
+    is refused when added (the reference aborts on it, slm/model.c:259-261)."""
+    cfg = qh.host.slm_config(16, n_layers=4, vocab=512)
+    src = qh.host.Blob(cfg, 5)
+    for bad in ("embd_type", "shape"):
+        b = qh.host.Blob.empty(cfg)
+        for name, typ, shape, ptr, nb in src.tensors():
+            data = C.string_at(ptr, nb)
+            if bad == "embd_type" and name == "token_embd.weight":
+                typ = 12
+                data = bytes((shape[0] // 256) * 144 * shape[1])
+            if bad == "shape" and name == "blk.0.ffn_gate.weight":
+                shape = (shape[0], shape[1] - 256)
+                data = data[:nb // cfg.ffn * (cfg.ffn - 256)]
+            b.add(name, typ, shape, data)
+        with pytest.raises(qh.QHError) as e:
+            qh.host.Slm(cfg, b, 1)
+        assert e.value.status == (-2 if bad == "embd_type" else -1), bad
+        b.close()
+    b = qh.host.Blob.empty(cfg)
+    with pytest.raises(qh.QHError) as e:
+        b.add("x", 1, (256, 4), bytes(256 * 4 * 2))
+    assert e.value.status == -2
+    b.close()
+    src.close()

@@ -7,13 +7,10 @@ Bar (north star): greedy token streams identical, except that a divergence
 is exempt at a step where the reference's top-2 logit gap is below 1e-3;
 comparison stops at the first exempt step.
 
-Two builds of the reference are used. `ref_cr` is the reference's sources
-with expf/logf correctly rounded, the arithmetic the device kernels
-implement: against it the bar above is asserted over the full BASELINE
-config-4 run. `ref` is the stock build on the host glibc, whose expf/logf
-are off by one ulp for ~6e-4 of inputs; the model's Q8_K activation
-quantization turns such ulps into int8 flips in later layers, so against
-it the test records where the streams part and asserts the start.
+The reference is its stock build (oracle/_ref/libqhref.so, the host C
+library's expf/logf, which the device reproduces bit for bit): on the full
+BASELINE config-4 run every one of the 319 logit vectors is asserted
+bit-identical, beyond the bar.
 """
 import numpy as np
 import pytest
@@ -70,12 +67,12 @@ def small(qh, cuda):
     return cfg, blob, blob.tensors()
 
 
-def test_small_model_batch1_parity(qh, cuda, ref_cr, small):
+def test_small_model_batch1_parity(qh, cuda, ref, small):
     from oracle.oracle import RefModel
     cfg, blob, tensors = small
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, cfg.vocab, 12).astype(np.int32)
-    rp, rg, rl = ref_run(ref_cr, RefModel, cfg, tensors, prompt, 20)
+    rp, rg, rl = ref_run(ref, RefModel, cfg, tensors, prompt, 20)
     slm = qh.host.Slm(cfg, blob, 1)
     gp, gl = gpu_run(slm, prompt[None, :], 20)
     n = check_stream(rp, rg, gp[0], "small b1")
@@ -86,7 +83,7 @@ def test_small_model_batch1_parity(qh, cuda, ref_cr, small):
     slm.close()
 
 
-def test_small_model_batched_sequences_independent(qh, cuda, ref_cr, small):
+def test_small_model_batched_sequences_independent(qh, cuda, ref, small):
     """8 sequences in one batch each match their own reference run."""
     from oracle.oracle import RefModel
     cfg, blob, tensors = small
@@ -96,7 +93,7 @@ def test_small_model_batched_sequences_independent(qh, cuda, ref_cr, small):
     slm = qh.host.Slm(cfg, blob, B)
     gp, _ = gpu_run(slm, prompts, n_new)
     for b in range(B):
-        rp, rg, _ = ref_run(ref_cr, RefModel, cfg, tensors, prompts[b], n_new)
+        rp, rg, _ = ref_run(ref, RefModel, cfg, tensors, prompts[b], n_new)
         check_stream(rp, rg, gp[b], f"seq {b}")
     slm.close()
 
@@ -193,16 +190,19 @@ def full(qh, cuda):
     return cfg, blob, blob.tensors(), prompt, gp[0], gl[0]
 
 
-def test_full_model_greedy_parity_config4(qh, cuda, ref_cr, full):
-    """full-size model, 64-token prompt, 256 greedy tokens."""
+def test_full_model_greedy_parity_config4(qh, cuda, ref, full):
+    """full-size model, 64-token prompt, 256 greedy
+    tokens, against the stock reference: the greedy stream meets the bar and
+    every logit vector is bit-identical."""
     from oracle.oracle import RefModel
     cfg, blob, tensors, prompt, gp, gl = full
-    rp, rg, rl = ref_run(ref_cr, RefModel, cfg, tensors, prompt, 256)
+    rp, rg, rl = ref_run(ref, RefModel, cfg, tensors, prompt, 256)
     n = check_stream(rp, rg, gp, "config 4")
     exact = sum(np.array_equal(gl[i].view(np.uint32), rl[i].view(np.uint32)) for i in range(n))
-    print(f"config 4 vs correctly rounded libm: {n} of {len(rp)} predictions equal, "
+    print(f"config 4 vs the stock reference: {n} of {len(rp)} predictions equal, "
           f"{exact} steps with bit-identical logits")
-    assert n == len(rp) or rg[n] < GAP
+    assert n == len(rp), f"streams part at step {n} (top-2 gap {rg[n]:.3g})"
+    assert exact == len(rp), f"{len(rp) - exact} logit vectors differ"
 
 
 def test_full_model_vs_stock_libm_reference(qh, cuda, ref, full):

@@ -4,7 +4,7 @@ sample_with (slm/sampler.c:134-180).
 
 CPU: the restatement in oracle/qh_oracle.c against the committed golden
 picks (tests/golden/sampler/sampler.npz, made by the reference compiled from its
-sources with a correctly rounded expf) and against the live reference; the
+sources, expf the host C library's) and against the live reference; the
 product's host-side helpers (defaults, generator seeding).
 GPU: qh_sample on the device against the same golden picks, generator words
 and penalized logits, three successive draws per row with the generator
@@ -52,10 +52,10 @@ def test_oracle_sampler_matches_golden(qh, oracle, ci):
 
 
 @pytest.mark.parametrize("ci", [0, 5, 9, 14])
-def test_oracle_sampler_matches_live_reference(qh, oracle, ref_cr, ci):
+def test_oracle_sampler_matches_live_reference(qh, oracle, ref, ci):
     name, vocab, rows = CASES[ci]
     a = sc.run(oracle.sample_with, qh.host.rng_seed, qh.host, name, vocab, rows)
-    b = sc.run(ref_cr.sample_with, ref_cr.rng_seed, qh.host, name, vocab, rows)
+    b = sc.run(ref.sample_with, ref.rng_seed, qh.host, name, vocab, rows)
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) and a[2] == b[2]
 
 
@@ -169,7 +169,7 @@ def ref_generate(ref, RefModel, cfg, tensors, prompt, max_new, min_new, sp, seed
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("setting", ["defaults", "k256_plain", "tight"])
-def test_generate_sampled_matches_reference(qh, cuda, ref_cr, setting):
+def test_generate_sampled_matches_reference(qh, cuda, ref, setting):
     """qh_slm_generate_sampled on three sequences against the reference's
     generation loop, token for token (small 4-layer model, vocab 4096).
     eos/eot are set to tokens the model favours, so the min_new masking and
@@ -194,7 +194,7 @@ def test_generate_sampled_matches_reference(qh, cuda, ref_cr, setting):
                                  stop_ids=stops)
     slm.close()
     for b in range(B):
-        want = ref_generate(ref_cr, RefModel, cfg, tensors, prompts[b], max_new, min_new, sp.as_dict(),
+        want = ref_generate(ref, RefModel, cfg, tensors, prompts[b], max_new, min_new, sp.as_dict(),
                             int(seeds[b]), eos, eot, stops)
         assert np.array_equal(got[b], want), f"sequence {b}: {got[b].tolist()} != {want.tolist()}"
         assert np.array_equal(again[b], got[b]), "re-seeded run differs"

@@ -31,7 +31,7 @@ def device_steps(slm, toks, pos0):
 
 
 @pytest.mark.parametrize("B", [2, 12])
-def test_snapshot_restore_matches_reference(qh, cuda, ref_cr, model, B):
+def test_snapshot_restore_matches_reference(qh, cuda, ref, model, B):
     from oracle.oracle import RefModel
     cfg, blob, tensors = model
     rng = np.random.default_rng(40 + B)
@@ -53,7 +53,7 @@ def test_snapshot_restore_matches_reference(qh, cuda, ref_cr, model, B):
     slm.close()
     assert np.array_equal(bits(la2), bits(la)), "replay after restore differs"
     for b in range(min(B, 2)):
-        rm = RefModel(ref_cr, cfg, tensors)
+        rm = RefModel(ref, cfg, tensors)
         for i in range(n_p):
             rm.step(int(prompt[b, i]), i)
         rs = rm.snapshot(n_p)

@@ -25,7 +25,7 @@ def read(path):
 
 
 @pytest.mark.parametrize("B,seq", [(1, 0), (3, 1), (12, 7)])
-def test_trace_matches_reference(qh, cuda, ref_cr, tmp_path, B, seq):
+def test_trace_matches_reference(qh, cuda, ref, tmp_path, B, seq):
     from oracle.oracle import RefModel
     cfg = qh.host.slm_config(32, n_layers=4, vocab=4096)
     blob = qh.host.Blob(cfg, 0x7A + B)
@@ -41,7 +41,7 @@ def test_trace_matches_reference(qh, cuda, ref_cr, tmp_path, B, seq):
     # the step after the traced one runs from the graph again and agrees
     nxt = slm.step(np.full(B, 3, np.int32), 6)
     slm.close()
-    rm = RefModel(ref_cr, cfg, blob.tensors())
+    rm = RefModel(ref, cfg, blob.tensors())
     for p in range(5):
         rm.step(int(prompt[seq, p]), p)
     ref_path = str(tmp_path / "ref.jsonl")
