@@ -31,6 +31,18 @@ extern "C" {
  * QH_ERR_UNSUPPORTED for another architecture or tensor type. */
 int qh_gguf_load(const char *path, int32_t max_pos_cap, qh_slm_config *cfg, qh_blob **out);
 
+/* Special token ids of a GGUF file, as slm_model_load binds them: bos/eos
+ * from tokenizer.ggml.bos_token_id / eos_token_id (default 0; slm/qwen.c:
+ * 150-155), eot = the id of "<|im_end|>" (-1 if absent) and the stop set =
+ * the ids of "<|endoftext|>", "<|im_end|>", "<|fim_pad|>", "<|repo_name|>",
+ * "<|file_sep|>" present in tokenizer.ggml.tokens (slm/model.c:1153-1178). */
+typedef struct qh_special_tokens {
+    int32_t bos_id, eos_id, eot_id;
+    int32_t n_stop;
+    int32_t stop_ids[8];
+} qh_special_tokens;
+int qh_gguf_special_tokens(const char *path, qh_special_tokens *out);
+
 /* Writes cfg and every tensor of blob as a GGUF v3 file with
  * general.architecture = "qwen35", the qwen35.* keys above,
  * context_length = cfg->max_pos, a placeholder tokenizer.ggml.tokens

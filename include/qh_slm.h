@@ -134,6 +134,17 @@ int qh_slm_picks(qh_slm *m, int32_t from_pos, int32_t n, int32_t *out);
  * conv kernel 4 (QH_ERR_UNSUPPORTED otherwise). Synchronous. */
 int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt);
 
+/* qh_slm_prefill for a prompt that continues every sequence at position
+ * pos (the caches of positions 0..pos-1 kept; pos == 0 starts afresh):
+ * prompt[s][i] is the input of position pos + i, and the last prompt token
+ * is left as the input of the next step (position pos + n_prompt - 1). In
+ * QH_PREFILL_CHUNKED mode pos must be a multiple of 64 (the chunk grid);
+ * QH_ERR_UNSUPPORTED otherwise. Synchronous. */
+int qh_slm_prefill_at(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t pos);
+
+/* Position of the next step (its input token is already set). */
+int32_t qh_slm_position(const qh_slm *m);
+
 /* Tokens per sequence in one prompt chunk (0 = the default: 8192 rows over
  * all sequences); only before the first qh_slm_prefill. */
 int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq);
@@ -181,6 +192,21 @@ int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t 
 int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t max_new, int32_t min_new,
                             const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
                             const int32_t *stop_ids, int32_t n_stop, int32_t *out, int32_t *n_out);
+
+/* The sampled decode loop of qh_slm_generate_sampled in pieces, for a
+ * caller that inspects every token (stop rules, streaming) and continues
+ * sequences across calls as slm_generate_raw does (slm/slm.c:237-361):
+ *   qh_slm_sample_setup  sampler, eos/eot masking for the first min_new
+ *                        steps from the current position, the history
+ *                        hist[s][0..n_hist) every sequence's penalty window
+ *                        starts with, and seeds (as qh_slm_generate_sampled);
+ *   qh_slm_sample_steps  n_steps sampled steps from the current position,
+ *                        each fed the previous step's sample (after the
+ *                        pending input); out[s][i] the sample of step i.
+ * Synchronous. */
+int qh_slm_sample_setup(qh_slm *m, const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
+                        int32_t min_new, const int32_t *hist, int32_t n_hist);
+int qh_slm_sample_steps(qh_slm *m, int32_t n_steps, int32_t *out);
 
 /* Snapshot / restore of every sequence's decode state (slm_ctx_snapshot,
  * slm_ctx_restore, slm_snapshot_free; slm/model.c:1262-1371), held in device

@@ -149,6 +149,10 @@ SIGNATURES.update({
     "qh_slm_memory": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64)]),
     "qh_slm_begin": (_I, [_P, _P, C.c_int32]),
     "qh_slm_prefill": (_I, [_P, _P, C.c_int32]),
+    "qh_slm_prefill_at": (_I, [_P, _P, C.c_int32, C.c_int32]),
+    "qh_slm_position": (C.c_int32, [_P]),
+    "qh_slm_sample_setup": (_I, [_P, C.POINTER(Sampler), _P, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32]),
+    "qh_slm_sample_steps": (_I, [_P, C.c_int32, _P]),
     "qh_slm_set_prefill_chunk": (_I, [_P, C.c_int32]),
     "qh_slm_set_prefill_mode": (_I, [_P, C.c_int32]),
     "qh_slm_advance": (_I, [_P, C.c_int32]),
@@ -206,6 +210,46 @@ SIGNATURES.update({  # include/qh_kernels.h
                                      C.c_int32, _P, _P]),
 })
 
+class SlmSampler(C.Structure):
+    """struct slm_sampler (include/slm.h)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("repetition_window", C.c_int)]
+
+
+class SlmCtrl(C.Structure):
+    """struct slm_ctrl (include/slm.h)."""
+    _fields_ = [("tools", C.c_bool), ("think", C.c_bool), ("effort", C.c_char_p), ("debug", C.c_int32),
+                ("trace_tokens", C.c_bool), ("dump_layer", C.c_int32)]
+
+
+SLM_TOKEN_FN = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
+
+SIGNATURES.update({  # include/slm.h: the reference's slm.h entry points
+    "slm_model_load": (_P, [C.c_char_p]),
+    "slm_model_unload": (None, [_P]),
+    "slm_model_loaded": (C.c_bool, [_P]),
+    "slm_model_error": (C.c_char_p, [_P]),
+    "slm_ctx_create": (_P, [_P]),
+    "slm_ctx_destroy": (None, [_P]),
+    "slm_ctx_snapshot": (_P, [_P]),
+    "slm_ctx_restore": (None, [_P, _P]),
+    "slm_snapshot_free": (None, [_P]),
+    "slm_sampler_defaults": (SlmSampler, []),
+    "slm_ctrl_defaults": (SlmCtrl, []),
+    "slm_ctx_ctrl": (C.POINTER(SlmCtrl), [_P]),
+    "slm_generate_ids": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, C.POINTER(SlmSampler), _U64, SLM_TOKEN_FN,
+                                   _P]),
+    "slm_ctx_tokens": (C.POINTER(C.c_int32), [_P, C.POINTER(C.c_int32)]),
+    "slm_vocab_size": (C.c_int, [_P]),
+    "slm_eos_id": (C.c_int, [_P]),
+    "slm_bos_id": (C.c_int, [_P]),
+    "slm_pp_per_sec": (C.c_double, [_P]),
+    "slm_tg_per_sec": (C.c_double, [_P]),
+    "slm_n_prefill": (C.c_int32, [_P]),
+    "slm_n_generated": (C.c_int32, [_P]),
+    "qh_gguf_special_tokens": (_I, [C.c_char_p, _P]),
+})
+
 _lib = None
 
 
@@ -234,5 +278,5 @@ def row_bytes(gtype: int, k: int) -> int:
 
 from . import host  # noqa: E402  (host-side helpers over the bindings)
 
-__all__ = ["lib", "check", "QHError", "MatvecJob", "host", "row_bytes",
+__all__ = ["lib", "check", "QHError", "MatvecJob", "host", "row_bytes", "SlmSampler", "SlmCtrl", "SLM_TOKEN_FN",
            "F32", "Q8_0", "Q4_K", "Q5_K", "Q6_K", "BLOCK_BYTES", "BLOCK_WEIGHTS"]

@@ -255,6 +255,73 @@ done:
     return rc;
 }
 
+// The special token ids slm_model_load binds: bos/eos from their keys
+// (default 0, slm/qwen.c:150-155), eot = the id of "<|im_end|>" and the
+// end-of-generation set from the vocabulary strings (slm/model.c:1153-1178),
+// -1 / empty when absent.
+int qh_gguf_special_tokens(const char *path, qh_special_tokens *out) {
+    if (!path || !out) return QH_ERR_INVALID;
+    memset(out, 0, sizeof(*out));
+    out->eot_id = -1;
+    FILE *f = fopen(path, "rb");
+    if (!f) return QH_ERR_INVALID;
+    uint8_t *buf = NULL;
+    long sz = -1;
+    if (fseek(f, 0, SEEK_END) == 0) sz = ftell(f);
+    if (sz > 0 && fseek(f, 0, SEEK_SET) == 0) {
+        buf = (uint8_t *)malloc((size_t)sz);
+        if (buf && fread(buf, 1, (size_t)sz, f) != (size_t)sz) { free(buf); buf = NULL; }
+    }
+    fclose(f);
+    if (!buf) return QH_ERR_INVALID;
+    int rc = QH_ERR_INVALID;
+    rd r = {buf, (size_t)sz, 0, 0};
+    const uint32_t magic = (uint32_t)rd_uint(&r, 4), version = (uint32_t)rd_uint(&r, 4);
+    rd_uint(&r, 8);
+    const uint64_t n_kv = rd_uint(&r, 8);
+    kv_ref *kv = NULL;
+    if (r.bad || magic != 0x46554747u || version != 3 || n_kv > (uint64_t)sz) goto done;
+    kv = (kv_ref *)calloc((size_t)n_kv + 1, sizeof(kv_ref));
+    if (!kv) goto done;
+    for (uint64_t i = 0; i < n_kv && !r.bad; ++i) {
+        kv[i].key = rd_str(&r, &kv[i].klen);
+        kv[i].type = (uint32_t)rd_uint(&r, 4);
+        kv[i].at = r.c;
+        rd_skip_value(&r, kv[i].type);
+    }
+    if (r.bad) goto done;
+    out->bos_id = (int32_t)kv_int(&r, kv, n_kv, "tokenizer.ggml.bos_token_id", 0);
+    out->eos_id = (int32_t)kv_int(&r, kv, n_kv, "tokenizer.ggml.eos_token_id", 0);
+    {
+        static const char *const stops[] = {"<|endoftext|>", "<|im_end|>", "<|fim_pad|>", "<|repo_name|>",
+                                            "<|file_sep|>"};
+        int32_t found[5] = {-1, -1, -1, -1, -1};
+        const kv_ref *tk = find_kv(kv, n_kv, "tokenizer.ggml.tokens");
+        if (tk && tk->type == VT_ARR) {
+            rd tr = r;
+            tr.c = tk->at;
+            const uint32_t et = (uint32_t)rd_uint(&tr, 4);
+            const uint64_t n = rd_uint(&tr, 8);
+            for (uint64_t i = 0; et == VT_STR && i < n && !tr.bad; ++i) {
+                uint64_t l;
+                const char *t = rd_str(&tr, &l);
+                for (int j = 0; j < 5 && !tr.bad; ++j)
+                    if (found[j] < 0 && l == strlen(stops[j]) && memcmp(t, stops[j], (size_t)l) == 0)
+                        found[j] = (int32_t)i;
+            }
+            if (tr.bad) goto done;
+        }
+        out->eot_id = found[1];
+        for (int j = 0; j < 5; ++j)
+            if (found[j] >= 0) out->stop_ids[out->n_stop++] = found[j];
+    }
+    rc = QH_OK;
+done:
+    free(kv);
+    free(buf);
+    return rc;
+}
+
 // ---------------------------------------------------------------------------
 // writer
 // ---------------------------------------------------------------------------

@@ -882,29 +882,35 @@ int qh_slm_step(qh_slm *m, const int32_t *h_tokens, int32_t pos, int32_t *h_next
     return QH_OK;
 }
 
-int qh_slm_begin(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
-    if (!m || !prompt || n_prompt <= 0 || n_prompt > m->cfg.max_pos) return QH_ERR_INVALID;
+// Prompt tokens prompt[s][0..n_prompt) as the inputs of positions
+// p0 .. p0 + n_prompt - 1. p0 == 0 starts every sequence afresh (the conv
+// ring and recurrent state are read before they are written, so they are
+// cleared); p0 > 0 continues the sequences where the last step left them.
+static int begin_at(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t p0) {
+    if (!m || !prompt || n_prompt <= 0 || p0 < 0 || p0 + n_prompt > m->cfg.max_pos) return QH_ERR_INVALID;
     const int32_t B = m->B, P = m->cfg.max_pos;
     for (int64_t i = 0; i < (int64_t)B * n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab) return QH_ERR_INVALID;
-    // position 0 starts every sequence afresh: the conv ring and recurrent
-    // state are read before they are written, so they are cleared
-    CK(qh_slm_reset(m));
-    // prompt[s][i] -> d_prompt[s][i] (row pitch max_pos)
-    if (cudaMemcpy2DAsync(m->d_prompt, (size_t)P * 4, prompt, (size_t)n_prompt * 4, (size_t)n_prompt * 4,
+    if (p0 == 0) CK(qh_slm_reset(m));
+    // prompt[s][i] -> d_prompt[s][p0 + i] (row pitch max_pos)
+    if (cudaMemcpy2DAsync(m->d_prompt + p0, (size_t)P * 4, prompt, (size_t)n_prompt * 4, (size_t)n_prompt * 4,
                           (size_t)B, cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
         return QH_ERR_CUDA;
     CK(qh_stream_sync(m->stream));  // the pinned staging buffers below are reused
     for (int32_t b = 0; b < B; ++b) m->h_tok[b] = prompt[(int64_t)b * n_prompt];
-    m->h_ctl[0] = 0;
-    m->h_ctl[1] = n_prompt;
+    m->h_ctl[0] = p0;
+    m->h_ctl[1] = p0 + n_prompt;
     CK(qh_memcpy_h2d(m->d_ctl, m->h_ctl, 2 * sizeof(int32_t), m->stream));
     CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * B, m->stream));
     CK(qh_stream_sync(m->stream));
-    m->host_pos = 0;
-    m->n_prompt = n_prompt;
+    m->host_pos = p0;
+    m->n_prompt = p0 + n_prompt;
     return QH_OK;
 }
+
+int qh_slm_begin(qh_slm *m, const int32_t *prompt, int32_t n_prompt) { return begin_at(m, prompt, n_prompt, 0); }
+
+int32_t qh_slm_position(const qh_slm *m) { return m ? m->host_pos : -1; }
 
 int qh_slm_advance(qh_slm *m, int32_t n_steps) {
     if (!m || n_steps < 0 || m->host_pos + n_steps > m->cfg.max_pos) return QH_ERR_INVALID;
@@ -1100,21 +1106,23 @@ int qh_slm_set_prefill_mode(qh_slm *m, int32_t mode) {
     return QH_OK;
 }
 
-int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
-    CK(qh_slm_begin(m, prompt, n_prompt));
+int qh_slm_prefill_at(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t pos) {
+    CK(begin_at(m, prompt, n_prompt, pos));
     const int32_t n_ctx = n_prompt - 1;  // the last prompt token is the next step's input
     if (n_ctx == 0) return QH_OK;
     const qh_slm_config *c = &m->cfg;
     if (c->head_dim != 128 || c->gdn_head_dim != 128 || c->conv_kernel != 4) return QH_ERR_UNSUPPORTED;
+    // the chunk algebra counts its 64-token chunks from position 0
+    if (m->pf_mode == QH_PREFILL_CHUNKED && pos % 64) return QH_ERR_UNSUPPORTED;
     CK(ensure_prefill(m));
     const int32_t B = m->B, C = m->pf_chunk;
     int32_t *tok = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * C);
     if (!tok) return QH_ERR_INVALID;
     int rc = QH_OK;
-    for (int32_t p0 = 0; p0 < n_ctx && !rc; p0 += C) {
-        const int32_t cn = n_ctx - p0 < C ? n_ctx - p0 : C;
+    for (int32_t j0 = 0; j0 < n_ctx && !rc; j0 += C) {
+        const int32_t cn = n_ctx - j0 < C ? n_ctx - j0 : C, p0 = pos + j0;
         for (int32_t b = 0; b < B; ++b)
-            for (int32_t j = 0; j < cn; ++j) tok[(int64_t)b * cn + j] = prompt[(int64_t)b * n_prompt + p0 + j];
+            for (int32_t j = 0; j < cn; ++j) tok[(int64_t)b * cn + j] = prompt[(int64_t)b * n_prompt + j0 + j];
         // pageable sources: the copies are staged before these calls return
         rc = qh_memcpy_h2d(m->pf_tok, tok, sizeof(int32_t) * (size_t)B * cn, m->stream);
         if (!rc) rc = qh_memcpy_h2d(m->pf_pos, &p0, sizeof(int32_t), m->stream);
@@ -1122,16 +1130,20 @@ int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
     }
     free(tok);
     if (rc) return rc;
-    // next step: position n_ctx, input the last prompt token
+    // next step: position pos + n_ctx, input the last prompt token
     for (int32_t b = 0; b < B; ++b) m->h_tok[b] = prompt[(int64_t)b * n_prompt + n_ctx];
-    m->h_ctl[0] = n_ctx;
-    m->h_ctl[1] = n_prompt;
+    m->h_ctl[0] = pos + n_ctx;
+    m->h_ctl[1] = pos + n_prompt;
     CK(qh_memcpy_h2d(m->d_ctl, m->h_ctl, 2 * sizeof(int32_t), m->stream));
     CK(qh_memcpy_h2d(m->d_tok, m->h_tok, sizeof(int32_t) * B, m->stream));
     CK(qh_stream_sync(m->stream));
     CK(qh_check_device_error(NULL));
-    m->host_pos = n_ctx;
+    m->host_pos = pos + n_ctx;
     return QH_OK;
+}
+
+int qh_slm_prefill(qh_slm *m, const int32_t *prompt, int32_t n_prompt) {
+    return qh_slm_prefill_at(m, prompt, n_prompt, 0);
 }
 
 int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t *out) {
@@ -1146,35 +1158,20 @@ int qh_slm_generate(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t 
     return qh_slm_picks(m, n_prompt - 1, n_new, out);
 }
 
-int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t max_new, int32_t min_new,
-                            const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
-                            const int32_t *stop_ids, int32_t n_stop, int32_t *out, int32_t *n_out) {
-    if (!m || !prompt || !sp || !out || !n_out || n_prompt <= 0 || max_new < 0 || n_stop < 0 ||
-        (n_stop > 0 && !stop_ids) || n_prompt >= m->cfg.max_pos)
-        return QH_ERR_INVALID;
-    const int32_t B = m->B, P = m->cfg.max_pos, n = n_prompt;
-    // slm_generate_raw's decode loop runs while pos < max_position
-    const int32_t n_gen = max_new < P - n ? max_new : P - n;
-    // prompt at positions 0..n-1, then the decode loop re-feeds the last
-    // prompt token at position n: a prefill of the prompt plus that token
-    // leaves exactly this state with the token pending at position n
-    int32_t *ext = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * (n + 1));
+int qh_slm_sample_setup(qh_slm *m, const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
+                        int32_t min_new, const int32_t *hist, int32_t n_hist) {
+    if (!m || !sp || n_hist < 0 || n_hist > m->cfg.max_pos || (n_hist > 0 && !hist)) return QH_ERR_INVALID;
+    const int32_t B = m->B, P = m->cfg.max_pos;
+    int rc = QH_OK;
     int32_t *hn = (int32_t *)malloc(sizeof(int32_t) * (size_t)B);
     uint64_t *st = (uint64_t *)malloc(16 * (size_t)B);
-    int32_t *picks = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * (n_gen > 0 ? n_gen : 1));
-    int rc = (ext && hn && st && picks) ? QH_OK : QH_ERR_INVALID;
-    if (!rc) {
-        for (int32_t b = 0; b < B; ++b) {
-            memcpy(ext + (int64_t)b * (n + 1), prompt + (int64_t)b * n, sizeof(int32_t) * (size_t)n);
-            ext[(int64_t)b * (n + 1) + n] = prompt[(int64_t)b * n + n - 1];
-            hn[b] = n;
-        }
-        rc = qh_slm_prefill(m, ext, n + 1);
-    }
-    // the repetition-penalty history starts as this call's prompt (slm/slm.c:257-263)
-    if (!rc && cudaMemcpy2DAsync(m->d_hist, (size_t)(P + 1) * 4, prompt, (size_t)n * 4, (size_t)n * 4, (size_t)B,
-                                 cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
+    if (!hn || !st) rc = QH_ERR_INVALID;
+    // the repetition-penalty history (slm/slm.c:257-263)
+    if (!rc && n_hist > 0 &&
+        cudaMemcpy2DAsync(m->d_hist, (size_t)(P + 1) * 4, hist, (size_t)n_hist * 4, (size_t)n_hist * 4, (size_t)B,
+                          cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
         rc = QH_ERR_CUDA;
+    for (int32_t b = 0; b < B && !rc; ++b) hn[b] = n_hist;
     if (!rc) rc = qh_memcpy_h2d(m->d_hist_n, hn, sizeof(int32_t) * (size_t)B, m->stream);
     // a non-zero seed re-seeds a sequence's generator; zero continues it
     if (!rc && seeds) {
@@ -1191,16 +1188,51 @@ int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, 
         sc.eos_id = eos_id;
         sc.eot_id = eot_id;
         sc.min_new = min_new;
-        sc.gen0 = n;
+        sc.gen0 = m->host_pos;  // the next step is the first sampled one
         rc = qh_memcpy_h2d(m->d_sctl, &sc, sizeof(sc), m->stream);
         if (!rc) rc = qh_stream_sync(m->stream);
     }
-    if (!rc && n_gen > 0) {
-        m->sampling = 1;
-        rc = qh_slm_advance(m, n_gen);
-        m->sampling = 0;
-        if (!rc) rc = qh_slm_picks(m, n, n_gen, picks);
+    free(hn);
+    free(st);
+    return rc;
+}
+
+int qh_slm_sample_steps(qh_slm *m, int32_t n_steps, int32_t *out) {
+    if (!m || n_steps < 0 || (n_steps > 0 && !out) || m->host_pos + n_steps > m->cfg.max_pos) return QH_ERR_INVALID;
+    if (n_steps == 0) return QH_OK;
+    const int32_t p0 = m->host_pos;
+    m->sampling = 1;
+    int rc = qh_slm_advance(m, n_steps);
+    m->sampling = 0;
+    if (!rc) rc = qh_slm_picks(m, p0, n_steps, out);
+    return rc;
+}
+
+int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, int32_t max_new, int32_t min_new,
+                            const qh_sampler *sp, const uint64_t *seeds, int32_t eos_id, int32_t eot_id,
+                            const int32_t *stop_ids, int32_t n_stop, int32_t *out, int32_t *n_out) {
+    if (!m || !prompt || !sp || !out || !n_out || n_prompt <= 0 || max_new < 0 || n_stop < 0 ||
+        (n_stop > 0 && !stop_ids) || n_prompt >= m->cfg.max_pos)
+        return QH_ERR_INVALID;
+    const int32_t B = m->B, P = m->cfg.max_pos, n = n_prompt;
+    // slm_generate_raw's decode loop runs while pos < max_position
+    const int32_t n_gen = max_new < P - n ? max_new : P - n;
+    // prompt at positions 0..n-1, then the decode loop re-feeds the last
+    // prompt token at position n: a prefill of the prompt plus that token
+    // leaves exactly this state with the token pending at position n
+    int32_t *ext = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * (n + 1));
+    int32_t *picks = (int32_t *)malloc(sizeof(int32_t) * (size_t)B * (n_gen > 0 ? n_gen : 1));
+    int rc = (ext && picks) ? QH_OK : QH_ERR_INVALID;
+    if (!rc) {
+        for (int32_t b = 0; b < B; ++b) {
+            memcpy(ext + (int64_t)b * (n + 1), prompt + (int64_t)b * n, sizeof(int32_t) * (size_t)n);
+            ext[(int64_t)b * (n + 1) + n] = prompt[(int64_t)b * n + n - 1];
+        }
+        rc = qh_slm_prefill(m, ext, n + 1);
     }
+    // the history starts as this call's prompt (slm/slm.c:257-263)
+    if (!rc) rc = qh_slm_sample_setup(m, sp, seeds, eos_id, eot_id, min_new, prompt, n);
+    if (!rc) rc = qh_slm_sample_steps(m, n_gen, picks);
     if (!rc) {
         // a sequence ends at its first eos, eot or stop token, which is
         // counted (slm/slm.c:330-341)
@@ -1217,8 +1249,6 @@ int qh_slm_generate_sampled(qh_slm *m, const int32_t *prompt, int32_t n_prompt, 
         }
     }
     free(ext);
-    free(hn);
-    free(st);
     free(picks);
     return rc;
 }
