@@ -480,3 +480,14 @@ int ref_chunked_step(int32_t n, int32_t k_hd, int32_t v_hd, const float *q, cons
     for (int i = 0; i < 19; i++) free(s[i]);
     return ok ? 0 : -1;
 }
+
+// Accessors for a matmul backend that replaces the reference's
+// tensor_matmul_* entry points from another shared library (oracle/
+// ref_dropin.c): the fields of a struct tensor it needs, and a new 2-D
+// tensor in a given tensor's arena (tensor_new_2d, slm/tensor.c:251), so the
+// backend never depends on the struct's layout.
+float *ref_tensor_data(const struct tensor *t) { return t->data; }
+int64_t ref_tensor_ne(const struct tensor *t, int i) { return t->ne[i]; }
+struct tensor *ref_tensor_new_like(const struct tensor *t, int64_t n0, int64_t n1) {
+    return tensor_new_2d(t->arena, n0, n1);
+}
