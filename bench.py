@@ -236,26 +236,10 @@ def decode_step_bytes(cfg, B: int, weight_bytes: int, n_prompt: int, n_new: int)
 # ---------------------------------------------------------------------------
 # data-parallel plumbing (one process per GPU; also exercised on CPU/gloo)
 # ---------------------------------------------------------------------------
-def max_over_ranks(dist, values, device):
+def max_over_ranks(dp, values):
     """Element-wise max of a list of floats over all ranks (the job's time is
-    its slowest rank's)."""
-    import torch
-    if not dist.is_initialized() or dist.get_world_size() == 1:
-        return list(values)
-    t = torch.tensor(list(values), dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return [float(v) for v in t.tolist()]
-
-
-def gather_tokens(dist, local, out):
-    """All-gather of each rank's sampled tokens (int32 [B]) into out
-    [world * B], rank-major. NCCL: one all_gather_into_tensor; other
-    backends: all_gather into views of out."""
-    if dist.get_backend() == "nccl":
-        dist.all_gather_into_tensor(out, local)
-    else:
-        dist.all_gather(list(out.view(dist.get_world_size(), -1).unbind(0)), local)
-    return out
+    its slowest rank's), through the library's NCCL communicator (qh_dp)."""
+    return list(values) if dp is None else dp.max(list(values))
 
 
 # ---------------------------------------------------------------------------
@@ -343,7 +327,7 @@ def run_gemm(qh, torch, steps: int, warmup: int):
     return out
 
 
-def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_new: int,
+def run_decode(qh, torch, dist, dp, world: int, rank: int, B: int, n_prompt: int, n_new: int,
                profile_step: bool = False):
     """Greedy decode of B sequences per GPU: n_prompt teacher-forced steps,
     then n_new steps timed with CUDA events on the model's stream; the
@@ -363,10 +347,9 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     nxt = torch.as_tensor(_DevInts(slm.device_next, B), device="cuda")
     gathered = torch.empty(world * B, dtype=torch.int32, device="cuda")
 
-    def gather():
-        if world > 1:
-            with torch.cuda.stream(stream):
-                gather_tokens(dist, nxt, gathered)
+    def gather():  # the step's sampled tokens of every rank, on the model's stream (qh_dp_gather_tokens)
+        if dp is not None:
+            dp.gather(slm.device_next, B, gathered.data_ptr(), slm.stream)
 
     # warm-up: the first steps run directly, then the step is captured; a
     # short prefill allocates the prompt-chunk buffers and tiled weights
@@ -400,7 +383,7 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
         torch.cuda.cudart().cudaProfilerStop()
     torch.cuda.synchronize()
     prefill_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
-    prefill_ms, decode_ms, wall = max_over_ranks(dist, [prefill_ms, decode_ms, wall], "cuda")
+    prefill_ms, decode_ms, wall = max_over_ranks(dp, [prefill_ms, decode_ms, wall])
     # consistency: the gathered picks of the last step are this rank's picks
     if world > 1:
         mine = gathered.view(world, B)[rank].cpu().numpy()
@@ -421,7 +404,7 @@ def run_decode(qh, torch, dist, world: int, rank: int, B: int, n_prompt: int, n_
     ch.prefill(prompts)
     cev[1].record(cstream)
     torch.cuda.synchronize()
-    chunked_ms = max_over_ranks(dist, [cev[0].elapsed_time(cev[1])], "cuda")[0]
+    chunked_ms = max_over_ranks(dp, [cev[0].elapsed_time(cev[1])])[0]
     ch.close()
     step_bytes = decode_step_bytes(cfg, B, wb.value, n_prompt, n_new)
     step_ms = decode_ms / n_new
@@ -537,6 +520,10 @@ def run_ours(args):
     h = qh.host
     L = qh.lib()
     qh.check(L.qh_set_device(local), "qh_set_device")
+    # the library's own communicator (qh_dp, NCCL): token gathers and
+    # max-over-ranks timing; torch.distributed only carries its id and the
+    # barriers
+    dp = h.DataParallel.from_torch(dist, timeout_ms=120000) if world > 1 else None
     G = args.pool
     stream = torch.cuda.current_stream()
     sh = C.c_void_p(stream.cuda_stream)
@@ -588,7 +575,7 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     def max_time(v: float) -> float:
-        return max_over_ranks(dist, [v], "cuda")[0]
+        return max_over_ranks(dp, [v])[0]
 
     def pipelined_steps(n, e2e, kev=None):
         """n steps: step i = (e2e: copy activations in) + quantize into buffer
@@ -705,7 +692,7 @@ def run_ours(args):
         for B, n_prompt in ((1, 64), (args.decode_batch, args.decode_prompt)):
             if args.decode_only_batch and B != args.decode_only_batch:
                 continue
-            decode[f"batch{B}"], _, _, _ = run_decode(qh, torch, dist, world, rank, B, n_prompt, args.decode_new,
+            decode[f"batch{B}"], _, _, _ = run_decode(qh, torch, dist, dp, world, rank, B, n_prompt, args.decode_new,
                                                       args.profile_step)
         if args.sampled:
             for B, n_prompt in ((1, 64), (args.decode_batch, args.decode_prompt)):
@@ -716,12 +703,14 @@ def run_ours(args):
         decode.update({"clocks": dclk.stop(),
                   "data": "synthetic Qwen3.5-0.8B-shaped weights (Q4_K mix), seeded random prompts",
                   "roofline_peak_gbs": peak, "parallelism": f"dp{world}, replicated weights, "
-                  "sampled tokens all-gathered over NCCL each step"})
+                  "sampled tokens all-gathered each step by qh_dp_gather_tokens (NCCL)"})
         for d in runs:
             d["hbm_frac"] = round(d["hbm_gbs"] / peak, 4)
 
     if world > 1:
         dist.barrier()
+    if dp is not None:
+        dp.close()
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()

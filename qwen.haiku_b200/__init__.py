@@ -250,6 +250,17 @@ SIGNATURES.update({  # include/slm.h: the reference's slm.h entry points
     "qh_gguf_special_tokens": (_I, [C.c_char_p, _P]),
 })
 
+SIGNATURES.update({  # include/qh_dp.h
+    "qh_dp_unique_id": (_I, [_P]),
+    "qh_dp_create": (_I, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "qh_dp_destroy": (_I, [_P]),
+    "qh_dp_rank": (C.c_int32, [_P]),
+    "qh_dp_size": (C.c_int32, [_P]),
+    "qh_dp_gather_tokens": (_I, [_P, _P, C.c_int32, _P, _P]),
+    "qh_dp_wait": (_I, [_P, _P]),
+    "qh_dp_max_f64": (_I, [_P, C.POINTER(C.c_double), C.c_int32]),
+})
+
 _lib = None
 
 

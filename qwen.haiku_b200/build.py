@@ -88,7 +88,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             _run([cc, *CC_FLAGS, "-c", src, "-o", obj], verbose)
         objs.append(obj)
     if force or _stale(LIB, objs):
-        _run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lm", "-lpthread"], verbose)
+        _run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lm", "-lpthread", "-ldl"], verbose)
     return LIB
 
 

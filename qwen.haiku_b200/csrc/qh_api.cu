@@ -201,6 +201,9 @@ struct qh_matvec_plan_s {
 
 extern "C" {
 
+// For the library's C sources (not in a public header).
+void qh_internal_set_error(const char *msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
+
 const char *qh_version(void) { return "qh200 0.1.0 (sm_100a)"; }
 const char *qh_last_error(void) { return g_err; }
 

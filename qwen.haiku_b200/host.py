@@ -476,3 +476,48 @@ class Slm:
             self.close()
         except Exception:
             pass
+
+
+class DataParallel:
+    """qh_dp (include/qh_dp.h): the NCCL communicator of one rank of a
+    data-parallel job -- the token gather after each decode step and the
+    max-over-ranks of timings. The 128-byte unique id travels from rank 0 to
+    the others through `exchange(id_bytes_or_None) -> id_bytes` (e.g. a
+    torch.distributed broadcast, a file)."""
+
+    def __init__(self, rank: int, world: int, exchange, timeout_ms: int = 0):
+        L = lib()
+        buf = (C.c_uint8 * 128)()
+        if rank == 0:
+            check(L.qh_dp_unique_id(buf), "qh_dp_unique_id")
+        uid = exchange(bytes(buf) if rank == 0 else None)
+        C.memmove(buf, uid, 128)
+        h = C.c_void_p()
+        check(L.qh_dp_create(buf, world, rank, timeout_ms, C.byref(h)), "qh_dp_create")
+        self.handle, self.rank, self.world = h, rank, world
+
+    @classmethod
+    def from_torch(cls, dist, timeout_ms: int = 0):
+        """The id broadcast over an initialized torch.distributed group."""
+        def exchange(b):
+            obj = [b]
+            dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+        return cls(dist.get_rank(), dist.get_world_size(), exchange, timeout_ms)
+
+    def gather(self, d_local: int, n: int, d_all: int, stream: int = 0):
+        check(lib().qh_dp_gather_tokens(self.handle, C.c_void_p(d_local), n, C.c_void_p(d_all),
+                                        C.c_void_p(stream) if stream else None), "qh_dp_gather_tokens")
+
+    def wait(self, stream: int = 0):
+        check(lib().qh_dp_wait(self.handle, C.c_void_p(stream) if stream else None), "qh_dp_wait")
+
+    def max(self, values):
+        v = (C.c_double * len(values))(*values)
+        check(lib().qh_dp_max_f64(self.handle, v, len(values)), "qh_dp_max_f64")
+        return list(v)
+
+    def close(self):
+        if self.handle:
+            lib().qh_dp_destroy(self.handle)
+            self.handle = None

@@ -1,7 +1,10 @@
 # SPDX-License-Identifier: MIT
-"""CPU (gloo, world size 2): the data-parallel plumbing of bench.py --
-max-over-ranks timing, the per-step all-gather of sampled tokens, and the
-reference arm's rank-0-only rule -- without a GPU."""
+"""CPU (gloo, world size 2): the host side of the data-parallel plumbing --
+the library communicator's id handed from rank 0 to every rank over a
+torch.distributed group (qwen.haiku_b200.host.DataParallel; the NCCL
+collectives themselves are tested on GPUs, tests/test_dp_gpu.py), bench.py's
+max-over-ranks on a single rank, the reference arm's rank-0-only rule, and a
+rank that leaves before the exchange -- without a GPU."""
 import os
 import socket
 import sys
@@ -26,18 +29,29 @@ def _worker(rank, world, port, q):
     from datetime import timedelta
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        from conftest import load_pkg
+        qh = load_pkg()
+        import ctypes as C
+        got = []
+
+        def exchange(b):  # what DataParallel.from_torch does, without creating the NCCL communicator
+            obj = [b]
+            dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+        if rank == 0:
+            buf = (C.c_uint8 * 128)()
+            qh.check(qh.lib().qh_dp_unique_id(buf), "qh_dp_unique_id")
+            got = exchange(bytes(buf))
+            assert got == bytes(buf)
+        else:
+            got = exchange(None)
+        assert isinstance(got, bytes) and len(got) == 128 and any(got)
+        ids = [None] * world
+        dist.all_gather_object(ids, got)
+        assert all(i == ids[0] for i in ids), "ranks received different ids"
         import bench
-        # slowest rank's time wins, element-wise
-        got = bench.max_over_ranks(dist, [1.0 + rank, 10.0 - rank], "cpu")
-        assert got == [float(world), 10.0], got
-        # token gather: rank-major concatenation, repeated over steps
-        B = 5
-        out = torch.empty(world * B, dtype=torch.int32)
-        for step in range(3):
-            local = torch.arange(B, dtype=torch.int32) + 100 * rank + 1000 * step
-            bench.gather_tokens(dist, local, out)
-            want = torch.cat([torch.arange(B, dtype=torch.int32) + 100 * r + 1000 * step for r in range(world)])
-            assert torch.equal(out, want), (out, want)
+        assert bench.max_over_ranks(None, [1.0, 2.0]) == [1.0, 2.0]  # one rank: its own times
         q.put((rank, "ok"))
     except Exception as e:  # report to the parent instead of hanging the peer
         q.put((rank, repr(e)))
@@ -70,18 +84,15 @@ def test_reference_arm_only_rank0_works(monkeypatch):
 
 
 def _leaver(rank, world, port, q):
-    """Rank 1 leaves between steps (after one token gather) without taking
-    part in the next; rank 0's next gather must end with an error within the
-    process group's short timeout instead of waiting for good."""
+    """Rank 1 leaves before the communicator's id is handed out; rank 0's
+    exchange must end with an error within the process group's short
+    timeout instead of waiting for good."""
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import time
     from datetime import timedelta
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
-    import bench
-    B = 4
-    out = torch.empty(world * B, dtype=torch.int32)
-    bench.gather_tokens(dist, torch.full((B,), rank, dtype=torch.int32), out)
+    dist.barrier()
     if rank == 1:
         q.put((rank, "left"))
         q.close()
@@ -89,7 +100,9 @@ def _leaver(rank, world, port, q):
         os._exit(0)  # leaves between steps: nothing of it is in flight
     t0 = time.monotonic()
     try:
-        bench.gather_tokens(dist, torch.zeros(B, dtype=torch.int32), out)
+        obj = [bytes(128)]
+        dist.broadcast_object_list(obj, src=0)
+        dist.barrier()
         q.put((rank, "no error"))
     except Exception as e:
         q.put((rank, f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}"))
