@@ -234,6 +234,16 @@ int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, 
                         int *smem_bytes);
 int qh_matvec_plan_destroy(qh_matvec_plan plan);
 
+/* Failure-detection test hook (no reference counterpart): the plan's next
+ * runs leave out every copy of tile `tile` (-1: none), so the consumers'
+ * bounded wait for that stage runs out after wait_limit polls (0: the
+ * kernels' default limit, seconds) -- the path a lost copy or a stalled
+ * producer takes: the CTA records the timeout in the device error word,
+ * stops, waits (bounded) for its own copies in flight and returns, and
+ * qh_check_device_error then reports QH_ERR_DEVICE. Nothing faults and
+ * nothing is left in flight; the outputs of that launch are not defined. */
+int qh_matvec_plan_test_timeout(qh_matvec_plan plan, int32_t tile, uint32_t wait_limit);
+
 /* ------------------------------------------------------------------------
  * Tensor-core matmul for many tokens (prefill, batched decode): the same
  * results as tensor_matmul_{q4k,q5k,q6k}_f32 (slm/tensor.c:827-853, 898-919,

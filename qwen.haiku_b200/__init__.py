@@ -101,6 +101,7 @@ SIGNATURES = {
     "qh_matvec_plan_run": (_I, [_P, _P]),
     "qh_matvec_plan_info": (_I, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
     "qh_matvec_plan_destroy": (_I, [_P]),
+    "qh_matvec_plan_test_timeout": (_I, [_P, C.c_int32, C.c_uint32]),
     "qh_gemm_weight_bytes": (_I64, [_I, _I64, _I64]),
     "qh_gemm_pack_weights": (_I, [_I, _P, _I64, _I64, _P, _P]),
     "qh_gemm_expanded_bytes": (_I64, [_I, _I64, _I64]),

@@ -509,6 +509,15 @@ int qh_matvec_plan_run(qh_matvec_plan plan, void *stream) {
     return QH_OK;
 }
 
+int qh_matvec_plan_test_timeout(qh_matvec_plan plan, int32_t tile, uint32_t wait_limit) {
+    if (!plan) return fail(QH_ERR_INVALID, "plan_test_timeout: null plan");
+    if (tile < -1 || tile >= plan->params.total_tiles)
+        return fail(QH_ERR_INVALID, "plan_test_timeout: tile %d outside [-1, %d)", tile, plan->params.total_tiles);
+    plan->params.test_withhold = tile + 1;
+    plan->params.wait_limit = wait_limit;
+    return QH_OK;
+}
+
 int qh_matvec_plan_info(qh_matvec_plan plan, int *rows_per_tile, int *n_stages, int *grid, int *smem_bytes) {
     if (!plan) return fail(QH_ERR_INVALID, "plan_info: null plan");
     if (rows_per_tile) *rows_per_tile = plan->params.rows_per_tile;

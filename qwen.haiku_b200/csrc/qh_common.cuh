@@ -80,6 +80,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
+// The same with at most `limit` polls.
+__device__ __forceinline__ bool mbar_wait_n(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
 
 // 1-D bulk copy global -> shared through the TMA engine, completing `bytes`
 // of transaction count on `bar`. src and dst 16-byte aligned, bytes a

@@ -216,6 +216,79 @@ __device__ __forceinline__ void kquant_accumulate(const uint32_t (&wa)[4], const
     }
 }
 
+// Sum over the 4 lanes of a row of four per-block partials p0..p3 (blocks
+// b..b+3), transposed: lane q of the row ends with the total of block b + q
+// (3 shuffles for the four blocks instead of 2 per block). Integer sums:
+// the order of the additions does not matter.
+__device__ __forceinline__ int quad_transpose_sum(int p0, int p1, int p2, int p3, int q) {
+    const bool up = (q & 2) != 0;
+    int k0 = up ? p2 : p0, k1 = up ? p3 : p1;
+    const int s0 = up ? p0 : p2, s1 = up ? p1 : p3;
+    k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    const bool odd = (q & 1) != 0;
+    return (odd ? k1 : k0) + __shfl_xor_sync(0xffffffffu, odd ? k0 : k1, 1);
+}
+
+// Q4_K, whole rows, four blocks at a time: each lane forms its partial
+// integer sums of the four blocks, the transposed reduction gives lane q the
+// totals of block b + q, lane q alone forms that block's fp32 term, and the
+// four terms are added to the row sum in block order -- the same operations
+// on the same values as one block at a time, with a quarter of the
+// reductions and of the fp32 work.
+template <int NT>
+__device__ __forceinline__ void q4k_quad(const uint8_t *row, const GemvJob &job, const XView &x, int b, int q,
+                                         float (&acc)[NT], int n_tok) {
+    const int j0 = q >> 1, r0 = (q & 1) << 4, hi = r0 >> 4;
+    const uint32_t sh = 16u * static_cast<uint32_t>(j0);
+    int is[4][NT], mn[4][NT];
+    uint32_t hx[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const uint8_t *blk = row + (b + u) * QH_Q4K_BYTES;
+        const uint4 h = lds128(blk);
+        const uint4 qa = lds128(blk + 16 + 16 * q);
+        const uint4 qc = lds128(blk + 80 + 16 * q);
+        const KScales s = unpack_kscales(h, sh);
+        hx[u] = h.x;
+        const uint32_t m4 = 0x0f0f0f0fu, h4 = 0xf0f0f0f0u;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            is[u][t] = 0;
+            mn[u][t] = 0;
+            if (t < n_tok) {
+                const int8_t *xq = x.qs + t * job.k + (b + u) * QH_QK + 64 * j0 + r0;
+                const int4 xa = lds128i(xq), xb = lds128i(xq + 32), xc = lds128i(xq + 128), xd = lds128i(xq + 160);
+                const int da = dot16(qa.x & m4, qa.y & m4, qa.z & m4, qa.w & m4, xa, 0);
+                const int db = dot16_u(qa.x & h4, qa.y & h4, qa.z & h4, qa.w & h4, xb, 0) >> 4;
+                const int dc = dot16(qc.x & m4, qc.y & m4, qc.z & m4, qc.w & m4, xc, 0);
+                const int dd = dot16_u(qc.x & h4, qc.y & h4, qc.z & h4, qc.w & h4, xd, 0) >> 4;
+                is[u][t] = da * s.sc_a + db * s.sc_b + dc * s.sc_c + dd * s.sc_d;
+                const int2 bp = *reinterpret_cast<const int2 *>(x.bs + (t * job.nb + b + u) * 16 + 4 * j0 + 8 * hi);
+                const int msel = hi ? s.mins_cd : s.mins_ab;
+                mn[u][t] = __dp2a_hi(bp.y, msel, __dp2a_lo(bp.x, msel, 0));
+            }
+        }
+    }
+    const uint32_t hq = q == 0 ? hx[0] : q == 1 ? hx[1] : q == 2 ? hx[2] : hx[3];
+    const float dw = h2f_bits(hq), dmw = h2f_bits(hq >> 16);
+    const int base = (threadIdx.x & 31) & ~3;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (t < n_tok) {
+            const int isum = quad_transpose_sum(is[0][t], is[1][t], is[2][t], is[3][t], q);
+            const int mins = quad_transpose_sum(mn[0][t], mn[1][t], mn[2][t], mn[3][t], q);
+            const float yd = reinterpret_cast<const float *>(x.d)[t * job.d_stride + b + q];
+            const float term = __fsub_rn(__fmul_rn(__fmul_rn(yd, dw), static_cast<float>(isum)),
+                                         __fmul_rn(__fmul_rn(yd, dmw), static_cast<float>(mins)));
+            float a = acc[t];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) a = __fadd_rn(a, __shfl_sync(0xffffffffu, term, base + u));
+            acc[t] = a;
+        }
+    }
+}
+
 template <int NT>
 __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job, const XView &x, int row0,
                                           int nvalid, int n_tok, int b_first, int b_step, float *terms) {
@@ -225,10 +298,15 @@ __device__ __forceinline__ void group_q4k(const uint8_t *grp, const GemvJob &job
     const uint32_t sh = 16u * static_cast<uint32_t>(j0);
     Sink<NT> acc;
     acc.init(terms, job.nb);
+    int b = b_first;
+    if constexpr (NT == 1) {
+        if (!terms)  // whole rows: four blocks at a time, then the rest one by one
+            for (; b + 4 <= job.nb; b += 4) q4k_quad<NT>(row, job, x, b, q, acc.acc, n_tok);
+    }
     // unrolled: the loads and integer work of neighbouring blocks overlap
     // (the row sum still adds the blocks' terms in order)
 #pragma unroll 4
-    for (int b = b_first; b < job.nb; b += b_step) {
+    for (; b < job.nb; b += b_step) {
         const uint8_t *blk = row + b * QH_Q4K_BYTES;
         const uint4 h = lds128(blk);
         const uint4 qa = lds128(blk + 16 + 16 * q);  // qs[32*j0 + r0 .. +16]
@@ -605,6 +683,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 
     const int S = p.n_stages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t lim = p.wait_limit ? p.wait_limit : kWaitLimit;
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -629,8 +708,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         // programmatic launch they stream in while the previous kernel (the
         // activation quantizer) finishes; the activation planes follow the wait.
         const int n_pre = min(n_my, S);
-        auto issue_x = [&](int s) {
-            if (lane == 0 && !p.xform) {
+        // test hook: the tile whose copies are left out (its stage never fills)
+        auto withheld = [&](int i) { return p.test_withhold != 0 && t_begin + i == p.test_withhold - 1; };
+        auto issue_x = [&](int i, int s) {  // tile i of this CTA in stage s
+            if (lane == 0 && !p.xform && !withheld(i)) {
                 const GemvJob &jb = meta[s].job;
                 uint32_t xq_b, xb_b, xd_b;
                 x_plane_bytes(TYPE, jb, p.n_tok, &xq_b, &xb_b, &xd_b);
@@ -646,14 +727,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         for (int i = 0; i < n_my; ++i) {
             if (i == n_pre && !p.xform) {
                 pdl_wait();
-                for (int t = 0; t < n_pre; ++t) issue_x(t);
+                for (int t = 0; t < n_pre; ++t) issue_x(t, t);
             }
             // Every decision that ends the loop is made warp-uniform, so the
             // __syncwarp below never waits for a lane that has left.
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
             const int s = i % S;
             const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-            const bool ok = __all_sync(0xffffffffu, i < S || mbar_wait(&empty[s], ph ^ 1u));
+            const bool ok = __all_sync(0xffffffffu, i < S || mbar_wait_n(&empty[s], ph ^ 1u, lim));
             if (!ok) {
                 if (lane == 0) {
                     report_error(p.err_flag, kDevWaitTimeout);
@@ -684,20 +765,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 // Order this thread's generic-proxy shared writes before the
                 // async-proxy bulk copies that later reuse the stage.
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive_expect_tx(&full[s], wbytes + xq_b + xb_b + xd_b);
+                if (!withheld(i)) mbar_arrive_expect_tx(&full[s], wbytes + xq_b + xb_b + xd_b);
             }
             __syncwarp();
-            if (lane == 0 && wbytes) bulk_copy_g2s(dst, a0, wbytes, &full[s]);
-            if (i >= n_pre) issue_x(s);
+            if (lane == 0 && wbytes && !withheld(i)) bulk_copy_g2s(dst, a0, wbytes, &full[s]);
+            if (i >= n_pre) issue_x(i, s);
             ++issued;
         }
         if (issued == n_pre && n_pre > 0 && !p.xform) {  // the loop ended inside the first ring
             pdl_wait();
-            for (int t = 0; t < n_pre; ++t) issue_x(t);
+            for (int t = 0; t < n_pre; ++t) issue_x(t, t);
         }
         // Drain: wait for this CTA's copies in flight before exiting.
         for (int i = max(0, issued - S); i < issued; ++i)
-            if (!mbar_wait(&full[i % S], static_cast<uint32_t>(i / S) & 1u) && lane == 0)
+            if (!mbar_wait_n(&full[i % S], static_cast<uint32_t>(i / S) & 1u, lim) && lane == 0)
                 report_error(p.err_flag, kDevWaitTimeout);
         return;
     }
@@ -729,7 +810,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         for (int i = 0; i < n_my; ++i) {
             const int s = i % S;
             const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-            const bool ok = !*abort_flag && mbar_wait(&full[s], ph);
+            const bool ok = !*abort_flag && mbar_wait_n(&full[s], ph, lim);
             if (bar_any(1, 32 * kConsumerWarps, !ok)) {
                 if (!ok) {
                     report_error(p.err_flag, kDevWaitTimeout);
@@ -768,7 +849,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     for (int i = 0; i < n_my; ++i) {
         const int s = i % S;
         const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-        if (!mbar_wait(&full[s], ph)) {
+        if (!mbar_wait_n(&full[s], ph, lim)) {
             report_error(p.err_flag, kDevWaitTimeout);
             *abort_flag = 1;
             break;

@@ -74,6 +74,11 @@ struct GemvParams {
     uint8_t *txq;
     unsigned *ticket;      // zero between launches
     int *err_flag;         // device error word
+    // Failure-detection test hook (qh_matvec_plan_test_timeout): tile
+    // test_withhold - 1 gets no copies (0: none), and bounded waits poll at
+    // most wait_limit times (0: kWaitLimit).
+    int32_t test_withhold;
+    uint32_t wait_limit;
     GemvJob jobs[kGemvInlineJobs];
 };
 
