@@ -661,6 +661,21 @@ def run_ours(args):
     e1.record(stream)
     barrier()
     e2e_ms = max_time(e0.elapsed_time(e1))
+    # the host copies alone, every rank at once: the end-to-end bound when
+    # many GPUs share the host's PCIe and memory (slowest rank)
+    def copy_ms(dst, src, st, n=20):
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        c0.record(st)
+        for _ in range(n):
+            dst.copy_(src, non_blocking=True)
+        c1.record(st)
+        barrier()
+        return max_time(c0.elapsed_time(c1)) / n
+    with torch.cuda.stream(s_out):
+        d2h_ms = copy_ms(out_pin[0], out[0], s_out)
+    with torch.cuda.stream(s_in):
+        h2d_ms = copy_ms(x_dev[0], x_pin, s_in)
     clk = clocks.stop()
     qh.check(L.qh_check_device_error(None), "device error word")
     if not np.array_equal(out_pin[(args.steps - 1) % 2][G - 1].numpy().view(np.uint32),
@@ -751,7 +766,11 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": G * ALGO_BYTES, "traffic": traffic},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": G * K_IN * 4, "d2h_bytes_per_step": G * N_OUT * 4,
-                "ms_per_step": round(e2e_ms / args.steps, 4)},
+                "ms_per_step": round(e2e_ms / args.steps, 4),
+                "host_copy_gbs": {"d2h": round(G * N_OUT * 4 / (d2h_ms / 1e3) / 1e9, 1),
+                                  "h2d": round(G * K_IN * 4 / (h2d_ms / 1e3) / 1e9, 1),
+                                  "note": "one step's output / input copies alone on every rank at once, "
+                                          "pinned host buffers (slowest rank): the end-to-end limiter at many GPUs"}},
         "gpu_launches": 2 * args.steps,
         "pipelining": "two activation/output buffers: quantize (and e2e copy-in) of step i+1 and copy-out of step i-1 overlap step i's matvecs",
         "clocks": clk,
