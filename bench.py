@@ -48,6 +48,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Q4_K GEMV HBM GB/s (% of 8 TB/s); decode tok/s at batch 1 and 64/GPU"
 K_IN, N_OUT = 1024, 3072
+Q4K_TYPE = 12  # GGUF type id of Q4_K
 W_BYTES = N_OUT * (K_IN // 256) * 144          # 1,769,472
 X_BYTES = (K_IN // 256) * 292                   # Q8_K activation (reference block size)
 O_BYTES = N_OUT * 4
@@ -132,15 +133,31 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU side: the reference's own SIMD dot over all host cores
 # ---------------------------------------------------------------------------
+def numpy_q4k_blocks(n_blocks: int, seed: int):
+    """Seeded Q4_K super-blocks without this library (for the reference arm):
+    uniform random bytes with fp16 d and dmin drawn from U[1e-3, 1e-2]."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, (n_blocks, 144), dtype=np.uint8)
+    b[:, 0:4] = rng.uniform(1e-3, 1e-2, (n_blocks, 2)).astype(np.float16).view(np.uint8).reshape(n_blocks, 4)
+    return b.reshape(-1)
+
+
 def cpu_reference_run(qh, n_mats: int, passes_budget_s: float, max_passes: int = None):
-    """Returns (GB/s, cores, sample description, kind, per-pass seconds list)."""
+    """Returns (GB/s, cores, sample description, kind, per-pass seconds list).
+    qh None: the inputs are generated with numpy (the reference arm maps no
+    library of this repository)."""
     import numpy as np
     from oracle.oracle import Oracle, Ref, to_q8k_blocks
     cores = len(os.sched_getaffinity(0))
-    h = qh.host
-    base = [h.synth_blocks(qh.Q4_K, N_OUT * 4, 0xC0FFEE + i) for i in range(min(n_mats, 8))]
+    if qh is not None:
+        h = qh.host
+        base = [h.synth_blocks(Q4K_TYPE, N_OUT * 4, 0xC0FFEE + i) for i in range(min(n_mats, 8))]
+        x = h.synth_normal(K_IN, 0xACE)
+    else:
+        base = [numpy_q4k_blocks(N_OUT * 4, 0xC0FFEE + i) for i in range(min(n_mats, 8))]
+        x = np.random.default_rng(0xACE).standard_normal(K_IN).astype(np.float32)
     pool = [base[i % len(base)].copy() for i in range(n_mats)]  # distinct addresses
-    x = h.synth_normal(K_IN, 0xACE)
     if Ref.available():
         ref = Ref()
         qs, d, bs = ref.quantize_q8k(x.reshape(1, K_IN))
@@ -148,7 +165,7 @@ def cpu_reference_run(qh, n_mats: int, passes_budget_s: float, max_passes: int =
         out = np.empty(N_OUT, np.float32)
 
         def one_pass():
-            ref.matvec_pool_mt(qh.Q4_K, pool, N_OUT, K_IN, xq, cores, out)
+            ref.matvec_pool_mt(Q4K_TYPE, pool, N_OUT, K_IN, xq, cores, out)
         kind = "reference"
         label = ref.label
     else:
@@ -157,7 +174,7 @@ def cpu_reference_run(qh, n_mats: int, passes_budget_s: float, max_passes: int =
 
         def one_pass():
             for w in pool:
-                orc.matvec_preq(qh.Q4_K, w, N_OUT, K_IN, qs[0], d[0], bs[0])
+                orc.matvec_preq(Q4K_TYPE, w, N_OUT, K_IN, qs[0], d[0], bs[0])
         kind, label, cores = "port", "oracle restatement (1 thread)", 1
     times = []
     t_total = 0.0
@@ -182,9 +199,8 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    qh = load_pkg()
-    n_mats = 64
-    gbs, cores, sample, kind, times = cpu_reference_run(qh, n_mats, 0.0, max_passes=args.warmup + args.steps)
+    n_mats = 64  # inputs from numpy: the reference arm maps only oracle/_ref (and liboracle)
+    gbs, cores, sample, kind, times = cpu_reference_run(None, n_mats, 0.0, max_passes=args.warmup + args.steps)
     timed = times[args.warmup:] if len(times) > args.warmup else times
     per = statistics.median(timed)
     value = n_mats * ALGO_BYTES / per / 1e9
