@@ -239,6 +239,87 @@ int qh_sample_feed(float *d_logits, int32_t B, int64_t vocab, const qh_sample_ct
  * checking those functions against the host library. */
 int qh_libm_eval(int fn, uint32_t first, int64_t n, float *d_out, void *stream);
 
+/* ---- Persistent decode step (one sequence) ------------------------------
+ * A run of consecutive operations of slm_forward_step (slm/qwen.c:874-981)
+ * for ONE sequence, executed as one cooperative launch of one CTA per SM
+ * with a grid-wide barrier between phases, instead of one launch per
+ * operation. Two kinds of phase:
+ *   QH_STEP_MATVEC  form the Q8_K input row of xk values in every CTA --
+ *     residual add + RMSNorm (QH_STEP_X_RESNORM: x = xa (+ xb), norm weight
+ *     xw, eps; x written to xh_out by one CTA when xh_out is given; the
+ *     operations of qh_rmsnorm_q8k), SwiGLU (QH_STEP_X_SWIGLU: silu(xa) * xb,
+ *     as qh_swiglu_q8k) or plain quantization (QH_STEP_X_QUANT: xa, as
+ *     qh_quantize_q8k) -- then out = W x for up to QH_STEP_MAX_PROJ
+ *     K-quant weights (Q4_K, Q5_K, Q6_K; the values of qh_matmul_preq:
+ *     tensor_matmul_*_f32, slm/tensor.c:827-1033);
+ *   QH_STEP_GDN  one Gated DeltaNet token update for every head (the
+ *     operations of qh_gdn_fused_y, slm/qwen.c:318-611), fp32 output rows y.
+ * Weight tiles stream into shared memory ahead of the phase that reads them
+ * (weights do not depend on activations), so a phase's time is its
+ * dependency latency, not a launch's ramp. Outputs are bit-identical to the
+ * launch-per-operation chain. Positions are read from *d_pos. Every wait in
+ * the kernel is bounded; a timeout is reported through
+ * qh_check_device_error. */
+#define QH_STEP_MATVEC 0
+#define QH_STEP_GDN 1
+#define QH_STEP_X_RESNORM 1
+#define QH_STEP_X_SWIGLU 2
+#define QH_STEP_X_QUANT 3
+#define QH_STEP_MAX_PROJ 8
+
+typedef struct qh_step_proj {
+    int32_t type;      /* QH_GGUF_Q4_K, QH_GGUF_Q5_K or QH_GGUF_Q6_K */
+    const void *d_w;   /* GGUF blocks [out_f][k], 16-byte aligned */
+    int64_t k, out_f;
+    float *d_out;      /* [out_f] */
+} qh_step_proj;
+
+typedef struct qh_step_phase {
+    int32_t kind;      /* QH_STEP_MATVEC or QH_STEP_GDN */
+    /* QH_STEP_MATVEC */
+    int32_t xform;     /* QH_STEP_X_* */
+    int64_t xk;
+    float eps;         /* RMSNorm epsilon (also the DeltaNet gated-norm epsilon) */
+    const float *d_xa, *d_xb, *d_xw;
+    float *d_xh_out;
+    int32_t n_proj;
+    qh_step_proj proj[QH_STEP_MAX_PROJ];
+    /* optional: with two projections of one shape (ffn gate, up), also
+     * act[r] = silu(out0[r]) * out1[r] (the values qh_swiglu forms), each
+     * CTA for the rows it computed; the next phase then quantizes act
+     * (QH_STEP_X_QUANT) instead of every CTA forming the SwiGLU row */
+    float *d_act_out;
+    /* QH_STEP_GDN (sequence 0 of the qh_gdn_fused_y arguments) */
+    const float *d_qkv;
+    float *d_ring;
+    const float *d_conv_w, *d_b, *d_a, *d_dt_bias, *d_ssm_a;
+    float *d_state;
+    const float *d_z, *d_norm_w;
+    float *d_y;
+    int32_t heads, head_dim, conv_kernel;
+} qh_step_phase;
+
+typedef struct qh_step_prog qh_step_prog;
+
+/* Validates and uploads the phases (device tables, barrier counters) for the
+ * current device. QH_ERR_UNSUPPORTED for weight types other than the K-quants
+ * or a device without cooperative launch. */
+int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t *d_pos, qh_step_prog **out);
+/* Runs phases [first, first + count) as one launch on `stream`. Launches of
+ * one program must not overlap (they share the barrier counters). */
+int qh_step_run(qh_step_prog *prog, int32_t first, int32_t count, void *stream);
+void qh_step_destroy(qh_step_prog *prog);
+/* Measurement hook: with d_stamps non-null (qh_step_phase_count records of
+ * 8 + G uint64, G = the device's SM count, the launch's CTAs), later
+ * launches write %globaltimer (ns) per phase p into record p: [0] CTA 0 at
+ * the phase start, [1] input formed, [2] work done, [3] past the grid
+ * barrier; [4..7] inside a DeltaNet head update of CTA 0 (inputs ready,
+ * state landed, recurrence done, output written); [8 + c] CTA c's work done.
+ * Null turns it off. Launches already captured in a CUDA graph keep the
+ * setting they were captured with. */
+int qh_step_set_stamps(qh_step_prog *prog, uint64_t *d_stamps);
+int32_t qh_step_phase_count(const qh_step_prog *prog);
+
 #ifdef __cplusplus
 }
 #endif

@@ -165,6 +165,31 @@ int qh_slm_set_prefill_chunk(qh_slm *m, int32_t max_tokens_per_seq);
 #define QH_PREFILL_CHUNKED 1
 int qh_slm_set_prefill_mode(qh_slm *m, int32_t mode);
 
+/* How a decode step (qh_slm_step, qh_slm_advance, the generation loops)
+ * runs, with bit-identical results either way:
+ *   QH_DECODE_PERSISTENT (default) -- for one sequence whose projection
+ *     weights are all K-quants: the step's operations as a few cooperative
+ *     launches of one CTA per SM with grid-wide barriers between phases
+ *     (qh_step_run, include/qh_kernels.h), the attention layers' cache
+ *     kernels between them; weights stream ahead of the phase that reads
+ *     them. Models that do not qualify (more sequences, Q8_0 or F32
+ *     projections, an F32 embedding table) run QH_DECODE_LAUNCHES;
+ *   QH_DECODE_LAUNCHES -- one launch per operation (norm, projection set,
+ *     DeltaNet head update, attention, ...), captured in a CUDA graph.
+ * A traced step (qh_slm_trace) always runs QH_DECODE_LAUNCHES. */
+#define QH_DECODE_PERSISTENT 0
+#define QH_DECODE_LAUNCHES 1
+int qh_slm_set_decode_mode(qh_slm *m, int32_t mode);
+/* The mode decode steps of m actually run (after the first step: a model
+ * that does not qualify for QH_DECODE_PERSISTENT reports QH_DECODE_LAUNCHES). */
+int32_t qh_slm_decode_mode(const qh_slm *m);
+/* The persistent step's measurement hook (qh_step_set_stamps) for the next
+ * steps of m: returns the number of phases P (d_stamps holds P records of
+ * 8 + SM-count uint64), or QH_ERR_UNSUPPORTED when m does not run
+ * QH_DECODE_PERSISTENT (after its first step). Replaces the captured step
+ * graphs. */
+int qh_slm_step_stamps(qh_slm *m, uint64_t *d_stamps);
+
 /* Greedy generation, the per-step prefill path of slm_generate_raw
  * (slm/slm.c:237-357) for every sequence: the prompt runs through
  * qh_slm_prefill (the same caches as feeding one token per step) and the

@@ -27,8 +27,9 @@ STATUS_NAMES = {
     -4: "QH_ERR_ALIGN", -5: "QH_ERR_WORKSPACE", -6: "QH_ERR_DEVICE",
 }
 
-# qh_slm_set_prefill_mode (include/qh_slm.h)
+# qh_slm_set_prefill_mode, qh_slm_set_decode_mode (include/qh_slm.h)
 PREFILL_STEPWISE, PREFILL_CHUNKED = 0, 1
+DECODE_PERSISTENT, DECODE_LAUNCHES = 0, 1
 
 # GGUF tensor types (slm/gguf.c:52-59).
 F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
@@ -40,6 +41,29 @@ BLOCK_WEIGHTS = {Q4_K: 256, Q5_K: 256, Q6_K: 256, Q8_0: 32}
 class GemmJob(C.Structure):
     """qh_gemm_job (include/qh_backend.h)."""
     _fields_ = [("d_wt", C.c_void_p), ("out_f", C.c_int64), ("d_out", C.c_void_p), ("ld_out", C.c_int64)]
+
+
+# qh_step_* (include/qh_kernels.h): persistent decode-step programs.
+STEP_MATVEC, STEP_GDN = 0, 1
+STEP_X_RESNORM, STEP_X_SWIGLU, STEP_X_QUANT = 1, 2, 3
+STEP_MAX_PROJ = 8
+
+
+class StepProj(C.Structure):
+    """qh_step_proj (include/qh_kernels.h)."""
+    _fields_ = [("type", C.c_int32), ("d_w", C.c_void_p), ("k", C.c_int64), ("out_f", C.c_int64),
+                ("d_out", C.c_void_p)]
+
+
+class StepPhase(C.Structure):
+    """qh_step_phase (include/qh_kernels.h)."""
+    _fields_ = [("kind", C.c_int32), ("xform", C.c_int32), ("xk", C.c_int64), ("eps", C.c_float),
+                ("d_xa", C.c_void_p), ("d_xb", C.c_void_p), ("d_xw", C.c_void_p), ("d_xh_out", C.c_void_p),
+                ("n_proj", C.c_int32), ("proj", StepProj * STEP_MAX_PROJ), ("d_act_out", C.c_void_p),
+                ("d_qkv", C.c_void_p), ("d_ring", C.c_void_p), ("d_conv_w", C.c_void_p), ("d_b", C.c_void_p),
+                ("d_a", C.c_void_p), ("d_dt_bias", C.c_void_p), ("d_ssm_a", C.c_void_p), ("d_state", C.c_void_p),
+                ("d_z", C.c_void_p), ("d_norm_w", C.c_void_p), ("d_y", C.c_void_p),
+                ("heads", C.c_int32), ("head_dim", C.c_int32), ("conv_kernel", C.c_int32)]
 
 
 class QHError(RuntimeError):
@@ -156,6 +180,9 @@ SIGNATURES.update({
     "qh_slm_sample_steps": (_I, [_P, C.c_int32, _P]),
     "qh_slm_set_prefill_chunk": (_I, [_P, C.c_int32]),
     "qh_slm_set_prefill_mode": (_I, [_P, C.c_int32]),
+    "qh_slm_set_decode_mode": (_I, [_P, C.c_int32]),
+    "qh_slm_decode_mode": (C.c_int32, [_P]),
+    "qh_slm_step_stamps": (_I, [_P, _P]),
     "qh_slm_advance": (_I, [_P, C.c_int32]),
     "qh_slm_picks": (_I, [_P, C.c_int32, C.c_int32, _P]),
     "qh_slm_stream": (_P, [_P]),
@@ -165,6 +192,11 @@ SIGNATURES.update({
 _F32P = C.c_void_p
 SIGNATURES.update({  # include/qh_kernels.h
     "qh_libm_eval": (_I, [_I, C.c_uint32, _I64, _P, _P]),
+    "qh_step_create": (_I, [_P, C.c_int32, _P, _P]),
+    "qh_step_run": (_I, [_P, C.c_int32, C.c_int32, _P]),
+    "qh_step_destroy": (None, [_P]),
+    "qh_step_set_stamps": (_I, [_P, _P]),
+    "qh_step_phase_count": (C.c_int32, [_P]),
     "qh_embed_q6k": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
     "qh_embed_f32": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
     "qh_rmsnorm": (_I, [_P, _P, _I64, _I64, C.c_float, _P, _P]),

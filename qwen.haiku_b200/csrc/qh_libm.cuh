@@ -76,14 +76,14 @@ __device__ __forceinline__ float logf_ref(float x) {
         ix = __float_as_uint(__fmul_rn(x, 0x1p23f)) - (23u << 23);      // subnormal
     }
     if (kLogExcN > 0) {  // the measured inputs the evaluation below rounds the other way
+        // one pass over the short list, every load independent (one memory
+        // latency, where a binary search waits for log2(n) of them)
         const uint32_t xb = __float_as_uint(x);
-        int lo = 0, hi = kLogExcN;
-        while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            const uint32_t v = __ldg(&kLogExcIn[mid]);
-            if (v == xb) return __uint_as_float(__ldg(&kLogExcOut[mid]));
-            if (v < xb) lo = mid + 1; else hi = mid;
-        }
+        int hit = -1;
+#pragma unroll
+        for (int e = 0; e < kLogExcN; ++e)
+            if (__ldg(&kLogExcIn[e]) == xb) hit = e;
+        if (hit >= 0) return __uint_as_float(__ldg(&kLogExcOut[hit]));
     }
     const uint32_t tmp = ix - 0x3f330000u;
     const int i = static_cast<int>((tmp >> 19) & 15u);

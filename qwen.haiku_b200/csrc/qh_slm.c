@@ -133,7 +133,16 @@ struct qh_slm {
     cudaGraph_t graph[2];
     cudaGraphExec_t graph_exec[2];
     int steps_run[2];
+    int no_graph[2];               // the step could not be captured: launched directly
     int sampling;                  // the step ends in qh_sample_feed
+    // persistent decode (QH_DECODE_PERSISTENT): the step's phases as one
+    // program, run as segments separated by the attention layers' cache
+    // kernels (qh_attn_pre, qh_attn_decode)
+    int32_t decode_mode;           // requested
+    int step_state;                // 0 not built, 1 built, -1 the model does not qualify
+    qh_step_prog *step_prog;
+    int32_t n_seg;
+    struct { int32_t first, count, attn_layer; } seg[MAX_LAYERS + 1];
     // sampled decoding (qh_slm_generate_sampled)
     qh_sample_ctl *d_sctl;
     int32_t *d_hist, *d_hist_n;    // [B][max_pos + 1] prompt + generated tokens, lengths
@@ -591,6 +600,7 @@ void qh_slm_destroy(qh_slm *m) {
         free_plans(&m->L[l].p_down);
     }
     free_plans(&m->p_head);
+    qh_step_destroy(m->step_prog);
     for (int i = 0; i < 2; ++i) {
         if (m->graph_exec[i]) cudaGraphExecDestroy(m->graph_exec[i]);
         if (m->graph[i]) cudaGraphDestroy(m->graph[i]);
@@ -827,28 +837,214 @@ static int forward(qh_slm *m) {
     return QH_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Persistent decode step (one sequence): the operations of forward() as
+// phases of qh_step programs. Every projection phase forms its own Q8_K
+// input (the fused norm/SwiGLU/quantize kernels of forward()), a DeltaNet
+// layer is one phase, and each attention layer ends a segment: its cache
+// kernels run as launches between two segments.
+// ---------------------------------------------------------------------------
+static void step_mv(qh_step_phase *ph, int32_t xform, int64_t xk, const float *xa, const float *xb, const float *xw,
+                    float *xh_out, float eps, const plan_set *ps) {
+    memset(ph, 0, sizeof(*ph));
+    ph->kind = QH_STEP_MATVEC;
+    ph->xform = xform;
+    ph->xk = xk;
+    ph->eps = eps;
+    ph->d_xa = xa;
+    ph->d_xb = xb;
+    ph->d_xw = xw;
+    ph->d_xh_out = xh_out;
+    ph->n_proj = ps->n;
+    for (int i = 0; i < ps->n; ++i) {
+        ph->proj[i].type = ps->w[i]->type;
+        ph->proj[i].d_w = ps->w[i]->d;
+        ph->proj[i].k = ps->w[i]->k;
+        ph->proj[i].out_f = ps->w[i]->out_f;
+        ph->proj[i].d_out = ps->out[i];
+    }
+}
+
+static int step_set_ok(const plan_set *ps) { return ps->n > 0 && ps->n <= QH_STEP_MAX_PROJ && !ps->n32 && !ps->gemm; }
+
+// Builds the program; step_state -1 (and QH_OK) when the model does not qualify.
+static int build_step_prog(qh_slm *m) {
+    const qh_slm_config *c = &m->cfg;
+    m->step_state = -1;
+    if (m->B != 1 || !step_set_ok(&m->p_head) || c->gdn_head_dim != 128) return QH_OK;
+    for (int l = 0; l < c->n_layers; ++l) {
+        const layer *Ly = &m->L[l];
+        if (!step_set_ok(&Ly->p_in) || !step_set_ok(&Ly->p_out) || !step_set_ok(&Ly->p_ffn) ||
+            !step_set_ok(&Ly->p_down))
+            return QH_OK;
+    }
+    const int64_t H = c->hidden, F = c->ffn, hd = c->head_dim;
+    const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
+    const int64_t qdim = (int64_t)c->n_heads * hd;
+    // at most 5 phases per layer (DeltaNet: input projections, head update,
+    // output projection, FFN up, FFN down) and the head
+    const int max_ph = 5 * c->n_layers + 1;
+    qh_step_phase *ph = (qh_step_phase *)calloc((size_t)max_ph, sizeof(qh_step_phase));
+    if (!ph) return QH_ERR_INVALID;
+    int np = 0, first = 0;
+    m->n_seg = 0;
+    // the residual stream alternates between h and h2, as in forward()
+    float *hc = m->h, *hx = m->h2;
+    const float *pending = NULL;
+    for (int l = 0; l < c->n_layers; ++l) {
+        const layer *Ly = &m->L[l];
+        step_mv(&ph[np++], QH_STEP_X_RESNORM, H, hc, pending, Ly->attn_norm, pending ? hx : NULL, c->norm_eps,
+                &Ly->p_in);
+        if (pending) { float *t = hc; hc = hx; hx = t; }
+        if (Ly->is_attn) {
+            m->seg[m->n_seg].first = first;
+            m->seg[m->n_seg].count = np - first;
+            m->seg[m->n_seg].attn_layer = l;
+            m->n_seg++;
+            first = np;
+            step_mv(&ph[np++], QH_STEP_X_QUANT, qdim, m->actx, NULL, NULL, NULL, c->norm_eps, &Ly->p_out);
+        } else {
+            const int64_t gi = Ly->gdn_index;
+            qh_step_phase *g = &ph[np++];
+            g->kind = QH_STEP_GDN;
+            g->eps = c->norm_eps;
+            g->d_qkv = m->qkv;
+            g->d_ring = m->ring + gi * c->conv_kernel * conv_dim;
+            g->d_conv_w = Ly->conv_w;
+            g->d_b = m->bt;
+            g->d_a = m->at;
+            g->d_dt_bias = Ly->dt_bias;
+            g->d_ssm_a = Ly->ssm_a;
+            g->d_state = m->state + gi * c->gdn_heads * (int64_t)c->gdn_head_dim * c->gdn_head_dim;
+            g->d_z = m->z;
+            g->d_norm_w = Ly->ssm_norm;
+            g->d_y = m->gy;
+            g->heads = c->gdn_heads;
+            g->head_dim = c->gdn_head_dim;
+            g->conv_kernel = c->conv_kernel;
+            step_mv(&ph[np++], QH_STEP_X_QUANT, kdim, m->gy, NULL, NULL, NULL, c->norm_eps, &Ly->p_out);
+        }
+        pending = m->mix;
+        // gate/up also form the SwiGLU row (each CTA its own rows), which the
+        // down projection's phase only quantizes
+        step_mv(&ph[np], QH_STEP_X_RESNORM, H, hc, pending, Ly->ffn_norm, hx, c->norm_eps, &Ly->p_ffn);
+        ph[np++].d_act_out = m->fact;
+        { float *t = hc; hc = hx; hx = t; }
+        step_mv(&ph[np++], QH_STEP_X_QUANT, F, m->fact, NULL, NULL, NULL, c->norm_eps, &Ly->p_down);
+        pending = m->mix;
+    }
+    step_mv(&ph[np++], QH_STEP_X_RESNORM, H, hc, pending, m->out_norm, hx, c->norm_eps, &m->p_head);
+    m->seg[m->n_seg].first = first;
+    m->seg[m->n_seg].count = np - first;
+    m->seg[m->n_seg].attn_layer = -1;
+    m->n_seg++;
+    const int rc = qh_step_create(ph, np, m->d_ctl, &m->step_prog);
+    free(ph);
+    if (rc == QH_ERR_UNSUPPORTED) return QH_OK;
+    if (rc) return rc;
+    m->step_state = 1;
+    return QH_OK;
+}
+
+static int forward_persistent(qh_slm *m) {
+    const qh_slm_config *c = &m->cfg;
+    const int32_t B = m->B;
+    const int64_t H = c->hidden, hd = c->head_dim, kvd = (int64_t)c->n_kv_heads * hd;
+    void *s = m->stream;
+    CK(m->tok_embd.type == QH_GGUF_F32 ? qh_embed_f32((const float *)m->tok_embd.d, H, m->d_tok, B, m->h, s)
+                                       : qh_embed_q6k(m->tok_embd.d, H, m->d_tok, B, m->h, s));
+    for (int i = 0; i < m->n_seg; ++i) {
+        CK(qh_step_run(m->step_prog, m->seg[i].first, m->seg[i].count, s));
+        if (m->seg[i].attn_layer < 0) continue;
+        const layer *Ly = &m->L[m->seg[i].attn_layer];
+        const int64_t ai = Ly->attn_index;
+        uint16_t *kc = m->kcache + ai * B * c->max_pos * kvd;
+        uint16_t *vc = m->vcache + ai * B * c->max_pos * kvd;
+        CK(qh_attn_pre(m->qraw, m->kb, m->vb, Ly->q_norm, Ly->k_norm, m->rope, B, c->n_heads, c->n_kv_heads,
+                       (int32_t)hd, c->rope_dim, c->norm_eps, m->d_ctl, c->max_pos, m->aq, m->agate, kc, vc, s));
+        CK(qh_attn_decode(m->aq, kc, vc, m->agate, B, c->n_heads, c->n_kv_heads, (int32_t)hd, m->d_ctl, c->max_pos,
+                          m->actx, s));
+    }
+    if (m->sampling)
+        CK(qh_sample_feed(m->logits, B, c->vocab, m->d_sctl, m->d_hist, c->max_pos + 1, m->d_hist_n, m->d_rng,
+                          m->d_next, c->max_pos, m->d_ctl, m->d_tok, m->d_picks, m->d_sticket, s));
+    else
+        CK(qh_argmax_feed(m->logits, B, c->vocab, m->amax_scratch, m->d_next, m->d_prompt, c->max_pos, m->d_ctl,
+                          m->d_tok, m->d_picks, s));
+    return QH_OK;
+}
+
+static void drop_graphs(qh_slm *m) {
+    for (int i = 0; i < 2; ++i) {
+        if (m->graph_exec[i]) cudaGraphExecDestroy(m->graph_exec[i]);
+        if (m->graph[i]) cudaGraphDestroy(m->graph[i]);
+        m->graph_exec[i] = NULL;
+        m->graph[i] = NULL;
+        m->steps_run[i] = 0;
+        m->no_graph[i] = 0;
+    }
+}
+
+int qh_slm_set_decode_mode(qh_slm *m, int32_t mode) {
+    if (!m || (mode != QH_DECODE_PERSISTENT && mode != QH_DECODE_LAUNCHES)) return QH_ERR_INVALID;
+    if (mode == m->decode_mode) return QH_OK;
+    if (qh_stream_sync(m->stream)) return QH_ERR_CUDA;
+    drop_graphs(m);  // the next step captures the other form
+    m->decode_mode = mode;
+    return QH_OK;
+}
+
+int32_t qh_slm_decode_mode(const qh_slm *m) {
+    if (!m) return -1;
+    return m->decode_mode == QH_DECODE_PERSISTENT && m->step_state == 1 ? QH_DECODE_PERSISTENT : QH_DECODE_LAUNCHES;
+}
+
+int qh_slm_step_stamps(qh_slm *m, uint64_t *d_stamps) {
+    if (!m) return QH_ERR_INVALID;
+    if (m->decode_mode != QH_DECODE_PERSISTENT || m->step_state != 1) return QH_ERR_UNSUPPORTED;
+    if (qh_stream_sync(m->stream)) return QH_ERR_CUDA;
+    drop_graphs(m);
+    CK(qh_step_set_stamps(m->step_prog, d_stamps));
+    return qh_step_phase_count(m->step_prog);
+}
+
+// The step's operations, either form (not while tracing).
+static int forward_step(qh_slm *m) {
+    if (m->decode_mode == QH_DECODE_PERSISTENT && m->step_state == 1) return forward_persistent(m);
+    return forward(m);
+}
+
 static int launch_step(qh_slm *m) {
     const int gi = m->sampling ? 1 : 0;
+    if (m->decode_mode == QH_DECODE_PERSISTENT && m->step_state == 0) CK(build_step_prog(m));
     if (m->graph_exec[gi]) {
         if (cudaGraphLaunch(m->graph_exec[gi], m->stream) != cudaSuccess) return QH_ERR_CUDA;
         return QH_OK;
     }
-    if (m->steps_run[gi]++ == 0) return forward(m);  // first run sets kernel attributes
-    // capture the step once, then replay it
-    if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return forward(m);
-    int rc = forward(m);
+    // the first run sets kernel attributes (and builds programs) outside a capture
+    if (m->steps_run[gi]++ == 0 || m->no_graph[gi]) return forward_step(m);
+    // capture the step once, then replay it; a step that cannot be captured
+    // runs its launches directly from then on
+    if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        m->no_graph[gi] = 1;
+        return forward_step(m);
+    }
+    int rc = forward_step(m);
     cudaGraph_t g = NULL;
     cudaError_t e = cudaStreamEndCapture(m->stream, &g);
     if (rc || e != cudaSuccess || g == NULL) {
         if (g) cudaGraphDestroy(g);
         cudaGetLastError();
-        return rc ? rc : forward(m);
+        m->no_graph[gi] = 1;
+        return forward_step(m);
     }
     if (cudaGraphInstantiate(&m->graph_exec[gi], g, 0) != cudaSuccess) {
         cudaGraphDestroy(g);
         m->graph_exec[gi] = NULL;
         cudaGetLastError();
-        return forward(m);
+        m->no_graph[gi] = 1;
+        return forward_step(m);
     }
     m->graph[gi] = g;
     return cudaGraphLaunch(m->graph_exec[gi], m->stream) == cudaSuccess ? QH_OK : QH_ERR_CUDA;

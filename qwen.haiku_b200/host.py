@@ -450,6 +450,14 @@ class Slm:
             check(lib().qh_slm_set_prefill_mode(self.handle, mode), "qh_slm_set_prefill_mode")
         check(lib().qh_slm_prefill(self.handle, p.ctypes.data, p.shape[1]), "qh_slm_prefill")
 
+    def set_decode_mode(self, mode: int):
+        """qh_slm_set_decode_mode (DECODE_PERSISTENT / DECODE_LAUNCHES)."""
+        check(lib().qh_slm_set_decode_mode(self.handle, mode), "qh_slm_set_decode_mode")
+
+    def decode_mode(self) -> int:
+        """qh_slm_decode_mode: the form decode steps actually run."""
+        return int(lib().qh_slm_decode_mode(self.handle))
+
     def advance(self, n_steps: int):
         check(lib().qh_slm_advance(self.handle, n_steps), "qh_slm_advance")
 
