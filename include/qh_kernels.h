@@ -253,7 +253,12 @@ int qh_libm_eval(int fn, uint32_t first, int64_t n, float *d_out, void *stream);
  *     K-quant weights (Q4_K, Q5_K, Q6_K; the values of qh_matmul_preq:
  *     tensor_matmul_*_f32, slm/tensor.c:827-1033);
  *   QH_STEP_GDN  one Gated DeltaNet token update for every head (the
- *     operations of qh_gdn_fused_y, slm/qwen.c:318-611), fp32 output rows y.
+ *     operations of qh_gdn_fused_y, slm/qwen.c:318-611), fp32 output rows y;
+ *   QH_STEP_ATTN  one gated-attention token for every query head (the
+ *     operations of qh_attn_pre + qh_attn_decode, slm/model.c:766-953):
+ *     q/k RMSNorm, MRoPE, the fp16 K/V append at *d_pos, softmax attention
+ *     over the cache, the sigmoid gate; fp32 output rows ctx. Not directly
+ *     before a QH_STEP_GDN phase (they share a shared-memory region).
  * Weight tiles stream into shared memory ahead of the phase that reads them
  * (weights do not depend on activations), so a phase's time is its
  * dependency latency, not a launch's ramp. Outputs are bit-identical to the
@@ -262,10 +267,13 @@ int qh_libm_eval(int fn, uint32_t first, int64_t n, float *d_out, void *stream);
  * qh_check_device_error. */
 #define QH_STEP_MATVEC 0
 #define QH_STEP_GDN 1
+#define QH_STEP_ATTN 2
 #define QH_STEP_X_RESNORM 1
 #define QH_STEP_X_SWIGLU 2
 #define QH_STEP_X_QUANT 3
 #define QH_STEP_MAX_PROJ 8
+/* Longest cache a QH_STEP_ATTN phase takes (its scores live in shared memory). */
+#define QH_STEP_ATTN_MAX_POS 8192
 
 typedef struct qh_step_proj {
     int32_t type;      /* QH_GGUF_Q4_K, QH_GGUF_Q5_K or QH_GGUF_Q6_K */
@@ -297,6 +305,12 @@ typedef struct qh_step_phase {
     const float *d_z, *d_norm_w;
     float *d_y;
     int32_t heads, head_dim, conv_kernel;
+    /* QH_STEP_ATTN (sequence 0 of the qh_attn_pre + qh_attn_decode
+     * arguments; head_dim above must be 128; caches [max_pos][n_kv_heads][128]) */
+    const float *d_qraw, *d_kin, *d_vin, *d_qnorm_w, *d_knorm_w, *d_rope;
+    uint16_t *d_kcache, *d_vcache;
+    float *d_ctx;
+    int32_t n_heads, n_kv_heads, rope_dim, max_pos;
 } qh_step_phase;
 
 typedef struct qh_step_prog qh_step_prog;

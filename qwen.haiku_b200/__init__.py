@@ -44,7 +44,7 @@ class GemmJob(C.Structure):
 
 
 # qh_step_* (include/qh_kernels.h): persistent decode-step programs.
-STEP_MATVEC, STEP_GDN = 0, 1
+STEP_MATVEC, STEP_GDN, STEP_ATTN = 0, 1, 2
 STEP_X_RESNORM, STEP_X_SWIGLU, STEP_X_QUANT = 1, 2, 3
 STEP_MAX_PROJ = 8
 
@@ -63,7 +63,11 @@ class StepPhase(C.Structure):
                 ("d_qkv", C.c_void_p), ("d_ring", C.c_void_p), ("d_conv_w", C.c_void_p), ("d_b", C.c_void_p),
                 ("d_a", C.c_void_p), ("d_dt_bias", C.c_void_p), ("d_ssm_a", C.c_void_p), ("d_state", C.c_void_p),
                 ("d_z", C.c_void_p), ("d_norm_w", C.c_void_p), ("d_y", C.c_void_p),
-                ("heads", C.c_int32), ("head_dim", C.c_int32), ("conv_kernel", C.c_int32)]
+                ("heads", C.c_int32), ("head_dim", C.c_int32), ("conv_kernel", C.c_int32),
+                ("d_qraw", C.c_void_p), ("d_kin", C.c_void_p), ("d_vin", C.c_void_p), ("d_qnorm_w", C.c_void_p),
+                ("d_knorm_w", C.c_void_p), ("d_rope", C.c_void_p), ("d_kcache", C.c_void_p),
+                ("d_vcache", C.c_void_p), ("d_ctx", C.c_void_p), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("rope_dim", C.c_int32), ("max_pos", C.c_int32)]
 
 
 class QHError(RuntimeError):

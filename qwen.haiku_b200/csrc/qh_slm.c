@@ -880,7 +880,10 @@ static int build_step_prog(qh_slm *m) {
     }
     const int64_t H = c->hidden, F = c->ffn, hd = c->head_dim;
     const int64_t kdim = (int64_t)c->gdn_heads * c->gdn_head_dim, conv_dim = 3 * kdim;
-    const int64_t qdim = (int64_t)c->n_heads * hd;
+    const int64_t qdim = (int64_t)c->n_heads * hd, kvd = (int64_t)c->n_kv_heads * hd;
+    // attention inside the program while its scores fit the kernel's shared
+    // memory; longer caches split the program at the attention layers
+    const int attn_inside = c->max_pos <= QH_STEP_ATTN_MAX_POS;
     // at most 5 phases per layer (DeltaNet: input projections, head update,
     // output projection, FFN up, FFN down) and the head
     const int max_ph = 5 * c->n_layers + 1;
@@ -897,11 +900,32 @@ static int build_step_prog(qh_slm *m) {
                 &Ly->p_in);
         if (pending) { float *t = hc; hc = hx; hx = t; }
         if (Ly->is_attn) {
-            m->seg[m->n_seg].first = first;
-            m->seg[m->n_seg].count = np - first;
-            m->seg[m->n_seg].attn_layer = l;
-            m->n_seg++;
-            first = np;
+            if (attn_inside) {
+                const int64_t ai = Ly->attn_index;
+                qh_step_phase *a = &ph[np++];
+                a->kind = QH_STEP_ATTN;
+                a->eps = c->norm_eps;
+                a->head_dim = (int32_t)hd;
+                a->d_qraw = m->qraw;
+                a->d_kin = m->kb;
+                a->d_vin = m->vb;
+                a->d_qnorm_w = Ly->q_norm;
+                a->d_knorm_w = Ly->k_norm;
+                a->d_rope = m->rope;
+                a->d_kcache = m->kcache + ai * c->max_pos * kvd;
+                a->d_vcache = m->vcache + ai * c->max_pos * kvd;
+                a->d_ctx = m->actx;
+                a->n_heads = c->n_heads;
+                a->n_kv_heads = c->n_kv_heads;
+                a->rope_dim = c->rope_dim;
+                a->max_pos = c->max_pos;
+            } else {  // the cache kernels run as launches between two segments
+                m->seg[m->n_seg].first = first;
+                m->seg[m->n_seg].count = np - first;
+                m->seg[m->n_seg].attn_layer = l;
+                m->n_seg++;
+                first = np;
+            }
             step_mv(&ph[np++], QH_STEP_X_QUANT, qdim, m->actx, NULL, NULL, NULL, c->norm_eps, &Ly->p_out);
         } else {
             const int64_t gi = Ly->gdn_index;

@@ -55,14 +55,16 @@ constexpr int kStepTermsFloats = kStepTerms / 8;
 constexpr int kStepTaps = 4;  // conv kernel of the DeltaNet layers (other widths run as launches)
 constexpr int kStepHD = 128;
 constexpr int kFormChunk = 8;  // blocks of an input row whose loads are in flight together
+constexpr int kStepPairFloats = 1024;  // a paired (gate/up) phase's outputs kept per CTA
 constexpr int kStepStateBytes = kStepHD * kStepHD * 4;
 // DeltaNet shared-memory region: state [128 k][128 v], then the head's conv
 // ring rows [3 parts][taps][128] and conv weights [3 parts][128][taps]
 constexpr int kStepGdnRowBytes = 3 * kStepTaps * kStepHD * 4;
 constexpr int kStepGdnBytes = kStepStateBytes + 2 * kStepGdnRowBytes;
 constexpr uint64_t kStepBarrierNs = 2000000000ull;  // grid-barrier wait limit: 2 s
+constexpr int kStepBarExit = 32;                    // word of the exit counter (its own 128-byte line)
 
-enum StepKind : int32_t { kPhaseMatvec = 0, kPhaseGdn = 1 };
+enum StepKind : int32_t { kPhaseMatvec = 0, kPhaseGdn = 1, kPhaseAttn = 2 };
 
 struct StepJob {
     const uint8_t *w;
@@ -82,6 +84,22 @@ struct StepGdn {
     float eps;
 };
 
+// One gated-attention layer for one token (sequence 0 of the arguments of
+// qh_attn_pre + qh_attn_decode): CTA j serves query head j.
+struct StepAttn {
+    const float *qraw, *kin, *vin, *qn_w, *kn_w, *rope;
+    __half *kcache, *vcache;  // [max_pos][kvh][128]
+    float *ctx;               // [nh * 128]
+    int32_t nh, kvh, rope_dim, max_pos;
+    float eps;
+};
+constexpr int kAttnChunk = 32;  // V rows per cp.async chunk
+constexpr int kAttnBufs = 4;    // chunk buffers: up to 3 chunks in flight ahead
+__host__ __device__ constexpr int64_t attn_scratch_bytes(int64_t max_pos) {
+    // q, new K row, new V row (floats), scores, V chunks (fp16)
+    return 3 * 128 * 4 + ((max_pos + 3) / 4 * 4) * 4 + kAttnBufs * kAttnChunk * 128 * 2;
+}
+
 struct StepPhase {
     int32_t kind;
     int32_t xform, xk;   // QH_STEP_X_*, input width
@@ -90,7 +108,7 @@ struct StepPhase {
     float *xh_out;
     float *act;          // paired phase: silu(out of job 0) * out of job 1, per row
     int32_t job0, njobs, rows_per_tile, total_tiles, split;
-    int32_t gdn;         // kPhaseGdn: index into the DeltaNet table
+    int32_t gdn;         // kPhaseGdn / kPhaseAttn: index into the DeltaNet / attention table
 };
 
 // What the producer tells the consumers about the tile in a ring slot.
@@ -106,11 +124,12 @@ struct StepParams {
     const StepPhase *phases;
     const StepJob *jobs;
     const StepGdn *gdns;
+    const StepAttn *attns;
     int32_t first, count;
-    int32_t ring_bytes, ring_off, x_off, row_off, terms_off, state_off;
+    int32_t ring_bytes, ring_off, x_off, row_off, terms_off, state_off, w_off, w_floats;
     const int32_t *pos_ptr;
     // [0] grid-barrier arrivals (barrier n completes at n * gridDim.x),
-    // [1] exits; zero between launches
+    // [kStepBarExit] exits; zero between launches
     unsigned *bar;
     int *err_flag;
     uint64_t *stamps;  // measurement hook (qh_step_set_stamps), or null
@@ -160,20 +179,24 @@ __device__ __forceinline__ bool step_grid_barrier(const StepParams &p, unsigned 
     consumers_sync();
     if (threadIdx.x == 0) {
         // release: this CTA's writes (ordered before thread 0 by the barrier
-        // above) become visible with the arrival; one trip to L2, no reply
+        // above) become visible with the arrival; one trip to L2, no reply.
+        // (Measured: a separate fence before or after costs ~0.4 us each;
+        // copies of the counter on other L2 lines do not help.)
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const unsigned target = n * gridDim.x;
         bool ok = false;
         const uint64_t t0 = global_ns();
-        for (;;) {
+        for (uint32_t it = 1;; ++it) {
             if (ld_acquire_u32(p.bar) >= target) {
                 ok = true;
                 break;
             }
-            if (*reinterpret_cast<volatile int *>(p.err_flag) != 0) break;
-            if (global_ns() - t0 > kStepBarrierNs) {
-                report_error(p.err_flag, kDevWaitTimeout);
-                break;
+            if ((it & 63u) == 0) {  // the error word and the time limit, now and then
+                if (*reinterpret_cast<volatile int *>(p.err_flag) != 0) break;
+                if (global_ns() - t0 > kStepBarrierNs) {
+                    report_error(p.err_flag, kDevWaitTimeout);
+                    break;
+                }
             }
         }
         s_ok = ok ? 1 : 0;
@@ -205,7 +228,8 @@ __device__ __forceinline__ void stamp_cta(const StepParams &p, int ph) {
 // order), swiglu_q8k_kernel or quantize_q8k_kernel; quantized one Q8_K block
 // per warp by q8k_block_warp. CTA 0 writes the residual sum when asked.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void step_form_input(const StepPhase &P, uint8_t *xs, float *rowbuf) {
+__device__ __forceinline__ void step_form_input(const StepPhase &P, uint8_t *xs, float *rowbuf, const float *wsm,
+                                                uint64_t *tstamp = nullptr) {
     __shared__ double dscr[kConsumerWarps];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = P.xk, nb = K / QH_QK;
@@ -225,19 +249,18 @@ __device__ __forceinline__ void step_form_input(const StepPhase &P, uint8_t *xs,
     // First pass over all 256 threads, every load issued at once: thread t
     // takes elements t, t + 256, ... (the element order of the reference
     // norm's double sum of squares, as resnorm_q8k_kernel).
-    float *wbuf = rowbuf + K;  // RMSNorm weights
+    const float *wbuf = wsm;  // RMSNorm weights, copied into shared memory a phase ahead
     float rscale = 0.0f;
     if (P.xform == QH_STEP_X_RESNORM) {
         double s = 0.0;
         for (int j0 = 0; j0 < nb; j0 += kFormChunk) {
-            float xv[kFormChunk], yv[kFormChunk], wv[kFormChunk];
+            float xv[kFormChunk], yv[kFormChunk];
 #pragma unroll
             for (int u = 0; u < kFormChunk; ++u) {
                 const int i = (j0 + u) * QH_QK + tid;
                 if (j0 + u < nb) {
                     xv[u] = ldcg_f(P.xa + i);
                     yv[u] = P.xb ? ldcg_f(P.xb + i) : 0.0f;
-                    wv[u] = __ldg(P.xw + i);
                 }
             }
 #pragma unroll
@@ -246,13 +269,14 @@ __device__ __forceinline__ void step_form_input(const StepPhase &P, uint8_t *xs,
                 if (j0 + u < nb) {
                     const float x = P.xb ? __fadd_rn(xv[u], yv[u]) : xv[u];
                     rowbuf[i] = x;
-                    wbuf[i] = wv[u];
                     if (P.xh_out && blockIdx.x == 0) P.xh_out[i] = x;
                     s += static_cast<double>(__fmul_rn(x, x));
                 }
             }
         }
+        if (tstamp && tid == 0) tstamp[4] = global_ns();
         const double ssq = consumers_sum_d(s, dscr);  // ends with a consumer barrier: rowbuf complete
+        if (tstamp && tid == 0) tstamp[5] = global_ns();
         rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(K)), P.eps)));
     } else {  // SwiGLU
         for (int j0 = 0; j0 < nb; j0 += kFormChunk) {
@@ -458,6 +482,176 @@ __device__ __forceinline__ void gdn_prefetch(const StepGdn &g, int h, float *st_
     }
 }
 
+// ---------------------------------------------------------------------------
+// One query head of a gated-attention layer for one token, on the 256
+// consumer threads of CTA j (query head j, KV head c = j / (nh / kvh)): the
+// operations and orders of attn_pre_kernel and attn_decode_gqa_kernel.
+//   * warps 0-3: RMSNorm (double sum: warp tree, then the 4 warps in order)
+//     + MRoPE of the query row; warps 4-7 the same for the KV head's new K
+//     row. Every CTA of a KV head forms that row itself (so no CTA waits for
+//     another), and the first of them appends K and V to the caches.
+//   * scores: thread t takes positions t, t + 256, ...: a sequential fp32 dot
+//     over the 128 dims with the fp16 cache rows (the new row from shared
+//     memory, rounded to fp16 as the cache holds it), times 1/sqrt(128);
+//   * max, exp, one thread's sequential sum, scaling, then per dim (threads
+//     0-127) the sequential sum over positions of p_i * V_i, the V rows
+//     staged by cp.async in chunks; ctx = o * sigmoid(gate).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void attn_sync_hi() { asm volatile("bar.sync 4, 128;" ::: "memory"); }
+
+__device__ __forceinline__ double attn_sum_hi(double v, double *scratch) {  // warps 4-7
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int w = (threadIdx.x >> 5) - 4, lane = threadIdx.x & 31;
+    attn_sync_hi();
+    if (lane == 0) scratch[w] = v;
+    attn_sync_hi();
+    double t = 0.0;
+    for (int i = 0; i < 4; ++i) t += scratch[i];
+    return t;
+}
+
+__device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t *scr, const int32_t *pos_ptr) {
+    constexpr int HD = kStepHD;
+    __shared__ double sq[4], sk[4];
+    __shared__ float s_red[kConsumerWarps], s_inv;
+    float *qs = reinterpret_cast<float *>(scr);
+    float *kn = qs + HD, *vn = kn + HD;
+    float *sc = vn + HD;
+    __half *vbuf = reinterpret_cast<__half *>(sc + (A.max_pos + 3) / 4 * 4);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, t = tid & (HD - 1);
+    const int G = A.nh / A.kvh, c = j / G;
+    const int pos = min(max(__ldcg(pos_ptr), 0), A.max_pos - 1), n = pos + 1;
+    const int64_t rstride = static_cast<int64_t>(A.kvh) * HD;
+    const __half *kb = A.kcache + static_cast<int64_t>(c) * HD;
+    const __half *vb = A.vcache + static_cast<int64_t>(c) * HD;
+    // V rows of chunk q (rows below pos, from the cache) into buffer q % kAttnBufs
+    const int n_old = pos, n_chunks = (n_old + kAttnChunk - 1) / kAttnChunk;
+    auto issue_v = [&](int q) {
+        if (q < n_chunks) {
+            const int r0 = q * kAttnChunk, rows = min(kAttnChunk, n_old - r0);
+            __half *dst = vbuf + (q % kAttnBufs) * kAttnChunk * HD;
+            for (int piece = tid; piece < rows * (HD / 8); piece += 32 * kConsumerWarps) {
+                const int r = piece / (HD / 8), q16 = piece % (HD / 8);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst + r * HD + q16 * 8)),
+                             "l"(vb + (r0 + r) * rstride + q16 * 8)
+                             : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int q = 0; q < kAttnBufs - 1; ++q) issue_v(q);
+    // ---- norms and MRoPE (attn_pre_kernel) ----
+    const bool hi = warp >= 4;
+    float x, gt = 0.0f;
+    if (!hi) {
+        const float *src = A.qraw + static_cast<int64_t>(j) * 2 * HD;
+        x = ldcg_f(src + t);
+        gt = ldcg_f(src + HD + t);
+    } else {
+        x = ldcg_f(A.kin + static_cast<int64_t>(c) * HD + t);
+    }
+    const float vin = hi ? ldcg_f(A.vin + static_cast<int64_t>(c) * HD + t) : 0.0f;
+    const double ssq = hi ? attn_sum_hi(static_cast<double>(__fmul_rn(x, x)), sk)
+                          : gdn_sum_d(static_cast<double>(__fmul_rn(x, x)), sq);
+    const float rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(HD)), A.eps)));
+    const float xn = __fmul_rn(__fmul_rn(x, rscale), __ldg((hi ? A.kn_w : A.qn_w) + t));
+    float *xrow = hi ? kn : qs;
+    xrow[t] = xn;
+    consumers_sync();
+    const int half = A.rope_dim / 2;
+    float y = xn;
+    if (t < A.rope_dim) {
+        const int i = t < half ? t : t - half;
+        const float co = __ldg(A.rope + (static_cast<int64_t>(pos) * half + i) * 2);
+        const float sn = __ldg(A.rope + (static_cast<int64_t>(pos) * half + i) * 2 + 1);
+        const float x0 = xrow[i], x1 = xrow[i + half];
+        y = t < half ? __fsub_rn(__fmul_rn(x0, co), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, co));
+    }
+    consumers_sync();  // every thread has read xrow
+    if (!hi) {
+        qs[t] = y;
+    } else {
+        const __half kh = __float2half_rn(y), vh = __float2half_rn(vin);
+        kn[t] = __half2float(kh);
+        vn[t] = __half2float(vh);
+        if (j % G == 0) {  // the first query head of the group appends the rows
+            const int64_t row = (static_cast<int64_t>(pos) * A.kvh + c) * HD + t;
+            A.kcache[row] = kh;
+            A.vcache[row] = vh;
+        }
+    }
+    consumers_sync();
+    // ---- scores ----
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
+    float lmax = -INFINITY;
+    for (int i = tid; i < n; i += 32 * kConsumerWarps) {
+        float dot = 0.0f;
+        if (i < pos) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + i * rstride);
+            uint4 row[HD / 8];
+#pragma unroll
+            for (int q = 0; q < HD / 8; ++q) row[q] = __ldcg(kr + q);
+#pragma unroll
+            for (int q = 0; q < HD / 8; ++q) {
+                const __half2 *hp = reinterpret_cast<const __half2 *>(&row[q]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(hp[e]);
+                    dot = __fadd_rn(dot, __fmul_rn(qs[8 * q + 2 * e], f.x));
+                    dot = __fadd_rn(dot, __fmul_rn(qs[8 * q + 2 * e + 1], f.y));
+                }
+            }
+        } else {
+            for (int d = 0; d < HD; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kn[d]));
+        }
+        const float sv = __fmul_rn(dot, scale);
+        sc[i] = sv;
+        lmax = fmaxf(lmax, sv);
+    }
+    for (int off = 16; off > 0; off >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
+    if (lane == 0) s_red[warp] = lmax;
+    consumers_sync();
+    float m = s_red[0];
+    for (int w = 1; w < kConsumerWarps; ++w) m = fmaxf(m, s_red[w]);
+    for (int i = tid; i < n; i += 32 * kConsumerWarps) sc[i] = expf_ref(__fsub_rn(sc[i], m));
+    consumers_sync();
+    if (tid == 0) {  // the sequential sum
+        float sum = 0.0f;
+        int i = 0;
+        for (; i + 8 <= n; i += 8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = sc[i + e];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sum = __fadd_rn(sum, v[e]);
+        }
+        for (; i < n; ++i) sum = __fadd_rn(sum, sc[i]);
+        s_inv = __fdiv_rn(1.0f, sum);
+    }
+    consumers_sync();
+    const float inv = s_inv;
+    for (int i = tid; i < n; i += 32 * kConsumerWarps) sc[i] = __fmul_rn(sc[i], inv);
+    consumers_sync();
+    // ---- weighted V sum, per dim in position order ----
+    float o = 0.0f;
+    for (int q = 0; q < n_chunks; ++q) {
+        issue_v(q + kAttnBufs - 1);
+        asm volatile("cp.async.wait_group %0;" ::"n"(kAttnBufs - 1) : "memory");
+        consumers_sync();
+        if (tid < HD) {
+            const __half *vc = vbuf + (q % kAttnBufs) * kAttnChunk * HD;
+            const int r0 = q * kAttnChunk, rows = min(kAttnChunk, n_old - r0);
+            for (int r = 0; r < rows; ++r) o = __fadd_rn(o, __fmul_rn(sc[r0 + r], __half2float(vc[r * HD + tid])));
+        }
+        consumers_sync();  // this buffer is refilled by the issue of chunk q + kAttnBufs
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (tid < HD) {
+        o = __fadd_rn(o, __fmul_rn(sc[pos], vn[tid]));
+        A.ctx[static_cast<int64_t>(j) * HD + tid] = __fmul_rn(o, sigmoid_f(gt));
+    }
+}
+
 // Runtime-typed 8-row group consumer (one token).
 __device__ __forceinline__ void step_group(int type, const uint8_t *wbase, int trow, const GemvJob &job,
                                            const XView &x, int row0, int nvalid, int b_first, int b_step,
@@ -491,7 +685,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kStepSlots;
     uint64_t *st_bar = empty + kStepSlots;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 8 * (2 * kStepSlots + 1));
+    uint64_t *wbar = st_bar + 1;  // [2] RMSNorm weight copies
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 8 * (2 * kStepSlots + 3));
     SlotMeta *meta = reinterpret_cast<SlotMeta *>(smem + 1024);  // [kStepSlots]
     float *gates = reinterpret_cast<float *>(smem + 1024 + kStepSlots * sizeof(SlotMeta));  // DeltaNet beta, g
     uint8_t *ring = smem + p.ring_off;
@@ -503,6 +698,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
             mbar_init(&empty[s], kConsumerWarps);
         }
         mbar_init(st_bar, 1);
+        mbar_init(&wbar[0], 1);
+        mbar_init(&wbar[1], 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -609,12 +806,35 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
         if (N.kind == kPhaseGdn && static_cast<int>(blockIdx.x) < p.gdns[N.gdn].heads)
             gdn_prefetch(p.gdns[N.gdn], blockIdx.x, st_s, st_bar);
     };
+    // The RMSNorm weights of phase k go to buffer k & 1, copied at the start
+    // of phase k - 1 by a CTA that has tiles in phase k.
+    float *wpre = reinterpret_cast<float *>(smem + p.w_off);
+    uint32_t wuse[2] = {0u, 0u};
+    auto norm_prefetch = [&](int k) {
+        if (k >= p.count) return false;
+        const StepPhase &N = p.phases[p.first + k];
+        if (N.kind != kPhaseMatvec || N.xform != QH_STEP_X_RESNORM) return false;
+        int a, b;
+        my_tiles(N, a, b);
+        if (a >= b) return false;
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(&wbar[k & 1], static_cast<uint32_t>(N.xk) * 4u);
+            bulk_copy_g2s(wpre + (k & 1) * p.w_floats, N.xw, static_cast<uint32_t>(N.xk) * 4u, &wbar[k & 1]);
+        }
+        return true;
+    };
     maybe_prefetch(0);
+    bool w_next = norm_prefetch(0);
     for (int k = 0; k < p.count && ok; ++k) {
+        const bool w_here = w_next;
         maybe_prefetch(k + 1);
+        w_next = norm_prefetch(k + 1);
         stamp(p, p.first + k, 0);
         const StepPhase &P = p.phases[p.first + k];
-        if (P.kind == kPhaseGdn) {
+        if (P.kind == kPhaseAttn) {
+            const StepAttn &A = p.attns[P.gdn];
+            if (static_cast<int>(blockIdx.x) < A.nh) step_attn_head(A, blockIdx.x, reinterpret_cast<uint8_t *>(st_s), p.pos_ptr);
+        } else if (P.kind == kPhaseGdn) {
             const StepGdn &G = p.gdns[P.gdn];
             if (static_cast<int>(blockIdx.x) < G.heads) {
                 uint64_t *ts = (p.stamps && blockIdx.x == 0)
@@ -627,11 +847,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                 ++n_gdn;
             }
         } else {
-            if (P.xform) step_form_input(P, xs, rowbuf);
-            consumers_sync();
-            stamp(p, p.first + k, 1);
             int t0, t1;
             my_tiles(P, t0, t1);
+            if (w_here) {  // this phase's RMSNorm weights
+                const int b = k & 1;
+                if (!mbar_wait(&wbar[b], wuse[b] & 1u)) report_error(p.err_flag, kDevWaitTimeout);
+                ++wuse[b];
+                stamp(p, p.first + k, 6);
+            }
+            uint64_t *fts = (p.stamps && blockIdx.x == 0)
+                                ? p.stamps + static_cast<int64_t>(p.first + k) * (kStampFixed + gridDim.x)
+                                : nullptr;
+            if (t0 < t1) step_form_input(P, xs, rowbuf, wpre + (k & 1) * p.w_floats, fts);  // a CTA without tiles needs no input
+            consumers_sync();
+            stamp(p, p.first + k, 1);
+            // paired phase: the CTA's gate / up outputs stay in shared memory
+            // (rowbuf, free once the input is formed) for the SwiGLU epilogue
+            const int pr0 = P.act ? (t0 >> 1) * P.rows_per_tile : 0;
+            const int prows = P.act ? (t1 >> 1) * P.rows_per_tile - pr0 : 0;
+            float *pair_out = rowbuf;
             XView x;
             x.qs = reinterpret_cast<const int8_t *>(xs);
             auto job_of = [&](const SlotMeta &M) {
@@ -680,44 +914,51 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                     }
                 }
             } else {
-                int group_base = 0;
-                for (int t = t0; t < t1; ++t, ++i) {
-                    const int s = i % kStepSlots;
-                    if (!mbar_wait(&full[s], static_cast<uint32_t>(i / kStepSlots) & 1u)) {
+                // Group G of the CTA's tiles (tile G / gpt, its group G % gpt) goes
+                // to warp G % 8; a warp waits for, and releases, only the tiles it
+                // works on. A tile's empty barrier takes 8 arrivals: one per group
+                // and, from the warp of group 0, the 8 - gpt groups it does not have.
+                const int gpt = P.rows_per_tile / kGroupRows;  // groups per tile (<= 8)
+                const int ng = (t1 - t0) * gpt;
+                for (int G = warp; G < ng; G += kConsumerWarps) {
+                    const int tl = G / gpt, gi = G - tl * gpt, ii = i + tl, s = ii % kStepSlots;
+                    if (*abort_flag || !mbar_wait(&full[s], static_cast<uint32_t>(ii / kStepSlots) & 1u)) {
                         report_error(p.err_flag, kDevWaitTimeout);
                         *abort_flag = 1;
                         ok = false;
                         break;
                     }
-                    const int nrows = meta[s].nrows;
-                    const int ngroups = (nrows + kGroupRows - 1) / kGroupRows;
-                    int gi = warp - group_base % kConsumerWarps;
-                    if (gi < 0) gi += kConsumerWarps;
-                    if (gi < ngroups) {
-                        const SlotMeta M = meta[s];
-                        const GemvJob job = job_of(M);
-                        const uint8_t *base = ring + M.off;
-                        for (; gi < ngroups; gi += kConsumerWarps)
-                            step_group(M.type, base, kGroupRows * gi, job, x, M.row0 + kGroupRows * gi,
-                                       min(kGroupRows, nrows - kGroupRows * gi), 0, 1, nullptr);
+                    const SlotMeta M = meta[s];
+                    if (kGroupRows * gi < M.nrows) {
+                        GemvJob job = job_of(M);
+                        int row0 = M.row0;
+                        if (P.act) {  // rows of job 0 then job 1, relative to the CTA's first row
+                            job.out = pair_out + ((t0 + tl) & 1) * prows;
+                            row0 -= pr0;
+                        }
+                        step_group(M.type, ring + M.off, kGroupRows * gi, job, x, row0 + kGroupRows * gi,
+                                   min(kGroupRows, M.nrows - kGroupRows * gi), 0, 1, nullptr);
                     }
-                    group_base += ngroups;
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
-                    if (*abort_flag) { ok = false; break; }
+                    if (lane == 0) mbar_arrive_n(&empty[s], gi == 0 ? kConsumerWarps + 1 - gpt : 1);
                 }
+                i += t1 - t0;
                 // the loop's exit is per warp; the barrier below needs all of them
                 ok = !bar_any(1, 32 * kConsumerWarps, !ok);
+                stamp(p, p.first + k, 7);
                 if (ok && P.act) {
-                    // SwiGLU of the rows this CTA computed (its outputs, read back
-                    // from L2 after the CTA barrier): the values swiglu_q8k_kernel
-                    // forms, for the next phase to quantize
-                    const StepJob &G0 = p.jobs[P.job0];
-                    const float *gate = G0.out, *up = p.jobs[P.job0 + 1].out;
-                    const int r0 = (t0 >> 1) * P.rows_per_tile;
-                    const int r1 = min((t1 >> 1) * P.rows_per_tile, G0.n_rows);
-                    for (int r = r0 + static_cast<int>(threadIdx.x); r < r1; r += 32 * kConsumerWarps)
-                        P.act[r] = __fmul_rn(silu_f(ldcg_f(gate + r)), ldcg_f(up + r));
+                    // SwiGLU of the rows this CTA computed: the values
+                    // swiglu_q8k_kernel forms, for the next phase to quantize;
+                    // the two projections' outputs are stored as well
+                    const StepJob &J0 = p.jobs[P.job0];
+                    float *out1 = p.jobs[P.job0 + 1].out;
+                    const int r1 = min(pr0 + prows, J0.n_rows);
+                    for (int r = pr0 + static_cast<int>(threadIdx.x); r < r1; r += 32 * kConsumerWarps) {
+                        const float gv = pair_out[r - pr0], uv = pair_out[prows + r - pr0];
+                        P.act[r] = __fmul_rn(silu_f(gv), uv);
+                        J0.out[r] = gv;
+                        out1[r] = uv;
+                    }
                 }
             }
         }
@@ -732,9 +973,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
         bulk_wait_all();  // the last state store has completed
         // the last CTA to leave resets the counters for the next launch
         __threadfence();
-        if (atomicAdd(p.bar + 1, 1u) == gridDim.x - 1) {
+        if (atomicAdd(p.bar + kStepBarExit, 1u) == gridDim.x - 1) {
             p.bar[0] = 0u;
-            p.bar[1] = 0u;
+            p.bar[kStepBarExit] = 0u;
             __threadfence();
         }
     }
@@ -751,6 +992,7 @@ struct qh_step_prog {
     qh::StepPhase *d_phases = nullptr;
     qh::StepJob *d_jobs = nullptr;
     qh::StepGdn *d_gdns = nullptr;
+    qh::StepAttn *d_attns = nullptr;
     unsigned *d_bar = nullptr;
     int nphases = 0;
 };
@@ -792,18 +1034,43 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
     std::vector<StepPhase> hp(static_cast<size_t>(n_phases));
     std::vector<StepJob> hj;
     std::vector<StepGdn> hg;
-    int64_t max_x = 0, max_row = 0, max_res_k = 0;
-    bool any_gdn = false;
+    std::vector<StepAttn> ha;
+    int64_t max_x = 0, max_row = 0, max_res_k = 0, max_norm_k = 0;
+    int64_t aux_bytes = 0;  // DeltaNet state and attention scratch share one region
     for (int k = 0; k < n_phases; ++k) {
         const qh_step_phase &ph = phases[k];
         StepPhase P = {};
         P.kind = ph.kind;
         P.gdn = -1;
+        if (ph.kind == QH_STEP_ATTN) {
+            if (!ph.d_qraw || !ph.d_kin || !ph.d_vin || !ph.d_qnorm_w || !ph.d_knorm_w || !ph.d_rope ||
+                !ph.d_kcache || !ph.d_vcache || !ph.d_ctx || ph.n_heads <= 0 || ph.n_kv_heads <= 0 ||
+                ph.n_heads % ph.n_kv_heads || ph.n_heads > sms || ph.rope_dim < 0 || ph.rope_dim > kStepHD ||
+                ph.rope_dim % 2 || ph.max_pos <= 0 || !a16(ph.d_kcache) || !a16(ph.d_vcache))
+                return step_bad("qh_step_create: bad attention phase");
+            if (ph.max_pos > QH_STEP_ATTN_MAX_POS) {
+                set_last_error_message("qh_step_create: attention cache longer than QH_STEP_ATTN_MAX_POS");
+                return QH_ERR_UNSUPPORTED;
+            }
+            if (ph.head_dim != kStepHD) {
+                set_last_error_message("qh_step_create: attention head dim must be 128");
+                return QH_ERR_UNSUPPORTED;
+            }
+            StepAttn a = {ph.d_qraw, ph.d_kin, ph.d_vin, ph.d_qnorm_w, ph.d_knorm_w, ph.d_rope,
+                          reinterpret_cast<__half *>(ph.d_kcache), reinterpret_cast<__half *>(ph.d_vcache), ph.d_ctx,
+                          ph.n_heads, ph.n_kv_heads, ph.rope_dim, ph.max_pos, ph.eps};
+            P.kind = kPhaseAttn;
+            P.gdn = static_cast<int32_t>(ha.size());
+            ha.push_back(a);
+            aux_bytes = std::max<int64_t>(aux_bytes, attn_scratch_bytes(ph.max_pos));
+            hp[static_cast<size_t>(k)] = P;
+            continue;
+        }
         if (ph.kind == QH_STEP_GDN) {
             // a DeltaNet phase's state is copied in during the phase before it,
             // into one region per CTA: two in a row are refused
-            if (k > 0 && phases[k - 1].kind == QH_STEP_GDN)
-                return step_bad("qh_step_create: two DeltaNet phases in a row");
+            if (k > 0 && (phases[k - 1].kind == QH_STEP_GDN || phases[k - 1].kind == QH_STEP_ATTN))
+                return step_bad("qh_step_create: a DeltaNet phase directly after a DeltaNet or attention phase");
             if (!ph.d_qkv || !ph.d_ring || !ph.d_conv_w || !ph.d_b || !ph.d_a || !ph.d_dt_bias || !ph.d_ssm_a ||
                 !ph.d_state || !ph.d_z || !ph.d_norm_w || !ph.d_y || ph.heads <= 0 || ph.heads > sms ||
                 !a16(ph.d_state) || !a16(ph.d_ring) || !a16(ph.d_conv_w))
@@ -821,7 +1088,7 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
             P.kind = kPhaseGdn;
             P.gdn = static_cast<int32_t>(hg.size());
             hg.push_back(g);
-            any_gdn = true;
+            aux_bytes = std::max<int64_t>(aux_bytes, kStepGdnBytes);
             hp[static_cast<size_t>(k)] = P;
             continue;
         }
@@ -872,7 +1139,11 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
         }
         max_row = std::max(max_row, prow);
         // residual row + norm weights (RMSNorm) or the SwiGLU row, as fp32
-        if (ph.xform == QH_STEP_X_RESNORM) max_res_k = std::max<int64_t>(max_res_k, 2 * K);
+        if (ph.xform == QH_STEP_X_RESNORM) {
+            max_res_k = std::max<int64_t>(max_res_k, K);
+            max_norm_k = std::max<int64_t>(max_norm_k, K);
+            if (!a16(ph.d_xw)) return step_bad("qh_step_create: RMSNorm weights not 16-byte aligned");
+        }
         if (ph.xform == QH_STEP_X_SWIGLU) max_res_k = std::max<int64_t>(max_res_k, K);
         max_x = std::max<int64_t>(max_x, K + (K / QH_QK) * 32 + qhf_q8k_d_stride(K) * 4);
         // rows per tile and split decided below, once the ring size is known
@@ -884,10 +1155,13 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
     // shared-memory plan: header, activation planes, residual row, split
     // terms, DeltaNet state, then the ring
     const int64_t x_bytes = (max_x + 127) / 128 * 128;
-    const int64_t row_bytes = (max_res_k * 4 + 127) / 128 * 128;
+    // (a paired phase keeps at most kStepPairFloats gate/up outputs per CTA
+    // there too: checked below, once its rows per tile are known)
+    const int64_t row_bytes = (std::max<int64_t>(max_res_k, kStepPairFloats) * 4 + 127) / 128 * 128;
     const int64_t x_off = kStepHeader, row_off = x_off + x_bytes, terms_off = row_off + row_bytes;
-    const int64_t state_off = terms_off + kStepTerms;
-    const int64_t ring_off = (state_off + (any_gdn ? kStepGdnBytes : 0) + 127) / 128 * 128;
+    const int64_t w_off = terms_off + kStepTerms, w_floats = (max_norm_k + 31) / 32 * 32;
+    const int64_t state_off = w_off + 2 * w_floats * 4;
+    const int64_t ring_off = (state_off + aux_bytes + 127) / 128 * 128;
     // dynamic shared memory: the opt-in maximum less the kernel's static arrays
     cudaFuncAttributes fa = {};
     if ((e = cudaFuncGetAttributes(&fa, step_kernel)) != cudaSuccess) return step_cuda(e, "cudaFuncGetAttributes");
@@ -902,7 +1176,7 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
         // rows per CTA; at least four tiles fit the ring
         const int64_t r_cap = std::max<int64_t>(8, ((ring_bytes / 4 - 256) / prow) / 8 * 8);
         const int64_t r_bal = (total_rows / (4 * static_cast<int64_t>(sms))) / 8 * 8;
-        const int64_t R = std::min(r_cap, std::max<int64_t>(8, r_bal));
+        const int64_t R = std::min<int64_t>(std::min(r_cap, std::max<int64_t>(8, r_bal)), 8 * kGroupRows);
         int64_t tiles = 0;
         for (int q = 0; q < P.njobs; ++q) {
             StepJob &J = hj[static_cast<size_t>(P.job0 + q)];
@@ -913,6 +1187,8 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
         P.rows_per_tile = static_cast<int32_t>(R);
         P.total_tiles = static_cast<int32_t>(tiles);
         P.split = (!P.act && R == 8 && tiles <= sms && max_nb > 1 && 8 * max_nb <= kStepTermsFloats) ? 1 : 0;
+        if (P.act && 2 * ((tiles / 2 + sms - 1) / sms) * R > kStepPairFloats)
+            return step_bad("qh_step_create: a SwiGLU phase has too many rows per CTA");
     }
     qh_step_prog *prog = new qh_step_prog();
     prog->dev = dev;
@@ -923,7 +1199,8 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
     if ((e = cudaMalloc(&prog->d_phases, hp.size() * sizeof(StepPhase))) != cudaSuccess ||
         (e = cudaMalloc(&prog->d_jobs, std::max<size_t>(1, hj.size()) * sizeof(StepJob))) != cudaSuccess ||
         (e = cudaMalloc(&prog->d_gdns, std::max<size_t>(1, hg.size()) * sizeof(StepGdn))) != cudaSuccess ||
-        (e = cudaMalloc(&prog->d_bar, 64 * sizeof(unsigned))) != cudaSuccess) {
+        (e = cudaMalloc(&prog->d_attns, std::max<size_t>(1, ha.size()) * sizeof(StepAttn))) != cudaSuccess ||
+        (e = cudaMalloc(&prog->d_bar, (kStepBarExit + 32) * sizeof(unsigned))) != cudaSuccess) {
         cleanup();
         return step_cuda(e, "qh_step_create: cudaMalloc");
     }
@@ -935,7 +1212,10 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
         (!hg.empty() &&
          (e = cudaMemcpy(prog->d_gdns, hg.data(), hg.size() * sizeof(StepGdn), cudaMemcpyHostToDevice)) !=
              cudaSuccess) ||
-        (e = cudaMemset(prog->d_bar, 0, 64 * sizeof(unsigned))) != cudaSuccess) {
+        (!ha.empty() &&
+         (e = cudaMemcpy(prog->d_attns, ha.data(), ha.size() * sizeof(StepAttn), cudaMemcpyHostToDevice)) !=
+             cudaSuccess) ||
+        (e = cudaMemset(prog->d_bar, 0, (kStepBarExit + 32) * sizeof(unsigned))) != cudaSuccess) {
         cleanup();
         return step_cuda(e, "qh_step_create: upload");
     }
@@ -957,12 +1237,15 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
     b.phases = prog->d_phases;
     b.jobs = prog->d_jobs;
     b.gdns = prog->d_gdns;
+    b.attns = prog->d_attns;
     b.ring_bytes = static_cast<int32_t>(ring_bytes);
     b.ring_off = static_cast<int32_t>(ring_off);
     b.x_off = static_cast<int32_t>(x_off);
     b.row_off = static_cast<int32_t>(row_off);
     b.terms_off = static_cast<int32_t>(terms_off);
     b.state_off = static_cast<int32_t>(state_off);
+    b.w_off = static_cast<int32_t>(w_off);
+    b.w_floats = static_cast<int32_t>(w_floats);
     b.pos_ptr = d_pos;
     b.bar = prog->d_bar;
     b.err_flag = err;
@@ -1010,6 +1293,7 @@ void qh_step_destroy(qh_step_prog *prog) {
     if (prog->d_phases) cudaFree(prog->d_phases);
     if (prog->d_jobs) cudaFree(prog->d_jobs);
     if (prog->d_gdns) cudaFree(prog->d_gdns);
+    if (prog->d_attns) cudaFree(prog->d_attns);
     if (prog->d_bar) cudaFree(prog->d_bar);
     delete prog;
 }
