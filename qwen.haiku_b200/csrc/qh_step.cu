@@ -510,7 +510,11 @@ __device__ __forceinline__ double attn_sum_hi(double v, double *scratch) {  // w
     return t;
 }
 
-__device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t *scr, const int32_t *pos_ptr) {
+__device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t *scr, const int32_t *pos_ptr,
+                                               uint64_t *tstamp = nullptr) {
+    auto mark = [&](int i) {
+        if (tstamp && threadIdx.x == 0) tstamp[i] = global_ns();
+    };
     constexpr int HD = kStepHD;
     __shared__ double sq[4], sk[4];
     __shared__ float s_red[kConsumerWarps], s_inv;
@@ -558,6 +562,7 @@ __device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t
     float *xrow = hi ? kn : qs;
     xrow[t] = xn;
     consumers_sync();
+    mark(4);
     const int half = A.rope_dim / 2;
     float y = xn;
     if (t < A.rope_dim) {
@@ -611,6 +616,7 @@ __device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t
     for (int off = 16; off > 0; off >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
     if (lane == 0) s_red[warp] = lmax;
     consumers_sync();
+    mark(5);
     float m = s_red[0];
     for (int w = 1; w < kConsumerWarps; ++w) m = fmaxf(m, s_red[w]);
     for (int i = tid; i < n; i += 32 * kConsumerWarps) sc[i] = expf_ref(__fsub_rn(sc[i], m));
@@ -632,6 +638,7 @@ __device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t
     const float inv = s_inv;
     for (int i = tid; i < n; i += 32 * kConsumerWarps) sc[i] = __fmul_rn(sc[i], inv);
     consumers_sync();
+    mark(6);
     // ---- weighted V sum, per dim in position order ----
     float o = 0.0f;
     for (int q = 0; q < n_chunks; ++q) {
@@ -650,6 +657,7 @@ __device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t
         o = __fadd_rn(o, __fmul_rn(sc[pos], vn[tid]));
         A.ctx[static_cast<int64_t>(j) * HD + tid] = __fmul_rn(o, sigmoid_f(gt));
     }
+    mark(7);
 }
 
 // Runtime-typed 8-row group consumer (one token).
@@ -833,7 +841,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
         const StepPhase &P = p.phases[p.first + k];
         if (P.kind == kPhaseAttn) {
             const StepAttn &A = p.attns[P.gdn];
-            if (static_cast<int>(blockIdx.x) < A.nh) step_attn_head(A, blockIdx.x, reinterpret_cast<uint8_t *>(st_s), p.pos_ptr);
+            uint64_t *ts = (p.stamps && blockIdx.x == 0)
+                               ? p.stamps + static_cast<int64_t>(p.first + k) * (kStampFixed + gridDim.x)
+                               : nullptr;
+            if (static_cast<int>(blockIdx.x) < A.nh)
+                step_attn_head(A, blockIdx.x, reinterpret_cast<uint8_t *>(st_s), p.pos_ptr, ts);
         } else if (P.kind == kPhaseGdn) {
             const StepGdn &G = p.gdns[P.gdn];
             if (static_cast<int>(blockIdx.x) < G.heads) {
