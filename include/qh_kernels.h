@@ -333,6 +333,16 @@ void qh_step_destroy(qh_step_prog *prog);
  * setting they were captured with. */
 int qh_step_set_stamps(qh_step_prog *prog, uint64_t *d_stamps);
 int32_t qh_step_phase_count(const qh_step_prog *prog);
+/* Failure-detection test hook (no reference counterpart): the program's next
+ * launches leave out the copy of the tile that CTA 0 streams as its number
+ * `tile` (counted from 0 over the launch's projection phases; -1: none), and
+ * every shared-memory barrier wait polls at most wait_limit times (0: the
+ * kernel's default, seconds) -- the path of a lost copy: CTA 0 records the
+ * timeout in the device error word and stops, the other CTAs leave at their
+ * next grid barrier, every CTA waits (bounded) for its own copies in flight,
+ * and qh_check_device_error reports QH_ERR_DEVICE. Nothing faults; the
+ * outputs of such a launch are not defined. */
+int qh_step_test_timeout(qh_step_prog *prog, int32_t tile, uint32_t wait_limit);
 
 #ifdef __cplusplus
 }

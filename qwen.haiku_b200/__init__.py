@@ -201,6 +201,7 @@ SIGNATURES.update({  # include/qh_kernels.h
     "qh_step_destroy": (None, [_P]),
     "qh_step_set_stamps": (_I, [_P, _P]),
     "qh_step_phase_count": (C.c_int32, [_P]),
+    "qh_step_test_timeout": (_I, [_P, C.c_int32, C.c_uint32]),
     "qh_embed_q6k": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
     "qh_embed_f32": (_I, [_P, _I64, _P, C.c_int32, _P, _P]),
     "qh_rmsnorm": (_I, [_P, _P, _I64, _I64, C.c_float, _P, _P]),

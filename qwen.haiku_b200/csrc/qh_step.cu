@@ -133,6 +133,11 @@ struct StepParams {
     unsigned *bar;
     int *err_flag;
     uint64_t *stamps;  // measurement hook (qh_step_set_stamps), or null
+    // failure-detection test hook (qh_step_test_timeout): tile number
+    // test_tile of CTA 0 gets no copy (-1: none); mbarrier waits poll at most
+    // wait_limit times (0: kWaitLimit)
+    int32_t test_tile;
+    uint32_t wait_limit;
 };
 
 // ---------------------------------------------------------------------------
@@ -371,7 +376,8 @@ __device__ __forceinline__ void step_gdn_gates(const StepGdn &g, int h, float *g
 }
 
 __device__ __forceinline__ void step_gdn_head(const StepGdn &g, int h, float *st_s, uint64_t *st_bar, uint32_t parity,
-                                              const int32_t *pos_ptr, int *err, uint64_t *tstamp, const float *gates) {
+                                              const int32_t *pos_ptr, int *err, uint64_t *tstamp, const float *gates,
+                                              uint32_t lim) {
     auto mark = [&](int i) {
         if (tstamp && threadIdx.x == 0) tstamp[i] = global_ns();
     };
@@ -388,7 +394,7 @@ __device__ __forceinline__ void step_gdn_head(const StepGdn &g, int h, float *st
     for (int part = 0; part < 3; ++part) xin[part] = ldcg_f(g.qkv + part * kdim + h * HD + t);
     const float zv = ldcg_f(g.z + h * HD + t);
     // state, conv ring rows and conv weights were copied in during the phase before
-    if (!mbar_wait(st_bar, parity)) report_error(err, kDevWaitTimeout);
+    if (!mbar_wait_n(st_bar, parity, lim)) report_error(err, kDevWaitTimeout);
     mark(5);
     float cw[3][kk], rows[3][kk];
 #pragma unroll
@@ -700,6 +706,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     uint8_t *ring = smem + p.ring_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t RB = static_cast<uint32_t>(p.ring_bytes);
+    const uint32_t lim = p.wait_limit ? p.wait_limit : kWaitLimit;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStepSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -716,6 +723,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     if (warp == kConsumerWarps) {
         // ----- producer (lane 0): every projection phase's tiles of this CTA, in order -----
         if (lane != 0) return;
+        auto withheld = [&](int q) { return p.test_tile >= 0 && blockIdx.x == 0 && q == p.test_tile; };
         uint32_t vstart[kStepSlots];
         uint64_t vhead = 0;
         int i = 0, oldest = 0;
@@ -754,7 +762,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                 if (static_cast<uint32_t>(vs % RB) + sz > RB) vs = (vs / RB + 1) * RB;
                 while (oldest < i && (i - oldest >= kStepSlots || vs + sz - vstart[oldest % kStepSlots] > RB)) {
                     if (*abort_flag ||
-                        !mbar_wait(&empty[oldest % kStepSlots], static_cast<uint32_t>(oldest / kStepSlots) & 1u)) {
+                        !mbar_wait_n(&empty[oldest % kStepSlots], static_cast<uint32_t>(oldest / kStepSlots) & 1u, lim)) {
                         report_error(p.err_flag, kDevWaitTimeout);
                         *abort_flag = 1;
                         stop = true;
@@ -779,6 +787,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                 M.k = J.k;
                 M.row_bytes = J.row_bytes;
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                if (withheld(i)) continue;  // test hook: this tile never arrives
                 if (wbytes) {
                     mbar_arrive_expect_tx(&full[s], wbytes);
                     bulk_copy_g2s(dst, a0, wbytes, &full[s]);
@@ -789,7 +798,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
         }
         // Drain: no copy of this CTA stays in flight past its exit.
         for (int q = max(0, i - kStepSlots); q < i; ++q)
-            if (!mbar_wait(&full[q % kStepSlots], static_cast<uint32_t>(q / kStepSlots) & 1u))
+            if (!withheld(q) && !mbar_wait_n(&full[q % kStepSlots], static_cast<uint32_t>(q / kStepSlots) & 1u, lim))
                 report_error(p.err_flag, kDevWaitTimeout);
         return;
     }
@@ -853,7 +862,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                                    ? p.stamps + static_cast<int64_t>(p.first + k) * (kStampFixed + gridDim.x)
                                    : nullptr;
                 if (warp < kStepHD / 32)
-                    step_gdn_head(G, blockIdx.x, st_s, st_bar, n_gdn & 1u, p.pos_ptr, p.err_flag, ts, gates);
+                    step_gdn_head(G, blockIdx.x, st_s, st_bar, n_gdn & 1u, p.pos_ptr, p.err_flag, ts, gates, lim);
                 else if (warp == kStepHD / 32)
                     step_gdn_gates(G, blockIdx.x, gates);
                 ++n_gdn;
@@ -863,7 +872,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
             my_tiles(P, t0, t1);
             if (w_here) {  // this phase's RMSNorm weights
                 const int b = k & 1;
-                if (!mbar_wait(&wbar[b], wuse[b] & 1u)) report_error(p.err_flag, kDevWaitTimeout);
+                if (!mbar_wait_n(&wbar[b], wuse[b] & 1u, lim)) report_error(p.err_flag, kDevWaitTimeout);
                 ++wuse[b];
                 stamp(p, p.first + k, 6);
             }
@@ -900,7 +909,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                 for (int t = t0; t < t1; ++t, ++i) {
                     const int s = i % kStepSlots;
                     const bool got = !*abort_flag &&
-                                     mbar_wait(&full[s], static_cast<uint32_t>(i / kStepSlots) & 1u);
+                                     mbar_wait_n(&full[s], static_cast<uint32_t>(i / kStepSlots) & 1u, lim);
                     if (bar_any(1, 32 * kConsumerWarps, !got)) {
                         if (!got) {
                             report_error(p.err_flag, kDevWaitTimeout);
@@ -934,7 +943,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                 const int ng = (t1 - t0) * gpt;
                 for (int G = warp; G < ng; G += kConsumerWarps) {
                     const int tl = G / gpt, gi = G - tl * gpt, ii = i + tl, s = ii % kStepSlots;
-                    if (*abort_flag || !mbar_wait(&full[s], static_cast<uint32_t>(ii / kStepSlots) & 1u)) {
+                    if (*abort_flag || !mbar_wait_n(&full[s], static_cast<uint32_t>(ii / kStepSlots) & 1u, lim)) {
                         report_error(p.err_flag, kDevWaitTimeout);
                         *abort_flag = 1;
                         ok = false;
@@ -1261,6 +1270,8 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
     b.pos_ptr = d_pos;
     b.bar = prog->d_bar;
     b.err_flag = err;
+    b.test_tile = -1;
+    b.wait_limit = 0;
     *out = prog;
     return QH_OK;
 }
@@ -1299,6 +1310,13 @@ int qh_step_set_stamps(qh_step_prog *prog, uint64_t *d_stamps) {
 }
 
 int32_t qh_step_phase_count(const qh_step_prog *prog) { return prog ? prog->nphases : -1; }
+
+int qh_step_test_timeout(qh_step_prog *prog, int32_t tile, uint32_t wait_limit) {
+    if (!prog || tile < -1) return step_bad("qh_step_test_timeout: bad arguments");
+    prog->base.test_tile = tile;
+    prog->base.wait_limit = wait_limit;
+    return QH_OK;
+}
 
 void qh_step_destroy(qh_step_prog *prog) {
     if (!prog) return;

@@ -232,3 +232,58 @@ def test_models_that_do_not_qualify_run_launches(qh, cuda):
         slm.step(np.zeros(n_seq, np.int32), 0)
         assert slm.decode_mode() == qh.DECODE_LAUNCHES
         slm.close()
+
+
+def test_step_timeout_is_reported_and_recovers(qh, cuda):
+    """Failure detection without a fault: qh_step_test_timeout leaves out one
+    tile's copy in CTA 0 with a short wait limit. The launch ends by itself
+    (every wait is bounded; the other CTAs leave at their next grid barrier),
+    qh_check_device_error reports QH_ERR_DEVICE once, and the same program
+    then runs clean with the hook off, equal bit for bit to the separate
+    kernels."""
+    torch = cuda
+    h = qh.host
+    L = qh.lib()
+    H, N1, N2 = 1024, 3000, 1024
+    a = h.to_device(h.synth_normal(H, 0x7101))
+    w = h.to_device(h.synth_normal(H, 0x7102, 1.0, 0.02))
+    x2 = h.to_device(h.synth_normal(3584, 0x7103))
+    w1 = h.to_device(h.synth_blocks(Q4_K, N1 * H // 256, 0x7201))
+    w2 = h.to_device(h.synth_blocks(Q6_K, N2 * 3584 // 256, 0x7202))
+    s = h.stream_handle()
+    ref1 = torch.empty(N1, dtype=torch.float32, device="cuda")
+    ref2 = torch.empty(N2, dtype=torch.float32, device="cuda")
+    xq1 = torch.empty(int(L.qh_q8k_bytes(H, 1)), dtype=torch.uint8, device="cuda")
+    xq2 = torch.empty(int(L.qh_q8k_bytes(3584, 1)), dtype=torch.uint8, device="cuda")
+    qh.check(L.qh_rmsnorm_q8k(h.dptr(a), None, None, h.dptr(w), H, 1, 1e-6, h.dptr(xq1), 0, s), "rn")
+    p1 = h.MatvecPlan(Q4_K, [(w1, xq1, ref1, H, N1)], 1)
+    p1.run()
+    qh.check(L.qh_quantize_q8k(h.dptr(x2), 3584, 1, h.dptr(xq2), s), "quantize")
+    p2 = h.MatvecPlan(Q6_K, [(w2, xq2, ref2, 3584, N2)], 1)
+    p2.run()
+    torch.cuda.synchronize()
+    out1 = torch.empty(N1, dtype=torch.float32, device="cuda")
+    out2 = torch.empty(N2, dtype=torch.float32, device="cuda")
+    pos = torch.zeros(4, dtype=torch.int32, device="cuda")
+    phases = [matvec_phase(qh, qh.STEP_X_RESNORM, H, a, None, w, None, projs=[(Q4_K, w1, N1, out1)]),
+              matvec_phase(qh, qh.STEP_X_QUANT, 3584, x2, projs=[(Q6_K, w2, N2, out2)])]
+    prog = make_program(qh, phases, pos)
+    try:
+        assert L.qh_check_device_error(None) == 0
+        qh.check(L.qh_step_test_timeout(prog, 1, 1 << 12), "qh_step_test_timeout")
+        qh.check(L.qh_step_run(prog, 0, 2, s), "qh_step_run (tile withheld)")
+        torch.cuda.synchronize()
+        assert L.qh_check_device_error(None) == -6  # QH_ERR_DEVICE
+        assert L.qh_check_device_error(None) == 0   # read and cleared
+        qh.check(L.qh_step_test_timeout(prog, -1, 0), "qh_step_test_timeout off")
+        for _ in range(2):
+            out1.fill_(5.0)
+            out2.fill_(5.0)
+            qh.check(L.qh_step_run(prog, 0, 2, s), "qh_step_run")
+            torch.cuda.synchronize()
+            assert L.qh_check_device_error(None) == 0
+            assert torch.equal(bits(out1), bits(ref1)) and torch.equal(bits(out2), bits(ref2))
+    finally:
+        L.qh_step_destroy(prog)
+        p1.close()
+        p2.close()
