@@ -1062,6 +1062,133 @@ __global__ void __launch_bounds__(HD)
     if (t == 0) bulk_wait_all();  // the state store has completed before the CTA exits
 }
 
+// Gated DeltaNet token update for many (sequence, head) pairs, persistent
+// and pipelined: CTA c (128 threads, three per SM) takes pairs c,
+// c + gridDim.x, ...; thread t holds state column t in registers while it is
+// updated, and the next pair's 64 KB state is copied into shared memory (one
+// bulk copy) while the current pair computes -- so the state stream and the
+// double-precision chains overlap instead of taking turns wave by wave. Per
+// pair the operations and orders of gdn_fused_kernel<128, false>.
+template <int KK>
+__global__ void __launch_bounds__(128, 2)
+    gdn_stream_kernel(const float *__restrict__ qkv, float *__restrict__ ring, const float *__restrict__ conv_w,
+                      const float *__restrict__ bb, const float *__restrict__ aa, const float *__restrict__ dt_bias,
+                      const float *__restrict__ ssm_a, float *__restrict__ state, const float *__restrict__ z,
+                      const float *__restrict__ norm_w, int heads, float eps, const int32_t *__restrict__ pos_ptr,
+                      int n_pairs, int *__restrict__ err_flag, float *__restrict__ y_out) {
+    constexpr int HD = 128;
+    pdl_launch_dependents();
+    extern __shared__ __align__(128) float st_s[];  // [HD k][HD v]: the next pair's state
+    __shared__ uint64_t st_bar;
+    __shared__ double scratch[64];
+    __shared__ float Ks[HD], Qs[HD];
+    __shared__ float s_beta, s_g;
+    const int t = threadIdx.x;
+    const int kdim = heads * HD, conv_dim = 3 * kdim;
+    if (t == 0) {
+        mbar_init(&st_bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    int pair = blockIdx.x;
+    auto issue = [&](int pr) {  // thread 0
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the column reads come first
+        mbar_arrive_expect_tx(&st_bar, HD * HD * 4);
+        bulk_copy_g2s(st_s, state + static_cast<int64_t>(pr) * HD * HD, HD * HD * 4, &st_bar);
+    };
+    if (t == 0 && pair < n_pairs) issue(pair);
+    const int pos = max(*pos_ptr, 0);
+    const int slot = pos % KK, head_after = (pos + 1) % KK;
+    uint32_t parity = 0;
+    for (; pair < n_pairs; pair += gridDim.x) {
+        const int b = pair / heads, h = pair % heads;
+        // ---- conv ring + SiLU + L2 norms + beta/g (gdn_fused_kernel's order) ----
+        float cw[3][KK];
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+#pragma unroll
+            for (int k = 0; k < KK; ++k) cw[part][k] = conv_w[(part * kdim + h * HD + t) * KK + k];
+        const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
+        float *rg = ring + static_cast<int64_t>(b) * KK * conv_dim;
+        float xin[3], rows[3][KK];
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const int ch = part * kdim + h * HD + t;
+            xin[part] = src[ch];
+#pragma unroll
+            for (int r = 0; r < KK; ++r) rows[part][r] = rg[static_cast<int64_t>(r) * conv_dim + ch];
+        }
+        if (t == 32) {
+            const int i = b * heads + h;
+            s_beta = sigmoid_f(bb[i]);
+            const float a = __fadd_rn(aa[i], dt_bias[h]);
+            const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
+            s_g = expf_ref(__fmul_rn(ssm_a[h], sp));
+        }
+        float mixed[3];
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const int ch = part * kdim + h * HD + t;
+            float taps[KK - 1];
+#pragma unroll
+            for (int k = 0; k < KK - 1; ++k) {
+                const int rsel = (head_after + k) % KK;
+                float v = 0.0f;
+#pragma unroll
+                for (int r = 0; r < KK; ++r)
+                    if (r == rsel) v = rows[part][r];
+                taps[k] = v;
+            }
+            rg[static_cast<int64_t>(slot) * conv_dim + ch] = xin[part];
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < KK; ++k) acc = __fadd_rn(acc, __fmul_rn(k < KK - 1 ? taps[k] : xin[part], cw[part][k]));
+            mixed[part] = silu_f(acc);
+        }
+        const double2 qkss = block_sum_d2(static_cast<double>(__fmul_rn(mixed[0], mixed[0])),
+                                          static_cast<double>(__fmul_rn(mixed[1], mixed[1])), scratch);
+        const float qrs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qkss.x)), 1e-6f));
+        const float krs = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn(static_cast<float>(qkss.y)), 1e-6f));
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
+        Qs[t] = __fmul_rn(__fmul_rn(mixed[0], qrs), scale);
+        Ks[t] = __fmul_rn(mixed[1], krs);
+        const float vt = mixed[2];
+        const int64_t zi = static_cast<int64_t>(b) * kdim + h * HD + t;
+        const float zv = z[zi];
+        // ---- the state column into registers; the buffer then takes the next pair ----
+        if (!mbar_wait(&st_bar, parity)) report_error(err_flag, kDevWaitTimeout);
+        parity ^= 1u;
+        float S[HD];
+#pragma unroll
+        for (int k = 0; k < HD; ++k) S[k] = st_s[k * HD + t];
+        __syncthreads();  // every column read (and Ks, Qs, s_g, s_beta written)
+        if (t == 0 && pair + static_cast<int>(gridDim.x) < n_pairs) issue(pair + gridDim.x);
+        // ---- recurrence (gdn_fused_kernel's two chains) ----
+        const float gh = s_g, bh = s_beta;
+        double acc = 0.0;
+#pragma unroll
+        for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(S[k], gh), Ks[k]));
+        const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
+        double acc2 = 0.0;
+#pragma unroll
+        for (int k = 0; k < HD; ++k) {
+            S[k] = __fadd_rn(__fmul_rn(S[k], gh), __fmul_rn(Ks[k], delta));
+            acc2 += static_cast<double>(__fmul_rn(S[k], Qs[k]));
+        }
+        const float o = static_cast<float>(acc2);
+        float *st = state + static_cast<int64_t>(pair) * HD * HD;
+#pragma unroll
+        for (int k = 0; k < HD; ++k) st[k * HD + t] = S[k];
+        // ---- gated RMSNorm ----
+        const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
+        const float mean = static_cast<float>(ssq / static_cast<double>(HD));
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        y_out[zi] = __fmul_rn(__fmul_rn(__fmul_rn(o, rs), norm_w[t]), silu_f(zv));
+        __syncthreads();  // Ks, Qs and the scratch are rewritten by the next pair
+    }
+}
+
 // Gated DeltaNet over a chunk of n_tok prompt tokens per sequence: CTA
 // (sequence, head) runs, token after token, exactly the per-token work of
 // gdn_fused_kernel (same operations and order), with the head's state in
@@ -1355,6 +1482,21 @@ static int gdn_fused_impl(const float *d_qkv, float *d_ring, const float *d_conv
     if (!err) return bad("gdn: no device error word");
     const dim3 grid(static_cast<unsigned>(B), heads);
     cudaError_t le;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t pairs = static_cast<int64_t>(B) * heads;
+    if (d_y && kk == 4 && pairs > 2 * static_cast<int64_t>(sms)) {
+        // many (sequence, head) pairs: the persistent pipelined form
+        static bool sattr[64] = {};
+        if (dev >= 0 && dev < 64 && !sattr[dev]) {
+            cudaFuncSetAttribute(qh::gdn_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
+            sattr[dev] = true;
+        }
+        le = qh::launch_pdl(qh::gdn_stream_kernel<4>, dim3(static_cast<unsigned>(2 * sms)), dim3(128), 128 * 128 * 4,
+                            static_cast<cudaStream_t>(stream), d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a,
+                            d_state, d_z, d_norm_w, heads, eps, d_pos, static_cast<int>(pairs), err, d_y);
+        return launch_status(le, what);
+    }
     if (d_y)
         le = qh::launch_pdl(qh::gdn_fused_kernel<128, false>, grid, dim3(128), 128 * 128 * 4,
                             static_cast<cudaStream_t>(stream), d_qkv, d_ring, d_conv_w, d_b, d_a, d_dt_bias, d_ssm_a,
