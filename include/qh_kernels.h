@@ -324,11 +324,14 @@ int qh_step_create(const qh_step_phase *phases, int32_t n_phases, const int32_t 
 int qh_step_run(qh_step_prog *prog, int32_t first, int32_t count, void *stream);
 void qh_step_destroy(qh_step_prog *prog);
 /* Measurement hook: with d_stamps non-null (qh_step_phase_count records of
- * 8 + G uint64, G = the device's SM count, the launch's CTAs), later
+ * 8 + 2G uint64, G = the device's SM count, the launch's CTAs), later
  * launches write %globaltimer (ns) per phase p into record p: [0] CTA 0 at
  * the phase start, [1] input formed, [2] work done, [3] past the grid
- * barrier; [4..7] inside a DeltaNet head update of CTA 0 (inputs ready,
- * state landed, recurrence done, output written); [8 + c] CTA c's work done.
+ * barrier; [4..7] points inside the phase's work on CTA 0 (DeltaNet: inputs
+ * ready, state landed, recurrence done, output written; attention: norms
+ * done, scores, softmax, output written; RMSNorm inputs: sums formed, block
+ * sum done, weights landed); [8 + c] CTA c's work done; [8 + G + c] CTA c's
+ * input formed.
  * Null turns it off. Launches already captured in a CUDA graph keep the
  * setting they were captured with. */
 int qh_step_set_stamps(qh_step_prog *prog, uint64_t *d_stamps);

@@ -185,7 +185,7 @@ int qh_slm_set_decode_mode(qh_slm *m, int32_t mode);
 int32_t qh_slm_decode_mode(const qh_slm *m);
 /* The persistent step's measurement hook (qh_step_set_stamps) for the next
  * steps of m: returns the number of phases P (d_stamps holds P records of
- * 8 + SM-count uint64), or QH_ERR_UNSUPPORTED when m does not run
+ * 8 + 2 * SM-count uint64), or QH_ERR_UNSUPPORTED when m does not run
  * QH_DECODE_PERSISTENT (after its first step). Replaces the captured step
  * graphs. */
 int qh_slm_step_stamps(qh_slm *m, uint64_t *d_stamps);

@@ -211,18 +211,19 @@ __device__ __forceinline__ bool step_grid_barrier(const StepParams &p, unsigned 
 }
 
 // Measurement hook (qh_step_set_stamps), per phase ph a record of
-// kStampFixed + gridDim.x words: [0..3] CTA 0's %globaltimer at the phase
-// start, input formed, work done, past the barrier; [4..7] inside a DeltaNet
-// head update of CTA 0 (inputs ready, state landed, recurrence done, output
-// written); [8 + c] CTA c's work done.
+// kStampFixed + 2 * gridDim.x words: [0..3] CTA 0's %globaltimer at the phase
+// start, input formed, work done, past the barrier; [4..7] points inside the
+// phase's work on CTA 0; [8 + c] CTA c's work done, [8 + G + c] CTA c's input
+// formed.
 constexpr int kStampFixed = 8;
+__device__ __forceinline__ int64_t stamp_rec(int ph) { return static_cast<int64_t>(ph) * (kStampFixed + 2 * gridDim.x); }
 __device__ __forceinline__ void stamp(const StepParams &p, int ph, int what) {
-    if (p.stamps && blockIdx.x == 0 && threadIdx.x == 0)
-        p.stamps[static_cast<int64_t>(ph) * (kStampFixed + gridDim.x) + what] = global_ns();
+    if (p.stamps && blockIdx.x == 0 && threadIdx.x == 0) p.stamps[stamp_rec(ph) + what] = global_ns();
 }
-__device__ __forceinline__ void stamp_cta(const StepParams &p, int ph) {
+// [8 + c]: CTA c's work done; [8 + G + c]: CTA c's input formed
+__device__ __forceinline__ void stamp_cta(const StepParams &p, int ph, int second = 0) {
     if (p.stamps && threadIdx.x == 0)
-        p.stamps[static_cast<int64_t>(ph) * (kStampFixed + gridDim.x) + kStampFixed + blockIdx.x] = global_ns();
+        p.stamps[stamp_rec(ph) + kStampFixed + second * gridDim.x + blockIdx.x] = global_ns();
 }
 
 // ---------------------------------------------------------------------------
@@ -550,8 +551,18 @@ __device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     for (int q = 0; q < kAttnBufs - 1; ++q) issue_v(q);
-    // ---- norms and MRoPE (attn_pre_kernel) ----
+    // Loads that do not wait for this phase's inputs go first: the norm
+    // weight and this thread's rope pair.
     const bool hi = warp >= 4;
+    const float wnorm = __ldg((hi ? A.kn_w : A.qn_w) + t);
+    const int half = A.rope_dim / 2;
+    float rco = 1.0f, rsn = 0.0f;
+    if (t < A.rope_dim) {
+        const int i = t < half ? t : t - half;
+        rco = __ldg(A.rope + (static_cast<int64_t>(pos) * half + i) * 2);
+        rsn = __ldg(A.rope + (static_cast<int64_t>(pos) * half + i) * 2 + 1);
+    }
+    // ---- norms and MRoPE (attn_pre_kernel) ----
     float x, gt = 0.0f;
     if (!hi) {
         const float *src = A.qraw + static_cast<int64_t>(j) * 2 * HD;
@@ -564,19 +575,17 @@ __device__ __forceinline__ void step_attn_head(const StepAttn &A, int j, uint8_t
     const double ssq = hi ? attn_sum_hi(static_cast<double>(__fmul_rn(x, x)), sk)
                           : gdn_sum_d(static_cast<double>(__fmul_rn(x, x)), sq);
     const float rscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(HD)), A.eps)));
-    const float xn = __fmul_rn(__fmul_rn(x, rscale), __ldg((hi ? A.kn_w : A.qn_w) + t));
+    const float xn = __fmul_rn(__fmul_rn(x, rscale), wnorm);
     float *xrow = hi ? kn : qs;
     xrow[t] = xn;
     consumers_sync();
     mark(4);
-    const int half = A.rope_dim / 2;
     float y = xn;
     if (t < A.rope_dim) {
         const int i = t < half ? t : t - half;
-        const float co = __ldg(A.rope + (static_cast<int64_t>(pos) * half + i) * 2);
-        const float sn = __ldg(A.rope + (static_cast<int64_t>(pos) * half + i) * 2 + 1);
         const float x0 = xrow[i], x1 = xrow[i + half];
-        y = t < half ? __fsub_rn(__fmul_rn(x0, co), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, co));
+        y = t < half ? __fsub_rn(__fmul_rn(x0, rco), __fmul_rn(x1, rsn))
+                     : __fadd_rn(__fmul_rn(x0, rsn), __fmul_rn(x1, rco));
     }
     consumers_sync();  // every thread has read xrow
     if (!hi) {
@@ -851,7 +860,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
         if (P.kind == kPhaseAttn) {
             const StepAttn &A = p.attns[P.gdn];
             uint64_t *ts = (p.stamps && blockIdx.x == 0)
-                               ? p.stamps + static_cast<int64_t>(p.first + k) * (kStampFixed + gridDim.x)
+                               ? p.stamps + stamp_rec(p.first + k)
                                : nullptr;
             if (static_cast<int>(blockIdx.x) < A.nh)
                 step_attn_head(A, blockIdx.x, reinterpret_cast<uint8_t *>(st_s), p.pos_ptr, ts);
@@ -859,7 +868,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
             const StepGdn &G = p.gdns[P.gdn];
             if (static_cast<int>(blockIdx.x) < G.heads) {
                 uint64_t *ts = (p.stamps && blockIdx.x == 0)
-                                   ? p.stamps + static_cast<int64_t>(p.first + k) * (kStampFixed + gridDim.x)
+                                   ? p.stamps + stamp_rec(p.first + k)
                                    : nullptr;
                 if (warp < kStepHD / 32)
                     step_gdn_head(G, blockIdx.x, st_s, st_bar, n_gdn & 1u, p.pos_ptr, p.err_flag, ts, gates, lim);
@@ -877,11 +886,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
                 stamp(p, p.first + k, 6);
             }
             uint64_t *fts = (p.stamps && blockIdx.x == 0)
-                                ? p.stamps + static_cast<int64_t>(p.first + k) * (kStampFixed + gridDim.x)
+                                ? p.stamps + stamp_rec(p.first + k)
                                 : nullptr;
             if (t0 < t1) step_form_input(P, xs, rowbuf, wpre + (k & 1) * p.w_floats, fts);  // a CTA without tiles needs no input
             consumers_sync();
             stamp(p, p.first + k, 1);
+            stamp_cta(p, p.first + k, 1);
             // paired phase: the CTA's gate / up outputs stay in shared memory
             // (rowbuf, free once the input is formed) for the SwiGLU epilogue
             const int pr0 = P.act ? (t0 >> 1) * P.rows_per_tile : 0;
