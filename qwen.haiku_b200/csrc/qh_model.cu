@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
                                                               const __half *__restrict__ vcache,
                                                               const float *__restrict__ gate, int nh, int kvh,
                                                               const int32_t *__restrict__ pos_ptr, int max_pos,
-                                                              float *__restrict__ ctx, int rows_per_seq) {
+                                                              float *__restrict__ ctx, int rows_per_seq, int qgroup) {
     constexpr int HD = 128;
     pdl_launch_dependents();
     pdl_wait();
@@ -380,9 +380,12 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     __half *vbuf = reinterpret_cast<__half *>(sc + G * ((max_pos + 3) & ~3));
     __shared__ float red[G][32];
     __shared__ float s_inv[G];
-    // CTA (sequence b, KV head kh, query j): the query row b * rows_per_seq + j
-    // at position *pos_ptr + j (decode: j = 0, one row per sequence)
-    const int b = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    // CTA (sequence b, query heads q0 .. q0 + G - 1, query j): the query row
+    // b * rows_per_seq + j at position *pos_ptr + j (decode: j = 0, one row per
+    // sequence); the heads share KV head q0 / qgroup (G == qgroup: one CTA per
+    // KV head, every cache row read once for its G heads; G == 1: one CTA per
+    // query head, each reading the rows again -- more CTAs for many sequences)
+    const int b = blockIdx.x, q0 = blockIdx.y * G, kh = q0 / qgroup, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t qrow = static_cast<int64_t>(b) * rows_per_seq + blockIdx.z;
     const int pos = min(max(*pos_ptr + static_cast<int>(blockIdx.z), 0), max_pos - 1);
     const int n = pos + 1;
@@ -409,7 +412,7 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     // the first V chunks stream in while the scores are formed
     for (int c = 0; c < kAttnVBufs - 1; ++c) issue_v(c);
 #pragma unroll
-    for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(qrow * nh + kh * G + g) * HD + t];
+    for (int g = 0; g < G; ++g) qs[g * HD + t] = q[(qrow * nh + q0 + g) * HD + t];
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HD)));
     float lmax[G];
@@ -520,7 +523,7 @@ __global__ void __launch_bounds__(128) attn_decode_gqa_kernel(const float *__res
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const int64_t oi = qrow * nh * HD + (kh * G + g) * HD + t;
+        const int64_t oi = qrow * nh * HD + (q0 + g) * HD + t;
         ctx[oi] = __fmul_rn(o[g], sigmoid_f(gate[oi]));
     }
 }
@@ -696,29 +699,36 @@ bool gqa_ok(int32_t nh, int32_t kvh, int32_t hd, const void *kc) {
 int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_vcache, const float *d_gate,
                   int32_t n_seq, int32_t rows_per_seq, int32_t nh, int32_t kvh, const int32_t *d_pos,
                   int32_t max_pos, float *d_ctx, void *stream, const char *what) {
-    const int G = nh / kvh;
+    const int qgroup = nh / kvh;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // Query heads per CTA: the whole group (each cache row read once for all
+    // of them) when that already fills the GPU twice over, else one (more
+    // CTAs, each reading the rows again: decode at up to ~100 sequences)
+    const int64_t group_ctas = static_cast<int64_t>(n_seq) * rows_per_seq * kvh;
+    const int G = group_ctas >= 2 * static_cast<int64_t>(sms) ? qgroup : 1;
     const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + ((static_cast<size_t>(max_pos) + 3) & ~size_t(3))) +
                         qh::kAttnVBufs * qh::kAttnVChunk * 128 * sizeof(__half);
     if (smem > 200 * 1024) return bad("attention: context too long");
     if (rows_per_seq > 65535) return bad(what);
     static bool gattr[64][4] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
     const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
     void (*kern)(const float *, const __half *, const __half *, const float *, int, int, const int32_t *, int, float *,
-                 int) = G == 1   ? qh::attn_decode_gqa_kernel<1>
-                        : G == 2 ? qh::attn_decode_gqa_kernel<2>
-                        : G == 4 ? qh::attn_decode_gqa_kernel<4>
-                                 : qh::attn_decode_gqa_kernel<8>;
+                 int, int) = G == 1   ? qh::attn_decode_gqa_kernel<1>
+                             : G == 2 ? qh::attn_decode_gqa_kernel<2>
+                             : G == 4 ? qh::attn_decode_gqa_kernel<4>
+                                      : qh::attn_decode_gqa_kernel<8>;
     if (dev >= 0 && dev < 64 && !gattr[dev][gi]) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         gattr[dev][gi] = true;
     }
-    const cudaError_t le = qh::launch_pdl(kern, dim3(static_cast<unsigned>(n_seq), kvh, rows_per_seq), dim3(128), smem,
-                                          static_cast<cudaStream_t>(stream), d_q,
+    const cudaError_t le = qh::launch_pdl(kern, dim3(static_cast<unsigned>(n_seq), nh / G, rows_per_seq), dim3(128),
+                                          smem, static_cast<cudaStream_t>(stream), d_q,
                                           reinterpret_cast<const __half *>(d_kcache),
                                           reinterpret_cast<const __half *>(d_vcache), d_gate, nh, kvh, d_pos, max_pos,
-                                          d_ctx, rows_per_seq);
+                                          d_ctx, rows_per_seq, qgroup);
     return launch_status(le, what);
 }
 }  // namespace
