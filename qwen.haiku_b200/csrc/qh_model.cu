@@ -26,6 +26,7 @@
 #include "../../include/qh_kernels.h"
 #include "qh_common.cuh"
 #include "qh_internal.h"
+#include "qh_gdn.cuh"
 #include "qh_q8k.cuh"
 
 namespace qh {
@@ -986,26 +987,9 @@ __global__ void __launch_bounds__(HD)
     // The column is read from shared memory in both passes (the decayed
     // value recomputed), which keeps registers low enough for several
     // heads per SM.
-    double acc = 0.0;
-#pragma unroll 16
-    for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
-    const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
-    // one pass over the column: update each entry (independent per k) and
-    // add its product with Q to the output sum -- the sequential double
-    // chain runs over the updated values in k order, as in the reference
-    double acc2 = 0.0;
-    {
-        float *__restrict__ sc = st_s + t;
-        const float *__restrict__ kv = Ks;
-        const float *__restrict__ qv = Qs;
-#pragma unroll 16
-        for (int k = 0; k < HD; ++k) {
-            const float sn = __fadd_rn(__fmul_rn(sc[k * HD], gh), __fmul_rn(kv[k], delta));
-            sc[k * HD] = sn;
-            acc2 += static_cast<double>(__fmul_rn(sn, qv[k]));
-        }
-    }
-    const float o = static_cast<float>(acc2);
+    // both chains over the column, and its update in the same pass as the
+    // output sum, in k order as in the reference (qh_gdn.cuh)
+    const float o = gdn_recur_column<HD>(st_s + t, Ks, Qs, gh, bh, vt);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (t == 0) {
@@ -1286,24 +1270,7 @@ __global__ void __cluster_dims__(1, 2, 1) __launch_bounds__(HD)
             have_state = true;
         }
         const float gh = s_g, bh = s_beta;
-        double acc = 0.0;
-#pragma unroll 16
-        for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
-        const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
-        // update and output sum in one pass (see gdn_fused_kernel)
-        double acc2 = 0.0;
-        {
-            float *__restrict__ sc = st_s + t;
-            const float *__restrict__ kv = Ks;
-            const float *__restrict__ qv = Qs;
-#pragma unroll 16
-            for (int k = 0; k < HD; ++k) {
-                const float sn = __fadd_rn(__fmul_rn(sc[k * HD], gh), __fmul_rn(kv[k], delta));
-                sc[k * HD] = sn;
-                acc2 += static_cast<double>(__fmul_rn(sn, qv[k]));
-            }
-        }
-        const float o = static_cast<float>(acc2);
+        const float o = gdn_recur_column<HD>(st_s + t, Ks, Qs, gh, bh, vt);  // as gdn_fused_kernel
         const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
         const float mean = static_cast<float>(ssq / static_cast<double>(HD));
         const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));

@@ -39,6 +39,7 @@
 
 #include "qh_backend.h"
 #include "qh_common.cuh"
+#include "qh_gdn.cuh"
 #include "qh_gemv_dev.cuh"
 #include "qh_internal.h"
 #include "qh_kernels.h"
@@ -441,21 +442,7 @@ __device__ __forceinline__ void step_gdn_head(const StepGdn &g, int h, float *st
     gdn_gates_sync();  // with warp 4, which formed beta and g
     mark(4);
     const float gh = gates[1], bh = gates[0];
-    double acc = 0.0;
-#pragma unroll 16
-    for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(st_s[k * HD + t], gh), Ks[k]));
-    const float delta = __fmul_rn(__fsub_rn(vt, static_cast<float>(acc)), bh);
-    double acc2 = 0.0;
-    {
-        float *__restrict__ sc = st_s + t;
-#pragma unroll 16
-        for (int k = 0; k < HD; ++k) {
-            const float sn = __fadd_rn(__fmul_rn(sc[k * HD], gh), __fmul_rn(Ks[k], delta));
-            sc[k * HD] = sn;
-            acc2 += static_cast<double>(__fmul_rn(sn, Qs[k]));
-        }
-    }
-    const float o = static_cast<float>(acc2);
+    const float o = gdn_recur_column<HD>(st_s + t, Ks, Qs, gh, bh, vt);  // qh_gdn.cuh
     mark(6);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     gdn_sync();
