@@ -552,25 +552,37 @@ __global__ void __launch_bounds__(gemm_threads(EXP), 1) gemm_kernel(const __grid
                 const float2 rs = row_scale[ring * kGemmRows + er];
                 const float *ts = tok_scale + ring * kGemmTok + 32 * th;
                 const uint32_t tcol = tmem + lane_base + buf * kAccCols + 32 * th;
+                // With expanded weights (320 threads, registers to spare) both
+                // halves' accumulator loads are issued before one wait; the
+                // 576-thread form loads and waits per half.
+                constexpr bool kBoth = EXP && !MINS;
+                constexpr int kHalves = kBoth ? 2 : 1;
+                uint32_t vhi[kHalves][16], vlo[kHalves][16], vsl[kHalves][16], vsh[kHalves][16];
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
-                    uint32_t vhi[16], vlo[16], vsl[16], vsh[16];
-                    tc::ld_32x32b_x16(tcol + 16 * c, vhi);
-                    tc::ld_32x32b_x16(tcol + kGemmTok + 16 * c, vlo);
-                    if (MINS) {
-                        tc::ld_32x32b_x16(tcol + 2 * kGemmTok + 16 * c, vsl);
-                        tc::ld_32x32b_x16(tcol + 3 * kGemmTok + 16 * c, vsh);
+                    const int hv = kBoth ? c : 0;
+                    if (!kBoth || c == 0) {
+#pragma unroll
+                        for (int c2 = 0; c2 < (kBoth ? 2 : 1); ++c2) {
+                            const int cc = kBoth ? c2 : c, hh = kBoth ? c2 : 0;
+                            tc::ld_32x32b_x16(tcol + 16 * cc, vhi[hh]);
+                            tc::ld_32x32b_x16(tcol + kGemmTok + 16 * cc, vlo[hh]);
+                            if (MINS) {
+                                tc::ld_32x32b_x16(tcol + 2 * kGemmTok + 16 * cc, vsl[hh]);
+                                tc::ld_32x32b_x16(tcol + 3 * kGemmTok + 16 * cc, vsh[hh]);
+                            }
+                        }
+                        tc::wait_ld();
                     }
-                    tc::wait_ld();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const float yd = ts[16 * c + j];
-                        const int isum = static_cast<int>(vhi[j]) * 128 + static_cast<int>(vlo[j]);
+                        const int isum = static_cast<int>(vhi[hv][j]) * 128 + static_cast<int>(vlo[hv][j]);
                         float term;
                         if (!MINS) {
                             term = __fmul_rn(__fmul_rn(rs.x, yd), __int2float_rn(isum));
                         } else {
-                            const int imin = static_cast<int>(vsl[j]) + 128 * static_cast<int>(vsh[j]);
+                            const int imin = static_cast<int>(vsl[hv][j]) + 128 * static_cast<int>(vsh[hv][j]);
                             const float d = __fmul_rn(yd, rs.x), dm = __fmul_rn(yd, rs.y);
                             term = __fsub_rn(__fmul_rn(d, __int2float_rn(isum)), __fmul_rn(dm, __int2float_rn(imin)));
                         }
