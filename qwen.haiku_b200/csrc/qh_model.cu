@@ -1061,8 +1061,13 @@ __global__ void __launch_bounds__(HD)
 // c + gridDim.x, ...; thread t holds state column t in registers while it is
 // updated, and the next pair's 64 KB state is copied into shared memory (one
 // bulk copy) while the current pair computes -- so the state stream and the
-// double-precision chains overlap instead of taking turns wave by wave. Per
-// pair the operations and orders of gdn_fused_kernel<128, false>.
+// double-precision chains overlap instead of taking turns wave by wave.
+// The next pair's per-thread inputs (its conv rows, new qkv values, conv
+// weights, z) are copied into shared memory by cp.async at the start of the
+// current pair, so the pair starts without a global-memory round trip; the
+// gates (beta, g) of up to 128 of the CTA's pairs are formed at once, one
+// pair per thread, instead of by one thread inside every pair. Per pair the
+// operations and orders of gdn_fused_kernel<128, false>.
 template <int KK>
 __global__ void __launch_bounds__(128, 2)
     gdn_stream_kernel(const float *__restrict__ qkv, float *__restrict__ ring, const float *__restrict__ conv_w,
@@ -1076,9 +1081,43 @@ __global__ void __launch_bounds__(128, 2)
     __shared__ uint64_t st_bar;
     __shared__ double scratch[64];
     __shared__ float Ks[HD], Qs[HD];
-    __shared__ float s_beta, s_g;
+    __shared__ float s_beta[HD], s_g[HD];  // gates of the CTA's pairs pi0 .. pi0 + HD - 1
+    // per-thread inputs of the next pair: [part] new value, [part][r] conv
+    // ring rows, [part][k] conv weights, z
+    constexpr int kPreX = 0, kPreRows = 3, kPreW = 3 + 3 * KK, kPreZ = 3 + 6 * KK, kPre = 4 + 6 * KK;
+    __shared__ float pre[kPre][HD];
     const int t = threadIdx.x;
     const int kdim = heads * HD, conv_dim = 3 * kdim;
+    auto cp4 = [](float *dst, const float *src) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+    };
+    auto prefetch = [&](int pr) {  // every thread its own elements, one commit group
+        const int pb = pr / heads, ph = pr % heads;
+        const float *src = qkv + static_cast<int64_t>(pb) * conv_dim;
+        const float *rg = ring + static_cast<int64_t>(pb) * KK * conv_dim;
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const int ch = part * kdim + ph * HD + t;
+            cp4(&pre[kPreX + part][t], src + ch);
+#pragma unroll
+            for (int r = 0; r < KK; ++r) cp4(&pre[kPreRows + part * KK + r][t], rg + static_cast<int64_t>(r) * conv_dim + ch);
+#pragma unroll
+            for (int q = 0; q < KK; ++q) cp4(&pre[kPreW + part * KK + q][t], conv_w + static_cast<int64_t>(ch) * KK + q);
+        }
+        cp4(&pre[kPreZ][t], z + static_cast<int64_t>(pb) * kdim + ph * HD + t);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // thread t: the gates of the CTA's pair pi0 + t (pair index = sequence * heads + head)
+    auto form_gates = [&](int pi0) {
+        const int pr = blockIdx.x + (pi0 + t) * static_cast<int>(gridDim.x);
+        if (pr < n_pairs) {
+            const int ph = pr % heads;
+            s_beta[t] = sigmoid_f(bb[pr]);
+            const float a = __fadd_rn(aa[pr], dt_bias[ph]);
+            const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
+            s_g[t] = expf_ref(__fmul_rn(ssm_a[ph], sp));
+        }
+    };
     if (t == 0) {
         mbar_init(&st_bar, 1);
         mbar_fence_init();
@@ -1086,40 +1125,36 @@ __global__ void __launch_bounds__(128, 2)
     __syncthreads();
     pdl_wait();
     int pair = blockIdx.x;
+    if (pair < n_pairs) prefetch(pair);
     auto issue = [&](int pr) {  // thread 0
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the column reads come first
         mbar_arrive_expect_tx(&st_bar, HD * HD * 4);
         bulk_copy_g2s(st_s, state + static_cast<int64_t>(pr) * HD * HD, HD * HD * 4, &st_bar);
     };
     if (t == 0 && pair < n_pairs) issue(pair);
+    form_gates(0);  // published by the barrier after the first pair's column reads
+    const float nw = norm_w[t];
     const int pos = max(*pos_ptr, 0);
     const int slot = pos % KK, head_after = (pos + 1) % KK;
     uint32_t parity = 0;
-    for (; pair < n_pairs; pair += gridDim.x) {
+    for (int pi = 0; pair < n_pairs; pair += gridDim.x, ++pi) {
+        if (pi > 0 && pi % HD == 0) form_gates(pi);  // the previous pair's gate reads precede its last barrier
         const int b = pair / heads, h = pair % heads;
         // ---- conv ring + SiLU + L2 norms + beta/g (gdn_fused_kernel's order) ----
-        float cw[3][KK];
-#pragma unroll
-        for (int part = 0; part < 3; ++part)
-#pragma unroll
-            for (int k = 0; k < KK; ++k) cw[part][k] = conv_w[(part * kdim + h * HD + t) * KK + k];
-        const float *src = qkv + static_cast<int64_t>(b) * conv_dim;
-        float *rg = ring + static_cast<int64_t>(b) * KK * conv_dim;
-        float xin[3], rows[3][KK];
+        asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's prefetched inputs
+        float cw[3][KK], xin[3], rows[3][KK];
 #pragma unroll
         for (int part = 0; part < 3; ++part) {
-            const int ch = part * kdim + h * HD + t;
-            xin[part] = src[ch];
+            xin[part] = pre[kPreX + part][t];
 #pragma unroll
-            for (int r = 0; r < KK; ++r) rows[part][r] = rg[static_cast<int64_t>(r) * conv_dim + ch];
+            for (int r = 0; r < KK; ++r) rows[part][r] = pre[kPreRows + part * KK + r][t];
+#pragma unroll
+            for (int q = 0; q < KK; ++q) cw[part][q] = pre[kPreW + part * KK + q][t];
         }
-        if (t == 32) {
-            const int i = b * heads + h;
-            s_beta = sigmoid_f(bb[i]);
-            const float a = __fadd_rn(aa[i], dt_bias[h]);
-            const float sp = a > 20.0f ? a : logf_ref(__fadd_rn(1.0f, expf_ref(a)));
-            s_g = expf_ref(__fmul_rn(ssm_a[h], sp));
-        }
+        const float zs = silu_f(pre[kPreZ][t]);
+        // the buffer is this thread's alone: the next pair's inputs go in now
+        if (pair + static_cast<int>(gridDim.x) < n_pairs) prefetch(pair + gridDim.x);
+        float *rg = ring + static_cast<int64_t>(b) * KK * conv_dim;
         float mixed[3];
 #pragma unroll
         for (int part = 0; part < 3; ++part) {
@@ -1149,7 +1184,6 @@ __global__ void __launch_bounds__(128, 2)
         Ks[t] = __fmul_rn(mixed[1], krs);
         const float vt = mixed[2];
         const int64_t zi = static_cast<int64_t>(b) * kdim + h * HD + t;
-        const float zv = z[zi];
         // ---- the state column into registers; the buffer then takes the next pair ----
         if (!mbar_wait(&st_bar, parity)) report_error(err_flag, kDevWaitTimeout);
         parity ^= 1u;
@@ -1159,7 +1193,7 @@ __global__ void __launch_bounds__(128, 2)
         __syncthreads();  // every column read (and Ks, Qs, s_g, s_beta written)
         if (t == 0 && pair + static_cast<int>(gridDim.x) < n_pairs) issue(pair + gridDim.x);
         // ---- recurrence (gdn_fused_kernel's two chains) ----
-        const float gh = s_g, bh = s_beta;
+        const float gh = s_g[pi % HD], bh = s_beta[pi % HD];
         double acc = 0.0;
 #pragma unroll
         for (int k = 0; k < HD; ++k) acc += static_cast<double>(__fmul_rn(__fmul_rn(S[k], gh), Ks[k]));
@@ -1178,7 +1212,7 @@ __global__ void __launch_bounds__(128, 2)
         const double ssq = block_sum_d(static_cast<double>(__fmul_rn(o, o)), scratch);
         const float mean = static_cast<float>(ssq / static_cast<double>(HD));
         const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-        y_out[zi] = __fmul_rn(__fmul_rn(__fmul_rn(o, rs), norm_w[t]), silu_f(zv));
+        y_out[zi] = __fmul_rn(__fmul_rn(__fmul_rn(o, rs), nw), zs);
         __syncthreads();  // Ks, Qs and the scratch are rewritten by the next pair
     }
 }
