@@ -98,6 +98,29 @@ __device__ __forceinline__ float logf_ref(float x) {
     return __double2float_rn(y);
 }
 
+// Brings the tables of expf_ref / logf_ref into this SM's L1 (a hint: no
+// result, no fault). Called by lanes 0-9 of one warp before a kernel's
+// programmatic-launch wait (the tables are constants), so its first expf or
+// logf after the wait does not wait for a memory round trip per table step.
+__device__ __forceinline__ void libm_prefetch_l1(int lane) {
+    using namespace libm;
+    const void *p = nullptr;
+    switch (lane) {
+        case 0: p = &kExp2Tab[0]; break;
+        case 1: p = &kExp2Tab[31]; break;
+        case 2: p = &kLogInvC[0]; break;
+        case 3: p = &kLogInvC[15]; break;
+        case 4: p = &kLogLogC[0]; break;
+        case 5: p = &kLogLogC[15]; break;
+        case 6: p = &kLogExcIn[0]; break;
+        case 7: p = &kLogExcIn[kLogExcN > 0 ? kLogExcN - 1 : 0]; break;
+        case 8: p = &kLogExcOut[0]; break;
+        case 9: p = &kLogExcOut[kLogExcN > 0 ? kLogExcN - 1 : 0]; break;
+        default: break;
+    }
+    if (p) asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 }  // namespace qh
 
 #endif  // QH_LIBM_CUH

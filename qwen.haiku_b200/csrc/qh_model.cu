@@ -1091,7 +1091,19 @@ __global__ void __launch_bounds__(128, 2)
     auto cp4 = [](float *dst, const float *src) {
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
     };
-    auto prefetch = [&](int pr) {  // every thread its own elements, one commit group
+    // every thread its own elements: the conv weights (constants, so the
+    // first pair's may be copied before the launch wait), then the rest and
+    // one commit group
+    auto prefetch_w = [&](int pr) {
+        const int ph = pr % heads;
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const int ch = part * kdim + ph * HD + t;
+#pragma unroll
+            for (int q = 0; q < KK; ++q) cp4(&pre[kPreW + part * KK + q][t], conv_w + static_cast<int64_t>(ch) * KK + q);
+        }
+    };
+    auto prefetch_x = [&](int pr) {
         const int pb = pr / heads, ph = pr % heads;
         const float *src = qkv + static_cast<int64_t>(pb) * conv_dim;
         const float *rg = ring + static_cast<int64_t>(pb) * KK * conv_dim;
@@ -1101,8 +1113,6 @@ __global__ void __launch_bounds__(128, 2)
             cp4(&pre[kPreX + part][t], src + ch);
 #pragma unroll
             for (int r = 0; r < KK; ++r) cp4(&pre[kPreRows + part * KK + r][t], rg + static_cast<int64_t>(r) * conv_dim + ch);
-#pragma unroll
-            for (int q = 0; q < KK; ++q) cp4(&pre[kPreW + part * KK + q][t], conv_w + static_cast<int64_t>(ch) * KK + q);
         }
         cp4(&pre[kPreZ][t], z + static_cast<int64_t>(pb) * kdim + ph * HD + t);
         asm volatile("cp.async.commit_group;" ::: "memory");
@@ -1122,17 +1132,23 @@ __global__ void __launch_bounds__(128, 2)
         mbar_init(&st_bar, 1);
         mbar_fence_init();
     }
+    int pair = blockIdx.x;
+    if (t < 32) libm_prefetch_l1(t);
+    if (t == 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(dt_bias));
+    if (t == 33) asm volatile("prefetch.global.L1 [%0];" ::"l"(ssm_a));
+    if (pair < n_pairs) prefetch_w(pair);
     __syncthreads();
     pdl_wait();
-    int pair = blockIdx.x;
-    if (pair < n_pairs) prefetch(pair);
+    if (pair < n_pairs) prefetch_x(pair);
     auto issue = [&](int pr) {  // thread 0
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the column reads come first
         mbar_arrive_expect_tx(&st_bar, HD * HD * 4);
         bulk_copy_g2s(st_s, state + static_cast<int64_t>(pr) * HD * HD, HD * HD * 4, &st_bar);
     };
-    if (t == 0 && pair < n_pairs) issue(pair);
+    // the gates' loads go out before the state copies of every CTA fill the
+    // memory queues; the first state copy follows them
     form_gates(0);  // published by the barrier after the first pair's column reads
+    if (t == 0 && pair < n_pairs) issue(pair);
     const float nw = norm_w[t];
     const int pos = max(*pos_ptr, 0);
     const int slot = pos % KK, head_after = (pos + 1) % KK;
@@ -1153,7 +1169,10 @@ __global__ void __launch_bounds__(128, 2)
         }
         const float zs = silu_f(pre[kPreZ][t]);
         // the buffer is this thread's alone: the next pair's inputs go in now
-        if (pair + static_cast<int>(gridDim.x) < n_pairs) prefetch(pair + gridDim.x);
+        if (pair + static_cast<int>(gridDim.x) < n_pairs) {
+            prefetch_w(pair + gridDim.x);
+            prefetch_x(pair + gridDim.x);
+        }
         float *rg = ring + static_cast<int64_t>(b) * KK * conv_dim;
         float mixed[3];
 #pragma unroll
