@@ -706,10 +706,15 @@ int attn_gqa_impl(const float *d_q, const uint16_t *d_kcache, const uint16_t *d_
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     // Query heads per CTA: the whole group (each cache row read once for all
-    // of them) when that already fills the GPU twice over, else one (more
-    // CTAs, each reading the rows again: decode at up to ~100 sequences)
+    // of them) when that already fills the GPU twice over, else the fewest
+    // whose CTAs still run in one wave (three resident per SM): more CTAs,
+    // each reading the rows again, for decode at up to ~100 sequences
     const int64_t group_ctas = static_cast<int64_t>(n_seq) * rows_per_seq * kvh;
-    const int G = group_ctas >= 2 * static_cast<int64_t>(sms) ? qgroup : 1;
+    int G = qgroup;
+    if (group_ctas < 2 * static_cast<int64_t>(sms)) {
+        G = 1;
+        while (G < qgroup && group_ctas * (qgroup / G) > 3 * static_cast<int64_t>(sms)) G *= 2;
+    }
     const size_t smem = sizeof(float) * static_cast<size_t>(G) * (128 + ((static_cast<size_t>(max_pos) + 3) & ~size_t(3))) +
                         qh::kAttnVBufs * qh::kAttnVChunk * 128 * sizeof(__half);
     if (smem > 200 * 1024) return bad("attention: context too long");
