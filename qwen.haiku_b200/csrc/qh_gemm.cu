@@ -613,10 +613,28 @@ __global__ void __launch_bounds__(gemm_threads(EXP), 1) gemm_kernel(const __grid
                 asm volatile("bar.sync 2, %0;" ::"n"(32 * kEpiWarps) : "memory");
                 if (!last_flag) continue;
                 __threadfence();  // acquire the other chunks' terms
-                for (int b = 0; b < p.nb; ++b) {
+                // with expanded weights (registers to spare) two blocks'
+                // terms are in flight per round trip to L2; the adds stay in
+                // block order
+                auto term = [&](int b, int j) {
+                    return __ldcg(tterms + (static_cast<int64_t>(b) * kGemmTok + 32 * th + j) * kGemmRows + er);
+                };
+                int b = 0;
+                if constexpr (EXP) {
+                    for (; b + 2 <= p.nb; b += 2) {
+                        float v0[32], v1[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        acc[j] = __fadd_rn(acc[j], __ldcg(tterms + (static_cast<int64_t>(b) * kGemmTok + 32 * th + j) * kGemmRows + er));
+                        for (int j = 0; j < 32; ++j) {
+                            v0[j] = term(b, j);
+                            v1[j] = term(b + 1, j);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(__fadd_rn(acc[j], v0[j]), v1[j]);
+                    }
+                }
+                for (; b < p.nb; ++b) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], term(b, j));
                 }
             } else if (stop) {
                 break;
