@@ -63,6 +63,21 @@ constexpr int kGemmHeader = 1024;
 constexpr int kGemmSmemMax = 232448;            // 227 KB per CTA
 constexpr uint32_t kAccCols = 256;              // one accumulator set
 constexpr int kRing = 4;                        // scale ring depth (blocks)
+constexpr int kSpreadDone = 512;                // split-K: second counter of tile t at tickets[512 + t]
+constexpr int kSpreadMaxNb = 16;                // spread reduction: at most 16 blocks per tile
+constexpr int kSpreadPerThread = 4;             // ... and 4 elements per epilogue thread
+constexpr uint64_t kSpreadWaitNs = 2000000000ull;  // wait for the tile's other chunks: 2 s
+
+__device__ __forceinline__ uint64_t gemm_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned gemm_ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 struct GemmJob {
     const uint8_t *wt;  // tiled weights
@@ -76,10 +91,12 @@ struct GemmJob {
 struct GemmParams {
     int32_t n_jobs, total_items, nb, n_tok, t_tiles, n_stages;
     int32_t kchunks, kc_blocks;  // split of the super-blocks of one output tile over CTAs
+    int32_t spread;              // split-K: every chunk's CTA sums a slice of the tile (all resident)
     int32_t w_early;             // weights complete before the previous kernel: stream them before pdl_wait
     const uint8_t *xq;           // tiled Q8_K activations
     float *terms;                // split-K: per-block fp32 terms [tile][block][64 tokens][128 rows]
-    unsigned *tickets;           // split-K: arrivals per output tile (left at zero)
+    unsigned *tickets;           // split-K: arrivals per output tile, then (spread) readers done at
+                                 // kSpreadDone + tile (all left at zero)
     int *err_flag;
     GemmJob jobs[kGemmMaxJobs];
 };
@@ -605,6 +622,76 @@ __global__ void __launch_bounds__(gemm_threads(EXP), 1) gemm_kernel(const __grid
                     stop = true;
                     break;
                 }
+                if (EXP && p.spread) {
+                    // Every chunk's CTA of the tile is resident (one item per
+                    // CTA): each waits for all the chunks' terms, then sums a
+                    // slice of the tile's elements, all blocks' terms loaded
+                    // before the in-order adds.
+                    if (warp == XW && lane == 0) {
+                        atomicAdd(&p.tickets[it.tile], 1u);
+                        const unsigned target = static_cast<unsigned>(p.kchunks);
+                        const uint64_t t_start = gemm_ns();
+                        int ok = 0;
+                        for (uint32_t n = 1;; ++n) {
+                            if (gemm_ld_acquire(&p.tickets[it.tile]) >= target) { ok = 1; break; }
+                            if ((n & 63u) == 0) {
+                                if (*reinterpret_cast<volatile int *>(p.err_flag) != 0) break;
+                                if (gemm_ns() - t_start > kSpreadWaitNs) {
+                                    report_error(p.err_flag, kDevWaitTimeout);
+                                    break;
+                                }
+                            }
+                        }
+                        last_flag = ok;
+                    }
+                    asm volatile("bar.sync 2, %0;" ::"n"(32 * kEpiWarps) : "memory");
+                    if (!last_flag) {
+                        stop = true;
+                        break;
+                    }
+                    __threadfence();  // acquire the other chunks' terms
+                    constexpr int E = kGemmTok * kGemmRows;
+                    const int c = it.b0 / p.kc_blocks;
+                    const int lo = c * E / p.kchunks, hi = (c + 1) * E / p.kchunks;
+                    const int et = ew * 32 + lane;
+                    // two elements per round trip to L2 (bounded registers)
+#pragma unroll 1
+                    for (int e0 = 0; e0 < kSpreadPerThread; e0 += 2) {
+                        float v[2][kSpreadMaxNb];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int idx = lo + et + 32 * kEpiWarps * (e0 + e);
+#pragma unroll
+                            for (int b = 0; b < kSpreadMaxNb; ++b)
+                                if (idx < hi && b < p.nb) v[e][b] = __ldcg(tterms + static_cast<int64_t>(b) * E + idx);
+                        }
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int idx = lo + et + 32 * kEpiWarps * (e0 + e);
+                            if (idx < hi) {
+                                float sum = 0.0f;
+#pragma unroll
+                                for (int b = 0; b < kSpreadMaxNb; ++b)
+                                    if (b < p.nb) sum = __fadd_rn(sum, v[e][b]);
+                                const int tok = it.tt * kGemmTok + idx / kGemmRows;
+                                const int n = it.mt * kGemmRows + idx % kGemmRows;
+                                if (n < it.job.n_rows && tok < p.n_tok)
+                                    it.job.out[static_cast<int64_t>(tok) * it.job.ldo + n] = sum;
+                            }
+                        }
+                    }
+                    // every read of the tile's terms is done: the last reader
+                    // returns both counters to zero
+                    asm volatile("bar.sync 2, %0;" ::"n"(32 * kEpiWarps) : "memory");
+                    if (warp == XW && lane == 0) {
+                        const unsigned prev = atomicAdd(&p.tickets[kSpreadDone + it.tile], 1u);
+                        if (prev == static_cast<unsigned>(p.kchunks - 1)) {
+                            p.tickets[it.tile] = 0u;
+                            p.tickets[kSpreadDone + it.tile] = 0u;
+                        }
+                    }
+                    continue;
+                }
                 if (warp == XW && lane == 0) {
                     const unsigned prev = atomicAdd(&p.tickets[it.tile], 1u);
                     last_flag = prev == static_cast<unsigned>(p.kchunks - 1);
@@ -875,6 +962,7 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
     // tiles alone would leave most SMs idle (needs the scratch).
     p.kchunks = 1;
     p.kc_blocks = p.nb;
+    p.spread = 0;
     const int64_t need = qh_gemm_scratch_bytes(jobs, n_jobs, k, n_tok);
     // Expanded weights stream at the memory rate, so a split (whose last CTA
     // re-reads every block's terms) pays only for very few tiles.
@@ -885,6 +973,14 @@ int qh_gemm(int type, const qh_gemm_job *jobs, int n_jobs, int64_t k, const void
         p.kchunks = static_cast<int32_t>((p.nb + p.kc_blocks - 1) / p.kc_blocks);
         p.tickets = static_cast<unsigned *>(d_scratch);
         p.terms = reinterpret_cast<float *>(static_cast<uint8_t *>(d_scratch) + kTicketBytes);
+        // Spread reduction when every item has its own resident CTA (the
+        // chunks of a tile wait for one another) and a slice fits the
+        // per-thread registers.
+        const int64_t items = out_tiles * p.kchunks;
+        const int64_t slice = (static_cast<int64_t>(qh::kGemmTok) * qh::kGemmRows + p.kchunks - 1) / p.kchunks;
+        p.spread = (flags & QH_GEMM_EXPANDED) && items <= sms && out_tiles <= qh::kSpreadDone &&
+                   p.nb <= qh::kSpreadMaxNb &&
+                   slice <= static_cast<int64_t>(qh::kSpreadPerThread) * 32 * qh::kEpiWarps;
     }
     if (out_tiles * p.kchunks > 0x7fffffffll) return gfail(QH_ERR_INVALID, "gemm: too many tiles");
     p.total_items = static_cast<int32_t>(out_tiles * p.kchunks);

@@ -134,6 +134,34 @@ def test_expanded_weights_bitexact(qh, cuda, oracle, gt, k, out_f, n_tok, split)
     assert_bitwise(b.cpu().numpy(), a.cpu().numpy(), "expanded vs tiled")
 
 
+@pytest.mark.parametrize("gt,k,out_f,n_tok", [(Q6_K, 3584, 1024, 64), (Q4_K, 2048, 1024, 64), (Q5_K, 2048, 257, 1)])
+def test_expanded_split_spread_reduction(qh, cuda, oracle, gt, k, out_f, n_tok):
+    """Expanded weights, few output tiles: every chunk's CTA of a tile waits
+    for the others and sums a slice of the tile's elements in block order.
+    Equal to the oracle bit for bit, on two calls over one scratch, and both
+    arrival counters back at zero after each call."""
+    w = qh.host.synth_blocks(gt, out_f * (k // 256), 0x5D + k + gt)
+    x_np = qh.host.synth_normal(n_tok * k, 0x5E + k).reshape(n_tok, k)
+    we = qh.host.gemm_expand(gt, qh.host.gemm_pack(gt, qh.host.to_device(w), k, out_f), k, out_f)
+    xq = qh.host.quantize_q8kt(qh.host.to_device(x_np), k, n_tok)
+    want = oracle.matmul(gt, w, out_f, k, x_np).reshape(n_tok, out_f)
+    out = cuda.empty((n_tok, out_f), dtype=cuda.float32, device="cuda")
+    scratch = qh.host.gemm(gt, [(we, out_f, out, out_f)], k, xq, n_tok, split=True, flags=QH_GEMM_EXPANDED)
+    cuda.cuda.synchronize()
+    assert_bitwise(out.cpu().numpy(), want, "first call")
+    assert int(scratch[:4096].sum()) == 0, "split-K counters not reset"
+    from qwen_haiku_b200 import GemmJob
+    import ctypes as C
+    out2 = cuda.full_like(out, -3.0)
+    arr = (GemmJob * 1)(GemmJob(we.data_ptr(), out_f, out2.data_ptr(), out_f))
+    qh.check(qh.lib().qh_gemm(gt, C.cast(arr, C.c_void_p), 1, k, C.c_void_p(xq.data_ptr()), n_tok,
+                              C.c_void_p(scratch.data_ptr()), scratch.numel(), QH_GEMM_EXPANDED, None), "qh_gemm")
+    cuda.cuda.synchronize()
+    assert_bitwise(out2.cpu().numpy(), want, "second call on the same scratch")
+    assert int(scratch[:4096].sum()) == 0, "split-K counters not reset"
+    assert qh.lib().qh_check_device_error(None) == 0
+
+
 def test_expanded_grouped_jobs(qh, cuda, oracle):
     """Three expanded Q4_K matrices in one launch, 130 tokens (3 token tiles)."""
     k, n_tok = 1024, 130
