@@ -330,7 +330,7 @@ struct GemmSmem {
 // accumulators readable), acc_empty[2] (8 epilogue warps read them),
 // a_ready[2] (8 expander warps wrote a block's A buffer and scales),
 // scale_ready[2] (the MMA thread passes the scales on to the epilogue).
-template <int TYPE, bool EXP>
+template <int TYPE, bool EXP, bool SPREAD>
 __global__ void __launch_bounds__(gemm_threads(EXP), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
     using L = GemmSmem<TYPE, EXP>;
     constexpr int XW = gemm_exp_warps(EXP), kProducerWarp = XW + kEpiWarps, kMmaWarp = kProducerWarp + 1;
@@ -622,7 +622,7 @@ __global__ void __launch_bounds__(gemm_threads(EXP), 1) gemm_kernel(const __grid
                     stop = true;
                     break;
                 }
-                if (EXP && p.spread) {
+                if constexpr (SPREAD) {
                     // Every chunk's CTA of the tile is resident (one item per
                     // CTA): each waits for all the chunks' terms, then sums a
                     // slice of the tile's elements, all blocks' terms loaded
@@ -803,17 +803,20 @@ static cudaError_t gemm_launch_t(const GemmParams &p0, int sm_count, cudaStream_
     GemmParams p = p0;
     p.n_stages = L::kNStages;
     const int smem = L::kTotal;
-    static bool attr_done[64] = {false};
+    // the spread split-K reduction is its own instantiation, so the kernels
+    // of the other launches stay compact (registers, instruction cache)
+    static bool attr_done[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<TYPE, EXP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             L::kTotal);
+    const bool spread = EXP && p.spread;
+    auto kern = spread ? gemm_kernel<TYPE, EXP, EXP> : gemm_kernel<TYPE, EXP, false>;
+    if (dev >= 0 && dev < 64 && !attr_done[dev][spread]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
         if (e != cudaSuccess) return e;
-        attr_done[dev] = true;
+        attr_done[dev][spread] = true;
     }
     const int grid = std::min(p.total_items, sm_count);
-    return launch_pdl(gemm_kernel<TYPE, EXP>, dim3(grid), dim3(gemm_threads(EXP)), smem, stream, p);
+    return launch_pdl(kern, dim3(grid), dim3(gemm_threads(EXP)), smem, stream, p);
 }
 
 }  // namespace qh
