@@ -1409,14 +1409,29 @@ __global__ void __launch_bounds__(kArgmaxThreads)
     __shared__ int si[kArgmaxThreads / 32];
     __shared__ bool last;
     const int part = blockIdx.x, P = gridDim.x, row = blockIdx.y;
-    const int64_t chunk = (vocab + P - 1) / P;
+    // slices of a multiple of 4 logits: with 16-byte aligned rows each
+    // thread reads float4s, its indices still in increasing order
+    const int64_t chunk = (((vocab + P - 1) / P) + 3) & ~int64_t(3);
     const int64_t lo = part * chunk, hi = min(vocab, lo + chunk);
     const float *lr = logits + static_cast<int64_t>(row) * vocab;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        const float v = lr[i];
-        if (v > best) { best = v; bi = static_cast<int>(i); }
+    if ((vocab & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        const float4 *l4 = reinterpret_cast<const float4 *>(lr);
+#pragma unroll 4
+        for (int64_t q = lo / 4 + threadIdx.x; q < hi / 4; q += blockDim.x) {
+            const float4 v = l4[q];
+            const int i = static_cast<int>(4 * q);
+            if (v.x > best) { best = v.x; bi = i; }
+            if (v.y > best) { best = v.y; bi = i + 1; }
+            if (v.z > best) { best = v.z; bi = i + 2; }
+            if (v.w > best) { best = v.w; bi = i + 3; }
+        }
+    } else {
+        for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+            const float v = lr[i];
+            if (v > best) { best = v; bi = static_cast<int>(i); }
+        }
     }
     for (int off = 16; off > 0; off >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, off);
@@ -1592,14 +1607,22 @@ int qh_gdn_prefill(const float *d_qkv, float *d_ring, const float *d_conv_w, con
     return launch_status(le, "qh_gdn_prefill");
 }
 
-static int argmax_parts(int64_t vocab) {
-    const int64_t p = (vocab + 4095) / 4096;
+// Slices per row: at most one per 1024 logits and 64 in all (the scratch is
+// sized for that); for many rows fewer, so that the grid stays near 600
+// CTAs of 512 threads (about one wave at four per SM).
+static int argmax_parts_max(int64_t vocab) {
+    const int64_t p = (vocab + 1023) / 1024;
     return static_cast<int>(p < 1 ? 1 : (p > 64 ? 64 : p));
+}
+static int argmax_parts(int64_t vocab, int32_t B) {
+    const int pmax = argmax_parts_max(vocab);
+    const int p = (600 + B - 1) / B;
+    return p < 1 ? 1 : (p > pmax ? pmax : p);
 }
 
 int64_t qh_argmax_feed_scratch_bytes(int32_t B, int64_t vocab) {
     if (B <= 0 || vocab <= 0) return -1;
-    const int64_t P = argmax_parts(vocab);
+    const int64_t P = argmax_parts_max(vocab);
     return (static_cast<int64_t>(B) * P * 8 + (static_cast<int64_t>(B) + 1) * 4 + 255) & ~int64_t(255);
 }
 
@@ -1609,11 +1632,11 @@ int qh_argmax_feed(const float *d_logits, int32_t B, int64_t vocab, void *d_scra
     if (!d_logits || !d_scratch || !d_next || !d_prompt || !d_ctl || !d_tokens || !d_picks || B <= 0 ||
         B > 65535 || vocab <= 0 || vocab > 0x7ffffffe || stride <= 0)
         return bad("qh_argmax_feed: bad arguments");
-    const int P = argmax_parts(vocab);
+    const int P = argmax_parts(vocab, B), Pmax = argmax_parts_max(vocab);
     uint8_t *base = static_cast<uint8_t *>(d_scratch);
     float *pv = reinterpret_cast<float *>(base);
-    int *pi = reinterpret_cast<int *>(base + static_cast<int64_t>(B) * P * 4);
-    unsigned *tickets = reinterpret_cast<unsigned *>(base + static_cast<int64_t>(B) * P * 8);
+    int *pi = reinterpret_cast<int *>(base + static_cast<int64_t>(B) * Pmax * 4);
+    unsigned *tickets = reinterpret_cast<unsigned *>(base + static_cast<int64_t>(B) * Pmax * 8);
     const cudaError_t le = qh::launch_pdl(qh::argmax_feed_kernel, dim3(P, B), dim3(qh::kArgmaxThreads), 0,
                                           static_cast<cudaStream_t>(stream), d_logits, vocab, pv, pi, tickets,
                                           d_next, d_prompt, B, stride, d_ctl, d_tokens, d_picks);
