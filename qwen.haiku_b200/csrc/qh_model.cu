@@ -829,8 +829,11 @@ namespace qh {
 // reduction of rmsnorm_kernel with 256 threads), then quantizes its own
 // block; with a residual, CTA j writes h_out's block j (h_out != h, so no
 // CTA reads a value another one has updated).
+// NB: the most blocks a row may have (4: hidden sizes up to 1024, held to
+// 32 registers so that eight CTAs fit an SM for many-row prompt launches).
 constexpr int kResNormMaxBlocks = 16;
-__global__ void __launch_bounds__(256) resnorm_q8k_kernel(const float *__restrict__ h, const float *__restrict__ mix,
+template <int NB>
+__global__ void __launch_bounds__(256, NB <= 4 ? 8 : 1) resnorm_q8k_kernel(const float *__restrict__ h, const float *__restrict__ mix,
                                                           float *__restrict__ h_out, const float *__restrict__ w,
                                                           int dim, float eps, uint8_t *__restrict__ xq, int n_tok,
                                                           int tile) {
@@ -839,17 +842,26 @@ __global__ void __launch_bounds__(256) resnorm_q8k_kernel(const float *__restric
     __shared__ double scratch[32];
     __shared__ Q8KScratch sc;
     const int jb = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, nb = dim / QH_QK;
+    // every load of the thread (row values, residual branch, norm weight)
+    // goes out before the first add: one memory round trip
+    const int64_t r0 = static_cast<int64_t>(row) * dim + tid;
+    float hv[NB], mv[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+        hv[j] = j < nb ? h[r0 + j * QH_QK] : 0.0f;
+        mv[j] = (mix && j < nb) ? mix[r0 + j * QH_QK] : 0.0f;
+    }
+    const float wv = w[jb * QH_QK + tid];
     float mine = 0.0f;
     double s = 0.0;
 #pragma unroll
-    for (int j = 0; j < kResNormMaxBlocks; ++j) {
+    for (int j = 0; j < NB; ++j) {
         if (j < nb) {
-            const int64_t i = static_cast<int64_t>(row) * dim + j * QH_QK + tid;
-            float x = h[i];
-            if (mix) x = __fadd_rn(x, mix[i]);
+            float x = hv[j];
+            if (mix) x = __fadd_rn(x, mv[j]);
             if (j == jb) {
                 mine = x;
-                if (mix) h_out[i] = x;
+                if (mix) h_out[r0 + j * QH_QK] = x;
             }
             s += static_cast<double>(__fmul_rn(x, x));
         }
@@ -858,7 +870,7 @@ __global__ void __launch_bounds__(256) resnorm_q8k_kernel(const float *__restric
     const float rscale =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ssq / static_cast<double>(dim)), eps)));
     const Q8KRow r = q8k_row(xq, dim, n_tok, row, tile);
-    q8k_block256(__fmul_rn(__fmul_rn(mine, rscale), w[jb * QH_QK + tid]), sc, r, jb);
+    q8k_block256(__fmul_rn(__fmul_rn(mine, rscale), wv), sc, r, jb);
 }
 
 // SwiGLU + Q8_K: CTA (block, row), 256 threads.
@@ -1488,7 +1500,8 @@ int qh_rmsnorm_q8k(const float *d_h, const float *d_mix, float *d_h_out, const f
     if (!d_h || !d_w || !d_xq || dim <= 0 || dim % QH_QK || dim > qh::kResNormMaxBlocks * QH_QK || B <= 0 ||
         B > 65535 || !tile_ok(layout_tile) || (d_mix && (!d_h_out || d_h_out == d_h)))
         return bad("qh_rmsnorm_q8k: bad arguments");
-    const cudaError_t le = qh::launch_pdl(qh::resnorm_q8k_kernel, dim3(static_cast<unsigned>(dim / QH_QK), B),
+    auto kern = dim <= 4 * QH_QK ? qh::resnorm_q8k_kernel<4> : qh::resnorm_q8k_kernel<qh::kResNormMaxBlocks>;
+    const cudaError_t le = qh::launch_pdl(kern, dim3(static_cast<unsigned>(dim / QH_QK), B),
                                           dim3(256), 0, static_cast<cudaStream_t>(stream), d_h, d_mix, d_h_out, d_w,
                                           static_cast<int>(dim), eps, static_cast<uint8_t *>(d_xq), B, layout_tile);
     return launch_status(le, "qh_rmsnorm_q8k");
