@@ -356,8 +356,9 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const __half *__
     ctx[oi] = __fmul_rn(o, sigmoid_f(gate[oi]));
 }
 
-// Attention over the cache for a whole GQA group: CTA (sequence, KV head)
-// of HD threads serves the G query heads sharing that KV head, so every
+// Attention over the cache for G query heads of one GQA group: CTA
+// (sequence, G heads) of HD threads serves G heads sharing a KV head (the
+// whole group, or fewer so that the CTAs fill the GPU in one wave), so every
 // cache row is read once for G heads. Per head the arithmetic and its order
 // are those of attn_decode_kernel (tensor_attention, slm/tensor.c:1049-1102):
 // sequential dot per position, max, exp, sequential sum, scaling, and a
@@ -779,7 +780,7 @@ int qh_attn_decode(const float *d_q, const uint16_t *d_kcache, const uint16_t *d
                    const int32_t *d_pos, int32_t max_pos, float *d_ctx, void *stream) {
     if (B <= 0 || nh <= 0 || kvh <= 0 || nh % kvh || hd % 32 || hd > 1024 || !d_pos || max_pos <= 0)
         return bad("qh_attn_decode: bad arguments");
-    if (gqa_ok(nh, kvh, hd, d_kcache))  // one CTA per (sequence, KV head)
+    if (gqa_ok(nh, kvh, hd, d_kcache))  // CTAs of one or more query heads sharing a KV head
         return attn_gqa_impl(d_q, d_kcache, d_vcache, d_gate, B, 1, nh, kvh, d_pos, max_pos, d_ctx, stream,
                              "qh_attn_decode");
     const size_t smem = sizeof(float) * (static_cast<size_t>(hd) + max_pos + 32);
